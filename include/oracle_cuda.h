@@ -1,0 +1,208 @@
+/*
+ * oracle_cuda.h -- C ABI of the B200 (sm_100a) quantized-weight path.
+ *
+ * This library replaces Oracle's stubbed CUDA hook
+ * (src/backend/cuda/cuda_backend.cu:1-4, built under ORACLE_ENABLE_CUDA,
+ * CMakeLists.txt:53-58) for the path Oracle runs through the free functions in
+ * include/oracle/backend/cpu/quantized_reference.hpp:12-27 and
+ * include/oracle/model/storage_decode.hpp:38-41.  Paths below are relative to
+ * the Oracle repository.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  "Device" pointers address GPU memory of
+ *     the context's device; "host" pointers address CPU memory.
+ *   - Matrices are GGML row-major: `rows` rows of `cols` elements, each row
+ *     ggml_row_byte_size(cols, type) bytes (GGUF dims[0] = cols, dims[1] =
+ *     rows, quantized_reference.cpp:118-119).
+ *   - Activations x are `batch` contiguous f32 vectors of `cols` elements;
+ *     outputs y are `batch` contiguous f32 vectors of `rows` elements.
+ *   - Device-pointer calls are asynchronous on `stream` (a cudaStream_t; NULL
+ *     is the legacy default stream).  Host-pointer calls are synchronous, like
+ *     the reference.
+ *   - Every call validates its arguments on the host first, in the order the
+ *     reference does, and returns the status class of the C++ exception the
+ *     reference would throw; oracle_cuda_last_error() gives the message, which
+ *     repeats the reference's text.  Nothing is launched when validation fails.
+ *   - One context per device; calls on one context come from one host thread.
+ *
+ * Two arithmetic contracts
+ *   ORACLE_CUDA_CONTRACT_F32  Oracle's own: weights decoded to f32 exactly as
+ *                             Oracle decodes them, dotted with f32 x
+ *                             (quantized_reference.cpp:24-82).  Types f32,
+ *                             f16, bf16, q8_0, q4_K, q5_K, q6_K.
+ *   ORACLE_CUDA_CONTRACT_Q8K  GGML's integer contract: x quantized to Q8_K
+ *                             (f32 d, int8 qs[256], int16 bsums[16]), exact
+ *                             integer super-block dots, f32 combination in a
+ *                             fixed documented order.  Types q4_K, q6_K.
+ */
+#ifndef ORACLE_CUDA_H
+#define ORACLE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORACLE_CUDA_ABI_VERSION 1
+
+/* Status codes.  1..5 name the C++ exception class the reference throws for the
+ * same input, so a C++ adapter can rethrow the same type. */
+typedef enum oracle_cuda_status {
+    ORACLE_CUDA_OK = 0,
+    ORACLE_CUDA_INVALID_ARGUMENT = 1, /* std::invalid_argument */
+    ORACLE_CUDA_OUT_OF_RANGE = 2,     /* std::out_of_range */
+    ORACLE_CUDA_OVERFLOW = 3,         /* std::overflow_error */
+    ORACLE_CUDA_RUNTIME_ERROR = 4,    /* std::runtime_error */
+    ORACLE_CUDA_LOGIC_ERROR = 5,      /* std::logic_error */
+    ORACLE_CUDA_CUDA_ERROR = 6,       /* a CUDA runtime call failed */
+    ORACLE_CUDA_OUT_OF_MEMORY = 7,    /* device or pinned allocation failed */
+    ORACLE_CUDA_DEVICE_TIMEOUT = 8,   /* a kernel wait hit its deadline and returned early */
+    ORACLE_CUDA_UNSUPPORTED = 9       /* valid input this path does not implement */
+} oracle_cuda_status;
+
+typedef enum oracle_cuda_contract {
+    ORACLE_CUDA_CONTRACT_F32 = 0,
+    ORACLE_CUDA_CONTRACT_Q8K = 1
+} oracle_cuda_contract;
+
+typedef struct oracle_cuda_context oracle_cuda_context;
+typedef struct oracle_cuda_weight oracle_cuda_weight;
+
+/* ------------------------------------------------------------------ library */
+
+int oracle_cuda_abi_version(void);
+const char* oracle_cuda_status_name(oracle_cuda_status status);
+
+/* Message of the last failed call on `ctx` (or of the calling thread when ctx
+ * is NULL, e.g. after a failed create).  Valid until the next call. */
+const char* oracle_cuda_last_error(const oracle_cuda_context* ctx);
+
+/* ------------------------------------------------------------------ layout
+ * Host-only; no GPU needed.  Replaces ggml_type_layout / ggml_row_byte_size
+ * (include/oracle/model/ggml_type.hpp:17-19, src/model/ggml_type.cpp:69-94). */
+
+/* OK and the layout of a registered type; INVALID_ARGUMENT for an unknown or
+ * removed id (the reference returns nullptr). `name` may be NULL. */
+oracle_cuda_status oracle_ggml_type_layout(uint32_t type, uint64_t* block_elements,
+                                           uint64_t* bytes_per_block, int* quantized,
+                                           const char** name);
+
+/* ggml_row_byte_size: RUNTIME_ERROR for an unknown type or a ragged row,
+ * INVALID_ARGUMENT for zero elements, OVERFLOW on overflow. */
+oracle_cuda_status oracle_ggml_row_byte_size(uint64_t row_elements, uint32_t type,
+                                             uint64_t* out);
+
+/* ------------------------------------------------------------------ context */
+
+/* Create a context on CUDA device `device`: sets the device current, reads its
+ * SM count, allocates the device status word and pinned staging.  Replaces the
+ * reference's backend selection by name (src/runtime/engine.cpp:64-70). */
+oracle_cuda_status oracle_cuda_create(int device, oracle_cuda_context** out);
+oracle_cuda_status oracle_cuda_destroy(oracle_cuda_context* ctx);
+
+/* Context options (bit flags).  ORACLE_CUDA_FLAG_PDL launches the matvec
+ * kernels with programmatic dependent launch: a kernel may start streaming its
+ * weights before the preceding kernel in the stream finishes, and waits for it
+ * only before reading activations.  Only safe when the preceding kernel does
+ * not write the weight bytes. */
+#define ORACLE_CUDA_FLAG_PDL 1u
+oracle_cuda_status oracle_cuda_set_flags(oracle_cuda_context* ctx, uint32_t flags);
+
+/* Device status word written by kernels whose bounded waits expired.  Reads it
+ * (synchronising the device), clears it, and returns OK or DEVICE_TIMEOUT. */
+oracle_cuda_status oracle_cuda_device_status(oracle_cuda_context* ctx);
+
+/* Failure-detection self-test: launches one kernel whose only thread waits
+ * on a barrier that never completes, with a deadline of `limit_ns`.  The wait
+ * gives up, records a timeout in the device status word and the kernel ends;
+ * the context stays usable.  The next oracle_cuda_device_status() returns
+ * DEVICE_TIMEOUT. */
+oracle_cuda_status oracle_cuda_selftest_bounded_wait(oracle_cuda_context* ctx, uint64_t limit_ns);
+
+/* Number of kernels this context has launched (for launch accounting). */
+uint64_t oracle_cuda_launch_count(const oracle_cuda_context* ctx);
+
+/* ------------------------------------------------------------------ device-pointer path */
+
+/* decode_storage_row / reference_decode_mapped_tensor
+ * (storage_decode.cpp:244-294, quantized_reference.cpp:85-105): decode `rows`
+ * rows to f32, out_len == rows * cols. */
+oracle_cuda_status oracle_cuda_decode_rows(oracle_cuda_context* ctx, uint32_t type, uint64_t rows,
+                                           uint64_t cols, const void* w_dev, uint64_t w_nbytes,
+                                           float* out_dev, uint64_t out_len, void* stream);
+
+/* Q8_K activation quantizer: `batch` vectors of `cols` floats (cols % 256 == 0)
+ * into batch * (cols / 256) GGML block_q8_K records of 292 bytes.  No Oracle
+ * counterpart (only the layout is registered, ggml_type.cpp:28). */
+oracle_cuda_status oracle_cuda_quantize_q8_k(oracle_cuda_context* ctx, const float* x_dev,
+                                             uint64_t cols, uint64_t batch, void* q8k_dev,
+                                             uint64_t q8k_nbytes, void* stream);
+
+/* reference_storage_matvec (quantized_reference.cpp:128-162) on device
+ * buffers, for `batch` activation vectors: x_len == batch * cols, y_len ==
+ * batch * rows.  With CONTRACT_Q8K the activations are quantized to Q8_K
+ * inside the kernel (no intermediate buffer). */
+oracle_cuda_status oracle_cuda_storage_matvec(oracle_cuda_context* ctx, int contract, uint32_t type,
+                                              uint64_t rows, uint64_t cols, const void* w_dev,
+                                              uint64_t w_nbytes, const float* x_dev, uint64_t x_len,
+                                              float* y_dev, uint64_t y_len, void* stream);
+
+/* Q8_K contract with activations already quantized by oracle_cuda_quantize_q8_k
+ * (q8k_nbytes == batch * cols / 256 * 292). */
+oracle_cuda_status oracle_cuda_matvec_q8k_prequantized(oracle_cuda_context* ctx, uint32_t type,
+                                                       uint64_t rows, uint64_t cols,
+                                                       const void* w_dev, uint64_t w_nbytes,
+                                                       const void* q8k_dev, uint64_t q8k_nbytes,
+                                                       float* y_dev, uint64_t y_len, void* stream);
+
+/* ------------------------------------------------------------------ resident weights
+ * Oracle's weights are immutable GGUF bytes in a read-only mapping
+ * (MappedGgufModel, include/oracle/model/mapped_gguf.hpp:56-59).  They are
+ * copied to HBM once; a shard keeps rows [row_begin, row_end). */
+
+oracle_cuda_status oracle_cuda_weight_upload(oracle_cuda_context* ctx, uint32_t type, uint64_t rows,
+                                             uint64_t cols, const void* host_bytes, uint64_t nbytes,
+                                             uint64_t row_begin, uint64_t row_end,
+                                             oracle_cuda_weight** out);
+oracle_cuda_status oracle_cuda_weight_free(oracle_cuda_weight* weight);
+/* Device address, byte size and shard geometry of an uploaded weight. */
+oracle_cuda_status oracle_cuda_weight_info(const oracle_cuda_weight* weight, uint32_t* type,
+                                           uint64_t* rows, uint64_t* cols, uint64_t* row_begin,
+                                           const void** dev, uint64_t* nbytes);
+
+/* ------------------------------------------------------------------ host-pointer drop-ins
+ * Synchronous, host spans in and out, exactly the reference's signatures.  The
+ * weight bytes are made resident in HBM on first use, keyed by (host address,
+ * byte size, type, rows, cols), and reused afterwards, since Oracle's weights
+ * never change under a live mapping. */
+
+/* reference_storage_matvec (quantized_reference.cpp:128-162). */
+oracle_cuda_status oracle_cuda_host_storage_matvec(oracle_cuda_context* ctx, int contract,
+                                                   uint32_t type, uint64_t rows, uint64_t cols,
+                                                   const void* w_host, uint64_t w_nbytes,
+                                                   const float* x_host, uint64_t x_len,
+                                                   float* y_host, uint64_t y_len);
+
+/* reference_storage_dot (quantized_reference.cpp:24-82): one row. */
+oracle_cuda_status oracle_cuda_host_storage_dot(oracle_cuda_context* ctx, int contract,
+                                                uint32_t type, uint64_t cols, const void* row_host,
+                                                uint64_t row_nbytes, const float* x_host,
+                                                uint64_t x_len, float* out);
+
+/* decode_storage_row (storage_decode.cpp:244-294) and
+ * reference_decode_mapped_tensor (quantized_reference.cpp:85-105). */
+oracle_cuda_status oracle_cuda_host_decode_rows(oracle_cuda_context* ctx, uint32_t type,
+                                                uint64_t rows, uint64_t cols, const void* w_host,
+                                                uint64_t w_nbytes, float* out_host,
+                                                uint64_t out_len);
+
+/* Drop every resident copy made by the host-pointer calls. */
+oracle_cuda_status oracle_cuda_evict_resident(oracle_cuda_context* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ORACLE_CUDA_H */

@@ -1,0 +1,303 @@
+"""CPU checkers for the quantized-weight path -- TEST INFRASTRUCTURE ONLY.
+
+Two libraries, loaded with ctypes:
+
+* ``port`` -- ``liboracle_port.so``, the C restatement in ``quant_oracle.c``
+  (Oracle's decoders and f32 contract, plus GGML's Q8_K quantizer and integer
+  dots restated; provenance in ``quant_oracle.h``).
+* ``ref``  -- ``_ref/liboracle_ref.so``, the reference's own hot-path sources
+  compiled unmodified (``Makefile``), reached through ``ref_shim.cpp``.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+and reference legs may import this package.  The product library never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_PATH = os.path.join(HERE, "liboracle_port.so")
+REF_PATH = os.path.join(HERE, "_ref", "liboracle_ref.so")
+REFERENCE_TREE = "/root/reference"
+
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K, TYPE_Q8_K, TYPE_BF16 = (
+    0, 1, 8, 12, 13, 14, 15, 30)
+Q8K_BLOCK_BYTES = 292
+
+_u8p = C.POINTER(C.c_uint8)
+_f32p = C.POINTER(C.c_float)
+_f64p = C.POINTER(C.c_double)
+_u64p = C.POINTER(C.c_uint64)
+
+
+def build(reference_tree: str | None = REFERENCE_TREE) -> None:
+    """Compile the restatement, and the reference checker when its tree exists."""
+    targets = ["port"]
+    if reference_tree and os.path.isdir(reference_tree):
+        targets.append("ref")
+    subprocess.run(["make", "-s", "-C", HERE, f"REF={reference_tree}", *targets], check=True)
+
+
+def _ptr(a: np.ndarray, t):
+    return a.ctypes.data_as(t)
+
+
+class _Port:
+    def __init__(self, path: str = PORT_PATH):
+        if not os.path.exists(path):
+            build()
+        lib = C.CDLL(path)
+        lib.oq_f16_to_f32.argtypes = [C.c_uint16]
+        lib.oq_f16_to_f32.restype = C.c_float
+        lib.oq_bf16_to_f32.argtypes = [C.c_uint16]
+        lib.oq_bf16_to_f32.restype = C.c_float
+        lib.oq_f32_to_bf16_rne.argtypes = [C.c_float]
+        lib.oq_f32_to_bf16_rne.restype = C.c_uint16
+        lib.oq_row_bytes.argtypes = [C.c_uint32, C.c_uint64]
+        lib.oq_row_bytes.restype = C.c_uint64
+        lib.oq_decode_row.argtypes = [C.c_uint32, C.c_uint64, _u8p, _f32p]
+        lib.oq_quantize_row_q8_k.argtypes = [_f32p, C.c_uint64, _u8p]
+        lib.oq_block_sums_q4_k.argtypes = [_u8p, _u8p, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]
+        lib.oq_block_sums_q6_k.argtypes = [_u8p, _u8p, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]
+        lib.oq_vec_dot_q8_k.argtypes = [C.c_uint32, C.c_uint64, _u8p, _u8p]
+        lib.oq_vec_dot_q8_k.restype = C.c_float
+        lib.oq_vec_dot_q8_k_ggml_order.argtypes = [C.c_uint32, C.c_uint64, _u8p, _u8p]
+        lib.oq_vec_dot_q8_k_ggml_order.restype = C.c_float
+        lib.oq_matvec_q8_k.argtypes = [C.c_uint32, C.c_uint64, C.c_uint64, _u8p, _u8p,
+                                       C.c_uint64, _f32p]
+        lib.oq_storage_dot_f32.argtypes = [C.c_uint32, C.c_uint64, _u8p, _f32p]
+        lib.oq_storage_dot_f32.restype = C.c_float
+        lib.oq_storage_matvec_f32.argtypes = [C.c_uint32, C.c_uint64, C.c_uint64, _u8p, _f32p,
+                                              C.c_uint64, _f32p]
+        lib.oq_storage_matvec_f64.argtypes = [C.c_uint32, C.c_uint64, C.c_uint64, _u8p, _f32p,
+                                              C.c_uint64, _f64p]
+        lib.oq_gemm_sampled.argtypes = [C.c_uint32, C.c_uint64, C.c_uint64, _u8p, C.c_uint64,
+                                        _f32p, C.c_uint64, _u64p, _u64p, C.c_int, _f64p]
+        self.lib = lib
+
+    def row_bytes(self, qtype: int, k: int) -> int:
+        return int(self.lib.oq_row_bytes(qtype, k))
+
+    def f16_to_f32(self, bits: int) -> float:
+        return float(self.lib.oq_f16_to_f32(bits))
+
+    def decode_rows(self, qtype: int, rows: int, k: int, w: np.ndarray) -> np.ndarray:
+        w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1)
+        rb = self.row_bytes(qtype, k)
+        out = np.empty((rows, k), np.float32)
+        for r in range(rows):
+            seg = w[r * rb:(r + 1) * rb]
+            rc = self.lib.oq_decode_row(qtype, k, _ptr(seg, _u8p), _ptr(out[r], _f32p))
+            if rc:
+                raise ValueError(f"oq_decode_row failed with {rc}")
+        return out
+
+    def quantize_q8_k(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim == 1:
+            x = x[None]
+        batch, k = x.shape
+        out = np.empty((batch, (k // 256) * Q8K_BLOCK_BYTES), np.uint8)
+        for b in range(batch):
+            if self.lib.oq_quantize_row_q8_k(_ptr(x[b], _f32p), k, _ptr(out[b], _u8p)):
+                raise ValueError("k must be a positive multiple of 256")
+        return out
+
+    def block_sums(self, qtype: int, wblock: np.ndarray, q8block: np.ndarray):
+        i, m = C.c_int32(), C.c_int32()
+        wb = np.ascontiguousarray(wblock, np.uint8)
+        qb = np.ascontiguousarray(q8block, np.uint8)
+        fn = self.lib.oq_block_sums_q4_k if qtype == TYPE_Q4_K else self.lib.oq_block_sums_q6_k
+        fn(_ptr(wb, _u8p), _ptr(qb, _u8p), C.byref(i), C.byref(m))
+        return i.value, m.value
+
+    def matvec_q8_k(self, qtype: int, rows: int, k: int, w: np.ndarray, q8k: np.ndarray) -> np.ndarray:
+        w = np.ascontiguousarray(w, np.uint8).reshape(-1)
+        q8k = np.ascontiguousarray(q8k, np.uint8)
+        batch = q8k.size // ((k // 256) * Q8K_BLOCK_BYTES)
+        y = np.empty((batch, rows), np.float32)
+        rc = self.lib.oq_matvec_q8_k(qtype, rows, k, _ptr(w, _u8p), _ptr(q8k, _u8p), batch,
+                                     _ptr(y, _f32p))
+        if rc:
+            raise ValueError(f"oq_matvec_q8_k failed with {rc}")
+        return y
+
+    def vec_dot_q8_k_ggml_order(self, qtype: int, k: int, wrow: np.ndarray, q8row: np.ndarray) -> float:
+        wr = np.ascontiguousarray(wrow, np.uint8)
+        qr = np.ascontiguousarray(q8row, np.uint8)
+        return float(self.lib.oq_vec_dot_q8_k_ggml_order(qtype, k, _ptr(wr, _u8p), _ptr(qr, _u8p)))
+
+    def storage_matvec_f32(self, qtype: int, rows: int, k: int, w: np.ndarray, x: np.ndarray) -> np.ndarray:
+        w = np.ascontiguousarray(w, np.uint8).reshape(-1)
+        x = np.ascontiguousarray(x, np.float32)
+        batch = x.size // k
+        y = np.empty((batch, rows), np.float32)
+        rc = self.lib.oq_storage_matvec_f32(qtype, rows, k, _ptr(w, _u8p), _ptr(x, _f32p), batch,
+                                            _ptr(y, _f32p))
+        if rc:
+            raise ValueError(f"oq_storage_matvec_f32 failed with {rc}")
+        return y
+
+    def storage_matvec_f64(self, qtype: int, rows: int, k: int, w: np.ndarray, x: np.ndarray) -> np.ndarray:
+        w = np.ascontiguousarray(w, np.uint8).reshape(-1)
+        x = np.ascontiguousarray(x, np.float32)
+        batch = x.size // k
+        y = np.empty((batch, rows), np.float64)
+        rc = self.lib.oq_storage_matvec_f64(qtype, rows, k, _ptr(w, _u8p), _ptr(x, _f32p), batch,
+                                            _ptr(y, _f64p))
+        if rc:
+            raise ValueError(f"oq_storage_matvec_f64 failed with {rc}")
+        return y
+
+    def gemm_sampled(self, qtype: int, n: int, k: int, w: np.ndarray, x: np.ndarray,
+                     m_index: np.ndarray, n_index: np.ndarray, mode: int) -> np.ndarray:
+        w = np.ascontiguousarray(w, np.uint8).reshape(-1)
+        x = np.ascontiguousarray(x, np.float32)
+        m = x.size // k
+        order = np.lexsort((m_index, n_index))  # group by weight row for decode reuse
+        mi = np.ascontiguousarray(np.asarray(m_index, np.uint64)[order])
+        ni = np.ascontiguousarray(np.asarray(n_index, np.uint64)[order])
+        y = np.empty(len(mi), np.float64)
+        rc = self.lib.oq_gemm_sampled(qtype, n, k, _ptr(w, _u8p), m, _ptr(x, _f32p), len(mi),
+                                      _ptr(mi, _u64p), _ptr(ni, _u64p), mode, _ptr(y, _f64p))
+        if rc:
+            raise ValueError(f"oq_gemm_sampled failed with {rc}")
+        out = np.empty_like(y)
+        out[order] = y
+        return out
+
+
+class ReferenceError_(Exception):
+    """An exception the reference raised, carried across the C shim."""
+
+    KINDS = {1: "invalid_argument", 2: "out_of_range", 3: "overflow_error",
+             4: "runtime_error", 5: "logic_error", 9: "exception"}
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{self.KINDS.get(code, code)}: {message}")
+        self.code = code
+        self.kind = self.KINDS.get(code, str(code))
+        self.message = message
+
+
+class _Ref:
+    def __init__(self, path: str = REF_PATH):
+        if not os.path.exists(path):
+            build()
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} is not built and the reference tree is absent")
+        lib = C.CDLL(path)
+        cp, sz = C.c_char_p, C.c_size_t
+        lib.oref_f16_to_f32.argtypes = [C.c_uint16]
+        lib.oref_f16_to_f32.restype = C.c_float
+        lib.oref_bf16_to_f32.argtypes = [C.c_uint16]
+        lib.oref_bf16_to_f32.restype = C.c_float
+        lib.oref_type_layout.argtypes = [C.c_uint32, _u64p, _u64p, C.POINTER(C.c_int), cp, sz]
+        lib.oref_row_byte_size.argtypes = [C.c_uint64, C.c_uint32, _u64p, cp, sz]
+        lib.oref_decode_row.argtypes = [C.c_uint32, C.c_uint64, C.c_void_p, C.c_uint64, _f32p,
+                                        C.c_uint64, cp, sz]
+        lib.oref_storage_dot.argtypes = [C.c_uint32, C.c_uint64, C.c_void_p, C.c_uint64, _f32p,
+                                         C.c_uint64, _f32p, cp, sz]
+        lib.oref_storage_matvec.argtypes = [C.c_uint32, C.c_uint64, C.c_uint64, C.c_void_p,
+                                            C.c_uint64, _f32p, C.c_uint64, _f32p, C.c_uint64, cp, sz]
+        lib.oref_mapped_tensor_matvec.argtypes = [C.c_uint32, _u64p, C.c_uint64, C.c_void_p,
+                                                  C.c_uint64, _f32p, C.c_uint64, _f32p,
+                                                  C.c_uint64, cp, sz]
+        lib.oref_decode_mapped_tensor.argtypes = [C.c_uint32, _u64p, C.c_uint64, C.c_void_p,
+                                                  C.c_uint64, _f32p, C.c_uint64, cp, sz]
+        self.lib = lib
+
+    @staticmethod
+    def _check(rc: int, err) -> None:
+        if rc:
+            raise ReferenceError_(rc, err.value.decode())
+
+    def type_layout(self, qtype: int):
+        be, bb, q = C.c_uint64(), C.c_uint64(), C.c_int()
+        name = C.create_string_buffer(64)
+        if not self.lib.oref_type_layout(qtype, C.byref(be), C.byref(bb), C.byref(q), name, 64):
+            return None
+        return name.value.decode(), be.value, bb.value, bool(q.value)
+
+    def row_byte_size(self, k: int, qtype: int) -> int:
+        out, err = C.c_uint64(), C.create_string_buffer(512)
+        self._check(self.lib.oref_row_byte_size(k, qtype, C.byref(out), err, 512), err)
+        return out.value
+
+    def f16_to_f32(self, bits: int) -> float:
+        return float(self.lib.oref_f16_to_f32(bits))
+
+    def decode_row(self, qtype: int, k: int, row: np.ndarray, out_len: int | None = None) -> np.ndarray:
+        row = np.ascontiguousarray(row, np.uint8)
+        out = np.empty(k if out_len is None else out_len, np.float32)
+        err = C.create_string_buffer(512)
+        self._check(self.lib.oref_decode_row(qtype, k, row.ctypes.data, row.size,
+                                             _ptr(out, _f32p), out.size, err, 512), err)
+        return out
+
+    def storage_dot(self, qtype: int, k: int, row: np.ndarray, x: np.ndarray) -> float:
+        row = np.ascontiguousarray(row, np.uint8)
+        x = np.ascontiguousarray(x, np.float32)
+        out, err = C.c_float(), C.create_string_buffer(512)
+        self._check(self.lib.oref_storage_dot(qtype, k, row.ctypes.data, row.size,
+                                              _ptr(x, _f32p), x.size, C.byref(out), err, 512), err)
+        return out.value
+
+    def storage_matvec(self, qtype: int, rows: int, cols: int, w: np.ndarray, x: np.ndarray,
+                       y_len: int | None = None) -> np.ndarray:
+        w = np.ascontiguousarray(w, np.uint8).reshape(-1)
+        x = np.ascontiguousarray(x, np.float32).reshape(-1)
+        y = np.empty(rows if y_len is None else y_len, np.float32)
+        err = C.create_string_buffer(512)
+        self._check(self.lib.oref_storage_matvec(qtype, rows, cols, w.ctypes.data, w.size,
+                                                 _ptr(x, _f32p), x.size, _ptr(y, _f32p), y.size,
+                                                 err, 512), err)
+        return y
+
+    def mapped_tensor_matvec(self, qtype: int, dims, w: np.ndarray, x: np.ndarray,
+                             y_len: int) -> np.ndarray:
+        d = np.asarray(dims, np.uint64)
+        w = np.ascontiguousarray(w, np.uint8).reshape(-1)
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.empty(y_len, np.float32)
+        err = C.create_string_buffer(512)
+        self._check(self.lib.oref_mapped_tensor_matvec(qtype, _ptr(d, _u64p), d.size, w.ctypes.data,
+                                                       w.size, _ptr(x, _f32p), x.size,
+                                                       _ptr(y, _f32p), y.size, err, 512), err)
+        return y
+
+    def decode_mapped_tensor(self, qtype: int, dims, w: np.ndarray, out_len: int) -> np.ndarray:
+        d = np.asarray(dims, np.uint64)
+        w = np.ascontiguousarray(w, np.uint8).reshape(-1)
+        out = np.empty(out_len, np.float32)
+        err = C.create_string_buffer(512)
+        self._check(self.lib.oref_decode_mapped_tensor(qtype, _ptr(d, _u64p), d.size,
+                                                       w.ctypes.data, w.size, _ptr(out, _f32p),
+                                                       out.size, err, 512), err)
+        return out
+
+
+_port = None
+_ref = None
+
+
+def port() -> _Port:
+    global _port
+    if _port is None:
+        _port = _Port()
+    return _port
+
+
+def ref() -> _Ref:
+    global _ref
+    if _ref is None:
+        _ref = _Ref()
+    return _ref
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_PATH) or os.path.isdir(REFERENCE_TREE)

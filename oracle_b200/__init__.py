@@ -1,0 +1,323 @@
+"""B200 (sm_100a) quantized-weight path of Oracle, behind a C ABI.
+
+This package is the Python host mirror of ``include/oracle_cuda.h``.  It loads
+``liboracle_cuda.so`` (built in-tree by ``oracle_b200.build``) with ctypes and
+exposes the reference's entry points under the reference's names:
+
+=========================================  ==============================================
+reference (Oracle repository)              here
+=========================================  ==============================================
+ggml_type_layout / ggml_row_byte_size      :func:`type_layout` / :func:`row_byte_size`
+ (src/model/ggml_type.cpp:69-94)
+decode_storage_row,                        :meth:`Context.decode_rows` (device),
+ reference_decode_mapped_tensor             :meth:`Context.host_decode_rows` (host)
+ (storage_decode.cpp:244-294,
+  quantized_reference.cpp:85-105)
+reference_storage_dot (:24-82)             :meth:`Context.host_storage_dot`
+reference_storage_matvec (:128-162)        :meth:`Context.storage_matvec` (device),
+                                           :meth:`Context.host_storage_matvec` (host)
+(no counterpart) Q8_K quantizer            :meth:`Context.quantize_q8_k`
+=========================================  ==============================================
+
+Errors raise the subclass of :class:`OracleCudaError` that names the C++
+exception the reference throws for the same input, with the reference's
+message.  There is no CPU fallback: importing this package without the built
+library raises ``ImportError``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import synth  # noqa: F401  (re-exported helper module)
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle_cuda.so")
+
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K, TYPE_Q8_K, TYPE_BF16 = (
+    0, 1, 8, 12, 13, 14, 15, 30)
+CONTRACT_F32, CONTRACT_Q8K = 0, 1
+FLAG_PDL = 1
+Q8K_BLOCK_BYTES = 292
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(
+        f"{LIB_PATH} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'` "
+        "(there is no CPU fallback for this path)")
+
+_lib = C.CDLL(LIB_PATH)
+
+_vp, _u32, _u64, _i32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int
+_u64p = C.POINTER(C.c_uint64)
+
+
+def _proto(name, args, res=C.c_int):
+    fn = getattr(_lib, name)
+    fn.argtypes = args
+    fn.restype = res
+    return fn
+
+
+_proto("oracle_cuda_abi_version", [])
+_proto("oracle_cuda_status_name", [_i32], C.c_char_p)
+_proto("oracle_cuda_last_error", [_vp], C.c_char_p)
+_proto("oracle_ggml_type_layout", [_u32, _u64p, _u64p, C.POINTER(C.c_int), C.POINTER(C.c_char_p)])
+_proto("oracle_ggml_row_byte_size", [_u64, _u32, _u64p])
+_proto("oracle_cuda_create", [_i32, C.POINTER(_vp)])
+_proto("oracle_cuda_destroy", [_vp])
+_proto("oracle_cuda_set_flags", [_vp, _u32])
+_proto("oracle_cuda_device_status", [_vp])
+_proto("oracle_cuda_launch_count", [_vp], C.c_uint64)
+_proto("oracle_cuda_selftest_bounded_wait", [_vp, _u64])
+_proto("oracle_cuda_decode_rows", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp])
+_proto("oracle_cuda_quantize_q8_k", [_vp, _vp, _u64, _u64, _vp, _u64, _vp])
+_proto("oracle_cuda_storage_matvec", [_vp, _i32, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _u64, _vp])
+_proto("oracle_cuda_matvec_q8k_prequantized", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _u64, _vp])
+_proto("oracle_cuda_weight_upload", [_vp, _u32, _u64, _u64, _vp, _u64, _u64, _u64, C.POINTER(_vp)])
+_proto("oracle_cuda_weight_free", [_vp])
+_proto("oracle_cuda_weight_info", [_vp, C.POINTER(_u32), _u64p, _u64p, _u64p, C.POINTER(_vp), _u64p])
+_proto("oracle_cuda_host_storage_matvec", [_vp, _i32, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _u64])
+_proto("oracle_cuda_host_storage_dot", [_vp, _i32, _u32, _u64, _vp, _u64, _vp, _u64, _vp])
+_proto("oracle_cuda_host_decode_rows", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64])
+_proto("oracle_cuda_evict_resident", [_vp])
+
+
+class OracleCudaError(Exception):
+    """A non-OK status from the C ABI; ``status`` is the integer code."""
+
+    status = -1
+    reference_exception = "std::exception"
+
+    def __init__(self, message: str, status: int | None = None):
+        super().__init__(message)
+        if status is not None:
+            self.status = status
+
+
+class InvalidArgument(OracleCudaError, ValueError):
+    status, reference_exception = 1, "std::invalid_argument"
+
+
+class OutOfRange(OracleCudaError, IndexError):
+    status, reference_exception = 2, "std::out_of_range"
+
+
+class Overflow(OracleCudaError, OverflowError):
+    status, reference_exception = 3, "std::overflow_error"
+
+
+class RuntimeError_(OracleCudaError, RuntimeError):
+    status, reference_exception = 4, "std::runtime_error"
+
+
+class LogicError(OracleCudaError):
+    status, reference_exception = 5, "std::logic_error"
+
+
+class CudaError(OracleCudaError):
+    status = 6
+
+
+class OutOfMemory(OracleCudaError, MemoryError):
+    status = 7
+
+
+class DeviceTimeout(OracleCudaError):
+    status = 8
+
+
+class Unsupported(OracleCudaError):
+    status = 9
+
+
+_ERRORS = {c.status: c for c in (InvalidArgument, OutOfRange, Overflow, RuntimeError_, LogicError,
+                                 CudaError, OutOfMemory, DeviceTimeout, Unsupported)}
+
+
+def _raise(status: int, ctx) -> None:
+    if status == 0:
+        return
+    msg = _lib.oracle_cuda_last_error(ctx)
+    msg = msg.decode() if msg else ""
+    cls = _ERRORS.get(status, OracleCudaError)
+    raise cls(msg, status)
+
+
+def abi_version() -> int:
+    return int(_lib.oracle_cuda_abi_version())
+
+
+def type_layout(qtype: int):
+    """(name, block_elements, bytes_per_block, quantized) or None for an unknown id."""
+    be, bb, q, name = C.c_uint64(), C.c_uint64(), C.c_int(), C.c_char_p()
+    st = _lib.oracle_ggml_type_layout(qtype, C.byref(be), C.byref(bb), C.byref(q), C.byref(name))
+    if st:
+        return None
+    return name.value.decode(), be.value, bb.value, bool(q.value)
+
+
+def row_byte_size(cols: int, qtype: int) -> int:
+    out = C.c_uint64()
+    _raise(_lib.oracle_ggml_row_byte_size(cols, qtype, C.byref(out)), None)
+    return out.value
+
+
+def _addr(t) -> int:
+    """Device or host address of a torch tensor, numpy array or raw int."""
+    if t is None:
+        return 0
+    if isinstance(t, int):
+        return t
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data
+    return t.data_ptr()
+
+
+def _nbytes(t) -> int:
+    if isinstance(t, np.ndarray):
+        return t.nbytes
+    return t.numel() * t.element_size()
+
+
+def _numel(t) -> int:
+    return t.size if isinstance(t, np.ndarray) else t.numel()
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        try:
+            import torch
+            return torch.cuda.current_stream().cuda_stream
+        except Exception:  # pragma: no cover - torch without CUDA
+            return 0
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+class Weight:
+    """A weight (or a row shard of one) resident in HBM."""
+
+    def __init__(self, ctx: "Context", handle: int):
+        self._ctx = ctx
+        self._h = handle
+        t, r, c, rb, dev, nb = C.c_uint32(), C.c_uint64(), C.c_uint64(), C.c_uint64(), C.c_void_p(), C.c_uint64()
+        _raise(_lib.oracle_cuda_weight_info(handle, C.byref(t), C.byref(r), C.byref(c), C.byref(rb),
+                                            C.byref(dev), C.byref(nb)), None)
+        self.type, self.rows, self.cols = t.value, r.value, c.value
+        self.row_begin, self.dev, self.nbytes = rb.value, dev.value, nb.value
+
+    def free(self) -> None:
+        if self._h:
+            _lib.oracle_cuda_weight_free(self._h)
+            self._h = 0
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Context:
+    """One library context on one CUDA device (oracle_cuda_create)."""
+
+    def __init__(self, device: int = 0, flags: int = 0):
+        h = C.c_void_p()
+        _raise(_lib.oracle_cuda_create(device, C.byref(h)), None)
+        self._h = h.value
+        self.device = device
+        if flags:
+            self.set_flags(flags)
+
+    # -------------------------------------------------------------- lifecycle
+    def close(self) -> None:
+        if self._h:
+            _lib.oracle_cuda_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _check(self, status: int) -> None:
+        _raise(status, self._h)
+
+    def set_flags(self, flags: int) -> None:
+        self._check(_lib.oracle_cuda_set_flags(self._h, flags))
+
+    def device_status(self) -> None:
+        """Raise DeviceTimeout if any kernel's bounded wait expired."""
+        self._check(_lib.oracle_cuda_device_status(self._h))
+
+    def selftest_bounded_wait(self, limit_ns: int) -> None:
+        self._check(_lib.oracle_cuda_selftest_bounded_wait(self._h, limit_ns))
+
+    def launch_count(self) -> int:
+        return int(_lib.oracle_cuda_launch_count(self._h))
+
+    # -------------------------------------------------------------- device-pointer path
+    def decode_rows(self, qtype, rows, cols, w, out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_decode_rows(self._h, qtype, rows, cols, _addr(w), _nbytes(w), _addr(out),
+                                                 _numel(out), _stream(stream)))
+
+    def quantize_q8_k(self, x, cols, batch, q8k, stream=None) -> None:
+        self._check(_lib.oracle_cuda_quantize_q8_k(self._h, _addr(x), cols, batch, _addr(q8k), _nbytes(q8k),
+                                                   _stream(stream)))
+
+    def storage_matvec(self, contract, qtype, rows, cols, w, x, y, stream=None, w_nbytes=None) -> None:
+        self._check(_lib.oracle_cuda_storage_matvec(
+            self._h, contract, qtype, rows, cols, _addr(w), _nbytes(w) if w_nbytes is None else w_nbytes,
+            _addr(x), _numel(x), _addr(y), _numel(y), _stream(stream)))
+
+    def matvec_q8k_prequantized(self, qtype, rows, cols, w, q8k, y, stream=None) -> None:
+        self._check(_lib.oracle_cuda_matvec_q8k_prequantized(
+            self._h, qtype, rows, cols, _addr(w), _nbytes(w), _addr(q8k), _nbytes(q8k), _addr(y), _numel(y),
+            _stream(stream)))
+
+    # -------------------------------------------------------------- resident weights
+    def upload(self, qtype, rows, cols, host: np.ndarray, row_begin=0, row_end=None) -> Weight:
+        host = np.ascontiguousarray(host, np.uint8)
+        h = C.c_void_p()
+        self._check(_lib.oracle_cuda_weight_upload(self._h, qtype, rows, cols, host.ctypes.data, host.nbytes,
+                                                   row_begin, rows if row_end is None else row_end, C.byref(h)))
+        return Weight(self, h.value)
+
+    def matvec_weight(self, contract, weight: Weight, x, y, stream=None) -> None:
+        self.storage_matvec(contract, weight.type, weight.rows, weight.cols, weight.dev, x, y, stream,
+                            w_nbytes=weight.nbytes)
+
+    # -------------------------------------------------------------- host drop-ins
+    def host_storage_matvec(self, contract, qtype, rows, cols, w: np.ndarray, x: np.ndarray,
+                            y: np.ndarray | None = None) -> np.ndarray:
+        w = np.ascontiguousarray(w, np.uint8)
+        x = np.ascontiguousarray(x, np.float32)
+        batch = max(1, x.size // cols) if cols else 1
+        if y is None:
+            y = np.empty(rows * batch, np.float32)
+        self._check(_lib.oracle_cuda_host_storage_matvec(self._h, contract, qtype, rows, cols, w.ctypes.data,
+                                                         w.nbytes, x.ctypes.data, x.size, y.ctypes.data, y.size))
+        return y
+
+    def host_storage_dot(self, contract, qtype, cols, row: np.ndarray, x: np.ndarray) -> float:
+        row = np.ascontiguousarray(row, np.uint8)
+        x = np.ascontiguousarray(x, np.float32)
+        out = C.c_float()
+        self._check(_lib.oracle_cuda_host_storage_dot(self._h, contract, qtype, cols, row.ctypes.data, row.nbytes,
+                                                      x.ctypes.data, x.size, C.byref(out)))
+        return out.value
+
+    def host_decode_rows(self, qtype, rows, cols, w: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        w = np.ascontiguousarray(w, np.uint8)
+        if out is None:
+            out = np.empty(rows * cols, np.float32)
+        self._check(_lib.oracle_cuda_host_decode_rows(self._h, qtype, rows, cols, w.ctypes.data, w.nbytes,
+                                                      out.ctypes.data, out.size))
+        return out
+
+    def evict_resident(self) -> None:
+        self._check(_lib.oracle_cuda_evict_resident(self._h))

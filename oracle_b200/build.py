@@ -1,0 +1,65 @@
+"""Build recipe for the in-tree native libraries.
+
+* ``oracle_b200/liboracle_cuda.so`` -- the product: CUDA kernels for sm_100a
+  plus the C ABI of ``include/oracle_cuda.h``, built by nvcc with
+  ``-gencode arch=compute_100a,code=sm_100a`` (cudart linked statically).
+* ``oracle/liboracle_port.so`` and ``oracle/_ref/liboracle_ref.so`` -- the CPU
+  checkers used by the tests (``oracle/Makefile``); the second one only where
+  the reference tree exists.
+
+This file is loaded by path (``__graft_entry__.build``, ``tests/conftest.py``)
+so that it runs before the package's library exists.
+"""
+from __future__ import annotations
+
+import glob
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB = os.path.join(HERE, "liboracle_cuda.so")
+CSRC = os.path.join(HERE, "csrc")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+REFERENCE_TREE = "/root/reference"
+
+
+def _sources():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cuh"))) + \
+        sorted(glob.glob(os.path.join(CSRC, "*.hpp"))) + [os.path.join(ROOT, "include", "oracle_cuda.h")]
+
+
+def _stale(target: str, deps) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+
+
+def build_cuda(force: bool = False, verbose: bool = False) -> str:
+    if force or _stale(LIB, _sources()):
+        cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
+               "-o", LIB, os.path.join(CSRC, "oracle_cuda.cu")]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+        subprocess.run(cmd, check=True)
+    return LIB
+
+
+def build_oracle() -> None:
+    targets = ["port"]
+    if os.path.isdir(REFERENCE_TREE):
+        targets.append("ref")
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={REFERENCE_TREE}", *targets],
+                   check=True)
+
+
+def build_all(force: bool = False) -> None:
+    build_cuda(force=force)
+    build_oracle()
+
+
+if __name__ == "__main__":
+    build_all(force="--force" in sys.argv)

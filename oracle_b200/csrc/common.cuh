@@ -1,0 +1,153 @@
+// common.cuh -- device helpers shared by the quantized-path kernels (sm_100a).
+//
+// PTX wrappers for mbarriers and 1-D bulk async copies (the non-tensor TMA
+// path: cp.async.bulk global -> shared, completion counted in bytes on an
+// mbarrier), a bounded wait that never spins forever, and little-endian
+// field readers for GGML blocks held in shared memory.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace oracle_cuda {
+
+// Device-side status word.  Kernels never trap: a wait that runs past its
+// deadline records (code, where) here and the kernel returns early.  The host
+// reads it after synchronising (oracle_cuda_device_status).
+struct DeviceStatus {
+    unsigned int code;   // 0 ok, 1 wait timeout
+    unsigned int where;  // kernel-specific site id
+    unsigned int block;  // blockIdx.x that reported first
+    unsigned int pad;
+};
+
+enum : unsigned int { kDevOk = 0, kDevTimeout = 1 };
+
+// Deadline for any single wait: one second of %globaltimer.
+constexpr unsigned long long kWaitNs = 1000000000ull;
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void report_timeout(DeviceStatus* st, unsigned int where) {
+    if (st && atomicCAS(&st->code, kDevOk, kDevTimeout) == kDevOk) {
+        st->where = where;
+        st->block = blockIdx.x;
+    }
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Wait for the phase with the given parity to complete.  Returns false (and
+// records a timeout) if it has not completed within kWaitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, DeviceStatus* st,
+                                          unsigned int where, unsigned long long limit_ns = kWaitNs) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_timer_ns();
+#pragma unroll 1
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_timer_ns() - t0 > limit_ns) {
+            report_timeout(st, where);
+            return false;
+        }
+    }
+}
+
+// 1-D bulk copy global -> this CTA's shared memory.  dst and src must be
+// 16-byte aligned and bytes a positive multiple of 16.  Completion is signalled
+// as transaction bytes on `bar`.  The L2 policy marks the weight stream
+// evict-first: every packed weight byte is read exactly once per call.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+// Self-test of the bounded wait: one thread waits on a barrier that expects
+// an arrival nobody makes.  The wait must give up after `limit_ns`, record a
+// timeout in the status word and let the kernel finish normally.
+__global__ void bounded_wait_selftest_kernel(DeviceStatus* st, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_wait(&bar, 0, st, 99, limit_ns);
+    }
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------- block fields
+
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {
+    return __half2float(__ushort_as_half(h));  // exact, subnormals included
+}
+
+// Four little-endian bytes starting at an even shared-memory address.
+__device__ __forceinline__ uint32_t lds_u32_even(const uint8_t* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    if ((a & 3u) == 0) return *reinterpret_cast<const uint32_t*>(p);
+    const uint32_t* base = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+    return __funnelshift_r(base[0], base[1], 16);
+}
+
+__device__ __forceinline__ uint16_t lds_u16(const uint8_t* p) {
+    return *reinterpret_cast<const uint16_t*>(p);
+}
+
+// Sign-extended byte i (0..3) of a word.
+__device__ __forceinline__ int sbyte(uint32_t w, int i) {
+    return static_cast<int>(static_cast<int8_t>((w >> (8 * i)) & 0xFFu));
+}
+
+}  // namespace oracle_cuda

@@ -1,0 +1,734 @@
+// oracle_cuda.cu -- C ABI over the sm_100a kernels of the quantized-weight path.
+//
+// Host-side validation restates the reference's checks in its order and with
+// its messages (quantized_reference.cpp:128-153, storage_decode.cpp:182-198,
+// ggml_type.cpp:77-94), so the status code names the exception class the
+// reference would throw.  Nothing is launched unless validation passes.
+#include "../../include/oracle_cuda.h"
+
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <set>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "layout.hpp"
+#include "matvec_f32.cuh"
+#include "matvec_q8k.cuh"
+#include "q8k.cuh"
+
+using namespace oracle_cuda;
+
+struct oracle_cuda_weight {
+    oracle_cuda_context* ctx;
+    uint32_t type;
+    uint64_t rows;       // rows held (the shard)
+    uint64_t cols;
+    uint64_t row_begin;  // first global row of the shard
+    uint64_t nbytes;
+    void* dev;
+    bool owned_by_cache;
+};
+
+struct oracle_cuda_context {
+    int device = 0;
+    int sm_count = 0;
+    int max_smem_optin = 0;
+    uint32_t flags = 0;
+    uint64_t launches = 0;
+    DeviceStatus* status = nullptr;
+    std::string last_error;
+    std::set<const void*> smem_configured;
+    // resident copies for the host-pointer drop-ins
+    std::map<std::tuple<const void*, uint64_t, uint32_t, uint64_t, uint64_t>, oracle_cuda_weight*> resident;
+    // staging for the host-pointer drop-ins (grown on demand)
+    float* pin_x = nullptr;
+    float* pin_y = nullptr;
+    uint64_t pin_x_len = 0, pin_y_len = 0;
+    float* dev_x = nullptr;
+    float* dev_y = nullptr;
+    uint64_t dev_x_len = 0, dev_y_len = 0;
+};
+
+namespace {
+
+thread_local std::string g_thread_error;
+
+oracle_cuda_status fail(oracle_cuda_context* ctx, oracle_cuda_status s, const std::string& msg) {
+    if (ctx)
+        ctx->last_error = msg;
+    else
+        g_thread_error = msg;
+    return s;
+}
+
+oracle_cuda_status fail(oracle_cuda_context* ctx, const Error& e) {
+    return fail(ctx, static_cast<oracle_cuda_status>(static_cast<int>(e.kind)), e.message);
+}
+
+oracle_cuda_status cuda_fail(oracle_cuda_context* ctx, cudaError_t err, const char* what) {
+    return fail(ctx, err == cudaErrorMemoryAllocation ? ORACLE_CUDA_OUT_OF_MEMORY : ORACLE_CUDA_CUDA_ERROR,
+                std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+#define ORACLE_CUDA_TRY(ctx, call, what)                  \
+    do {                                                  \
+        cudaError_t _e = (call);                          \
+        if (_e != cudaSuccess) return cuda_fail(ctx, _e, what); \
+    } while (0)
+
+oracle_cuda_status ok(oracle_cuda_context* ctx) {
+    if (ctx) ctx->last_error.clear();
+    return ORACLE_CUDA_OK;
+}
+
+// The reference's row-view type gate (storage_decode.cpp:192-196), widened by q4_K.
+Error check_decodable(uint32_t type) {
+    if (!decodable(type))
+        return make_error(ErrorKind::InvalidArgument,
+                          "storage decoder does not support GGML type " + std::to_string(type));
+    return {};
+}
+
+// Pointer alignment the kernels rely on: 16 bytes for q4_K/q5_K (vector loads
+// of 16-byte aligned super-blocks), 4 for f32, 2 otherwise.
+Error check_weight_pointer(uint32_t type, const void* p) {
+    if (!p) return make_error(ErrorKind::InvalidArgument, "weight pointer is null");
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uintptr_t need = (type == kTypeQ4_K || type == kTypeQ5_K) ? 16 : type == kTypeF32 ? 4 : 2;
+    if (a % need)
+        return make_error(ErrorKind::InvalidArgument,
+                          "weight pointer must be " + std::to_string(need) + "-byte aligned for GGML type " +
+                              std::to_string(type));
+    return {};
+}
+
+// reference_storage_matvec's validation (quantized_reference.cpp:134-153),
+// generalised to `batch` activation vectors, plus the per-row type gate.
+Error check_matvec(uint32_t type, uint64_t rows, uint64_t cols, uint64_t w_nbytes, uint64_t x_len,
+                   uint64_t y_len, uint64_t* row_bytes, uint64_t* batch) {
+    if (rows == 0 || cols == 0)
+        return make_error(ErrorKind::InvalidArgument, "reference matvec dimensions must be non-zero");
+    if (x_len == 0 || x_len % cols != 0)
+        return make_error(ErrorKind::InvalidArgument, "reference matvec vector length mismatch");
+    *batch = x_len / cols;
+    uint64_t expect_y;
+    if (!checked_mul(rows, *batch, &expect_y) || y_len != expect_y)
+        return make_error(ErrorKind::InvalidArgument, "reference matvec output length mismatch");
+    if (Error e = row_byte_size(cols, type, row_bytes)) return e;
+    uint64_t total;
+    if (!checked_mul(rows, *row_bytes, &total))
+        return make_error(ErrorKind::Overflow, "reference matvec matrix size overflow");
+    if (w_nbytes != total)
+        return make_error(ErrorKind::InvalidArgument, "reference matvec matrix byte size mismatch");
+    return check_decodable(type);
+}
+
+// ---------------------------------------------------------------- launches
+
+template <typename Kernel, typename... Args>
+oracle_cuda_status launch(oracle_cuda_context* ctx, Kernel kernel, dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, bool pdl, Args... args) {
+    const void* key = reinterpret_cast<const void*>(kernel);
+    if (smem > 48 * 1024 && !ctx->smem_configured.count(key)) {
+        ORACLE_CUDA_TRY(ctx,
+                        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             ctx->max_smem_optin),
+                        "cudaFuncSetAttribute");
+        ctx->smem_configured.insert(key);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    ORACLE_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kernel, args...), "kernel launch");
+    ctx->launches += 1;
+    return ORACLE_CUDA_OK;
+}
+
+// Stage plan for the row-streaming kernels: about 24 KB per stage (at most one
+// row per consumer warp), as many stages as shared memory allows (<= 16).
+bool plan_stream(oracle_cuda_context* ctx, uint64_t rows, uint64_t row_bytes, uint32_t act_bytes, int ncw,
+                 StreamParams& sp, uint32_t& grid) {
+    grid = static_cast<uint32_t>(rows < uint64_t(ctx->sm_count) ? rows : ctx->sm_count);
+    const uint64_t budget = uint64_t(ctx->max_smem_optin) - stream_barrier_bytes(16) - act_bytes;
+    uint64_t R = 24576 / row_bytes;
+    if (R < 1) R = 1;
+    if (R > uint64_t(ncw)) R = ncw;
+    uint64_t stage = align_up(static_cast<uint32_t>(R * row_bytes + 32), 128u);
+    while (R > 1 && stage * 2 > budget) {
+        R -= 1;
+        stage = align_up(static_cast<uint32_t>(R * row_bytes + 32), 128u);
+    }
+    if (row_bytes + 32 > (1u << 30) || stage * 2 > budget) return false;
+    const uint64_t rows_per_cta = (rows + grid - 1) / grid;
+    const uint64_t tmax = (rows_per_cta + R - 1) / R;
+    uint64_t S = budget / stage;
+    if (S > 16) S = 16;
+    if (S > tmax) S = tmax < 1 ? 1 : tmax;
+    sp.rows = rows;
+    sp.row_bytes = row_bytes;
+    sp.rows_per_stage = static_cast<uint32_t>(R);
+    sp.stages = static_cast<uint32_t>(S);
+    sp.stage_bytes = static_cast<uint32_t>(stage);
+    sp.act_bytes = act_bytes;
+    sp.status = ctx->status;
+    return true;
+}
+
+constexpr int kConsumerWarps = 8;
+
+template <class Consumer>
+oracle_cuda_status launch_stream(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t row_bytes,
+                                 uint32_t act_bytes, const typename Consumer::Params& cp, cudaStream_t stream) {
+    StreamParams sp{};
+    uint32_t grid = 0;
+    if (!plan_stream(ctx, rows, row_bytes, act_bytes, Consumer::kWarps, sp, grid))
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "weight rows too long for the shared-memory stage ring");
+    sp.w = w;
+    const size_t smem = stream_smem_bytes(sp);
+    return launch(ctx, stream_rows_kernel<Consumer>, dim3(grid), dim3((Consumer::kWarps + 1) * 32), smem,
+                  stream, (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, sp, cp);
+}
+
+template <uint32_t kType>
+oracle_cuda_status launch_q8k_typed(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t row_bytes,
+                                    const MatvecQ8KParams& cp, cudaStream_t stream) {
+    const uint32_t passes = (cp.nb + 15) / 16;
+    const uint32_t act = q8k_image_bytes(cp.nb);
+    switch (passes) {
+        case 1: return launch_stream<MatvecQ8KConsumer<kType, 1, kConsumerWarps>>(ctx, w, rows, row_bytes, act, cp, stream);
+        case 2: return launch_stream<MatvecQ8KConsumer<kType, 2, kConsumerWarps>>(ctx, w, rows, row_bytes, act, cp, stream);
+        case 3: return launch_stream<MatvecQ8KConsumer<kType, 3, kConsumerWarps>>(ctx, w, rows, row_bytes, act, cp, stream);
+        case 4: return launch_stream<MatvecQ8KConsumer<kType, 4, kConsumerWarps>>(ctx, w, rows, row_bytes, act, cp, stream);
+        default:
+            return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "Q8_K matvec supports rows of at most 16384 elements");
+    }
+}
+
+// Q8_K contract, one activation vector per launch (x f32 or pre-quantized).
+oracle_cuda_status launch_q8k(oracle_cuda_context* ctx, uint32_t type, const void* w, uint64_t rows, uint64_t cols,
+                              uint64_t row_bytes, const float* x, const uint8_t* q8k, float* y, cudaStream_t stream) {
+    MatvecQ8KParams cp{};
+    cp.x = x;
+    cp.q8k = q8k;
+    cp.y = y;
+    cp.rows = rows;
+    cp.nb = static_cast<uint32_t>(cols / 256);
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    if (type == kTypeQ4_K) return launch_q8k_typed<12>(ctx, wb, rows, row_bytes, cp, stream);
+    return launch_q8k_typed<14>(ctx, wb, rows, row_bytes, cp, stream);
+}
+
+template <uint32_t kType>
+oracle_cuda_status launch_f32_typed(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t row_bytes,
+                                    const MatvecF32Params& cp, cudaStream_t stream) {
+    return launch_stream<MatvecF32Consumer<kType, kConsumerWarps>>(ctx, w, rows, row_bytes,
+                                                                   f32_image_bytes(cp.kpad, cp.batch), cp, stream);
+}
+
+constexpr uint32_t kF32ImageMax = 128 * 1024;
+
+oracle_cuda_status launch_f32(oracle_cuda_context* ctx, uint32_t type, const void* w, uint64_t rows, uint64_t cols,
+                              uint64_t row_bytes, const float* x, uint64_t batch, float* y, cudaStream_t stream) {
+    const uint32_t kpad = align_up(static_cast<uint32_t>(cols), 128u);
+    if (uint64_t(kpad) * 4 > kF32ImageMax)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "f32-contract matvec supports rows of at most 32768 elements");
+    const uint64_t chunk = kF32ImageMax / (uint64_t(kpad) * 4);
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    for (uint64_t b0 = 0; b0 < batch; b0 += chunk) {
+        MatvecF32Params cp{};
+        cp.x = x + b0 * cols;
+        cp.y = y + b0 * rows;
+        cp.rows = rows;
+        cp.k = static_cast<uint32_t>(cols);
+        cp.kpad = kpad;
+        cp.batch = static_cast<uint32_t>(batch - b0 < chunk ? batch - b0 : chunk);
+        oracle_cuda_status s;
+        switch (type) {
+            case kTypeF32: s = launch_f32_typed<0>(ctx, wb, rows, row_bytes, cp, stream); break;
+            case kTypeF16: s = launch_f32_typed<1>(ctx, wb, rows, row_bytes, cp, stream); break;
+            case kTypeBF16: s = launch_f32_typed<30>(ctx, wb, rows, row_bytes, cp, stream); break;
+            case kTypeQ8_0: s = launch_f32_typed<8>(ctx, wb, rows, row_bytes, cp, stream); break;
+            case kTypeQ4_K: s = launch_f32_typed<12>(ctx, wb, rows, row_bytes, cp, stream); break;
+            case kTypeQ5_K: s = launch_f32_typed<13>(ctx, wb, rows, row_bytes, cp, stream); break;
+            case kTypeQ6_K: s = launch_f32_typed<14>(ctx, wb, rows, row_bytes, cp, stream); break;
+            default: return fail(ctx, check_decodable(type));
+        }
+        if (s != ORACLE_CUDA_OK) return s;
+    }
+    return ORACLE_CUDA_OK;
+}
+
+template <uint32_t kType>
+oracle_cuda_status launch_decode_typed(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t cols,
+                                       uint64_t row_bytes, float* out, cudaStream_t stream) {
+    const uint64_t total = rows * ((cols + 3) / 4);
+    uint64_t blocks = (total + 255) / 256;
+    const uint64_t cap = uint64_t(ctx->sm_count) * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return launch(ctx, decode_rows_kernel<kType>, dim3(static_cast<uint32_t>(blocks)), dim3(256), 0, stream, false, w,
+                  rows, static_cast<uint32_t>(cols), row_bytes, out);
+}
+
+oracle_cuda_status launch_decode(oracle_cuda_context* ctx, uint32_t type, const void* w, uint64_t rows, uint64_t cols,
+                                 uint64_t row_bytes, float* out, cudaStream_t stream) {
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    switch (type) {
+        case kTypeF32: return launch_decode_typed<0>(ctx, wb, rows, cols, row_bytes, out, stream);
+        case kTypeF16: return launch_decode_typed<1>(ctx, wb, rows, cols, row_bytes, out, stream);
+        case kTypeBF16: return launch_decode_typed<30>(ctx, wb, rows, cols, row_bytes, out, stream);
+        case kTypeQ8_0: return launch_decode_typed<8>(ctx, wb, rows, cols, row_bytes, out, stream);
+        case kTypeQ4_K: return launch_decode_typed<12>(ctx, wb, rows, cols, row_bytes, out, stream);
+        case kTypeQ5_K: return launch_decode_typed<13>(ctx, wb, rows, cols, row_bytes, out, stream);
+        case kTypeQ6_K: return launch_decode_typed<14>(ctx, wb, rows, cols, row_bytes, out, stream);
+        default: return fail(ctx, check_decodable(type));
+    }
+}
+
+// Validation shared by the device and host matvec entry points.
+oracle_cuda_status validate_matvec(oracle_cuda_context* ctx, int contract, uint32_t type, uint64_t rows, uint64_t cols,
+                                   uint64_t w_nbytes, uint64_t x_len, uint64_t y_len, uint64_t* row_bytes,
+                                   uint64_t* batch) {
+    if (contract != ORACLE_CUDA_CONTRACT_F32 && contract != ORACLE_CUDA_CONTRACT_Q8K)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "unknown arithmetic contract " + std::to_string(contract));
+    if (Error e = check_matvec(type, rows, cols, w_nbytes, x_len, y_len, row_bytes, batch)) return fail(ctx, e);
+    if (contract == ORACLE_CUDA_CONTRACT_Q8K && !q8k_dot_type(type))
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED,
+                    "Q8_K integer dot supports q4_K and q6_K weights, not GGML type " + std::to_string(type));
+    return ORACLE_CUDA_OK;
+}
+
+oracle_cuda_status run_matvec(oracle_cuda_context* ctx, int contract, uint32_t type, uint64_t rows, uint64_t cols,
+                              uint64_t row_bytes, const void* w, const float* x, uint64_t batch, float* y,
+                              cudaStream_t stream) {
+    if (contract == ORACLE_CUDA_CONTRACT_F32) return launch_f32(ctx, type, w, rows, cols, row_bytes, x, batch, y, stream);
+    for (uint64_t b = 0; b < batch; ++b) {
+        oracle_cuda_status s = launch_q8k(ctx, type, w, rows, cols, row_bytes, x + b * cols, nullptr, y + b * rows, stream);
+        if (s != ORACLE_CUDA_OK) return s;
+    }
+    return ORACLE_CUDA_OK;
+}
+
+template <typename T>
+oracle_cuda_status grow_pinned(oracle_cuda_context* ctx, T*& p, uint64_t& have, uint64_t need) {
+    if (have >= need) return ORACLE_CUDA_OK;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    have = 0;
+    ORACLE_CUDA_TRY(ctx, cudaHostAlloc(reinterpret_cast<void**>(&p), need * sizeof(T), cudaHostAllocDefault),
+                    "cudaHostAlloc");
+    have = need;
+    return ORACLE_CUDA_OK;
+}
+
+template <typename T>
+oracle_cuda_status grow_device(oracle_cuda_context* ctx, T*& p, uint64_t& have, uint64_t need) {
+    if (have >= need) return ORACLE_CUDA_OK;
+    if (p) cudaFree(p);
+    p = nullptr;
+    have = 0;
+    ORACLE_CUDA_TRY(ctx, cudaMalloc(reinterpret_cast<void**>(&p), need * sizeof(T)), "cudaMalloc");
+    have = need;
+    return ORACLE_CUDA_OK;
+}
+
+oracle_cuda_status resident_weight(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
+                                   const void* host, uint64_t nbytes, oracle_cuda_weight** out) {
+    auto key = std::make_tuple(host, nbytes, type, rows, cols);
+    auto it = ctx->resident.find(key);
+    if (it != ctx->resident.end()) {
+        *out = it->second;
+        return ORACLE_CUDA_OK;
+    }
+    oracle_cuda_weight* w = nullptr;
+    oracle_cuda_status s = oracle_cuda_weight_upload(ctx, type, rows, cols, host, nbytes, 0, rows, &w);
+    if (s != ORACLE_CUDA_OK) return s;
+    w->owned_by_cache = true;
+    ctx->resident[key] = w;
+    *out = w;
+    return ORACLE_CUDA_OK;
+}
+
+bool is_pinned(const void* p) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return attr.type == cudaMemoryTypeHost;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+
+extern "C" {
+
+int oracle_cuda_abi_version(void) { return ORACLE_CUDA_ABI_VERSION; }
+
+const char* oracle_cuda_status_name(oracle_cuda_status s) {
+    switch (s) {
+        case ORACLE_CUDA_OK: return "OK";
+        case ORACLE_CUDA_INVALID_ARGUMENT: return "INVALID_ARGUMENT";
+        case ORACLE_CUDA_OUT_OF_RANGE: return "OUT_OF_RANGE";
+        case ORACLE_CUDA_OVERFLOW: return "OVERFLOW";
+        case ORACLE_CUDA_RUNTIME_ERROR: return "RUNTIME_ERROR";
+        case ORACLE_CUDA_LOGIC_ERROR: return "LOGIC_ERROR";
+        case ORACLE_CUDA_CUDA_ERROR: return "CUDA_ERROR";
+        case ORACLE_CUDA_OUT_OF_MEMORY: return "OUT_OF_MEMORY";
+        case ORACLE_CUDA_DEVICE_TIMEOUT: return "DEVICE_TIMEOUT";
+        case ORACLE_CUDA_UNSUPPORTED: return "UNSUPPORTED";
+    }
+    return "UNKNOWN";
+}
+
+const char* oracle_cuda_last_error(const oracle_cuda_context* ctx) {
+    return ctx ? ctx->last_error.c_str() : g_thread_error.c_str();
+}
+
+oracle_cuda_status oracle_ggml_type_layout(uint32_t type, uint64_t* block_elements, uint64_t* bytes_per_block,
+                                           int* quantized, const char** name) {
+    const TypeLayout* l = type_layout(type);
+    if (!l) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "unsupported GGML tensor type: " + std::to_string(type));
+    if (block_elements) *block_elements = l->block_elements;
+    if (bytes_per_block) *bytes_per_block = l->bytes_per_block;
+    if (quantized) *quantized = l->quantized ? 1 : 0;
+    if (name) *name = l->name;
+    return ORACLE_CUDA_OK;
+}
+
+oracle_cuda_status oracle_ggml_row_byte_size(uint64_t row_elements, uint32_t type, uint64_t* out) {
+    if (!out) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "output pointer is null");
+    if (Error e = row_byte_size(row_elements, type, out)) return fail(nullptr, e);
+    return ORACLE_CUDA_OK;
+}
+
+oracle_cuda_status oracle_cuda_create(int device, oracle_cuda_context** out) {
+    if (!out) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "output pointer is null");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDeviceCount");
+    if (device < 0 || device >= count)
+        return fail(nullptr, ORACLE_CUDA_OUT_OF_RANGE, "CUDA device index " + std::to_string(device) + " out of range");
+    if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(nullptr, e, "cudaSetDevice");
+    cudaDeviceProp prop{};
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess)
+        return cuda_fail(nullptr, e, "cudaGetDeviceProperties");
+    if (prop.major != 10)
+        return fail(nullptr, ORACLE_CUDA_UNSUPPORTED,
+                    std::string("this library is built for sm_100a (B200); device is ") + prop.name);
+    auto* ctx = new oracle_cuda_context();
+    ctx->device = device;
+    ctx->sm_count = prop.multiProcessorCount;
+    ctx->max_smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+    if ((e = cudaMalloc(reinterpret_cast<void**>(&ctx->status), sizeof(DeviceStatus))) != cudaSuccess) {
+        delete ctx;
+        return cuda_fail(nullptr, e, "cudaMalloc(status)");
+    }
+    cudaMemset(ctx->status, 0, sizeof(DeviceStatus));
+    *out = ctx;
+    return ORACLE_CUDA_OK;
+}
+
+oracle_cuda_status oracle_cuda_destroy(oracle_cuda_context* ctx) {
+    if (!ctx) return ORACLE_CUDA_OK;
+    cudaSetDevice(ctx->device);
+    cudaDeviceSynchronize();
+    for (auto& kv : ctx->resident) {
+        cudaFree(kv.second->dev);
+        delete kv.second;
+    }
+    if (ctx->pin_x) cudaFreeHost(ctx->pin_x);
+    if (ctx->pin_y) cudaFreeHost(ctx->pin_y);
+    if (ctx->dev_x) cudaFree(ctx->dev_x);
+    if (ctx->dev_y) cudaFree(ctx->dev_y);
+    if (ctx->status) cudaFree(ctx->status);
+    delete ctx;
+    return ORACLE_CUDA_OK;
+}
+
+oracle_cuda_status oracle_cuda_set_flags(oracle_cuda_context* ctx, uint32_t flags) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    ctx->flags = flags;
+    return ok(ctx);
+}
+
+uint64_t oracle_cuda_launch_count(const oracle_cuda_context* ctx) { return ctx ? ctx->launches : 0; }
+
+oracle_cuda_status oracle_cuda_device_status(oracle_cuda_context* ctx) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    DeviceStatus st{};
+    ORACLE_CUDA_TRY(ctx, cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    ORACLE_CUDA_TRY(ctx, cudaMemcpy(&st, ctx->status, sizeof st, cudaMemcpyDeviceToHost), "cudaMemcpy(status)");
+    ORACLE_CUDA_TRY(ctx, cudaMemset(ctx->status, 0, sizeof st), "cudaMemset(status)");
+    if (st.code != kDevOk)
+        return fail(ctx, ORACLE_CUDA_DEVICE_TIMEOUT,
+                    "kernel wait timed out at site " + std::to_string(st.where) + " in block " +
+                        std::to_string(st.block));
+    return ok(ctx);
+}
+
+oracle_cuda_status oracle_cuda_selftest_bounded_wait(oracle_cuda_context* ctx, uint64_t limit_ns) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (limit_ns == 0 || limit_ns > 2000000000ull)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "self-test deadline must be in (0, 2 s]");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    oracle_cuda_status s = launch(ctx, bounded_wait_selftest_kernel, dim3(1), dim3(32), 0, nullptr, false,
+                                  ctx->status, static_cast<unsigned long long>(limit_ns));
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+oracle_cuda_status oracle_cuda_decode_rows(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
+                                           const void* w_dev, uint64_t w_nbytes, float* out_dev, uint64_t out_len,
+                                           void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    uint64_t rb = 0, total = 0, elems = 0;
+    if (rows == 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "GGUF tensor must have at least one dimension");
+    if (Error e = row_byte_size(cols, type, &rb)) return fail(ctx, e);
+    if (!checked_mul(rows, rb, &total))
+        return fail(ctx, ORACLE_CUDA_OVERFLOW, "GGUF tensor byte size exceeds addressable size");
+    if (w_nbytes != total)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "GGUF tensor byte size does not match row geometry");
+    if (Error e = check_decodable(type)) return fail(ctx, e);
+    if (!checked_mul(rows, cols, &elems))
+        return fail(ctx, ORACLE_CUDA_OVERFLOW, "mapped tensor element count overflow");
+    if (out_len != elems)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "mapped tensor decode output length mismatch");
+    if (cols > 0xFFFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "rows longer than 2^32 elements");
+    if (Error e = check_weight_pointer(type, w_dev)) return fail(ctx, e);
+    if (!out_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "output pointer is null");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    oracle_cuda_status s = launch_decode(ctx, type, w_dev, rows, cols, rb, out_dev, static_cast<cudaStream_t>(stream));
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+oracle_cuda_status oracle_cuda_quantize_q8_k(oracle_cuda_context* ctx, const float* x_dev, uint64_t cols,
+                                             uint64_t batch, void* q8k_dev, uint64_t q8k_nbytes, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (cols == 0 || batch == 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Q8_K quantize dimensions must be non-zero");
+    uint64_t rb = 0;
+    if (Error e = row_byte_size(cols, kTypeQ8_K, &rb)) return fail(ctx, e);
+    uint64_t need = 0;
+    if (!checked_mul(rb, batch, &need)) return fail(ctx, ORACLE_CUDA_OVERFLOW, "Q8_K output size overflow");
+    if (q8k_nbytes != need) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Q8_K output byte size mismatch");
+    if (!x_dev || !q8k_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (reinterpret_cast<uintptr_t>(x_dev) % 4 || reinterpret_cast<uintptr_t>(q8k_dev) % 4)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Q8_K buffers must be 4-byte aligned");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const uint64_t blocks = (cols / 256) * batch;
+    const uint64_t grid = (blocks * 32 + 255) / 256;
+    if (grid > 0x7FFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "too many Q8_K blocks for one launch");
+    oracle_cuda_status s = launch(ctx, quantize_q8k_kernel, dim3(static_cast<uint32_t>(grid)), dim3(256), 0,
+                                  static_cast<cudaStream_t>(stream), false, x_dev, cols, batch,
+                                  static_cast<uint8_t*>(q8k_dev));
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+oracle_cuda_status oracle_cuda_storage_matvec(oracle_cuda_context* ctx, int contract, uint32_t type, uint64_t rows,
+                                              uint64_t cols, const void* w_dev, uint64_t w_nbytes, const float* x_dev,
+                                              uint64_t x_len, float* y_dev, uint64_t y_len, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    uint64_t rb = 0, batch = 0;
+    oracle_cuda_status s = validate_matvec(ctx, contract, type, rows, cols, w_nbytes, x_len, y_len, &rb, &batch);
+    if (s != ORACLE_CUDA_OK) return s;
+    if (Error e = check_weight_pointer(type, w_dev)) return fail(ctx, e);
+    if (!x_dev || !y_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "activation or output pointer is null");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    s = run_matvec(ctx, contract, type, rows, cols, rb, w_dev, x_dev, batch, y_dev, static_cast<cudaStream_t>(stream));
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+oracle_cuda_status oracle_cuda_matvec_q8k_prequantized(oracle_cuda_context* ctx, uint32_t type, uint64_t rows,
+                                                       uint64_t cols, const void* w_dev, uint64_t w_nbytes,
+                                                       const void* q8k_dev, uint64_t q8k_nbytes, float* y_dev,
+                                                       uint64_t y_len, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    uint64_t qrb = 0;
+    if (cols == 0 || rows == 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "reference matvec dimensions must be non-zero");
+    if (Error e = row_byte_size(cols, kTypeQ8_K, &qrb)) return fail(ctx, e);
+    if (q8k_nbytes == 0 || q8k_nbytes % qrb)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "reference matvec vector length mismatch");
+    const uint64_t batch = q8k_nbytes / qrb;
+    uint64_t rb = 0, b2 = 0;
+    oracle_cuda_status s = validate_matvec(ctx, ORACLE_CUDA_CONTRACT_Q8K, type, rows, cols, w_nbytes, batch * cols,
+                                           y_len, &rb, &b2);
+    if (s != ORACLE_CUDA_OK) return s;
+    if (Error e = check_weight_pointer(type, w_dev)) return fail(ctx, e);
+    if (!q8k_dev || !y_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "activation or output pointer is null");
+    if (reinterpret_cast<uintptr_t>(q8k_dev) % 4)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Q8_K buffers must be 4-byte aligned");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    for (uint64_t b = 0; b < batch; ++b) {
+        s = launch_q8k(ctx, type, w_dev, rows, cols, rb, nullptr, static_cast<const uint8_t*>(q8k_dev) + b * qrb,
+                       y_dev + b * rows, static_cast<cudaStream_t>(stream));
+        if (s != ORACLE_CUDA_OK) return s;
+    }
+    return ok(ctx);
+}
+
+oracle_cuda_status oracle_cuda_weight_upload(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
+                                             const void* host_bytes, uint64_t nbytes, uint64_t row_begin,
+                                             uint64_t row_end, oracle_cuda_weight** out) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (!out || !host_bytes) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "null pointer");
+    *out = nullptr;
+    uint64_t rb = 0, total = 0;
+    if (rows == 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "GGUF tensor must have at least one dimension");
+    if (Error e = row_byte_size(cols, type, &rb)) return fail(ctx, e);
+    if (!checked_mul(rows, rb, &total))
+        return fail(ctx, ORACLE_CUDA_OVERFLOW, "GGUF tensor byte size exceeds addressable size");
+    if (nbytes != total)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "GGUF tensor byte size does not match row geometry");
+    if (row_begin >= row_end || row_end > rows)
+        return fail(ctx, ORACLE_CUDA_OUT_OF_RANGE, "GGUF tensor row index exceeds row count");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    auto* w = new oracle_cuda_weight{ctx, type, row_end - row_begin, cols, row_begin, (row_end - row_begin) * rb,
+                                     nullptr, false};
+    // +16 bytes of tail padding keeps every aligned word read inside the allocation.
+    cudaError_t e = cudaMalloc(&w->dev, w->nbytes + 16);
+    if (e != cudaSuccess) {
+        delete w;
+        return cuda_fail(ctx, e, "cudaMalloc(weight)");
+    }
+    e = cudaMemcpy(w->dev, static_cast<const uint8_t*>(host_bytes) + row_begin * rb, w->nbytes,
+                   cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(w->dev);
+        delete w;
+        return cuda_fail(ctx, e, "cudaMemcpy(weight)");
+    }
+    *out = w;
+    return ok(ctx);
+}
+
+oracle_cuda_status oracle_cuda_weight_free(oracle_cuda_weight* w) {
+    if (!w) return ORACLE_CUDA_OK;
+    if (w->owned_by_cache) return fail(w->ctx, ORACLE_CUDA_INVALID_ARGUMENT, "resident cache entries are freed by oracle_cuda_evict_resident");
+    cudaSetDevice(w->ctx->device);
+    cudaFree(w->dev);
+    delete w;
+    return ORACLE_CUDA_OK;
+}
+
+oracle_cuda_status oracle_cuda_weight_info(const oracle_cuda_weight* w, uint32_t* type, uint64_t* rows, uint64_t* cols,
+                                           uint64_t* row_begin, const void** dev, uint64_t* nbytes) {
+    if (!w) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "weight is null");
+    if (type) *type = w->type;
+    if (rows) *rows = w->rows;
+    if (cols) *cols = w->cols;
+    if (row_begin) *row_begin = w->row_begin;
+    if (dev) *dev = w->dev;
+    if (nbytes) *nbytes = w->nbytes;
+    return ORACLE_CUDA_OK;
+}
+
+oracle_cuda_status oracle_cuda_evict_resident(oracle_cuda_context* ctx) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    cudaSetDevice(ctx->device);
+    cudaDeviceSynchronize();
+    for (auto& kv : ctx->resident) {
+        cudaFree(kv.second->dev);
+        delete kv.second;
+    }
+    ctx->resident.clear();
+    return ok(ctx);
+}
+
+oracle_cuda_status oracle_cuda_host_storage_matvec(oracle_cuda_context* ctx, int contract, uint32_t type,
+                                                   uint64_t rows, uint64_t cols, const void* w_host, uint64_t w_nbytes,
+                                                   const float* x_host, uint64_t x_len, float* y_host,
+                                                   uint64_t y_len) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    uint64_t rb = 0, batch = 0;
+    oracle_cuda_status s = validate_matvec(ctx, contract, type, rows, cols, w_nbytes, x_len, y_len, &rb, &batch);
+    if (s != ORACLE_CUDA_OK) return s;
+    if (!w_host || !x_host || !y_host) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "null pointer");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    oracle_cuda_weight* w = nullptr;
+    if ((s = resident_weight(ctx, type, rows, cols, w_host, w_nbytes, &w)) != ORACLE_CUDA_OK) return s;
+    if ((s = grow_device(ctx, ctx->dev_x, ctx->dev_x_len, x_len)) != ORACLE_CUDA_OK) return s;
+    if ((s = grow_device(ctx, ctx->dev_y, ctx->dev_y_len, y_len)) != ORACLE_CUDA_OK) return s;
+    const bool x_pinned = is_pinned(x_host), y_pinned = is_pinned(y_host);
+    const float* xsrc = x_host;
+    if (!x_pinned) {
+        if ((s = grow_pinned(ctx, ctx->pin_x, ctx->pin_x_len, x_len)) != ORACLE_CUDA_OK) return s;
+        std::memcpy(ctx->pin_x, x_host, x_len * sizeof(float));
+        xsrc = ctx->pin_x;
+    }
+    float* ydst = y_host;
+    if (!y_pinned) {
+        if ((s = grow_pinned(ctx, ctx->pin_y, ctx->pin_y_len, y_len)) != ORACLE_CUDA_OK) return s;
+        ydst = ctx->pin_y;
+    }
+    cudaStream_t st = nullptr;
+    ORACLE_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->dev_x, xsrc, x_len * sizeof(float), cudaMemcpyHostToDevice, st),
+                    "cudaMemcpyAsync(x)");
+    s = run_matvec(ctx, contract, type, rows, cols, rb, w->dev, ctx->dev_x, batch, ctx->dev_y, st);
+    if (s != ORACLE_CUDA_OK) return s;
+    ORACLE_CUDA_TRY(ctx, cudaMemcpyAsync(ydst, ctx->dev_y, y_len * sizeof(float), cudaMemcpyDeviceToHost, st),
+                    "cudaMemcpyAsync(y)");
+    ORACLE_CUDA_TRY(ctx, cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    if (!y_pinned) std::memcpy(y_host, ctx->pin_y, y_len * sizeof(float));
+    return ok(ctx);
+}
+
+oracle_cuda_status oracle_cuda_host_storage_dot(oracle_cuda_context* ctx, int contract, uint32_t type, uint64_t cols,
+                                                const void* row_host, uint64_t row_nbytes, const float* x_host,
+                                                uint64_t x_len, float* out) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    uint64_t rb = 0;
+    // make_storage_row_view (storage_decode.cpp:182-198), then the dot's length check (:27-29).
+    if (Error e = row_byte_size(cols, type, &rb)) return fail(ctx, e);
+    if (row_nbytes != rb)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                    "storage row byte size mismatch: expected " + std::to_string(rb) + ", received " +
+                        std::to_string(row_nbytes));
+    if (Error e = check_decodable(type)) return fail(ctx, e);
+    if (x_len != cols) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "reference dot vector length mismatch");
+    if (!out) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "output pointer is null");
+    return oracle_cuda_host_storage_matvec(ctx, contract, type, 1, cols, row_host, row_nbytes, x_host, x_len, out, 1);
+}
+
+oracle_cuda_status oracle_cuda_host_decode_rows(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
+                                                const void* w_host, uint64_t w_nbytes, float* out_host,
+                                                uint64_t out_len) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    uint64_t rb = 0, total = 0, elems = 0;
+    if (rows == 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "GGUF tensor must have at least one dimension");
+    if (Error e = row_byte_size(cols, type, &rb)) return fail(ctx, e);
+    if (!checked_mul(rows, rb, &total) || w_nbytes != total)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "GGUF tensor byte size does not match row geometry");
+    if (Error e = check_decodable(type)) return fail(ctx, e);
+    if (!checked_mul(rows, cols, &elems) || out_len != elems)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "mapped tensor decode output length mismatch");
+    if (!w_host || !out_host) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "null pointer");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    oracle_cuda_weight* w = nullptr;
+    oracle_cuda_status s = resident_weight(ctx, type, rows, cols, w_host, w_nbytes, &w);
+    if (s != ORACLE_CUDA_OK) return s;
+    if ((s = grow_device(ctx, ctx->dev_y, ctx->dev_y_len, out_len)) != ORACLE_CUDA_OK) return s;
+    s = launch_decode(ctx, type, w->dev, rows, cols, rb, ctx->dev_y, nullptr);
+    if (s != ORACLE_CUDA_OK) return s;
+    ORACLE_CUDA_TRY(ctx, cudaMemcpy(out_host, ctx->dev_y, out_len * sizeof(float), cudaMemcpyDeviceToHost),
+                    "cudaMemcpy(out)");
+    return ok(ctx);
+}
+
+}  // extern "C"

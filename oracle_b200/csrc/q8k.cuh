@@ -1,0 +1,147 @@
+// q8k.cuh -- Q8_K activation quantizer (f32 -> {f32 d; i8 qs[256]; i16 bsums[16]}).
+//
+// Restates GGML's quantize_row_q8_K_ref (ggml/src/ggml-quants.c, the commit
+// Oracle's docs pin); Oracle registers only the layout (ggml_type.cpp:28,
+// {15, "q8_K", 256, 292}).  Per 256-element block:
+//   max    = the element of largest magnitude, the first one on ties
+//   iscale = -127 / max                       (IEEE f32 division)
+//   q[j]   = min(127, round_half_even(iscale * x[j]))
+//   bsums  = sums of 16 consecutive q
+//   d      = 1 / iscale                       (IEEE f32 division)
+// An all-zero block gives d = 0, q = 0, bsums = 0.  Every f32 operation is an
+// explicit round-to-nearest intrinsic, so the bytes match the CPU restatement
+// exactly.  Inputs must be finite.
+#pragma once
+
+#include "common.cuh"
+
+namespace oracle_cuda {
+
+// One warp quantizes one 256-element block.  Lane l owns elements 8l..8l+7.
+// Outputs: q_lo/q_hi = the lane's 8 quants (little-endian bytes), bsum16 = the
+// sum over the 16-element group (lanes 2g, 2g+1) containing the lane, d.
+struct Q8KLane {
+    uint32_t q_lo, q_hi;
+    int bsum16;
+    float d;
+};
+
+__device__ __forceinline__ Q8KLane quantize_q8k_block_warp(const float* xb, int lane,
+                                                           bool aligned16) {
+    float v[8];
+    if (aligned16) {
+        const float4 a = reinterpret_cast<const float4*>(xb)[2 * lane];
+        const float4 b = reinterpret_cast<const float4*>(xb)[2 * lane + 1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = xb[8 * lane + j];
+    }
+    // first strictly-greater scan inside the lane, then a warp arg-max that
+    // prefers the lower index on ties: the result is the sequential scan's.
+    float amax = 0.0f, vmax = 0.0f;
+    int idx = 0x7FFFFFFF;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float a = fabsf(v[j]);
+        if (a > amax) {
+            amax = a;
+            vmax = v[j];
+            idx = 8 * lane + j;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xFFFFFFFFu, amax, off);
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, vmax, off);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, idx, off);
+        if (oa > amax || (oa == amax && oi < idx)) {
+            amax = oa;
+            vmax = ov;
+            idx = oi;
+        }
+    }
+    Q8KLane out;
+    if (amax == 0.0f) {
+        out.q_lo = out.q_hi = 0u;
+        out.bsum16 = 0;
+        out.d = 0.0f;
+        return out;
+    }
+    const float iscale = __fdiv_rn(-127.0f, vmax);
+    uint32_t packed[2] = {0u, 0u};
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        int q = __float2int_rn(__fmul_rn(iscale, v[j]));
+        q = q > 127 ? 127 : q;
+        sum += q;
+        packed[j / 4] |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * (j % 4));
+    }
+    out.q_lo = packed[0];
+    out.q_hi = packed[1];
+    out.bsum16 = sum + __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+    out.d = __fdiv_rn(1.0f, iscale);
+    return out;
+}
+
+// Standalone quantizer: one warp per (activation row, block); GGML byte layout
+// (292 bytes per block, 4-byte aligned fields).
+__global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x,
+                                                           uint64_t k, uint64_t batch,
+                                                           uint8_t* __restrict__ out) {
+    const uint64_t nb = k / 256;
+    const uint64_t block = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+    const int lane = threadIdx.x & 31;
+    if (block >= nb * batch) return;
+    const float* xb = x + block * 256;
+    const bool aligned16 = (reinterpret_cast<uintptr_t>(xb) & 15u) == 0;
+    const Q8KLane r = quantize_q8k_block_warp(xb, lane, aligned16);
+    uint8_t* ob = out + block * 292;
+    if (lane == 0) *reinterpret_cast<float*>(ob) = r.d;
+    uint32_t* qs = reinterpret_cast<uint32_t*>(ob + 4);
+    qs[2 * lane] = r.q_lo;
+    qs[2 * lane + 1] = r.q_hi;
+    if ((lane & 1) == 0) reinterpret_cast<int16_t*>(ob + 260)[lane / 2] = static_cast<int16_t>(r.bsum16);
+}
+
+// Shared-memory activation image used by the matvec kernels.  For block i:
+// qs at q + 256*i (natural element order), 16-element sums at bs + 16*i,
+// scale at d[i].
+struct ActImage {
+    int8_t* q;
+    int* bs;
+    float* d;
+};
+
+// Quantize `nb` blocks of x into the image, one block per warp, warps
+// [0, nwarps) cooperating.  The caller synchronises afterwards.
+__device__ __forceinline__ void quantize_to_image(const float* __restrict__ x, uint32_t nb,
+                                                  ActImage img, int warp, int nwarps, int lane) {
+    const bool aligned16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+    for (uint32_t i = warp; i < nb; i += nwarps) {
+        const Q8KLane r = quantize_q8k_block_warp(x + 256ull * i, lane, aligned16);
+        uint32_t* qs = reinterpret_cast<uint32_t*>(img.q + 256 * i);
+        qs[2 * lane] = r.q_lo;
+        qs[2 * lane + 1] = r.q_hi;
+        if ((lane & 1) == 0) img.bs[16 * i + lane / 2] = r.bsum16;
+        if (lane == 0) img.d[i] = r.d;
+    }
+}
+
+// Load pre-quantized GGML Q8_K blocks (global) into the image.
+__device__ __forceinline__ void load_q8k_to_image(const uint8_t* __restrict__ q8k, uint32_t nb,
+                                                  ActImage img, int warp, int nwarps, int lane) {
+    for (uint32_t i = warp; i < nb; i += nwarps) {
+        const uint8_t* b = q8k + 292ull * i;
+        const uint32_t* qs = reinterpret_cast<const uint32_t*>(b + 4);
+        uint32_t* dst = reinterpret_cast<uint32_t*>(img.q + 256 * i);
+        dst[2 * lane] = qs[2 * lane];
+        dst[2 * lane + 1] = qs[2 * lane + 1];
+        if (lane < 16) img.bs[16 * i + lane] = reinterpret_cast<const int16_t*>(b + 260)[lane];
+        if (lane == 0) img.d[i] = *reinterpret_cast<const float*>(b);
+    }
+}
+
+}  // namespace oracle_cuda

@@ -1,0 +1,153 @@
+// stream.cuh -- persistent row-streaming CTA for HBM-bound matvec kernels.
+//
+// Layout of one CTA: `Consumer::kWarps` consumer warps plus one producer warp.
+// Each CTA owns a contiguous, balanced range of weight rows.  The producer
+// streams that range through an S-stage ring in shared memory, R rows per
+// stage, with 1-D bulk async copies (cp.async.bulk, the non-tensor TMA path)
+// whose completion is counted in bytes on a per-stage "full" mbarrier.  The
+// 16-byte aligned interior of each stage moves by bulk copy; the < 16-byte
+// head and tail of an unaligned stage are copied by producer lanes, so any
+// row geometry works.  Consumer warps take rows round-robin, wait on the
+// stage's full barrier, compute, and arrive once per row on the stage's
+// "empty" barrier (expected count R), which frees the slot for stage t + S.
+//
+// Shared memory: [full[S], empty[S]] [activation image] [S stages].  Global
+// byte g of stage t sits at stage_base + (g - floor16(first byte of stage t)).
+//
+// Every wait is bounded (mbar_wait); a timeout stops the CTA, which first
+// waits (bounded) for its own bulk copies still in flight.
+#pragma once
+
+#include "common.cuh"
+
+namespace oracle_cuda {
+
+struct StreamParams {
+    const uint8_t* w;      // row-major matrix, rows * row_bytes bytes
+    uint64_t rows;
+    uint64_t row_bytes;
+    uint32_t rows_per_stage;  // R
+    uint32_t stages;          // S
+    uint32_t stage_bytes;     // bytes reserved per stage (>= R*row_bytes + 32, multiple of 128)
+    uint32_t act_bytes;       // activation image bytes (multiple of 128)
+    DeviceStatus* status;
+};
+
+__host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline uint32_t stream_barrier_bytes(uint32_t stages) {
+    return align_up(16u * stages, 128u);
+}
+
+__host__ inline uint64_t stream_smem_bytes(const StreamParams& p) {
+    return stream_barrier_bytes(p.stages) + uint64_t(p.act_bytes) + uint64_t(p.stages) * p.stage_bytes;
+}
+
+// Programmatic dependent launch: wait for the preceding grid's results (no-op
+// when the launch did not opt in), and let the next grid begin launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <class Consumer>
+__global__ void __launch_bounds__((Consumer::kWarps + 1) * 32, 1)
+    stream_rows_kernel(const StreamParams sp, const typename Consumer::Params cp) {
+    constexpr int NCW = Consumer::kWarps;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + sp.stages;
+    uint8_t* act = smem + stream_barrier_bytes(sp.stages);
+    uint8_t* stage0 = act + sp.act_bytes;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t R = sp.rows_per_stage;
+    const uint32_t S = sp.stages;
+    const uint64_t r0 = blockIdx.x * sp.rows / gridDim.x;
+    const uint64_t r1 = (blockIdx.x + 1ull) * sp.rows / gridDim.x;
+    const uint32_t nrows = static_cast<uint32_t>(r1 - r0);
+    const uint32_t T = (nrows + R - 1) / R;
+    const uintptr_t wbase = reinterpret_cast<uintptr_t>(sp.w);
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], R);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == NCW) {
+        // ---------------- producer warp
+        const uint64_t policy = l2_policy_evict_first();
+        uint32_t issued = 0;
+        for (uint32_t t = 0; t < T; ++t) {
+            const uint32_t s = t % S;
+            if (t >= S) {
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(&empty[s], ((t / S) - 1) & 1, sp.status, 1);
+                if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0)) break;
+            }
+            const uint64_t lo = r0 + uint64_t(t) * R;
+            const uint64_t hi = lo + R < r1 ? lo + R : r1;
+            const uintptr_t a = wbase + lo * sp.row_bytes;
+            const uintptr_t b = wbase + hi * sp.row_bytes;
+            const uintptr_t a16 = a & ~uintptr_t(15);
+            const uintptr_t A = (a + 15) & ~uintptr_t(15);
+            const uintptr_t B = b & ~uintptr_t(15);
+            uint8_t* dst = stage0 + size_t(s) * sp.stage_bytes;
+            uint32_t tx = 0;
+            if (B <= A) {
+                // the stage spans no whole 16-byte unit: lanes copy every byte
+                for (uintptr_t g = a + lane; g < b; g += 32)
+                    dst[g - a16] = *reinterpret_cast<const uint8_t*>(g);
+            } else {
+                if (a + lane < A) dst[a + lane - a16] = *reinterpret_cast<const uint8_t*>(a + lane);
+                if (B + lane < b) dst[B + lane - a16] = *reinterpret_cast<const uint8_t*>(B + lane);
+                tx = static_cast<uint32_t>(B - A);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[s], tx);
+                constexpr uint32_t kChunk = 32768;
+                for (uint32_t off = 0; off < tx; off += kChunk) {
+                    const uint32_t n = tx - off < kChunk ? tx - off : kChunk;
+                    bulk_copy_g2s(dst + (A - a16) + off, reinterpret_cast<const void*>(A + off), n,
+                                  &full[s], policy);
+                }
+            }
+            issued = t + 1;
+        }
+        // Drain: every copy this CTA issued must land before the CTA exits.
+        if (lane == 0) {
+            const uint32_t first = issued > S ? issued - S : 0;
+            for (uint32_t t = first; t < issued; ++t) mbar_wait(&full[t % S], (t / S) & 1, sp.status, 2);
+        }
+        return;
+    }
+
+    // ---------------- consumer warps
+    pdl_wait();  // activations may come from the preceding kernel
+    Consumer cons;
+    cons.prologue(cp, act, warp, lane);
+    named_barrier_sync(1, NCW * 32);
+    if (threadIdx.x == 0) pdl_launch_dependents();
+    cons.load(cp, act, warp, lane);
+
+    for (uint32_t q = warp; q < nrows; q += NCW) {
+        const uint32_t t = q / R;
+        const uint32_t s = t % S;
+        const bool ok = mbar_wait(&full[s], (t / S) & 1, sp.status, 3);
+        if (!__all_sync(0xFFFFFFFFu, ok)) break;
+        const uintptr_t a16 = (wbase + (r0 + uint64_t(t) * R) * sp.row_bytes) & ~uintptr_t(15);
+        const uint8_t* rowp = stage0 + size_t(s) * sp.stage_bytes +
+                              ((wbase + (r0 + q) * sp.row_bytes) - a16);
+        cons.row(cp, act, rowp, r0 + q, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+}
+
+}  // namespace oracle_cuda

@@ -1,0 +1,275 @@
+"""GPU parity: the CUDA path through the C ABI against the CPU checkers.
+
+Bars (written into each test):
+* decode, Q8_K quantization, the Q8_K integer matvec: bit-exact with the
+  restatement (which is bit-exact with Oracle's compiled decoders, see
+  test_oracle_pins.py);
+* Oracle's f32 contract: |gpu - oracle| <= 1e-6 + 1e-5 * |oracle| per element;
+  an element outside that is accepted only when the GPU value is at least as
+  close to the f64 arbiter as Oracle's own sequential f32 sum is.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle_b200 as ob
+from conftest import golden
+from oracle_b200 import synth
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def to_dev(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a).reshape(-1)).to(DEV)
+
+
+def bits_equal(a: np.ndarray, b: np.ndarray) -> bool:
+    a = np.asarray(a, np.float32).reshape(-1)
+    b = np.asarray(b, np.float32).reshape(-1)
+    return bool(np.all((a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))))
+
+
+def f32_contract_ok(got, oracle_y, exact):
+    got, oracle_y, exact = (np.asarray(v, np.float64).reshape(-1) for v in (got, oracle_y, exact))
+    bound = 1e-6 + 1e-5 * np.abs(oracle_y)
+    off = np.abs(got - oracle_y) > bound
+    closer = np.abs(got - exact) <= np.abs(oracle_y - exact) + 1e-6
+    return bool(np.all(~off | closer)), int(off.sum())
+
+
+# ---------------------------------------------------------------- decode (decode_storage_row)
+
+@pytest.mark.parametrize("qtype,rows,k", [
+    (ob.TYPE_Q8_0, 1, 32), (ob.TYPE_Q8_0, 7, 96), (ob.TYPE_Q8_0, 33, 4096),
+    (ob.TYPE_Q4_K, 1, 256), (ob.TYPE_Q4_K, 5, 768), (ob.TYPE_Q4_K, 17, 4096),
+    (ob.TYPE_Q5_K, 3, 512), (ob.TYPE_Q6_K, 1, 256), (ob.TYPE_Q6_K, 9, 1280),
+    (ob.TYPE_F16, 3, 37), (ob.TYPE_BF16, 3, 37), (ob.TYPE_F32, 4, 13)])
+def test_decode_rows_bit_exact(ctx, port, qtype, rows, k):
+    w = synth.weight(qtype, rows, k, "gpu", f"dec_{qtype}_{rows}_{k}")
+    out = torch.empty(rows * k, dtype=torch.float32, device=DEV)
+    ctx.decode_rows(qtype, rows, k, to_dev(w), out)
+    ctx.device_status()
+    assert bits_equal(out.cpu().numpy(), port.decode_rows(qtype, rows, k, w))
+
+
+def test_decode_rows_ggufpy_fixture(ctx):
+    g = golden("decode_ggufpy.npz")
+    for qtype, name in [(ob.TYPE_Q8_0, "Q8_0"), (ob.TYPE_Q4_K, "Q4_K"), (ob.TYPE_Q5_K, "Q5_K"),
+                        (ob.TYPE_Q6_K, "Q6_K")]:
+        blocks, want = g[f"{name}_blocks"], g[f"{name}_decoded"]
+        out = torch.empty(want.size, dtype=torch.float32, device=DEV)
+        ctx.decode_rows(qtype, blocks.shape[0], want.shape[1], to_dev(blocks), out)
+        assert bits_equal(out.cpu().numpy(), want), name
+
+
+def test_host_decode_rows_reference_fixture(ctx):
+    g = golden("reference.npz")
+    for qtype, name in [(ob.TYPE_Q8_0, "Q8_0"), (ob.TYPE_Q5_K, "Q5_K"), (ob.TYPE_Q6_K, "Q6_K"),
+                        (ob.TYPE_F16, "F16"), (ob.TYPE_BF16, "BF16"), (ob.TYPE_F32, "F32")]:
+        w, x = g[f"{name}_w"], g[f"{name}_x"]
+        got = ctx.host_decode_rows(qtype, w.shape[0], x.size, w)
+        assert bits_equal(got, g[f"{name}_decoded"]), name
+
+
+# ---------------------------------------------------------------- Q8_K quantizer
+
+def test_quantize_q8k_bit_exact(ctx, port):
+    g = golden("q8k.npz")
+    x = g["x"]
+    rng = synth.rng_for("gpu", "q8k")
+    xr = (rng.standard_normal(256 * 96) * rng.uniform(1e-3, 1e3, 256 * 96)).astype(np.float32)
+    for xs, batch in [(x, 1), (xr, 3), (xr[: 256 * 5], 1)]:
+        k = xs.size // batch
+        q = torch.empty(xs.size // 256 * 292, dtype=torch.uint8, device=DEV)
+        ctx.quantize_q8_k(to_dev(xs), k, batch, q)
+        ctx.device_status()
+        assert np.array_equal(q.cpu().numpy(), port.quantize_q8_k(xs.reshape(batch, k)).reshape(-1))
+    assert np.array_equal(port.quantize_q8_k(x)[0], g["q8k"])
+
+
+# ---------------------------------------------------------------- Q8_K integer matvec (north star)
+
+SHAPES_Q8K = [(1, 256), (2, 512), (3, 4096), (13, 4096), (257, 4096), (149, 3072), (100, 12288),
+              (37, 8192), (20, 16384), (1000, 1024)]
+
+
+@pytest.mark.parametrize("qtype", [ob.TYPE_Q4_K, ob.TYPE_Q6_K])
+@pytest.mark.parametrize("rows,k", SHAPES_Q8K)
+def test_matvec_q8k_bit_exact(ctx, port, qtype, rows, k):
+    w = synth.weight(qtype, rows, k, "gpu", f"mv_{qtype}_{rows}_{k}")
+    x = synth.activations(k, 1, "gpu", f"mv_x_{k}")
+    q8 = port.quantize_q8_k(x)
+    want = port.matvec_q8_k(qtype, rows, k, w, q8)[0]
+    wd, xd = to_dev(w), to_dev(x)
+    y = torch.empty(rows, dtype=torch.float32, device=DEV)
+    ctx.storage_matvec(ob.CONTRACT_Q8K, qtype, rows, k, wd, xd, y)  # quantize fused in-kernel
+    ctx.device_status()
+    assert bits_equal(y.cpu().numpy(), want)
+    y2 = torch.empty_like(y)
+    ctx.matvec_q8k_prequantized(qtype, rows, k, wd, to_dev(q8), y2)
+    ctx.device_status()
+    assert bits_equal(y2.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("qtype", [ob.TYPE_Q4_K, ob.TYPE_Q6_K])
+def test_matvec_q8k_batch(ctx, port, qtype):
+    rows, k, batch = 77, 2048, 3
+    w = synth.weight(qtype, rows, k, "gpu", f"mvb_{qtype}")
+    x = synth.activations(k, batch, "gpu", "mvb_x")
+    want = port.matvec_q8_k(qtype, rows, k, w, port.quantize_q8_k(x))
+    y = torch.empty(batch * rows, dtype=torch.float32, device=DEV)
+    ctx.storage_matvec(ob.CONTRACT_Q8K, qtype, rows, k, to_dev(w), to_dev(x), y)
+    assert bits_equal(y.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("rows,k", [(12288, 4096), (4096, 12288), (4096, 4096)])
+def test_config2_full_size_q4k(ctx, port, rows, k):
+    """BASELINE config 2 shapes, every element bit-exact."""
+    w = synth.weight(ob.TYPE_Q4_K, rows, k, "config2", f"W_{k}_{rows}")
+    x = synth.activations(k, 1, "config2", f"x_{k}")
+    want = port.matvec_q8_k(ob.TYPE_Q4_K, rows, k, w, port.quantize_q8_k(x))[0]
+    y = torch.empty(rows, dtype=torch.float32, device=DEV)
+    ctx.storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, rows, k, to_dev(w), to_dev(x), y)
+    ctx.device_status()
+    assert bits_equal(y.cpu().numpy(), want)
+
+
+def test_config3_lm_head_q6k(ctx, port):
+    """Q6_K 151936 x 4096 LM head, every logit bit-exact."""
+    rows, k = 151936, 4096
+    w = synth.weight(ob.TYPE_Q6_K, rows, k, "config3", "lm_head")
+    x = synth.activations(k, 1, "config3", "x")
+    want = port.matvec_q8_k(ob.TYPE_Q6_K, rows, k, w, port.quantize_q8_k(x))[0]
+    y = torch.empty(rows, dtype=torch.float32, device=DEV)
+    ctx.storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q6_K, rows, k, to_dev(w), to_dev(x), y)
+    ctx.device_status()
+    got = y.cpu().numpy()
+    assert bits_equal(got, want)
+    assert int(np.argmax(got)) == int(np.argmax(want))
+
+
+# ---------------------------------------------------------------- Oracle's f32 contract
+
+@pytest.mark.parametrize("qtype,rows,k", [
+    (ob.TYPE_Q8_0, 4096, 4096), (ob.TYPE_Q8_0, 5, 32), (ob.TYPE_Q8_0, 19, 160),
+    (ob.TYPE_Q4_K, 33, 4096), (ob.TYPE_Q5_K, 21, 1024), (ob.TYPE_Q6_K, 45, 4096),
+    (ob.TYPE_F16, 6, 37), (ob.TYPE_BF16, 6, 300), (ob.TYPE_F32, 7, 129)])
+def test_f32_contract(ctx, port, qtype, rows, k):
+    w = synth.weight(qtype, rows, k, "config1" if (rows, k) == (4096, 4096) else "gpu", f"f32_{qtype}_{rows}_{k}")
+    x = synth.activations(k, 1, "gpu", f"f32_x_{k}")
+    want = port.storage_matvec_f32(qtype, rows, k, w, x)[0]
+    exact = port.storage_matvec_f64(qtype, rows, k, w, x)[0]
+    y = torch.empty(rows, dtype=torch.float32, device=DEV)
+    ctx.storage_matvec(ob.CONTRACT_F32, qtype, rows, k, to_dev(w), to_dev(x), y)
+    ctx.device_status()
+    ok, off = f32_contract_ok(y.cpu().numpy(), want, exact)
+    assert ok, f"{off} elements outside tolerance and farther from f64 than Oracle's sum"
+
+
+def test_f32_contract_against_reference_binary(ctx, ref):
+    """Oracle's own compiled reference_storage_matvec as the expected value."""
+    for qtype, rows, k in [(ob.TYPE_Q8_0, 257, 4096), (ob.TYPE_Q6_K, 65, 2048), (ob.TYPE_Q5_K, 9, 512)]:
+        w = synth.weight(qtype, rows, k, "gpu", f"refbin_{qtype}")
+        x = synth.activations(k, 1, "gpu", f"refbin_x_{k}")[0]
+        want = ref.storage_matvec(qtype, rows, k, w, x)
+        got = ctx.host_storage_matvec(ob.CONTRACT_F32, qtype, rows, k, w, x)
+        import oracle
+        exact = oracle.port().storage_matvec_f64(qtype, rows, k, w, x)[0]
+        ok, off = f32_contract_ok(got, want, exact)
+        assert ok, (qtype, off)
+
+
+def test_f32_contract_batch(ctx, port):
+    rows, k, batch = 50, 1024, 4
+    w = synth.weight(ob.TYPE_Q8_0, rows, k, "gpu", "f32batch")
+    x = synth.activations(k, batch, "gpu", "f32batch_x")
+    want = port.storage_matvec_f32(ob.TYPE_Q8_0, rows, k, w, x)
+    exact = port.storage_matvec_f64(ob.TYPE_Q8_0, rows, k, w, x)
+    y = torch.empty(batch * rows, dtype=torch.float32, device=DEV)
+    ctx.storage_matvec(ob.CONTRACT_F32, ob.TYPE_Q8_0, rows, k, to_dev(w), to_dev(x), y)
+    assert f32_contract_ok(y.cpu().numpy(), want, exact)[0]
+
+
+# ---------------------------------------------------------------- host drop-ins: the reference's known answers
+
+def test_host_known_answers(ctx):
+    from test_oracle_pins import q5_fixture, q6_fixture, q8_0_fixture, q4_fixture
+    ones = np.ones(256, np.float32)
+    assert ctx.host_storage_dot(ob.CONTRACT_F32, ob.TYPE_Q5_K, 256, q5_fixture(), ones) == 4288.0
+    assert ctx.host_storage_dot(ob.CONTRACT_F32, ob.TYPE_Q6_K, 256, q6_fixture(), ones) == 4480.0
+    assert ctx.host_storage_dot(ob.CONTRACT_F32, ob.TYPE_Q8_0, 32, q8_0_fixture(), np.ones(32, np.float32)) == 14.0
+    assert ctx.host_storage_dot(ob.CONTRACT_F32, ob.TYPE_Q4_K, 256, q4_fixture(), ones) == 192.0
+    second = q5_fixture().copy()
+    second[16:] = 0
+    y = ctx.host_storage_matvec(ob.CONTRACT_F32, ob.TYPE_Q5_K, 2, 256, np.concatenate([q5_fixture(), second]), ones)
+    assert y.tolist() == [4288.0, -192.0]
+    mat8 = np.concatenate([q8_0_fixture(), q8_0_fixture(0x3800, [4] * 32)])
+    assert ctx.host_storage_matvec(ob.CONTRACT_F32, ob.TYPE_Q8_0, 2, 32, mat8,
+                                   np.ones(32, np.float32)).tolist() == [14.0, 64.0]
+    dec = ctx.host_decode_rows(ob.TYPE_Q5_K, 1, 256, q5_fixture())
+    assert np.all(dec.reshape(4, 64)[:, :32] == 16.25) and np.all(dec.reshape(4, 64)[:, 32:] == 17.25)
+
+
+def test_host_q8k_matches_device(ctx, port):
+    rows, k = 300, 4096
+    w = synth.weight(ob.TYPE_Q4_K, rows, k, "gpu", "host_q8k")
+    x = synth.activations(k, 1, "gpu", "host_q8k_x")
+    got = ctx.host_storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, rows, k, w, x)
+    assert bits_equal(got, port.matvec_q8_k(ob.TYPE_Q4_K, rows, k, w, port.quantize_q8_k(x))[0])
+    got2 = ctx.host_storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, rows, k, w, x)  # resident copy reused
+    assert bits_equal(got, got2)
+
+
+# ---------------------------------------------------------------- errors: same class and message as the reference
+
+def test_validation_matches_reference(ctx, ref):
+    import oracle
+    w = synth.weight(ob.TYPE_Q8_0, 2, 64, "gpu", "err")
+    x = np.ones(64, np.float32)
+    cases = [
+        (ob.TYPE_Q8_0, 0, 64, w, x, 2),          # zero rows
+        (ob.TYPE_Q8_0, 2, 64, w, x[:63], 2),     # vector length
+        (ob.TYPE_Q8_0, 2, 64, w, x, 3),          # output length
+        (ob.TYPE_Q8_0, 2, 64, w[:, :-1], x, 2),  # matrix bytes
+        (ob.TYPE_Q8_0, 2, 63, w, x[:63], 2),     # ragged row
+        (999, 2, 64, w, x, 2),                   # unknown type
+        (2, 2, 64, np.zeros(2 * 36, np.uint8), x, 2),  # registered, not decodable (q4_0)
+    ]
+    for qtype, rows, k, wb, xb, ylen in cases:
+        with pytest.raises(oracle.ReferenceError_) as want:
+            ref.storage_matvec(qtype, rows, k, wb, xb, y_len=ylen)
+        with pytest.raises(ob.OracleCudaError) as got:
+            ctx.host_storage_matvec(ob.CONTRACT_F32, qtype, rows, k, wb, xb, np.empty(ylen, np.float32))
+        assert got.value.status == want.value.code, (qtype, rows, k, str(got.value), want.value.message)
+        assert str(got.value) == want.value.message
+    with pytest.raises(ob.Unsupported):
+        ctx.host_storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q8_0, 2, 64, w, x)
+
+
+def test_device_pointer_validation(ctx):
+    w = to_dev(synth.weight(ob.TYPE_Q4_K, 4, 256, "gpu", "ptr"))
+    y = torch.empty(4, dtype=torch.float32, device=DEV)
+    x = torch.zeros(256, dtype=torch.float32, device=DEV)
+    with pytest.raises(ob.InvalidArgument, match="16-byte aligned"):
+        ctx.storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, 4, 256, w.data_ptr() + 8, x, y, w_nbytes=4 * 144)
+    ctx.storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, 4, 256, w, x, y)
+    assert torch.all(y == 0)  # x = 0 quantizes to d = 0
+
+
+# ---------------------------------------------------------------- failure detection without a fault
+
+def test_bounded_wait_reports_timeout_and_context_survives(ctx, port):
+    ctx.device_status()  # clean
+    ctx.selftest_bounded_wait(50_000_000)  # 50 ms deadline on a barrier nobody completes
+    with pytest.raises(ob.DeviceTimeout, match="site 99"):
+        ctx.device_status()
+    ctx.device_status()  # the status word was cleared and the context is still usable
+    rows, k = 8, 512
+    w = synth.weight(ob.TYPE_Q6_K, rows, k, "gpu", "after_timeout")
+    x = synth.activations(k, 1, "gpu", "after_timeout_x")
+    y = torch.empty(rows, dtype=torch.float32, device=DEV)
+    ctx.storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q6_K, rows, k, to_dev(w), to_dev(x), y)
+    assert bits_equal(y.cpu().numpy(), port.matvec_q8_k(ob.TYPE_Q6_K, rows, k, w, port.quantize_q8_k(x))[0])
