@@ -18,8 +18,10 @@
 // shuffle; slot[j] and slot[j + 16] live in the pair's two accumulators, and
 // the stride-8..1 folds are xor-16..2 lane shuffles.
 //
-// The lane's 128 activation quants (32 words), its sub-block bsums and d_x are
-// loaded once into registers (kPasses compile-time) and reused for every row.
+// The activation is quantized once per CTA into a shared-memory image
+// (q8k.cuh).  For rows of at most 16 super-blocks the lane's slice of it (32
+// quant words, bsums, d_x) is held in registers for every row; longer rows
+// re-read it per pass from the bank-conflict-free swizzled image.
 #pragma once
 
 #include "q8k.cuh"
@@ -37,6 +39,13 @@ struct MatvecQ8KParams {
 
 __device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) {
     return __dp4a(static_cast<int>(a), static_cast<int>(b), c);
+}
+
+// Unsigned bytes of a times signed bytes of b, accumulated into c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
 __device__ __forceinline__ int ubyte(uint32_t w, int i) { return static_cast<int>((w >> (8 * i)) & 0xFFu); }
@@ -65,15 +74,17 @@ __device__ __forceinline__ void q4k_half_sums(const uint8_t* sb, int part, const
         w[4 * v + 2] = t.z;
         w[4 * v + 3] = t.w;
     }
+    // High nibbles are used in place (byte & 0xF0 = 16 * nibble): their dot
+    // products come out 16x larger, exactly, and are shifted back.
     int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
         d0 = dp4a(w[t] & 0x0F0F0F0Fu, xw[t], d0);
-        d1 = dp4a((w[t] >> 4) & 0x0F0F0F0Fu, xw[8 + t], d1);
+        d1 = dp4a_us(w[t] & 0xF0F0F0F0u, xw[8 + t], d1);
         d2 = dp4a(w[8 + t] & 0x0F0F0F0Fu, xw[16 + t], d2);
-        d3 = dp4a((w[8 + t] >> 4) & 0x0F0F0F0Fu, xw[24 + t], d3);
+        d3 = dp4a_us(w[8 + t] & 0xF0F0F0F0u, xw[24 + t], d3);
     }
-    isum = ubyte(scw, 0) * d0 + ubyte(scw, 1) * d1 + ubyte(scw, 2) * d2 + ubyte(scw, 3) * d3;
+    isum = ubyte(scw, 0) * d0 + ubyte(scw, 1) * (d1 >> 4) + ubyte(scw, 2) * d2 + ubyte(scw, 3) * (d3 >> 4);
     msum = ubyte(mnw, 0) * xbs[0] + ubyte(mnw, 1) * xbs[1] + ubyte(mnw, 2) * xbs[2] +
            ubyte(mnw, 3) * xbs[3];
 }
@@ -123,27 +134,46 @@ __device__ __forceinline__ void q6k_half_sums(const uint8_t* sb, int h, const ui
     isum = s;
 }
 
-// Activation image region size for nb super-blocks.
-__host__ __device__ inline uint32_t q8k_image_bytes(uint32_t nb) {
-    return align_up(nb * 256u, 128u) + align_up(nb * 16u * 4u, 128u) + align_up(nb * 4u, 128u);
+// The lane's activation data for one pass: 128 quants (32 words) of half
+// `part` of block i, its four 32-element sums (Q4_K) or 32 x its eight
+// 16-element sums (Q6_K), and d_x.
+template <uint32_t kType>
+__device__ __forceinline__ void fetch_lane_x(const ActImage& img, uint32_t i, int part, uint32_t (&xw)[32],
+                                             int (&xbs)[8], float& xd) {
+    const uint32_t rho = 2u * i + part;
+    const uint8_t* row = reinterpret_cast<const uint8_t*>(img.q) + rho * 128u;
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+        const uint4 t = *reinterpret_cast<const uint4*>(row + 16u * (uint32_t(v) ^ (rho & 7u)));
+        xw[4 * v + 0] = t.x;
+        xw[4 * v + 1] = t.y;
+        xw[4 * v + 2] = t.z;
+        xw[4 * v + 3] = t.w;
+    }
+    if (kType == 12) {
+        const int4 b = *reinterpret_cast<const int4*>(img.bs32 + 8 * i + 4 * part);
+        xbs[0] = b.x; xbs[1] = b.y; xbs[2] = b.z; xbs[3] = b.w;
+        xbs[4] = xbs[5] = xbs[6] = xbs[7] = 0;
+    } else {
+        const int4 b0 = *reinterpret_cast<const int4*>(img.bs16 + 16 * i + 8 * part);
+        const int4 b1 = *reinterpret_cast<const int4*>(img.bs16 + 16 * i + 8 * part + 4);
+        xbs[0] = 32 * b0.x; xbs[1] = 32 * b0.y; xbs[2] = 32 * b0.z; xbs[3] = 32 * b0.w;
+        xbs[4] = 32 * b1.x; xbs[5] = 32 * b1.y; xbs[6] = 32 * b1.z; xbs[7] = 32 * b1.w;
+    }
+    xd = img.d[i];
 }
 
-__device__ __forceinline__ ActImage q8k_image(uint8_t* act, uint32_t nb) {
-    ActImage img;
-    img.q = reinterpret_cast<int8_t*>(act);
-    img.bs = reinterpret_cast<int*>(act + align_up(nb * 256u, 128u));
-    img.d = reinterpret_cast<float*>(act + align_up(nb * 256u, 128u) + align_up(nb * 64u, 128u));
-    return img;
-}
-
-template <uint32_t kType, int kPasses, int kWarps_>
+// kXReg: rows of at most 16 super-blocks (one pass); the lane's activation
+// data is fetched once into registers and reused for every row.  Otherwise
+// every pass re-reads it from the shared-memory image (conflict-free).
+template <uint32_t kType, bool kXReg, int kWarps_>
 struct MatvecQ8KConsumer {
     static constexpr int kWarps = kWarps_;
     using Params = MatvecQ8KParams;
 
-    uint32_t xw[kPasses][32];
-    int xbs[kPasses][8];
-    float xd[kPasses];
+    uint32_t xw[kXReg ? 32 : 1];
+    int xbs[kXReg ? 8 : 1];
+    float xd = 0.0f;
 
     __device__ __forceinline__ void prologue(const Params& p, uint8_t* act, int warp, int lane) {
         const ActImage img = q8k_image(act, p.nb);
@@ -154,68 +184,57 @@ struct MatvecQ8KConsumer {
     }
 
     __device__ __forceinline__ void load(const Params& p, uint8_t* act, int, int lane) {
-        const ActImage img = q8k_image(act, p.nb);
-        const int j = lane >> 1, part = lane & 1;
-#pragma unroll
-        for (int k = 0; k < kPasses; ++k) {
-            const uint32_t i = 16u * k + j;
+        if constexpr (kXReg) {
+            const uint32_t i = lane >> 1;
             if (i < p.nb) {
-                const uint4* src = reinterpret_cast<const uint4*>(img.q + 256 * i + 128 * part);
-#pragma unroll
-                for (int v = 0; v < 8; ++v) {
-                    const uint4 t = src[v];
-                    xw[k][4 * v + 0] = t.x;
-                    xw[k][4 * v + 1] = t.y;
-                    xw[k][4 * v + 2] = t.z;
-                    xw[k][4 * v + 3] = t.w;
-                }
-                const int* bs = img.bs + 16 * i + 8 * part;
-                if (kType == 12) {
-                    // sub-block (32 elements) sums for sub-blocks 4*part .. 4*part+3
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) xbs[k][t] = bs[2 * t] + bs[2 * t + 1];
-#pragma unroll
-                    for (int t = 4; t < 8; ++t) xbs[k][t] = 0;
-                } else {
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) xbs[k][t] = 32 * bs[t];
-                }
-                xd[k] = img.d[i];
+                fetch_lane_x<kType>(q8k_image(act, p.nb), i, lane & 1, xw, xbs, xd);
             } else {
 #pragma unroll
-                for (int v = 0; v < 32; ++v) xw[k][v] = 0u;
+                for (int v = 0; v < 32; ++v) xw[v] = 0u;
 #pragma unroll
-                for (int t = 0; t < 8; ++t) xbs[k][t] = 0;
-                xd[k] = 0.0f;
+                for (int t = 0; t < 8; ++t) xbs[t] = 0;
             }
         }
     }
 
-    __device__ __forceinline__ void row(const Params& p, uint8_t*, const uint8_t* rowp, uint64_t r,
+    __device__ __forceinline__ void row(const Params& p, uint8_t* act, const uint8_t* rowp, uint64_t r,
                                         int lane) {
         const int j = lane >> 1, part = lane & 1;
         constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
+        const uint32_t passes = kXReg ? 1u : (p.nb + 15u) / 16u;
+        const ActImage img = q8k_image(act, p.nb);
         float acc0 = 0.0f, acc1 = 0.0f;
-#pragma unroll
-        for (int k = 0; k < kPasses; ++k) {
+#pragma unroll 1
+        for (uint32_t k = 0; k < passes; ++k) {
             const uint32_t i = 16u * k + j;
             const bool active = i < p.nb;
             int isum = 0, msum = 0;
-            float dw = 0.0f, dmw = 0.0f;
+            float dw = 0.0f, dmw = 0.0f, dx = 0.0f;
             if (active) {
                 const uint8_t* sb = rowp + size_t(i) * kBlockBytes;
-                if (kType == 12)
-                    q4k_half_sums(sb, part, xw[k], xbs[k], isum, msum, dw, dmw);
-                else
-                    q6k_half_sums(sb, part, xw[k], xbs[k], isum, dw);
+                if constexpr (kXReg) {
+                    dx = xd;
+                    if (kType == 12)
+                        q4k_half_sums(sb, part, xw, xbs, isum, msum, dw, dmw);
+                    else
+                        q6k_half_sums(sb, part, xw, xbs, isum, dw);
+                } else {
+                    uint32_t w[32];
+                    int bs[8];
+                    fetch_lane_x<kType>(img, i, part, w, bs, dx);
+                    if (kType == 12)
+                        q4k_half_sums(sb, part, w, bs, isum, msum, dw, dmw);
+                    else
+                        q6k_half_sums(sb, part, w, bs, isum, dw);
+                }
             }
             isum += __shfl_xor_sync(0xFFFFFFFFu, isum, 1);
             if (kType == 12) msum += __shfl_xor_sync(0xFFFFFFFFu, msum, 1);
             if (active) {
-                const float dd = __fmul_rn(dw, xd[k]);
+                const float dd = __fmul_rn(dw, dx);
                 float pi = __fmul_rn(dd, __int2float_rn(isum));
                 if (kType == 12) {
-                    const float dm = __fmul_rn(dmw, xd[k]);
+                    const float dm = __fmul_rn(dmw, dx);
                     pi = __fsub_rn(pi, __fmul_rn(dm, __int2float_rn(msum)));
                 }
                 if (k & 1)

@@ -8,6 +8,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -38,6 +39,9 @@ struct oracle_cuda_context {
     int device = 0;
     int sm_count = 0;
     int max_smem_optin = 0;
+    uint64_t smem_budget = 0;  // per-CTA shared memory for stream kernels (0 = all)
+    uint64_t stage_target = 36864;  // bytes per stage the stage plan aims for
+    uint32_t copy_chunk = 32768;    // largest single bulk copy
     uint32_t flags = 0;
     uint64_t launches = 0;
     DeviceStatus* status = nullptr;
@@ -158,15 +162,19 @@ oracle_cuda_status launch(oracle_cuda_context* ctx, Kernel kernel, dim3 grid, di
     return ORACLE_CUDA_OK;
 }
 
-// Stage plan for the row-streaming kernels: about 24 KB per stage (at most one
-// row per consumer warp), as many stages as shared memory allows (<= 16).
+// Stage plan for the row-streaming kernels: up to one row per consumer warp
+// and about stage_target bytes per stage, as many stages as the
+// CTA's shared-memory budget allows (<= 16).
 bool plan_stream(oracle_cuda_context* ctx, uint64_t rows, uint64_t row_bytes, uint32_t act_bytes, int ncw,
                  StreamParams& sp, uint32_t& grid) {
     grid = static_cast<uint32_t>(rows < uint64_t(ctx->sm_count) ? rows : ctx->sm_count);
-    const uint64_t budget = uint64_t(ctx->max_smem_optin) - stream_barrier_bytes(16) - act_bytes;
-    uint64_t R = 24576 / row_bytes;
-    if (R < 1) R = 1;
+    const uint64_t cta_budget = ctx->smem_budget ? ctx->smem_budget : uint64_t(ctx->max_smem_optin);
+    if (act_bytes + stream_barrier_bytes(16) + 2 * 128 > cta_budget) return false;
+    const uint64_t budget = cta_budget - stream_barrier_bytes(16) - act_bytes;
+    // one row per consumer warp per stage when rows are short, fewer when long
+    uint64_t R = ctx->stage_target / row_bytes;
     if (R > uint64_t(ncw)) R = ncw;
+    if (R < 1) R = 1;
     uint64_t stage = align_up(static_cast<uint32_t>(R * row_bytes + 32), 128u);
     while (R > 1 && stage * 2 > budget) {
         R -= 1;
@@ -184,11 +192,13 @@ bool plan_stream(oracle_cuda_context* ctx, uint64_t rows, uint64_t row_bytes, ui
     sp.stages = static_cast<uint32_t>(S);
     sp.stage_bytes = static_cast<uint32_t>(stage);
     sp.act_bytes = act_bytes;
+    sp.copy_chunk = ctx->copy_chunk;
     sp.status = ctx->status;
     return true;
 }
 
 constexpr int kConsumerWarps = 8;
+constexpr int kQ8KConsumerWarps = 16;
 
 template <class Consumer>
 oracle_cuda_status launch_stream(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t row_bytes,
@@ -206,16 +216,12 @@ oracle_cuda_status launch_stream(oracle_cuda_context* ctx, const uint8_t* w, uin
 template <uint32_t kType>
 oracle_cuda_status launch_q8k_typed(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t row_bytes,
                                     const MatvecQ8KParams& cp, cudaStream_t stream) {
-    const uint32_t passes = (cp.nb + 15) / 16;
     const uint32_t act = q8k_image_bytes(cp.nb);
-    switch (passes) {
-        case 1: return launch_stream<MatvecQ8KConsumer<kType, 1, kConsumerWarps>>(ctx, w, rows, row_bytes, act, cp, stream);
-        case 2: return launch_stream<MatvecQ8KConsumer<kType, 2, kConsumerWarps>>(ctx, w, rows, row_bytes, act, cp, stream);
-        case 3: return launch_stream<MatvecQ8KConsumer<kType, 3, kConsumerWarps>>(ctx, w, rows, row_bytes, act, cp, stream);
-        case 4: return launch_stream<MatvecQ8KConsumer<kType, 4, kConsumerWarps>>(ctx, w, rows, row_bytes, act, cp, stream);
-        default:
-            return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "Q8_K matvec supports rows of at most 16384 elements");
-    }
+    if (cp.nb <= 16)
+        return launch_stream<MatvecQ8KConsumer<kType, true, kQ8KConsumerWarps>>(ctx, w, rows, row_bytes, act, cp,
+                                                                                stream);
+    return launch_stream<MatvecQ8KConsumer<kType, false, kQ8KConsumerWarps>>(ctx, w, rows, row_bytes, act, cp,
+                                                                             stream);
 }
 
 // Q8_K contract, one activation vector per launch (x f32 or pre-quantized).
@@ -436,6 +442,23 @@ oracle_cuda_status oracle_cuda_create(int device, oracle_cuda_context** out) {
     ctx->device = device;
     ctx->sm_count = prop.multiProcessorCount;
     ctx->max_smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+    // All of it: with 16 consumer warps the register file already holds one
+    // stream CTA per SM, so a deep stage ring (prefetching while a programmatic
+    // dependent launch waits for its predecessor) is worth more than room for a
+    // second CTA.  ORACLE_CUDA_SMEM_BUDGET (bytes) overrides it for tuning.
+    ctx->smem_budget = prop.sharedMemPerBlockOptin;
+    if (const char* env = std::getenv("ORACLE_CUDA_STAGE_BYTES")) {
+        const unsigned long long v = std::strtoull(env, nullptr, 10);
+        if (v >= 4096 && v <= 200000) ctx->stage_target = v;
+    }
+    if (const char* env = std::getenv("ORACLE_CUDA_COPY_CHUNK")) {
+        const unsigned long long v = std::strtoull(env, nullptr, 10);
+        if (v >= 4096 && v <= 196608 && v % 16 == 0) ctx->copy_chunk = static_cast<uint32_t>(v);
+    }
+    if (const char* env = std::getenv("ORACLE_CUDA_SMEM_BUDGET")) {
+        const unsigned long long v = std::strtoull(env, nullptr, 10);
+        if (v >= 16384 && v <= static_cast<unsigned long long>(ctx->max_smem_optin)) ctx->smem_budget = v;
+    }
     if ((e = cudaMalloc(reinterpret_cast<void**>(&ctx->status), sizeof(DeviceStatus))) != cudaSuccess) {
         delete ctx;
         return cuda_fail(nullptr, e, "cudaMalloc(status)");

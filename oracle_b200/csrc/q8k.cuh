@@ -17,6 +17,8 @@
 
 namespace oracle_cuda {
 
+__host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
 // One warp quantizes one 256-element block.  Lane l owns elements 8l..8l+7.
 // Outputs: q_lo/q_hi = the lane's 8 quants (little-endian bytes), bsum16 = the
 // sum over the 16-element group (lanes 2g, 2g+1) containing the lane, d.
@@ -26,9 +28,7 @@ struct Q8KLane {
     float d;
 };
 
-__device__ __forceinline__ Q8KLane quantize_q8k_block_warp(const float* xb, int lane,
-                                                           bool aligned16) {
-    float v[8];
+__device__ __forceinline__ void load_lane8(const float* xb, int lane, bool aligned16, float (&v)[8]) {
     if (aligned16) {
         const float4 a = reinterpret_cast<const float4*>(xb)[2 * lane];
         const float4 b = reinterpret_cast<const float4*>(xb)[2 * lane + 1];
@@ -38,6 +38,10 @@ __device__ __forceinline__ Q8KLane quantize_q8k_block_warp(const float* xb, int 
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = xb[8 * lane + j];
     }
+}
+
+// Quantize one block from the lane's 8 values (elements 8*lane .. 8*lane+7).
+__device__ __forceinline__ Q8KLane quantize_q8k_lane_values(const float (&v)[8], int lane) {
     // first strictly-greater scan inside the lane, then a warp arg-max that
     // prefers the lower index on ties: the result is the sequential scan's.
     float amax = 0.0f, vmax = 0.0f;
@@ -86,6 +90,12 @@ __device__ __forceinline__ Q8KLane quantize_q8k_block_warp(const float* xb, int 
     return out;
 }
 
+__device__ __forceinline__ Q8KLane quantize_q8k_block_warp(const float* xb, int lane, bool aligned16) {
+    float v[8];
+    load_lane8(xb, lane, aligned16, v);
+    return quantize_q8k_lane_values(v, lane);
+}
+
 // Standalone quantizer: one warp per (activation row, block); GGML byte layout
 // (292 bytes per block, 4-byte aligned fields).
 __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x,
@@ -106,27 +116,78 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restri
     if ((lane & 1) == 0) reinterpret_cast<int16_t*>(ob + 260)[lane / 2] = static_cast<int16_t>(r.bsum16);
 }
 
-// Shared-memory activation image used by the matvec kernels.  For block i:
-// qs at q + 256*i (natural element order), 16-element sums at bs + 16*i,
-// scale at d[i].
+// Shared-memory activation image used by the matvec kernels.  Quants are
+// stored in 128-byte rows, row rho = 2*i + h holding elements 128h..128h+127 of
+// block i; the 16-byte chunk v of row rho sits at chunk position
+// v ^ (rho & 7), so the eight lanes of a quarter-warp reading eight consecutive
+// rows hit eight different bank groups.  bs16[16*i + g] holds the sum of the
+// 16-element group g, bs32[8*i + j] that of the 32-element sub-block j, d[i]
+// the block scale.
 struct ActImage {
     int8_t* q;
-    int* bs;
+    int* bs16;
+    int* bs32;
     float* d;
 };
 
+__host__ __device__ inline uint32_t q8k_image_bytes(uint32_t nb) {
+    return align_up(nb * 256u, 128u) + align_up(nb * 64u, 128u) + align_up(nb * 32u, 128u) +
+           align_up(nb * 4u, 128u);
+}
+
+__device__ __forceinline__ ActImage q8k_image(uint8_t* act, uint32_t nb) {
+    ActImage img;
+    uint32_t off = 0;
+    img.q = reinterpret_cast<int8_t*>(act + off);
+    off += align_up(nb * 256u, 128u);
+    img.bs16 = reinterpret_cast<int*>(act + off);
+    off += align_up(nb * 64u, 128u);
+    img.bs32 = reinterpret_cast<int*>(act + off);
+    off += align_up(nb * 32u, 128u);
+    img.d = reinterpret_cast<float*>(act + off);
+    return img;
+}
+
+// Byte offset of element e (0..255) of block i in the swizzled quant rows.
+__device__ __forceinline__ uint32_t q8k_image_offset(uint32_t i, uint32_t e) {
+    const uint32_t rho = 2u * i + (e >> 7);
+    return rho * 128u + 16u * (((e >> 4) & 7u) ^ (rho & 7u)) + (e & 15u);
+}
+
+// Lane l of a warp holds elements 8l..8l+7 of block i and the sum of its
+// 16-element group (lanes 2g, 2g+1 share group g); store them in the image.
+__device__ __forceinline__ void store_block_to_image(ActImage img, uint32_t i, int lane, uint32_t q_lo,
+                                                     uint32_t q_hi, int bsum16, float d) {
+    uint2* dst = reinterpret_cast<uint2*>(img.q + q8k_image_offset(i, 8u * lane));
+    *dst = make_uint2(q_lo, q_hi);
+    const int bsum32 = bsum16 + __shfl_xor_sync(0xFFFFFFFFu, bsum16, 2);
+    if ((lane & 1) == 0) img.bs16[16 * i + lane / 2] = bsum16;
+    if ((lane & 3) == 0) img.bs32[8 * i + lane / 4] = bsum32;
+    if (lane == 0) img.d[i] = d;
+}
+
 // Quantize `nb` blocks of x into the image, one block per warp, warps
 // [0, nwarps) cooperating.  The caller synchronises afterwards.
+// The loads of up to kBatch blocks are issued together before any of them is
+// reduced, so a warp pays one memory round trip per kBatch blocks.
 __device__ __forceinline__ void quantize_to_image(const float* __restrict__ x, uint32_t nb,
                                                   ActImage img, int warp, int nwarps, int lane) {
+    constexpr int kBatch = 4;
     const bool aligned16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
-    for (uint32_t i = warp; i < nb; i += nwarps) {
-        const Q8KLane r = quantize_q8k_block_warp(x + 256ull * i, lane, aligned16);
-        uint32_t* qs = reinterpret_cast<uint32_t*>(img.q + 256 * i);
-        qs[2 * lane] = r.q_lo;
-        qs[2 * lane + 1] = r.q_hi;
-        if ((lane & 1) == 0) img.bs[16 * i + lane / 2] = r.bsum16;
-        if (lane == 0) img.d[i] = r.d;
+    for (uint32_t base = warp; base < nb; base += uint32_t(nwarps) * kBatch) {
+        float v[kBatch][8];
+#pragma unroll
+        for (int m = 0; m < kBatch; ++m) {
+            const uint32_t i = base + uint32_t(m) * nwarps;
+            if (i < nb) load_lane8(x + 256ull * i, lane, aligned16, v[m]);
+        }
+#pragma unroll
+        for (int m = 0; m < kBatch; ++m) {
+            const uint32_t i = base + uint32_t(m) * nwarps;
+            if (i >= nb) break;
+            const Q8KLane r = quantize_q8k_lane_values(v[m], lane);
+            store_block_to_image(img, i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
+        }
     }
 }
 
@@ -136,11 +197,9 @@ __device__ __forceinline__ void load_q8k_to_image(const uint8_t* __restrict__ q8
     for (uint32_t i = warp; i < nb; i += nwarps) {
         const uint8_t* b = q8k + 292ull * i;
         const uint32_t* qs = reinterpret_cast<const uint32_t*>(b + 4);
-        uint32_t* dst = reinterpret_cast<uint32_t*>(img.q + 256 * i);
-        dst[2 * lane] = qs[2 * lane];
-        dst[2 * lane + 1] = qs[2 * lane + 1];
-        if (lane < 16) img.bs[16 * i + lane] = reinterpret_cast<const int16_t*>(b + 260)[lane];
-        if (lane == 0) img.d[i] = *reinterpret_cast<const float*>(b);
+        const int bsum16 = reinterpret_cast<const int16_t*>(b + 260)[lane / 2];
+        store_block_to_image(img, i, lane, qs[2 * lane], qs[2 * lane + 1], bsum16,
+                             *reinterpret_cast<const float*>(b));
     }
 }
 

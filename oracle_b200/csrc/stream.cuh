@@ -7,9 +7,14 @@
 // whose completion is counted in bytes on a per-stage "full" mbarrier.  The
 // 16-byte aligned interior of each stage moves by bulk copy; the < 16-byte
 // head and tail of an unaligned stage are copied by producer lanes, so any
-// row geometry works.  Consumer warps take rows round-robin, wait on the
-// stage's full barrier, compute, and arrive once per row on the stage's
-// "empty" barrier (expected count R), which frees the slot for stage t + S.
+// row geometry works.  Rows go to consumer warps round-robin (CTA row q to
+// warp q % kWarps).  Every consumer warp walks EVERY stage in order: it waits
+// on the stage's full barrier, computes its rows of that stage (possibly
+// none), and arrives once on the stage's "empty" barrier (expected count
+// kWarps), which frees the slot for stage t + S.  Walking all stages keeps each
+// warp's view of a slot's phases strictly sequential: a warp never waits on a
+// phase two uses ahead of a slot, where the parity test of the wait would be
+// satisfied by the older phase.
 //
 // Shared memory: [full[S], empty[S]] [activation image] [S stages].  Global
 // byte g of stage t sits at stage_base + (g - floor16(first byte of stage t)).
@@ -19,6 +24,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "q8k.cuh"
 
 namespace oracle_cuda {
 
@@ -30,10 +36,9 @@ struct StreamParams {
     uint32_t stages;          // S
     uint32_t stage_bytes;     // bytes reserved per stage (>= R*row_bytes + 32, multiple of 128)
     uint32_t act_bytes;       // activation image bytes (multiple of 128)
+    uint32_t copy_chunk;      // largest single bulk copy (multiple of 16)
     DeviceStatus* status;
 };
-
-__host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 __host__ __device__ inline uint32_t stream_barrier_bytes(uint32_t stages) {
     return align_up(16u * stages, 128u);
@@ -73,9 +78,13 @@ __global__ void __launch_bounds__((Consumer::kWarps + 1) * 32, 1)
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], R);
+            mbar_init(&empty[s], NCW);
         }
         fence_mbar_init();
+        // The next kernel in the stream may launch now: it only reads its own
+        // (immutable) weights until its own pdl_wait, so its CTAs can start
+        // streaming on each SM as soon as this kernel's CTA there exits.
+        pdl_launch_dependents();
     }
     __syncthreads();
 
@@ -111,9 +120,9 @@ __global__ void __launch_bounds__((Consumer::kWarps + 1) * 32, 1)
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive_expect_tx(&full[s], tx);
-                constexpr uint32_t kChunk = 32768;
-                for (uint32_t off = 0; off < tx; off += kChunk) {
-                    const uint32_t n = tx - off < kChunk ? tx - off : kChunk;
+                const uint32_t chunk = sp.copy_chunk;
+                for (uint32_t off = 0; off < tx; off += chunk) {
+                    const uint32_t n = tx - off < chunk ? tx - off : chunk;
                     bulk_copy_g2s(dst + (A - a16) + off, reinterpret_cast<const void*>(A + off), n,
                                   &full[s], policy);
                 }
@@ -129,22 +138,24 @@ __global__ void __launch_bounds__((Consumer::kWarps + 1) * 32, 1)
     }
 
     // ---------------- consumer warps
-    pdl_wait();  // activations may come from the preceding kernel
+    pdl_wait();  // activations may come from the preceding kernel, and it may still read y
     Consumer cons;
     cons.prologue(cp, act, warp, lane);
     named_barrier_sync(1, NCW * 32);
-    if (threadIdx.x == 0) pdl_launch_dependents();
     cons.load(cp, act, warp, lane);
 
-    for (uint32_t q = warp; q < nrows; q += NCW) {
-        const uint32_t t = q / R;
+    for (uint32_t t = 0; t < T; ++t) {
         const uint32_t s = t % S;
         const bool ok = mbar_wait(&full[s], (t / S) & 1, sp.status, 3);
         if (!__all_sync(0xFFFFFFFFu, ok)) break;
-        const uintptr_t a16 = (wbase + (r0 + uint64_t(t) * R) * sp.row_bytes) & ~uintptr_t(15);
-        const uint8_t* rowp = stage0 + size_t(s) * sp.stage_bytes +
-                              ((wbase + (r0 + q) * sp.row_bytes) - a16);
-        cons.row(cp, act, rowp, r0 + q, lane);
+        const uint32_t q_lo = t * R;
+        const uint32_t q_hi = q_lo + R < nrows ? q_lo + R : nrows;
+        const uintptr_t a16 = (wbase + (r0 + q_lo) * sp.row_bytes) & ~uintptr_t(15);
+        const uint8_t* slot = stage0 + size_t(s) * sp.stage_bytes;
+        // first row of this stage owned by this warp
+        uint32_t q = q_lo + ((warp + NCW - q_lo % NCW) % NCW);
+        for (; q < q_hi; q += NCW)
+            cons.row(cp, act, slot + ((wbase + (r0 + q) * sp.row_bytes) - a16), r0 + q, lane);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
