@@ -157,6 +157,33 @@ oracle_cuda_status oracle_cuda_matvec_q8k_prequantized(oracle_cuda_context* ctx,
                                                        const void* q8k_dev, uint64_t q8k_nbytes,
                                                        float* y_dev, uint64_t y_len, void* stream);
 
+/* Matvec program: up to ORACLE_CUDA_PROGRAM_MAX_OPS Q8_K-contract matvecs
+ * (q4_K / q6_K weights) in ONE persistent launch.  The weights of all ops
+ * stream through one shared-memory ring without pausing at op boundaries;
+ * each op quantizes its f32 activation in-kernel, exactly like
+ * oracle_cuda_storage_matvec (bit-identical results).  An op with
+ * after_previous = 1 reads an activation written by an earlier op of the same
+ * call: it waits, on the device, for every CTA to finish all earlier ops
+ * (bounded; a timeout is reported by oracle_cuda_device_status).  Ops without
+ * it must not read what an earlier op of the call writes.  Programs launched
+ * from one context must not run concurrently with each other (they share the
+ * completion counters).  No Oracle counterpart: Oracle runs each projection
+ * as its own call (src/runtime/qwen35_block.cpp:108-119). */
+#define ORACLE_CUDA_PROGRAM_MAX_OPS 16
+typedef struct oracle_cuda_matvec_op {
+    uint32_t type;           /* 12 (q4_K) or 14 (q6_K) */
+    uint32_t after_previous; /* 1: x is produced by an earlier op of this call */
+    uint64_t rows;
+    uint64_t cols;
+    const void* w_dev;
+    uint64_t w_nbytes;
+    const float* x_dev;      /* cols floats */
+    float* y_dev;            /* rows floats */
+} oracle_cuda_matvec_op;
+
+oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops,
+                                              uint32_t n_ops, void* stream);
+
 /* ------------------------------------------------------------------ resident weights
  * Oracle's weights are immutable GGUF bytes in a read-only mapping
  * (MappedGgufModel, include/oracle/model/mapped_gguf.hpp:56-59).  They are

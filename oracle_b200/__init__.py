@@ -75,6 +75,17 @@ _proto("oracle_cuda_decode_rows", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, 
 _proto("oracle_cuda_quantize_q8_k", [_vp, _vp, _u64, _u64, _vp, _u64, _vp])
 _proto("oracle_cuda_storage_matvec", [_vp, _i32, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _u64, _vp])
 _proto("oracle_cuda_matvec_q8k_prequantized", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _u64, _vp])
+
+
+class MatvecOp(C.Structure):
+    """oracle_cuda_matvec_op of include/oracle_cuda.h."""
+    _fields_ = [("type", C.c_uint32), ("after_previous", C.c_uint32), ("rows", C.c_uint64),
+                ("cols", C.c_uint64), ("w_dev", C.c_void_p), ("w_nbytes", C.c_uint64),
+                ("x_dev", C.c_void_p), ("y_dev", C.c_void_p)]
+
+
+PROGRAM_MAX_OPS = 16
+_proto("oracle_cuda_matvec_program", [_vp, C.POINTER(MatvecOp), _u32, _vp])
 _proto("oracle_cuda_weight_upload", [_vp, _u32, _u64, _u64, _vp, _u64, _u64, _u64, C.POINTER(_vp)])
 _proto("oracle_cuda_weight_free", [_vp])
 _proto("oracle_cuda_weight_info", [_vp, C.POINTER(_u32), _u64p, _u64p, _u64p, C.POINTER(_vp), _u64p])
@@ -278,6 +289,14 @@ class Context:
         self._check(_lib.oracle_cuda_matvec_q8k_prequantized(
             self._h, qtype, rows, cols, _addr(w), _nbytes(w), _addr(q8k), _nbytes(q8k), _addr(y), _numel(y),
             _stream(stream)))
+
+    def matvec_program(self, ops, stream=None) -> None:
+        """ops: sequence of (qtype, rows, cols, w, x, y, after_previous) with
+        device tensors (or addresses); one persistent launch (Q8_K contract)."""
+        arr = (MatvecOp * len(ops))()
+        for i, (qtype, rows, cols, w, x, y, after) in enumerate(ops):
+            arr[i] = MatvecOp(qtype, 1 if after else 0, rows, cols, _addr(w), _nbytes(w), _addr(x), _addr(y))
+        self._check(_lib.oracle_cuda_matvec_program(self._h, arr, len(ops), _stream(stream)))
 
     # -------------------------------------------------------------- resident weights
     def upload(self, qtype, rows, cols, host: np.ndarray, row_begin=0, row_end=None) -> Weight:

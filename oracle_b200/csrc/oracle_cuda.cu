@@ -20,6 +20,7 @@
 #include "layout.hpp"
 #include "matvec_f32.cuh"
 #include "matvec_q8k.cuh"
+#include "program.cuh"
 #include "q8k.cuh"
 
 using namespace oracle_cuda;
@@ -42,9 +43,13 @@ struct oracle_cuda_context {
     uint64_t smem_budget = 0;  // per-CTA shared memory for stream kernels (0 = all)
     uint64_t stage_target = 36864;  // bytes per stage the stage plan aims for
     uint32_t copy_chunk = 32768;    // largest single bulk copy
+    uint32_t max_inflight = 16;     // stages a program producer keeps in flight
     uint32_t flags = 0;
     uint64_t launches = 0;
     DeviceStatus* status = nullptr;
+    unsigned int* program_counters = nullptr;  // kProgramMaxOps + 1, zero between launches
+    uint8_t* image_scratch = nullptr;          // prebuilt activation images of programs
+    uint64_t image_scratch_bytes = 0;
     std::string last_error;
     std::set<const void*> smem_configured;
     // resident copies for the host-pointer drop-ins
@@ -199,6 +204,9 @@ bool plan_stream(oracle_cuda_context* ctx, uint64_t rows, uint64_t row_bytes, ui
 
 constexpr int kConsumerWarps = 8;
 constexpr int kQ8KConsumerWarps = 16;
+// The program kernel carries both ops' code paths: with 15 consumer warps + 1
+// producer (4 warps per SM sub-partition) it may use 128 registers, unspilled.
+constexpr int kProgramWarps = 15;
 
 template <class Consumer>
 oracle_cuda_status launch_stream(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t row_bytes,
@@ -451,6 +459,10 @@ oracle_cuda_status oracle_cuda_create(int device, oracle_cuda_context** out) {
         const unsigned long long v = std::strtoull(env, nullptr, 10);
         if (v >= 4096 && v <= 200000) ctx->stage_target = v;
     }
+    if (const char* env = std::getenv("ORACLE_CUDA_MAX_INFLIGHT")) {
+        const unsigned long long v = std::strtoull(env, nullptr, 10);
+        if (v >= 1 && v <= 16) ctx->max_inflight = static_cast<uint32_t>(v);
+    }
     if (const char* env = std::getenv("ORACLE_CUDA_COPY_CHUNK")) {
         const unsigned long long v = std::strtoull(env, nullptr, 10);
         if (v >= 4096 && v <= 196608 && v % 16 == 0) ctx->copy_chunk = static_cast<uint32_t>(v);
@@ -464,6 +476,13 @@ oracle_cuda_status oracle_cuda_create(int device, oracle_cuda_context** out) {
         return cuda_fail(nullptr, e, "cudaMalloc(status)");
     }
     cudaMemset(ctx->status, 0, sizeof(DeviceStatus));
+    if ((e = cudaMalloc(reinterpret_cast<void**>(&ctx->program_counters),
+                        (kProgramMaxOps + 1) * sizeof(unsigned int))) != cudaSuccess) {
+        cudaFree(ctx->status);
+        delete ctx;
+        return cuda_fail(nullptr, e, "cudaMalloc(program counters)");
+    }
+    cudaMemset(ctx->program_counters, 0, (kProgramMaxOps + 1) * sizeof(unsigned int));
     *out = ctx;
     return ORACLE_CUDA_OK;
 }
@@ -481,6 +500,8 @@ oracle_cuda_status oracle_cuda_destroy(oracle_cuda_context* ctx) {
     if (ctx->dev_x) cudaFree(ctx->dev_x);
     if (ctx->dev_y) cudaFree(ctx->dev_y);
     if (ctx->status) cudaFree(ctx->status);
+    if (ctx->program_counters) cudaFree(ctx->program_counters);
+    if (ctx->image_scratch) cudaFree(ctx->image_scratch);
     delete ctx;
     return ORACLE_CUDA_OK;
 }
@@ -500,6 +521,9 @@ oracle_cuda_status oracle_cuda_device_status(oracle_cuda_context* ctx) {
     ORACLE_CUDA_TRY(ctx, cudaDeviceSynchronize(), "cudaDeviceSynchronize");
     ORACLE_CUDA_TRY(ctx, cudaMemcpy(&st, ctx->status, sizeof st, cudaMemcpyDeviceToHost), "cudaMemcpy(status)");
     ORACLE_CUDA_TRY(ctx, cudaMemset(ctx->status, 0, sizeof st), "cudaMemset(status)");
+    if (st.code != kDevOk)  // an aborted program may have left its counters set
+        ORACLE_CUDA_TRY(ctx, cudaMemset(ctx->program_counters, 0, (kProgramMaxOps + 1) * sizeof(unsigned int)),
+                        "cudaMemset(program counters)");
     if (st.code != kDevOk)
         return fail(ctx, ORACLE_CUDA_DEVICE_TIMEOUT,
                     "kernel wait timed out at site " + std::to_string(st.where) + " in block " +
@@ -604,6 +628,110 @@ oracle_cuda_status oracle_cuda_matvec_q8k_prequantized(oracle_cuda_context* ctx,
         if (s != ORACLE_CUDA_OK) return s;
     }
     return ok(ctx);
+}
+
+oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops,
+                                              uint32_t n_ops, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (!ops || n_ops == 0 || n_ops > kProgramMaxOps)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                    "a matvec program holds 1 to " + std::to_string(kProgramMaxOps) + " ops");
+    ProgramParams pp{};
+    pp.n_ops = n_ops;
+    uint64_t max_rows = 0, stage = 0;
+    uint32_t act_total = 0;
+    for (uint32_t k = 0; k < n_ops; ++k) {
+        const oracle_cuda_matvec_op& o = ops[k];
+        uint64_t rb = 0, batch = 0;
+        oracle_cuda_status st = validate_matvec(ctx, ORACLE_CUDA_CONTRACT_Q8K, o.type, o.rows, o.cols, o.w_nbytes,
+                                                o.cols, o.rows, &rb, &batch);
+        if (st != ORACLE_CUDA_OK) {
+            ctx->last_error = "op " + std::to_string(k) + ": " + ctx->last_error;
+            return st;
+        }
+        if (Error e = check_weight_pointer(o.type, o.w_dev)) return fail(ctx, e);
+        if (!o.x_dev || !o.y_dev)
+            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "op " + std::to_string(k) + ": null activation or output");
+        ProgramOp& p = pp.ops[k];
+        p.w = static_cast<const uint8_t*>(o.w_dev);
+        p.x = o.x_dev;
+        p.y = o.y_dev;
+        p.rows = o.rows;
+        p.row_bytes = rb;
+        p.type = o.type;
+        p.nb = static_cast<uint32_t>(o.cols / 256);
+        p.after_previous = (o.after_previous && k > 0) ? 1u : 0u;
+        if (p.after_previous) pp.ops[k - 1].publish = 1u;
+        p.act_offset = act_total;
+        act_total += q8k_image_bytes(p.nb);
+        uint64_t R = ctx->stage_target / rb;
+        if (R > uint64_t(kProgramWarps)) R = kProgramWarps;
+        if (R < 1) R = 1;
+        p.rows_per_stage = static_cast<uint32_t>(R);
+        const uint64_t sb = align_up(static_cast<uint32_t>(R * rb + 32), 128u);
+        if (sb > stage) stage = sb;
+        if (o.rows > max_rows) max_rows = o.rows;
+    }
+    pp.act_bytes = act_total;
+    // Images of ops whose activation comes from outside the launch are built
+    // once by quantize_images_kernel into the scratch region, laid out with
+    // the dependent ops' images last, so one contiguous copy serves them.
+    ImageJobs jobs{};
+    uint32_t prebuilt = 0, blocks = 0;
+    {
+        uint32_t off = 0;
+        for (uint32_t k = 0; k < n_ops; ++k)
+            if (!pp.ops[k].after_previous) {
+                pp.ops[k].act_offset = off;
+                pp.ops[k].prebuilt = 1u;
+                jobs.x[jobs.n_jobs] = pp.ops[k].x;
+                jobs.nb[jobs.n_jobs] = pp.ops[k].nb;
+                jobs.offset[jobs.n_jobs] = off;
+                jobs.first_block[jobs.n_jobs] = blocks;
+                blocks += pp.ops[k].nb;
+                jobs.n_jobs++;
+                off += q8k_image_bytes(pp.ops[k].nb);
+            }
+        prebuilt = off;
+        jobs.first_block[jobs.n_jobs] = blocks;
+        for (uint32_t k = 0; k < n_ops; ++k)
+            if (pp.ops[k].after_previous) {
+                pp.ops[k].act_offset = off;
+                off += q8k_image_bytes(pp.ops[k].nb);
+            }
+    }
+    const uint64_t budget = ctx->smem_budget - stream_barrier_bytes(16) - pp.act_bytes;
+    if (pp.act_bytes > 96 * 1024 || stage * 2 > budget)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "matvec program rows too long for the shared-memory stage ring");
+    uint64_t S = budget / stage;
+    if (S > 16) S = 16;
+    pp.stages = static_cast<uint32_t>(S);
+    pp.stage_bytes = static_cast<uint32_t>(stage);
+    pp.copy_chunk = ctx->copy_chunk;
+    pp.max_inflight = ctx->max_inflight;
+    pp.prebuilt_bytes = prebuilt;
+    pp.counters = ctx->program_counters;
+    pp.status = ctx->status;
+    const uint32_t grid = static_cast<uint32_t>(max_rows < uint64_t(ctx->sm_count) ? max_rows : ctx->sm_count);
+    const size_t smem = stream_barrier_bytes(pp.stages) + pp.act_bytes + size_t(pp.stages) * pp.stage_bytes;
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (prebuilt > 0) {
+        oracle_cuda_status gs = grow_device(ctx, ctx->image_scratch, ctx->image_scratch_bytes, prebuilt);
+        if (gs != ORACLE_CUDA_OK) return gs;
+        pp.images = ctx->image_scratch;
+        const uint32_t qgrid = (blocks * 32 + 255) / 256;
+        gs = launch(ctx, quantize_images_kernel, dim3(qgrid), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                    (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, jobs, ctx->image_scratch);
+        if (gs != ORACLE_CUDA_OK) return gs;
+    }
+    int types = 0;
+    for (uint32_t k = 0; k < n_ops; ++k) types |= ops[k].type == kTypeQ4_K ? 1 : 2;
+    auto kernel = types == 1 ? matvec_program_kernel<kProgramWarps, 1>
+                  : types == 2 ? matvec_program_kernel<kProgramWarps, 2>
+                               : matvec_program_kernel<kProgramWarps, 3>;
+    oracle_cuda_status st = launch(ctx, kernel, dim3(grid), dim3((kProgramWarps + 1) * 32), smem,
+                                   static_cast<cudaStream_t>(stream), (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, pp);
+    return st == ORACLE_CUDA_OK ? ok(ctx) : st;
 }
 
 oracle_cuda_status oracle_cuda_weight_upload(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,

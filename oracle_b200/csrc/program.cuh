@@ -1,0 +1,331 @@
+// program.cuh -- persistent multi-matvec kernel ("matvec program") for decode.
+//
+// One launch runs a list of Q8_K-contract matvecs (Q4_K or Q6_K weights).
+// Every CTA owns a balanced row range of EVERY op.  Its producer warp streams
+// the weights of op 0, then op 1, ... through one shared-memory stage ring
+// without pausing between ops, so HBM stays busy across op boundaries; the
+// consumer warps follow op by op: quantize that op's activation into the
+// shared image (q8k.cuh), then compute its rows exactly as matvec_q8k.cuh does
+// (same canonical f32 order, bit-identical results).
+//
+// An op flagged `after_previous` reads an activation written by earlier ops of
+// the same launch.  Its consumers first wait for every CTA to finish all
+// earlier ops: each CTA publishes completion of op k by a release increment of
+// counters[k] after its last row, and waiters spin (bounded by kWaitNs, then
+// record a timeout and stop) until counters[k-1] == gridDim.x.  The weight
+// stream never waits on it.  All CTAs must be co-resident, which holds because
+// the grid never exceeds the SM count and each CTA takes more than half of an
+// SM's shared memory.
+#pragma once
+
+#include "matvec_q8k.cuh"
+#include "stream.cuh"
+
+namespace oracle_cuda {
+
+constexpr int kProgramMaxOps = 16;
+
+struct ProgramOp {
+    const uint8_t* w;
+    const float* x;
+    float* y;
+    uint64_t rows;
+    uint64_t row_bytes;
+    uint32_t type;            // 12 (q4_K) or 14 (q6_K)
+    uint32_t nb;              // super-blocks per row
+    uint32_t rows_per_stage;  // R for this op
+    uint32_t after_previous;  // 1: wait for all earlier ops before reading x
+    uint32_t publish;         // 1: a later op depends on this one; count completions
+    uint32_t act_offset;      // byte offset of this op's activation image
+    uint32_t prebuilt;        // 1: the image was built by quantize_images_kernel
+};
+
+struct ProgramParams {
+    ProgramOp ops[kProgramMaxOps];
+    uint32_t n_ops;
+    uint32_t stages;
+    uint32_t stage_bytes;
+    uint32_t act_bytes;
+    uint32_t copy_chunk;
+    uint32_t max_inflight;   // at most this many issued stages not yet landed (>= 1)
+    const uint8_t* images;   // prebuilt images (global, same layout as shared memory)
+    uint32_t prebuilt_bytes; // bytes of the prebuilt region (multiple of 16)
+    unsigned int* counters;  // kProgramMaxOps completion counters + 1 exit counter, zero at launch
+    DeviceStatus* status;
+};
+
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(unsigned int* p, unsigned int v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until *counter >= target; false (and a recorded timeout) if it
+// does not happen within kWaitNs.
+__device__ __forceinline__ bool wait_counter(const unsigned int* counter, unsigned int target, DeviceStatus* st,
+                                             unsigned int where) {
+    if (ld_acquire_gpu(counter) >= target) return true;
+    const unsigned long long t0 = global_timer_ns();
+    while (ld_acquire_gpu(counter) < target) {
+        if (global_timer_ns() - t0 > kWaitNs) {
+            report_timeout(st, where);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
+// Consumer for one op of a program: Q4_K or Q6_K chosen at run time; rows of
+// at most 16 super-blocks keep the lane's activation slice in registers.
+template <int kWarps>
+struct ProgramConsumer {
+    uint32_t xw[32];
+    int xbs[8];
+    float xd = 0.0f;
+
+    __device__ __forceinline__ void prologue(const ProgramOp& op, uint8_t* act, int warp, int lane) {
+        quantize_to_image(op.x, op.nb, q8k_image(act + op.act_offset, op.nb), warp, kWarps, lane);
+    }
+
+    __device__ __forceinline__ void load(const ProgramOp& op, uint8_t* act, int lane) {
+        const uint32_t i = lane >> 1;
+        if (op.nb <= 16 && i < op.nb) {
+            if (op.type == 12)
+                fetch_lane_x<12>(q8k_image(act + op.act_offset, op.nb), i, lane & 1, xw, xbs, xd);
+            else
+                fetch_lane_x<14>(q8k_image(act + op.act_offset, op.nb), i, lane & 1, xw, xbs, xd);
+        }
+    }
+
+    template <uint32_t kType>
+    __device__ __forceinline__ void row_typed(const ProgramOp& op, uint8_t* act, const uint8_t* rowp, uint64_t r,
+                                              int lane) {
+        const int j = lane >> 1, part = lane & 1;
+        constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
+        const bool xreg = op.nb <= 16;
+        const uint32_t passes = xreg ? 1u : (op.nb + 15u) / 16u;
+        const ActImage img = q8k_image(act + op.act_offset, op.nb);
+        float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 1
+        for (uint32_t k = 0; k < passes; ++k) {
+            const uint32_t i = 16u * k + j;
+            const bool active = i < op.nb;
+            int isum = 0, msum = 0;
+            float dw = 0.0f, dmw = 0.0f, dx = 0.0f;
+            if (active) {
+                const uint8_t* sb = rowp + size_t(i) * kBlockBytes;
+                if (xreg) {
+                    dx = xd;
+                    if (kType == 12)
+                        q4k_half_sums(sb, part, xw, xbs, isum, msum, dw, dmw);
+                    else
+                        q6k_half_sums(sb, part, xw, xbs, isum, dw);
+                } else {
+                    uint32_t w[32];
+                    int bs[8];
+                    fetch_lane_x<kType>(img, i, part, w, bs, dx);
+                    if (kType == 12)
+                        q4k_half_sums(sb, part, w, bs, isum, msum, dw, dmw);
+                    else
+                        q6k_half_sums(sb, part, w, bs, isum, dw);
+                }
+            }
+            isum += __shfl_xor_sync(0xFFFFFFFFu, isum, 1);
+            if (kType == 12) msum += __shfl_xor_sync(0xFFFFFFFFu, msum, 1);
+            if (active) {
+                const float dd = __fmul_rn(dw, dx);
+                float pi = __fmul_rn(dd, __int2float_rn(isum));
+                if (kType == 12) pi = __fsub_rn(pi, __fmul_rn(__fmul_rn(dmw, dx), __int2float_rn(msum)));
+                if (k & 1)
+                    acc1 = __fadd_rn(acc1, pi);
+                else
+                    acc0 = __fadd_rn(acc0, pi);
+            }
+        }
+        float v = __fadd_rn(acc0, acc1);
+#pragma unroll
+        for (int off = 16; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+        if (lane == 0) op.y[r] = v;
+    }
+};
+
+// kTypes: 1 = every op is q4_K, 2 = every op is q6_K, 3 = mixed.
+template <int kWarps, int kTypes>
+__global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(const __grid_constant__ ProgramParams pp) {
+    constexpr int NCW = kWarps;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + pp.stages;
+    uint8_t* act = smem + stream_barrier_bytes(pp.stages);
+    uint8_t* stage0 = act + pp.act_bytes;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t S = pp.stages;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NCW);
+        }
+        fence_mbar_init();
+        pdl_launch_dependents();
+    }
+    __syncthreads();
+
+    if (warp == NCW) {
+        // ---------------- producer: every op's stages, back to back
+        const uint64_t policy = l2_policy_evict_first();
+        uint32_t g = 0;  // global stage counter across ops
+        bool ok = true;
+        for (uint32_t k = 0; k < pp.n_ops && ok; ++k) {
+            const ProgramOp op = pp.ops[k];
+            const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
+            const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
+            const uint32_t R = op.rows_per_stage;
+            const uint32_t T = static_cast<uint32_t>((r1 - r0 + R - 1) / R);
+            const uintptr_t wbase = reinterpret_cast<uintptr_t>(op.w);
+            for (uint32_t t = 0; t < T; ++t, ++g) {
+                const uint32_t s = g % S;
+                bool w_ok = true;
+                // Keep at most max_inflight stages in the memory system: deeper
+                // queues add latency to the activation loads that share them.
+                if (lane == 0 && g >= pp.max_inflight) {
+                    const uint32_t h = g - pp.max_inflight;
+                    w_ok = mbar_wait(&full[h % S], (h / S) & 1, pp.status, 15);
+                }
+                if (lane == 0 && w_ok && g >= S) w_ok = mbar_wait(&empty[s], ((g / S) - 1) & 1, pp.status, 11);
+                if (!__shfl_sync(0xFFFFFFFFu, w_ok ? 1 : 0, 0)) {
+                    ok = false;
+                    break;
+                }
+                const uint64_t lo = r0 + uint64_t(t) * R;
+                const uint64_t hi = lo + R < r1 ? lo + R : r1;
+                const uintptr_t a = wbase + lo * op.row_bytes;
+                const uintptr_t b = wbase + hi * op.row_bytes;
+                const uintptr_t a16 = a & ~uintptr_t(15);
+                const uintptr_t A = (a + 15) & ~uintptr_t(15);
+                const uintptr_t B = b & ~uintptr_t(15);
+                uint8_t* dst = stage0 + size_t(s) * pp.stage_bytes;
+                uint32_t tx = 0;
+                if (B <= A) {
+                    for (uintptr_t x = a + lane; x < b; x += 32) dst[x - a16] = *reinterpret_cast<const uint8_t*>(x);
+                } else {
+                    if (a + lane < A) dst[a + lane - a16] = *reinterpret_cast<const uint8_t*>(a + lane);
+                    if (B + lane < b) dst[B + lane - a16] = *reinterpret_cast<const uint8_t*>(B + lane);
+                    tx = static_cast<uint32_t>(B - A);
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[s], tx);
+                    for (uint32_t off = 0; off < tx; off += pp.copy_chunk) {
+                        const uint32_t n = tx - off < pp.copy_chunk ? tx - off : pp.copy_chunk;
+                        bulk_copy_g2s(dst + (A - a16) + off, reinterpret_cast<const void*>(A + off), n, &full[s],
+                                      policy);
+                    }
+                }
+            }
+        }
+        if (lane == 0) {
+            const uint32_t first = g > S ? g - S : 0;
+            for (uint32_t t = first; t < g; ++t) mbar_wait(&full[t % S], (t / S) & 1, pp.status, 12);
+        }
+        return;
+    }
+
+    // ---------------- consumers
+    // A failed (timed-out) wait marks the warp failed; it then skips work but
+    // still takes every named barrier and stage arrival, so no other warp can
+    // be left waiting at a barrier without a deadline.
+    pdl_wait();
+    ProgramConsumer<NCW> cons;
+    bool failed = false;
+    // Every op that reads an activation from outside this launch had its image
+    // built once, before this kernel, by quantize_images_kernel (the preceding
+    // launch on the stream); copy those images into shared memory, so
+    // consumers flow from one op's rows into the next without stopping.
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(pp.images);
+        uint4* dst = reinterpret_cast<uint4*>(act);
+        for (uint32_t i = threadIdx.x; i < pp.prebuilt_bytes / 16; i += NCW * 32) dst[i] = __ldcg(src + i);
+    }
+    named_barrier_sync(1, NCW * 32);
+    uint32_t s = 0, phase = 0;  // slot and parity of the global stage counter
+    for (uint32_t k = 0; k < pp.n_ops; ++k) {
+        const ProgramOp op = pp.ops[k];
+        if (op.after_previous && k > 0) {
+            if (!failed) {
+                bool ok = true;
+                if (lane == 0) ok = wait_counter(pp.counters + (k - 1), gridDim.x, pp.status, 13);
+                failed = !__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0);
+            }
+            named_barrier_sync(1, NCW * 32);  // (orders the acquire above before every warp's loads)
+            if (!failed) cons.prologue(op, act, warp, lane);
+            named_barrier_sync(1, NCW * 32);
+        }
+        if (!failed) cons.load(op, act, lane);
+
+        const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
+        const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
+        const uint32_t nrows = static_cast<uint32_t>(r1 - r0);
+        const uint32_t R = op.rows_per_stage;
+        const uint32_t T = (nrows + R - 1) / R;
+        const uint32_t rb = static_cast<uint32_t>(op.row_bytes);
+        const uint32_t wlo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w));
+        const uint32_t row0 = static_cast<uint32_t>(r0);
+        uint32_t owner_base = 0;  // (t * R) % NCW
+        for (uint32_t t = 0; t < T; ++t) {
+            if (!failed) {
+                const bool ok = mbar_wait(&full[s], phase, pp.status, 14);
+                failed = !__all_sync(0xFFFFFFFFu, ok);
+            }
+            if (!failed) {
+                const uint32_t q_lo = t * R;
+                const uint32_t n_here = nrows - q_lo < R ? nrows - q_lo : R;
+                const uint32_t head = (wlo + (row0 + q_lo) * rb) & 15u;
+                const uint8_t* slot = stage0 + s * pp.stage_bytes + head;
+                uint32_t j = warp >= owner_base ? warp - owner_base : warp + NCW - owner_base;
+                for (; j < n_here; j += NCW) {
+                    if (kTypes == 1 || (kTypes == 3 && op.type == 12))
+                        cons.template row_typed<12>(op, act, slot + j * rb, r0 + q_lo + j, lane);
+                    else
+                        cons.template row_typed<14>(op, act, slot + j * rb, r0 + q_lo + j, lane);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == S) {
+                s = 0;
+                phase ^= 1u;
+            }
+            owner_base += R % NCW;
+            if (owner_base >= NCW) owner_base -= NCW;
+        }
+        if (op.publish) {
+            // publish this CTA's completion of op k (its y rows are written)
+            named_barrier_sync(1, NCW * 32);
+            if (threadIdx.x == 0) {
+                __threadfence();
+                red_release_gpu_add(pp.counters + k, 1u);
+            }
+        }
+    }
+    // The last CTA to finish zeroes the counters for the next launch.  A later
+    // launch reads them only after its griddepcontrol.wait, i.e. after this
+    // grid has completed.
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned int done = atomicAdd(pp.counters + kProgramMaxOps, 1u);
+        if (done == gridDim.x - 1) {
+            for (uint32_t k = 0; k < kProgramMaxOps; ++k) pp.counters[k] = 0u;
+            pp.counters[kProgramMaxOps] = 0u;
+            __threadfence();
+        }
+    }
+}
+
+}  // namespace oracle_cuda

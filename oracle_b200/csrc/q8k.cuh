@@ -29,14 +29,16 @@ struct Q8KLane {
 };
 
 __device__ __forceinline__ void load_lane8(const float* xb, int lane, bool aligned16, float (&v)[8]) {
+    // L2 (.cg) loads: the activation may have been written by another SM
+    // earlier in the same launch (matvec programs), so L1 must not serve it.
     if (aligned16) {
-        const float4 a = reinterpret_cast<const float4*>(xb)[2 * lane];
-        const float4 b = reinterpret_cast<const float4*>(xb)[2 * lane + 1];
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(xb) + 2 * lane);
+        const float4 b = __ldcg(reinterpret_cast<const float4*>(xb) + 2 * lane + 1);
         v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
         v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = xb[8 * lane + j];
+        for (int j = 0; j < 8; ++j) v[j] = __ldcg(xb + 8 * lane + j);
     }
 }
 
@@ -189,6 +191,36 @@ __device__ __forceinline__ void quantize_to_image(const float* __restrict__ x, u
             store_block_to_image(img, i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
         }
     }
+}
+
+// Quantize up to kMaxImageJobs activations, each into its own image inside
+// one global buffer laid out exactly like the shared-memory images, so a
+// consumer can copy the whole region into shared memory unchanged.  One warp
+// per 256-element block; blocks of all jobs are numbered consecutively.
+constexpr int kMaxImageJobs = 16;
+struct ImageJobs {
+    const float* x[kMaxImageJobs];
+    uint32_t nb[kMaxImageJobs];
+    uint32_t offset[kMaxImageJobs];  // byte offset of the job's image
+    uint32_t first_block[kMaxImageJobs + 1];
+    uint32_t n_jobs;
+};
+
+__global__ void __launch_bounds__(256) quantize_images_kernel(const __grid_constant__ ImageJobs jobs, uint8_t* images) {
+    // The image buffer is reused by every program launch: wait until the
+    // preceding kernel (possibly the previous program, still reading it) is
+    // done, but let the next kernel start streaming its weights already.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    const int lane = threadIdx.x & 31;
+    if (gw >= jobs.first_block[jobs.n_jobs]) return;
+    uint32_t j = 0;
+    while (gw >= jobs.first_block[j + 1]) ++j;
+    const uint32_t i = gw - jobs.first_block[j];
+    const float* xb = jobs.x[j] + 256ull * i;
+    const Q8KLane r = quantize_q8k_block_warp(xb, lane, (reinterpret_cast<uintptr_t>(xb) & 15u) == 0);
+    store_block_to_image(q8k_image(images + jobs.offset[j], jobs.nb[j]), i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
 }
 
 // Load pre-quantized GGML Q8_K blocks (global) into the image.

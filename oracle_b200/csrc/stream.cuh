@@ -144,20 +144,31 @@ __global__ void __launch_bounds__((Consumer::kWarps + 1) * 32, 1)
     named_barrier_sync(1, NCW * 32);
     cons.load(cp, act, warp, lane);
 
+    // Lean walk: slot, phase and this warp's first row in the stage advance
+    // incrementally; shared-memory offsets are 32-bit (a stage is < 2^32 B).
+    const uint32_t rb = static_cast<uint32_t>(sp.row_bytes);
+    const uint32_t wlo = static_cast<uint32_t>(wbase);
+    uint32_t s = 0, phase = 0;
+    uint32_t owner_base = 0;  // (t * R) % NCW
+    uint32_t row0 = static_cast<uint32_t>(r0);
     for (uint32_t t = 0; t < T; ++t) {
-        const uint32_t s = t % S;
-        const bool ok = mbar_wait(&full[s], (t / S) & 1, sp.status, 3);
+        const bool ok = mbar_wait(&full[s], phase, sp.status, 3);
         if (!__all_sync(0xFFFFFFFFu, ok)) break;
         const uint32_t q_lo = t * R;
-        const uint32_t q_hi = q_lo + R < nrows ? q_lo + R : nrows;
-        const uintptr_t a16 = (wbase + (r0 + q_lo) * sp.row_bytes) & ~uintptr_t(15);
-        const uint8_t* slot = stage0 + size_t(s) * sp.stage_bytes;
-        // first row of this stage owned by this warp
-        uint32_t q = q_lo + ((warp + NCW - q_lo % NCW) % NCW);
-        for (; q < q_hi; q += NCW)
-            cons.row(cp, act, slot + ((wbase + (r0 + q) * sp.row_bytes) - a16), r0 + q, lane);
+        const uint32_t n_here = nrows - q_lo < R ? nrows - q_lo : R;
+        // byte offset of the stage's first row past its 16-byte floor
+        const uint32_t head = (wlo + (row0 + q_lo) * rb) & 15u;
+        const uint8_t* slot = stage0 + s * sp.stage_bytes + head;
+        uint32_t j = warp >= owner_base ? warp - owner_base : warp + NCW - owner_base;
+        for (; j < n_here; j += NCW) cons.row(cp, act, slot + j * rb, r0 + q_lo + j, lane);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == S) {
+            s = 0;
+            phase ^= 1u;
+        }
+        owner_base += R % NCW;
+        if (owner_base >= NCW) owner_base -= NCW;
     }
 }
 

@@ -273,3 +273,71 @@ def test_bounded_wait_reports_timeout_and_context_survives(ctx, port):
     y = torch.empty(rows, dtype=torch.float32, device=DEV)
     ctx.storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q6_K, rows, k, to_dev(w), to_dev(x), y)
     assert bits_equal(y.cpu().numpy(), port.matvec_q8_k(ob.TYPE_Q6_K, rows, k, w, port.quantize_q8_k(x))[0])
+
+
+# ---------------------------------------------------------------- matvec programs (one persistent launch)
+
+def _program_case(port, specs, cfg):
+    """specs: (qtype, rows, cols, after_previous); activations chain when flagged."""
+    host, dev_ops, want = [], [], []
+    prev_y_host = prev_y_dev = None
+    for i, (qtype, rows, cols, after) in enumerate(specs):
+        w = synth.weight(qtype, rows, cols, cfg, f"prog_w{i}")
+        if after:
+            x_host, x_dev = prev_y_host[:cols], prev_y_dev
+        else:
+            x_host = synth.activations(cols, 1, cfg, f"prog_x{i}")[0]
+            x_dev = to_dev(x_host)
+        y_host = port.matvec_q8_k(qtype, rows, cols, w, port.quantize_q8_k(x_host))[0]
+        y_dev = torch.empty(rows, dtype=torch.float32, device=DEV)
+        dev_ops.append((qtype, rows, cols, to_dev(w), x_dev, y_dev, after))
+        want.append(y_host)
+        prev_y_host, prev_y_dev = y_host, y_dev
+    return dev_ops, want
+
+
+def test_program_independent_ops(ctx, port):
+    specs = [(ob.TYPE_Q4_K, 1536, 4096, 0), (ob.TYPE_Q4_K, 512, 12288, 0), (ob.TYPE_Q4_K, 777, 4096, 0),
+             (ob.TYPE_Q4_K, 3, 256, 0)]
+    ops, want = _program_case(port, specs, "prog_ind")
+    ctx.matvec_program(ops)
+    ctx.device_status()
+    for (_, _, _, _, _, y, _), w in zip(ops, want):
+        assert bits_equal(y.cpu().numpy(), w)
+
+
+def test_program_dependent_chain_and_repeat(ctx, port):
+    # y0 = W0 x0 (4096 -> 12288); y1 = W1 y0 (12288 -> 4096); y2 = W2 y1 (4096 -> 4096)
+    specs = [(ob.TYPE_Q4_K, 12288, 4096, 0), (ob.TYPE_Q4_K, 4096, 12288, 1), (ob.TYPE_Q4_K, 4096, 4096, 1)]
+    ops, want = _program_case(port, specs, "prog_chain")
+    for _ in range(3):  # completion counters reset themselves between launches
+        for op in ops:
+            op[5].fill_(float("nan"))
+        ctx.matvec_program(ops)
+        ctx.device_status()
+        for (_, _, _, _, _, y, _), w in zip(ops, want):
+            assert bits_equal(y.cpu().numpy(), w)
+
+
+def test_program_mixed_types(ctx, port):
+    specs = [(ob.TYPE_Q6_K, 1000, 4096, 0), (ob.TYPE_Q4_K, 300, 768, 0), (ob.TYPE_Q6_K, 513, 768, 0)]
+    ops, want = _program_case(port, specs, "prog_mixed")
+    ctx.matvec_program(ops)
+    ctx.device_status()
+    for (_, _, _, _, _, y, _), w in zip(ops, want):
+        assert bits_equal(y.cpu().numpy(), w)
+
+
+def test_program_validation(ctx):
+    w = to_dev(synth.weight(ob.TYPE_Q4_K, 4, 256, "gpu", "progval"))
+    x = torch.zeros(256, dtype=torch.float32, device=DEV)
+    y = torch.empty(4, dtype=torch.float32, device=DEV)
+    with pytest.raises(ob.InvalidArgument):
+        ctx.matvec_program([])
+    with pytest.raises(ob.InvalidArgument):
+        ctx.matvec_program([(ob.TYPE_Q4_K, 4, 256, w, x, y, 0)] * 17)
+    w8 = to_dev(synth.weight(ob.TYPE_Q8_0, 4, 256, "gpu", "progval8"))
+    with pytest.raises(ob.Unsupported, match="op 1"):
+        ctx.matvec_program([(ob.TYPE_Q4_K, 4, 256, w, x, y, 0), (ob.TYPE_Q8_0, 4, 256, w8, x, y, 0)])
+    with pytest.raises(ob.InvalidArgument, match="op 0: reference matvec matrix byte size mismatch"):
+        ctx.matvec_program([(ob.TYPE_Q4_K, 4, 256, w8, x, y, 0)])
