@@ -27,8 +27,10 @@
  *
  * Two arithmetic contracts
  *   ORACLE_CUDA_CONTRACT_F32  Oracle's own: weights decoded to f32 exactly as
- *                             Oracle decodes them, dotted with f32 x
- *                             (quantized_reference.cpp:24-82).  Types f32,
+ *                             Oracle decodes them, products added into one
+ *                             running f32 sum in element order
+ *                             (quantized_reference.cpp:24-82): results are
+ *                             bit-identical to the reference.  Types f32,
  *                             f16, bf16, q8_0, q4_K, q5_K, q6_K.
  *   ORACLE_CUDA_CONTRACT_Q8K  GGML's integer contract: x quantized to Q8_K
  *                             (f32 d, int8 qs[256], int16 bsums[16]), exact

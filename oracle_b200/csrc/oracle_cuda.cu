@@ -18,7 +18,7 @@
 #include <vector>
 
 #include "layout.hpp"
-#include "matvec_f32.cuh"
+#include "matvec_seq.cuh"
 #include "matvec_q8k.cuh"
 #include "program.cuh"
 #include "q8k.cuh"
@@ -202,7 +202,6 @@ bool plan_stream(oracle_cuda_context* ctx, uint64_t rows, uint64_t row_bytes, ui
     return true;
 }
 
-constexpr int kConsumerWarps = 8;
 constexpr int kQ8KConsumerWarps = 16;
 // The program kernel carries both ops' code paths: with 15 consumer warps + 1
 // producer (4 warps per SM sub-partition) it may use 128 registers, unspilled.
@@ -247,38 +246,36 @@ oracle_cuda_status launch_q8k(oracle_cuda_context* ctx, uint32_t type, const voi
 }
 
 template <uint32_t kType>
-oracle_cuda_status launch_f32_typed(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t row_bytes,
-                                    const MatvecF32Params& cp, cudaStream_t stream) {
-    return launch_stream<MatvecF32Consumer<kType, kConsumerWarps>>(ctx, w, rows, row_bytes,
-                                                                   f32_image_bytes(cp.kpad, cp.batch), cp, stream);
+oracle_cuda_status launch_seq_typed(oracle_cuda_context* ctx, const MatvecSeqParams& sp, cudaStream_t stream) {
+    const uint64_t per_cta = uint64_t(kSeqWarps) * 32;
+    const uint64_t grid = (sp.rows + per_cta - 1) / per_cta;
+    if (grid > 0x7FFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "too many rows for one launch");
+    return launch(ctx, matvec_seq_kernel<kType>, dim3(static_cast<uint32_t>(grid)), dim3(kSeqWarps * 32), 0, stream,
+                  false, sp);
 }
 
-constexpr uint32_t kF32ImageMax = 128 * 1024;
-
+// Oracle's f32 contract, bit-exact: one lane per row, sequential f32 sum.
 oracle_cuda_status launch_f32(oracle_cuda_context* ctx, uint32_t type, const void* w, uint64_t rows, uint64_t cols,
                               uint64_t row_bytes, const float* x, uint64_t batch, float* y, cudaStream_t stream) {
-    const uint32_t kpad = align_up(static_cast<uint32_t>(cols), 128u);
-    if (uint64_t(kpad) * 4 > kF32ImageMax)
-        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "f32-contract matvec supports rows of at most 32768 elements");
-    const uint64_t chunk = kF32ImageMax / (uint64_t(kpad) * 4);
-    const uint8_t* wb = static_cast<const uint8_t*>(w);
-    for (uint64_t b0 = 0; b0 < batch; b0 += chunk) {
-        MatvecF32Params cp{};
-        cp.x = x + b0 * cols;
-        cp.y = y + b0 * rows;
-        cp.rows = rows;
-        cp.k = static_cast<uint32_t>(cols);
-        cp.kpad = kpad;
-        cp.batch = static_cast<uint32_t>(batch - b0 < chunk ? batch - b0 : chunk);
+    if (cols > 0xFFFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "rows longer than 2^32 elements");
+    for (uint64_t b0 = 0; b0 < batch; b0 += kSeqMaxBatch) {
+        MatvecSeqParams sp{};
+        sp.w = static_cast<const uint8_t*>(w);
+        sp.x = x + b0 * cols;
+        sp.y = y + b0 * rows;
+        sp.rows = rows;
+        sp.row_bytes = row_bytes;
+        sp.k = static_cast<uint32_t>(cols);
+        sp.batch = static_cast<uint32_t>(batch - b0 < kSeqMaxBatch ? batch - b0 : kSeqMaxBatch);
         oracle_cuda_status s;
         switch (type) {
-            case kTypeF32: s = launch_f32_typed<0>(ctx, wb, rows, row_bytes, cp, stream); break;
-            case kTypeF16: s = launch_f32_typed<1>(ctx, wb, rows, row_bytes, cp, stream); break;
-            case kTypeBF16: s = launch_f32_typed<30>(ctx, wb, rows, row_bytes, cp, stream); break;
-            case kTypeQ8_0: s = launch_f32_typed<8>(ctx, wb, rows, row_bytes, cp, stream); break;
-            case kTypeQ4_K: s = launch_f32_typed<12>(ctx, wb, rows, row_bytes, cp, stream); break;
-            case kTypeQ5_K: s = launch_f32_typed<13>(ctx, wb, rows, row_bytes, cp, stream); break;
-            case kTypeQ6_K: s = launch_f32_typed<14>(ctx, wb, rows, row_bytes, cp, stream); break;
+            case kTypeF32: s = launch_seq_typed<0>(ctx, sp, stream); break;
+            case kTypeF16: s = launch_seq_typed<1>(ctx, sp, stream); break;
+            case kTypeBF16: s = launch_seq_typed<30>(ctx, sp, stream); break;
+            case kTypeQ8_0: s = launch_seq_typed<8>(ctx, sp, stream); break;
+            case kTypeQ4_K: s = launch_seq_typed<12>(ctx, sp, stream); break;
+            case kTypeQ5_K: s = launch_seq_typed<13>(ctx, sp, stream); break;
+            case kTypeQ6_K: s = launch_seq_typed<14>(ctx, sp, stream); break;
             default: return fail(ctx, check_decodable(type));
         }
         if (s != ORACLE_CUDA_OK) return s;
