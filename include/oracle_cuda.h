@@ -186,6 +186,27 @@ typedef struct oracle_cuda_matvec_op {
 oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops,
                                               uint32_t n_ops, void* stream);
 
+/* The same matvec program for callers that cannot allocate device memory:
+ * e.g. an engine that has already reserved nearly all of HBM for its own
+ * pools, or a latency-critical path on which cudaMalloc, which can synchronise
+ * the device, is not allowed.  It takes no context and allocates nothing: its
+ * scratch (activation images of at most ORACLE_CUDA_NOALLOC_IMAGE_BYTES, the
+ * completion counters and a status word) is one static device array that every
+ * GPU loading this library holds until the process exits.  Works on the
+ * current CUDA device.  The first call on a device looks the array up
+ * (cudaGetSymbolAddress) and sets kernel attributes; make that first call
+ * before any stream capture.  Each call clears the counters on `stream` and
+ * then overwrites the images, so calls that overlap on the GPU (other streams,
+ * other threads) race with each other.  Programs whose activation images need
+ * more than ORACLE_CUDA_NOALLOC_IMAGE_BYTES are rejected with
+ * INVALID_ARGUMENT.  Errors are reported through oracle_cuda_last_error(NULL);
+ * device-side wait timeouts are not reported.  Results equal those of
+ * oracle_cuda_matvec_program.  No counterpart in the reference (Oracle's path
+ * never touches device memory). */
+#define ORACLE_CUDA_NOALLOC_IMAGE_BYTES 65536
+oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cuda_matvec_op* ops, uint32_t n_ops,
+                                                      void* stream);
+
 /* ------------------------------------------------------------------ resident weights
  * Oracle's weights are immutable GGUF bytes in a read-only mapping
  * (MappedGgufModel, include/oracle/model/mapped_gguf.hpp:56-59).  They are

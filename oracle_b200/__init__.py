@@ -86,6 +86,24 @@ class MatvecOp(C.Structure):
 
 PROGRAM_MAX_OPS = 16
 _proto("oracle_cuda_matvec_program", [_vp, C.POINTER(MatvecOp), _u32, _vp])
+_proto("oracle_cuda_matvec_program_noalloc", [C.POINTER(MatvecOp), _u32, _vp])
+NOALLOC_IMAGE_BYTES = 65536
+
+
+def _matvec_ops(ops):
+    arr = (MatvecOp * len(ops))()
+    for i, (qtype, rows, cols, w, x, y, after) in enumerate(ops):
+        arr[i] = MatvecOp(qtype, 1 if after else 0, rows, cols, _addr(w), _nbytes(w), _addr(x), _addr(y))
+    return arr
+
+
+def matvec_program_noalloc(ops, stream=None) -> None:
+    """oracle_cuda_matvec_program_noalloc: the matvec program without any
+    device allocation (no context; scratch is a static device array), for
+    callers that cannot allocate device memory.  Runs on the current device;
+    ops as for :meth:`Context.matvec_program`."""
+    arr = _matvec_ops(ops)
+    _raise(_lib.oracle_cuda_matvec_program_noalloc(arr, len(ops), _stream(stream)), None)
 _proto("oracle_cuda_weight_upload", [_vp, _u32, _u64, _u64, _vp, _u64, _u64, _u64, C.POINTER(_vp)])
 _proto("oracle_cuda_weight_free", [_vp])
 _proto("oracle_cuda_weight_info", [_vp, C.POINTER(_u32), _u64p, _u64p, _u64p, C.POINTER(_vp), _u64p])

@@ -880,3 +880,184 @@ oracle_cuda_status oracle_cuda_host_decode_rows(oracle_cuda_context* ctx, uint32
 }
 
 }  // extern "C"
+
+// ====================================================================== no-allocation program
+//
+// oracle_cuda_matvec_program_noalloc: the matvec program for callers that may
+// not allocate device memory themselves -- for instance an engine that has
+// already reserved nearly all of HBM for its own pools, or a latency-critical
+// path where cudaMalloc (which can synchronise the device) is not allowed.  It
+// needs no context: its scratch (the prebuilt activation images, the
+// completion counters and the device status word) is one file-scope device
+// array, present on every GPU that loads this library until the process exits.
+
+namespace {
+
+constexpr uint64_t kNoAllocImageBytes = ORACLE_CUDA_NOALLOC_IMAGE_BYTES;
+constexpr uint64_t kNoAllocCountersOffset = kNoAllocImageBytes;
+constexpr uint64_t kNoAllocStatusOffset = kNoAllocImageBytes + 256;
+constexpr uint64_t kNoAllocScratchBytes = kNoAllocImageBytes + 512;
+constexpr int kNoAllocMaxDevices = 64;
+
+}  // namespace
+
+// Host code must not use this name as an address: on the host it is only a
+// stand-in for the symbol.  The device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+struct NoAllocDevice {
+    bool ready = false;
+    unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+    int sm_count = 0;
+    int smem_optin = 0;
+};
+
+NoAllocDevice g_noalloc_devices[kNoAllocMaxDevices];
+std::mutex g_noalloc_mutex;
+
+// Once per device, with that device current: resolve the array's device
+// address, read the SM count and shared-memory limit, and allow the program
+// kernels their dynamic shared memory.
+oracle_cuda_status noalloc_setup(int device, NoAllocDevice** out) {
+    if (device < 0 || device >= kNoAllocMaxDevices)
+        return fail(nullptr, ORACLE_CUDA_UNSUPPORTED, "device index too large for the no-allocation entry point");
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    NoAllocDevice& d = g_noalloc_devices[device];
+    if (!d.ready) {
+        cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.scratch), g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+        int major = 0;
+        if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device)) != cudaSuccess)
+            return cuda_fail(nullptr, e, "cudaDeviceGetAttribute");
+        if (major != 10) return fail(nullptr, ORACLE_CUDA_UNSUPPORTED, "this library is built for sm_100a (B200)");
+        if ((e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess ||
+            (e = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device)) !=
+                cudaSuccess)
+            return cuda_fail(nullptr, e, "cudaDeviceGetAttribute");
+        const void* kernels[3] = {reinterpret_cast<const void*>(matvec_program_kernel<kProgramWarps, 1>),
+                                  reinterpret_cast<const void*>(matvec_program_kernel<kProgramWarps, 2>),
+                                  reinterpret_cast<const void*>(matvec_program_kernel<kProgramWarps, 3>)};
+        for (const void* k : kernels)
+            if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_optin)) !=
+                cudaSuccess)
+                return cuda_fail(nullptr, e, "cudaFuncSetAttribute");
+        d.ready = true;
+    }
+    *out = &d;
+    return ORACLE_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cuda_matvec_op* ops, uint32_t n_ops,
+                                                                 void* stream) {
+    if (!ops || n_ops == 0 || n_ops > kProgramMaxOps)
+        return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT,
+                    "a matvec program holds 1 to " + std::to_string(kProgramMaxOps) + " ops");
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDevice");
+    NoAllocDevice* dev = nullptr;
+    oracle_cuda_status st = noalloc_setup(device, &dev);
+    if (st != ORACLE_CUDA_OK) return st;
+
+    ProgramParams pp{};
+    pp.n_ops = n_ops;
+    uint64_t max_rows = 0, stage = 0, prebuilt = 0, dependent = 0;
+    for (uint32_t k = 0; k < n_ops; ++k) {
+        const oracle_cuda_matvec_op& o = ops[k];
+        uint64_t rb = 0, batch = 0;
+        st = validate_matvec(nullptr, ORACLE_CUDA_CONTRACT_Q8K, o.type, o.rows, o.cols, o.w_nbytes, o.cols, o.rows, &rb,
+                             &batch);
+        if (st != ORACLE_CUDA_OK)
+            return fail(nullptr, st, "op " + std::to_string(k) + ": " + oracle_cuda_last_error(nullptr));
+        if (Error err = check_weight_pointer(o.type, o.w_dev)) return fail(nullptr, err);
+        if (!o.x_dev || !o.y_dev)
+            return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "op " + std::to_string(k) + ": null activation or output");
+        ProgramOp& p = pp.ops[k];
+        p.w = static_cast<const uint8_t*>(o.w_dev);
+        p.x = o.x_dev;
+        p.y = o.y_dev;
+        p.rows = o.rows;
+        p.row_bytes = rb;
+        p.type = o.type;
+        p.nb = static_cast<uint32_t>(o.cols / 256);
+        p.after_previous = (o.after_previous && k > 0) ? 1u : 0u;
+        if (p.after_previous) pp.ops[k - 1].publish = 1u;
+        uint64_t R = 36864 / rb;
+        if (R > uint64_t(kProgramWarps)) R = kProgramWarps;
+        if (R < 1) R = 1;
+        p.rows_per_stage = static_cast<uint32_t>(R);
+        const uint64_t sb = align_up(static_cast<uint32_t>(R * rb + 32), 128u);
+        if (sb > stage) stage = sb;
+        if (o.rows > max_rows) max_rows = o.rows;
+        (p.after_previous ? dependent : prebuilt) += q8k_image_bytes(p.nb);
+    }
+    // The activation images of ops fed from outside the call live in the
+    // static array; they must fit its stated size.
+    if (prebuilt > kNoAllocImageBytes)
+        return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT,
+                    "the activation images of this program need " + std::to_string(prebuilt) +
+                        " bytes; the no-allocation entry point holds at most " + std::to_string(kNoAllocImageBytes));
+    ImageJobs jobs{};
+    uint32_t off = 0, blocks = 0;
+    for (uint32_t k = 0; k < n_ops; ++k)
+        if (!pp.ops[k].after_previous) {
+            pp.ops[k].act_offset = off;
+            pp.ops[k].prebuilt = 1u;
+            jobs.x[jobs.n_jobs] = pp.ops[k].x;
+            jobs.nb[jobs.n_jobs] = pp.ops[k].nb;
+            jobs.offset[jobs.n_jobs] = off;
+            jobs.first_block[jobs.n_jobs] = blocks;
+            blocks += pp.ops[k].nb;
+            jobs.n_jobs++;
+            off += q8k_image_bytes(pp.ops[k].nb);
+        }
+    jobs.first_block[jobs.n_jobs] = blocks;
+    const uint32_t prebuilt_bytes = off;
+    for (uint32_t k = 0; k < n_ops; ++k)
+        if (pp.ops[k].after_previous) {
+            pp.ops[k].act_offset = off;
+            off += q8k_image_bytes(pp.ops[k].nb);
+        }
+    pp.act_bytes = off;
+    const uint64_t budget = uint64_t(dev->smem_optin) - stream_barrier_bytes(16) - pp.act_bytes;
+    if (pp.act_bytes > 96 * 1024 || stage * 2 > budget)
+        return fail(nullptr, ORACLE_CUDA_UNSUPPORTED, "matvec program rows too long for the shared-memory stage ring");
+    uint64_t S = budget / stage;
+    if (S > 16) S = 16;
+    pp.stages = static_cast<uint32_t>(S);
+    pp.stage_bytes = static_cast<uint32_t>(stage);
+    pp.copy_chunk = 32768;
+    pp.max_inflight = 16;
+    pp.images = dev->scratch;
+    pp.prebuilt_bytes = prebuilt_bytes;
+    pp.counters = reinterpret_cast<unsigned int*>(dev->scratch + kNoAllocCountersOffset);
+    pp.status = reinterpret_cast<DeviceStatus*>(dev->scratch + kNoAllocStatusOffset);
+
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Counters and status must start at zero; the array keeps whatever the
+    // previous call left there.
+    if ((e = cudaMemsetAsync(dev->scratch + kNoAllocCountersOffset, 0, 512, s)) != cudaSuccess)
+        return cuda_fail(nullptr, e, "cudaMemsetAsync(no-allocation counters)");
+    if (prebuilt_bytes > 0) {
+        const uint32_t qgrid = (blocks * 32 + 255) / 256;
+        quantize_images_kernel<<<qgrid, 256, 0, s>>>(jobs, dev->scratch);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(nullptr, e, "quantize_images_kernel launch");
+    }
+    int types = 0;
+    for (uint32_t k = 0; k < n_ops; ++k) types |= ops[k].type == kTypeQ4_K ? 1 : 2;
+    const uint32_t grid = static_cast<uint32_t>(max_rows < uint64_t(dev->sm_count) ? max_rows : dev->sm_count);
+    const size_t smem = stream_barrier_bytes(pp.stages) + pp.act_bytes + size_t(pp.stages) * pp.stage_bytes;
+    const dim3 block((kProgramWarps + 1) * 32);
+    if (types == 1)
+        matvec_program_kernel<kProgramWarps, 1><<<grid, block, smem, s>>>(pp);
+    else if (types == 2)
+        matvec_program_kernel<kProgramWarps, 2><<<grid, block, smem, s>>>(pp);
+    else
+        matvec_program_kernel<kProgramWarps, 3><<<grid, block, smem, s>>>(pp);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(nullptr, e, "matvec_program_kernel launch");
+    return ORACLE_CUDA_OK;
+}
