@@ -1,9 +1,11 @@
 """Benchmark of the north-star op: Q4_K x Q8_K decode matvec on B200.
 
-Workload (batch 1): one step = the three Q4_K matvecs
-4096->12288, 12288->4096 and 4096->4096, each quantizing its f32 activation
-to Q8_K inside the kernel.  Algorithmic bytes per matvec = packed weight bytes
-N*(K/256)*144 + f32 activation K*4 + f32 output N*4; 66,224,128 B per step.
+Default workload (batch 1): one step = the three Q4_K
+matvecs 4096->12288, 12288->4096 and 4096->4096, each quantizing its f32
+activation to Q8_K in the call.  Algorithmic bytes per matvec = packed weight
+bytes + f32 activation K*4 + f32 output N*4; 66,224,128 B per step.
+--workload config3 (Q6_K LM head 4096->151936) and config1 (Q8_0 4096x4096,
+Oracle's f32 contract) print the same line for those configurations.
 
 * value   -- GB/s over the timed region: K steps replayed from a CUDA graph,
              CUDA events on the capture stream, barrier + synchronize on both
@@ -39,30 +41,57 @@ import time
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-SHAPES = [(4096, 12288), (12288, 4096), (4096, 4096)]  # (K, N): K -> N
-TYPE_Q4_K = 12
-POOL_SETS = 6
-METRIC = "Q4_K x Q8_K decode matvec GB/s"
+TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 8, 12, 14
+CONTRACT_F32, CONTRACT_Q8K = 0, 1
 UNIT = "GB/s"
+BLOCK = {TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144), TYPE_Q6_K: (256, 210)}
 
 
-def algorithmic_bytes(k: int, n: int) -> int:
-    return n * (k // 256) * 144 + k * 4 + n * 4
+def weight_bytes(qtype: int, k: int, n: int) -> int:
+    be, bb = BLOCK[qtype]
+    return n * (k // be) * bb
 
 
-STEP_BYTES = sum(algorithmic_bytes(k, n) for k, n in SHAPES)
-H2D_BYTES = sum(k * 4 for k, _ in SHAPES)
-D2H_BYTES = sum(n * 4 for _, n in SHAPES)
+def algorithmic_bytes(qtype: int, k: int, n: int) -> int:
+    """Packed weight bytes + f32 activation read + f32 output written."""
+    return weight_bytes(qtype, k, n) + k * 4 + n * 4
 
 
-def config_block(n_gpus: int) -> dict:
-    return {"workload": "config2: Q4_K x Q8_K decode matvec, batch 1, shapes 4096->12288, 12288->4096, "
-                        "4096->4096 (activation quantized to Q8_K in-kernel)",
-            "shapes_k_to_n": [f"{k}->{n}" for k, n in SHAPES],
-            "batch": 1,
-            "bytes_per_step": STEP_BYTES,
-            "l2": f"weights rotate through {POOL_SETS} sets ({POOL_SETS * sum(n * (k // 256) * 144 for k, n in SHAPES) / 1e6:.0f} MB > 3x L2)",
-            "parallelism": f"replicas{n_gpus}" if n_gpus > 1 else "single"}
+class Workload:
+    """One step of a benchmark configuration: a list of matvecs (qtype, K, N)."""
+
+    def __init__(self, name, metric, description, ops, contract, pool_sets, program, cpu_kind, dtype):
+        self.name, self.metric, self.description = name, metric, description
+        self.ops, self.contract, self.pool_sets, self.program = ops, contract, pool_sets, program
+        self.cpu_kind, self.dtype = cpu_kind, dtype
+        self.step_bytes = sum(algorithmic_bytes(t, k, n) for t, k, n in ops)
+        self.h2d = sum(k * 4 for _, k, _ in ops)
+        self.d2h = sum(n * 4 for _, _, n in ops)
+
+    def config(self, n_gpus: int) -> dict:
+        wb = sum(weight_bytes(t, k, n) for t, k, n in self.ops)
+        return {"workload": self.description, "shapes_k_to_n": [f"{k}->{n}" for _, k, n in self.ops], "batch": 1,
+                "bytes_per_step": self.step_bytes,
+                "l2": f"weights rotate through {self.pool_sets} sets ({self.pool_sets * wb / 1e6:.0f} MB > 3x L2)",
+                "parallelism": f"replicas{n_gpus}" if n_gpus > 1 else "single"}
+
+
+WORKLOADS = {
+    "config2": Workload(
+        "config2", "Q4_K x Q8_K decode matvec GB/s",
+        "config2: Q4_K x Q8_K decode matvec, batch 1, shapes 4096->12288, 12288->4096, 4096->4096 "
+        "(activations quantized to Q8_K in the call), one matvec-program launch per step",
+        [(TYPE_Q4_K, 4096, 12288), (TYPE_Q4_K, 12288, 4096), (TYPE_Q4_K, 4096, 4096)], CONTRACT_Q8K, 6, True,
+        "port", "int8 x u4 -> int32, f32 combine"),
+    "config3": Workload(
+        "config3", "Q6_K x Q8_K LM-head matvec GB/s",
+        "config3: Q6_K x Q8_K LM-head matvec 4096->151936, batch 1", [(TYPE_Q6_K, 4096, 151936)], CONTRACT_Q8K, 2,
+        False, "port", "int8 x u6 -> int32, f32 combine"),
+    "config1": Workload(
+        "config1", "Q8_0 f32-contract matvec GB/s",
+        "config1: Q8_0 4096x4096 dequant-matvec against f32 x, Oracle's sequential f32 sum (bit-identical)",
+        [(TYPE_Q8_0, 4096, 4096)], CONTRACT_F32, 8, False, "reference", "f32"),
+}
 
 
 def load_peaks() -> tuple[float, str]:
@@ -74,8 +103,9 @@ def load_peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def load_traffic() -> float | None:
-    path = os.path.join(ROOT, "profiles", "q4k_q8k_matvec_traffic.json")
+def load_traffic(wl: Workload):
+    """DRAM bytes per step of the dominant kernel from the committed ncu capture."""
+    path = os.path.join(ROOT, "profiles", f"{wl.name}_traffic.json")
     try:
         with open(path) as f:
             return float(json.load(f)["dram_bytes_per_step"])
@@ -193,95 +223,100 @@ def max_over_ranks(value: float, world: int) -> float:
 
 # ---------------------------------------------------------------- CPU legs
 
-def cpu_sample_rows(k: int, n: int, fraction: float) -> int:
-    return max(1, int(n * fraction))
-
-
-def time_cpu_port(weights, xs, fraction: float, threads: int) -> tuple[float, int, float]:
-    """Run the restatement's Q8_K quantize + matvec over `fraction` of each
-    matrix's rows on `threads` threads.  Returns (seconds, bytes, check)."""
-    import oracle
-    port = oracle.port()
-    total_bytes = 0
-    jobs = []
-    for (k, n), w, x in zip(SHAPES, weights, xs):
-        rows = cpu_sample_rows(k, n, fraction)
-        total_bytes += rows * (k // 256) * 144 + k * 4 + rows * 4
-        jobs.append((k, rows, w, x))
-    results = []
-
-    def work(k, lo, hi, w, q8):
-        results.append(port.matvec_q8_k(TYPE_Q4_K, hi - lo, k, w[lo:hi], q8)[0].sum())
-
-    t0 = time.perf_counter()
-    for k, rows, w, x in jobs:
-        q8 = port.quantize_q8_k(x)
-        bounds = np.linspace(0, rows, threads + 1).astype(int)
-        ts = [threading.Thread(target=work, args=(k, bounds[i], bounds[i + 1], w, q8))
-              for i in range(threads) if bounds[i + 1] > bounds[i]]
-        for t in ts:
-            t.start()
-        for t in ts:
-            t.join()
-    dt = time.perf_counter() - t0
-    return dt, total_bytes, float(np.sum(results))
-
-
-def host_weights():
+def host_weights(wl: Workload):
     from oracle_b200 import synth
-    ws = [synth.weight(TYPE_Q4_K, n, k, "config2", f"W_{k}_{n}") for k, n in SHAPES]
-    xs = [synth.activations(k, 1, "config2", f"x_{k}")[0] for k, _ in SHAPES]
+    ws = [synth.weight(t, n, k, wl.name, f"W_{k}_{n}") for t, k, n in wl.ops]
+    xs = [synth.activations(k, 1, wl.name, f"x_{k}")[0] for _, k, _ in wl.ops]
     return ws, xs
 
 
-def cpu_baseline_leg(target_seconds: float = 3.0) -> dict:
-    """The whole config-2 step on one core, repeated for about target_seconds."""
-    ws, xs = host_weights()
-    time_cpu_port(ws, xs, 1.0, 1)  # warm
+def time_cpu(wl: Workload, ws, xs, fraction: float, threads: int) -> tuple[float, int]:
+    """Run `fraction` of every matrix's rows of one step on `threads` host
+    threads with the CPU implementation (ctypes releases the GIL).  config2/3:
+    the C restatement's Q8_K quantize + integer dot; config1: the reference's
+    own compiled reference_storage_matvec.  Returns (seconds, bytes)."""
+    import oracle
+    port = oracle.port()
+    ref = oracle.ref() if wl.cpu_kind == "reference" else None
+    jobs, total = [], 0
+    for (t, k, n), w, x in zip(wl.ops, ws, xs):
+        rows = max(1, int(n * fraction))
+        total += weight_bytes(t, k, rows) + k * 4 + rows * 4
+        jobs.append((t, k, rows, w, x))
+
+    def work(t, k, lo, hi, w, xin):
+        if ref is not None:
+            ref.storage_matvec(t, hi - lo, k, w[lo:hi], xin)
+        else:
+            port.matvec_q8_k(t, hi - lo, k, w[lo:hi], xin)
+
+    t0 = time.perf_counter()
+    for t, k, rows, w, x in jobs:
+        xin = x if ref is not None else port.quantize_q8_k(x)
+        bounds = np.linspace(0, rows, threads + 1).astype(int)
+        th = [threading.Thread(target=work, args=(t, k, bounds[i], bounds[i + 1], w, xin))
+              for i in range(threads) if bounds[i + 1] > bounds[i]]
+        for h in th:
+            h.start()
+        for h in th:
+            h.join()
+    return time.perf_counter() - t0, total
+
+
+def cpu_what(wl: Workload) -> str:
+    if wl.cpu_kind == "reference":
+        return "Oracle's own reference_storage_matvec compiled from the reference sources (oracle/_ref)"
+    return ("the C restatement of GGML's Q8_K quantize + integer dot (oracle/quant_oracle.c); Oracle has no "
+            "Q4_K decoder and no Q8_K dot (storage_decode.cpp:192-196 rejects type 12)")
+
+
+def cpu_baseline_leg(wl: Workload, target_seconds: float = 10.0) -> dict:
+    """One core, a bounded row sample of the step, about target_seconds."""
+    ws, xs = host_weights(wl)
+    dt, _ = time_cpu(wl, ws, xs, 0.02, 1)
+    fraction = min(1.0, 0.02 * (target_seconds / 4) / max(dt, 1e-4))
     total_t, total_b, reps = 0.0, 0, 0
-    while total_t < target_seconds:
-        dt, nbytes, _ = time_cpu_port(ws, xs, 1.0, 1)
+    while total_t < target_seconds and reps < 1000:
+        dt, nb = time_cpu(wl, ws, xs, fraction, 1)
         total_t += dt
-        total_b += nbytes
+        total_b += nb
         reps += 1
-    return {"value": total_b / total_t / 1e9, "unit": UNIT, "cores": 1, "kind": "port",
-            "sample": f"the full config-2 step ({STEP_BYTES / 1e6:.1f} MB) x {reps} repetitions, Q8_K quantize + "
-                      f"integer dot, single-threaded C restatement (oracle/quant_oracle.c), {total_t:.1f} s"}
+    return {"value": total_b / total_t / 1e9, "unit": UNIT, "cores": 1, "kind": wl.cpu_kind,
+            "sample": f"{fraction * 100:.1f}% of the rows of every {wl.name} matrix x {reps} repetitions "
+                      f"({total_b / 1e6:.0f} MB in {total_t:.1f} s, single thread): {cpu_what(wl)}"}
 
 
-def reference_arm(args) -> None:
+def reference_arm(args, wl: Workload) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if world > 1 and rank != 0:
         return
     threads = os.cpu_count() or 1
-    ws, xs = host_weights()
-    dt, _, _ = time_cpu_port(ws, xs, 0.01, threads)
+    ws, xs = host_weights(wl)
+    dt, _ = time_cpu(wl, ws, xs, 0.05, threads)
     # one step is a bounded sample sized for about 0.5 s on all threads
-    fraction = min(1.0, 0.01 * 0.5 / max(dt, 1e-4))
+    fraction = min(1.0, 0.05 * 0.5 / max(dt, 1e-4))
     for _ in range(args.warmup):
-        time_cpu_port(ws, xs, fraction, threads)
+        time_cpu(wl, ws, xs, fraction, threads)
     total_t, total_b = 0.0, 0
     for _ in range(args.steps):
-        dt, nb, _ = time_cpu_port(ws, xs, fraction, threads)
+        dt, nb = time_cpu(wl, ws, xs, fraction, threads)
         total_t += dt
         total_b += nb
     value = total_b / total_t / 1e9
-    sample = (f"{fraction * 100:.2f}% of the rows of each config-2 matrix per step on {threads} threads; "
-              "Oracle has no Q4_K decoder or Q8_K dot (storage_decode.cpp:192-196 rejects type 12), so this "
-              "is the C restatement of GGML's algorithm (oracle/quant_oracle.c)")
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+    sample = f"{fraction * 100:.2f}% of the rows of every {wl.name} matrix per step on {threads} threads: {cpu_what(wl)}"
+    line = {"impl": "reference", "metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_t / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/u4 -> f32",
-            "data": "synthetic", "config": config_block(args.gpus),
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+            "data": "synthetic", "config": wl.config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": wl.cpu_kind, "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------- GPU arm
 
-def gpu_arm(args) -> None:
+def gpu_arm(args, wl: Workload) -> None:
     import torch
 
     import oracle_b200 as ob
@@ -290,66 +325,72 @@ def gpu_arm(args) -> None:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     ctx = ob.Context(local, flags=ob.FLAG_PDL if not args.no_pdl else 0)
-    ws, xs = host_weights()
-    # weight pool: set 0 is the seeded host weights; others are byte-rotations
-    # of it (same distribution, distinct addresses) so every step misses L2
+    ws, xs = host_weights(wl)
+    # weight pool: set 0 is the seeded host weights; the others are rotations
+    # by whole blocks (same distribution, distinct addresses), so no step finds
+    # its weights in L2
     pool = []
-    for s in range(POOL_SETS):
-        pool.append([torch.from_numpy(np.roll(w.reshape(-1), s * 144)).to(dev) for w in ws])
+    for s in range(wl.pool_sets):
+        pool.append([torch.from_numpy(np.roll(w.reshape(-1), s * BLOCK[t][1])).to(dev)
+                     for w, (t, _, _) in zip(ws, wl.ops)])
     x_dev = [torch.from_numpy(x).to(dev) for x in xs]
-    y_dev = [torch.empty(n, dtype=torch.float32, device=dev) for _, n in SHAPES]
+    y_dev = [torch.empty(n, dtype=torch.float32, device=dev) for _, _, n in wl.ops]
     stream = torch.cuda.Stream(dev)
 
     def step(s: int):
-        # one persistent launch runs the three independent matvecs
-        ctx.matvec_program([(TYPE_Q4_K, n, k, pool[s % POOL_SETS][i], x_dev[i], y_dev[i], 0)
-                            for i, (k, n) in enumerate(SHAPES)], stream=stream)
+        ws_ = pool[s % wl.pool_sets]
+        if wl.program:
+            # one persistent launch runs all the (independent) matvecs of the step
+            ctx.matvec_program([(t, n, k, ws_[i], x_dev[i], y_dev[i], 0) for i, (t, k, n) in enumerate(wl.ops)],
+                               stream=stream)
+        else:
+            step_separate(s)
 
     def step_separate(s: int):
-        for i, (k, n) in enumerate(SHAPES):
-            ctx.storage_matvec(ob.CONTRACT_Q8K, TYPE_Q4_K, n, k, pool[s % POOL_SETS][i], x_dev[i], y_dev[i],
-                               stream=stream)
+        ws_ = pool[s % wl.pool_sets]
+        for i, (t, k, n) in enumerate(wl.ops):
+            ctx.storage_matvec(wl.contract, t, n, k, ws_[i], x_dev[i], y_dev[i], stream=stream)
 
-    # correctness gate on this box: set 0 of every shape against the restatement
+    # correctness gate on this box: set 0 of every op against the CPU checker
     with torch.cuda.stream(stream):
         step(0)
     stream.synchronize()
     ctx.device_status()
     import oracle
     port = oracle.port()
-    wants = [port.matvec_q8_k(TYPE_Q4_K, n, k, ws[i], port.quantize_q8_k(xs[i]))[0]
-             for i, (k, n) in enumerate(SHAPES)]
-    for i in range(len(SHAPES)):
+    wants = []
+    for i, (t, k, n) in enumerate(wl.ops):
+        if wl.contract == CONTRACT_Q8K:
+            wants.append(port.matvec_q8_k(t, n, k, ws[i], port.quantize_q8_k(xs[i]))[0])
+        else:
+            wants.append(port.storage_matvec_f32(t, n, k, ws[i], xs[i])[0])
         if not np.array_equal(y_dev[i].cpu().numpy().view(np.uint32), wants[i].view(np.uint32)):
-            raise SystemExit("GPU result differs from the restatement; refusing to report a number")
-    want = wants[2]
+            raise SystemExit("GPU result differs from the CPU checker; refusing to report a number")
 
-    # graph of one pass over the pool (POOL_SETS steps)
+    # graph of one pass over the pool (pool_sets steps); K mod pool_sets more from a tail graph
     launches0 = ctx.launch_count()
-    graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
-        for s in range(POOL_SETS):
+        for s in range(wl.pool_sets):
             step(s)
     stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        for s in range(POOL_SETS):
+        for s in range(wl.pool_sets):
             step(s)
-    launches_per_step = (ctx.launch_count() - launches0) // (2 * POOL_SETS)
-    # the remaining K mod POOL_SETS steps run from a second graph, so exactly K
-    # steps are timed (and exactly W warmed up)
-    rem = args.steps % POOL_SETS
+    launches_per_step = (ctx.launch_count() - launches0) // (2 * wl.pool_sets)
+    rem = args.steps % wl.pool_sets
     tail = None
     if rem:
         tail = torch.cuda.CUDAGraph()
         with torch.cuda.graph(tail, stream=stream):
             for s in range(rem):
                 step(s)
-    # graph replays go to the current stream: make that the capture stream,
-    # so the events below bracket exactly the replayed kernels
+    # graph replays go to the current stream: make that the capture stream, so
+    # the events below bracket exactly the replayed kernels
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup // POOL_SETS):
+        for _ in range(args.warmup // wl.pool_sets):
             graph.replay()
-        for s in range(args.warmup % POOL_SETS):
+        for s in range(args.warmup % wl.pool_sets):
             step(s)
     torch.cuda.synchronize()
     barrier(world)
@@ -358,72 +399,73 @@ def gpu_arm(args) -> None:
     sampler = ClockSampler(local)
     with sampler, torch.cuda.stream(stream):
         start.record(stream)
-        for _ in range(args.steps // POOL_SETS):
+        for _ in range(args.steps // wl.pool_sets):
             graph.replay()
         if tail is not None:
             tail.replay()
         end.record(stream)
         torch.cuda.synchronize()
-    steps_timed = args.steps
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world)
     ctx.device_status()
-    value = world * steps_timed * STEP_BYTES / (ms / 1e3) / 1e9
+    steps_timed = args.steps
+    value = world * steps_timed * wl.step_bytes / (ms / 1e3) / 1e9
+    # the timed region holds nothing but the step's kernels
+    achieved = wl.step_bytes / (ms / steps_timed * 1e-3) / 1e9
+    peak, peak_kind = load_peaks()
 
-    # the same step as three separate launches (one kernel per matvec)
-    gsep = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gsep, stream=stream):
-        for s in range(POOL_SETS):
-            step_separate(s)
-    with torch.cuda.stream(stream):
-        gsep.replay()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(20):
-            gsep.replay()
-        b.record(stream)
-        torch.cuda.synchronize()
-    sep_us = a.elapsed_time(b) * 1e3 / (20 * POOL_SETS)
-    del gsep
-
-    # per-shape launch durations, graphs of back-to-back single-matvec launches
-    per_shape = []
-    reps = 60
-    for i, (k, n) in enumerate(SHAPES):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for r in range(reps):
-                ctx.storage_matvec(ob.CONTRACT_Q8K, TYPE_Q4_K, n, k, pool[r % POOL_SETS][i], x_dev[i], y_dev[i],
-                                   stream=stream)
+    extra = {}
+    if wl.program:
+        # the same step as separate single-matvec launches
+        gsep = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gsep, stream=stream):
+            for s in range(wl.pool_sets):
+                step_separate(s)
         with torch.cuda.stream(stream):
-            g.replay()
+            gsep.replay()
             torch.cuda.synchronize()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            for _ in range(5):
-                g.replay()
+            for _ in range(20):
+                gsep.replay()
             b.record(stream)
             torch.cuda.synchronize()
-        us = a.elapsed_time(b) * 1e3 / (5 * reps)
-        per_shape.append({"shape": f"{k}->{n}", "us_per_launch": us,
-                          "gbs": algorithmic_bytes(k, n) / (us * 1e-6) / 1e9})
-        del g
-    # the timed region holds nothing but the program kernel (one launch per step)
-    achieved = STEP_BYTES / (ms / steps_timed * 1e-3) / 1e9
-    peak, peak_kind = load_peaks()
+        sep_us = a.elapsed_time(b) * 1e3 / (20 * wl.pool_sets)
+        extra["separate_launches"] = {"us_per_step": sep_us, "gbs": wl.step_bytes / (sep_us * 1e-6) / 1e9}
+        del gsep
+        per_op = []
+        reps = 60
+        for i, (t, k, n) in enumerate(wl.ops):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for r in range(reps):
+                    ctx.storage_matvec(wl.contract, t, n, k, pool[r % wl.pool_sets][i], x_dev[i], y_dev[i],
+                                       stream=stream)
+            with torch.cuda.stream(stream):
+                g.replay()
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(5):
+                    g.replay()
+                b.record(stream)
+                torch.cuda.synchronize()
+            us = a.elapsed_time(b) * 1e3 / (5 * reps)
+            per_op.append({"shape": f"{k}->{n}", "us_per_launch": us, "gbs": algorithmic_bytes(t, k, n) / (us * 1e-6) / 1e9})
+            del g
+        extra["per_shape_single_launch"] = per_op
 
     # e2e through the host-pointer C ABI with pinned buffers
     x_pin = [torch.from_numpy(x).pin_memory() for x in xs]
-    y_pin = [torch.empty(n, dtype=torch.float32).pin_memory() for _, n in SHAPES]
+    y_pin = [torch.empty(n, dtype=torch.float32).pin_memory() for _, _, n in wl.ops]
     x_np = [t.numpy() for t in x_pin]
     y_np = [t.numpy() for t in y_pin]
 
     def e2e_step():
-        for i, (k, n) in enumerate(SHAPES):
-            ctx.host_storage_matvec(ob.CONTRACT_Q8K, TYPE_Q4_K, n, k, ws[i], x_np[i], y_np[i])
+        for i, (t, k, n) in enumerate(wl.ops):
+            ctx.host_storage_matvec(wl.contract, t, n, k, ws[i], x_np[i], y_np[i])
 
-    for _ in range(max(3, args.warmup // 100)):
+    for _ in range(3):
         e2e_step()
     e2e_steps = max(10, min(args.steps, 2000))
     torch.cuda.synchronize()
@@ -432,30 +474,28 @@ def gpu_arm(args) -> None:
     for _ in range(e2e_steps):
         e2e_step()
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-    e2e_value = world * e2e_steps * STEP_BYTES / e2e_s / 1e9
-    if not np.array_equal(y_np[2].view(np.uint32), want.view(np.uint32)):
-        raise SystemExit("host-path result differs from the restatement")
+    e2e_value = world * e2e_steps * wl.step_bytes / e2e_s / 1e9
+    for i in range(len(wl.ops)):
+        if not np.array_equal(y_np[i].view(np.uint32), wants[i].view(np.uint32)):
+            raise SystemExit("host-path result differs from the CPU checker")
 
-    cpu = cpu_baseline_leg() if (rank == 0 and world == 1 and not args.no_cpu) else None
-    traffic = load_traffic()
+    cpu = cpu_baseline_leg(wl) if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
-        clocks = sampler.summary()
-        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps_timed,
+        kernel = ("matvec_program_kernel" if wl.program else
+                  "matvec_seq_kernel (lane per row, sequential f32)" if wl.contract == CONTRACT_F32 else
+                  "stream_rows_kernel<MatvecQ8KConsumer>")
+        line = {"metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps_timed,
                 "warmup": args.warmup, "ms_per_step": ms / steps_timed, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "int8 x u4 -> int32, f32 combine",
-                "data": "synthetic (seeded; BASELINE config-2 distributions)", "config": config_block(world),
+                "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+                "data": f"synthetic (seeded; BASELINE {wl.name} distributions)", "config": wl.config(world),
                 "gpu_launches": launches_per_step * steps_timed,
-                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": H2D_BYTES,
-                        "d2h_bytes_per_step": D2H_BYTES,
-                        "how": "oracle_cuda_host_storage_matvec (Q8_K contract) per shape, pinned host x/y, "
-                               "wall clock over synchronous calls"},
+                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
+                        "how": "oracle_cuda_host_storage_matvec per matvec, pinned host x/y, wall clock over "
+                               "synchronous calls, weights resident"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                             "traffic": traffic, "kernel": "matvec_program_kernel (3 Q4_K x Q8_K ops per launch)",
-                             "separate_launches": {"us_per_step": sep_us,
-                                                   "gbs": STEP_BYTES / (sep_us * 1e-6) / 1e9},
-                             "per_shape_single_launch": per_shape},
-                "cpu_baseline": cpu, "clocks": clocks, "pdl": not args.no_pdl}
+                             "traffic": load_traffic(wl), "kernel": kernel, **extra},
+                "cpu_baseline": cpu, "clocks": sampler.summary(), "pdl": not args.no_pdl}
         print(json.dumps(line), flush=True)
     del graph, tail
     ctx.close()
@@ -470,15 +510,17 @@ def main():
     ap.add_argument("--steps", type=int, default=12000)
     ap.add_argument("--warmup", type=int, default=600)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    wl = WORKLOADS[args.workload]
     if args.impl == "reference":
-        reference_arm(args)
+        reference_arm(args, wl)
     else:
-        gpu_arm(args)
+        gpu_arm(args, wl)
 
 
 if __name__ == "__main__":
