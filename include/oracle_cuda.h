@@ -207,6 +207,21 @@ oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const or
 oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cuda_matvec_op* ops, uint32_t n_ops,
                                                       void* stream);
 
+/* ------------------------------------------------------------------ prefill dequant-GEMM
+ * Y[m][n] = sum_k X[m][k] * W[n][k] for m < m_tokens: the batched form of the
+ * matvec for prompt ingestion (M >= 64 tokens).  W: `rows` GGML rows of `cols`
+ * columns (Q4_K only), device memory, 16-byte aligned.  X: m_tokens x cols f32,
+ * row-major, 16-byte aligned.  Y: m_tokens x rows f32, row-major.  Both operands
+ * are rounded to bf16 (round to nearest even; W from its exact f32 decode) and
+ * multiplied on the tensor cores with f32 accumulation; when K is split across
+ * CTAs (small grids) the partial sums are added atomically, so the last bits
+ * may vary between runs.  Asynchronous on `stream`.  No counterpart in the
+ * reference: Oracle ingests prompts one matvec at a time
+ * (src/runtime/qwen35_generation.cpp:737-747). */
+oracle_cuda_status oracle_cuda_prefill_gemm(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
+                                            const void* w_dev, uint64_t w_nbytes, const float* x_dev,
+                                            uint64_t m_tokens, float* y_dev, void* stream);
+
 /* ------------------------------------------------------------------ resident weights
  * Oracle's weights are immutable GGUF bytes in a read-only mapping
  * (MappedGgufModel, include/oracle/model/mapped_gguf.hpp:56-59).  They are

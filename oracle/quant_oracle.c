@@ -468,11 +468,12 @@ int oq_gemm_sampled(uint32_t type, uint64_t n, uint64_t k, const uint8_t* w, uin
         double s = 0.0;
         for (uint64_t i = 0; i < k; ++i) {
             float a = xr[i], b = dec[i];
-            if (mode == 1) {
+            if (mode == 1 || mode == 2) {
                 a = oq_bf16_to_f32(oq_f32_to_bf16_rne(a));
                 b = oq_bf16_to_f32(oq_f32_to_bf16_rne(b));
             }
-            s += (double)a * (double)b;
+            const double t = (double)a * (double)b;
+            s += mode >= 2 ? fabs(t) : t;
         }
         y[c] = s;
     }

@@ -109,7 +109,9 @@ int oq_storage_matvec_f64(uint32_t type, uint64_t rows, uint64_t k, const uint8_
 /* Prefill GEMM references, Y[m][n] = sum_k X[m][k] * W[n][k], evaluated only
  * at the `count` sampled (m, n) pairs.  f64 accumulation throughout.
  *   mode 0: f32 operands (X as given, W = Oracle's f32 decode);
- *   mode 1: both operands rounded to bf16 (round-to-nearest-even) first. */
+ *   mode 1: both operands rounded to bf16 (round-to-nearest-even) first;
+ *   mode 2: sum of |products| of the mode-1 operands (error scale);
+ *   mode 3: sum of |products| of the mode-0 operands. */
 int oq_gemm_sampled(uint32_t type, uint64_t n, uint64_t k, const uint8_t* w, uint64_t m,
                     const float* x, uint64_t count, const uint64_t* m_index,
                     const uint64_t* n_index, int mode, double* y);

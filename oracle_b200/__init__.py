@@ -111,6 +111,7 @@ _proto("oracle_cuda_host_storage_matvec", [_vp, _i32, _u32, _u64, _u64, _vp, _u6
 _proto("oracle_cuda_host_storage_dot", [_vp, _i32, _u32, _u64, _vp, _u64, _vp, _u64, _vp])
 _proto("oracle_cuda_host_decode_rows", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64])
 _proto("oracle_cuda_evict_resident", [_vp])
+_proto("oracle_cuda_prefill_gemm", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _vp])
 
 
 class OracleCudaError(Exception):
@@ -315,6 +316,14 @@ class Context:
         for i, (qtype, rows, cols, w, x, y, after) in enumerate(ops):
             arr[i] = MatvecOp(qtype, 1 if after else 0, rows, cols, _addr(w), _nbytes(w), _addr(x), _addr(y))
         self._check(_lib.oracle_cuda_matvec_program(self._h, arr, len(ops), _stream(stream)))
+
+    def prefill_gemm(self, qtype, rows, cols, w, x, m, y, stream=None, w_nbytes=None) -> None:
+        """oracle_cuda_prefill_gemm: y[m][n] = sum_k x[m][k] * W[n][k] on the
+        tensor cores (bf16 operands, f32 accumulation); x is m x cols f32,
+        y is m x rows f32, all device memory."""
+        self._check(_lib.oracle_cuda_prefill_gemm(
+            self._h, qtype, rows, cols, _addr(w), _nbytes(w) if w_nbytes is None else w_nbytes, _addr(x), m,
+            _addr(y), _stream(stream)))
 
     # -------------------------------------------------------------- resident weights
     def upload(self, qtype, rows, cols, host: np.ndarray, row_begin=0, row_end=None) -> Weight:

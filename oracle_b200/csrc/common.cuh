@@ -127,6 +127,10 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+__device__ __forceinline__ void named_barrier_arrive(uint32_t id, uint32_t threads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ---------------------------------------------------------------- block fields
 
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {

@@ -1,0 +1,347 @@
+// gemm_q4k.cuh -- prefill dequant-GEMM on the 5th-generation tensor cores.
+//
+//   Y[m][n] = sum_k X[m][k] * W[n][k]      X: M x K activations, W: N x K Q4_K rows
+//
+// There is no reference counterpart: Oracle ingests prompts one matvec at a
+// time (qwen35_generation.cpp:737-747).  Operands are bf16, accumulation f32:
+//   * W tiles are dequantized in shared memory: each element is Oracle's f32
+//     decode (d*sc)*q - dmin*m (storage_decode.cpp:44-94, Q5_K without the
+//     high-bit plane), rounded once to bf16 (round to nearest even);
+//   * X is converted to bf16 (round to nearest even) by a separate kernel and
+//     read with tensor-memory-accelerator (TMA) tile loads.
+//
+// CTA tile: 128 weight rows (the MMA's M, TMEM lanes) x 256 tokens (the MMA's
+// N, TMEM columns), K in stages of 64 (one 128-byte swizzle row of bf16).
+// Warp roles (12 warps):
+//   warp 0  lane 0: X tile loads (2-D TMA, 128-byte swizzle) into the B ring;
+//                   the warp also owns the TMEM allocation (256 columns)
+//   warp 1  lane 0: issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32), 4 per
+//                   stage, and tcgen05.commit to free stages / signal the end
+//   warp 2  lane 0: raw Q4_K loads: 2-D TMA boxes of 128 rows x 144 bytes (one
+//                   super-block column) into a ring of raw stages
+//   warps 4-11:     dequantize raw super-blocks into the A ring (K-major,
+//                   128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7)),
+//                   then, after the last MMA, read the accumulator out of TMEM
+//                   (tcgen05.ld 32x32b) and store Y (coalesced along n)
+// Every mbarrier wait is bounded (common.cuh); a timeout sets a CTA abort flag,
+// the roles leave their loops, outstanding TMA loads and MMAs are waited for
+// (bounded), TMEM is freed and the kernel returns with the status recorded.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace oracle_cuda {
+
+constexpr uint32_t kGemmTileN = 128;  // weight rows per CTA (UMMA M)
+constexpr uint32_t kGemmTileM = 256;  // tokens per CTA (UMMA N)
+constexpr uint32_t kGemmTileK = 64;   // K per stage
+constexpr uint32_t kGemmStages = 3;
+constexpr uint32_t kGemmRawStages = 3;
+constexpr uint32_t kGemmSbBytes = 144;  // Q4_K super-block
+constexpr uint32_t kGemmABytes = kGemmTileN * kGemmTileK * 2;
+constexpr uint32_t kGemmBBytes = kGemmTileM * kGemmTileK * 2;
+constexpr uint32_t kGemmRawBytes = kGemmTileN * kGemmSbBytes;
+constexpr uint32_t kGemmDequantWarps = 8;
+constexpr uint32_t kGemmThreads = (4 + kGemmDequantWarps) * 32;
+constexpr uint32_t kGemmTmemCols = 256;
+constexpr uint32_t kGemmOffB = kGemmStages * kGemmABytes;
+constexpr uint32_t kGemmOffRaw = kGemmOffB + kGemmStages * kGemmBBytes;
+constexpr uint32_t kGemmOffBars = kGemmOffRaw + kGemmRawStages * kGemmRawBytes;
+constexpr uint32_t kGemmBars = 3 * kGemmStages + 2 * kGemmRawStages + 1;
+constexpr uint32_t kGemmSmemBytes = 1024 + kGemmOffBars + kGemmBars * 8 + 16;
+
+struct GemmParams {
+    float* y;                // m x n row-major
+    uint32_t n, m, k;        // weight rows, tokens, columns
+    uint32_t k_per_split;    // columns per blockIdx.z (multiple of 256)
+    uint32_t accumulate;     // 1: add into y (split K), 0: store
+    DeviceStatus* status;
+};
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 1024 bytes stacked densely (stride byte offset 1024), descriptor version 1.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem) {
+    return static_cast<uint64_t>((smem >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+// Instruction descriptor: D f32, A and B bf16, both K-major, M = 128, N = 256.
+constexpr uint32_t kGemmIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((kGemmTileM >> 3) << 17) |
+                                ((kGemmTileN >> 4) << 24);
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+            "r"(dst),
+        "l"(map), "r"(smem_addr(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// q (0..15) to f32 exactly: the nibble placed under the exponent of 2^23.
+__device__ __forceinline__ float nib_to_f32(uint32_t nib) {
+    return __fsub_rn(__uint_as_float(0x4B000000u | nib), 8388608.0f);
+}
+
+// 6-bit scale and min of sub-block j from the three little-endian words
+// holding the 12 packed bytes (storage_decode.cpp:44-61).
+__device__ __forceinline__ void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t j, uint32_t& sc,
+                                              uint32_t& mn) {
+    if (j < 4) {
+        sc = (s0 >> (8 * j)) & 63u;
+        mn = (s1 >> (8 * j)) & 63u;
+    } else {
+        const uint32_t t = 8 * (j - 4);
+        sc = ((s2 >> t) & 0x0Fu) | (((s0 >> t) & 0xC0u) >> 2);
+        mn = ((s2 >> t) >> 4 & 0x0Fu) | (((s1 >> t) & 0xC0u) >> 2);
+    }
+}
+
+// 8 consecutive elements (one nibble half of 8 bytes) -> 4 packed bf16 pairs.
+__device__ __forceinline__ uint4 dequant8(uint32_t w0, uint32_t w1, uint32_t shift, float dsc, float dm) {
+    float f[8];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        f[t] = __fsub_rn(__fmul_rn(dsc, nib_to_f32((w0 >> (8 * t + shift)) & 0x0Fu)), dm);
+        f[4 + t] = __fsub_rn(__fmul_rn(dsc, nib_to_f32((w1 >> (8 * t + shift)) & 0x0Fu)), dm);
+    }
+    return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                      pack_bf16x2(f[6], f[7]));
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_q4k_bf16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                         const GemmParams p) {
+    extern __shared__ uint8_t gemm_smem[];
+    const uint32_t raw_base = smem_addr(gemm_smem);
+    const uint32_t base = (raw_base + 1023u) & ~1023u;
+    uint8_t* smem = gemm_smem + (base - raw_base);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGemmOffBars);
+    uint64_t* full_a = bars;                          // dequant warps -> MMA
+    uint64_t* full_b = bars + kGemmStages;            // X TMA -> MMA
+    uint64_t* empty = bars + 2 * kGemmStages;         // MMA commit -> producers
+    uint64_t* raw_full = bars + 3 * kGemmStages;      // raw TMA -> dequant
+    uint64_t* raw_empty = raw_full + kGemmRawStages;  // dequant -> raw TMA
+    uint64_t* acc_full = raw_empty + kGemmRawStages;  // last MMA -> epilogue
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + kGemmBars);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t m0 = blockIdx.x * kGemmTileM, n0 = blockIdx.y * kGemmTileN;
+    const uint32_t k_begin = blockIdx.z * p.k_per_split;
+    const uint32_t k_end = p.k - k_begin < p.k_per_split ? p.k : k_begin + p.k_per_split;
+    const uint32_t nk = (k_end - k_begin) / kGemmTileK;
+    const uint32_t nsb = nk / 4;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kGemmStages; ++s) {
+            mbar_init(&full_a[s], kGemmDequantWarps);
+            mbar_init(&full_b[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (uint32_t r = 0; r < kGemmRawStages; ++r) {
+            mbar_init(&raw_full[r], 1);
+            mbar_init(&raw_empty[r], kGemmDequantWarps);
+        }
+        mbar_init(acc_full, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_addr(const_cast<uint32_t*>(tmem_slot))),
+                     "r"(kGemmTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------------------------------------------------- X tiles
+            uint32_t issued = 0;
+            for (uint32_t kc = 0; kc < nk && !*abort_flag; ++kc) {
+                const uint32_t s = kc % kGemmStages;
+                if (kc >= kGemmStages && !mbar_wait(&empty[s], ((kc / kGemmStages) - 1) & 1, p.status, 41)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full_b[s], kGemmBBytes);
+                tma_load_2d(base + kGemmOffB + s * kGemmBBytes, &tmap_x, &full_b[s],
+                            static_cast<int>(k_begin + kc * kGemmTileK), static_cast<int>(m0));
+                issued = kc + 1;
+            }
+            // no load may still be in flight when the CTA exits
+            for (uint32_t kc = issued > kGemmStages ? issued - kGemmStages : 0; kc < issued; ++kc)
+                mbar_wait(&full_b[kc % kGemmStages], (kc / kGemmStages) & 1, p.status, 42);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------------------------------------------------- MMA issue
+            for (uint32_t kc = 0; kc < nk && !*abort_flag; ++kc) {
+                const uint32_t s = kc % kGemmStages, par = (kc / kGemmStages) & 1;
+                if (!mbar_wait(&full_b[s], par, p.status, 43) || !mbar_wait(&full_a[s], par, p.status, 44)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t ad = umma_desc_sw128(base + s * kGemmABytes);
+                const uint64_t bd = umma_desc_sw128(base + kGemmOffB + s * kGemmBBytes);
+#pragma unroll
+                for (uint32_t kk = 0; kk < kGemmTileK / 16; ++kk)
+                    umma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, kGemmIdesc, (kc | kk) != 0);
+                umma_commit(&empty[s]);
+            }
+            umma_commit(acc_full);  // also after an abort: completes once issued MMAs finish
+        }
+    } else if (warp == 2) {
+        if (lane == 0) {
+            // ---------------------------------------------------------- raw Q4_K tiles
+            uint32_t issued = 0;
+            for (uint32_t j = 0; j < nsb && !*abort_flag; ++j) {
+                const uint32_t r = j % kGemmRawStages;
+                if (j >= kGemmRawStages &&
+                    !mbar_wait(&raw_empty[r], ((j / kGemmRawStages) - 1) & 1, p.status, 45)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&raw_full[r], kGemmRawBytes);
+                tma_load_2d(base + kGemmOffRaw + r * kGemmRawBytes, &tmap_w, &raw_full[r],
+                            static_cast<int>((k_begin / 256 + j) * kGemmSbBytes), static_cast<int>(n0));
+                issued = j + 1;
+            }
+            for (uint32_t j = issued > kGemmRawStages ? issued - kGemmRawStages : 0; j < issued; ++j)
+                mbar_wait(&raw_full[j % kGemmRawStages], (j / kGemmRawStages) & 1, p.status, 46);
+        }
+    } else if (warp >= 4) {
+        // -------------------------------------------------------------- dequantize
+        const uint32_t t = threadIdx.x - 128;
+        bool ok = true;
+        for (uint32_t kc = 0; kc < nk; ++kc) {
+            if (*abort_flag) {
+                ok = false;
+                break;
+            }
+            const uint32_t s = kc % kGemmStages, j = kc / 4, g = kc % 4, r = j % kGemmRawStages;
+            if (g == 0 && !mbar_wait(&raw_full[r], (j / kGemmRawStages) & 1, p.status, 47)) ok = false;
+            if (ok && kc >= kGemmStages && !mbar_wait(&empty[s], ((kc / kGemmStages) - 1) & 1, p.status, 48))
+                ok = false;
+            if (!ok) {
+                *abort_flag = 1;
+                break;
+            }
+            const uint8_t* raw = smem + kGemmOffRaw + r * kGemmRawBytes;
+            uint8_t* a = smem + s * kGemmABytes;
+#pragma unroll
+            for (uint32_t i = 0; i < 2; ++i) {
+                const uint32_t u = t + 256 * i, row = u >> 2, o = u & 3;
+                const uint8_t* rp = raw + row * kGemmSbBytes;
+                const uint4 h = *reinterpret_cast<const uint4*>(rp);
+                const float d = f16_bits_to_f32(static_cast<uint16_t>(h.x & 0xFFFFu));
+                const float dmin = f16_bits_to_f32(static_cast<uint16_t>(h.x >> 16));
+                uint32_t sc_lo, mn_lo, sc_hi, mn_hi;
+                q4k_scale_min(h.y, h.z, h.w, 2 * g, sc_lo, mn_lo);
+                q4k_scale_min(h.y, h.z, h.w, 2 * g + 1, sc_hi, mn_hi);
+                const uint2 q = *reinterpret_cast<const uint2*>(rp + 16 + 32 * g + 8 * o);
+                const uint4 lo = dequant8(q.x, q.y, 0, __fmul_rn(d, static_cast<float>(sc_lo)),
+                                          __fmul_rn(dmin, static_cast<float>(mn_lo)));
+                const uint4 hi = dequant8(q.x, q.y, 4, __fmul_rn(d, static_cast<float>(sc_hi)),
+                                          __fmul_rn(dmin, static_cast<float>(mn_hi)));
+                *reinterpret_cast<uint4*>(a + row * 128 + ((o ^ (row & 7)) * 16)) = lo;
+                *reinterpret_cast<uint4*>(a + row * 128 + (((4 + o) ^ (row & 7)) * 16)) = hi;
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&full_a[s]);
+                if (g == 3) mbar_arrive(&raw_empty[r]);
+            }
+        }
+        // ------------------------------------------------------------------ epilogue
+        if (!mbar_wait(acc_full, 0, p.status, 49)) ok = false;
+        tc_fence_after();
+        const uint32_t q = warp & 3, half = (warp - 4) >> 2;
+        const uint32_t n = n0 + 32 * q + lane;
+        if (ok && !*abort_flag) {
+#pragma unroll 1
+            for (uint32_t cb = 0; cb < kGemmTileM / 64; ++cb) {
+                const uint32_t col0 = half * (kGemmTileM / 2) + 32 * cb;
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem + ((32 * q) << 16) + col0, v);
+                if (n < p.n) {
+#pragma unroll
+                    for (uint32_t jj = 0; jj < 32; ++jj) {
+                        const uint32_t m = m0 + col0 + jj;
+                        if (m < p.m) {
+                            float* dst = p.y + static_cast<uint64_t>(m) * p.n + n;
+                            if (p.accumulate)
+                                atomicAdd(dst, __uint_as_float(v[jj]));
+                            else
+                                *dst = __uint_as_float(v[jj]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmTmemCols)
+                     : "memory");
+    }
+}
+
+// X f32 -> bf16 (round to nearest even), 4 elements per thread-step.
+__global__ void __launch_bounds__(256) convert_bf16_kernel(const float* __restrict__ x, uint32_t* __restrict__ out,
+                                                           uint64_t n4) {
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n4; i += uint64_t(gridDim.x) * blockDim.x) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+        reinterpret_cast<uint2*>(out)[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    }
+}
+
+}  // namespace oracle_cuda

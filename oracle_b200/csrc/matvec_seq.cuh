@@ -7,33 +7,50 @@
 // that order, so its output equals the reference's bit for bit:
 //   sum = __fadd_rn(sum, __fmul_rn(w_e, x_e)),  w_e = Oracle's decode (decode.cuh)
 //
-// Mapping: one lane per row (a row's sum is a serial chain; rows run in
-// parallel).  A warp owns 32 consecutive rows.  The row is walked in chunks of
-// whole blocks (kChunkBlocks blocks, kChunkElems elements, kChunkBytes bytes).
-// For each chunk the warp copies its 32 rows' chunk bytes into a shared slot
-// per row, realigned so every slot starts at a 4-byte boundary (each slot word
-// is a funnel shift of two aligned global words, read coalesced), with an odd
-// slot stride in words so that lane-per-row shared reads are conflict-free.
-// Each lane then decodes its own slot at compile-time offsets.  x is read with
-// warp-uniform (broadcast) loads.
+// The additions of one row form a serial chain of K dependent f32 adds; that
+// chain, not HBM, bounds the kernel (K x add latency per row).  Everything
+// else is independent work, so the CTA splits it off:
+//   * chain warps (kBatch of them, warp b owns activation vector b): lane r
+//     keeps the running sum of row r and does nothing but one 128-bit shared
+//     load per 4 products and the adds;
+//   * producer warps (the other 8 - kBatch) copy the CTA's rows a chunk of
+//     C elements at a time into a ring of raw stages with cp.async (4-byte
+//     words covering the chunk, so any 2-byte row alignment works), several
+//     chunks ahead of use, then decode each chunk from shared memory (decode4),
+//     multiply by x and store the products to a two-deep product ring.
+// Product stages are handed to the chains with named barriers (FULL: producers
+// arrive, chains sync; EMPTY: chains arrive, producers sync before reuse).
+// Raw stages are private to the producers (cp.async groups + a producer-only
+// barrier).  Product layout per stage and vector: rows of C + 4 words, so a
+// chain lane's 128-bit loads hit distinct banks in every quarter-warp.
 #pragma once
 
 #include "decode.cuh"
 
 namespace oracle_cuda {
 
-template <uint32_t kType>
-struct SeqChunk;
-template <> struct SeqChunk<8>  { static constexpr uint32_t kBlocks = 8, kBlockElems = 32,  kBlockBytes = 34; };
-template <> struct SeqChunk<12> { static constexpr uint32_t kBlocks = 1, kBlockElems = 256, kBlockBytes = 144; };
-template <> struct SeqChunk<13> { static constexpr uint32_t kBlocks = 1, kBlockElems = 256, kBlockBytes = 176; };
-template <> struct SeqChunk<14> { static constexpr uint32_t kBlocks = 1, kBlockElems = 256, kBlockBytes = 210; };
-template <> struct SeqChunk<0>  { static constexpr uint32_t kBlocks = 64, kBlockElems = 1, kBlockBytes = 4; };
-template <> struct SeqChunk<1>  { static constexpr uint32_t kBlocks = 128, kBlockElems = 1, kBlockBytes = 2; };
-template <> struct SeqChunk<30> { static constexpr uint32_t kBlocks = 128, kBlockElems = 1, kBlockBytes = 2; };
-
-constexpr int kSeqWarps = 4;
+constexpr uint32_t kSeqRows = 8;       // rows per CTA (one chain lane each; several CTAs per SM)
+constexpr uint32_t kSeqThreads = 256;  // 8 warps: kBatch chain warps + producers
+constexpr uint32_t kSeqStages = 2;     // product stages
 constexpr uint32_t kSeqMaxBatch = 4;
+constexpr uint32_t kSeqMaxRawStages = 16;
+// named barrier ids: FULL 1..2, EMPTY 3..4, producers-only 5
+constexpr uint32_t kSeqBarFull = 1, kSeqBarEmpty = 1 + kSeqStages, kSeqBarProducers = 1 + 2 * kSeqStages;
+
+// Elements per chunk: whole blocks, at least 128 elements.
+__host__ __device__ constexpr uint32_t seq_chunk_elems(uint32_t type) {
+    return (type == 12 || type == 13 || type == 14) ? 256u : 128u;
+}
+__host__ __device__ constexpr uint32_t seq_chunk_bytes(uint32_t type) {
+    return type == 8 ? 136u : type == 12 ? 144u : type == 13 ? 176u : type == 14 ? 210u : type == 0 ? 512u : 256u;
+}
+// raw slot per row: the chunk's bytes as aligned words plus one word of slack
+__host__ __device__ constexpr uint32_t seq_raw_slot_bytes(uint32_t type) {
+    return (((seq_chunk_bytes(type) + 3u) & ~3u) + 4u + 15u) & ~15u;
+}
+__host__ __device__ constexpr uint32_t seq_prod_bytes(uint32_t type, uint32_t batch) {
+    return kSeqStages * batch * kSeqRows * (seq_chunk_elems(type) + 4u) * 4u;
+}
 
 struct MatvecSeqParams {
     const uint8_t* w;
@@ -42,144 +59,153 @@ struct MatvecSeqParams {
     uint64_t rows;
     uint64_t row_bytes;
     uint32_t k;
-    uint32_t batch;  // <= kSeqMaxBatch
+    uint32_t raw_stages;  // 3 .. kSeqMaxRawStages
 };
 
-__device__ __forceinline__ uint32_t slot_byte(const uint32_t* s, uint32_t off) {
-    return (s[off >> 2] >> (8u * (off & 3u))) & 0xFFu;
+__device__ __forceinline__ void cp_async_4(uint32_t dst_smem, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async_wait_dyn(uint32_t n) {
+    // wait_group takes an immediate; the prefetch distance is at most 14
+    switch (n) {
+        case 0: cp_async_wait<0>(); break;
+        case 1: cp_async_wait<1>(); break;
+        case 2: cp_async_wait<2>(); break;
+        case 3: cp_async_wait<3>(); break;
+        case 4: cp_async_wait<4>(); break;
+        case 5: cp_async_wait<5>(); break;
+        case 6: cp_async_wait<6>(); break;
+        case 7: cp_async_wait<7>(); break;
+        case 8: cp_async_wait<8>(); break;
+        case 9: cp_async_wait<9>(); break;
+        case 10: cp_async_wait<10>(); break;
+        case 11: cp_async_wait<11>(); break;
+        case 12: cp_async_wait<12>(); break;
+        case 13: cp_async_wait<13>(); break;
+        default: cp_async_wait<14>(); break;
+    }
 }
 
-template <uint32_t kType>
-__global__ void __launch_bounds__(kSeqWarps * 32) matvec_seq_kernel(const MatvecSeqParams p) {
-    using Ch = SeqChunk<kType>;
-    constexpr uint32_t kChunkBytes = Ch::kBlocks * Ch::kBlockBytes;
-    constexpr uint32_t kChunkElems = Ch::kBlocks * Ch::kBlockElems;
-    constexpr uint32_t kWords = (kChunkBytes + 3) / 4 + 1;           // + 1: a misaligned chunk spans one more word
-    constexpr uint32_t kStride = (kWords % 2) ? kWords : kWords + 1;  // odd: conflict-free lane-per-row reads
-    __shared__ uint32_t slots[kSeqWarps][32 * kStride];
+template <uint32_t kType, uint32_t kBatch>
+__global__ void __launch_bounds__(kSeqThreads) matvec_seq_kernel(const MatvecSeqParams p) {
+    constexpr uint32_t C = seq_chunk_elems(kType);
+    constexpr uint32_t kStride = C + 4;
+    constexpr uint32_t kVecWords = kSeqRows * kStride;
+    constexpr uint32_t kSlot = seq_raw_slot_bytes(kType);
+    extern __shared__ __align__(16) float prod[];  // [stage][batch][row][kStride], then the raw ring
+    uint8_t* raw = reinterpret_cast<uint8_t*>(prod + kSeqStages * kBatch * kVecWords);
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint32_t* myslots = slots[warp];
-    const uint64_t row_base = (static_cast<uint64_t>(blockIdx.x) * kSeqWarps + warp) * 32;
-    if (row_base >= p.rows) return;
-    const uint32_t nr = p.rows - row_base < 32 ? static_cast<uint32_t>(p.rows - row_base) : 32u;
-    const uint64_t my_row = row_base + lane;
-    const bool live = lane < static_cast<int>(nr);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t row_base = static_cast<uint64_t>(blockIdx.x) * kSeqRows;
+    const uint32_t nr = p.rows - row_base < kSeqRows ? static_cast<uint32_t>(p.rows - row_base) : kSeqRows;
+    const uint32_t n_chunks = (p.k + C - 1) / C;
 
-    float sum[kSeqMaxBatch];
-#pragma unroll
-    for (uint32_t b = 0; b < kSeqMaxBatch; ++b) sum[b] = 0.0f;
-
-    const uint32_t n_chunks = (p.k + kChunkElems - 1) / kChunkElems;
-    for (uint32_t c = 0; c < n_chunks; ++c) {
-        const uint32_t e0 = c * kChunkElems;
-        const uint32_t elems = p.k - e0 < kChunkElems ? p.k - e0 : kChunkElems;
-        const uint32_t blocks = elems / Ch::kBlockElems;  // whole blocks in this chunk
-        const uint32_t cbytes = blocks * Ch::kBlockBytes;
-        // ---- cooperative copy: slot word j of row i = bytes [4j, 4j+4) of the chunk
-        const uint32_t words = (cbytes + 3) / 4;
-        __syncwarp();
-        for (uint32_t t = lane; t < nr * words; t += 32) {
-            const uint32_t i = t / words, j = t % words;
-            const uintptr_t start = reinterpret_cast<uintptr_t>(p.w) + (row_base + i) * p.row_bytes +
-                                    static_cast<uint64_t>(c) * (kChunkElems / Ch::kBlockElems) * Ch::kBlockBytes;
-            const uintptr_t aw = (start & ~uintptr_t(3)) + 4u * j;
-            const uint32_t sh = static_cast<uint32_t>(start & 3u) * 8u;
-            const uint32_t lo = *reinterpret_cast<const uint32_t*>(aw);
-            // the next aligned word is read only if it holds wanted bytes
-            const bool need_hi = sh != 0 && (aw + 4) < start + cbytes;
-            const uint32_t hi = need_hi ? *reinterpret_cast<const uint32_t*>(aw + 4) : 0u;
-            myslots[i * kStride + j] = sh ? __funnelshift_r(lo, hi, sh) : lo;
+    if (warp < kBatch) {
+        // ---------------------------------------------------------- chain warp
+        const uint32_t b = warp;
+        float sum = 0.0f;
+        for (uint32_t c = 0; c < n_chunks; ++c) {
+            const uint32_t s = c % kSeqStages;
+            named_barrier_sync(kSeqBarFull + s, kSeqThreads);
+            const uint32_t elems = p.k - c * C < C ? p.k - c * C : C;
+            const float* row = prod + (s * kBatch + b) * kVecWords + (lane < kSeqRows ? lane : 0) * kStride;
+            if (elems == C) {
+#pragma unroll 8
+                for (uint32_t e = 0; e < C; e += 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(row + e);
+                    sum = __fadd_rn(sum, v.x);
+                    sum = __fadd_rn(sum, v.y);
+                    sum = __fadd_rn(sum, v.z);
+                    sum = __fadd_rn(sum, v.w);
+                }
+            } else {
+                for (uint32_t e = 0; e < elems; ++e) sum = __fadd_rn(sum, row[e]);
+            }
+            if (c + kSeqStages < n_chunks) named_barrier_arrive(kSeqBarEmpty + s, kSeqThreads);
         }
-        __syncwarp();
-        if (!live) continue;
-        const uint32_t* s = myslots + lane * kStride;
-        // ---- decode this lane's chunk and accumulate in element order
-        for (uint32_t bi = 0; bi < blocks; ++bi) {
-            const uint32_t bo = bi * Ch::kBlockBytes;  // block offset in the slot
-            const uint32_t eb = e0 + bi * Ch::kBlockElems;
-            if constexpr (kType == 8) {
-                const float d = f16_bits_to_f32(static_cast<uint16_t>(slot_byte(s, bo) | (slot_byte(s, bo + 1) << 8)));
-#pragma unroll 8
-                for (uint32_t l = 0; l < 32; ++l) {
-                    const int q = static_cast<int>(static_cast<int8_t>(slot_byte(s, bo + 2 + l)));
-                    const float wv = __fmul_rn(d, static_cast<float>(q));
-#pragma unroll
-                    for (uint32_t b = 0; b < kSeqMaxBatch; ++b)
-                        if (b < p.batch) sum[b] = __fadd_rn(sum[b], __fmul_rn(wv, __ldg(p.x + uint64_t(b) * p.k + eb + l)));
-                }
-            } else if constexpr (kType == 12 || kType == 13) {
-                constexpr uint32_t kQs = kType == 12 ? 16u : 48u;
-                const float d = f16_bits_to_f32(static_cast<uint16_t>(slot_byte(s, bo) | (slot_byte(s, bo + 1) << 8)));
-                const float dmin = f16_bits_to_f32(static_cast<uint16_t>(slot_byte(s, bo + 2) | (slot_byte(s, bo + 3) << 8)));
-                for (uint32_t g = 0; g < 4; ++g) {
-                    for (uint32_t up = 0; up < 2; ++up) {
-                        const uint32_t jsb = 2 * g + up;
-                        int sc, mn;
-                        if (jsb < 4) {
-                            sc = slot_byte(s, bo + 4 + jsb) & 63;
-                            mn = slot_byte(s, bo + 8 + jsb) & 63;
-                        } else {
-                            sc = (slot_byte(s, bo + 8 + jsb) & 0x0F) | ((slot_byte(s, bo + jsb) >> 6) << 4);
-                            mn = (slot_byte(s, bo + 8 + jsb) >> 4) | ((slot_byte(s, bo + 4 + jsb) >> 6) << 4);
-                        }
-                        const float dsc = __fmul_rn(d, static_cast<float>(sc));
-                        const float dm = __fmul_rn(dmin, static_cast<float>(mn));
-#pragma unroll 8
-                        for (uint32_t l = 0; l < 32; ++l) {
-                            const uint32_t byte = slot_byte(s, bo + kQs + 32 * g + l);
-                            uint32_t q = up ? (byte >> 4) : (byte & 0x0F);
-                            if constexpr (kType == 13) q |= ((slot_byte(s, bo + 16 + l) >> jsb) & 1u) << 4;
-                            const float wv = __fsub_rn(__fmul_rn(dsc, static_cast<float>(q)), dm);
-                            const uint32_t e = eb + 64 * g + 32 * up + l;
-#pragma unroll
-                            for (uint32_t b = 0; b < kSeqMaxBatch; ++b)
-                                if (b < p.batch) sum[b] = __fadd_rn(sum[b], __fmul_rn(wv, __ldg(p.x + uint64_t(b) * p.k + e)));
-                        }
-                    }
-                }
-            } else if constexpr (kType == 14) {
-                const float d = f16_bits_to_f32(static_cast<uint16_t>(slot_byte(s, bo + 208) | (slot_byte(s, bo + 209) << 8)));
-                for (uint32_t h = 0; h < 2; ++h) {
-                    for (uint32_t sg = 0; sg < 4; ++sg) {
-                        for (uint32_t half16 = 0; half16 < 2; ++half16) {
-                            const int scale = static_cast<int>(static_cast<int8_t>(slot_byte(s, bo + 192 + 8 * h + half16 + 2 * sg)));
-                            const float dsc = __fmul_rn(d, static_cast<float>(scale));
-#pragma unroll 8
-                            for (uint32_t l16 = 0; l16 < 16; ++l16) {
-                                const uint32_t l = 16 * half16 + l16;
-                                const uint32_t lo_byte = slot_byte(s, bo + 64 * h + l + ((sg & 1u) ? 32u : 0u));
-                                const uint32_t lo = sg >= 2 ? (lo_byte >> 4) : (lo_byte & 0x0F);
-                                const uint32_t hi = (slot_byte(s, bo + 128 + 32 * h + l) >> (2 * sg)) & 3u;
-                                const int q = static_cast<int>(lo | (hi << 4)) - 32;
-                                const float wv = __fmul_rn(dsc, static_cast<float>(q));
-                                const uint32_t e = eb + 128 * h + 32 * sg + l;
-#pragma unroll
-                                for (uint32_t b = 0; b < kSeqMaxBatch; ++b)
-                                    if (b < p.batch) sum[b] = __fadd_rn(sum[b], __fmul_rn(wv, __ldg(p.x + uint64_t(b) * p.k + e)));
-                            }
-                        }
-                    }
-                }
-            } else {  // f32, f16, bf16: one element per block
-                float wv;
-                if constexpr (kType == 0) {
-                    wv = __uint_as_float(s[bo >> 2]);
-                } else {
-                    const uint32_t h16 = slot_byte(s, bo) | (slot_byte(s, bo + 1) << 8);
-                    wv = kType == 1 ? f16_bits_to_f32(static_cast<uint16_t>(h16)) : __uint_as_float(h16 << 16);
-                }
-#pragma unroll
-                for (uint32_t b = 0; b < kSeqMaxBatch; ++b)
-                    if (b < p.batch) sum[b] = __fadd_rn(sum[b], __fmul_rn(wv, __ldg(p.x + uint64_t(b) * p.k + eb)));
+        if (lane < nr) p.y[uint64_t(b) * p.rows + row_base + lane] = sum;
+        return;
+    }
+
+    // ---------------------------------------------------------- producer warps
+    constexpr uint32_t kProducers = kSeqThreads - 32 * kBatch;
+    const uint32_t pt = threadIdx.x - 32 * kBatch;
+    const uint32_t raw_base = static_cast<uint32_t>(__cvta_generic_to_shared(raw));
+    const uint32_t dist = p.raw_stages - 2;  // chunks in flight ahead of the one being decoded
+    constexpr uint32_t kFullBytes = seq_chunk_bytes(kType);
+
+    // bytes of chunk c (the last one may be partial)
+    auto chunk_bytes = [&](uint32_t c) -> uint32_t {
+        const uint32_t elems = p.k - c * C < C ? p.k - c * C : C;
+        if constexpr (kType == 8) return elems / 32u * 34u;
+        else if constexpr (kType == 12 || kType == 13 || kType == 14) return kFullBytes;
+        else if constexpr (kType == 0) return elems * 4u;
+        else return elems * 2u;
+    };
+    // cp.async the aligned words covering chunk c of every row into raw stage
+    // c % raw_stages: thread u of the flat (row, word) space copies one word
+    constexpr uint32_t kSlotWords = kSlot / 4;
+    auto issue = [&](uint32_t c) {
+        if (c < n_chunks) {
+            const uint32_t bytes = chunk_bytes(c);
+            const uint32_t slot0 = raw_base + (c % p.raw_stages) * (kSeqRows * kSlot);
+            const uintptr_t chunk0 = reinterpret_cast<uintptr_t>(p.w) + row_base * p.row_bytes +
+                                     static_cast<uint64_t>(c) * kFullBytes;
+            for (uint32_t u = pt; u < nr * kSlotWords; u += kProducers) {
+                const uint32_t r = u / kSlotWords, j = u - r * kSlotWords;
+                const uintptr_t start = chunk0 + r * p.row_bytes;
+                const uintptr_t a0 = start & ~uintptr_t(3);
+                if (a0 + 4u * j < start + bytes) cp_async_4(slot0 + r * kSlot + 4u * j, reinterpret_cast<const void*>(a0 + 4u * j));
             }
         }
-    }
-    if (live) {
+        cp_async_commit();
+    };
+
+    for (uint32_t c = 0; c < dist; ++c) issue(c);
+    for (uint32_t c = 0; c < n_chunks; ++c) {
+        issue(c + dist);
+        cp_async_wait_dyn(dist);                                   // this thread's copies of chunk c landed
+        named_barrier_sync(kSeqBarProducers, kProducers);          // ... and every producer's
+        const uint32_t s = c % kSeqStages;
+        if (c >= kSeqStages) named_barrier_sync(kSeqBarEmpty + s, kSeqThreads);
+        const uint32_t e0 = c * C;
+        const uint32_t elems = p.k - e0 < C ? p.k - e0 : C;
+        const uint32_t groups = (elems + 3) / 4;
+        const uint8_t* slot0 = raw + (c % p.raw_stages) * (kSeqRows * kSlot);
+        for (uint32_t u = pt; u < nr * groups; u += kProducers) {
+            const uint32_t r = groups == C / 4 ? u / (C / 4) : u / groups;
+            const uint32_t g = u - r * groups;
+            const uintptr_t start = reinterpret_cast<uintptr_t>(p.w) + (row_base + r) * p.row_bytes +
+                                    static_cast<uint64_t>(c) * kFullBytes;
+            float wv[4];
+            decode4<kType, true>(slot0 + r * kSlot + (start & 3u), 4 * g, elems, wv);
+            const uint32_t e = e0 + 4 * g;
 #pragma unroll
-        for (uint32_t b = 0; b < kSeqMaxBatch; ++b)
-            if (b < p.batch) p.y[uint64_t(b) * p.rows + my_row] = sum[b];
+            for (uint32_t b = 0; b < kBatch; ++b) {
+                const float* xb = p.x + uint64_t(b) * p.k + e;
+                float4 xv;
+                if (e + 3 < p.k && (reinterpret_cast<uintptr_t>(xb) & 15u) == 0) {
+                    xv = __ldg(reinterpret_cast<const float4*>(xb));
+                } else {
+                    xv.x = __ldg(xb);
+                    xv.y = e + 1 < p.k ? __ldg(xb + 1) : 0.0f;
+                    xv.z = e + 2 < p.k ? __ldg(xb + 2) : 0.0f;
+                    xv.w = e + 3 < p.k ? __ldg(xb + 3) : 0.0f;
+                }
+                float4 o;
+                o.x = __fmul_rn(wv[0], xv.x);
+                o.y = __fmul_rn(wv[1], xv.y);
+                o.z = __fmul_rn(wv[2], xv.z);
+                o.w = __fmul_rn(wv[3], xv.w);
+                *reinterpret_cast<float4*>(prod + (s * kBatch + b) * kVecWords + r * kStride + 4 * g) = o;
+            }
+        }
+        named_barrier_arrive(kSeqBarFull + s, kSeqThreads);
     }
+    cp_async_wait<0>();
 }
 
 }  // namespace oracle_cuda

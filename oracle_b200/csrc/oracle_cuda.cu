@@ -17,6 +17,7 @@
 #include <tuple>
 #include <vector>
 
+#include "gemm_q4k.cuh"
 #include "layout.hpp"
 #include "matvec_seq.cuh"
 #include "matvec_q8k.cuh"
@@ -61,6 +62,9 @@ struct oracle_cuda_context {
     float* dev_x = nullptr;
     float* dev_y = nullptr;
     uint64_t dev_x_len = 0, dev_y_len = 0;
+    // prefill GEMM: bf16 copy of the activations
+    uint16_t* gemm_x = nullptr;
+    uint64_t gemm_x_len = 0;
 };
 
 namespace {
@@ -245,20 +249,39 @@ oracle_cuda_status launch_q8k(oracle_cuda_context* ctx, uint32_t type, const voi
     return launch_q8k_typed<14>(ctx, wb, rows, row_bytes, cp, stream);
 }
 
-template <uint32_t kType>
-oracle_cuda_status launch_seq_typed(oracle_cuda_context* ctx, const MatvecSeqParams& sp, cudaStream_t stream) {
-    const uint64_t per_cta = uint64_t(kSeqWarps) * 32;
-    const uint64_t grid = (sp.rows + per_cta - 1) / per_cta;
+template <uint32_t kType, uint32_t kBatch>
+oracle_cuda_status launch_seq_batch(oracle_cuda_context* ctx, MatvecSeqParams sp, cudaStream_t stream) {
+    const uint64_t grid = (sp.rows + kSeqRows - 1) / kSeqRows;
     if (grid > 0x7FFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "too many rows for one launch");
-    return launch(ctx, matvec_seq_kernel<kType>, dim3(static_cast<uint32_t>(grid)), dim3(kSeqWarps * 32), 0, stream,
-                  false, sp);
+    const uint64_t budget = ctx->smem_budget ? ctx->smem_budget : uint64_t(ctx->max_smem_optin);
+    const uint64_t prod = seq_prod_bytes(kType, kBatch);
+    const uint64_t stage = uint64_t(kSeqRows) * seq_raw_slot_bytes(kType);
+    uint64_t raw_stages = budget > prod ? (budget - prod) / stage : 0;
+    if (raw_stages > kSeqMaxRawStages) raw_stages = kSeqMaxRawStages;
+    if (raw_stages < 3) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "shared-memory budget too small for the f32-contract kernel");
+    sp.raw_stages = static_cast<uint32_t>(raw_stages);
+    return launch(ctx, matvec_seq_kernel<kType, kBatch>, dim3(static_cast<uint32_t>(grid)), dim3(kSeqThreads),
+                  static_cast<size_t>(prod + raw_stages * stage), stream, false, sp);
 }
 
-// Oracle's f32 contract, bit-exact: one lane per row, sequential f32 sum.
+template <uint32_t kType>
+oracle_cuda_status launch_seq_typed(oracle_cuda_context* ctx, const MatvecSeqParams& sp, uint32_t batch,
+                                    cudaStream_t stream) {
+    switch (batch) {
+        case 1: return launch_seq_batch<kType, 1>(ctx, sp, stream);
+        case 2: return launch_seq_batch<kType, 2>(ctx, sp, stream);
+        case 3: return launch_seq_batch<kType, 3>(ctx, sp, stream);
+        default: return launch_seq_batch<kType, 4>(ctx, sp, stream);
+    }
+}
+
+// Oracle's f32 contract, bit-exact: sequential f32 sum per row (matvec_seq.cuh).
+// Up to 4 activation vectors per launch (2 for the K-quants, whose chunks are longer).
 oracle_cuda_status launch_f32(oracle_cuda_context* ctx, uint32_t type, const void* w, uint64_t rows, uint64_t cols,
                               uint64_t row_bytes, const float* x, uint64_t batch, float* y, cudaStream_t stream) {
     if (cols > 0xFFFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "rows longer than 2^32 elements");
-    for (uint64_t b0 = 0; b0 < batch; b0 += kSeqMaxBatch) {
+    const uint64_t per_launch = seq_chunk_elems(type) > 128 ? 2 : kSeqMaxBatch;
+    for (uint64_t b0 = 0; b0 < batch; b0 += per_launch) {
         MatvecSeqParams sp{};
         sp.w = static_cast<const uint8_t*>(w);
         sp.x = x + b0 * cols;
@@ -266,16 +289,16 @@ oracle_cuda_status launch_f32(oracle_cuda_context* ctx, uint32_t type, const voi
         sp.rows = rows;
         sp.row_bytes = row_bytes;
         sp.k = static_cast<uint32_t>(cols);
-        sp.batch = static_cast<uint32_t>(batch - b0 < kSeqMaxBatch ? batch - b0 : kSeqMaxBatch);
+        const uint32_t nb = static_cast<uint32_t>(batch - b0 < per_launch ? batch - b0 : per_launch);
         oracle_cuda_status s;
         switch (type) {
-            case kTypeF32: s = launch_seq_typed<0>(ctx, sp, stream); break;
-            case kTypeF16: s = launch_seq_typed<1>(ctx, sp, stream); break;
-            case kTypeBF16: s = launch_seq_typed<30>(ctx, sp, stream); break;
-            case kTypeQ8_0: s = launch_seq_typed<8>(ctx, sp, stream); break;
-            case kTypeQ4_K: s = launch_seq_typed<12>(ctx, sp, stream); break;
-            case kTypeQ5_K: s = launch_seq_typed<13>(ctx, sp, stream); break;
-            case kTypeQ6_K: s = launch_seq_typed<14>(ctx, sp, stream); break;
+            case kTypeF32: s = launch_seq_typed<0>(ctx, sp, nb, stream); break;
+            case kTypeF16: s = launch_seq_typed<1>(ctx, sp, nb, stream); break;
+            case kTypeBF16: s = launch_seq_typed<30>(ctx, sp, nb, stream); break;
+            case kTypeQ8_0: s = launch_seq_typed<8>(ctx, sp, nb, stream); break;
+            case kTypeQ4_K: s = launch_seq_typed<12>(ctx, sp, nb, stream); break;
+            case kTypeQ5_K: s = launch_seq_typed<13>(ctx, sp, nb, stream); break;
+            case kTypeQ6_K: s = launch_seq_typed<14>(ctx, sp, nb, stream); break;
             default: return fail(ctx, check_decodable(type));
         }
         if (s != ORACLE_CUDA_OK) return s;
@@ -499,6 +522,7 @@ oracle_cuda_status oracle_cuda_destroy(oracle_cuda_context* ctx) {
     if (ctx->status) cudaFree(ctx->status);
     if (ctx->program_counters) cudaFree(ctx->program_counters);
     if (ctx->image_scratch) cudaFree(ctx->image_scratch);
+    if (ctx->gemm_x) cudaFree(ctx->gemm_x);
     delete ctx;
     return ORACLE_CUDA_OK;
 }
@@ -1060,4 +1084,108 @@ extern "C" oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cu
         matvec_program_kernel<kProgramWarps, 3><<<grid, block, smem, s>>>(pp);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(nullptr, e, "matvec_program_kernel launch");
     return ORACLE_CUDA_OK;
+}
+
+// ---------------------------------------------------------------- prefill dequant-GEMM
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// Columns per split of K: halve while the grid is at most half the SMs and
+// each split keeps at least 1024 columns of whole super-blocks.
+uint32_t gemm_k_per_split(uint64_t tiles, uint64_t cols, int sm_count) {
+    uint64_t splits = 1;
+    while (tiles * splits * 2 <= uint64_t(sm_count) && (cols / 256) % (splits * 2) == 0 &&
+           cols / (splits * 2) >= 1024)
+        splits *= 2;
+    return static_cast<uint32_t>(cols / splits);
+}
+
+}  // namespace
+
+extern "C" oracle_cuda_status oracle_cuda_prefill_gemm(oracle_cuda_context* ctx, uint32_t type, uint64_t rows,
+                                                       uint64_t cols, const void* w_dev, uint64_t w_nbytes,
+                                                       const float* x_dev, uint64_t m, float* y_dev,
+                                                       void* stream_handle) {
+    const cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (rows == 0 || cols == 0 || m == 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "prefill GEMM dimensions must be positive");
+    uint64_t row_bytes = 0;
+    if (Error e = row_byte_size(cols, type, &row_bytes)) return fail(ctx, e);
+    if (type != kTypeQ4_K) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "prefill GEMM supports Q4_K weights only");
+    uint64_t total = 0;
+    if (!checked_mul(rows, row_bytes, &total)) return fail(ctx, ORACLE_CUDA_OVERFLOW, "prefill GEMM weight size overflow");
+    if (w_nbytes != total) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "prefill GEMM weight byte size mismatch");
+    if (Error e = check_weight_pointer(type, w_dev)) return fail(ctx, e);
+    if (!x_dev || (reinterpret_cast<uintptr_t>(x_dev) & 15u))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "activation pointer must be non-null and 16-byte aligned");
+    if (!y_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "output pointer is null");
+    if (rows > 0x7FFFFFFFull || m > 0x7FFFFFFFull || cols > 0x7FFFFFFFull)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "prefill GEMM dimensions above 2^31");
+    const EncodeTiledFn encode = encode_tiled();
+    if (!encode) return fail(ctx, ORACLE_CUDA_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    oracle_cuda_status s = grow_device(ctx, ctx->gemm_x, ctx->gemm_x_len, m * cols);
+    if (s != ORACLE_CUDA_OK) return s;
+
+    // activations to bf16
+    const uint64_t n4 = m * cols / 4;
+    uint64_t blocks = (n4 + 255) / 256;
+    if (blocks > uint64_t(ctx->sm_count) * 16) blocks = uint64_t(ctx->sm_count) * 16;
+    s = launch(ctx, convert_bf16_kernel, dim3(static_cast<uint32_t>(blocks)), dim3(256), 0, stream, false, x_dev,
+               reinterpret_cast<uint32_t*>(ctx->gemm_x), n4);
+    if (s != ORACLE_CUDA_OK) return s;
+
+    CUtensorMap tx{}, tw{};
+    {
+        const cuuint64_t dims[2] = {cols, m};
+        const cuuint64_t strides[1] = {cols * 2};
+        const cuuint32_t box[2] = {kGemmTileK, kGemmTileM};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ctx->gemm_x, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return fail(ctx, ORACLE_CUDA_CUDA_ERROR, "tensor map for the activations rejected");
+    }
+    {
+        const cuuint64_t dims[2] = {row_bytes, rows};
+        const cuuint64_t strides[1] = {row_bytes};
+        const cuuint32_t box[2] = {kGemmSbBytes, kGemmTileN};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w_dev), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return fail(ctx, ORACLE_CUDA_CUDA_ERROR, "tensor map for the weights rejected");
+    }
+    const uint64_t tiles_m = (m + kGemmTileM - 1) / kGemmTileM, tiles_n = (rows + kGemmTileN - 1) / kGemmTileN;
+    if (tiles_n > 65535) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "too many weight rows for one prefill GEMM launch");
+    GemmParams gp{};
+    gp.y = y_dev;
+    gp.n = static_cast<uint32_t>(rows);
+    gp.m = static_cast<uint32_t>(m);
+    gp.k = static_cast<uint32_t>(cols);
+    gp.k_per_split = gemm_k_per_split(tiles_m * tiles_n, cols, ctx->sm_count);
+    gp.accumulate = gp.k_per_split < cols ? 1u : 0u;
+    gp.status = ctx->status;
+    if (gp.accumulate) ORACLE_CUDA_TRY(ctx, cudaMemsetAsync(y_dev, 0, m * rows * sizeof(float), stream), "cudaMemsetAsync");
+    return launch(ctx, gemm_q4k_bf16_kernel, dim3(static_cast<uint32_t>(tiles_m), static_cast<uint32_t>(tiles_n),
+                                                  static_cast<uint32_t>(cols / gp.k_per_split)),
+                  dim3(kGemmThreads), kGemmSmemBytes, stream, false, tx, tw, gp);
 }

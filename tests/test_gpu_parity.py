@@ -170,14 +170,17 @@ def test_f32_contract_against_reference_binary(ctx, ref):
         assert bits_equal(got, want), (qtype, rows, k)
 
 
-def test_f32_contract_batch(ctx, port):
-    rows, k, batch = 50, 1024, 6
-    w = synth.weight(ob.TYPE_Q8_0, rows, k, "gpu", "f32batch")
-    x = synth.activations(k, batch, "gpu", "f32batch_x")
-    want = port.storage_matvec_f32(ob.TYPE_Q8_0, rows, k, w, x)
+@pytest.mark.parametrize("qtype,rows,k,batch", [
+    (ob.TYPE_Q8_0, 50, 1024, 6), (ob.TYPE_Q8_0, 70, 4096, 2), (ob.TYPE_Q6_K, 33, 512, 3),
+    (ob.TYPE_Q4_K, 31, 1280, 4), (ob.TYPE_F16, 40, 301, 5), (ob.TYPE_F32, 3, 5, 4)])
+def test_f32_contract_batch(ctx, port, qtype, rows, k, batch):
+    w = synth.weight(qtype, rows, k, "gpu", f"f32batch_{qtype}_{k}")
+    x = synth.activations(k, batch, "gpu", f"f32batch_x_{k}_{batch}")
+    want = port.storage_matvec_f32(qtype, rows, k, w, x)
     y = torch.empty(batch * rows, dtype=torch.float32, device=DEV)
-    ctx.storage_matvec(ob.CONTRACT_F32, ob.TYPE_Q8_0, rows, k, to_dev(w), to_dev(x), y)
-    assert bits_equal(y.cpu().numpy(), want)
+    ctx.storage_matvec(ob.CONTRACT_F32, qtype, rows, k, to_dev(w), to_dev(x), y)
+    ctx.device_status()
+    assert bits_equal(y.cpu().numpy().reshape(batch, rows), want.reshape(batch, rows))
 
 
 def test_f32_contract_unaligned_rows(ctx, port):
