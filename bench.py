@@ -26,8 +26,11 @@ Oracle's f32 contract) print the same line for those configurations.
 --impl reference times the CPU implementation of the path on all host
 threads.  Oracle has no Q4_K decoder and no Q8_K integer dot (its storage
 decoder rejects type 12), so that arm runs the C restatement of GGML's
-algorithm (kind "port").  Multi-GPU (torchrun): every rank runs the full step
-on its own weights (weak scaling, no collective in the data path).
+algorithm (kind "port").  Multi-GPU (torchrun, one process per GPU): every
+matrix is row-sharded over the ranks and each step ends with one NCCL
+all-gather of the packed outputs (strong scaling: the whole job processes the
+same matrices at every N; oracle_b200/shard.py).
+--workload config4 times the prefill dequant-GEMM (TFLOP/s, tensor roofline).
 """
 from __future__ import annotations
 
@@ -73,7 +76,8 @@ class Workload:
         return {"workload": self.description, "shapes_k_to_n": [f"{k}->{n}" for _, k, n in self.ops], "batch": 1,
                 "bytes_per_step": self.step_bytes,
                 "l2": f"weights rotate through {self.pool_sets} sets ({self.pool_sets * wb / 1e6:.0f} MB > 3x L2)",
-                "parallelism": f"replicas{n_gpus}" if n_gpus > 1 else "single"}
+                "parallelism": (f"tp{n_gpus}: rows sharded over {n_gpus} GPUs, one NCCL all-gather of the "
+                                "outputs per step" if n_gpus > 1 else "single")}
 
 
 WORKLOADS = {
@@ -94,6 +98,32 @@ WORKLOADS = {
 }
 
 
+class GemmWorkload:
+    """prefill dequant-GEMMs Y = X . dequant(W)^T on the
+    tensor cores; a step is one GEMM per (K, N) shape at M tokens."""
+
+    name = "config4"
+    metric = "Q4_K prefill dequant-GEMM TFLOP/s"
+    unit = "TFLOP/s"
+    dtype = "bf16 x bf16 -> f32 (tcgen05)"
+    pool_sets = 3
+
+    def __init__(self, m: int = 512, shapes=((4096, 12288), (12288, 4096)), extra_m=(2048,)):
+        self.m, self.shapes, self.extra_m = m, list(shapes), list(extra_m)
+        self.step_flops = sum(2 * m * k * n for k, n in self.shapes)
+        self.h2d = sum(m * k * 4 for k, _ in self.shapes)
+        self.d2h = sum(m * n * 4 for _, n in self.shapes)
+        self.description = (f"config4: Q4_K prefill dequant-GEMM, M={m} tokens x (4096->12288, 12288->4096); W "
+                            "tiles dequantized to bf16 in shared memory, X rounded to bf16, f32 accumulation in TMEM")
+
+    def config(self, n_gpus: int) -> dict:
+        wb = sum(weight_bytes(TYPE_Q4_K, k, n) for k, n in self.shapes)
+        return {"workload": self.description, "m_tokens": self.m,
+                "shapes_k_to_n": [f"{k}->{n}" for k, n in self.shapes], "flops_per_step": self.step_flops,
+                "l2": f"weights rotate through {self.pool_sets} sets ({self.pool_sets * wb / 1e6:.0f} MB > L2)",
+                "parallelism": f"replicas{n_gpus}" if n_gpus > 1 else "single"}
+
+
 def load_peaks() -> tuple[float, str]:
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -101,6 +131,17 @@ def load_peaks() -> tuple[float, str]:
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def load_tensor_peak() -> tuple[float, str]:
+    """Dense bf16 TFLOP/s: the sustained figure (the timed loop runs for
+    seconds under the power cap), else the fallback."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]), "measured bf16_tflops_sustained"
+    except Exception:
+        return 1400.0, "fallback sustained"
 
 
 def load_traffic(wl: Workload):
@@ -294,8 +335,10 @@ def reference_arm(args, wl: Workload) -> None:
     threads = os.cpu_count() or 1
     ws, xs = host_weights(wl)
     dt, _ = time_cpu(wl, ws, xs, 0.05, threads)
-    # one step is a bounded sample sized for about 0.5 s on all threads
-    fraction = min(1.0, 0.05 * 0.5 / max(dt, 1e-4))
+    # one step is a bounded sample: about 0.5 s on all threads, less when
+    # many steps are asked for, so that the whole run stays near two minutes
+    per_step = min(0.5, 120.0 / max(1, args.steps + args.warmup))
+    fraction = min(1.0, max(1e-4, 0.05 * per_step / max(dt, 1e-4)))
     for _ in range(args.warmup):
         time_cpu(wl, ws, xs, fraction, threads)
     total_t, total_b = 0.0, 0
@@ -326,30 +369,51 @@ def gpu_arm(args, wl: Workload) -> None:
     torch.cuda.set_device(dev)
     ctx = ob.Context(local, flags=ob.FLAG_PDL if not args.no_pdl else 0)
     ws, xs = host_weights(wl)
+    # N > 1: every matrix is row-sharded (rank r owns an equal contiguous row
+    # range); each step ends with ONE NCCL all-gather of the packed per-rank
+    # outputs, after which every rank holds every output (oracle_b200/shard.py)
+    from oracle_b200.shard import PackPlan
+    plan = PackPlan([n for _, _, n in wl.ops], world, rank)
+    local_ops = [(t, k, sh.local_rows) for (t, k, _), sh in zip(wl.ops, plan.shards)]
+    ws_local = [np.ascontiguousarray(sh.weight_slice(w)) for w, sh in zip(ws, plan.shards)]
     # weight pool: set 0 is the seeded host weights; the others are rotations
     # by whole blocks (same distribution, distinct addresses), so no step finds
     # its weights in L2
     pool = []
     for s in range(wl.pool_sets):
         pool.append([torch.from_numpy(np.roll(w.reshape(-1), s * BLOCK[t][1])).to(dev)
-                     for w, (t, _, _) in zip(ws, wl.ops)])
+                     for w, (t, _, _) in zip(ws_local, wl.ops)])
     x_dev = [torch.from_numpy(x).to(dev) for x in xs]
-    y_dev = [torch.empty(n, dtype=torch.float32, device=dev) for _, _, n in wl.ops]
+    y_pack = torch.empty(plan.pack_len, dtype=torch.float32, device=dev)
+    y_dev = [y_pack[o:o + sh.local_rows] for o, sh in zip(plan.offsets, plan.shards)]
+    gathered = torch.empty(world * plan.pack_len, dtype=torch.float32, device=dev) if world > 1 else None
     stream = torch.cuda.Stream(dev)
+
+    def exchange():
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(gathered, y_pack)
 
     def step(s: int):
         ws_ = pool[s % wl.pool_sets]
         if wl.program:
             # one persistent launch runs all the (independent) matvecs of the step
-            ctx.matvec_program([(t, n, k, ws_[i], x_dev[i], y_dev[i], 0) for i, (t, k, n) in enumerate(wl.ops)],
+            ctx.matvec_program([(t, n, k, ws_[i], x_dev[i], y_dev[i], 0) for i, (t, k, n) in enumerate(local_ops)],
                                stream=stream)
+            exchange()
         else:
             step_separate(s)
 
     def step_separate(s: int):
         ws_ = pool[s % wl.pool_sets]
-        for i, (t, k, n) in enumerate(wl.ops):
+        for i, (t, k, n) in enumerate(local_ops):
             ctx.storage_matvec(wl.contract, t, n, k, ws_[i], x_dev[i], y_dev[i], stream=stream)
+        exchange()
+
+    def outputs() -> list:
+        if world > 1:
+            return plan.unpack(gathered.cpu().numpy())
+        return [y.cpu().numpy() for y in y_dev]
 
     # correctness gate on this box: set 0 of every op against the CPU checker
     with torch.cuda.stream(stream):
@@ -359,12 +423,13 @@ def gpu_arm(args, wl: Workload) -> None:
     import oracle
     port = oracle.port()
     wants = []
+    got = outputs()
     for i, (t, k, n) in enumerate(wl.ops):
         if wl.contract == CONTRACT_Q8K:
             wants.append(port.matvec_q8_k(t, n, k, ws[i], port.quantize_q8_k(xs[i]))[0])
         else:
             wants.append(port.storage_matvec_f32(t, n, k, ws[i], xs[i])[0])
-        if not np.array_equal(y_dev[i].cpu().numpy().view(np.uint32), wants[i].view(np.uint32)):
+        if not np.array_equal(got[i].view(np.uint32), wants[i].view(np.uint32)):
             raise SystemExit("GPU result differs from the CPU checker; refusing to report a number")
 
     # graph of one pass over the pool (pool_sets steps); K mod pool_sets more from a tail graph
@@ -409,13 +474,14 @@ def gpu_arm(args, wl: Workload) -> None:
     ms = max_over_ranks(start.elapsed_time(end), world)
     ctx.device_status()
     steps_timed = args.steps
-    value = world * steps_timed * wl.step_bytes / (ms / 1e3) / 1e9
-    # the timed region holds nothing but the step's kernels
-    achieved = wl.step_bytes / (ms / steps_timed * 1e-3) / 1e9
+    # whole-job bytes: the full matrices, whatever the rank count (strong scaling)
+    value = steps_timed * wl.step_bytes / (ms / 1e3) / 1e9
+    # the timed region holds nothing but the step's kernels (and, N > 1, the all-gather)
+    achieved = wl.step_bytes / world / (ms / steps_timed * 1e-3) / 1e9
     peak, peak_kind = load_peaks()
 
     extra = {}
-    if wl.program:
+    if wl.program and world == 1:
         # the same step as separate single-matvec launches
         gsep = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gsep, stream=stream):
@@ -455,15 +521,35 @@ def gpu_arm(args, wl: Workload) -> None:
             del g
         extra["per_shape_single_launch"] = per_op
 
-    # e2e through the host-pointer C ABI with pinned buffers
+    # e2e: N = 1 through the host-pointer C ABI (the drop-in call) with pinned
+    # buffers; N > 1 pinned x copied in on every rank, the sharded step with
+    # its all-gather, the whole output copied out, synchronised every step
     x_pin = [torch.from_numpy(x).pin_memory() for x in xs]
-    y_pin = [torch.empty(n, dtype=torch.float32).pin_memory() for _, _, n in wl.ops]
     x_np = [t.numpy() for t in x_pin]
-    y_np = [t.numpy() for t in y_pin]
+    if world == 1:
+        y_pin = [torch.empty(n, dtype=torch.float32).pin_memory() for _, _, n in wl.ops]
+        y_np = [t.numpy() for t in y_pin]
 
-    def e2e_step():
-        for i, (t, k, n) in enumerate(wl.ops):
-            ctx.host_storage_matvec(wl.contract, t, n, k, ws[i], x_np[i], y_np[i])
+        def e2e_step():
+            for i, (t, k, n) in enumerate(wl.ops):
+                ctx.host_storage_matvec(wl.contract, t, n, k, ws[i], x_np[i], y_np[i])
+
+        e2e_how = "oracle_cuda_host_storage_matvec per matvec, pinned host x/y, wall clock over synchronous calls, weights resident"
+        e2e_d2h = wl.d2h
+    else:
+        g_pin = torch.empty(world * plan.pack_len, dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                for i in range(len(wl.ops)):
+                    x_dev[i].copy_(x_pin[i], non_blocking=True)
+                step(0)
+                g_pin.copy_(gathered, non_blocking=True)
+            stream.synchronize()
+
+        e2e_how = ("pinned x copied in on every rank, row-sharded step + NCCL all-gather, every rank copies the "
+                   "whole output out, synchronised each step; wall clock, max over ranks")
+        e2e_d2h = world * plan.pack_len * 4
 
     for _ in range(3):
         e2e_step()
@@ -474,10 +560,11 @@ def gpu_arm(args, wl: Workload) -> None:
     for _ in range(e2e_steps):
         e2e_step()
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-    e2e_value = world * e2e_steps * wl.step_bytes / e2e_s / 1e9
+    e2e_value = e2e_steps * wl.step_bytes / e2e_s / 1e9
+    e2e_out = [y_np[i] for i in range(len(wl.ops))] if world == 1 else plan.unpack(g_pin.numpy())
     for i in range(len(wl.ops)):
-        if not np.array_equal(y_np[i].view(np.uint32), wants[i].view(np.uint32)):
-            raise SystemExit("host-path result differs from the CPU checker")
+        if not np.array_equal(e2e_out[i].view(np.uint32), wants[i].view(np.uint32)):
+            raise SystemExit("end-to-end result differs from the CPU checker")
 
     cpu = cpu_baseline_leg(wl) if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
@@ -486,16 +573,252 @@ def gpu_arm(args, wl: Workload) -> None:
                   "stream_rows_kernel<MatvecQ8KConsumer>")
         line = {"metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps_timed,
                 "warmup": args.warmup, "ms_per_step": ms / steps_timed, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+                "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype,
                 "data": f"synthetic (seeded; BASELINE {wl.name} distributions)", "config": wl.config(world),
                 "gpu_launches": launches_per_step * steps_timed,
-                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
-                        "how": "oracle_cuda_host_storage_matvec per matvec, pinned host x/y, wall clock over "
-                               "synchronous calls, weights resident"},
+                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": e2e_d2h,
+                        "how": e2e_how},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                              "traffic": load_traffic(wl), "kernel": kernel, **extra},
                 "cpu_baseline": cpu, "clocks": sampler.summary(), "pdl": not args.no_pdl}
+        print(json.dumps(line), flush=True)
+    del graph, tail
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- prefill GEMM (config 4)
+
+def gemm_host(wl: GemmWorkload, m: int):
+    from oracle_b200 import synth
+    ws = [synth.weight(TYPE_Q4_K, n, k, "config4", f"W_{k}_{n}") for k, n in wl.shapes]
+    xs = [synth.activations(k, m, "config4", f"X_{k}_{m}") for k, _ in wl.shapes]
+    return ws, xs
+
+
+def gemm_cpu(wl: GemmWorkload, ws, xs, samples: int, threads: int, seed: int) -> tuple[float, float]:
+    """`samples` output elements of every shape by the C restatement (f32
+    operands, f64 sums) on `threads` host threads; returns (seconds, flops)."""
+    import oracle
+    port = oracle.port()
+    rng = np.random.default_rng(seed)
+    jobs = []
+    for (k, n), w, x in zip(wl.shapes, ws, xs):
+        mi = rng.integers(0, x.shape[0], samples)
+        ni = np.sort(rng.integers(0, n, samples))
+        jobs.append((k, n, w, x, mi, ni))
+    t0 = time.perf_counter()
+    for k, n, w, x, mi, ni in jobs:
+        parts = np.array_split(np.arange(samples), threads)
+        th = [threading.Thread(target=port.gemm_sampled, args=(TYPE_Q4_K, n, k, w, x, mi[p], ni[p], 0))
+              for p in parts if len(p)]
+        for h in th:
+            h.start()
+        for h in th:
+            h.join()
+    return time.perf_counter() - t0, float(sum(2 * k * samples for k, _ in wl.shapes))
+
+
+def gemm_cpu_baseline(wl: GemmWorkload, ws, xs, target_seconds: float = 10.0) -> dict:
+    dt, fl = gemm_cpu(wl, ws, xs, 64, 1, 1)
+    samples = max(64, int(64 * (target_seconds / 3) / max(dt, 1e-4)))
+    total_t, total_f, reps = 0.0, 0.0, 0
+    while total_t < target_seconds and reps < 100:
+        dt, fl = gemm_cpu(wl, ws, xs, samples, 1, 2 + reps)
+        total_t += dt
+        total_f += fl
+        reps += 1
+    return {"value": total_f / total_t / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+            "sample": f"{reps} x {samples} sampled output elements of each config4 shape (M={wl.m}), single "
+                      "thread: the C restatement's f32-operand dot per element (oracle/quant_oracle.c "
+                      "oq_gemm_sampled); Oracle has no prefill GEMM (it ingests prompts one matvec at a time)"}
+
+
+def gemm_reference_arm(args, wl: GemmWorkload) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 and rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    ws, xs = gemm_host(wl, wl.m)
+    dt, _ = gemm_cpu(wl, ws, xs, 256 * threads, threads, 1)
+    per_step = min(0.5, 120.0 / max(1, args.steps + args.warmup))
+    samples = max(threads, int(256 * threads * per_step / max(dt, 1e-4)))
+    for i in range(args.warmup):
+        gemm_cpu(wl, ws, xs, samples, threads, 100 + i)
+    total_t, total_f = 0.0, 0.0
+    for i in range(args.steps):
+        dt, fl = gemm_cpu(wl, ws, xs, samples, threads, 1000 + i)
+        total_t += dt
+        total_f += fl
+    value = total_f / total_t / 1e12
+    line = {"impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_t / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (CPU)",
+            "data": "synthetic", "config": wl.config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
+                             "sample": f"{samples} sampled output elements per shape per step on {threads} threads"},
+            "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def gemm_arm(args, wl: GemmWorkload) -> None:
+    import torch
+
+    import oracle
+    import oracle_b200 as ob
+
+    rank, local, world = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    ctx = ob.Context(local)
+    port = oracle.port()
+    ws, xs = gemm_host(wl, wl.m)
+    pool = [[torch.from_numpy(np.roll(w.reshape(-1), s * 144)).to(dev) for w in ws] for s in range(wl.pool_sets)]
+    x_dev = [torch.from_numpy(x.reshape(-1)).to(dev) for x in xs]
+    y_dev = [torch.empty(wl.m * n, dtype=torch.float32, device=dev) for _, n in wl.shapes]
+    stream = torch.cuda.Stream(dev)
+
+    def step(s: int):
+        for i, (k, n) in enumerate(wl.shapes):
+            ctx.prefill_gemm(TYPE_Q4_K, n, k, pool[s % wl.pool_sets][i], x_dev[i], wl.m, y_dev[i], stream=stream)
+
+    def gate(ys, ws_, xs_, m):
+        rng = np.random.default_rng(7)
+        for (k, n), y, w, x in zip(wl.shapes, ys, ws_, xs_):
+            mi, ni = rng.integers(0, m, 400), rng.integers(0, n, 400)
+            ref = port.gemm_sampled(TYPE_Q4_K, n, k, w, x, mi, ni, 1)
+            scale = port.gemm_sampled(TYPE_Q4_K, n, k, w, x, mi, ni, 2)
+            got = y.cpu().numpy().reshape(m, n)[mi, ni]
+            if not np.all(np.abs(got - ref) <= 1e-4 * scale + 1e-6):
+                raise SystemExit("GPU GEMM differs from the CPU checker; refusing to report a number")
+
+    with torch.cuda.stream(stream):
+        step(0)
+    stream.synchronize()
+    ctx.device_status()
+    gate(y_dev, ws, xs, wl.m)
+
+    launches0 = ctx.launch_count()
+    with torch.cuda.stream(stream):
+        for s in range(wl.pool_sets):
+            step(s)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for s in range(wl.pool_sets):
+            step(s)
+    launches_per_step = (ctx.launch_count() - launches0) // (2 * wl.pool_sets)
+    rem = args.steps % wl.pool_sets
+    tail = None
+    if rem:
+        tail = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(tail, stream=stream):
+            for s in range(rem):
+                step(s)
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup // wl.pool_sets)):
+            graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    with sampler, torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps // wl.pool_sets):
+            graph.replay()
+        if tail is not None:
+            tail.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    ctx.device_status()
+    value = world * args.steps * wl.step_flops / (ms / 1e3) / 1e12
+    achieved = wl.step_flops / (ms / args.steps * 1e-3) / 1e12
+    peak, peak_kind = load_tensor_peak()
+
+    # each shape alone, and at the larger token counts
+    per_shape = []
+    for m in [wl.m] + wl.extra_m:
+        ws_m, xs_m = (ws, xs) if m == wl.m else gemm_host(wl, m)
+        xm = [torch.from_numpy(x.reshape(-1)).to(dev) for x in xs_m]
+        ym = [torch.empty(m * n, dtype=torch.float32, device=dev) for _, n in wl.shapes]
+        for i, (k, n) in enumerate(wl.shapes):
+            with torch.cuda.stream(stream):
+                ctx.prefill_gemm(TYPE_Q4_K, n, k, pool[0][i], xm[i], m, ym[i], stream=stream)
+            stream.synchronize()
+            if m != wl.m:
+                rng = np.random.default_rng(11)
+                mi, ni = rng.integers(0, m, 200), rng.integers(0, n, 200)
+                ref = port.gemm_sampled(TYPE_Q4_K, n, k, ws_m[i], xs_m[i], mi, ni, 1)
+                scale = port.gemm_sampled(TYPE_Q4_K, n, k, ws_m[i], xs_m[i], mi, ni, 2)
+                got = ym[i].cpu().numpy().reshape(m, n)[mi, ni]
+                if not np.all(np.abs(got - ref) <= 1e-4 * scale + 1e-6):
+                    raise SystemExit(f"GPU GEMM differs from the CPU checker at M={m}")
+            reps = 3 * wl.pool_sets
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for r in range(reps):
+                    ctx.prefill_gemm(TYPE_Q4_K, n, k, pool[r % wl.pool_sets][i], xm[i], m, ym[i], stream=stream)
+            with torch.cuda.stream(stream):
+                g.replay()
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(10):
+                    g.replay()
+                b.record(stream)
+                torch.cuda.synchronize()
+            us = a.elapsed_time(b) * 1e3 / (10 * reps)
+            per_shape.append({"m": m, "shape": f"{k}->{n}", "us": us,
+                              "tflops": 2 * m * k * n / (us * 1e-6) / 1e12})
+            del g
+        del xm, ym
+
+    # e2e: pinned host X in, GEMMs, host Y out, synchronous per step
+    x_pin = [torch.from_numpy(x.reshape(-1)).pin_memory() for x in xs]
+    y_pin = [torch.empty(wl.m * n, dtype=torch.float32).pin_memory() for _, n in wl.shapes]
+
+    def e2e_step():
+        for i, (k, n) in enumerate(wl.shapes):
+            x_dev[i].copy_(x_pin[i], non_blocking=True)
+            ctx.prefill_gemm(TYPE_Q4_K, n, k, pool[0][i], x_dev[i], wl.m, y_dev[i],
+                             stream=torch.cuda.current_stream())
+            y_pin[i].copy_(y_dev[i], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    e2e_steps = 50
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e_value = world * e2e_steps * wl.step_flops / e2e_s / 1e12
+    gate([y.cuda() for y in y_pin], ws, xs, wl.m)
+
+    cpu = gemm_cpu_baseline(wl, ws, xs) if (rank == 0 and world == 1 and not args.no_cpu) else None
+    if rank == 0:
+        line = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+                "data": "synthetic (seeded; BASELINE config4 distributions)", "config": wl.config(world),
+                "gpu_launches": launches_per_step * args.steps,
+                "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d,
+                        "d2h_bytes_per_step": wl.d2h,
+                        "how": "pinned host X copied in, oracle_cuda_prefill_gemm, Y copied out, synchronised "
+                               "every step, weights resident"},
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                             "frac": achieved / peak, "peak_source": peak_kind, "traffic": load_traffic(wl),
+                             "kernel": "gemm_q4k_bf16_kernel (+ convert_bf16_kernel, 1 per GEMM)",
+                             "per_shape": per_shape},
+                "cpu_baseline": cpu, "clocks": sampler.summary()}
         print(json.dumps(line), flush=True)
     del graph, tail
     ctx.close()
@@ -510,12 +833,16 @@ def main():
     ap.add_argument("--steps", type=int, default=12000)
     ap.add_argument("--warmup", type=int, default=600)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["config4"], default="config2")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "config4":
+        wl = GemmWorkload()
+        (gemm_reference_arm if args.impl == "reference" else gemm_arm)(args, wl)
+        return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         reference_arm(args, wl)

@@ -20,7 +20,9 @@
 //   warp 2  lane 0: raw Q4_K loads: 2-D TMA boxes of 128 rows x 144 bytes (one
 //                   super-block column) into a ring of raw stages
 //   warps 4-11:     dequantize raw super-blocks into the A ring (K-major,
-//                   128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7)),
+//                   128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7));
+//                   two groups of 4 warps take alternate stages, a thread
+//                   per weight row,
 //                   then, after the last MMA, read the accumulator out of TMEM
 //                   (tcgen05.ld 32x32b) and store Y (coalesced along n)
 // Every mbarrier wait is bounded (common.cuh); a timeout sets a CTA abort flag,
@@ -116,11 +118,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return r;
 }
 
-// q (0..15) to f32 exactly: the nibble placed under the exponent of 2^23.
-__device__ __forceinline__ float nib_to_f32(uint32_t nib) {
-    return __fsub_rn(__uint_as_float(0x4B000000u | nib), 8388608.0f);
-}
-
 // 6-bit scale and min of sub-block j from the three little-endian words
 // holding the 12 packed bytes (storage_decode.cpp:44-61).
 __device__ __forceinline__ void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t j, uint32_t& sc,
@@ -135,16 +132,34 @@ __device__ __forceinline__ void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t
     }
 }
 
-// 8 consecutive elements (one nibble half of 8 bytes) -> 4 packed bf16 pairs.
-__device__ __forceinline__ uint4 dequant8(uint32_t w0, uint32_t w1, uint32_t shift, float dsc, float dm) {
-    float f[8];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        f[t] = __fsub_rn(__fmul_rn(dsc, nib_to_f32((w0 >> (8 * t + shift)) & 0x0Fu)), dm);
-        f[4 + t] = __fsub_rn(__fmul_rn(dsc, nib_to_f32((w1 >> (8 * t + shift)) & 0x0Fu)), dm);
-    }
-    return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
-                      pack_bf16x2(f[6], f[7]));
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+// Four nibbles (one per byte of `nib4`, values 0..15) to bf16 pairs of the
+// exact f32 decode (dsc * q) - dm, each operation rounded to nearest (packed
+// f32x2 arithmetic: two IEEE operations per instruction), then rounded once to
+// bf16.  q becomes a float exactly: the byte placed under the exponent of 2^23
+// and 2^23 subtracted.
+__device__ __forceinline__ uint2 dequant4(uint32_t nib4, uint64_t dsc2, uint64_t dm2) {
+    const uint64_t two23 = 0x4B0000004B000000ull;
+    const uint64_t m01 = f32x2(__uint_as_float(__byte_perm(nib4, 0x4B000000u, 0x7440u)),
+                               __uint_as_float(__byte_perm(nib4, 0x4B000000u, 0x7441u)));
+    const uint64_t m23 = f32x2(__uint_as_float(__byte_perm(nib4, 0x4B000000u, 0x7442u)),
+                               __uint_as_float(__byte_perm(nib4, 0x4B000000u, 0x7443u)));
+    uint64_t a, b;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(a) : "l"(m01), "l"(two23));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(b) : "l"(m23), "l"(two23));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(a) : "l"(a), "l"(dsc2));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(b) : "l"(b), "l"(dsc2));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(a) : "l"(a), "l"(dm2));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(b) : "l"(b), "l"(dm2));
+    uint2 r;
+    asm("{\n\t.reg .f32 lo, hi;\n\tmov.b64 {lo, hi}, %1;\n\tcvt.rn.bf16x2.f32 %0, hi, lo;\n\t}" : "=r"(r.x) : "l"(a));
+    asm("{\n\t.reg .f32 lo, hi;\n\tmov.b64 {lo, hi}, %1;\n\tcvt.rn.bf16x2.f32 %0, hi, lo;\n\t}" : "=r"(r.y) : "l"(b));
+    return r;
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -173,7 +188,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < kGemmStages; ++s) {
-            mbar_init(&full_a[s], kGemmDequantWarps);
+            mbar_init(&full_a[s], kGemmDequantWarps / 2);  // one group of 4 warps per stage
             mbar_init(&full_b[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -256,46 +271,56 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp >= 4) {
         // -------------------------------------------------------------- dequantize
-        const uint32_t t = threadIdx.x - 128;
+        // Two groups of 4 warps take alternate K stages; thread = weight row,
+        // the whole 64-element stage of its row (32 bytes of nibbles, two
+        // sub-blocks).  A quarter-warp stores 8 consecutive rows' same logical
+        // chunk, which the swizzle spreads over all banks.
+        const uint32_t grp = (warp - 4) >> 2, row = (threadIdx.x - 128) & 127;
         bool ok = true;
-        for (uint32_t kc = 0; kc < nk; ++kc) {
+        for (uint32_t kc = grp; kc < nk; kc += 2) {
             if (*abort_flag) {
                 ok = false;
                 break;
             }
             const uint32_t s = kc % kGemmStages, j = kc / 4, g = kc % 4, r = j % kGemmRawStages;
-            if (g == 0 && !mbar_wait(&raw_full[r], (j / kGemmRawStages) & 1, p.status, 47)) ok = false;
+            if (g == grp && !mbar_wait(&raw_full[r], (j / kGemmRawStages) & 1, p.status, 47)) ok = false;
             if (ok && kc >= kGemmStages && !mbar_wait(&empty[s], ((kc / kGemmStages) - 1) & 1, p.status, 48))
                 ok = false;
             if (!ok) {
                 *abort_flag = 1;
                 break;
             }
-            const uint8_t* raw = smem + kGemmOffRaw + r * kGemmRawBytes;
-            uint8_t* a = smem + s * kGemmABytes;
+            const uint8_t* rp = smem + kGemmOffRaw + r * kGemmRawBytes + row * kGemmSbBytes;
+            const uint4 h = *reinterpret_cast<const uint4*>(rp);
+            const uint4 qa = *reinterpret_cast<const uint4*>(rp + 16 + 32 * g);
+            const uint4 qb = *reinterpret_cast<const uint4*>(rp + 32 + 32 * g);
+            const float d = f16_bits_to_f32(static_cast<uint16_t>(h.x & 0xFFFFu));
+            const float dmin = f16_bits_to_f32(static_cast<uint16_t>(h.x >> 16));
+            uint32_t sc_lo, mn_lo, sc_hi, mn_hi;
+            q4k_scale_min(h.y, h.z, h.w, 2 * g, sc_lo, mn_lo);
+            q4k_scale_min(h.y, h.z, h.w, 2 * g + 1, sc_hi, mn_hi);
+            const float dsl = __fmul_rn(d, static_cast<float>(sc_lo)), dml = __fmul_rn(dmin, static_cast<float>(mn_lo));
+            const float dsh = __fmul_rn(d, static_cast<float>(sc_hi)), dmh = __fmul_rn(dmin, static_cast<float>(mn_hi));
+            const uint64_t dsl2 = f32x2(dsl, dsl), dml2 = f32x2(dml, dml);
+            const uint64_t dsh2 = f32x2(dsh, dsh), dmh2 = f32x2(dmh, dmh);
+            const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+            uint8_t* arow = smem + s * kGemmABytes + row * 128;
 #pragma unroll
-            for (uint32_t i = 0; i < 2; ++i) {
-                const uint32_t u = t + 256 * i, row = u >> 2, o = u & 3;
-                const uint8_t* rp = raw + row * kGemmSbBytes;
-                const uint4 h = *reinterpret_cast<const uint4*>(rp);
-                const float d = f16_bits_to_f32(static_cast<uint16_t>(h.x & 0xFFFFu));
-                const float dmin = f16_bits_to_f32(static_cast<uint16_t>(h.x >> 16));
-                uint32_t sc_lo, mn_lo, sc_hi, mn_hi;
-                q4k_scale_min(h.y, h.z, h.w, 2 * g, sc_lo, mn_lo);
-                q4k_scale_min(h.y, h.z, h.w, 2 * g + 1, sc_hi, mn_hi);
-                const uint2 q = *reinterpret_cast<const uint2*>(rp + 16 + 32 * g + 8 * o);
-                const uint4 lo = dequant8(q.x, q.y, 0, __fmul_rn(d, static_cast<float>(sc_lo)),
-                                          __fmul_rn(dmin, static_cast<float>(mn_lo)));
-                const uint4 hi = dequant8(q.x, q.y, 4, __fmul_rn(d, static_cast<float>(sc_hi)),
-                                          __fmul_rn(dmin, static_cast<float>(mn_hi)));
-                *reinterpret_cast<uint4*>(a + row * 128 + ((o ^ (row & 7)) * 16)) = lo;
-                *reinterpret_cast<uint4*>(a + row * 128 + (((4 + o) ^ (row & 7)) * 16)) = hi;
+            for (uint32_t c = 0; c < 4; ++c) {
+                // chunk c: elements 8c..8c+7 = low nibbles of bytes 8c..8c+7;
+                // chunk 4+c: elements 32+8c.. = their high nibbles
+                const uint2 l0 = dequant4(qw[2 * c] & 0x0F0F0F0Fu, dsl2, dml2);
+                const uint2 l1 = dequant4(qw[2 * c + 1] & 0x0F0F0F0Fu, dsl2, dml2);
+                const uint2 h0 = dequant4((qw[2 * c] >> 4) & 0x0F0F0F0Fu, dsh2, dmh2);
+                const uint2 h1 = dequant4((qw[2 * c + 1] >> 4) & 0x0F0F0F0Fu, dsh2, dmh2);
+                *reinterpret_cast<uint4*>(arow + ((c ^ (row & 7)) * 16)) = make_uint4(l0.x, l0.y, l1.x, l1.y);
+                *reinterpret_cast<uint4*>(arow + (((4 + c) ^ (row & 7)) * 16)) = make_uint4(h0.x, h0.y, h1.x, h1.y);
             }
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&full_a[s]);
-                if (g == 3) mbar_arrive(&raw_empty[r]);
+                if (g == grp + 2) mbar_arrive(&raw_empty[r]);
             }
         }
         // ------------------------------------------------------------------ epilogue

@@ -163,16 +163,85 @@ __device__ __forceinline__ void fetch_lane_x(const ActImage& img, uint32_t i, in
     xd = img.d[i];
 }
 
-// kXReg: rows of at most 16 super-blocks (one pass); the lane's activation
-// data is fetched once into registers and reused for every row.  Otherwise
-// every pass re-reads it from the shared-memory image (conflict-free).
+// One row's dot product in the canonical order; the result is valid on lane 0.
+// kXReg: rows of at most 16 super-blocks (one pass) with the lane's activation
+// slice (xw, xbs, xd) already in registers; otherwise every pass re-reads it
+// from the shared-memory image (conflict-free).
+template <uint32_t kType, bool kXReg>
+__device__ __forceinline__ float q8k_row_dot(uint32_t nb, const ActImage& img, const uint8_t* rowp,
+                                             const uint32_t (&xw)[32], const int (&xbs)[8], float xd, int lane) {
+    const int j = lane >> 1, part = lane & 1;
+    constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
+    const uint32_t passes = kXReg ? 1u : (nb + 15u) / 16u;
+    float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 1
+    for (uint32_t k = 0; k < passes; ++k) {
+        const uint32_t i = 16u * k + j;
+        const bool active = i < nb;
+        int isum = 0, msum = 0;
+        float dw = 0.0f, dmw = 0.0f, dx = 0.0f;
+        if (active) {
+            const uint8_t* sb = rowp + size_t(i) * kBlockBytes;
+            if constexpr (kXReg) {
+                dx = xd;
+                if (kType == 12)
+                    q4k_half_sums(sb, part, xw, xbs, isum, msum, dw, dmw);
+                else
+                    q6k_half_sums(sb, part, xw, xbs, isum, dw);
+            } else {
+                uint32_t w[32];
+                int bs[8];
+                fetch_lane_x<kType>(img, i, part, w, bs, dx);
+                if (kType == 12)
+                    q4k_half_sums(sb, part, w, bs, isum, msum, dw, dmw);
+                else
+                    q6k_half_sums(sb, part, w, bs, isum, dw);
+            }
+        }
+        isum += __shfl_xor_sync(0xFFFFFFFFu, isum, 1);
+        if (kType == 12) msum += __shfl_xor_sync(0xFFFFFFFFu, msum, 1);
+        if (active) {
+            const float dd = __fmul_rn(dw, dx);
+            float pi = __fmul_rn(dd, __int2float_rn(isum));
+            if (kType == 12) {
+                const float dm = __fmul_rn(dmw, dx);
+                pi = __fsub_rn(pi, __fmul_rn(dm, __int2float_rn(msum)));
+            }
+            if (k & 1)
+                acc1 = __fadd_rn(acc1, pi);
+            else
+                acc0 = __fadd_rn(acc0, pi);
+        }
+    }
+    float v = __fadd_rn(acc0, acc1);
+#pragma unroll
+    for (int off = 16; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+    return v;
+}
+
+// The lane's activation slice for register-resident rows (<= 16 super-blocks).
+template <uint32_t kType>
+__device__ __forceinline__ void load_lane_x(const ActImage& img, uint32_t nb, int lane, uint32_t (&xw)[32],
+                                            int (&xbs)[8], float& xd) {
+    const uint32_t i = lane >> 1;
+    if (i < nb) {
+        fetch_lane_x<kType>(img, i, lane & 1, xw, xbs, xd);
+    } else {
+#pragma unroll
+        for (int v = 0; v < 32; ++v) xw[v] = 0u;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) xbs[t] = 0;
+        xd = 0.0f;
+    }
+}
+
 template <uint32_t kType, bool kXReg, int kWarps_>
 struct MatvecQ8KConsumer {
     static constexpr int kWarps = kWarps_;
     using Params = MatvecQ8KParams;
 
-    uint32_t xw[kXReg ? 32 : 1];
-    int xbs[kXReg ? 8 : 1];
+    uint32_t xw[32];
+    int xbs[8];
     float xd = 0.0f;
 
     __device__ __forceinline__ void prologue(const Params& p, uint8_t* act, int warp, int lane) {
@@ -184,68 +253,12 @@ struct MatvecQ8KConsumer {
     }
 
     __device__ __forceinline__ void load(const Params& p, uint8_t* act, int, int lane) {
-        if constexpr (kXReg) {
-            const uint32_t i = lane >> 1;
-            if (i < p.nb) {
-                fetch_lane_x<kType>(q8k_image(act, p.nb), i, lane & 1, xw, xbs, xd);
-            } else {
-#pragma unroll
-                for (int v = 0; v < 32; ++v) xw[v] = 0u;
-#pragma unroll
-                for (int t = 0; t < 8; ++t) xbs[t] = 0;
-            }
-        }
+        if constexpr (kXReg) load_lane_x<kType>(q8k_image(act, p.nb), p.nb, lane, xw, xbs, xd);
     }
 
     __device__ __forceinline__ void row(const Params& p, uint8_t* act, const uint8_t* rowp, uint64_t r,
                                         int lane) {
-        const int j = lane >> 1, part = lane & 1;
-        constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
-        const uint32_t passes = kXReg ? 1u : (p.nb + 15u) / 16u;
-        const ActImage img = q8k_image(act, p.nb);
-        float acc0 = 0.0f, acc1 = 0.0f;
-#pragma unroll 1
-        for (uint32_t k = 0; k < passes; ++k) {
-            const uint32_t i = 16u * k + j;
-            const bool active = i < p.nb;
-            int isum = 0, msum = 0;
-            float dw = 0.0f, dmw = 0.0f, dx = 0.0f;
-            if (active) {
-                const uint8_t* sb = rowp + size_t(i) * kBlockBytes;
-                if constexpr (kXReg) {
-                    dx = xd;
-                    if (kType == 12)
-                        q4k_half_sums(sb, part, xw, xbs, isum, msum, dw, dmw);
-                    else
-                        q6k_half_sums(sb, part, xw, xbs, isum, dw);
-                } else {
-                    uint32_t w[32];
-                    int bs[8];
-                    fetch_lane_x<kType>(img, i, part, w, bs, dx);
-                    if (kType == 12)
-                        q4k_half_sums(sb, part, w, bs, isum, msum, dw, dmw);
-                    else
-                        q6k_half_sums(sb, part, w, bs, isum, dw);
-                }
-            }
-            isum += __shfl_xor_sync(0xFFFFFFFFu, isum, 1);
-            if (kType == 12) msum += __shfl_xor_sync(0xFFFFFFFFu, msum, 1);
-            if (active) {
-                const float dd = __fmul_rn(dw, dx);
-                float pi = __fmul_rn(dd, __int2float_rn(isum));
-                if (kType == 12) {
-                    const float dm = __fmul_rn(dmw, dx);
-                    pi = __fsub_rn(pi, __fmul_rn(dm, __int2float_rn(msum)));
-                }
-                if (k & 1)
-                    acc1 = __fadd_rn(acc1, pi);
-                else
-                    acc0 = __fadd_rn(acc0, pi);
-            }
-        }
-        float v = __fadd_rn(acc0, acc1);
-#pragma unroll
-        for (int off = 16; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+        const float v = q8k_row_dot<kType, kXReg>(p.nb, q8k_image(act, p.nb), rowp, xw, xbs, xd, lane);
         if (lane == 0) p.y[r] = v;
     }
 };

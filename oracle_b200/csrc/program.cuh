@@ -80,79 +80,56 @@ __device__ __forceinline__ bool wait_counter(const unsigned int* counter, unsign
     return true;
 }
 
-// Consumer for one op of a program: Q4_K or Q6_K chosen at run time; rows of
-// at most 16 super-blocks keep the lane's activation slice in registers.
-template <int kWarps>
-struct ProgramConsumer {
+// Consumer walk over one op's stages with the row code specialised at compile
+// time (weight type; activation slice in registers or re-read per pass).
+// Every warp walks every stage (also those holding none of its rows) and
+// arrives on its `empty` barrier, so no warp ever waits two phases ahead.
+template <int NCW, uint32_t kType, bool kXReg>
+__device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* act, uint8_t* stage0,
+                                                uint32_t stage_bytes, uint32_t S, uint64_t* full, uint64_t* empty,
+                                                uint32_t& s, uint32_t& phase, bool& failed, DeviceStatus* status,
+                                                int warp, int lane) {
+    const ActImage img = q8k_image(act + op.act_offset, op.nb);
     uint32_t xw[32];
     int xbs[8];
     float xd = 0.0f;
-
-    __device__ __forceinline__ void prologue(const ProgramOp& op, uint8_t* act, int warp, int lane) {
-        quantize_to_image(op.x, op.nb, q8k_image(act + op.act_offset, op.nb), warp, kWarps, lane);
-    }
-
-    __device__ __forceinline__ void load(const ProgramOp& op, uint8_t* act, int lane) {
-        const uint32_t i = lane >> 1;
-        if (op.nb <= 16 && i < op.nb) {
-            if (op.type == 12)
-                fetch_lane_x<12>(q8k_image(act + op.act_offset, op.nb), i, lane & 1, xw, xbs, xd);
-            else
-                fetch_lane_x<14>(q8k_image(act + op.act_offset, op.nb), i, lane & 1, xw, xbs, xd);
+    if (kXReg && !failed) load_lane_x<kType>(img, op.nb, lane, xw, xbs, xd);
+    const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
+    const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
+    const uint32_t nrows = static_cast<uint32_t>(r1 - r0);
+    const uint32_t R = op.rows_per_stage;
+    const uint32_t T = (nrows + R - 1) / R;
+    const uint32_t rb = static_cast<uint32_t>(op.row_bytes);
+    const uint32_t wlo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w));
+    const uint32_t row0 = static_cast<uint32_t>(r0);
+    float* const y = op.y + r0;
+    uint32_t owner_base = 0;  // (t * R) % NCW
+    for (uint32_t t = 0; t < T; ++t) {
+        if (!failed) {
+            const bool ok = mbar_wait(&full[s], phase, status, 14);
+            failed = !__all_sync(0xFFFFFFFFu, ok);
         }
-    }
-
-    template <uint32_t kType>
-    __device__ __forceinline__ void row_typed(const ProgramOp& op, uint8_t* act, const uint8_t* rowp, uint64_t r,
-                                              int lane) {
-        const int j = lane >> 1, part = lane & 1;
-        constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
-        const bool xreg = op.nb <= 16;
-        const uint32_t passes = xreg ? 1u : (op.nb + 15u) / 16u;
-        const ActImage img = q8k_image(act + op.act_offset, op.nb);
-        float acc0 = 0.0f, acc1 = 0.0f;
-#pragma unroll 1
-        for (uint32_t k = 0; k < passes; ++k) {
-            const uint32_t i = 16u * k + j;
-            const bool active = i < op.nb;
-            int isum = 0, msum = 0;
-            float dw = 0.0f, dmw = 0.0f, dx = 0.0f;
-            if (active) {
-                const uint8_t* sb = rowp + size_t(i) * kBlockBytes;
-                if (xreg) {
-                    dx = xd;
-                    if (kType == 12)
-                        q4k_half_sums(sb, part, xw, xbs, isum, msum, dw, dmw);
-                    else
-                        q6k_half_sums(sb, part, xw, xbs, isum, dw);
-                } else {
-                    uint32_t w[32];
-                    int bs[8];
-                    fetch_lane_x<kType>(img, i, part, w, bs, dx);
-                    if (kType == 12)
-                        q4k_half_sums(sb, part, w, bs, isum, msum, dw, dmw);
-                    else
-                        q6k_half_sums(sb, part, w, bs, isum, dw);
-                }
-            }
-            isum += __shfl_xor_sync(0xFFFFFFFFu, isum, 1);
-            if (kType == 12) msum += __shfl_xor_sync(0xFFFFFFFFu, msum, 1);
-            if (active) {
-                const float dd = __fmul_rn(dw, dx);
-                float pi = __fmul_rn(dd, __int2float_rn(isum));
-                if (kType == 12) pi = __fsub_rn(pi, __fmul_rn(__fmul_rn(dmw, dx), __int2float_rn(msum)));
-                if (k & 1)
-                    acc1 = __fadd_rn(acc1, pi);
-                else
-                    acc0 = __fadd_rn(acc0, pi);
+        if (!failed) {
+            const uint32_t q_lo = t * R;
+            const uint32_t n_here = nrows - q_lo < R ? nrows - q_lo : R;
+            const uint32_t head = (wlo + (row0 + q_lo) * rb) & 15u;
+            const uint8_t* slot = stage0 + s * stage_bytes + head;
+            uint32_t j = warp >= static_cast<int>(owner_base) ? warp - owner_base : warp + NCW - owner_base;
+            for (; j < n_here; j += NCW) {
+                const float v = q8k_row_dot<kType, kXReg>(op.nb, img, slot + j * rb, xw, xbs, xd, lane);
+                if (lane == 0) y[q_lo + j] = v;
             }
         }
-        float v = __fadd_rn(acc0, acc1);
-#pragma unroll
-        for (int off = 16; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-        if (lane == 0) op.y[r] = v;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == S) {
+            s = 0;
+            phase ^= 1u;
+        }
+        owner_base += R % NCW;
+        if (owner_base >= NCW) owner_base -= NCW;
     }
-};
+}
 
 // kTypes: 1 = every op is q4_K, 2 = every op is q6_K, 3 = mixed.
 template <int kWarps, int kTypes>
@@ -242,7 +219,6 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
     // still takes every named barrier and stage arrival, so no other warp can
     // be left waiting at a barrier without a deadline.
     pdl_wait();
-    ProgramConsumer<NCW> cons;
     bool failed = false;
     // Every op that reads an activation from outside this launch had its image
     // built once, before this kernel, by quantize_images_kernel (the preceding
@@ -264,46 +240,22 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                 failed = !__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0);
             }
             named_barrier_sync(1, NCW * 32);  // (orders the acquire above before every warp's loads)
-            if (!failed) cons.prologue(op, act, warp, lane);
+            if (!failed) quantize_to_image(op.x, op.nb, q8k_image(act + op.act_offset, op.nb), warp, NCW, lane);
             named_barrier_sync(1, NCW * 32);
         }
-        if (!failed) cons.load(op, act, lane);
-
-        const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
-        const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
-        const uint32_t nrows = static_cast<uint32_t>(r1 - r0);
-        const uint32_t R = op.rows_per_stage;
-        const uint32_t T = (nrows + R - 1) / R;
-        const uint32_t rb = static_cast<uint32_t>(op.row_bytes);
-        const uint32_t wlo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w));
-        const uint32_t row0 = static_cast<uint32_t>(r0);
-        uint32_t owner_base = 0;  // (t * R) % NCW
-        for (uint32_t t = 0; t < T; ++t) {
-            if (!failed) {
-                const bool ok = mbar_wait(&full[s], phase, pp.status, 14);
-                failed = !__all_sync(0xFFFFFFFFu, ok);
-            }
-            if (!failed) {
-                const uint32_t q_lo = t * R;
-                const uint32_t n_here = nrows - q_lo < R ? nrows - q_lo : R;
-                const uint32_t head = (wlo + (row0 + q_lo) * rb) & 15u;
-                const uint8_t* slot = stage0 + s * pp.stage_bytes + head;
-                uint32_t j = warp >= owner_base ? warp - owner_base : warp + NCW - owner_base;
-                for (; j < n_here; j += NCW) {
-                    if (kTypes == 1 || (kTypes == 3 && op.type == 12))
-                        cons.template row_typed<12>(op, act, slot + j * rb, r0 + q_lo + j, lane);
-                    else
-                        cons.template row_typed<14>(op, act, slot + j * rb, r0 + q_lo + j, lane);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            if (++s == S) {
-                s = 0;
-                phase ^= 1u;
-            }
-            owner_base += R % NCW;
-            if (owner_base >= NCW) owner_base -= NCW;
+        const bool q4 = kTypes == 1 || (kTypes == 3 && op.type == 12);
+        if (q4) {
+            if (op.nb <= 16)
+                program_walk_op<NCW, 12, true>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
+                                               pp.status, warp, lane);
+            else
+                program_walk_op<NCW, 12, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
+                                                pp.status, warp, lane);
+        } else {
+            // Q6_K ops re-read their activation slice per pass: the register-resident
+            // variant does not fit beside the Q4_K code in 128 registers
+            program_walk_op<NCW, 14, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
+                                            pp.status, warp, lane);
         }
         if (op.publish) {
             // publish this CTA's completion of op k (its y rows are written)
