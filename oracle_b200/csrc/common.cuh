@@ -74,17 +74,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+// try_wait that may suspend the thread (up to `hint_ns`) until the phase
+// completes: a waiting warp then takes no issue slots from the working ones.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return done != 0;
+}
+
 // Wait for the phase with the given parity to complete.  Returns false (and
 // records a timeout) if it has not completed within kWaitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, DeviceStatus* st,
                                           unsigned int where, unsigned long long limit_ns = kWaitNs) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
     const unsigned long long t0 = global_timer_ns();
 #pragma unroll 1
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
         if (global_timer_ns() - t0 > limit_ns) {
             report_timeout(st, where);
             return false;

@@ -36,23 +36,43 @@
 
 namespace oracle_cuda {
 
-constexpr uint32_t kGemmTileN = 128;  // weight rows per CTA (UMMA M)
-constexpr uint32_t kGemmTileM = 256;  // tokens per CTA (UMMA N)
+constexpr uint32_t kGemmTileN = 128;  // weight rows per CTA (TMEM lanes)
+constexpr uint32_t kGemmTileM = 256;  // tokens per CTA or CTA pair (UMMA N, TMEM columns)
 constexpr uint32_t kGemmTileK = 64;   // K per stage
-constexpr uint32_t kGemmStages = 3;
 constexpr uint32_t kGemmRawStages = 3;
 constexpr uint32_t kGemmSbBytes = 144;  // Q4_K super-block
 constexpr uint32_t kGemmABytes = kGemmTileN * kGemmTileK * 2;
-constexpr uint32_t kGemmBBytes = kGemmTileM * kGemmTileK * 2;
 constexpr uint32_t kGemmRawBytes = kGemmTileN * kGemmSbBytes;
 constexpr uint32_t kGemmDequantWarps = 8;
 constexpr uint32_t kGemmThreads = (4 + kGemmDequantWarps) * 32;
-constexpr uint32_t kGemmTmemCols = 256;
-constexpr uint32_t kGemmOffB = kGemmStages * kGemmABytes;
-constexpr uint32_t kGemmOffRaw = kGemmOffB + kGemmStages * kGemmBBytes;
-constexpr uint32_t kGemmOffBars = kGemmOffRaw + kGemmRawStages * kGemmRawBytes;
-constexpr uint32_t kGemmBars = 3 * kGemmStages + 2 * kGemmRawStages + 1;
-constexpr uint32_t kGemmSmemBytes = 1024 + kGemmOffBars + kGemmBars * 8 + 16;
+
+// Shared-memory plan of one CTA.  kPair: a CTA pair (cluster of 2) shares
+// each MMA: M = 256 weight rows (128 per CTA), and each CTA loads half of the
+// 256 tokens, so a stage's B tile is 128 rows.
+//
+// kPair = false keeps the dequantized A tiles in TMEM (tcgen05.st from the
+// dequant warps, tcgen05.mma reading A from tensor memory): shared memory then
+// carries only B and the raw weights, which leaves its bandwidth to the MMA's
+// B reads.  TMEM: columns [0, 256) accumulator, then 32 columns per stage of A
+// (64 bf16 of K per row, two per column).
+template <bool kPair>
+struct GemmPlan {
+    static constexpr bool kATmem = !kPair;
+    static constexpr uint32_t kStages = 4;
+    static constexpr uint32_t kTmemCols = kATmem ? 512 : 256;
+    static constexpr uint32_t kATmemCol = kGemmTileM;  // first A column
+    static constexpr uint32_t kBRows = kPair ? kGemmTileM / 2 : kGemmTileM;
+    static constexpr uint32_t kBBytes = kBRows * kGemmTileK * 2;
+    static constexpr uint32_t kOffB = kATmem ? 0 : kStages * kGemmABytes;
+    static constexpr uint32_t kOffRaw = kOffB + kStages * kBBytes;
+    static constexpr uint32_t kOffBars = kOffRaw + kGemmRawStages * kGemmRawBytes;
+    // full_a, full_b, empty, peer_full per stage; raw_full, raw_empty per raw stage; acc_full
+    static constexpr uint32_t kBars = 4 * kStages + 2 * kGemmRawStages + 1;
+    static constexpr uint32_t kSmemBytes = 1024 + kOffBars + kBars * 8 + 16;
+    // Instruction descriptor: D f32, A and B bf16, both K-major, M = 128 or 256 (pair), N = 256.
+    static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((kGemmTileM >> 3) << 17) |
+                                       (((kPair ? 2 * kGemmTileN : kGemmTileN) >> 4) << 24);
+};
 
 struct GemmParams {
     float* y;                // m x n row-major
@@ -68,10 +88,6 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem) {
     return static_cast<uint64_t>((smem >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
            (2ull << 61);
 }
-
-// Instruction descriptor: D f32, A and B bf16, both K-major, M = 128, N = 256.
-constexpr uint32_t kGemmIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((kGemmTileM >> 3) << 17) |
-                                ((kGemmTileN >> 4) << 24);
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
     asm volatile(
@@ -110,6 +126,18 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)
           "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]),
+        "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]),
+        "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -162,35 +190,107 @@ __device__ __forceinline__ uint2 dequant4(uint32_t nib4, uint64_t dsc2, uint64_t
     return r;
 }
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// A from tensor memory (cta_group::1).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+template <bool kPair>
+__device__ __forceinline__ void umma_bf16_issue(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    constexpr uint32_t idesc = GemmPlan<kPair>::kIdesc;
+    if constexpr (kPair)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    else
+        umma_bf16(tmem_d, adesc, bdesc, idesc, accumulate);
+}
+
+// tcgen05.commit to a barrier given by its cluster address (own or the peer's).
+template <bool kPair>
+__device__ __forceinline__ void umma_commit_to(uint32_t cluster_addr) {
+    if constexpr (kPair)
+        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
+                     : "memory");
+    else
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
+                     : "memory");
+}
+
+// kPair = false: one CTA per (128 weight rows x 256 tokens) tile, tcgen05.mma
+// with cta_group::1 (M = 128).  kPair = true: clusters of 2 CTAs along x, each
+// CTA owning 128 weight rows and loading half of the pair's 256 tokens; the
+// leader (rank 0) issues tcgen05.mma with cta_group::2 (M = 256), which reads
+// A and B from both CTAs' shared memory at the same offsets and leaves each
+// CTA's 128 x 256 accumulator in its own TMEM.  The peer's warp 1 relays "my
+// stage is full" to the leader with a remote mbarrier arrive; the leader's
+// commits arrive on both CTAs' `empty` and `acc_full` barriers.
+template <bool kPair>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_q4k_bf16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                          const GemmParams p) {
+    using Plan = GemmPlan<kPair>;
+    constexpr uint32_t S = Plan::kStages;
     extern __shared__ uint8_t gemm_smem[];
     const uint32_t raw_base = smem_addr(gemm_smem);
     const uint32_t base = (raw_base + 1023u) & ~1023u;
     uint8_t* smem = gemm_smem + (base - raw_base);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGemmOffBars);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Plan::kOffBars);
     uint64_t* full_a = bars;                          // dequant warps -> MMA
-    uint64_t* full_b = bars + kGemmStages;            // X TMA -> MMA
-    uint64_t* empty = bars + 2 * kGemmStages;         // MMA commit -> producers
-    uint64_t* raw_full = bars + 3 * kGemmStages;      // raw TMA -> dequant
+    uint64_t* full_b = bars + S;                      // X TMA -> MMA
+    uint64_t* empty = bars + 2 * S;                   // MMA commit -> producers
+    uint64_t* peer_full = bars + 3 * S;               // (pair, leader) peer relay -> MMA
+    uint64_t* raw_full = bars + 4 * S;                // raw TMA -> dequant
     uint64_t* raw_empty = raw_full + kGemmRawStages;  // dequant -> raw TMA
     uint64_t* acc_full = raw_empty + kGemmRawStages;  // last MMA -> epilogue
-    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + kGemmBars);
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + Plan::kBars);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t m0 = blockIdx.x * kGemmTileM, n0 = blockIdx.y * kGemmTileN;
+    const uint32_t rank = kPair ? cluster_rank() : 0u;
+    const uint32_t n0 = blockIdx.x * kGemmTileN, m0 = blockIdx.y * kGemmTileM;
+    const uint32_t b_row0 = m0 + rank * Plan::kBRows;  // this CTA's B rows (tokens)
     const uint32_t k_begin = blockIdx.z * p.k_per_split;
     const uint32_t k_end = p.k - k_begin < p.k_per_split ? p.k : k_begin + p.k_per_split;
     const uint32_t nk = (k_end - k_begin) / kGemmTileK;
     const uint32_t nsb = nk / 4;
 
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < kGemmStages; ++s) {
+        for (uint32_t s = 0; s < S; ++s) {
             mbar_init(&full_a[s], kGemmDequantWarps / 2);  // one group of 4 warps per stage
             mbar_init(&full_b[s], 1);
             mbar_init(&empty[s], 1);
+            mbar_init(&peer_full[s], 1);
         }
         for (uint32_t r = 0; r < kGemmRawStages; ++r) {
             mbar_init(&raw_full[r], 1);
@@ -201,14 +301,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_mbar_init();
     }
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_addr(const_cast<uint32_t*>(tmem_slot))),
-                     "r"(kGemmTmemCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        const uint32_t slot = smem_addr(const_cast<uint32_t*>(tmem_slot));
+        if constexpr (kPair) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot),
+                         "r"(Plan::kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot),
+                         "r"(Plan::kTmemCols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync_all();  // both CTAs' barriers exist before any remote arrive
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -217,38 +325,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // ---------------------------------------------------------- X tiles
             uint32_t issued = 0;
             for (uint32_t kc = 0; kc < nk && !*abort_flag; ++kc) {
-                const uint32_t s = kc % kGemmStages;
-                if (kc >= kGemmStages && !mbar_wait(&empty[s], ((kc / kGemmStages) - 1) & 1, p.status, 41)) {
+                const uint32_t s = kc % S;
+                if (kc >= S && !mbar_wait(&empty[s], ((kc / S) - 1) & 1, p.status, 41)) {
                     *abort_flag = 1;
                     break;
                 }
-                mbar_arrive_expect_tx(&full_b[s], kGemmBBytes);
-                tma_load_2d(base + kGemmOffB + s * kGemmBBytes, &tmap_x, &full_b[s],
-                            static_cast<int>(k_begin + kc * kGemmTileK), static_cast<int>(m0));
+                mbar_arrive_expect_tx(&full_b[s], Plan::kBBytes);
+                tma_load_2d(base + Plan::kOffB + s * Plan::kBBytes, &tmap_x, &full_b[s],
+                            static_cast<int>(k_begin + kc * kGemmTileK), static_cast<int>(b_row0));
                 issued = kc + 1;
             }
             // no load may still be in flight when the CTA exits
-            for (uint32_t kc = issued > kGemmStages ? issued - kGemmStages : 0; kc < issued; ++kc)
-                mbar_wait(&full_b[kc % kGemmStages], (kc / kGemmStages) & 1, p.status, 42);
+            for (uint32_t kc = issued > S ? issued - S : 0; kc < issued; ++kc)
+                mbar_wait(&full_b[kc % S], (kc / S) & 1, p.status, 42);
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && rank == 0) {
             // ---------------------------------------------------------- MMA issue
+            const uint32_t peer = kPair ? 1u : 0u;
             for (uint32_t kc = 0; kc < nk && !*abort_flag; ++kc) {
-                const uint32_t s = kc % kGemmStages, par = (kc / kGemmStages) & 1;
-                if (!mbar_wait(&full_b[s], par, p.status, 43) || !mbar_wait(&full_a[s], par, p.status, 44)) {
+                const uint32_t s = kc % S, par = (kc / S) & 1;
+                if (!mbar_wait(&full_b[s], par, p.status, 43) || !mbar_wait(&full_a[s], par, p.status, 44) ||
+                    (kPair && !mbar_wait(&peer_full[s], par, p.status, 50))) {
                     *abort_flag = 1;
                     break;
                 }
                 tc_fence_after();
-                const uint64_t ad = umma_desc_sw128(base + s * kGemmABytes);
-                const uint64_t bd = umma_desc_sw128(base + kGemmOffB + s * kGemmBBytes);
+                const uint64_t bd = umma_desc_sw128(base + Plan::kOffB + s * Plan::kBBytes);
+                if constexpr (Plan::kATmem) {
 #pragma unroll
-                for (uint32_t kk = 0; kk < kGemmTileK / 16; ++kk)
-                    umma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, kGemmIdesc, (kc | kk) != 0);
-                umma_commit(&empty[s]);
+                    for (uint32_t kk = 0; kk < kGemmTileK / 16; ++kk)
+                        umma_bf16_ts(tmem, tmem + Plan::kATmemCol + 32 * s + 8 * kk, bd + 2 * kk, Plan::kIdesc,
+                                     (kc | kk) != 0);
+                } else {
+                    const uint64_t ad = umma_desc_sw128(base + s * kGemmABytes);
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kGemmTileK / 16; ++kk)
+                        umma_bf16_issue<kPair>(tmem, ad + 2 * kk, bd + 2 * kk, (kc | kk) != 0);
+                }
+                umma_commit_to<kPair>(smem_addr(&empty[s]));
+                if (kPair) umma_commit_to<kPair>(mapa_shared(smem_addr(&empty[s]), peer));
             }
-            umma_commit(acc_full);  // also after an abort: completes once issued MMAs finish
+            // also after an abort: completes once the issued MMAs finish
+            umma_commit_to<kPair>(smem_addr(acc_full));
+            if (kPair) umma_commit_to<kPair>(mapa_shared(smem_addr(acc_full), peer));
+        } else if (kPair && lane == 0) {
+            // ---------------------------------------------------------- peer: relay full stages
+            for (uint32_t kc = 0; kc < nk && !*abort_flag; ++kc) {
+                const uint32_t s = kc % S, par = (kc / S) & 1;
+                if (!mbar_wait(&full_b[s], par, p.status, 51) || !mbar_wait(&full_a[s], par, p.status, 52)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_remote(mapa_shared(smem_addr(&peer_full[s]), 0));
+            }
         }
     } else if (warp == 2) {
         if (lane == 0) {
@@ -262,7 +392,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     break;
                 }
                 mbar_arrive_expect_tx(&raw_full[r], kGemmRawBytes);
-                tma_load_2d(base + kGemmOffRaw + r * kGemmRawBytes, &tmap_w, &raw_full[r],
+                tma_load_2d(base + Plan::kOffRaw + r * kGemmRawBytes, &tmap_w, &raw_full[r],
                             static_cast<int>((k_begin / 256 + j) * kGemmSbBytes), static_cast<int>(n0));
                 issued = j + 1;
             }
@@ -282,15 +412,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 ok = false;
                 break;
             }
-            const uint32_t s = kc % kGemmStages, j = kc / 4, g = kc % 4, r = j % kGemmRawStages;
+            const uint32_t s = kc % S, j = kc / 4, g = kc % 4, r = j % kGemmRawStages;
             if (g == grp && !mbar_wait(&raw_full[r], (j / kGemmRawStages) & 1, p.status, 47)) ok = false;
-            if (ok && kc >= kGemmStages && !mbar_wait(&empty[s], ((kc / kGemmStages) - 1) & 1, p.status, 48))
-                ok = false;
+            if (ok && kc >= S && !mbar_wait(&empty[s], ((kc / S) - 1) & 1, p.status, 48)) ok = false;
             if (!ok) {
                 *abort_flag = 1;
                 break;
             }
-            const uint8_t* rp = smem + kGemmOffRaw + r * kGemmRawBytes + row * kGemmSbBytes;
+            const uint8_t* rp = smem + Plan::kOffRaw + r * kGemmRawBytes + row * kGemmSbBytes;
             const uint4 h = *reinterpret_cast<const uint4*>(rp);
             const uint4 qa = *reinterpret_cast<const uint4*>(rp + 16 + 32 * g);
             const uint4 qb = *reinterpret_cast<const uint4*>(rp + 32 + 32 * g);
@@ -304,19 +433,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint64_t dsl2 = f32x2(dsl, dsl), dml2 = f32x2(dml, dml);
             const uint64_t dsh2 = f32x2(dsh, dsh), dmh2 = f32x2(dmh, dmh);
             const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-            uint8_t* arow = smem + s * kGemmABytes + row * 128;
+            // element e of the stage's 64 goes to word e / 2 (low half for even e):
+            // words 0..15 = low nibbles of bytes 0..31, words 16..31 = high nibbles
+            uint32_t av[32];
 #pragma unroll
             for (uint32_t c = 0; c < 4; ++c) {
-                // chunk c: elements 8c..8c+7 = low nibbles of bytes 8c..8c+7;
-                // chunk 4+c: elements 32+8c.. = their high nibbles
                 const uint2 l0 = dequant4(qw[2 * c] & 0x0F0F0F0Fu, dsl2, dml2);
                 const uint2 l1 = dequant4(qw[2 * c + 1] & 0x0F0F0F0Fu, dsl2, dml2);
                 const uint2 h0 = dequant4((qw[2 * c] >> 4) & 0x0F0F0F0Fu, dsh2, dmh2);
                 const uint2 h1 = dequant4((qw[2 * c + 1] >> 4) & 0x0F0F0F0Fu, dsh2, dmh2);
-                *reinterpret_cast<uint4*>(arow + ((c ^ (row & 7)) * 16)) = make_uint4(l0.x, l0.y, l1.x, l1.y);
-                *reinterpret_cast<uint4*>(arow + (((4 + c) ^ (row & 7)) * 16)) = make_uint4(h0.x, h0.y, h1.x, h1.y);
+                av[4 * c + 0] = l0.x, av[4 * c + 1] = l0.y, av[4 * c + 2] = l1.x, av[4 * c + 3] = l1.y;
+                av[16 + 4 * c + 0] = h0.x, av[16 + 4 * c + 1] = h0.y, av[16 + 4 * c + 2] = h1.x,
+                                av[16 + 4 * c + 3] = h1.y;
             }
-            fence_async_smem();
+            if constexpr (Plan::kATmem) {
+                // this warp's 32 rows are TMEM lanes 32 * (warp % 4) ...
+                tmem_st_32x32b_x32(tmem + ((32u * (warp & 3u)) << 16) + Plan::kATmemCol + 32 * s, av);
+                tc_fence_before();
+            } else {
+                // K-major, 128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7)
+                uint8_t* arow = smem + s * kGemmABytes + row * 128;
+#pragma unroll
+                for (uint32_t c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4*>(arow + ((c ^ (row & 7)) * 16)) =
+                        make_uint4(av[4 * c], av[4 * c + 1], av[4 * c + 2], av[4 * c + 3]);
+                fence_async_smem();
+            }
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&full_a[s]);
@@ -352,11 +494,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync_all();  // no CTA leaves while its peer may still touch it
     if (warp == 0) {
         __syncwarp();
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmTmemCols)
-                     : "memory");
+        if constexpr (kPair)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Plan::kTmemCols)
+                         : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Plan::kTmemCols)
+                         : "memory");
     }
 }
 

@@ -65,6 +65,7 @@ struct oracle_cuda_context {
     // prefill GEMM: bf16 copy of the activations
     uint16_t* gemm_x = nullptr;
     uint64_t gemm_x_len = 0;
+    bool gemm_pair = false;  // prefill GEMM on CTA pairs (cta_group::2); ORACLE_CUDA_GEMM_PAIR=1
 };
 
 namespace {
@@ -491,6 +492,7 @@ oracle_cuda_status oracle_cuda_create(int device, oracle_cuda_context** out) {
         const unsigned long long v = std::strtoull(env, nullptr, 10);
         if (v >= 16384 && v <= static_cast<unsigned long long>(ctx->max_smem_optin)) ctx->smem_budget = v;
     }
+    if (const char* env = std::getenv("ORACLE_CUDA_GEMM_PAIR")) ctx->gemm_pair = std::strtoull(env, nullptr, 10) != 0;
     if ((e = cudaMalloc(reinterpret_cast<void**>(&ctx->status), sizeof(DeviceStatus))) != cudaSuccess) {
         delete ctx;
         return cuda_fail(nullptr, e, "cudaMalloc(status)");
@@ -1153,11 +1155,17 @@ extern "C" oracle_cuda_status oracle_cuda_prefill_gemm(oracle_cuda_context* ctx,
                reinterpret_cast<uint32_t*>(ctx->gemm_x), n4);
     if (s != ORACLE_CUDA_OK) return s;
 
+    const uint64_t tiles_m = (m + kGemmTileM - 1) / kGemmTileM, tiles_n = (rows + kGemmTileN - 1) / kGemmTileN;
+    // CTA pairs (cta_group::2) when enabled (ORACLE_CUDA_GEMM_PAIR=1)
+    const bool pair = ctx->gemm_pair && tiles_n >= 2;
+    const uint64_t grid_n = pair ? (tiles_n + 1) / 2 * 2 : tiles_n;
+    if (grid_n > 0x7FFFFFFFull || tiles_m > 65535)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "prefill GEMM grid too large for one launch");
     CUtensorMap tx{}, tw{};
     {
         const cuuint64_t dims[2] = {cols, m};
         const cuuint64_t strides[1] = {cols * 2};
-        const cuuint32_t box[2] = {kGemmTileK, kGemmTileM};
+        const cuuint32_t box[2] = {kGemmTileK, pair ? GemmPlan<true>::kBRows : GemmPlan<false>::kBRows};
         const cuuint32_t estr[2] = {1, 1};
         if (encode(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ctx->gemm_x, dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1174,18 +1182,42 @@ extern "C" oracle_cuda_status oracle_cuda_prefill_gemm(oracle_cuda_context* ctx,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return fail(ctx, ORACLE_CUDA_CUDA_ERROR, "tensor map for the weights rejected");
     }
-    const uint64_t tiles_m = (m + kGemmTileM - 1) / kGemmTileM, tiles_n = (rows + kGemmTileN - 1) / kGemmTileN;
-    if (tiles_n > 65535) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "too many weight rows for one prefill GEMM launch");
     GemmParams gp{};
     gp.y = y_dev;
     gp.n = static_cast<uint32_t>(rows);
     gp.m = static_cast<uint32_t>(m);
     gp.k = static_cast<uint32_t>(cols);
-    gp.k_per_split = gemm_k_per_split(tiles_m * tiles_n, cols, ctx->sm_count);
+    gp.k_per_split = gemm_k_per_split(tiles_m * grid_n, cols, ctx->sm_count);
     gp.accumulate = gp.k_per_split < cols ? 1u : 0u;
     gp.status = ctx->status;
     if (gp.accumulate) ORACLE_CUDA_TRY(ctx, cudaMemsetAsync(y_dev, 0, m * rows * sizeof(float), stream), "cudaMemsetAsync");
-    return launch(ctx, gemm_q4k_bf16_kernel, dim3(static_cast<uint32_t>(tiles_m), static_cast<uint32_t>(tiles_n),
-                                                  static_cast<uint32_t>(cols / gp.k_per_split)),
-                  dim3(kGemmThreads), kGemmSmemBytes, stream, false, tx, tw, gp);
+    const dim3 grid(static_cast<uint32_t>(grid_n), static_cast<uint32_t>(tiles_m),
+                    static_cast<uint32_t>(cols / gp.k_per_split));
+    if (!pair)
+        return launch(ctx, gemm_q4k_bf16_kernel<false>, grid, dim3(kGemmThreads), GemmPlan<false>::kSmemBytes, stream,
+                      false, tx, tw, gp);
+    // clusters of two CTAs along x
+    const void* key = reinterpret_cast<const void*>(gemm_q4k_bf16_kernel<true>);
+    if (!ctx->smem_configured.count(key)) {
+        ORACLE_CUDA_TRY(ctx,
+                        cudaFuncSetAttribute(gemm_q4k_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             ctx->max_smem_optin),
+                        "cudaFuncSetAttribute");
+        ctx->smem_configured.insert(key);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = GemmPlan<true>::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ORACLE_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, gemm_q4k_bf16_kernel<true>, tx, tw, gp), "kernel launch");
+    ctx->launches += 1;
+    return ORACLE_CUDA_OK;
 }

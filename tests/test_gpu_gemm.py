@@ -93,3 +93,16 @@ def test_gemm_validation(ctx):
     with pytest.raises(ob.RuntimeError_, match="not divisible by block size"):
         ctx.prefill_gemm(ob.TYPE_Q4_K, n, 200, w, x, m, y)
     ctx.device_status()
+
+
+def test_gemm_cta_pair_mode(port, monkeypatch):
+    """The CTA-pair kernel (tcgen05.mma cta_group::2, ORACLE_CUDA_GEMM_PAIR=1) gives the same products."""
+    monkeypatch.setenv("ORACLE_CUDA_GEMM_PAIR", "1")
+    with ob.Context(0) as ctx2:
+        for n, k, m in [(256, 512, 300), (384, 1024, 64), (1024, 4096, 512)]:
+            w = synth.weight(ob.TYPE_Q4_K, n, k, "gemm", f"pair_w_{n}_{k}")
+            x = synth.activations(k, m, "gemm", f"pair_x_{k}_{m}")
+            got = run_gemm(ctx2, w, x, n, k, m)
+            rng = np.random.default_rng(n + k)
+            mi, ni = sample(rng, m, n, 2000)
+            check(port, w, x, n, k, m, got, mi, ni)
