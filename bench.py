@@ -76,8 +76,9 @@ class Workload:
         return {"workload": self.description, "shapes_k_to_n": [f"{k}->{n}" for _, k, n in self.ops], "batch": 1,
                 "bytes_per_step": self.step_bytes,
                 "l2": f"weights rotate through {self.pool_sets} sets ({self.pool_sets * wb / 1e6:.0f} MB > 3x L2)",
-                "parallelism": (f"tp{n_gpus}: rows sharded over {n_gpus} GPUs, one NCCL all-gather of the "
-                                "outputs per step" if n_gpus > 1 else "single")}
+                "parallelism": (f"tp{n_gpus}: rows sharded over {n_gpus} GPUs, outputs all-gathered every step "
+                                "(inside the matvec kernel over NVLink, or one NCCL all-gather with --exchange nccl)"
+                                if n_gpus > 1 else "single")}
 
 
 WORKLOADS = {
@@ -350,7 +351,7 @@ def reference_arm(args, wl: Workload) -> None:
     sample = f"{fraction * 100:.2f}% of the rows of every {wl.name} matrix per step on {threads} threads: {cpu_what(wl)}"
     line = {"impl": "reference", "metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_t / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype,
             "data": "synthetic", "config": wl.config(args.gpus),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": wl.cpu_kind, "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -384,22 +385,38 @@ def gpu_arm(args, wl: Workload) -> None:
         pool.append([torch.from_numpy(np.roll(w.reshape(-1), s * BLOCK[t][1])).to(dev)
                      for w, (t, _, _) in zip(ws_local, wl.ops)])
     x_dev = [torch.from_numpy(x).to(dev) for x in xs]
-    y_pack = torch.empty(plan.pack_len, dtype=torch.float32, device=dev)
+    # N > 1, Q8_K contract: the all-gather is fused into the matvec program
+    # (rows stored into every peer's gather buffer over NVLink, CUDA IPC);
+    # --exchange nccl (or the f32 contract) uses one NCCL all-gather instead
+    fused = world > 1 and args.exchange == "fused" and wl.contract == CONTRACT_Q8K
+    group = None
+    if fused:
+        import torch.distributed as dist
+        group = ob.PeerGroup(ctx, rank, world, (world * plan.pack_len * 4 + 15) // 16 * 16)
+        handles = [None] * world
+        dist.all_gather_object(handles, group.handle)
+        group.connect(handles)
+        gathered = group.tensor()[:world * plan.pack_len]
+        y_pack = gathered[rank * plan.pack_len:(rank + 1) * plan.pack_len]
+    else:
+        y_pack = torch.empty(plan.pack_len, dtype=torch.float32, device=dev)
+        gathered = torch.empty(world * plan.pack_len, dtype=torch.float32, device=dev) if world > 1 else None
     y_dev = [y_pack[o:o + sh.local_rows] for o, sh in zip(plan.offsets, plan.shards)]
-    gathered = torch.empty(world * plan.pack_len, dtype=torch.float32, device=dev) if world > 1 else None
     stream = torch.cuda.Stream(dev)
 
     def exchange():
-        if world > 1:
+        if world > 1 and not fused:
             import torch.distributed as dist
             dist.all_gather_into_tensor(gathered, y_pack)
 
     def step(s: int):
         ws_ = pool[s % wl.pool_sets]
-        if wl.program:
+        ops_ = [(t, n, k, ws_[i], x_dev[i], y_dev[i], 0) for i, (t, k, n) in enumerate(local_ops)]
+        if fused:
+            ctx.matvec_program_allgather(group, ops_, stream=stream)
+        elif wl.program:
             # one persistent launch runs all the (independent) matvecs of the step
-            ctx.matvec_program([(t, n, k, ws_[i], x_dev[i], y_dev[i], 0) for i, (t, k, n) in enumerate(local_ops)],
-                               stream=stream)
+            ctx.matvec_program(ops_, stream=stream)
             exchange()
         else:
             step_separate(s)
@@ -547,8 +564,9 @@ def gpu_arm(args, wl: Workload) -> None:
                 g_pin.copy_(gathered, non_blocking=True)
             stream.synchronize()
 
-        e2e_how = ("pinned x copied in on every rank, row-sharded step + NCCL all-gather, every rank copies the "
-                   "whole output out, synchronised each step; wall clock, max over ranks")
+        e2e_how = ("pinned x copied in on every rank, row-sharded step with its all-gather "
+                   f"({'in the matvec kernel' if fused else 'NCCL'}), every rank copies the whole output out, "
+                   "synchronised each step; wall clock, max over ranks")
         e2e_d2h = world * plan.pack_len * 4
 
     for _ in range(3):
@@ -581,9 +599,15 @@ def gpu_arm(args, wl: Workload) -> None:
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                              "traffic": load_traffic(wl), "kernel": kernel, **extra},
-                "cpu_baseline": cpu, "clocks": sampler.summary(), "pdl": not args.no_pdl}
+                "cpu_baseline": cpu, "clocks": sampler.summary(), "pdl": not args.no_pdl,
+                "exchange": ("fused all-gather in the matvec kernel (NVLink stores to CUDA-IPC gather buffers)"
+                             if fused else "NCCL all_gather_into_tensor" if world > 1 else None)}
         print(json.dumps(line), flush=True)
     del graph, tail
+    torch.cuda.synchronize()
+    barrier(world)  # no peer still writes into this rank's gather buffer
+    if group is not None:
+        group.close()
     ctx.close()
     if world > 1:
         import torch.distributed as dist
@@ -836,6 +860,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["config4"], default="config2")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: all-gather inside the matvec kernel (fused) or one NCCL all-gather per step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -207,6 +207,40 @@ oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const or
 oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cuda_matvec_op* ops, uint32_t n_ops,
                                                       void* stream);
 
+/* ------------------------------------------------------------------ row-sharded programs over GPUs
+ * Tensor-parallel decode on the GPUs of one node, one process per GPU: every
+ * rank holds an equal contiguous row range of each weight matrix and runs the
+ * same matvec program on it; every output row is stored both locally and,
+ * over NVLink, into every peer's gather buffer at the same offset, so that
+ * when the launch completes each rank holds all ranks' rows (the all-gather
+ * of the outputs happens inside the matvec kernel; no NCCL call).
+ *   1. oracle_cuda_peer_group_create on every rank: allocates the rank's
+ *      gather buffer (data_bytes, device memory) and returns its CUDA IPC
+ *      handle (ORACLE_CUDA_IPC_HANDLE_BYTES) to publish to the other ranks;
+ *   2. oracle_cuda_peer_group_connect with all ranks' handles, in rank order;
+ *   3. oracle_cuda_matvec_program_allgather: like oracle_cuda_matvec_program,
+ *      with every op's y_dev inside this rank's gather data region
+ *      (oracle_cuda_peer_group_data) at the offset of this rank's rows; all
+ *      ranks must run the same program shapes, launch for launch.
+ * The gather buffer is overwritten by peers on their next launch: a caller
+ * that needs the previous gathered output while peers run ahead alternates
+ * two groups.  A peer that does not launch makes the waiting kernel give up
+ * after one second and record a device timeout (oracle_cuda_device_status).
+ * No counterpart in the reference (Oracle runs on one CPU thread); the north
+ * star's per-layer NCCL all-gather is what this replaces. */
+#define ORACLE_CUDA_IPC_HANDLE_BYTES 64
+#define ORACLE_CUDA_MAX_PEERS 8
+typedef struct oracle_cuda_peer_group oracle_cuda_peer_group;
+oracle_cuda_status oracle_cuda_peer_group_create(oracle_cuda_context* ctx, uint32_t rank, uint32_t world,
+                                                 uint64_t data_bytes, oracle_cuda_peer_group** out,
+                                                 void* ipc_handle_out);
+oracle_cuda_status oracle_cuda_peer_group_connect(oracle_cuda_peer_group* group, const void* handles);
+oracle_cuda_status oracle_cuda_peer_group_data(oracle_cuda_peer_group* group, float** data_dev);
+oracle_cuda_status oracle_cuda_peer_group_destroy(oracle_cuda_peer_group* group);
+oracle_cuda_status oracle_cuda_matvec_program_allgather(oracle_cuda_context* ctx, oracle_cuda_peer_group* group,
+                                                        const oracle_cuda_matvec_op* ops, uint32_t n_ops,
+                                                        void* stream);
+
 /* ------------------------------------------------------------------ prefill dequant-GEMM
  * Y[m][n] = sum_k X[m][k] * W[n][k] for m < m_tokens: the batched form of the
  * matvec for prompt ingestion (M >= 64 tokens).  W: `rows` GGML rows of `cols`

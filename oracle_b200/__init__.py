@@ -112,6 +112,55 @@ _proto("oracle_cuda_host_storage_dot", [_vp, _i32, _u32, _u64, _vp, _u64, _vp, _
 _proto("oracle_cuda_host_decode_rows", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64])
 _proto("oracle_cuda_evict_resident", [_vp])
 _proto("oracle_cuda_prefill_gemm", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _vp])
+_proto("oracle_cuda_peer_group_create", [_vp, _u32, _u32, _u64, C.POINTER(_vp), _vp])
+_proto("oracle_cuda_peer_group_connect", [_vp, _vp])
+_proto("oracle_cuda_peer_group_data", [_vp, C.POINTER(_vp)])
+_proto("oracle_cuda_peer_group_destroy", [_vp])
+_proto("oracle_cuda_matvec_program_allgather", [_vp, _vp, C.POINTER(MatvecOp), _u32, _vp])
+IPC_HANDLE_BYTES = 64
+MAX_PEERS = 8
+
+
+class _CudaArray:
+    """A raw device float32 array exposed through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 2}
+
+
+class PeerGroup:
+    """oracle_cuda_peer_group: this rank's gather buffer plus the mapped
+    buffers of the other ranks (CUDA IPC), for row-sharded matvec programs
+    whose outputs are all-gathered inside the kernel.  Publish ``handle`` to
+    the other ranks, then :meth:`connect` with every rank's handle in rank
+    order."""
+
+    def __init__(self, ctx: "Context", rank: int, world: int, data_bytes: int):
+        self._ctx = ctx
+        self._h = C.c_void_p()
+        buf = (C.c_ubyte * IPC_HANDLE_BYTES)()
+        ctx._check(_lib.oracle_cuda_peer_group_create(ctx._h, rank, world, data_bytes, C.byref(self._h), buf))
+        self.handle = bytes(buf)
+        self.rank, self.world, self.data_bytes = rank, world, data_bytes
+        p = C.c_void_p()
+        ctx._check(_lib.oracle_cuda_peer_group_data(self._h, C.byref(p)))
+        self.data_ptr = p.value
+
+    def connect(self, handles) -> None:
+        blob = b"".join(handles)
+        if len(blob) != self.world * IPC_HANDLE_BYTES:
+            raise InvalidArgument("one IPC handle per rank expected")
+        self._ctx._check(_lib.oracle_cuda_peer_group_connect(self._h, blob))
+
+    def tensor(self):
+        """The gather data region as a float32 CUDA tensor (no copy)."""
+        import torch
+        return torch.as_tensor(_CudaArray(self.data_ptr, self.data_bytes // 4), device="cuda")
+
+    def close(self) -> None:
+        if self._h:
+            _lib.oracle_cuda_peer_group_destroy(self._h)
+            self._h = None
 
 
 class OracleCudaError(Exception):
@@ -316,6 +365,13 @@ class Context:
         for i, (qtype, rows, cols, w, x, y, after) in enumerate(ops):
             arr[i] = MatvecOp(qtype, 1 if after else 0, rows, cols, _addr(w), _nbytes(w), _addr(x), _addr(y))
         self._check(_lib.oracle_cuda_matvec_program(self._h, arr, len(ops), _stream(stream)))
+
+    def matvec_program_allgather(self, group: "PeerGroup", ops, stream=None) -> None:
+        """oracle_cuda_matvec_program_allgather: the program on this rank's
+        rows, every output row also stored into every peer's gather buffer;
+        ops as for :meth:`matvec_program`, y inside the group's data region."""
+        arr = _matvec_ops(ops)
+        self._check(_lib.oracle_cuda_matvec_program_allgather(self._h, group._h, arr, len(ops), _stream(stream)))
 
     def prefill_gemm(self, qtype, rows, cols, w, x, m, y, stream=None, w_nbytes=None) -> None:
         """oracle_cuda_prefill_gemm: y[m][n] = sum_k x[m][k] * W[n][k] on the

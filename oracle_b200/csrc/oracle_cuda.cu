@@ -653,8 +653,33 @@ oracle_cuda_status oracle_cuda_matvec_q8k_prequantized(oracle_cuda_context* ctx,
     return ok(ctx);
 }
 
+struct oracle_cuda_peer_group {
+    oracle_cuda_context* ctx = nullptr;
+    uint32_t rank = 0, world = 1;
+    uint64_t data_bytes = 0;
+    uint8_t* local = nullptr;                 // 256-byte header (counter, epoch) + data
+    uint8_t* mapped[kMaxPeers] = {};          // every rank's allocation, mapped here (own = local)
+    bool connected = false;
+};
+
+namespace {
+
+constexpr uint64_t kGatherHeader = 256;
+
+oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops, uint32_t n_ops,
+                               void* stream, const oracle_cuda_peer_group* group);
+
+}  // namespace
+
 oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops,
                                               uint32_t n_ops, void* stream) {
+    return program_run(ctx, ops, n_ops, stream, nullptr);
+}
+
+namespace {
+
+oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops, uint32_t n_ops,
+                               void* stream, const oracle_cuda_peer_group* group) {
     if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
     if (!ops || n_ops == 0 || n_ops > kProgramMaxOps)
         return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
@@ -735,6 +760,28 @@ oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const or
     pp.prebuilt_bytes = prebuilt;
     pp.counters = ctx->program_counters;
     pp.status = ctx->status;
+    pp.px.world = 1;
+    if (group) {
+        if (!group->connected) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "peer group is not connected");
+        if (group->ctx != ctx) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "peer group belongs to another context");
+        const float* lo = reinterpret_cast<const float*>(group->local + kGatherHeader);
+        const float* hi = lo + group->data_bytes / sizeof(float);
+        for (uint32_t k = 0; k < n_ops; ++k) {
+            const float* y0 = ops[k].y_dev;
+            if (y0 < lo || y0 + ops[k].rows > hi)
+                return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                            "op " + std::to_string(k) + ": output must lie inside the peer group's gather buffer");
+        }
+        pp.px.world = group->world;
+        pp.px.rank = group->rank;
+        pp.px.local_base = lo;
+        for (uint32_t r = 0; r < group->world; ++r) {
+            pp.px.peer_base[r] = reinterpret_cast<float*>(group->mapped[r] + kGatherHeader);
+            pp.px.peer_counter[r] = reinterpret_cast<unsigned int*>(group->mapped[r]);
+        }
+        pp.px.my_counter = reinterpret_cast<unsigned int*>(group->local);
+        pp.px.my_epoch = reinterpret_cast<unsigned int*>(group->local) + 1;
+    }
     const uint32_t grid = static_cast<uint32_t>(max_rows < uint64_t(ctx->sm_count) ? max_rows : ctx->sm_count);
     const size_t smem = stream_barrier_bytes(pp.stages) + pp.act_bytes + size_t(pp.stages) * pp.stage_bytes;
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
@@ -755,6 +802,93 @@ oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const or
     oracle_cuda_status st = launch(ctx, kernel, dim3(grid), dim3((kProgramWarps + 1) * 32), smem,
                                    static_cast<cudaStream_t>(stream), (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, pp);
     return st == ORACLE_CUDA_OK ? ok(ctx) : st;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- row-sharded programs over peers
+
+extern "C" oracle_cuda_status oracle_cuda_peer_group_create(oracle_cuda_context* ctx, uint32_t rank, uint32_t world,
+                                                            uint64_t data_bytes, oracle_cuda_peer_group** out,
+                                                            void* ipc_handle_out) {
+    if (!ctx || !out || !ipc_handle_out) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (world < 1 || world > kMaxPeers || rank >= world)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                    "peer group needs 1 <= world <= " + std::to_string(kMaxPeers) + " and rank < world");
+    if (data_bytes == 0 || data_bytes % 16) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "gather data size must be a positive multiple of 16");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    auto* g = new oracle_cuda_peer_group();
+    g->ctx = ctx;
+    g->rank = rank;
+    g->world = world;
+    g->data_bytes = data_bytes;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&g->local), kGatherHeader + data_bytes);
+    if (e == cudaSuccess) e = cudaMemset(g->local, 0, kGatherHeader + data_bytes);
+    cudaIpcMemHandle_t h{};
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, g->local);
+    if (e != cudaSuccess) {
+        if (g->local) cudaFree(g->local);
+        delete g;
+        return cuda_fail(ctx, e, "peer group gather buffer");
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == ORACLE_CUDA_IPC_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(ipc_handle_out, &h, sizeof h);
+    g->mapped[rank] = g->local;
+    if (world == 1) g->connected = true;
+    *out = g;
+    return ok(ctx);
+}
+
+extern "C" oracle_cuda_status oracle_cuda_peer_group_connect(oracle_cuda_peer_group* g, const void* handles) {
+    if (!g || !handles) return fail(g ? g->ctx : nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "null argument");
+    oracle_cuda_context* ctx = g->ctx;
+    if (g->connected) return ok(ctx);
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const uint8_t* hb = static_cast<const uint8_t*>(handles);
+    for (uint32_t r = 0; r < g->world; ++r) {
+        if (r == g->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hb + size_t(r) * ORACLE_CUDA_IPC_HANDLE_BYTES, sizeof h);
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (uint32_t q = 0; q < r; ++q)
+                if (q != g->rank && g->mapped[q]) {
+                    cudaIpcCloseMemHandle(g->mapped[q]);
+                    g->mapped[q] = nullptr;
+                }
+            return cuda_fail(ctx, e, ("cudaIpcOpenMemHandle (rank " + std::to_string(r) + ")").c_str());
+        }
+        g->mapped[r] = static_cast<uint8_t*>(p);
+    }
+    g->connected = true;
+    return ok(ctx);
+}
+
+extern "C" oracle_cuda_status oracle_cuda_peer_group_data(oracle_cuda_peer_group* g, float** data_dev) {
+    if (!g || !data_dev) return fail(g ? g->ctx : nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "null argument");
+    *data_dev = reinterpret_cast<float*>(g->local + kGatherHeader);
+    return ok(g->ctx);
+}
+
+extern "C" oracle_cuda_status oracle_cuda_peer_group_destroy(oracle_cuda_peer_group* g) {
+    if (!g) return ORACLE_CUDA_OK;
+    cudaSetDevice(g->ctx->device);
+    cudaDeviceSynchronize();
+    for (uint32_t r = 0; r < g->world; ++r)
+        if (r != g->rank && g->mapped[r]) cudaIpcCloseMemHandle(g->mapped[r]);
+    if (g->local) cudaFree(g->local);
+    delete g;
+    return ORACLE_CUDA_OK;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_matvec_program_allgather(oracle_cuda_context* ctx,
+                                                                   oracle_cuda_peer_group* group,
+                                                                   const oracle_cuda_matvec_op* ops, uint32_t n_ops,
+                                                                   void* stream) {
+    if (!group) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "peer group is null");
+    return program_run(ctx, ops, n_ops, stream, group);
 }
 
 oracle_cuda_status oracle_cuda_weight_upload(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,

@@ -40,6 +40,26 @@ struct ProgramOp {
     uint32_t prebuilt;        // 1: the image was built by quantize_images_kernel
 };
 
+constexpr uint32_t kMaxPeers = 8;
+
+// Row-sharded programs over the GPUs of one node: every rank runs the same
+// program on its own row range of every op, and each CTA, after its last row,
+// copies its rows of every op into every peer's gather buffer at the same
+// offset (NVLink stores to IPC-mapped memory), so each rank ends the launch
+// holding every rank's rows.  Completion: each CTA then fences at system scope
+// and adds 1 to every peer's arrival counter; the last CTA of the grid waits (bounded)
+// until its own counter has received (world - 1) * gridDim.x arrivals for
+// this launch, counted against a local epoch.  world == 1: no exchange.
+struct PeerExchange {
+    uint32_t world;
+    uint32_t rank;
+    const float* local_base;                 // this rank's gather data region
+    float* peer_base[kMaxPeers];             // each rank's data region, mapped here
+    unsigned int* peer_counter[kMaxPeers];   // each rank's arrival counter, mapped here
+    unsigned int* my_counter;
+    unsigned int* my_epoch;                  // launches completed (local only)
+};
+
 struct ProgramParams {
     ProgramOp ops[kProgramMaxOps];
     uint32_t n_ops;
@@ -52,7 +72,18 @@ struct ProgramParams {
     uint32_t prebuilt_bytes; // bytes of the prebuilt region (multiple of 16)
     unsigned int* counters;  // kProgramMaxOps completion counters + 1 exit counter, zero at launch
     DeviceStatus* status;
+    PeerExchange px;
 };
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_sys_add(unsigned int* p, unsigned int v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 __device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
     unsigned int v;
@@ -88,7 +119,7 @@ template <int NCW, uint32_t kType, bool kXReg>
 __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* act, uint8_t* stage0,
                                                 uint32_t stage_bytes, uint32_t S, uint64_t* full, uint64_t* empty,
                                                 uint32_t& s, uint32_t& phase, bool& failed, DeviceStatus* status,
-                                                int warp, int lane) {
+                                                const PeerExchange& px, int warp, int lane) {
     const ActImage img = q8k_image(act + op.act_offset, op.nb);
     uint32_t xw[32];
     int xbs[8];
@@ -247,15 +278,15 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
         if (q4) {
             if (op.nb <= 16)
                 program_walk_op<NCW, 12, true>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
-                                               pp.status, warp, lane);
+                                               pp.status, pp.px, warp, lane);
             else
                 program_walk_op<NCW, 12, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
-                                                pp.status, warp, lane);
+                                                pp.status, pp.px, warp, lane);
         } else {
             // Q6_K ops re-read their activation slice per pass: the register-resident
             // variant does not fit beside the Q4_K code in 128 registers
             program_walk_op<NCW, 14, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
-                                            pp.status, warp, lane);
+                                            pp.status, pp.px, warp, lane);
         }
         if (op.publish) {
             // publish this CTA's completion of op k (its y rows are written)
@@ -266,6 +297,40 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             }
         }
     }
+    if (pp.px.world > 1) {
+        // push this CTA's rows of every op to every peer: each op's rows of this
+        // CTA are contiguous, so all consumer threads copy them with 16-byte
+        // stores where the alignment allows (NVLink writes to IPC-mapped memory)
+        named_barrier_sync(1, NCW * 32);
+        for (uint32_t k = 0; k < pp.n_ops; ++k) {
+            const ProgramOp& op = pp.ops[k];
+            const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
+            const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
+            const float* src = op.y + r0;
+            const size_t off = static_cast<size_t>(src - pp.px.local_base);
+            const uint32_t n = static_cast<uint32_t>(r1 - r0);
+            // floats before the first 16-byte boundary (same in every rank's buffer)
+            const uint32_t head = static_cast<uint32_t>((4u - ((reinterpret_cast<uintptr_t>(src) >> 2) & 3u)) & 3u);
+            const uint32_t h = head < n ? head : n;
+            const uint32_t nv = (n - h) / 4;
+#pragma unroll 1
+            for (uint32_t p = 0; p < pp.px.world; ++p) {
+                if (p == pp.px.rank) continue;
+                float* dst = pp.px.peer_base[p] + off;
+                for (uint32_t i = threadIdx.x; i < h; i += NCW * 32) dst[i] = __ldcg(src + i);
+                for (uint32_t i = threadIdx.x; i < nv; i += NCW * 32)
+                    reinterpret_cast<float4*>(dst + h)[i] = __ldcg(reinterpret_cast<const float4*>(src + h) + i);
+                for (uint32_t i = h + 4 * nv + threadIdx.x; i < n; i += NCW * 32) dst[i] = __ldcg(src + i);
+            }
+        }
+        named_barrier_sync(1, NCW * 32);
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+#pragma unroll
+            for (uint32_t p = 0; p < kMaxPeers; ++p)
+                if (p < pp.px.world && p != pp.px.rank) red_release_sys_add(pp.px.peer_counter[p], 1u);
+        }
+    }
     // The last CTA to finish zeroes the counters for the next launch.  A later
     // launch reads them only after its griddepcontrol.wait, i.e. after this
     // grid has completed.
@@ -273,8 +338,27 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
         __threadfence();
         const unsigned int done = atomicAdd(pp.counters + kProgramMaxOps, 1u);
         if (done == gridDim.x - 1) {
-            for (uint32_t k = 0; k < kProgramMaxOps; ++k) pp.counters[k] = 0u;
-            pp.counters[kProgramMaxOps] = 0u;
+            if (pp.px.world > 1) {
+                // every peer's rows of this launch have arrived once the counter
+                // reaches (epoch + 1) * (world - 1) * grid (wrap-safe compare)
+                const unsigned int epoch = *pp.px.my_epoch;
+                const unsigned int target = (epoch + 1u) * (pp.px.world - 1u) * gridDim.x;
+                const unsigned long long t0 = global_timer_ns();
+                bool ok = true;
+                while (static_cast<int>(ld_acquire_sys(pp.px.my_counter) - target) < 0) {
+                    if (global_timer_ns() - t0 > kWaitNs) {
+                        report_timeout(pp.status, 16);
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(128);
+                }
+                // a timed-out exchange still advances the epoch: the next launch
+                // then waits for its own arrivals, not for this one's stragglers
+                *pp.px.my_epoch = epoch + 1u;
+                (void)ok;
+            }
+            for (uint32_t k = 0; k <= kProgramMaxOps; ++k) pp.counters[k] = 0u;
             __threadfence();
         }
     }

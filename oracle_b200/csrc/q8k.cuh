@@ -206,6 +206,16 @@ struct ImageJobs {
     uint32_t n_jobs;
 };
 
+// One warp quantizes block `gw` of the jobs' concatenated blocks into its image.
+__device__ __forceinline__ void quantize_image_block(const ImageJobs& jobs, uint32_t gw, uint8_t* images, int lane) {
+    uint32_t j = 0;
+    while (gw >= jobs.first_block[j + 1]) ++j;
+    const uint32_t i = gw - jobs.first_block[j];
+    const float* xb = jobs.x[j] + 256ull * i;
+    const Q8KLane r = quantize_q8k_block_warp(xb, lane, (reinterpret_cast<uintptr_t>(xb) & 15u) == 0);
+    store_block_to_image(q8k_image(images + jobs.offset[j], jobs.nb[j]), i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
+}
+
 __global__ void __launch_bounds__(256) quantize_images_kernel(const __grid_constant__ ImageJobs jobs, uint8_t* images) {
     // The image buffer is reused by every program launch: wait until the
     // preceding kernel (possibly the previous program, still reading it) is
@@ -215,12 +225,7 @@ __global__ void __launch_bounds__(256) quantize_images_kernel(const __grid_const
     const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
     const int lane = threadIdx.x & 31;
     if (gw >= jobs.first_block[jobs.n_jobs]) return;
-    uint32_t j = 0;
-    while (gw >= jobs.first_block[j + 1]) ++j;
-    const uint32_t i = gw - jobs.first_block[j];
-    const float* xb = jobs.x[j] + 256ull * i;
-    const Q8KLane r = quantize_q8k_block_warp(xb, lane, (reinterpret_cast<uintptr_t>(xb) & 15u) == 0);
-    store_block_to_image(q8k_image(images + jobs.offset[j], jobs.nb[j]), i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
+    quantize_image_block(jobs, gw, images, lane);
 }
 
 // Load pre-quantized GGML Q8_K blocks (global) into the image.
