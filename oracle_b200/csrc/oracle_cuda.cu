@@ -795,9 +795,15 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         if (gs != ORACLE_CUDA_OK) return gs;
     }
     int types = 0;
-    for (uint32_t k = 0; k < n_ops; ++k) types |= ops[k].type == kTypeQ4_K ? 1 : 2;
+    bool short_rows = true;
+    for (uint32_t k = 0; k < n_ops; ++k) {
+        types |= ops[k].type == kTypeQ4_K ? 1 : 2;
+        short_rows = short_rows && ops[k].cols <= 16 * 256;
+    }
+    if (types == 2 && short_rows) types = 4;
     auto kernel = types == 1 ? matvec_program_kernel<kProgramWarps, 1>
                   : types == 2 ? matvec_program_kernel<kProgramWarps, 2>
+                  : types == 4 ? matvec_program_kernel<kProgramWarps, 4>
                                : matvec_program_kernel<kProgramWarps, 3>;
     oracle_cuda_status st = launch(ctx, kernel, dim3(grid), dim3((kProgramWarps + 1) * 32), smem,
                                    static_cast<cudaStream_t>(stream), (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, pp);

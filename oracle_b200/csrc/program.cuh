@@ -43,13 +43,14 @@ struct ProgramOp {
 constexpr uint32_t kMaxPeers = 8;
 
 // Row-sharded programs over the GPUs of one node: every rank runs the same
-// program on its own row range of every op, and each CTA, after its last row,
-// copies its rows of every op into every peer's gather buffer at the same
-// offset (NVLink stores to IPC-mapped memory), so each rank ends the launch
-// holding every rank's rows.  Completion: each CTA then fences at system scope
-// and adds 1 to every peer's arrival counter; the last CTA of the grid waits (bounded)
-// until its own counter has received (world - 1) * gridDim.x arrivals for
-// this launch, counted against a local epoch.  world == 1: no exchange.
+// program on its own row range of every op, and every output row is also
+// stored into every peer's gather buffer at the same offset as it is computed
+// (NVLink stores to IPC-mapped memory), so each rank ends the launch holding
+// every rank's rows.  Completion: the last CTA of the grid (which has
+// acquired every CTA's exit) fences at system scope, adds 1 to every peer's
+// arrival counter, and waits (bounded) until its own counter has received
+// world - 1 arrivals for this launch, counted against a local epoch.
+// world == 1: no exchange.
 struct PeerExchange {
     uint32_t world;
     uint32_t rank;
@@ -148,7 +149,16 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
             uint32_t j = warp >= static_cast<int>(owner_base) ? warp - owner_base : warp + NCW - owner_base;
             for (; j < n_here; j += NCW) {
                 const float v = q8k_row_dot<kType, kXReg>(op.nb, img, slot + j * rb, xw, xbs, xd, lane);
-                if (lane == 0) y[q_lo + j] = v;
+                if (lane == 0) {
+                    y[q_lo + j] = v;
+                    if (px.world > 1) {
+                        // the same row into every peer's gather buffer (NVLink store)
+                        const size_t off = static_cast<size_t>(y + q_lo + j - px.local_base);
+#pragma unroll
+                        for (uint32_t p = 0; p < kMaxPeers; ++p)
+                            if (p < px.world && p != px.rank) px.peer_base[p][off] = v;
+                    }
+                }
             }
         }
         __syncwarp();
@@ -162,7 +172,8 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
     }
 }
 
-// kTypes: 1 = every op is q4_K, 2 = every op is q6_K, 3 = mixed.
+// kTypes: 1 = every op is q4_K, 2 = every op is q6_K, 3 = mixed, 4 = every op is
+// q6_K with at most 16 super-blocks per row (activation slice in registers).
 template <int kWarps, int kTypes>
 __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(const __grid_constant__ ProgramParams pp) {
     constexpr int NCW = kWarps;
@@ -275,6 +286,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             named_barrier_sync(1, NCW * 32);
         }
         const bool q4 = kTypes == 1 || (kTypes == 3 && op.type == 12);
+        static_assert(kTypes >= 1 && kTypes <= 4, "program type set");
         if (q4) {
             if (op.nb <= 16)
                 program_walk_op<NCW, 12, true>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
@@ -282,9 +294,12 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             else
                 program_walk_op<NCW, 12, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                                 pp.status, pp.px, warp, lane);
+        } else if (kTypes == 4) {
+            program_walk_op<NCW, 14, true>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
+                                           pp.status, pp.px, warp, lane);
         } else {
-            // Q6_K ops re-read their activation slice per pass: the register-resident
-            // variant does not fit beside the Q4_K code in 128 registers
+            // in mixed programs Q6_K ops re-read their activation slice per pass: the
+            // register-resident variant does not fit beside the Q4_K code in 128 registers
             program_walk_op<NCW, 14, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                             pp.status, pp.px, warp, lane);
         }
@@ -297,40 +312,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             }
         }
     }
-    if (pp.px.world > 1) {
-        // push this CTA's rows of every op to every peer: each op's rows of this
-        // CTA are contiguous, so all consumer threads copy them with 16-byte
-        // stores where the alignment allows (NVLink writes to IPC-mapped memory)
-        named_barrier_sync(1, NCW * 32);
-        for (uint32_t k = 0; k < pp.n_ops; ++k) {
-            const ProgramOp& op = pp.ops[k];
-            const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
-            const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
-            const float* src = op.y + r0;
-            const size_t off = static_cast<size_t>(src - pp.px.local_base);
-            const uint32_t n = static_cast<uint32_t>(r1 - r0);
-            // floats before the first 16-byte boundary (same in every rank's buffer)
-            const uint32_t head = static_cast<uint32_t>((4u - ((reinterpret_cast<uintptr_t>(src) >> 2) & 3u)) & 3u);
-            const uint32_t h = head < n ? head : n;
-            const uint32_t nv = (n - h) / 4;
-#pragma unroll 1
-            for (uint32_t p = 0; p < pp.px.world; ++p) {
-                if (p == pp.px.rank) continue;
-                float* dst = pp.px.peer_base[p] + off;
-                for (uint32_t i = threadIdx.x; i < h; i += NCW * 32) dst[i] = __ldcg(src + i);
-                for (uint32_t i = threadIdx.x; i < nv; i += NCW * 32)
-                    reinterpret_cast<float4*>(dst + h)[i] = __ldcg(reinterpret_cast<const float4*>(src + h) + i);
-                for (uint32_t i = h + 4 * nv + threadIdx.x; i < n; i += NCW * 32) dst[i] = __ldcg(src + i);
-            }
-        }
-        named_barrier_sync(1, NCW * 32);
-        if (threadIdx.x == 0) {
-            __threadfence_system();
-#pragma unroll
-            for (uint32_t p = 0; p < kMaxPeers; ++p)
-                if (p < pp.px.world && p != pp.px.rank) red_release_sys_add(pp.px.peer_counter[p], 1u);
-        }
-    }
+    // every consumer warp's rows (and peer stores) precede this CTA's exit count
+    if (pp.px.world > 1) named_barrier_sync(1, NCW * 32);
     // The last CTA to finish zeroes the counters for the next launch.  A later
     // launch reads them only after its griddepcontrol.wait, i.e. after this
     // grid has completed.
@@ -339,10 +322,18 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
         const unsigned int done = atomicAdd(pp.counters + kProgramMaxOps, 1u);
         if (done == gridDim.x - 1) {
             if (pp.px.world > 1) {
-                // every peer's rows of this launch have arrived once the counter
-                // reaches (epoch + 1) * (world - 1) * grid (wrap-safe compare)
+                // Every CTA's rows (and their peer stores) happen before its
+                // exit-counter increment, which this thread acquired: after a
+                // system-scope fence, one release arrival per peer announces
+                // the whole grid's rows.  Every peer's rows of this launch have
+                // arrived once the own counter reaches (epoch + 1) * (world - 1)
+                // (wrap-safe compare).
+                __threadfence_system();
+#pragma unroll
+                for (uint32_t p = 0; p < kMaxPeers; ++p)
+                    if (p < pp.px.world && p != pp.px.rank) red_release_sys_add(pp.px.peer_counter[p], 1u);
                 const unsigned int epoch = *pp.px.my_epoch;
-                const unsigned int target = (epoch + 1u) * (pp.px.world - 1u) * gridDim.x;
+                const unsigned int target = (epoch + 1u) * (pp.px.world - 1u);
                 const unsigned long long t0 = global_timer_ns();
                 bool ok = true;
                 while (static_cast<int>(ld_acquire_sys(pp.px.my_counter) - target) < 0) {

@@ -328,6 +328,18 @@ def test_program_mixed_types(ctx, port):
         assert bits_equal(y.cpu().numpy(), w)
 
 
+@pytest.mark.parametrize("specs", [
+    [(ob.TYPE_Q6_K, 1000, 4096, 0), (ob.TYPE_Q6_K, 513, 768, 0), (ob.TYPE_Q6_K, 7, 256, 0)],  # short rows
+    [(ob.TYPE_Q6_K, 300, 8192, 0), (ob.TYPE_Q6_K, 77, 512, 0)]])                              # a long row
+def test_program_q6k_only(ctx, port, specs):
+    """Q6_K-only programs: register-resident activation slices when every row has <= 16 super-blocks."""
+    ops, want = _program_case(port, specs, f"prog_q6_{len(specs)}")
+    ctx.matvec_program(ops)
+    ctx.device_status()
+    for (_, _, _, _, _, y, _), w in zip(ops, want):
+        assert bits_equal(y.cpu().numpy(), w)
+
+
 def test_program_validation(ctx):
     w = to_dev(synth.weight(ob.TYPE_Q4_K, 4, 256, "gpu", "progval"))
     x = torch.zeros(256, dtype=torch.float32, device=DEV)
