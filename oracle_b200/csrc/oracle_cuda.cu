@@ -208,9 +208,11 @@ bool plan_stream(oracle_cuda_context* ctx, uint64_t rows, uint64_t row_bytes, ui
 }
 
 constexpr int kQ8KConsumerWarps = 16;
-// The program kernel carries both ops' code paths: with 15 consumer warps + 1
-// producer (4 warps per SM sub-partition) it may use 128 registers, unspilled.
-constexpr int kProgramWarps = 15;
+// The program kernel carries several ops' code paths and may use 128 registers
+// unspilled; 14 consumer warps + 1 producer take 61,440 of the SM's 65,536
+// registers, which leaves room for one warp of the next step's quantizer
+// (quantize_images_kernel, one warp per CTA) to run beside a program CTA.
+constexpr int kProgramWarps = 14;
 
 template <class Consumer>
 oracle_cuda_status launch_stream(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t row_bytes,
@@ -789,8 +791,9 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         oracle_cuda_status gs = grow_device(ctx, ctx->image_scratch, ctx->image_scratch_bytes, prebuilt);
         if (gs != ORACLE_CUDA_OK) return gs;
         pp.images = ctx->image_scratch;
-        const uint32_t qgrid = (blocks * 32 + 255) / 256;
-        gs = launch(ctx, quantize_images_kernel, dim3(qgrid), dim3(256), 0, static_cast<cudaStream_t>(stream),
+        // one warp per CTA: a warp fits beside a program CTA on every SM, so the
+        // quantizer starts the moment its predecessor completes
+        gs = launch(ctx, quantize_images_kernel, dim3(blocks), dim3(32), 0, static_cast<cudaStream_t>(stream),
                     (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, jobs, ctx->image_scratch);
         if (gs != ORACLE_CUDA_OK) return gs;
     }
