@@ -207,6 +207,33 @@ oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const or
 oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cuda_matvec_op* ops, uint32_t n_ops,
                                                       void* stream);
 
+/* ------------------------------------------------------------------ either side of the matvecs
+ * Embedding gather: out[t][0..cols) = the exact f32 decode of row ids[t] of a
+ * GGML table (rows x cols, device memory), for n_ids token ids in device
+ * memory; Oracle's embedding_row (src/runtime/qwen35_forward.cpp:51-70) for a
+ * batch.  An id >= rows is not read: its output row is left as it was and the
+ * next oracle_cuda_device_status reports OUT_OF_RANGE ("token id N exceeds the
+ * embedding row count").  Asynchronous on `stream`. */
+oracle_cuda_status oracle_cuda_gather_rows(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
+                                           const void* w_dev, uint64_t w_nbytes, const uint32_t* ids_dev,
+                                           uint64_t n_ids, float* out_dev, void* stream);
+
+/* Greedy token of Oracle's sampler (src/runtime/sampler.cpp:22-46): the first
+ * index of the largest logit.  oracle_cuda_argmax writes a 64-bit key to
+ * key_dev (zeroed on `stream` first; asynchronous, graph-capturable) for the
+ * n logits whose token ids start at index_base (a rank's shard of the vocabulary);
+ * oracle_cuda_argmax_decode turns a key into the token, failing like the
+ * reference (INVALID_ARGUMENT "logits contain NaN" / "logits contain no finite
+ * candidates").  Keys of several shards combine by taking their maximum, so the
+ * argmax of row-sharded logits needs only one key per rank.
+ * oracle_cuda_greedy_token is the synchronous form (empty input: "cannot
+ * sample an empty logits vector"). */
+oracle_cuda_status oracle_cuda_argmax(oracle_cuda_context* ctx, const float* x_dev, uint64_t n,
+                                      uint32_t index_base, unsigned long long* key_dev, void* stream);
+oracle_cuda_status oracle_cuda_argmax_decode(unsigned long long key, uint32_t* token, float* value);
+oracle_cuda_status oracle_cuda_greedy_token(oracle_cuda_context* ctx, const float* logits_dev, uint64_t n,
+                                            uint32_t* token);
+
 /* ------------------------------------------------------------------ row-sharded programs over GPUs
  * Tensor-parallel decode on the GPUs of one node, one process per GPU: every
  * rank holds an equal contiguous row range of each weight matrix and runs the

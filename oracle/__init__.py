@@ -209,6 +209,7 @@ class _Ref:
                                                   C.c_uint64, cp, sz]
         lib.oref_decode_mapped_tensor.argtypes = [C.c_uint32, _u64p, C.c_uint64, C.c_void_p,
                                                   C.c_uint64, _f32p, C.c_uint64, cp, sz]
+        lib.oref_greedy_token.argtypes = [_f32p, C.c_uint64, C.POINTER(C.c_uint32), cp, sz]
         self.lib = lib
 
     @staticmethod
@@ -238,6 +239,13 @@ class _Ref:
         self._check(self.lib.oref_decode_row(qtype, k, row.ctypes.data, row.size,
                                              _ptr(out, _f32p), out.size, err, 512), err)
         return out
+
+    def greedy_token(self, logits: np.ndarray) -> int:
+        """Oracle's Sampler::sample at temperature 0 (sampler.cpp:22-46)."""
+        logits = np.ascontiguousarray(logits, np.float32).reshape(-1)
+        out, err = C.c_uint32(), C.create_string_buffer(512)
+        self._check(self.lib.oref_greedy_token(_ptr(logits, _f32p), logits.size, C.byref(out), err, 512), err)
+        return int(out.value)
 
     def storage_dot(self, qtype: int, k: int, row: np.ndarray, x: np.ndarray) -> float:
         row = np.ascontiguousarray(row, np.uint8)

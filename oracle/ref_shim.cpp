@@ -3,7 +3,8 @@
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
 // the reference's unmodified sources, where they lie in the reference tree
 // (src/model/{ggml_type,storage_decode,mapped_gguf,gguf}.cpp,
-// src/backend/cpu/quantized_reference.cpp, src/core/mapped_file.cpp), into
+// src/backend/cpu/quantized_reference.cpp, src/core/mapped_file.cpp,
+// src/runtime/sampler.cpp), into
 // oracle/_ref/liboracle_ref.so.  Tests use it to pin the C restatement
 // (quant_oracle.c) and the CUDA path against the reference itself, and
 // bench.py's reference arm times reference_storage_matvec through it.
@@ -17,6 +18,7 @@
 #include "oracle/model/gguf.hpp"
 #include "oracle/model/mapped_gguf.hpp"
 #include "oracle/model/storage_decode.hpp"
+#include "oracle/runtime/sampler.hpp"
 
 #include <cstddef>
 #include <cstdint>
@@ -155,3 +157,13 @@ int oref_decode_mapped_tensor(std::uint32_t type, const std::uint64_t* dims, std
 }
 
 }  // extern "C"
+
+// Sampler::sample with the default configuration (temperature 0: greedy),
+// src/runtime/sampler.cpp:22-46.
+extern "C" int oref_greedy_token(const float* logits, std::uint64_t n, std::uint32_t* token, char* err,
+                                 std::size_t errlen) {
+    return guarded(err, errlen, [&] {
+        oracle::runtime::Sampler sampler{};
+        *token = sampler.sample(std::span<const float>(logits, static_cast<std::size_t>(n))).token_id;
+    });
+}

@@ -117,8 +117,19 @@ _proto("oracle_cuda_peer_group_connect", [_vp, _vp])
 _proto("oracle_cuda_peer_group_data", [_vp, C.POINTER(_vp)])
 _proto("oracle_cuda_peer_group_destroy", [_vp])
 _proto("oracle_cuda_matvec_program_allgather", [_vp, _vp, C.POINTER(MatvecOp), _u32, _vp])
+_proto("oracle_cuda_gather_rows", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _vp])
+_proto("oracle_cuda_argmax", [_vp, _vp, _u64, _u32, _vp, _vp])
+_proto("oracle_cuda_argmax_decode", [C.c_uint64, C.POINTER(_u32), C.POINTER(C.c_float)])
+_proto("oracle_cuda_greedy_token", [_vp, _vp, _u64, C.POINTER(_u32)])
 IPC_HANDLE_BYTES = 64
 MAX_PEERS = 8
+
+
+def argmax_decode(key: int) -> int:
+    """oracle_cuda_argmax_decode: token id of an argmax key (raises like Oracle's sampler)."""
+    t = _u32()
+    _raise(_lib.oracle_cuda_argmax_decode(key, C.byref(t), None), None)
+    return int(t.value)
 
 
 class _CudaArray:
@@ -365,6 +376,22 @@ class Context:
         for i, (qtype, rows, cols, w, x, y, after) in enumerate(ops):
             arr[i] = MatvecOp(qtype, 1 if after else 0, rows, cols, _addr(w), _nbytes(w), _addr(x), _addr(y))
         self._check(_lib.oracle_cuda_matvec_program(self._h, arr, len(ops), _stream(stream)))
+
+    def gather_rows(self, qtype, rows, cols, w, ids, out, stream=None, w_nbytes=None) -> None:
+        """oracle_cuda_gather_rows: out[t] = decode(row ids[t]) (device uint32 ids, f32 out)."""
+        self._check(_lib.oracle_cuda_gather_rows(self._h, qtype, rows, cols, _addr(w),
+                                                 _nbytes(w) if w_nbytes is None else w_nbytes, _addr(ids),
+                                                 _numel(ids), _addr(out), _stream(stream)))
+
+    def argmax(self, x, key, index_base=0, stream=None) -> None:
+        """oracle_cuda_argmax: the argmax key of device f32 x into device key (uint64 / int64 tensor)."""
+        self._check(_lib.oracle_cuda_argmax(self._h, _addr(x), _numel(x), index_base, _addr(key), _stream(stream)))
+
+    def greedy_token(self, logits) -> int:
+        """oracle_cuda_greedy_token: Oracle's greedy sampler on device logits."""
+        t = _u32()
+        self._check(_lib.oracle_cuda_greedy_token(self._h, _addr(logits), _numel(logits), C.byref(t)))
+        return int(t.value)
 
     def matvec_program_allgather(self, group: "PeerGroup", ops, stream=None) -> None:
         """oracle_cuda_matvec_program_allgather: the program on this rank's

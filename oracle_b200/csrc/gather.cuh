@@ -1,0 +1,110 @@
+// gather.cuh -- the steps either side of the matvecs: embedding-row gather and
+// greedy argmax over logits.
+//
+// gather_rows_kernel restates Oracle's embedding lookup (embedding_row,
+// src/runtime/qwen35_forward.cpp:51-70: bounds check of the token id, then
+// decode_storage_row of that row) for a batch of token ids held in device
+// memory; every element is Oracle's exact f32 decode (decode4).  A token id
+// outside the table is not read: the kernel records it in the status word
+// (kDevBadIndex) and leaves that output row untouched.
+//
+// argmax_kernel restates the greedy branch of Oracle's sampler
+// (src/runtime/sampler.cpp:22-46): the first index holding the largest value,
+// NaN anywhere is an error, a non-finite maximum is an error.  Each value maps
+// to a 64-bit key, (order-preserving bits of the value) << 32 | ~index, so
+// the largest key is the largest value at the lowest index; -0.0 counts as
+// +0.0 (the reference compares with `>`), and a NaN maps to the all-ones key,
+// which no number reaches.  Blocks reduce their keys and combine them with one
+// 64-bit atomicMax into a key the caller zeroed.
+#pragma once
+
+#include "decode.cuh"
+
+namespace oracle_cuda {
+
+enum : unsigned int { kDevBadIndex = 2 };
+
+template <uint32_t kType>
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint8_t* __restrict__ w, uint64_t rows, uint32_t k,
+                                                          uint64_t row_bytes, const uint32_t* __restrict__ ids,
+                                                          uint64_t n_ids, float* __restrict__ out,
+                                                          DeviceStatus* st) {
+    const uint32_t chunks = (k + 3) / 4;
+    const uint64_t total = n_ids * chunks;
+    for (uint64_t c = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; c < total;
+         c += uint64_t(gridDim.x) * blockDim.x) {
+        const uint64_t t = c / chunks;
+        const uint32_t e = static_cast<uint32_t>(c % chunks) * 4u;
+        const uint32_t id = __ldg(ids + t);
+        if (id >= rows) {
+            if (e == 0 && st && atomicCAS(&st->code, kDevOk, kDevBadIndex) == kDevOk) {
+                st->where = id;
+                st->block = static_cast<unsigned int>(t);
+            }
+            continue;
+        }
+        float v[4];
+        decode4<kType, true>(w + id * row_bytes, e, k, v);
+        float* o = out + t * k + e;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (e + q < k) o[q] = v[q];
+    }
+}
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
+    if (v != v) return ~0ull;  // NaN
+    uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);  // order-preserving
+    return (static_cast<unsigned long long>(b) << 32) | static_cast<unsigned long long>(~index);
+}
+
+__global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ x, uint64_t n, uint32_t index_base,
+                                                     unsigned long long* __restrict__ key_out) {
+    __shared__ unsigned long long warp_best[8];
+    unsigned long long best = 0;
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x) {
+        const unsigned long long k = argmax_key(__ldg(x + i), index_base + static_cast<uint32_t>(i));
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xFFFFFFFFu, best, off);
+        best = o > best ? o : best;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) warp_best[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = warp_best[w] > best ? warp_best[w] : best;
+        atomicMax(key_out, best);
+    }
+}
+
+// Host-side decode of an argmax key: token index and whether the maximum is
+// a finite number; `nan` when some value was NaN.
+struct ArgmaxResult {
+    uint32_t index;
+    bool nan;
+    bool finite;
+    float value;
+};
+
+inline ArgmaxResult decode_argmax_key(unsigned long long key) {
+    ArgmaxResult r{};
+    if (key == ~0ull) {
+        r.nan = true;
+        return r;
+    }
+    uint32_t b = static_cast<uint32_t>(key >> 32);
+    b = (b & 0x80000000u) ? (b & 0x7FFFFFFFu) : ~b;
+    float v;
+    static_assert(sizeof v == sizeof b, "float width");
+    memcpy(&v, &b, sizeof v);
+    r.value = v;
+    r.index = ~static_cast<uint32_t>(key & 0xFFFFFFFFull);
+    r.finite = v == v && v - v == 0.0f;
+    return r;
+}
+
+}  // namespace oracle_cuda

@@ -17,6 +17,7 @@
 #include <tuple>
 #include <vector>
 
+#include "gather.cuh"
 #include "gemm_q4k.cuh"
 #include "layout.hpp"
 #include "matvec_seq.cuh"
@@ -65,7 +66,8 @@ struct oracle_cuda_context {
     // prefill GEMM: bf16 copy of the activations
     uint16_t* gemm_x = nullptr;
     uint64_t gemm_x_len = 0;
-    bool gemm_pair = false;  // prefill GEMM on CTA pairs (cta_group::2); ORACLE_CUDA_GEMM_PAIR=1
+    bool gemm_pair = false;
+    unsigned long long* argmax_key = nullptr;  // one key for oracle_cuda_greedy_token  // prefill GEMM on CTA pairs (cta_group::2); ORACLE_CUDA_GEMM_PAIR=1
 };
 
 namespace {
@@ -527,6 +529,7 @@ oracle_cuda_status oracle_cuda_destroy(oracle_cuda_context* ctx) {
     if (ctx->program_counters) cudaFree(ctx->program_counters);
     if (ctx->image_scratch) cudaFree(ctx->image_scratch);
     if (ctx->gemm_x) cudaFree(ctx->gemm_x);
+    if (ctx->argmax_key) cudaFree(ctx->argmax_key);
     delete ctx;
     return ORACLE_CUDA_OK;
 }
@@ -549,6 +552,9 @@ oracle_cuda_status oracle_cuda_device_status(oracle_cuda_context* ctx) {
     if (st.code != kDevOk)  // an aborted program may have left its counters set
         ORACLE_CUDA_TRY(ctx, cudaMemset(ctx->program_counters, 0, (kProgramMaxOps + 1) * sizeof(unsigned int)),
                         "cudaMemset(program counters)");
+    if (st.code == kDevBadIndex)  // embedding_row (qwen35_forward.cpp:59-61)
+        return fail(ctx, ORACLE_CUDA_OUT_OF_RANGE,
+                    "token id " + std::to_string(st.where) + " exceeds the embedding row count");
     if (st.code != kDevOk)
         return fail(ctx, ORACLE_CUDA_DEVICE_TIMEOUT,
                     "kernel wait timed out at site " + std::to_string(st.where) + " in block " +
@@ -1363,4 +1369,102 @@ extern "C" oracle_cuda_status oracle_cuda_prefill_gemm(oracle_cuda_context* ctx,
     ORACLE_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, gemm_q4k_bf16_kernel<true>, tx, tw, gp), "kernel launch");
     ctx->launches += 1;
     return ORACLE_CUDA_OK;
+}
+
+// ---------------------------------------------------------------- embedding gather, greedy argmax
+
+namespace {
+
+template <uint32_t kType>
+oracle_cuda_status launch_gather_typed(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t cols,
+                                       uint64_t row_bytes, const uint32_t* ids, uint64_t n_ids, float* out,
+                                       cudaStream_t stream) {
+    const uint64_t total = n_ids * ((cols + 3) / 4);
+    uint64_t blocks = (total + 255) / 256;
+    const uint64_t cap = uint64_t(ctx->sm_count) * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return launch(ctx, gather_rows_kernel<kType>, dim3(static_cast<uint32_t>(blocks)), dim3(256), 0, stream, false, w,
+                  rows, static_cast<uint32_t>(cols), row_bytes, ids, n_ids, out, ctx->status);
+}
+
+}  // namespace
+
+extern "C" oracle_cuda_status oracle_cuda_gather_rows(oracle_cuda_context* ctx, uint32_t type, uint64_t rows,
+                                                      uint64_t cols, const void* w_dev, uint64_t w_nbytes,
+                                                      const uint32_t* ids_dev, uint64_t n_ids, float* out_dev,
+                                                      void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    uint64_t rb = 0, total = 0;
+    if (rows == 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "GGUF tensor must have at least one dimension");
+    if (Error e = row_byte_size(cols, type, &rb)) return fail(ctx, e);
+    if (!checked_mul(rows, rb, &total))
+        return fail(ctx, ORACLE_CUDA_OVERFLOW, "GGUF tensor byte size exceeds addressable size");
+    if (w_nbytes != total)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "GGUF tensor byte size does not match row geometry");
+    if (Error e = check_decodable(type)) return fail(ctx, e);
+    if (cols > 0xFFFFFFFFull || rows > 0xFFFFFFFFull)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "tables above 2^32 rows or columns");
+    if (Error e = check_weight_pointer(type, w_dev)) return fail(ctx, e);
+    if (n_ids == 0) return ok(ctx);
+    if (!ids_dev || !out_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "null token ids or output");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const uint8_t* wb = static_cast<const uint8_t*>(w_dev);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    oracle_cuda_status s;
+    switch (type) {
+        case kTypeF32: s = launch_gather_typed<0>(ctx, wb, rows, cols, rb, ids_dev, n_ids, out_dev, st); break;
+        case kTypeF16: s = launch_gather_typed<1>(ctx, wb, rows, cols, rb, ids_dev, n_ids, out_dev, st); break;
+        case kTypeBF16: s = launch_gather_typed<30>(ctx, wb, rows, cols, rb, ids_dev, n_ids, out_dev, st); break;
+        case kTypeQ8_0: s = launch_gather_typed<8>(ctx, wb, rows, cols, rb, ids_dev, n_ids, out_dev, st); break;
+        case kTypeQ4_K: s = launch_gather_typed<12>(ctx, wb, rows, cols, rb, ids_dev, n_ids, out_dev, st); break;
+        case kTypeQ5_K: s = launch_gather_typed<13>(ctx, wb, rows, cols, rb, ids_dev, n_ids, out_dev, st); break;
+        case kTypeQ6_K: s = launch_gather_typed<14>(ctx, wb, rows, cols, rb, ids_dev, n_ids, out_dev, st); break;
+        default: return fail(ctx, check_decodable(type));
+    }
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_argmax(oracle_cuda_context* ctx, const float* x_dev, uint64_t n,
+                                                 uint32_t index_base, unsigned long long* key_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (n == 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "cannot sample an empty logits vector");
+    if (n + index_base > 0xFFFFFFFFull)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "logits vector exceeds token-id range");
+    if (!x_dev || !key_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "null logits or key");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    ORACLE_CUDA_TRY(ctx, cudaMemsetAsync(key_dev, 0, sizeof(unsigned long long), st), "cudaMemsetAsync");
+    uint64_t blocks = (n + 255) / 256;
+    if (blocks > uint64_t(ctx->sm_count) * 4) blocks = uint64_t(ctx->sm_count) * 4;
+    const oracle_cuda_status s =
+        launch(ctx, argmax_kernel, dim3(static_cast<uint32_t>(blocks)), dim3(256), 0, st, false, x_dev, n, index_base,
+               key_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_argmax_decode(unsigned long long key, uint32_t* token, float* value) {
+    const ArgmaxResult r = decode_argmax_key(key);
+    if (r.nan) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "logits contain NaN");
+    if (!r.finite) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "logits contain no finite candidates");
+    if (token) *token = r.index;
+    if (value) *value = r.value;
+    return ORACLE_CUDA_OK;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_greedy_token(oracle_cuda_context* ctx, const float* logits_dev, uint64_t n,
+                                                       uint32_t* token) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (!token) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "token pointer is null");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (!ctx->argmax_key)
+        ORACLE_CUDA_TRY(ctx, cudaMalloc(reinterpret_cast<void**>(&ctx->argmax_key), sizeof(unsigned long long)),
+                        "cudaMalloc");
+    oracle_cuda_status s = oracle_cuda_argmax(ctx, logits_dev, n, 0, ctx->argmax_key, nullptr);
+    if (s != ORACLE_CUDA_OK) return s;
+    unsigned long long key = 0;
+    ORACLE_CUDA_TRY(ctx, cudaMemcpy(&key, ctx->argmax_key, sizeof key, cudaMemcpyDeviceToHost), "cudaMemcpy");
+    s = oracle_cuda_argmax_decode(key, token, nullptr);
+    if (s != ORACLE_CUDA_OK) return fail(ctx, s, oracle_cuda_last_error(nullptr));
+    return ok(ctx);
 }

@@ -82,3 +82,21 @@ def test_context_without_gpu_fails_loudly():
         pytest.skip("a GPU is present")
     with pytest.raises(ob.OracleCudaError):
         ob.Context(0)
+
+
+def test_argmax_key_decode_without_gpu():
+    """oracle_cuda_argmax_decode is host code: keys built by hand decode to the token, and the
+    NaN / non-finite keys fail with the messages of Oracle's sampler (sampler.cpp:33-43)."""
+    import struct
+
+    def key(value, index):
+        b = struct.unpack("<I", struct.pack("<f", value))[0]
+        b = (~b & 0xFFFFFFFF) if b & 0x80000000 else (b | 0x80000000)
+        return (b << 32) | (~index & 0xFFFFFFFF)
+
+    assert ob.argmax_decode(key(1.5, 7)) == 7
+    assert ob.argmax_decode(max(key(1.5, 7), key(1.5, 3), key(-2.0, 1))) == 3
+    with pytest.raises(ob.InvalidArgument, match="logits contain NaN"):
+        ob.argmax_decode(0xFFFFFFFFFFFFFFFF)
+    with pytest.raises(ob.InvalidArgument, match="no finite candidates"):
+        ob.argmax_decode(key(float("inf"), 0))
