@@ -57,21 +57,28 @@ def build_oracle() -> None:
 
 
 CPP_TEST = os.path.join(ROOT, "tests", "cpp", "adapter_test")
+CPP_GGUF_TEST = os.path.join(ROOT, "tests", "cpp", "gguf_test")
 
 
 def build_cpp_tests() -> None:
-    """The C++ adapter test (tests/cpp/adapter_test.cpp): compiled against
-    Oracle's headers, so only where the reference tree exists; the binary
-    travels with the repository snapshot."""
+    """The C++ tests (tests/cpp/adapter_test.cpp, gguf_test.cpp): compiled
+    against Oracle's headers, so only where the reference tree exists; the
+    binaries travel with the repository snapshot."""
     inc = os.path.join(REFERENCE_TREE, "include")
-    src = os.path.join(ROOT, "tests", "cpp", "adapter_test.cpp")
-    deps = [src, os.path.join(ROOT, "include", "oracle_cuda.hpp"), os.path.join(ROOT, "include", "oracle_cuda.h"), LIB]
-    if not os.path.isdir(inc) or not _stale(CPP_TEST, deps):
+    if not os.path.isdir(inc):
         return
     ref_dir = os.path.join(ROOT, "oracle", "_ref")
-    subprocess.run(["g++", "-std=c++20", "-O2", "-I", os.path.join(ROOT, "include"), "-I", inc, src, "-o", CPP_TEST,
-                    "-L", HERE, "-loracle_cuda", "-L", ref_dir, "-loracle_ref",
-                    "-Wl,-rpath,$ORIGIN/../../oracle_b200", "-Wl,-rpath,$ORIGIN/../../oracle/_ref"], check=True)
+    port_dir = os.path.join(ROOT, "oracle")
+    for binary, name in ((CPP_TEST, "adapter_test.cpp"), (CPP_GGUF_TEST, "gguf_test.cpp")):
+        src = os.path.join(ROOT, "tests", "cpp", name)
+        deps = [src, os.path.join(ROOT, "include", "oracle_cuda.hpp"), os.path.join(ROOT, "include", "oracle_cuda.h"),
+                LIB]
+        if not _stale(binary, deps):
+            continue
+        subprocess.run(["g++", "-std=c++20", "-O2", "-I", os.path.join(ROOT, "include"), "-I", inc, src, "-o", binary,
+                        "-L", HERE, "-loracle_cuda", "-L", ref_dir, "-loracle_ref", "-L", port_dir, "-loracle_port",
+                        "-Wl,-rpath,$ORIGIN/../../oracle_b200", "-Wl,-rpath,$ORIGIN/../../oracle/_ref",
+                        "-Wl,-rpath,$ORIGIN/../../oracle"], check=True)
 
 
 def build_all(force: bool = False) -> None:

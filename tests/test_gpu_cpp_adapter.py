@@ -22,3 +22,21 @@ def test_cpp_adapter_against_reference():
     r = subprocess.run([BINARY], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "all checks passed" in r.stdout
+
+
+def test_mapped_gguf_views_through_cpp_adapter(tmp_path):
+    """A GGUF file mapped by Oracle's own MappedGgufModel; every tensor view goes through the
+    C++ adapter and must match the reference's compiled functions (or the restatement for Q4_K)."""
+    import subprocess
+    import sys
+
+    binary = os.path.join(ROOT, "tests", "cpp", "gguf_test")
+    if not os.path.exists(binary):
+        pytest.skip("tests/cpp/gguf_test is built only where the reference tree exists")
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import make_gguf
+    path = str(tmp_path / "synthetic.gguf")
+    tensors = make_gguf.write(path)
+    r = subprocess.run([binary, path], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert f"{len(tensors) + 1} tensors, 0 failures" in r.stdout, r.stdout
