@@ -234,6 +234,46 @@ oracle_cuda_status oracle_cuda_argmax_decode(unsigned long long key, uint32_t* t
 oracle_cuda_status oracle_cuda_greedy_token(oracle_cuda_context* ctx, const float* logits_dev, uint64_t n,
                                             uint32_t* token);
 
+/* ------------------------------------------------------------------ decoder glue, one decode step
+ * Device-memory, stream-ordered restatements of Oracle's decoder helpers, same
+ * arithmetic (f32 / f64 as the reference; every product and sum rounded; the
+ * reference's order wherever it sums sequentially; double sums in a tree).
+ *   rms_norm_rows   rms_norm_rows, src/runtime/qwen35_block.cpp:161-188
+ *   rope            apply_qwen35_rope, src/runtime/reference_kernels.cpp:74-123
+ *                   (in place on heads [n_heads][head_dim]; cos/sin on the host
+ *                   by the reference's expressions)
+ *   attention_step  causal_attention_step, reference_kernels.cpp:125-190: appends
+ *                   k_new/v_new at `length` of a KV cache laid out as Oracle's
+ *                   (keys[token][kv_head][key_dim]); scores_dev holds
+ *                   q_heads * (length + 1) floats of scratch
+ *   conv_step       causal_depthwise_convolution_step, reference_kernels.cpp:192-219
+ *                   (history [channels][kernel], updated in place)
+ *   gated_delta_step gated_delta_step, reference_kernels.cpp:221-335 (state
+ *                   [heads][key_dim][value_dim], updated in place)
+ *   swiglu          silu(gate) * up, qwen35_block.cpp:138-159 and 315-318
+ *   add             add_vectors, qwen35_block.cpp:190-200 */
+oracle_cuda_status oracle_cuda_rms_norm_rows(oracle_cuda_context* ctx, const float* in_dev, const float* weight_dev,
+                                             uint64_t rows, uint64_t width, float eps, float* out_dev, void* stream);
+oracle_cuda_status oracle_cuda_rope(oracle_cuda_context* ctx, float* heads_dev, uint64_t n_heads, uint64_t head_dim,
+                                    uint64_t rotary_dim, const int32_t* sections, float base, uint64_t pos_temporal,
+                                    uint64_t pos_height, uint64_t pos_width, void* stream);
+oracle_cuda_status oracle_cuda_attention_step(oracle_cuda_context* ctx, const float* q_dev, const float* k_new_dev,
+                                              const float* v_new_dev, float* keys_dev, float* values_dev,
+                                              uint64_t capacity, uint64_t length, uint32_t q_heads,
+                                              uint32_t kv_heads, uint32_t key_dim, uint32_t value_dim,
+                                              float* scores_dev, float* out_dev, void* stream);
+oracle_cuda_status oracle_cuda_conv_step(oracle_cuda_context* ctx, const float* in_dev, const float* weights_dev,
+                                         float* history_dev, uint64_t channels, uint32_t kernel, int apply_silu,
+                                         float* out_dev, void* stream);
+oracle_cuda_status oracle_cuda_gated_delta_step(oracle_cuda_context* ctx, const float* q_dev, const float* k_dev,
+                                                const float* v_dev, const float* beta_dev, const float* log_decay_dev,
+                                                float* state_dev, uint32_t heads, uint32_t key_dim,
+                                                uint32_t value_dim, float eps, float* out_dev, void* stream);
+oracle_cuda_status oracle_cuda_swiglu(oracle_cuda_context* ctx, const float* gate_dev, const float* up_dev, uint64_t n,
+                                      float* out_dev, void* stream);
+oracle_cuda_status oracle_cuda_add(oracle_cuda_context* ctx, const float* a_dev, const float* b_dev, uint64_t n,
+                                   float* out_dev, void* stream);
+
 /* ------------------------------------------------------------------ row-sharded programs over GPUs
  * Tensor-parallel decode on the GPUs of one node, one process per GPU: every
  * rank holds an equal contiguous row range of each weight matrix and runs the

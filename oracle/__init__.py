@@ -77,6 +77,9 @@ class _Port:
                                               C.c_uint64, _f64p]
         lib.oq_gemm_sampled.argtypes = [C.c_uint32, C.c_uint64, C.c_uint64, _u8p, C.c_uint64,
                                         _f32p, C.c_uint64, _u64p, _u64p, C.c_int, _f64p]
+        lib.oq_rms_norm_rows.argtypes = [_f32p, _f32p, C.c_uint64, C.c_uint64, C.c_float, _f32p]
+        lib.oq_swiglu.argtypes = [_f32p, _f32p, C.c_uint64, _f32p]
+        lib.oq_swiglu.restype = None
         self.lib = lib
 
     def row_bytes(self, qtype: int, k: int) -> int:
@@ -171,6 +174,25 @@ class _Port:
         return out
 
 
+    def rms_norm_rows(self, x: np.ndarray, weight: np.ndarray, eps: float) -> np.ndarray:
+        """Oracle's rms_norm_rows (qwen35_block.cpp:161-188); x is rows x width."""
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(weight, np.float32).reshape(-1)
+        out = np.empty_like(x)
+        rc = self.lib.oq_rms_norm_rows(_ptr(x, _f32p), _ptr(w, _f32p), x.size // w.size, w.size, eps, _ptr(out, _f32p))
+        if rc:
+            raise ValueError(f"oq_rms_norm_rows failed with {rc}")
+        return out
+
+    def swiglu(self, gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+        """silu(gate) * up as Oracle's FFN computes it (qwen35_block.cpp:315-318)."""
+        g = np.ascontiguousarray(gate, np.float32).reshape(-1)
+        u = np.ascontiguousarray(up, np.float32).reshape(-1)
+        out = np.empty_like(g)
+        self.lib.oq_swiglu(_ptr(g, _f32p), _ptr(u, _f32p), g.size, _ptr(out, _f32p))
+        return out
+
+
 class ReferenceError_(Exception):
     """An exception the reference raised, carried across the C shim."""
 
@@ -210,6 +232,13 @@ class _Ref:
         lib.oref_decode_mapped_tensor.argtypes = [C.c_uint32, _u64p, C.c_uint64, C.c_void_p,
                                                   C.c_uint64, _f32p, C.c_uint64, cp, sz]
         lib.oref_greedy_token.argtypes = [_f32p, C.c_uint64, C.POINTER(C.c_uint32), cp, sz]
+        u64 = C.c_uint64
+        lib.oref_rope.argtypes = [_f32p, u64, u64, u64, C.POINTER(C.c_int32), C.c_float, u64, u64, u64, cp, sz]
+        lib.oref_attention_step.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, u64, u64, u64, u64, u64, u64, _f32p,
+                                            cp, sz]
+        lib.oref_conv_step.argtypes = [_f32p, _f32p, _f32p, u64, u64, C.c_int, _f32p, cp, sz]
+        lib.oref_gated_delta_step.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, u64, u64, u64, C.c_float,
+                                              _f32p, cp, sz]
         self.lib = lib
 
     @staticmethod
@@ -239,6 +268,57 @@ class _Ref:
         self._check(self.lib.oref_decode_row(qtype, k, row.ctypes.data, row.size,
                                              _ptr(out, _f32p), out.size, err, 512), err)
         return out
+
+    def rope(self, heads: np.ndarray, rotary_dim: int, sections, base: float, position) -> np.ndarray:
+        """apply_qwen35_rope (reference_kernels.cpp:74-123) on a copy of heads [n x head_dim]."""
+        h = np.array(heads, np.float32, copy=True)
+        sec = (C.c_int32 * 4)(*sections)
+        err = C.create_string_buffer(512)
+        pt, ph, pw = position
+        self._check(self.lib.oref_rope(_ptr(h, _f32p), h.shape[0], h.shape[1], rotary_dim, sec, base, pt, ph, pw,
+                                       err, 512), err)
+        return h
+
+    def attention_step(self, q, k_new, v_new, keys, values, capacity) -> np.ndarray:
+        """causal_attention_step (reference_kernels.cpp:125-190) after `len(keys)` cached tokens."""
+        q, k_new, v_new = (np.ascontiguousarray(a, np.float32) for a in (q, k_new, v_new))
+        keys = np.ascontiguousarray(keys, np.float32)
+        values = np.ascontiguousarray(values, np.float32)
+        hq, dk = q.shape
+        hkv, dv = v_new.shape
+        out = np.empty((hq, dv), np.float32)
+        err = C.create_string_buffer(512)
+        self._check(self.lib.oref_attention_step(_ptr(q, _f32p), _ptr(k_new, _f32p), _ptr(v_new, _f32p),
+                                                 _ptr(keys, _f32p), _ptr(values, _f32p), keys.shape[0], capacity,
+                                                 hq, hkv, dk, dv, _ptr(out, _f32p), err, 512), err)
+        return out
+
+    def conv_step(self, x, weights, history, apply_silu=True):
+        """causal_depthwise_convolution_step (reference_kernels.cpp:192-219): (out, new history)."""
+        x = np.ascontiguousarray(x, np.float32).reshape(-1)
+        w = np.ascontiguousarray(weights, np.float32)
+        hist = np.array(history, np.float32, copy=True)
+        out = np.empty_like(x)
+        err = C.create_string_buffer(512)
+        self._check(self.lib.oref_conv_step(_ptr(x, _f32p), _ptr(w, _f32p), _ptr(hist, _f32p), x.size,
+                                            hist.size // x.size, 1 if apply_silu else 0, _ptr(out, _f32p), err, 512),
+                    err)
+        return out, hist
+
+    def gated_delta_step(self, q, k, v, beta, log_decay, state, eps=1e-6):
+        """gated_delta_step (reference_kernels.cpp:221-335): (out, new state)."""
+        q, k, v = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+        b = np.ascontiguousarray(beta, np.float32)
+        g = np.ascontiguousarray(log_decay, np.float32)
+        st = np.array(state, np.float32, copy=True)
+        heads, dk = q.shape
+        dv = v.shape[1]
+        out = np.empty((heads, dv), np.float32)
+        err = C.create_string_buffer(512)
+        self._check(self.lib.oref_gated_delta_step(_ptr(q, _f32p), _ptr(k, _f32p), _ptr(v, _f32p), _ptr(b, _f32p),
+                                                   _ptr(g, _f32p), _ptr(st, _f32p), heads, dk, dv, eps,
+                                                   _ptr(out, _f32p), err, 512), err)
+        return out, st
 
     def greedy_token(self, logits: np.ndarray) -> int:
         """Oracle's Sampler::sample at temperature 0 (sampler.cpp:22-46)."""

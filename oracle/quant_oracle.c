@@ -480,3 +480,35 @@ int oq_gemm_sampled(uint32_t type, uint64_t n, uint64_t k, const uint8_t* w, uin
     free(dec);
     return OQ_OK;
 }
+
+/* qwen35_block.cpp:161-188 */
+int oq_rms_norm_rows(const float* in, const float* weight, uint64_t rows, uint64_t width, float eps, float* out) {
+    if (width == 0 || !(eps > 0.0f)) return OQ_EINVAL;
+    for (uint64_t r = 0; r < rows; ++r) {
+        const float* x = in + r * width;
+        double sum = 0.0;
+        for (uint64_t c = 0; c < width; ++c) {
+            const double v = (double)x[c];
+            sum += v * v;
+        }
+        const double mean = sum / (double)width;
+        const float inv = (float)(1.0 / sqrt(mean + (double)eps));
+        for (uint64_t c = 0; c < width; ++c) out[r * width + c] = x[c] * inv * weight[c];
+    }
+    return OQ_OK;
+}
+
+/* qwen35_block.cpp:138-145 */
+static float oq_sigmoid(float v) {
+    if (v >= 0.0f) {
+        const float e = expf(-v);
+        return 1.0f / (1.0f + e);
+    }
+    const float e = expf(v);
+    return e / (1.0f + e);
+}
+
+/* qwen35_block.cpp:157-159, 315-318 */
+void oq_swiglu(const float* gate, const float* up, uint64_t n, float* out) {
+    for (uint64_t i = 0; i < n; ++i) out[i] = gate[i] * oq_sigmoid(gate[i]) * up[i];
+}

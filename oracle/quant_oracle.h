@@ -116,6 +116,14 @@ int oq_gemm_sampled(uint32_t type, uint64_t n, uint64_t k, const uint8_t* w, uin
                     const float* x, uint64_t count, const uint64_t* m_index,
                     const uint64_t* n_index, int mode, double* y);
 
+/* Decoder glue restated from Oracle's block code (anonymous-namespace
+ * helpers of src/runtime/qwen35_block.cpp, not linkable):
+ *   rms_norm_rows (:161-188): per row, sum of squares in double, inverse RMS
+ *   as float(1 / sqrt(mean + eps)), out = (x * inv) * w in float;
+ *   swiglu (:138-159, :315-318): silu(gate) * up with the two-branch sigmoid. */
+int oq_rms_norm_rows(const float* in, const float* weight, uint64_t rows, uint64_t width, float eps, float* out);
+void oq_swiglu(const float* gate, const float* up, uint64_t n, float* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -3,8 +3,9 @@
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
 // the reference's unmodified sources, where they lie in the reference tree
 // (src/model/{ggml_type,storage_decode,mapped_gguf,gguf}.cpp,
-// src/backend/cpu/quantized_reference.cpp, src/core/mapped_file.cpp,
-// src/runtime/sampler.cpp), into
+// src/backend/cpu/quantized_reference.cpp, src/core/{mapped_file,tensor}.cpp,
+// src/runtime/{sampler,reference_kernels,hybrid_cache}.cpp,
+// src/model/qwen35_manifest.cpp), into
 // oracle/_ref/liboracle_ref.so.  Tests use it to pin the C restatement
 // (quant_oracle.c) and the CUDA path against the reference itself, and
 // bench.py's reference arm times reference_storage_matvec through it.
@@ -18,8 +19,10 @@
 #include "oracle/model/gguf.hpp"
 #include "oracle/model/mapped_gguf.hpp"
 #include "oracle/model/storage_decode.hpp"
+#include "oracle/runtime/reference_kernels.hpp"
 #include "oracle/runtime/sampler.hpp"
 
+#include <algorithm>
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
@@ -165,5 +168,86 @@ extern "C" int oref_greedy_token(const float* logits, std::uint64_t n, std::uint
     return guarded(err, errlen, [&] {
         oracle::runtime::Sampler sampler{};
         *token = sampler.sample(std::span<const float>(logits, static_cast<std::size_t>(n))).token_id;
+    });
+}
+
+// ---------------------------------------------------------------- decoder kernels (reference_kernels.cpp)
+
+namespace {
+
+oracle::core::Tensor tensor_from(const float* data, std::size_t rows, std::size_t cols) {
+    oracle::core::Tensor t({rows, cols});
+    std::copy(data, data + rows * cols, t.data().begin());
+    return t;
+}
+
+}  // namespace
+
+// apply_qwen35_rope (reference_kernels.cpp:74-123) on heads [n_heads x head_dim], in place.
+extern "C" int oref_rope(float* heads, std::uint64_t n_heads, std::uint64_t head_dim, std::uint64_t rotary_dim,
+                         const std::int32_t* sections, float base, std::uint64_t pos_t, std::uint64_t pos_h,
+                         std::uint64_t pos_w, char* err, std::size_t errlen) {
+    return guarded(err, errlen, [&] {
+        auto t = tensor_from(heads, n_heads, head_dim);
+        oracle::runtime::apply_qwen35_rope(t, {pos_t, pos_h, pos_w}, rotary_dim,
+                                           {sections[0], sections[1], sections[2], sections[3]}, base);
+        std::copy(t.data().begin(), t.data().end(), heads);
+    });
+}
+
+// causal_attention_step (reference_kernels.cpp:125-190): a KV cache holding
+// `length` earlier tokens (keys/values [length][kv_heads][dim]), one new token
+// appended, attention of q [q_heads x key_dim] over all of them.
+extern "C" int oref_attention_step(const float* q, const float* k_new, const float* v_new, const float* keys,
+                                   const float* values, std::uint64_t length, std::uint64_t capacity,
+                                   std::uint64_t q_heads, std::uint64_t kv_heads, std::uint64_t key_dim,
+                                   std::uint64_t value_dim, float* out, char* err, std::size_t errlen) {
+    return guarded(err, errlen, [&] {
+        oracle::runtime::KvCache cache(capacity, kv_heads, key_dim, value_dim);
+        for (std::uint64_t t = 0; t < length; ++t)
+            cache.append(std::span<const float>(keys + t * kv_heads * key_dim, kv_heads * key_dim),
+                         std::span<const float>(values + t * kv_heads * value_dim, kv_heads * value_dim));
+        auto tq = tensor_from(q, q_heads, key_dim);
+        auto tk = tensor_from(k_new, kv_heads, key_dim);
+        auto tv = tensor_from(v_new, kv_heads, value_dim);
+        oracle::core::Tensor to({q_heads, value_dim});
+        oracle::runtime::causal_attention_step(tq, tk, tv, cache, to);
+        std::copy(to.data().begin(), to.data().end(), out);
+    });
+}
+
+// causal_depthwise_convolution_step (reference_kernels.cpp:192-219); history
+// [channels][kernel] in and out.
+extern "C" int oref_conv_step(const float* in, const float* weights, float* history, std::uint64_t channels,
+                              std::uint64_t kernel, int apply_silu, float* out, char* err, std::size_t errlen) {
+    return guarded(err, errlen, [&] {
+        oracle::runtime::SsmState state(channels, kernel, 1, 1, 1);
+        auto h = state.convolution_history();
+        std::copy(history, history + channels * kernel, h.begin());
+        oracle::runtime::causal_depthwise_convolution_step(std::span<const float>(in, channels),
+                                                           std::span<const float>(weights, channels * kernel), state,
+                                                           std::span<float>(out, channels), apply_silu != 0);
+        std::copy(h.begin(), h.end(), history);
+    });
+}
+
+// gated_delta_step (reference_kernels.cpp:221-335); recurrent state
+// [heads][key_dim][value_dim] in and out.
+extern "C" int oref_gated_delta_step(const float* q, const float* k, const float* v, const float* beta,
+                                     const float* log_decay, float* state_io, std::uint64_t heads,
+                                     std::uint64_t key_dim, std::uint64_t value_dim, float eps, float* out, char* err,
+                                     std::size_t errlen) {
+    return guarded(err, errlen, [&] {
+        oracle::runtime::SsmState state(1, 1, heads, key_dim, value_dim);
+        auto r = state.recurrent();
+        std::copy(state_io, state_io + heads * key_dim * value_dim, r.begin());
+        auto tq = tensor_from(q, heads, key_dim);
+        auto tk = tensor_from(k, heads, key_dim);
+        auto tv = tensor_from(v, heads, value_dim);
+        oracle::core::Tensor to({heads, value_dim});
+        oracle::runtime::gated_delta_step(tq, tk, tv, std::span<const float>(beta, heads),
+                                          std::span<const float>(log_decay, heads), state, to, eps);
+        std::copy(to.data().begin(), to.data().end(), out);
+        std::copy(r.begin(), r.end(), state_io);
     });
 }

@@ -121,6 +121,14 @@ _proto("oracle_cuda_gather_rows", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, 
 _proto("oracle_cuda_argmax", [_vp, _vp, _u64, _u32, _vp, _vp])
 _proto("oracle_cuda_argmax_decode", [C.c_uint64, C.POINTER(_u32), C.POINTER(C.c_float)])
 _proto("oracle_cuda_greedy_token", [_vp, _vp, _u64, C.POINTER(_u32)])
+_proto("oracle_cuda_rms_norm_rows", [_vp, _vp, _vp, _u64, _u64, C.c_float, _vp, _vp])
+_proto("oracle_cuda_rope", [_vp, _vp, _u64, _u64, _u64, C.POINTER(C.c_int32), C.c_float, _u64, _u64, _u64, _vp])
+_proto("oracle_cuda_attention_step", [_vp, _vp, _vp, _vp, _vp, _vp, _u64, _u64, _u32, _u32, _u32, _u32, _vp, _vp,
+                                      _vp])
+_proto("oracle_cuda_conv_step", [_vp, _vp, _vp, _vp, _u64, _u32, _i32, _vp, _vp])
+_proto("oracle_cuda_gated_delta_step", [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, C.c_float, _vp, _vp])
+_proto("oracle_cuda_swiglu", [_vp, _vp, _vp, _u64, _vp, _vp])
+_proto("oracle_cuda_add", [_vp, _vp, _vp, _u64, _vp, _vp])
 IPC_HANDLE_BYTES = 64
 MAX_PEERS = 8
 
@@ -392,6 +400,39 @@ class Context:
         t = _u32()
         self._check(_lib.oracle_cuda_greedy_token(self._h, _addr(logits), _numel(logits), C.byref(t)))
         return int(t.value)
+
+    # -------------------------------------------------------------- decoder glue
+    def rms_norm_rows(self, x, weight, rows, width, eps, out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_rms_norm_rows(self._h, _addr(x), _addr(weight), rows, width, eps, _addr(out),
+                                                   _stream(stream)))
+
+    def rope(self, heads, n_heads, head_dim, rotary_dim, sections, base, position, stream=None) -> None:
+        sec = (C.c_int32 * 4)(*sections)
+        pt, ph, pw = position
+        self._check(_lib.oracle_cuda_rope(self._h, _addr(heads), n_heads, head_dim, rotary_dim, sec, base, pt, ph, pw,
+                                          _stream(stream)))
+
+    def attention_step(self, q, k_new, v_new, keys, values, capacity, length, q_heads, kv_heads, key_dim, value_dim,
+                       scores, out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_attention_step(self._h, _addr(q), _addr(k_new), _addr(v_new), _addr(keys),
+                                                    _addr(values), capacity, length, q_heads, kv_heads, key_dim,
+                                                    value_dim, _addr(scores), _addr(out), _stream(stream)))
+
+    def conv_step(self, x, weights, history, channels, kernel, apply_silu, out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_conv_step(self._h, _addr(x), _addr(weights), _addr(history), channels, kernel,
+                                               1 if apply_silu else 0, _addr(out), _stream(stream)))
+
+    def gated_delta_step(self, q, k, v, beta, log_decay, state, heads, key_dim, value_dim, eps, out,
+                         stream=None) -> None:
+        self._check(_lib.oracle_cuda_gated_delta_step(self._h, _addr(q), _addr(k), _addr(v), _addr(beta),
+                                                      _addr(log_decay), _addr(state), heads, key_dim, value_dim, eps,
+                                                      _addr(out), _stream(stream)))
+
+    def swiglu(self, gate, up, n, out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_swiglu(self._h, _addr(gate), _addr(up), n, _addr(out), _stream(stream)))
+
+    def add(self, a, b, n, out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_add(self._h, _addr(a), _addr(b), n, _addr(out), _stream(stream)))
 
     def matvec_program_allgather(self, group: "PeerGroup", ops, stream=None) -> None:
         """oracle_cuda_matvec_program_allgather: the program on this rank's

@@ -8,6 +8,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -17,6 +18,7 @@
 #include <tuple>
 #include <vector>
 
+#include "decoder_ops.cuh"
 #include "gather.cuh"
 #include "gemm_q4k.cuh"
 #include "layout.hpp"
@@ -552,6 +554,8 @@ oracle_cuda_status oracle_cuda_device_status(oracle_cuda_context* ctx) {
     if (st.code != kDevOk)  // an aborted program may have left its counters set
         ORACLE_CUDA_TRY(ctx, cudaMemset(ctx->program_counters, 0, (kProgramMaxOps + 1) * sizeof(unsigned int)),
                         "cudaMemset(program counters)");
+    if (st.code == 3u)  // causal_attention_step (reference_kernels.cpp:170-172)
+        return fail(ctx, ORACLE_CUDA_RUNTIME_ERROR, "causal attention softmax normalization failed");
     if (st.code == kDevBadIndex)  // embedding_row (qwen35_forward.cpp:59-61)
         return fail(ctx, ORACLE_CUDA_OUT_OF_RANGE,
                     "token id " + std::to_string(st.where) + " exceeds the embedding row count");
@@ -1467,4 +1471,162 @@ extern "C" oracle_cuda_status oracle_cuda_greedy_token(oracle_cuda_context* ctx,
     s = oracle_cuda_argmax_decode(key, token, nullptr);
     if (s != ORACLE_CUDA_OK) return fail(ctx, s, oracle_cuda_last_error(nullptr));
     return ok(ctx);
+}
+
+// ---------------------------------------------------------------- decoder glue (decoder_ops.cuh)
+
+namespace {
+
+uint32_t grid_for(uint64_t n, int sm_count) {
+    uint64_t b = (n + 255) / 256;
+    const uint64_t cap = uint64_t(sm_count) * 16;
+    if (b > cap) b = cap;
+    return static_cast<uint32_t>(b < 1 ? 1 : b);
+}
+
+// position_for_frequency (reference_kernels.cpp:28-40)
+uint64_t rope_coordinate(size_t f, uint64_t pt, uint64_t ph, uint64_t pw, const int32_t* sections) {
+    const size_t height_count = static_cast<size_t>(sections[1]);
+    const size_t width_count = static_cast<size_t>(sections[2]);
+    if (f % 3u == 1u && f / 3u < height_count) return ph;
+    if (f % 3u == 2u && f / 3u < width_count) return pw;
+    return pt;
+}
+
+}  // namespace
+
+extern "C" oracle_cuda_status oracle_cuda_rms_norm_rows(oracle_cuda_context* ctx, const float* in_dev,
+                                                        const float* weight_dev, uint64_t rows, uint64_t width,
+                                                        float eps, float* out_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (width == 0 || rows == 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Qwen3.5 RMSNorm dimensions are incompatible");
+    if (!(eps > 0.0f) || !std::isfinite(eps))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Qwen3.5 RMSNorm epsilon must be positive and finite");
+    if (rows > 0x7FFFFFFFull || width > 0xFFFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "RMSNorm shape too large");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s = launch(ctx, rms_norm_rows_kernel, dim3(static_cast<uint32_t>(rows)), dim3(256), 0,
+                                        static_cast<cudaStream_t>(stream), false, in_dev, weight_dev,
+                                        static_cast<uint32_t>(width), eps, out_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_rope(oracle_cuda_context* ctx, float* heads_dev, uint64_t n_heads,
+                                               uint64_t head_dim, uint64_t rotary_dim, const int32_t* sections,
+                                               float base, uint64_t pos_temporal, uint64_t pos_height,
+                                               uint64_t pos_width, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    // apply_qwen35_rope's checks (reference_kernels.cpp:79-99), same messages
+    if (rotary_dim == 0 || rotary_dim % 2 != 0 || rotary_dim > head_dim)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE dimension must be non-zero, even, and within head width");
+    if (!(base > 0.0f) || !std::isfinite(base))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE frequency base must be positive and finite");
+    if (!sections) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE sections pointer is null");
+    int64_t section_sum = 0;
+    for (int i = 0; i < 4; ++i) {
+        if (sections[i] < 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE dimension sections must be non-negative");
+        section_sum += sections[i];
+    }
+    if (section_sum != static_cast<int64_t>(rotary_dim / 2))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE dimension sections must sum to half the rotary dimension");
+    if (rotary_dim / 2 > kRopeMaxHalf || n_heads * (rotary_dim / 2) > 0xFFFFFFFFull)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "rotary dimension above 256");
+    // the cos/sin table, by the reference's own expressions (reference_kernels.cpp:104-113)
+    RopeTable t{};
+    t.half = static_cast<uint32_t>(rotary_dim / 2);
+    for (size_t f = 0; f < t.half; ++f) {
+        const double exponent = (2.0 * static_cast<double>(f)) / static_cast<double>(rotary_dim);
+        const double inverse_frequency = 1.0 / std::pow(base, exponent);
+        const uint64_t coordinate = rope_coordinate(f, pos_temporal, pos_height, pos_width, sections);
+        const double angle = static_cast<double>(coordinate) * inverse_frequency;
+        t.cosv[f] = static_cast<float>(std::cos(angle));
+        t.sinv[f] = static_cast<float>(std::sin(angle));
+    }
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const uint64_t n = n_heads * t.half;
+    const oracle_cuda_status s = launch(ctx, rope_kernel, dim3(static_cast<uint32_t>((n + 255) / 256)), dim3(256), 0,
+                                        static_cast<cudaStream_t>(stream), false, heads_dev,
+                                        static_cast<uint32_t>(n_heads), static_cast<uint32_t>(head_dim), t);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_attention_step(oracle_cuda_context* ctx, const float* q_dev,
+                                                         const float* k_new_dev, const float* v_new_dev,
+                                                         float* keys_dev, float* values_dev, uint64_t capacity,
+                                                         uint64_t length, uint32_t q_heads, uint32_t kv_heads,
+                                                         uint32_t key_dim, uint32_t value_dim, float* scores_dev,
+                                                         float* out_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (kv_heads == 0 || q_heads % kv_heads != 0 || key_dim == 0 || value_dim == 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "causal_attention_step dimensions are incompatible");
+    if (length >= capacity) return fail(ctx, ORACLE_CUDA_OVERFLOW, "KV cache capacity exceeded");
+    if (length + 1 > 0xFFFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "attention over more than 2^32 tokens");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const uint32_t tokens = static_cast<uint32_t>(length + 1);
+    const uint32_t nk = kv_heads * key_dim, nv = kv_heads * value_dim;
+    oracle_cuda_status s = launch(ctx, attention_append_kernel, dim3(grid_for(nk + nv, ctx->sm_count)), dim3(256), 0,
+                                  st, false, k_new_dev, v_new_dev, keys_dev, values_dev, length, nk, nv);
+    if (s != ORACLE_CUDA_OK) return s;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(key_dim));
+    const uint64_t warps = uint64_t(q_heads) * tokens;
+    s = launch(ctx, attention_scores_kernel, dim3(static_cast<uint32_t>((warps * 32 + 255) / 256)), dim3(256), 0, st,
+               false, q_dev, static_cast<const float*>(keys_dev), tokens, q_heads, kv_heads, key_dim, scale,
+               scores_dev);
+    if (s != ORACLE_CUDA_OK) return s;
+    s = launch(ctx, attention_output_kernel, dim3(q_heads), dim3(256), 0, st, false, scores_dev,
+               static_cast<const float*>(values_dev), tokens, q_heads, kv_heads, value_dim, out_dev, ctx->status);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_conv_step(oracle_cuda_context* ctx, const float* in_dev,
+                                                    const float* weights_dev, float* history_dev, uint64_t channels,
+                                                    uint32_t kernel, int apply_silu, float* out_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (channels == 0 || kernel == 0 || channels > 0xFFFFFFFFull)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "depthwise convolution dimensions do not match SSM state");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s = launch(ctx, conv_step_kernel, dim3(static_cast<uint32_t>((channels + 255) / 256)),
+                                        dim3(256), 0, static_cast<cudaStream_t>(stream), false, in_dev, weights_dev,
+                                        history_dev, static_cast<uint32_t>(channels), kernel, apply_silu, out_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_gated_delta_step(oracle_cuda_context* ctx, const float* q_dev,
+                                                           const float* k_dev, const float* v_dev,
+                                                           const float* beta_dev, const float* log_decay_dev,
+                                                           float* state_dev, uint32_t heads, uint32_t key_dim,
+                                                           uint32_t value_dim, float eps, float* out_dev,
+                                                           void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (!(eps > 0.0f)) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "gated delta normalization epsilon must be positive");
+    if (heads == 0 || key_dim == 0 || value_dim == 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "gated_delta_step dimensions do not match SSM state");
+    if (value_dim > 1024 || value_dim % 32 != 0 || key_dim > 4096)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "gated delta value dimension must be a multiple of 32 up to 1024");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s =
+        launch(ctx, gated_delta_kernel, dim3(heads), dim3(value_dim), 2 * key_dim * sizeof(float),
+               static_cast<cudaStream_t>(stream), false, q_dev, k_dev, v_dev, beta_dev, log_decay_dev, state_dev,
+               key_dim, value_dim, eps, out_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_swiglu(oracle_cuda_context* ctx, const float* gate_dev, const float* up_dev,
+                                                 uint64_t n, float* out_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (n == 0) return ok(ctx);
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s = launch(ctx, swiglu_kernel, dim3(grid_for(n, ctx->sm_count)), dim3(256), 0,
+                                        static_cast<cudaStream_t>(stream), false, gate_dev, up_dev, n, out_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_add(oracle_cuda_context* ctx, const float* a_dev, const float* b_dev,
+                                              uint64_t n, float* out_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (n == 0) return ok(ctx);
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s = launch(ctx, add_kernel, dim3(grid_for(n, ctx->sm_count)), dim3(256), 0,
+                                        static_cast<cudaStream_t>(stream), false, a_dev, b_dev, n, out_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
