@@ -31,6 +31,8 @@ matrix is row-sharded over the ranks and each step ends with one NCCL
 all-gather of the packed outputs (strong scaling: the whole job processes the
 same matrices at every N; oracle_b200/shard.py).
 --workload config4 times the prefill dequant-GEMM (TFLOP/s, tensor roofline).
+--workload config5 times greedy decoding of the synthetic Qwen3.5-style hybrid
+decoder (tokens/s; its tokens are checked against Oracle's own decode loop).
 """
 from __future__ import annotations
 
@@ -851,13 +853,203 @@ def gemm_arm(args, wl: GemmWorkload) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------- config 5: the hybrid decoder
+
+class DecoderWorkload:
+    """greedy decoding of the synthetic Qwen3.5-style hybrid
+    model (oracle_b200/qwen35.py CONFIG5, Q4_K_M, 4.95 GB of weights) from a
+    seeded 128-token prompt, batch 1.  A step is one decode token: one replay
+    of the captured step graph (oracle_b200/decoder.py)."""
+    name = "config5"
+    metric = "batch-1 decode tokens/s (Qwen3.5-style hybrid, Q4_K_M)"
+    unit = "tokens/s"
+    prompt_len = 128
+    n_new = 256
+    dtype = "f32 activations, Q8_K x Q4_K/Q6_K integer dots"
+
+    def __init__(self):
+        from oracle_b200 import qwen35
+        self.cfg = qwen35.CONFIG5
+        self.specs = qwen35.tensor_specs(self.cfg)
+
+    def config(self, n_gpus: int) -> dict:
+        c = self.cfg
+        return {"workload": "config5: synthetic Qwen3.5-style hybrid decoder, 32 blocks (24 Gated DeltaNet + 8 "
+                            "gated GQA attention), hidden 4096, FFN 12288, vocab 151936, Q4_K_M, greedy",
+                "batch": 1, "prompt_tokens": self.prompt_len, "new_tokens": self.n_new, "kv_capacity": c.context,
+                "contract": "q8k", "parallelism": "single GPU" if n_gpus == 1 else f"replicas x{n_gpus}",
+                "l2": "no flush needed: each step streams 4.7 GB of weights (> 37x the 126 MB L2)"}
+
+    def step_bytes(self, position: int) -> int:
+        """Algorithmic HBM bytes of one decode step at a cache length: every
+        projection's packed weights, one embedding row, each recurrent
+        state read and written once, the conv histories, and the KV rows
+        read by attention."""
+        from oracle_b200 import qwen35
+        c = self.cfg
+        total = 0
+        for name, qtype, dims, _, _ in self.specs:
+            be, bb = qwen35.BLOCK[qtype]
+            n = int(np.prod(dims)) // be * bb
+            if name == "token_embd.weight":
+                n //= dims[1]
+            total += n
+        recurrent = sum(not c.is_attention(i) for i in range(c.layers))
+        attention = c.layers - recurrent
+        total += recurrent * (2 * c.value_heads * c.state_size * c.state_size * 4 + 2 * c.conv_channels * 4 * 4)
+        total += attention * (position + 1) * 2 * c.kv_width * 4
+        return total
+
+
+def decoder_host_model(wl: DecoderWorkload):
+    from oracle_b200 import qwen35
+    tensors = qwen35.synthetic_model(wl.cfg, "q4_k_m", "config5")
+    rng = np.random.default_rng(5150)
+    prompt = rng.integers(0, wl.cfg.vocab, wl.prompt_len).astype(np.uint32)
+    return tensors, prompt
+
+
+def decoder_cpu_leg(wl: DecoderWorkload, tensors, prompt, n_prompt: int = 2, n_new: int = 2):
+    """Oracle's decode loop (oracle/ref_qwen35.cpp, Q8_K checker build) on the
+    same model: greedy tokens for a short prompt, and its speed."""
+    import oracle
+    r = oracle.Qwen35Reference("q8k", tensors=tensors, manifest=wl.cfg.manifest(), admit_q4k=True,
+                               max_tokens=n_prompt + n_new + 1)
+    t0 = time.perf_counter()
+    toks = r.greedy(prompt[:n_prompt], n_new)
+    s = time.perf_counter() - t0
+    forwards = n_prompt + n_new - 1
+    r.close()
+    return toks, forwards / s, forwards, s
+
+
+def decoder_reference_arm(args, wl: DecoderWorkload) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    tensors, prompt = decoder_host_model(wl)
+    forwards = max(2, min(args.steps, 4))
+    _, tps, n, s = decoder_cpu_leg(wl, tensors, prompt, n_prompt=1, n_new=forwards)
+    cpu = {"value": tps, "unit": wl.unit, "cores": 1, "kind": "reference",
+           "sample": f"{n} decode steps of the full config-5 model from a 1-token prompt",
+           "note": "Oracle's execute_qwen35_reference_token + greedy Sampler compiled from its sources "
+                   "(single-threaded); Q4_K/Q6_K projections through the C restatement of GGML's Q8_K dot, "
+                   "since Oracle's own decoder rejects Q4_K"}
+    line = {"impl": "reference", "metric": wl.metric, "value": tps, "unit": wl.unit, "n_gpus": args.gpus,
+            "steps": n, "warmup": 0, "ms_per_step": s * 1e3 / n, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded Q4_K_M weights)",
+            "config": wl.config(1), "cpu_baseline": cpu,
+            "e2e": {"value": tps, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def decoder_arm(args, wl: DecoderWorkload) -> None:
+    import torch
+
+    import oracle_b200 as ob
+    from oracle_b200.decoder import Qwen35Decoder
+
+    rank, local, world = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    ctx = ob.Context(local)
+    tensors, prompt = decoder_host_model(wl)
+    max_new = max(wl.n_new, args.warmup + args.steps + 1)
+    dec = Qwen35Decoder(ctx, wl.cfg, tensors, contract="q8k", capacity=wl.cfg.context, max_new=max_new,
+                        device=local)
+    if wl.prompt_len + max_new > wl.cfg.context:
+        raise SystemExit("warm-up + timed steps exceed the KV cache capacity")
+
+    # gate: the GPU's greedy tokens on a short prompt equal Oracle's decode loop's
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        want, tps, n, s = decoder_cpu_leg(wl, tensors, prompt)
+        got = dec.generate(prompt[:2], 2)
+        if not np.array_equal(got, want):
+            raise SystemExit(f"GPU tokens {got.tolist()} differ from the CPU reference {want.tolist()}")
+        cpu = {"value": tps, "unit": wl.unit, "cores": 1, "kind": "reference",
+               "sample": f"{n} decode steps (2-token prompt, 2 new tokens) of the full config-5 model",
+               "note": "Oracle's execute_qwen35_reference_token + greedy Sampler compiled from its sources "
+                       "(single-threaded); Q4_K/Q6_K projections through the C restatement of GGML's Q8_K "
+                       "dot, since Oracle's own decoder rejects Q4_K; tokens identical to the GPU's"}
+
+    # timed region: decode steps after the 128-token prompt
+    dec.start(prompt)
+    launches = dec.launches_per_step()
+    dec.start(prompt)
+    with torch.cuda.stream(dec.stream):
+        for _ in range(wl.prompt_len + args.warmup):
+            dec.graph.replay()
+    dec.stream.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    with sampler, torch.cuda.stream(dec.stream):
+        start.record(dec.stream)
+        for _ in range(args.steps):
+            dec.graph.replay()
+        end.record(dec.stream)
+        dec.stream.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    ctx.device_status()
+    value = world * args.steps / (ms / 1e3)
+    mid = wl.prompt_len + args.warmup + args.steps // 2
+    step_bytes = wl.step_bytes(mid)
+    peak, peak_kind = load_peaks()
+    ms_step = ms / args.steps
+
+    # the matvec programs' share: one uncaptured step with events around each projection call
+    dec.start(prompt)
+    with torch.cuda.stream(dec.stream):
+        for _ in range(wl.prompt_len):
+            dec.graph.replay()
+    proj_bytes, proj_ms, _ = dec.profile_projections()
+    proj_gbs = proj_bytes / (proj_ms * 1e-3) / 1e9
+
+    # e2e: host prompt in, Qwen35Decoder.generate, host tokens out
+    dec.generate(prompt, 8)
+    barrier(world)
+    t0 = time.perf_counter()
+    toks = dec.generate(prompt, wl.n_new)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    forwards = wl.prompt_len + wl.n_new - 1
+    if rank == 0:
+        line = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded Q4_K_M weights and prompt)",
+                "config": wl.config(world), "gpu_launches": launches * args.steps,
+                "e2e": {"value": world * wl.n_new / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 4,
+                        "d2h_bytes_per_step": 4,
+                        "how": f"Qwen35Decoder.generate: 128-token host prompt in, {wl.n_new} greedy tokens out "
+                               f"({forwards} graph replays, prompt ingested token by token as Oracle does); "
+                               f"value = generated tokens / wall time",
+                        "forward_steps_per_s": world * forwards / e2e_s, "first_tokens": toks[:8].tolist()},
+                "roofline": {"bound": "hbm", "achieved": proj_gbs, "peak": peak, "unit": "GB/s",
+                             "frac": proj_gbs / peak, "peak_source": peak_kind, "traffic": None,
+                             "kernel": "matvec_program_kernel (the step's projections, one uncaptured step "
+                                       "timed with CUDA events around each program call)",
+                             "projection_ms_per_step": proj_ms, "projection_bytes_per_step": proj_bytes,
+                             "step_bytes": step_bytes, "step_achieved": step_bytes / (ms_step * 1e-3) / 1e9,
+                             "step_frac": step_bytes / (ms_step * 1e-3) / 1e9 / peak,
+                             "launches_per_step": launches},
+                "cpu_baseline": cpu, "clocks": sampler.summary()}
+        print(json.dumps(line), flush=True)
+    del dec
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=12000)
     ap.add_argument("--warmup", type=int, default=600)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["config4"], default="config2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["config4", "config5"], default="config2")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
@@ -865,6 +1057,10 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "config5":
+        wl5 = DecoderWorkload()
+        (decoder_reference_arm if args.impl == "reference" else decoder_arm)(args, wl5)
+        return
     if args.workload == "config4":
         wl = GemmWorkload()
         (gemm_reference_arm if args.impl == "reference" else gemm_arm)(args, wl)

@@ -249,7 +249,10 @@ oracle_cuda_status oracle_cuda_greedy_token(oracle_cuda_context* ctx, const floa
  *   conv_step       causal_depthwise_convolution_step, reference_kernels.cpp:192-219
  *                   (history [channels][kernel], updated in place)
  *   gated_delta_step gated_delta_step, reference_kernels.cpp:221-335 (state
- *                   [heads][key_dim][value_dim], updated in place)
+ *                   [heads][key_dim][value_dim], updated in place); q and k
+ *                   hold qk_heads rows of key_dim, head h reading row
+ *                   h % qk_heads: the block's repeat_heads_tiled
+ *                   (qwen35_block.cpp:225-243, 531-538) folded into the step
  *   swiglu          silu(gate) * up, qwen35_block.cpp:138-159 and 315-318
  *   add             add_vectors, qwen35_block.cpp:190-200 */
 oracle_cuda_status oracle_cuda_rms_norm_rows(oracle_cuda_context* ctx, const float* in_dev, const float* weight_dev,
@@ -267,12 +270,67 @@ oracle_cuda_status oracle_cuda_conv_step(oracle_cuda_context* ctx, const float* 
                                          float* out_dev, void* stream);
 oracle_cuda_status oracle_cuda_gated_delta_step(oracle_cuda_context* ctx, const float* q_dev, const float* k_dev,
                                                 const float* v_dev, const float* beta_dev, const float* log_decay_dev,
-                                                float* state_dev, uint32_t heads, uint32_t key_dim,
-                                                uint32_t value_dim, float eps, float* out_dev, void* stream);
+                                                float* state_dev, uint32_t heads, uint32_t qk_heads,
+                                                uint32_t key_dim, uint32_t value_dim, float eps, float* out_dev,
+                                                void* stream);
 oracle_cuda_status oracle_cuda_swiglu(oracle_cuda_context* ctx, const float* gate_dev, const float* up_dev, uint64_t n,
                                       float* out_dev, void* stream);
 oracle_cuda_status oracle_cuda_add(oracle_cuda_context* ctx, const float* a_dev, const float* b_dev, uint64_t n,
                                    float* out_dev, void* stream);
+
+/* ------------------------------------------------------------------ graph-replayable decode step
+ * A decode step captured once in a CUDA graph and replayed for every token
+ * keeps the token position in device memory (pos_dev, one uint32): the forms
+ * below read it there, and oracle_cuda_position_advance adds one at the end
+ * of a step.  Same arithmetic as oracle_cuda_rope / oracle_cuda_attention_step.
+ * A position >= the cache capacity (or the table's positions) is skipped and
+ * reported by the next oracle_cuda_device_status as OVERFLOW ("KV cache
+ * capacity exceeded ..."), the class KvCache::append throws.
+ *   rope_table        cos/sin of every text position p < positions
+ *                     (RopePosition::text, reference_kernels.hpp:18-20) by
+ *                     apply_qwen35_rope's expressions, reference_kernels.cpp:104-113;
+ *                     table_dev holds positions * rotary_dim floats; synchronous
+ *   rope_at           apply_qwen35_rope at position *pos_dev
+ *   attention_step_at causal_attention_step at length *pos_dev; scores_dev
+ *                     holds q_heads * capacity floats
+ *   split_query_gate  the joint query/gate projection [heads][2 * width] split
+ *                     into query and gate [heads][width], qwen35_block.cpp:676-688
+ *   gate_sigmoid_mul  x[i] *= sigmoid(gate[i]), qwen35_block.cpp:738-742
+ *   mul_silu          x[i] *= silu(z[i]), qwen35_block.cpp:589-592
+ *   gdn_gates         beta_out = sigmoid(beta), log_decay = softplus(alpha +
+ *                     time_step_bias) * decay, qwen35_block.cpp:472-489 */
+oracle_cuda_status oracle_cuda_rope_table(oracle_cuda_context* ctx, uint64_t rotary_dim, const int32_t* sections,
+                                          float base, uint64_t positions, float* table_dev);
+oracle_cuda_status oracle_cuda_rope_at(oracle_cuda_context* ctx, float* heads_dev, uint64_t n_heads, uint64_t head_dim,
+                                       uint64_t rotary_dim, const float* table_dev, uint64_t positions,
+                                       const uint32_t* pos_dev, void* stream);
+oracle_cuda_status oracle_cuda_attention_step_at(oracle_cuda_context* ctx, const float* q_dev, const float* k_new_dev,
+                                                 const float* v_new_dev, float* keys_dev, float* values_dev,
+                                                 uint64_t capacity, const uint32_t* pos_dev, uint32_t q_heads,
+                                                 uint32_t kv_heads, uint32_t key_dim, uint32_t value_dim,
+                                                 float* scores_dev, float* out_dev, void* stream);
+oracle_cuda_status oracle_cuda_position_advance(oracle_cuda_context* ctx, uint32_t* pos_dev, void* stream);
+oracle_cuda_status oracle_cuda_split_query_gate(oracle_cuda_context* ctx, const float* full_dev, uint32_t heads,
+                                                uint32_t width, float* query_dev, float* gate_dev, void* stream);
+oracle_cuda_status oracle_cuda_gate_sigmoid_mul(oracle_cuda_context* ctx, float* x_dev, const float* gate_dev,
+                                                uint64_t n, void* stream);
+oracle_cuda_status oracle_cuda_mul_silu(oracle_cuda_context* ctx, float* x_dev, const float* z_dev, uint64_t n,
+                                        void* stream);
+/* token_commit: after oracle_cuda_argmax into key_dev, the sampled token
+ * (Sampler::sample at temperature 0, src/runtime/sampler.cpp:22-46) and the
+ * next step's input: *next_id_dev = prompt[*pos + 1] while *pos + 1 < n_prompt
+ * (prompt ingestion one token at a time, qwen35_generation.cpp:737-747), else
+ * the sampled token, also stored at tokens_dev[*pos + 1 - n_prompt] when that
+ * index is < tokens_capacity; then *pos_dev += 1.  NaN / no finite logit:
+ * INVALID_ARGUMENT from the next oracle_cuda_device_status with the sampler's
+ * message, and the position does not advance. */
+oracle_cuda_status oracle_cuda_token_commit(oracle_cuda_context* ctx, const unsigned long long* key_dev,
+                                            const uint32_t* prompt_dev, uint32_t n_prompt, uint32_t* pos_dev,
+                                            uint32_t* next_id_dev, uint32_t* tokens_dev, uint32_t tokens_capacity,
+                                            void* stream);
+oracle_cuda_status oracle_cuda_gdn_gates(oracle_cuda_context* ctx, const float* beta_dev, const float* alpha_dev,
+                                         const float* time_step_bias_dev, const float* decay_dev, uint32_t heads,
+                                         float* beta_out_dev, float* log_decay_dev, void* stream);
 
 /* ------------------------------------------------------------------ row-sharded programs over GPUs
  * Tensor-parallel decode on the GPUs of one node, one process per GPU: every

@@ -7,6 +7,10 @@ Two libraries, loaded with ctypes:
   dots restated; provenance in ``quant_oracle.h``).
 * ``ref``  -- ``_ref/liboracle_ref.so``, the reference's own hot-path sources
   compiled unmodified (``Makefile``), reached through ``ref_shim.cpp``.
+* ``Qwen35Reference`` -- the reference's own Qwen3.5 decode step and greedy
+  loop (``ref_qwen35.cpp``), from ``liboracle_ref.so`` (Oracle's f32 contract)
+  or ``_ref/liboracle_ref_q8k.so`` (the same sources with GGML's Q8_K
+  contract for Q4_K/Q6_K projections, ``ref_q8k_projection.cpp``).
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
 and reference legs may import this package.  The product library never does.
@@ -22,6 +26,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_PATH = os.path.join(HERE, "liboracle_port.so")
 REF_PATH = os.path.join(HERE, "_ref", "liboracle_ref.so")
+REF_Q8K_PATH = os.path.join(HERE, "_ref", "liboracle_ref_q8k.so")
 REFERENCE_TREE = "/root/reference"
 
 TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K, TYPE_Q8_K, TYPE_BF16 = (
@@ -38,7 +43,7 @@ def build(reference_tree: str | None = REFERENCE_TREE) -> None:
     """Compile the restatement, and the reference checker when its tree exists."""
     targets = ["port"]
     if reference_tree and os.path.isdir(reference_tree):
-        targets.append("ref")
+        targets += ["ref", "ref_q8k"]
     subprocess.run(["make", "-s", "-C", HERE, f"REF={reference_tree}", *targets], check=True)
 
 
@@ -367,6 +372,123 @@ class _Ref:
                                                        w.ctypes.data, w.size, _ptr(out, _f32p),
                                                        out.size, err, 512), err)
         return out
+
+
+class _Qwen35Manifest(C.Structure):
+    """oref_qwen35_manifest (ref_qwen35.cpp): the Qwen35Manifest fields of a
+    model held in host buffers."""
+    _fields_ = [(n, C.c_uint32) for n in ("block_count", "context_length", "embedding_length",
+                                          "feed_forward_length", "head_count", "head_count_kv", "key_length",
+                                          "value_length")] + [
+        ("rms_epsilon", C.c_float), ("rope_dimension_count", C.c_uint32), ("rope_sections", C.c_int32 * 4),
+        ("rope_frequency_base", C.c_float)] + [
+        (n, C.c_uint32) for n in ("conv_kernel", "state_size", "group_count", "time_step_rank", "inner_size",
+                                  "full_attention_interval", "vocabulary_size")]
+
+
+_qwen35_libs = {}
+
+
+def _qwen35_lib(contract: str):
+    path = {"f32": REF_PATH, "q8k": REF_Q8K_PATH}[contract]
+    if contract not in _qwen35_libs:
+        if not os.path.exists(path):
+            build()
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} is not built and the reference tree is absent")
+        lib = C.CDLL(path)
+        cp, sz, vp, u32, u64 = C.c_char_p, C.c_size_t, C.c_void_p, C.c_uint32, C.c_uint64
+        lib.oref_qwen35_open_gguf.argtypes = [cp, C.c_int, u64, C.POINTER(vp), cp, sz]
+        lib.oref_qwen35_open_buffers.argtypes = [C.POINTER(_Qwen35Manifest), u32, C.POINTER(cp),
+                                                 C.POINTER(u32), C.POINTER(u32), C.POINTER(u64), C.POINTER(vp),
+                                                 C.POINTER(u64), C.c_int, u64, C.POINTER(vp), cp, sz]
+        lib.oref_qwen35_vocab.argtypes = [vp]
+        lib.oref_qwen35_vocab.restype = u32
+        lib.oref_qwen35_reset.argtypes = [vp]
+        lib.oref_qwen35_forward.argtypes = [vp, u32, _f32p, cp, sz]
+        lib.oref_qwen35_greedy.argtypes = [vp, C.POINTER(u32), u64, u64, C.POINTER(u32), cp, sz]
+        lib.oref_qwen35_close.argtypes = [vp]
+        _qwen35_libs[contract] = lib
+    return _qwen35_libs[contract]
+
+
+class Qwen35Reference:
+    """Oracle's own Qwen3.5 decode (execute_qwen35_reference_token on its
+    HybridCache, greedy Sampler) over one model.
+
+    contract "f32": the reference compiled unmodified (its f32 contract; its
+    binder admits Q5_K/Q6_K/Q8_0/float matrices).  contract "q8k": the same
+    sources with Q4_K/Q6_K projections on GGML's Q8_K contract and Q4_K
+    admitted (``admit_q4k``).  The model is a GGUF file (``gguf_path``) or
+    host buffers: ``tensors`` = [(name, ggml_type, dims, uint8 array)], dims
+    GGUF-ordered (dims[0] = columns), with ``manifest`` a dict of
+    ``_Qwen35Manifest`` fields."""
+
+    def __init__(self, contract: str, gguf_path: str | None = None, tensors=None, manifest: dict | None = None,
+                 admit_q4k: bool = False, max_tokens: int = 4096):
+        self.lib = _qwen35_lib(contract)
+        self._h = C.c_void_p()
+        err = C.create_string_buffer(512)
+        if gguf_path is not None:
+            rc = self.lib.oref_qwen35_open_gguf(gguf_path.encode(), int(admit_q4k), max_tokens, C.byref(self._h),
+                                                err, 512)
+        else:
+            mf = _Qwen35Manifest()
+            for k, v in manifest.items():
+                if k == "rope_sections":
+                    mf.rope_sections = (C.c_int32 * 4)(*v)
+                else:
+                    setattr(mf, k, v)
+            n = len(tensors)
+            self._keep = [np.ascontiguousarray(t[3]).view(np.uint8) for t in tensors]
+            names = (C.c_char_p * n)(*[t[0].encode() for t in tensors])
+            types = (C.c_uint32 * n)(*[t[1] for t in tensors])
+            ndims = (C.c_uint32 * n)(*[len(t[2]) for t in tensors])
+            dims = (C.c_uint64 * (4 * n))()
+            for i, t in enumerate(tensors):
+                for j, d in enumerate(t[2]):
+                    dims[4 * i + j] = d
+            data = (C.c_void_p * n)(*[a.ctypes.data for a in self._keep])
+            sizes = (C.c_uint64 * n)(*[a.nbytes for a in self._keep])
+            rc = self.lib.oref_qwen35_open_buffers(C.byref(mf), n, names, types, ndims, dims, data, sizes,
+                                                   int(admit_q4k), max_tokens, C.byref(self._h), err, 512)
+        if rc:
+            raise ReferenceError_(rc, err.value.decode())
+        self.vocab = int(self.lib.oref_qwen35_vocab(self._h))
+
+    def reset(self) -> None:
+        self.lib.oref_qwen35_reset(self._h)
+
+    def forward(self, token: int) -> np.ndarray:
+        """One token at the cache's current length; returns the logits."""
+        out = np.empty(self.vocab, np.float32)
+        err = C.create_string_buffer(512)
+        rc = self.lib.oref_qwen35_forward(self._h, token, _ptr(out, _f32p), err, 512)
+        if rc:
+            raise ReferenceError_(rc, err.value.decode())
+        return out
+
+    def greedy(self, prompt, n_new: int) -> np.ndarray:
+        """Fresh greedy generation of n_new tokens after the prompt."""
+        p = np.ascontiguousarray(prompt, np.uint32)
+        out = np.zeros(n_new, np.uint32)
+        err = C.create_string_buffer(512)
+        rc = self.lib.oref_qwen35_greedy(self._h, p.ctypes.data_as(C.POINTER(C.c_uint32)), p.size, n_new,
+                                         out.ctypes.data_as(C.POINTER(C.c_uint32)), err, 512)
+        if rc:
+            raise ReferenceError_(rc, err.value.decode())
+        return out
+
+    def close(self) -> None:
+        if self._h:
+            self.lib.oref_qwen35_close(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 _port = None

@@ -126,7 +126,18 @@ _proto("oracle_cuda_rope", [_vp, _vp, _u64, _u64, _u64, C.POINTER(C.c_int32), C.
 _proto("oracle_cuda_attention_step", [_vp, _vp, _vp, _vp, _vp, _vp, _u64, _u64, _u32, _u32, _u32, _u32, _vp, _vp,
                                       _vp])
 _proto("oracle_cuda_conv_step", [_vp, _vp, _vp, _vp, _u64, _u32, _i32, _vp, _vp])
-_proto("oracle_cuda_gated_delta_step", [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, C.c_float, _vp, _vp])
+_proto("oracle_cuda_gated_delta_step", [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, C.c_float, _vp,
+                                        _vp])
+_proto("oracle_cuda_rope_table", [_vp, _u64, C.POINTER(C.c_int32), C.c_float, _u64, _vp])
+_proto("oracle_cuda_rope_at", [_vp, _vp, _u64, _u64, _u64, _vp, _u64, _vp, _vp])
+_proto("oracle_cuda_attention_step_at", [_vp, _vp, _vp, _vp, _vp, _vp, _u64, _vp, _u32, _u32, _u32, _u32, _vp, _vp,
+                                         _vp])
+_proto("oracle_cuda_position_advance", [_vp, _vp, _vp])
+_proto("oracle_cuda_split_query_gate", [_vp, _vp, _u32, _u32, _vp, _vp, _vp])
+_proto("oracle_cuda_gate_sigmoid_mul", [_vp, _vp, _vp, _u64, _vp])
+_proto("oracle_cuda_mul_silu", [_vp, _vp, _vp, _u64, _vp])
+_proto("oracle_cuda_gdn_gates", [_vp, _vp, _vp, _vp, _vp, _u32, _vp, _vp, _vp])
+_proto("oracle_cuda_token_commit", [_vp, _vp, _vp, _u32, _vp, _vp, _vp, _u32, _vp])
 _proto("oracle_cuda_swiglu", [_vp, _vp, _vp, _u64, _vp, _vp])
 _proto("oracle_cuda_add", [_vp, _vp, _vp, _u64, _vp, _vp])
 IPC_HANDLE_BYTES = 64
@@ -423,10 +434,50 @@ class Context:
                                                1 if apply_silu else 0, _addr(out), _stream(stream)))
 
     def gated_delta_step(self, q, k, v, beta, log_decay, state, heads, key_dim, value_dim, eps, out,
-                         stream=None) -> None:
+                         stream=None, qk_heads=None) -> None:
+        """oracle_cuda_gated_delta_step; q and k hold qk_heads rows (default: heads)."""
         self._check(_lib.oracle_cuda_gated_delta_step(self._h, _addr(q), _addr(k), _addr(v), _addr(beta),
-                                                      _addr(log_decay), _addr(state), heads, key_dim, value_dim, eps,
-                                                      _addr(out), _stream(stream)))
+                                                      _addr(log_decay), _addr(state), heads,
+                                                      heads if qk_heads is None else qk_heads, key_dim, value_dim,
+                                                      eps, _addr(out), _stream(stream)))
+
+    # -------------------------------------------------------------- graph-replayable step
+    def rope_table(self, rotary_dim, sections, base, positions, table) -> None:
+        sec = (C.c_int32 * 4)(*sections)
+        self._check(_lib.oracle_cuda_rope_table(self._h, rotary_dim, sec, base, positions, _addr(table)))
+
+    def rope_at(self, heads, n_heads, head_dim, rotary_dim, table, positions, pos, stream=None) -> None:
+        self._check(_lib.oracle_cuda_rope_at(self._h, _addr(heads), n_heads, head_dim, rotary_dim, _addr(table),
+                                             positions, _addr(pos), _stream(stream)))
+
+    def attention_step_at(self, q, k_new, v_new, keys, values, capacity, pos, q_heads, kv_heads, key_dim, value_dim,
+                          scores, out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_attention_step_at(self._h, _addr(q), _addr(k_new), _addr(v_new), _addr(keys),
+                                                       _addr(values), capacity, _addr(pos), q_heads, kv_heads,
+                                                       key_dim, value_dim, _addr(scores), _addr(out),
+                                                       _stream(stream)))
+
+    def position_advance(self, pos, stream=None) -> None:
+        self._check(_lib.oracle_cuda_position_advance(self._h, _addr(pos), _stream(stream)))
+
+    def split_query_gate(self, full, heads, width, query, gate, stream=None) -> None:
+        self._check(_lib.oracle_cuda_split_query_gate(self._h, _addr(full), heads, width, _addr(query), _addr(gate),
+                                                      _stream(stream)))
+
+    def gate_sigmoid_mul(self, x, gate, n, stream=None) -> None:
+        self._check(_lib.oracle_cuda_gate_sigmoid_mul(self._h, _addr(x), _addr(gate), n, _stream(stream)))
+
+    def mul_silu(self, x, z, n, stream=None) -> None:
+        self._check(_lib.oracle_cuda_mul_silu(self._h, _addr(x), _addr(z), n, _stream(stream)))
+
+    def token_commit(self, key, prompt, n_prompt, pos, next_id, tokens, tokens_capacity, stream=None) -> None:
+        self._check(_lib.oracle_cuda_token_commit(self._h, _addr(key), _addr(prompt), n_prompt, _addr(pos),
+                                                  _addr(next_id), _addr(tokens), tokens_capacity, _stream(stream)))
+
+    def gdn_gates(self, beta, alpha, time_step_bias, decay, heads, beta_out, log_decay, stream=None) -> None:
+        self._check(_lib.oracle_cuda_gdn_gates(self._h, _addr(beta), _addr(alpha), _addr(time_step_bias),
+                                               _addr(decay), heads, _addr(beta_out), _addr(log_decay),
+                                               _stream(stream)))
 
     def swiglu(self, gate, up, n, out, stream=None) -> None:
         self._check(_lib.oracle_cuda_swiglu(self._h, _addr(gate), _addr(up), n, _addr(out), _stream(stream)))

@@ -51,7 +51,7 @@ def build_cuda(force: bool = False, verbose: bool = False) -> str:
 def build_oracle() -> None:
     targets = ["port"]
     if os.path.isdir(REFERENCE_TREE):
-        targets.append("ref")
+        targets += ["ref", "ref_q8k"]
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={REFERENCE_TREE}", *targets],
                    check=True)
 

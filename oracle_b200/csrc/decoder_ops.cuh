@@ -179,18 +179,20 @@ __global__ void __launch_bounds__(256) conv_step_kernel(const float* __restrict_
 }
 
 // One CTA per head, thread per value index v (blockDim.x = value_dim <= 1024);
-// recurrent state[head][key][value].
+// recurrent state[head][key][value].  q and k hold qk_heads rows; head h reads
+// row h % qk_heads, which is Oracle's repeat_heads_tiled (qwen35_block.cpp:225-243)
+// applied before the step (qwen35_block.cpp:531-538).
 __global__ void gated_delta_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                    const float* __restrict__ v, const float* __restrict__ beta,
-                                   const float* __restrict__ log_decay, float* state, uint32_t key_dim,
-                                   uint32_t value_dim, float eps, float* __restrict__ out) {
+                                   const float* __restrict__ log_decay, float* state, uint32_t qk_heads,
+                                   uint32_t key_dim, uint32_t value_dim, float eps, float* __restrict__ out) {
     extern __shared__ float gd_smem[];  // normalized q, normalized k
     __shared__ double scratch[32];
     float* nq = gd_smem;
     float* nk = gd_smem + key_dim;
     const uint32_t h = blockIdx.x, vi = threadIdx.x;
-    const float* qh = q + static_cast<uint64_t>(h) * key_dim;
-    const float* kh = k + static_cast<uint64_t>(h) * key_dim;
+    const float* qh = q + static_cast<uint64_t>(h % qk_heads) * key_dim;
+    const float* kh = k + static_cast<uint64_t>(h % qk_heads) * key_dim;
     double qs = 0.0, ks = 0.0;
     for (uint32_t d = threadIdx.x; d < key_dim; d += blockDim.x) {
         const double a = qh[d], b = kh[d];

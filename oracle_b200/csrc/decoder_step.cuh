@@ -1,0 +1,183 @@
+// decoder_step.cuh -- graph-replayable forms of the decode step's glue.
+//
+// A decode step captured once in a CUDA graph is replayed for every token, so
+// nothing that changes per token may live in kernel parameters: the token
+// position is a device counter (`pos`, advanced by step_advance_kernel at the
+// end of a step), RoPE reads its cos/sin from a table of every position the
+// host computed once by the reference's expressions, and the attention kernels
+// read the cache length from `pos`.  Arithmetic is that of decoder_ops.cuh.
+// A position at or past the cache capacity (or the RoPE table) is not
+// processed: the kernels skip it and report kDevKvOverflow, which
+// oracle_cuda_device_status returns as OVERFLOW, the class KvCache::append
+// throws (hybrid_cache.cpp).
+// The small elementwise kernels restate Oracle's block code
+// (src/runtime/qwen35_block.cpp):
+//   split_query_gate_kernel  joint query/gate projection -> query, gate (:676-688)
+//   gate_sigmoid_mul_kernel  attention *= sigmoid(gate)                (:738-742)
+//   gdn_gates_kernel         beta = sigmoid(beta), log_decay =
+//                            softplus(alpha + time_step_bias) * decay  (:472-489)
+//   mul_silu_kernel          gated *= silu(z)                          (:589-592)
+#pragma once
+
+#include "decoder_ops.cuh"
+
+namespace oracle_cuda {
+
+enum : unsigned int { kDevKvOverflow = 4 };
+
+__device__ __forceinline__ void report_overflow(DeviceStatus* st, uint32_t pos) {
+    if (st && atomicCAS(&st->code, kDevOk, kDevKvOverflow) == kDevOk) {
+        st->where = pos;
+        st->block = blockIdx.x;
+    }
+}
+
+__device__ __forceinline__ float ref_softplus(float v) {
+    // qwen35_block.cpp:147-155
+    if (v > 20.0f) return v;
+    if (v < -20.0f) return expf(v);
+    return log1pf(expf(v));
+}
+
+__global__ void __launch_bounds__(256) rope_pos_kernel(float* __restrict__ heads, uint32_t n_heads, uint32_t head_dim,
+                                                       uint32_t half, const float* __restrict__ table,
+                                                       const uint32_t* __restrict__ pos, uint32_t positions,
+                                                       DeviceStatus* st) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_heads * half) return;
+    if (*pos >= positions) {
+        if (i == 0) report_overflow(st, *pos);
+        return;
+    }
+    const uint32_t h = i / half, f = i % half;
+    const float* row = table + (static_cast<uint64_t>(*pos) * half + f) * 2;
+    float* base = heads + static_cast<uint64_t>(h) * head_dim;
+    const float a = base[f], b = base[half + f], c = row[0], s = row[1];
+    base[f] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    base[half + f] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+}
+
+__global__ void __launch_bounds__(256) attention_append_pos_kernel(const float* __restrict__ k_new,
+                                                                   const float* __restrict__ v_new, float* keys,
+                                                                   float* values, const uint32_t* __restrict__ pos,
+                                                                   uint32_t capacity, uint32_t nk, uint32_t nv,
+                                                                   DeviceStatus* st) {
+    const uint64_t length = *pos;
+    if (length >= capacity) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) report_overflow(st, static_cast<uint32_t>(length));
+        return;
+    }
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nk + nv; i += gridDim.x * blockDim.x) {
+        if (i < nk)
+            keys[length * nk + i] = k_new[i];
+        else
+            values[length * nv + (i - nk)] = v_new[i - nk];
+    }
+}
+
+// grid (q_heads, chunks); warps of all chunks of a head stride over tokens.
+__global__ void __launch_bounds__(256) attention_scores_pos_kernel(const float* __restrict__ q,
+                                                                   const float* __restrict__ keys,
+                                                                   const uint32_t* __restrict__ pos, uint32_t capacity,
+                                                                   uint32_t q_heads, uint32_t kv_heads,
+                                                                   uint32_t key_dim, float scale,
+                                                                   float* __restrict__ scores) {
+    if (*pos >= capacity) return;
+    const uint32_t tokens = *pos + 1;
+    const uint32_t h = blockIdx.x, lane = threadIdx.x & 31;
+    const uint32_t w = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const uint32_t nw = gridDim.y * (blockDim.x >> 5);
+    const uint32_t kvh = h / (q_heads / kv_heads);
+    const float* qh = q + static_cast<uint64_t>(h) * key_dim;
+    for (uint32_t t = w; t < tokens; t += nw) {
+        const float* kt = keys + (static_cast<uint64_t>(t) * kv_heads + kvh) * key_dim;
+        double s = 0.0;
+        for (uint32_t d = lane; d < key_dim; d += 32)
+            s = __dadd_rn(s, __dmul_rn(static_cast<double>(qh[d]), static_cast<double>(kt[d])));
+        s = warp_sum_f64(s);
+        if (lane == 0) scores[static_cast<uint64_t>(h) * capacity + t] = __fmul_rn(__double2float_rn(s), scale);
+    }
+}
+
+__global__ void __launch_bounds__(256) attention_output_pos_kernel(float* __restrict__ scores,
+                                                                   const float* __restrict__ values,
+                                                                   const uint32_t* __restrict__ pos, uint32_t capacity,
+                                                                   uint32_t q_heads, uint32_t kv_heads,
+                                                                   uint32_t value_dim, float* __restrict__ out,
+                                                                   DeviceStatus* st) {
+    __shared__ double scratch[32];
+    __shared__ float fmax_s[32];
+    if (*pos >= capacity) return;
+    const uint32_t tokens = *pos + 1;
+    const uint32_t h = blockIdx.x, kvh = h / (q_heads / kv_heads);
+    float* sc = scores + static_cast<uint64_t>(h) * capacity;
+    float m = -INFINITY;
+    for (uint32_t t = threadIdx.x; t < tokens; t += blockDim.x) m = fmaxf(m, sc[t]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    if ((threadIdx.x & 31) == 0) fmax_s[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = -INFINITY;
+    for (uint32_t w = 0; w < (blockDim.x >> 5); ++w) m = fmaxf(m, fmax_s[w]);
+    double den = 0.0;
+    for (uint32_t t = threadIdx.x; t < tokens; t += blockDim.x) {
+        const float e = expf(__fsub_rn(sc[t], m));
+        sc[t] = e;
+        den = __dadd_rn(den, static_cast<double>(e));
+    }
+    den = block_sum_f64(den, scratch);
+    if (!(den > 0.0) || !isfinite(den)) {
+        if (threadIdx.x == 0 && st) atomicCAS(&st->code, kDevOk, 3u);
+        return;
+    }
+    for (uint32_t t = threadIdx.x; t < tokens; t += blockDim.x)
+        sc[t] = __double2float_rn(__ddiv_rn(static_cast<double>(sc[t]), den));
+    __syncthreads();
+    for (uint32_t d = threadIdx.x; d < value_dim; d += blockDim.x) {
+        const float* vp = values + static_cast<uint64_t>(kvh) * value_dim + d;
+        const uint64_t stride = static_cast<uint64_t>(kv_heads) * value_dim;
+        float acc = 0.0f;
+        for (uint32_t t = 0; t < tokens; ++t) acc = __fadd_rn(acc, __fmul_rn(sc[t], __ldg(vp + t * stride)));
+        out[static_cast<uint64_t>(h) * value_dim + d] = acc;
+    }
+}
+
+__global__ void step_advance_kernel(uint32_t* pos) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) *pos += 1u;
+}
+
+// query_full [heads][2 * width] (query then gate per head) -> query, gate [heads][width]
+__global__ void __launch_bounds__(256) split_query_gate_kernel(const float* __restrict__ full, uint32_t heads,
+                                                               uint32_t width, float* __restrict__ query,
+                                                               float* __restrict__ gate) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= heads * width) return;
+    const uint32_t h = i / width, c = i % width;
+    query[i] = full[static_cast<uint64_t>(h) * 2 * width + c];
+    gate[i] = full[static_cast<uint64_t>(h) * 2 * width + width + c];
+}
+
+__global__ void __launch_bounds__(256) gate_sigmoid_mul_kernel(float* __restrict__ x, const float* __restrict__ gate,
+                                                               uint32_t n) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = __fmul_rn(x[i], ref_sigmoid(gate[i]));
+}
+
+__global__ void __launch_bounds__(256) gdn_gates_kernel(const float* __restrict__ beta_in,
+                                                        const float* __restrict__ alpha,
+                                                        const float* __restrict__ time_step_bias,
+                                                        const float* __restrict__ decay, uint32_t heads,
+                                                        float* __restrict__ beta_out,
+                                                        float* __restrict__ log_decay) {
+    const uint32_t h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (h >= heads) return;
+    beta_out[h] = ref_sigmoid(beta_in[h]);
+    log_decay[h] = __fmul_rn(ref_softplus(__fadd_rn(alpha[h], time_step_bias[h])), decay[h]);
+}
+
+__global__ void __launch_bounds__(256) mul_silu_kernel(float* __restrict__ x, const float* __restrict__ z, uint32_t n) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = __fmul_rn(x[i], ref_silu(z[i]));
+}
+
+}  // namespace oracle_cuda

@@ -90,7 +90,7 @@ struct ArgmaxResult {
     float value;
 };
 
-inline ArgmaxResult decode_argmax_key(unsigned long long key) {
+__host__ __device__ inline ArgmaxResult decode_argmax_key(unsigned long long key) {
     ArgmaxResult r{};
     if (key == ~0ull) {
         r.nan = true;
@@ -99,12 +99,50 @@ inline ArgmaxResult decode_argmax_key(unsigned long long key) {
     uint32_t b = static_cast<uint32_t>(key >> 32);
     b = (b & 0x80000000u) ? (b & 0x7FFFFFFFu) : ~b;
     float v;
+#ifdef __CUDA_ARCH__
+    v = __uint_as_float(b);
+#else
     static_assert(sizeof v == sizeof b, "float width");
     memcpy(&v, &b, sizeof v);
+#endif
     r.value = v;
     r.index = ~static_cast<uint32_t>(key & 0xFFFFFFFFull);
     r.finite = v == v && v - v == 0.0f;
     return r;
+}
+
+enum : unsigned int { kDevLogitsNaN = 5, kDevLogitsNonFinite = 6 };
+
+// One decode step's bookkeeping on the device, so that a step captured in a
+// CUDA graph can be replayed token after token without the host: the argmax
+// key of the step's logits becomes the sampled token (Sampler::sample at
+// temperature 0), and the next step's input id is the next prompt token while
+// the prompt lasts (the reference ingests prompts one token at a time,
+// qwen35_generation.cpp:737-747), else the sampled token, which is also
+// appended to tokens_out.  Then the position advances.  A NaN or non-finite
+// maximum is reported (the sampler's invalid_argument) and ends sampling:
+// the position does not advance.
+__global__ void token_commit_kernel(const unsigned long long* __restrict__ key, const uint32_t* __restrict__ prompt,
+                                    uint32_t n_prompt, uint32_t* pos, uint32_t* next_id, uint32_t* tokens_out,
+                                    uint32_t out_capacity, DeviceStatus* st) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const ArgmaxResult r = decode_argmax_key(*key);
+    const uint32_t p = *pos;
+    if (r.nan || !r.finite) {
+        if (st && atomicCAS(&st->code, kDevOk, r.nan ? kDevLogitsNaN : kDevLogitsNonFinite) == kDevOk) {
+            st->where = p;
+            st->block = 0;
+        }
+        return;
+    }
+    if (p + 1 < n_prompt) {
+        *next_id = prompt[p + 1];
+    } else {
+        *next_id = r.index;
+        const uint32_t i = p + 1 - n_prompt;
+        if (i < out_capacity) tokens_out[i] = r.index;
+    }
+    *pos = p + 1;
 }
 
 }  // namespace oracle_cuda

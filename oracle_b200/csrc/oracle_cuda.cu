@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "decoder_ops.cuh"
+#include "decoder_step.cuh"
 #include "gather.cuh"
 #include "gemm_q4k.cuh"
 #include "layout.hpp"
@@ -556,6 +557,13 @@ oracle_cuda_status oracle_cuda_device_status(oracle_cuda_context* ctx) {
                         "cudaMemset(program counters)");
     if (st.code == 3u)  // causal_attention_step (reference_kernels.cpp:170-172)
         return fail(ctx, ORACLE_CUDA_RUNTIME_ERROR, "causal attention softmax normalization failed");
+    if (st.code == kDevKvOverflow)  // KvCache::append (hybrid_cache.cpp)
+        return fail(ctx, ORACLE_CUDA_OVERFLOW,
+                    "KV cache capacity exceeded at position " + std::to_string(st.where));
+    if (st.code == kDevLogitsNaN)  // Sampler::sample (sampler.cpp:34-36)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "logits contain NaN");
+    if (st.code == kDevLogitsNonFinite)  // Sampler::sample (sampler.cpp:42-44)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "logits contain no finite candidates");
     if (st.code == kDevBadIndex)  // embedding_row (qwen35_forward.cpp:59-61)
         return fail(ctx, ORACLE_CUDA_OUT_OF_RANGE,
                     "token id " + std::to_string(st.where) + " exceeds the embedding row count");
@@ -1594,20 +1602,22 @@ extern "C" oracle_cuda_status oracle_cuda_conv_step(oracle_cuda_context* ctx, co
 extern "C" oracle_cuda_status oracle_cuda_gated_delta_step(oracle_cuda_context* ctx, const float* q_dev,
                                                            const float* k_dev, const float* v_dev,
                                                            const float* beta_dev, const float* log_decay_dev,
-                                                           float* state_dev, uint32_t heads, uint32_t key_dim,
-                                                           uint32_t value_dim, float eps, float* out_dev,
-                                                           void* stream) {
+                                                           float* state_dev, uint32_t heads, uint32_t qk_heads,
+                                                           uint32_t key_dim, uint32_t value_dim, float eps,
+                                                           float* out_dev, void* stream) {
     if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
     if (!(eps > 0.0f)) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "gated delta normalization epsilon must be positive");
     if (heads == 0 || key_dim == 0 || value_dim == 0)
         return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "gated_delta_step dimensions do not match SSM state");
+    if (qk_heads == 0 || heads % qk_heads != 0)  // repeat_heads_tiled (qwen35_block.cpp:229-233)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Qwen3.5 repeated-head dimensions are incompatible");
     if (value_dim > 1024 || value_dim % 32 != 0 || key_dim > 4096)
         return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "gated delta value dimension must be a multiple of 32 up to 1024");
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
     const oracle_cuda_status s =
         launch(ctx, gated_delta_kernel, dim3(heads), dim3(value_dim), 2 * key_dim * sizeof(float),
                static_cast<cudaStream_t>(stream), false, q_dev, k_dev, v_dev, beta_dev, log_decay_dev, state_dev,
-               key_dim, value_dim, eps, out_dev);
+               qk_heads, key_dim, value_dim, eps, out_dev);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
 
@@ -1628,5 +1638,175 @@ extern "C" oracle_cuda_status oracle_cuda_add(oracle_cuda_context* ctx, const fl
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
     const oracle_cuda_status s = launch(ctx, add_kernel, dim3(grid_for(n, ctx->sm_count)), dim3(256), 0,
                                         static_cast<cudaStream_t>(stream), false, a_dev, b_dev, n, out_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+// ---------------------------------------------------------------- graph-replayable decode step
+
+extern "C" oracle_cuda_status oracle_cuda_rope_table(oracle_cuda_context* ctx, uint64_t rotary_dim,
+                                                     const int32_t* sections, float base, uint64_t positions,
+                                                     float* table_dev) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (rotary_dim == 0 || rotary_dim % 2 != 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE dimension must be non-zero, even, and within head width");
+    if (!(base > 0.0f) || !std::isfinite(base))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE frequency base must be positive and finite");
+    if (!sections) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE sections pointer is null");
+    int64_t section_sum = 0;
+    for (int i = 0; i < 4; ++i) {
+        if (sections[i] < 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE dimension sections must be non-negative");
+        section_sum += sections[i];
+    }
+    if (section_sum != static_cast<int64_t>(rotary_dim / 2))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE dimension sections must sum to half the rotary dimension");
+    if (positions == 0 || positions > 0xFFFFFFFFull || rotary_dim / 2 > kRopeMaxHalf)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "RoPE table positions must be in [1, 2^32), rotary dimension <= 256");
+    if (!table_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE table pointer is null");
+    // apply_qwen35_rope's expressions (reference_kernels.cpp:104-113) for text
+    // positions (RopePosition::text: every coordinate equals the position)
+    const size_t half = rotary_dim / 2;
+    std::vector<double> inverse_frequency(half);
+    for (size_t f = 0; f < half; ++f) {
+        const double exponent = (2.0 * static_cast<double>(f)) / static_cast<double>(rotary_dim);
+        inverse_frequency[f] = 1.0 / std::pow(base, exponent);
+    }
+    std::vector<float> table(positions * half * 2);
+    for (uint64_t p = 0; p < positions; ++p)
+        for (size_t f = 0; f < half; ++f) {
+            const uint64_t coordinate = rope_coordinate(f, p, p, p, sections);
+            const double angle = static_cast<double>(coordinate) * inverse_frequency[f];
+            table[(p * half + f) * 2] = static_cast<float>(std::cos(angle));
+            table[(p * half + f) * 2 + 1] = static_cast<float>(std::sin(angle));
+        }
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    ORACLE_CUDA_TRY(ctx, cudaMemcpy(table_dev, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice),
+                    "cudaMemcpy(RoPE table)");
+    return ok(ctx);
+}
+
+extern "C" oracle_cuda_status oracle_cuda_rope_at(oracle_cuda_context* ctx, float* heads_dev, uint64_t n_heads,
+                                                  uint64_t head_dim, uint64_t rotary_dim, const float* table_dev,
+                                                  uint64_t positions, const uint32_t* pos_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (rotary_dim == 0 || rotary_dim % 2 != 0 || rotary_dim > head_dim)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE dimension must be non-zero, even, and within head width");
+    if (!table_dev || !pos_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE table or position pointer is null");
+    if (positions > 0xFFFFFFFFull || n_heads * (rotary_dim / 2) > 0xFFFFFFFFull || head_dim > 0xFFFFFFFFull)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "RoPE shape too large");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const uint64_t n = n_heads * (rotary_dim / 2);
+    const oracle_cuda_status s =
+        launch(ctx, rope_pos_kernel, dim3(static_cast<uint32_t>((n + 255) / 256)), dim3(256), 0,
+               static_cast<cudaStream_t>(stream), false, heads_dev, static_cast<uint32_t>(n_heads),
+               static_cast<uint32_t>(head_dim), static_cast<uint32_t>(rotary_dim / 2), table_dev, pos_dev,
+               static_cast<uint32_t>(positions), ctx->status);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_attention_step_at(oracle_cuda_context* ctx, const float* q_dev,
+                                                            const float* k_new_dev, const float* v_new_dev,
+                                                            float* keys_dev, float* values_dev, uint64_t capacity,
+                                                            const uint32_t* pos_dev, uint32_t q_heads,
+                                                            uint32_t kv_heads, uint32_t key_dim, uint32_t value_dim,
+                                                            float* scores_dev, float* out_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (kv_heads == 0 || q_heads % kv_heads != 0 || key_dim == 0 || value_dim == 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "causal_attention_step dimensions are incompatible");
+    if (capacity == 0 || capacity > 0xFFFFFFFFull || !pos_dev)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "KV cache capacity must be in [1, 2^32) with a position");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const uint32_t cap = static_cast<uint32_t>(capacity);
+    const uint32_t nk = kv_heads * key_dim, nv = kv_heads * value_dim;
+    oracle_cuda_status s = launch(ctx, attention_append_pos_kernel, dim3(grid_for(nk + nv, ctx->sm_count)), dim3(256),
+                                  0, st, false, k_new_dev, v_new_dev, keys_dev, values_dev, pos_dev, cap, nk, nv,
+                                  ctx->status);
+    if (s != ORACLE_CUDA_OK) return s;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(key_dim));
+    // enough warps per head that a full cache takes about 32 tokens per warp
+    uint32_t chunks = static_cast<uint32_t>((capacity + 255) / 256);
+    if (chunks > 64) chunks = 64;
+    s = launch(ctx, attention_scores_pos_kernel, dim3(q_heads, chunks), dim3(256), 0, st, false, q_dev,
+               static_cast<const float*>(keys_dev), pos_dev, cap, q_heads, kv_heads, key_dim, scale, scores_dev);
+    if (s != ORACLE_CUDA_OK) return s;
+    s = launch(ctx, attention_output_pos_kernel, dim3(q_heads), dim3(256), 0, st, false, scores_dev,
+               static_cast<const float*>(values_dev), pos_dev, cap, q_heads, kv_heads, value_dim, out_dev,
+               ctx->status);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_position_advance(oracle_cuda_context* ctx, uint32_t* pos_dev,
+                                                           void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (!pos_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "position pointer is null");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s =
+        launch(ctx, step_advance_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), false, pos_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_split_query_gate(oracle_cuda_context* ctx, const float* full_dev,
+                                                           uint32_t heads, uint32_t width, float* query_dev,
+                                                           float* gate_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (heads == 0 || width == 0 || uint64_t(heads) * width > 0xFFFFFFFFull)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Qwen3.5 joint query/gate projection width mismatch");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const uint64_t n = uint64_t(heads) * width;
+    const oracle_cuda_status s = launch(ctx, split_query_gate_kernel, dim3(static_cast<uint32_t>((n + 255) / 256)),
+                                        dim3(256), 0, static_cast<cudaStream_t>(stream), false, full_dev, heads,
+                                        width, query_dev, gate_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_gate_sigmoid_mul(oracle_cuda_context* ctx, float* x_dev,
+                                                           const float* gate_dev, uint64_t n, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (n == 0) return ok(ctx);
+    if (n > 0xFFFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "vector too long");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s = launch(ctx, gate_sigmoid_mul_kernel, dim3(static_cast<uint32_t>((n + 255) / 256)),
+                                        dim3(256), 0, static_cast<cudaStream_t>(stream), false, x_dev, gate_dev,
+                                        static_cast<uint32_t>(n));
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_mul_silu(oracle_cuda_context* ctx, float* x_dev, const float* z_dev,
+                                                   uint64_t n, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (n == 0) return ok(ctx);
+    if (n > 0xFFFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "vector too long");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s = launch(ctx, mul_silu_kernel, dim3(static_cast<uint32_t>((n + 255) / 256)), dim3(256),
+                                        0, static_cast<cudaStream_t>(stream), false, x_dev, z_dev,
+                                        static_cast<uint32_t>(n));
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_gdn_gates(oracle_cuda_context* ctx, const float* beta_dev,
+                                                    const float* alpha_dev, const float* time_step_bias_dev,
+                                                    const float* decay_dev, uint32_t heads, float* beta_out_dev,
+                                                    float* log_decay_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (heads == 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Qwen3.5 recurrent alpha/beta width mismatch");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s = launch(ctx, gdn_gates_kernel, dim3((heads + 255) / 256), dim3(256), 0,
+                                        static_cast<cudaStream_t>(stream), false, beta_dev, alpha_dev,
+                                        time_step_bias_dev, decay_dev, heads, beta_out_dev, log_decay_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_token_commit(oracle_cuda_context* ctx, const unsigned long long* key_dev,
+                                                       const uint32_t* prompt_dev, uint32_t n_prompt,
+                                                       uint32_t* pos_dev, uint32_t* next_id_dev,
+                                                       uint32_t* tokens_dev, uint32_t tokens_capacity,
+                                                       void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (!key_dev || !pos_dev || !next_id_dev || (n_prompt > 0 && !prompt_dev) || (tokens_capacity > 0 && !tokens_dev))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "token commit pointer is null");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s =
+        launch(ctx, token_commit_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), false, key_dev,
+               prompt_dev, n_prompt, pos_dev, next_id_dev, tokens_dev, tokens_capacity, ctx->status);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }

@@ -1,0 +1,295 @@
+"""Greedy decoding of the Qwen3.5 hybrid model on one B200.
+
+The per-token step is Oracle's execute_qwen35_reference_token
+(src/runtime/qwen35_forward.cpp:400-470) with its blocks
+(src/runtime/qwen35_block.cpp: recurrent 407-604, attention 606-760, MLP and
+residual 300-352) laid out as a sequence of this library's kernels on one
+stream, captured once in a CUDA graph and replayed for every token:
+
+* every weight stays resident in HBM in its GGML bytes; the projections of a
+  block that read the same input run as ONE matvec program (Q8_K contract:
+  ``qkv/z/beta/alpha``, ``q/k/v``, ``gate/up``), or one Oracle-f32-contract
+  matvec each (``contract="f32"``);
+* the KV caches (f32, [token][kv_head][dim]), convolution histories and
+  recurrent states live on the device; the token position is a device counter
+  read by RoPE (a cos/sin table of every position) and attention, so the
+  graph is position-independent;
+* sampling stays on the device: argmax of the logits into a 64-bit key,
+  then ``token_commit`` picks the next input id (the next prompt token while
+  the prompt lasts, else the sampled token, which it also records) and
+  advances the position.  A whole generation is graph replays with no host
+  round trip; the host reads the tokens once at the end.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import CONTRACT_F32, CONTRACT_Q8K, Context, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K
+from .qwen35 import Qwen35Config
+
+
+def tensors_from_gguf(path: str) -> tuple:
+    """(Qwen35Config, [(name, ggml type, gguf dims, uint8 bytes)]) of a
+    Qwen3.5 GGUF file, read with gguf-py's memory-mapped reader; metadata keys
+    as Oracle's load_qwen35_manifest reads them (qwen35_manifest.cpp:151-206)."""
+    import gguf
+
+    r = gguf.GGUFReader(path)
+
+    def val(key):
+        f = r.fields[key]
+        return f.parts[f.data[0]].tolist()[0] if len(f.data) == 1 else [f.parts[i].tolist()[0] for i in f.data]
+
+    cfg = Qwen35Config(
+        hidden=val("qwen35.embedding_length"), ffn=val("qwen35.feed_forward_length"),
+        layers=val("qwen35.block_count"), heads=val("qwen35.attention.head_count"),
+        kv_heads=val("qwen35.attention.head_count_kv"), head_dim=val("qwen35.attention.key_length"),
+        rope_dim=val("qwen35.rope.dimension_count"), rope_sections=tuple(val("qwen35.rope.dimension_sections")),
+        rope_base=float(val("qwen35.rope.freq_base")), conv_kernel=val("qwen35.ssm.conv_kernel"),
+        state_size=val("qwen35.ssm.state_size"), key_heads=val("qwen35.ssm.group_count"),
+        value_heads=val("qwen35.ssm.time_step_rank"), vocab=len(r.fields["tokenizer.ggml.tokens"].data),
+        eps=float(val("qwen35.attention.layer_norm_rms_epsilon")),
+        interval=val("qwen35.full_attention_interval"), context=val("qwen35.context_length"))
+    tensors = []
+    for t in r.tensors:
+        dims = tuple(int(d) for d in t.shape)
+        tensors.append((t.name, int(t.tensor_type), dims, np.asarray(t.data).view(np.uint8).reshape(-1)))
+    return cfg, tensors
+
+
+class Qwen35Decoder:
+    """Resident weights, device state and the captured decode step of one model.
+
+    tensors: [(name, ggml type, gguf dims, uint8 bytes)] as produced by
+    ``qwen35.synthetic_model`` or ``tensors_from_gguf``.  contract "q8k"
+    (GGML's Q8_K activations; Q4_K / Q6_K matrices) or "f32" (Oracle's own
+    f32 contract; any storage type the reference admits)."""
+
+    def __init__(self, ctx: Context, cfg: Qwen35Config, tensors, contract: str = "q8k",
+                 capacity: int | None = None, max_new: int = 4096, device: int = 0):
+        import torch
+
+        if contract not in ("q8k", "f32"):
+            raise ValueError("contract must be 'q8k' or 'f32'")
+        self.torch = torch
+        self.ctx, self.cfg, self.contract = ctx, cfg, contract
+        self.dev = torch.device("cuda", device)
+        self.cap = int(capacity or cfg.context)
+        self.max_new = int(max_new)
+        dev = self.dev
+        self.w = {}
+        for name, qtype, dims, data in tensors:
+            arr = np.ascontiguousarray(data).view(np.uint8)
+            host = torch.from_numpy(arr if arr.flags.writeable else arr.copy())
+            self.w[name] = (int(qtype), tuple(dims), host.to(dev))
+            if contract == "q8k" and len(dims) == 2 and qtype not in (TYPE_F32, TYPE_Q4_K, TYPE_Q6_K) \
+                    and name != "token_embd.weight":
+                raise ValueError(f"{name}: the Q8_K contract runs Q4_K / Q6_K matrices only")
+        H, F = cfg.hidden, cfg.ffn
+        f32 = lambda n: torch.zeros(n, dtype=torch.float32, device=dev)  # noqa: E731
+        self.hidden, self.normed, self.resid, self.branch = f32(H), f32(H), f32(H), f32(H)
+        self.ffn_gate, self.ffn_up, self.ffn_act, self.ffn_out = f32(F), f32(F), f32(F), f32(H)
+        # recurrent blocks
+        self.qkv, self.conv_out, self.z = f32(cfg.conv_channels), f32(cfg.conv_channels), f32(cfg.value_width)
+        self.beta, self.alpha = f32(cfg.value_heads), f32(cfg.value_heads)
+        self.beta_s, self.log_decay = f32(cfg.value_heads), f32(cfg.value_heads)
+        self.rec_out, self.gated = f32(cfg.value_width), f32(cfg.value_width)
+        # attention blocks
+        self.q_full, self.q, self.gate = f32(2 * cfg.q_width), f32(cfg.q_width), f32(cfg.q_width)
+        self.qn, self.k, self.kn, self.v = f32(cfg.q_width), f32(cfg.kv_width), f32(cfg.kv_width), f32(cfg.kv_width)
+        self.attn, self.scores = f32(cfg.q_width), f32(cfg.heads * self.cap)
+        self.logits = f32(cfg.vocab)
+        self.keys, self.values, self.hist, self.state = {}, {}, {}, {}
+        for i in range(cfg.layers):
+            if cfg.is_attention(i):
+                self.keys[i] = f32(self.cap * cfg.kv_width)
+                self.values[i] = f32(self.cap * cfg.kv_width)
+            else:
+                self.hist[i] = f32(cfg.conv_channels * cfg.conv_kernel)
+                self.state[i] = f32(cfg.value_heads * cfg.state_size * cfg.state_size)
+        self.rope_table = f32(self.cap * cfg.rope_dim)
+        ctx.rope_table(cfg.rope_dim, cfg.rope_sections, cfg.rope_base, self.cap, self.rope_table)
+        u32 = lambda n: torch.zeros(n, dtype=torch.int32, device=dev)  # noqa: E731
+        self.pos, self.next_id = u32(1), u32(1)
+        self.prompt, self.tokens = u32(self.cap), u32(self.max_new)
+        self.key = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.stream = torch.cuda.Stream(device=dev)
+        self.graph, self.graph_prompt = None, None
+        self.timer = None  # list of (start, end) CUDA events around projections, when set
+
+    # ---------------------------------------------------------------- pieces
+    def _t(self, name):
+        return self.w[name][2]
+
+    def _vec(self, name):
+        return self.w[name][2].view(self.torch.float32)
+
+    def _project(self, ops, s) -> None:
+        """ops: [(weight name, x, y)] that read inputs produced before the call."""
+        if self.timer is not None:
+            ev = (self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
+            ev[0].record(self.stream)
+        if self.contract == "q8k":
+            prog = []
+            for name, x, y in ops:
+                qtype, dims, w = self.w[name]
+                prog.append((qtype, dims[1], dims[0], w, x, y, False))
+            self.ctx.matvec_program(prog, s)
+        else:
+            for name, x, y in ops:
+                qtype, dims, w = self.w[name]
+                self.ctx.storage_matvec(CONTRACT_F32, qtype, dims[1], dims[0], w, x, y, s)
+        if self.timer is not None:
+            ev[1].record(self.stream)
+            self.timer.append((ev, sum(self.w[name][2].numel() for name, _, _ in ops)))
+
+    def _recurrent(self, i: int, s) -> None:
+        cfg, ctx, p = self.cfg, self.ctx, f"blk.{i}."
+        self._project([(p + "attn_qkv.weight", self.normed, self.qkv), (p + "attn_gate.weight", self.normed, self.z),
+                       (p + "ssm_beta.weight", self.normed, self.beta),
+                       (p + "ssm_alpha.weight", self.normed, self.alpha)], s)
+        ctx.gdn_gates(self.beta, self.alpha, self._vec(p + "ssm_dt.bias"), self._vec(p + "ssm_a"), cfg.value_heads,
+                      self.beta_s, self.log_decay, s)
+        ctx.conv_step(self.qkv, self._vec(p + "ssm_conv1d.weight"), self.hist[i], cfg.conv_channels,
+                      cfg.conv_kernel, True, self.conv_out, s)
+        kw = cfg.key_width
+        ctx.gated_delta_step(self.conv_out[:kw], self.conv_out[kw:2 * kw], self.conv_out[2 * kw:], self.beta_s,
+                             self.log_decay, self.state[i], cfg.value_heads, cfg.state_size, cfg.state_size, cfg.eps,
+                             self.rec_out, s, qk_heads=cfg.key_heads)
+        ctx.rms_norm_rows(self.rec_out, self._vec(p + "ssm_norm.weight"), cfg.value_heads, cfg.state_size, cfg.eps,
+                          self.gated, s)
+        ctx.mul_silu(self.gated, self.z, cfg.value_width, s)
+        self._project([(p + "ssm_out.weight", self.gated, self.branch)], s)
+
+    def _attention(self, i: int, s) -> None:
+        cfg, ctx, p = self.cfg, self.ctx, f"blk.{i}."
+        self._project([(p + "attn_q.weight", self.normed, self.q_full), (p + "attn_k.weight", self.normed, self.k),
+                       (p + "attn_v.weight", self.normed, self.v)], s)
+        ctx.split_query_gate(self.q_full, cfg.heads, cfg.head_dim, self.q, self.gate, s)
+        ctx.rms_norm_rows(self.q, self._vec(p + "attn_q_norm.weight"), cfg.heads, cfg.head_dim, cfg.eps, self.qn, s)
+        ctx.rms_norm_rows(self.k, self._vec(p + "attn_k_norm.weight"), cfg.kv_heads, cfg.head_dim, cfg.eps, self.kn,
+                          s)
+        ctx.rope_at(self.qn, cfg.heads, cfg.head_dim, cfg.rope_dim, self.rope_table, self.cap, self.pos, s)
+        ctx.rope_at(self.kn, cfg.kv_heads, cfg.head_dim, cfg.rope_dim, self.rope_table, self.cap, self.pos, s)
+        ctx.attention_step_at(self.qn, self.kn, self.v, self.keys[i], self.values[i], self.cap, self.pos, cfg.heads,
+                              cfg.kv_heads, cfg.head_dim, cfg.head_dim, self.scores, self.attn, s)
+        ctx.gate_sigmoid_mul(self.attn, self.gate, cfg.q_width, s)
+        self._project([(p + "attn_output.weight", self.attn, self.branch)], s)
+
+    def _enqueue_step(self, n_prompt: int, s) -> None:
+        cfg, ctx = self.cfg, self.ctx
+        H = cfg.hidden
+        et, edims, emb = self.w["token_embd.weight"]
+        ctx.gather_rows(et, edims[1], edims[0], emb, self.next_id, self.hidden, s)
+        for i in range(cfg.layers):
+            p = f"blk.{i}."
+            ctx.rms_norm_rows(self.hidden, self._vec(p + "attn_norm.weight"), 1, H, cfg.eps, self.normed, s)
+            if cfg.is_attention(i):
+                self._attention(i, s)
+            else:
+                self._recurrent(i, s)
+            # finish_block (qwen35_block.cpp:326-352)
+            ctx.add(self.hidden, self.branch, H, self.resid, s)
+            ctx.rms_norm_rows(self.resid, self._vec(p + "post_attention_norm.weight"), 1, H, cfg.eps, self.normed, s)
+            self._project([(p + "ffn_gate.weight", self.normed, self.ffn_gate),
+                           (p + "ffn_up.weight", self.normed, self.ffn_up)], s)
+            ctx.swiglu(self.ffn_gate, self.ffn_up, cfg.ffn, self.ffn_act, s)
+            self._project([(p + "ffn_down.weight", self.ffn_act, self.ffn_out)], s)
+            ctx.add(self.resid, self.ffn_out, H, self.hidden, s)
+        ctx.rms_norm_rows(self.hidden, self._vec("output_norm.weight"), 1, H, cfg.eps, self.normed, s)
+        out = "output.weight" if "output.weight" in self.w else "token_embd.weight"
+        self._project([(out, self.normed, self.logits)], s)
+        ctx.argmax(self.logits, self.key, 0, s)
+        ctx.token_commit(self.key, self.prompt, n_prompt, self.pos, self.next_id, self.tokens, self.max_new, s)
+
+    # ---------------------------------------------------------------- control
+    def reset(self) -> None:
+        """Empty caches and states, position 0 (HybridCache::reset)."""
+        with self.torch.cuda.stream(self.stream):
+            for t in (*self.keys.values(), *self.values.values(), *self.hist.values(), *self.state.values()):
+                t.zero_()
+            self.pos.zero_()
+            self.tokens.zero_()
+        self.stream.synchronize()
+
+    def capture(self, n_prompt: int) -> None:
+        """Capture the step in a CUDA graph (after one uncaptured warm-up step
+        that sizes every scratch buffer; the state is reset afterwards)."""
+        torch = self.torch
+        s = self.stream
+        self.reset()
+        self._enqueue_step(n_prompt, s.cuda_stream)
+        s.synchronize()
+        self.ctx.device_status()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self._enqueue_step(n_prompt, s.cuda_stream)
+        self.graph, self.graph_prompt = g, n_prompt
+        self.reset()
+
+    def step(self) -> None:
+        """Replay one captured step on the decoder's stream (asynchronous)."""
+        with self.torch.cuda.stream(self.stream):
+            self.graph.replay()
+
+    def start(self, prompt) -> None:
+        """Reset and load a prompt; the next step ingests prompt[0]."""
+        torch = self.torch
+        prompt = np.ascontiguousarray(prompt, np.uint32)
+        if prompt.size == 0 or prompt.size > self.cap:
+            raise ValueError("prompt must hold 1 .. capacity tokens")
+        if self.graph is None or self.graph_prompt != prompt.size:
+            self.capture(int(prompt.size))
+        self.reset()
+        with torch.cuda.stream(self.stream):
+            self.prompt[:prompt.size].copy_(torch.from_numpy(prompt.view(np.int32)).to(self.dev, non_blocking=False))
+            self.next_id.fill_(int(prompt[0]))
+        self.stream.synchronize()
+
+    def generate(self, prompt, n_new: int) -> np.ndarray:
+        """Fresh greedy generation: n_new tokens after the prompt
+        (Qwen35GenerationSession::generate_fresh at temperature 0)."""
+        if not 1 <= n_new <= self.max_new:
+            raise ValueError(f"n_new must be in [1, {self.max_new}]")
+        self.start(prompt)
+        with self.torch.cuda.stream(self.stream):
+            for _ in range(len(prompt) + n_new - 1):
+                self.graph.replay()
+        self.stream.synchronize()
+        self.ctx.device_status()
+        return self.tokens[:n_new].cpu().numpy().view(np.uint32).copy()
+
+    def forward(self, token: int) -> np.ndarray:
+        """One step on `token` at the current position; returns the logits."""
+        if self.graph is None:
+            self.capture(1)
+        with self.torch.cuda.stream(self.stream):
+            self.next_id.fill_(int(token))
+            self.graph.replay()
+        self.stream.synchronize()
+        self.ctx.device_status()
+        return self.logits.cpu().numpy().copy()
+
+    def profile_projections(self) -> tuple:
+        """One uncaptured step with CUDA events around every projection call:
+        (weight bytes streamed by the projections, their summed milliseconds,
+        the whole step's milliseconds).  The state is reset afterwards."""
+        torch = self.torch
+        self.timer = []
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(self.stream)
+        self._enqueue_step(self.graph_prompt or 1, self.stream.cuda_stream)
+        b.record(self.stream)
+        self.stream.synchronize()
+        timer, self.timer = self.timer, None
+        self.reset()
+        return (sum(n for _, n in timer), sum(e[0].elapsed_time(e[1]) for e, _ in timer), a.elapsed_time(b))
+
+    def launches_per_step(self) -> int:
+        """Kernels one step launches (counted by the context on an uncaptured step)."""
+        before = self.ctx.launch_count()
+        self._enqueue_step(self.graph_prompt or 1, self.stream.cuda_stream)
+        self.stream.synchronize()
+        n = self.ctx.launch_count() - before
+        self.reset()
+        return n
