@@ -186,6 +186,39 @@ typedef struct oracle_cuda_matvec_op {
 oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops,
                                               uint32_t n_ops, void* stream);
 
+/* Matvec program with activation transforms and residual outputs: the decode
+ * step of a transformer block as few launches.  Per op, on top of
+ * oracle_cuda_matvec_op:
+ *   xform         ORACLE_CUDA_XFORM_NONE: the activation is x_dev;
+ *                 ORACLE_CUDA_XFORM_RMS: (x * inv) * norm_dev[i] with inv =
+ *                 1 / sqrt(sum(x^2) / cols + eps) (double sum, float inverse):
+ *                 Oracle's rms_norm_rows over one row (src/runtime/
+ *                 qwen35_block.cpp:161-188), never written out;
+ *                 ORACLE_CUDA_XFORM_SWIGLU: silu(x) * x2_dev[i] (the MLP
+ *                 activation, qwen35_block.cpp:315-318);
+ *   residual_dev  optional (rows floats): y = residual + W.x, Oracle's
+ *                 add_vectors of the block input and the branch
+ *                 (qwen35_block.cpp:190-200, 333, 349);
+ * each then quantized to Q8_K exactly as oracle_cuda_quantize_q8_k would
+ * quantize the transformed vector.  Ops whose sources (x, xform, x2 / norm,
+ * eps) are identical share one image: an op repeating an earlier op's source
+ * needs no wait (after_previous is then ignored).  No Oracle counterpart:
+ * Oracle runs each projection, norm and add as its own call. */
+#define ORACLE_CUDA_XFORM_NONE 0u
+#define ORACLE_CUDA_XFORM_RMS 1u
+#define ORACLE_CUDA_XFORM_SWIGLU 2u
+typedef struct oracle_cuda_matvec_op_ex {
+    oracle_cuda_matvec_op base;
+    uint32_t xform;
+    float eps;
+    const float* x2_dev;
+    const float* norm_dev;
+    const float* residual_dev;
+} oracle_cuda_matvec_op_ex;
+
+oracle_cuda_status oracle_cuda_matvec_program_ex(oracle_cuda_context* ctx, const oracle_cuda_matvec_op_ex* ops,
+                                                 uint32_t n_ops, void* stream);
+
 /* The same matvec program for callers that cannot allocate device memory:
  * e.g. an engine that has already reserved nearly all of HBM for its own
  * pools, or a latency-critical path on which cudaMalloc, which can synchronise
@@ -328,6 +361,39 @@ oracle_cuda_status oracle_cuda_token_commit(oracle_cuda_context* ctx, const unsi
                                             const uint32_t* prompt_dev, uint32_t n_prompt, uint32_t* pos_dev,
                                             uint32_t* next_id_dev, uint32_t* tokens_dev, uint32_t tokens_capacity,
                                             void* stream);
+/* Fused block cores (graph-replayable, position in device memory):
+ *   gdn_core        a Gated DeltaNet block from its projections to the vector
+ *                   its output projection reads (qwen35_block.cpp:472-592):
+ *                   gates, depthwise conv + SiLU (history [2][channels][kernel],
+ *                   double-buffered by position parity: zero both halves to
+ *                   reset), gated_delta_step on state [value_heads][head_dim]
+ *                   [head_dim] with q / k of key head h % key_heads, RMSNorm
+ *                   of each head's output, * silu(z); key and value head widths
+ *                   equal (Oracle's layout: both ssm.state_size)
+ *   attention_prep_at  per query head: the query half of q_full [heads][2 *
+ *                   head_dim], its RMSNorm and RoPE (q_out); per KV head the
+ *                   same for the key, appended with the value at *pos
+ *   attention_core_at  scores, softmax and values over the cache (no append),
+ *                   times sigmoid(gate) when gate_dev is given (gate of head h
+ *                   at gate_dev + h * gate_stride) */
+oracle_cuda_status oracle_cuda_gdn_core(oracle_cuda_context* ctx, const float* qkv_dev, const float* z_dev,
+                                        const float* beta_dev, const float* alpha_dev,
+                                        const float* time_step_bias_dev, const float* decay_dev,
+                                        const float* conv_weights_dev, float* history_dev, float* state_dev,
+                                        const float* norm_dev, uint32_t key_heads, uint32_t value_heads,
+                                        uint32_t head_dim, uint32_t conv_kernel, float eps, const uint32_t* pos_dev,
+                                        float* out_dev, void* stream);
+oracle_cuda_status oracle_cuda_attention_prep_at(oracle_cuda_context* ctx, const float* q_full_dev, const float* k_dev,
+                                                 const float* v_dev, const float* q_norm_dev, const float* k_norm_dev,
+                                                 float eps, const float* table_dev, uint64_t rotary_dim,
+                                                 uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                                                 float* keys_dev, float* values_dev, uint64_t capacity,
+                                                 const uint32_t* pos_dev, float* q_out_dev, void* stream);
+oracle_cuda_status oracle_cuda_attention_core_at(oracle_cuda_context* ctx, const float* q_dev, const float* keys_dev,
+                                                 const float* values_dev, uint64_t capacity, const uint32_t* pos_dev,
+                                                 uint32_t q_heads, uint32_t kv_heads, uint32_t key_dim,
+                                                 uint32_t value_dim, const float* gate_dev, uint32_t gate_stride,
+                                                 float* scores_dev, float* out_dev, void* stream);
 oracle_cuda_status oracle_cuda_gdn_gates(oracle_cuda_context* ctx, const float* beta_dev, const float* alpha_dev,
                                          const float* time_step_bias_dev, const float* decay_dev, uint32_t heads,
                                          float* beta_out_dev, float* log_decay_dev, void* stream);

@@ -84,8 +84,16 @@ class MatvecOp(C.Structure):
                 ("x_dev", C.c_void_p), ("y_dev", C.c_void_p)]
 
 
+class MatvecOpEx(C.Structure):
+    """oracle_cuda_matvec_op_ex of include/oracle_cuda.h."""
+    _fields_ = [("base", MatvecOp), ("xform", C.c_uint32), ("eps", C.c_float), ("x2_dev", C.c_void_p),
+                ("norm_dev", C.c_void_p), ("residual_dev", C.c_void_p)]
+
+
+XFORM_NONE, XFORM_RMS, XFORM_SWIGLU = 0, 1, 2
 PROGRAM_MAX_OPS = 16
 _proto("oracle_cuda_matvec_program", [_vp, C.POINTER(MatvecOp), _u32, _vp])
+_proto("oracle_cuda_matvec_program_ex", [_vp, C.POINTER(MatvecOpEx), _u32, _vp])
 _proto("oracle_cuda_matvec_program_noalloc", [C.POINTER(MatvecOp), _u32, _vp])
 NOALLOC_IMAGE_BYTES = 65536
 
@@ -138,6 +146,12 @@ _proto("oracle_cuda_gate_sigmoid_mul", [_vp, _vp, _vp, _u64, _vp])
 _proto("oracle_cuda_mul_silu", [_vp, _vp, _vp, _u64, _vp])
 _proto("oracle_cuda_gdn_gates", [_vp, _vp, _vp, _vp, _vp, _u32, _vp, _vp, _vp])
 _proto("oracle_cuda_token_commit", [_vp, _vp, _vp, _u32, _vp, _vp, _vp, _u32, _vp])
+_proto("oracle_cuda_gdn_core", [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32,
+                                C.c_float, _vp, _vp, _vp])
+_proto("oracle_cuda_attention_prep_at", [_vp, _vp, _vp, _vp, _vp, _vp, C.c_float, _vp, _u64, _u32, _u32, _u32, _vp,
+                                         _vp, _u64, _vp, _vp, _vp])
+_proto("oracle_cuda_attention_core_at", [_vp, _vp, _vp, _vp, _u64, _vp, _u32, _u32, _u32, _u32, _vp, _u32, _vp, _vp,
+                                         _vp])
 _proto("oracle_cuda_swiglu", [_vp, _vp, _vp, _u64, _vp, _vp])
 _proto("oracle_cuda_add", [_vp, _vp, _vp, _u64, _vp, _vp])
 IPC_HANDLE_BYTES = 64
@@ -396,6 +410,20 @@ class Context:
             arr[i] = MatvecOp(qtype, 1 if after else 0, rows, cols, _addr(w), _nbytes(w), _addr(x), _addr(y))
         self._check(_lib.oracle_cuda_matvec_program(self._h, arr, len(ops), _stream(stream)))
 
+    def matvec_program_ex(self, ops, stream=None) -> None:
+        """ops: sequence of dicts with keys qtype, rows, cols, w, x, y and
+        optional after (bool), xform (XFORM_*), eps, x2, norm, residual."""
+        arr = (MatvecOpEx * len(ops))()
+        for i, o in enumerate(ops):
+            arr[i].base = MatvecOp(o["qtype"], 1 if o.get("after") else 0, o["rows"], o["cols"], _addr(o["w"]),
+                                   _nbytes(o["w"]), _addr(o["x"]), _addr(o["y"]))
+            arr[i].xform = o.get("xform", XFORM_NONE)
+            arr[i].eps = o.get("eps", 0.0)
+            arr[i].x2_dev = _addr(o.get("x2"))
+            arr[i].norm_dev = _addr(o.get("norm"))
+            arr[i].residual_dev = _addr(o.get("residual"))
+        self._check(_lib.oracle_cuda_matvec_program_ex(self._h, arr, len(ops), _stream(stream)))
+
     def gather_rows(self, qtype, rows, cols, w, ids, out, stream=None, w_nbytes=None) -> None:
         """oracle_cuda_gather_rows: out[t] = decode(row ids[t]) (device uint32 ids, f32 out)."""
         self._check(_lib.oracle_cuda_gather_rows(self._h, qtype, rows, cols, _addr(w),
@@ -473,6 +501,26 @@ class Context:
     def token_commit(self, key, prompt, n_prompt, pos, next_id, tokens, tokens_capacity, stream=None) -> None:
         self._check(_lib.oracle_cuda_token_commit(self._h, _addr(key), _addr(prompt), n_prompt, _addr(pos),
                                                   _addr(next_id), _addr(tokens), tokens_capacity, _stream(stream)))
+
+    def gdn_core(self, qkv, z, beta, alpha, time_step_bias, decay, conv_weights, history, state, norm, key_heads,
+                 value_heads, head_dim, conv_kernel, eps, pos, out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_gdn_core(self._h, _addr(qkv), _addr(z), _addr(beta), _addr(alpha),
+                                              _addr(time_step_bias), _addr(decay), _addr(conv_weights),
+                                              _addr(history), _addr(state), _addr(norm), key_heads, value_heads,
+                                              head_dim, conv_kernel, eps, _addr(pos), _addr(out), _stream(stream)))
+
+    def attention_prep_at(self, q_full, k, v, q_norm, k_norm, eps, table, rotary_dim, q_heads, kv_heads, head_dim,
+                          keys, values, capacity, pos, q_out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_attention_prep_at(self._h, _addr(q_full), _addr(k), _addr(v), _addr(q_norm),
+                                                       _addr(k_norm), eps, _addr(table), rotary_dim, q_heads,
+                                                       kv_heads, head_dim, _addr(keys), _addr(values), capacity,
+                                                       _addr(pos), _addr(q_out), _stream(stream)))
+
+    def attention_core_at(self, q, keys, values, capacity, pos, q_heads, kv_heads, key_dim, value_dim, gate,
+                          gate_stride, scores, out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_attention_core_at(self._h, _addr(q), _addr(keys), _addr(values), capacity,
+                                                       _addr(pos), q_heads, kv_heads, key_dim, value_dim, _addr(gate),
+                                                       gate_stride, _addr(scores), _addr(out), _stream(stream)))
 
     def gdn_gates(self, beta, alpha, time_step_bias, decay, heads, beta_out, log_decay, stream=None) -> None:
         self._check(_lib.oracle_cuda_gdn_gates(self._h, _addr(beta), _addr(alpha), _addr(time_step_bias),

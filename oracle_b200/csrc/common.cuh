@@ -167,4 +167,30 @@ __device__ __forceinline__ int sbyte(uint32_t w, int i) {
     return static_cast<int>(static_cast<int8_t>((w >> (8 * i)) & 0xFFu));
 }
 
+// sigmoid and silu of Oracle's block code (qwen35_block.cpp:138-159): float
+// arithmetic around the float exponential.
+__device__ __forceinline__ float ref_sigmoid(float v) {
+    if (v >= 0.0f) {
+        const float e = expf(-v);
+        return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+    }
+    const float e = expf(v);
+    return __fdiv_rn(e, __fadd_rn(1.0f, e));
+}
+
+__device__ __forceinline__ float ref_silu(float v) { return __fmul_rn(v, ref_sigmoid(v)); }
+
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
+    return v;
+}
+
+// 1 / sqrt(mean + eps) rounded to float, from a double sum of squares
+// (rms_norm_rows, qwen35_block.cpp:174-180).
+__device__ __forceinline__ float rms_inverse(double sum_squares, uint32_t width, float eps) {
+    const double mean = __ddiv_rn(sum_squares, static_cast<double>(width));
+    return __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(mean, static_cast<double>(eps)))));
+}
+
 }  // namespace oracle_cuda

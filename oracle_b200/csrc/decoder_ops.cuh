@@ -23,23 +23,6 @@
 
 namespace oracle_cuda {
 
-__device__ __forceinline__ float ref_sigmoid(float v) {
-    if (v >= 0.0f) {
-        const float e = expf(-v);
-        return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
-    }
-    const float e = expf(v);
-    return __fdiv_rn(e, __fadd_rn(1.0f, e));
-}
-
-__device__ __forceinline__ float ref_silu(float v) { return __fmul_rn(v, ref_sigmoid(v)); }
-
-__device__ __forceinline__ double warp_sum_f64(double v) {
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
-    return v;
-}
-
 // Block-wide double sum (blockDim.x a multiple of 32, <= 1024); every thread gets it.
 __device__ __forceinline__ double block_sum_f64(double v, double* scratch) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -62,9 +45,7 @@ __global__ void __launch_bounds__(256) rms_norm_rows_kernel(const float* __restr
         const double v = static_cast<double>(x[c]);
         s = __dadd_rn(s, __dmul_rn(v, v));  // product and sum each rounded, as in the reference
     }
-    const double total = block_sum_f64(s, scratch);
-    const double mean = __ddiv_rn(total, static_cast<double>(width));
-    const float inv = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(mean, static_cast<double>(eps)))));
+    const float inv = rms_inverse(block_sum_f64(s, scratch), width, eps);
     for (uint32_t c = threadIdx.x; c < width; c += blockDim.x) y[c] = __fmul_rn(__fmul_rn(x[c], inv), w[c]);
 }
 

@@ -103,7 +103,8 @@ __global__ void __launch_bounds__(256) attention_output_pos_kernel(float* __rest
                                                                    const float* __restrict__ values,
                                                                    const uint32_t* __restrict__ pos, uint32_t capacity,
                                                                    uint32_t q_heads, uint32_t kv_heads,
-                                                                   uint32_t value_dim, float* __restrict__ out,
+                                                                   uint32_t value_dim, const float* __restrict__ gate,
+                                                                   uint32_t gate_stride, float* __restrict__ out,
                                                                    DeviceStatus* st) {
     __shared__ double scratch[32];
     __shared__ float fmax_s[32];
@@ -138,6 +139,8 @@ __global__ void __launch_bounds__(256) attention_output_pos_kernel(float* __rest
         const uint64_t stride = static_cast<uint64_t>(kv_heads) * value_dim;
         float acc = 0.0f;
         for (uint32_t t = 0; t < tokens; ++t) acc = __fadd_rn(acc, __fmul_rn(sc[t], __ldg(vp + t * stride)));
+        // the output gate, attention *= sigmoid(gate) (qwen35_block.cpp:738-742)
+        if (gate) acc = __fmul_rn(acc, ref_sigmoid(gate[static_cast<uint64_t>(h) * gate_stride + d]));
         out[static_cast<uint64_t>(h) * value_dim + d] = acc;
     }
 }
@@ -178,6 +181,152 @@ __global__ void __launch_bounds__(256) gdn_gates_kernel(const float* __restrict_
 __global__ void __launch_bounds__(256) mul_silu_kernel(float* __restrict__ x, const float* __restrict__ z, uint32_t n) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) x[i] = __fmul_rn(x[i], ref_silu(z[i]));
+}
+
+// ---------------------------------------------------------------- fused block cores
+//
+// A Gated DeltaNet block between its input projections and its output
+// projection, as ONE kernel: Oracle's recurrent block (qwen35_block.cpp:
+// 472-592) from the projected qkv / z / beta / alpha to the gated vector the
+// output projection reads.  One CTA per value head, thread t = value (and key)
+// index, key_dim == value_dim == kD; thread t keeps state column t in
+// registers for the whole update (one read and one write of the state):
+//   gates      beta = sigmoid(beta), log_decay = softplus(alpha + dt_bias) * a
+//   conv       the depthwise causal conv + SiLU of the head's q, k (key head
+//              h % key_heads, repeat_heads_tiled) and v channels; the
+//              convolution history is double-buffered by position parity
+//              (read slot pos & 1, write the other), so the CTAs that share a
+//              key head read a history nobody writes during the step; the
+//              CTA h < key_heads writes the shared q / k channels
+//   delta      gated_delta_step (reference_kernels.cpp:221-335) on the head's
+//              [key][value] state
+//   out        rms_norm_rows over the head's row, then * silu(z)
+// Each stage keeps the operations and order of the corresponding separate
+// kernel (decoder_ops.cuh), so results are those of the unfused sequence.
+template <int kD>
+__global__ void __launch_bounds__(kD) gdn_core_kernel(const float* __restrict__ qkv, const float* __restrict__ z,
+                                                      const float* __restrict__ beta_in, const float* __restrict__ alpha,
+                                                      const float* __restrict__ dt_bias,
+                                                      const float* __restrict__ decay_a,
+                                                      const float* __restrict__ conv_w, float* hist, float* state,
+                                                      const float* __restrict__ norm_w, uint32_t key_heads,
+                                                      uint32_t value_heads, uint32_t conv_kernel, float eps,
+                                                      const uint32_t* __restrict__ pos, float* __restrict__ out) {
+    __shared__ float nq[kD], nk[kD];
+    __shared__ double scratch[32];
+    const uint32_t h = blockIdx.x, t = threadIdx.x;
+    // the head's state column t, [key d][value t], held in registers: loads
+    // issued up front, independent of everything computed before the update
+    float* sh = state + static_cast<uint64_t>(h) * kD * kD + t;
+    float col[kD];
+#pragma unroll
+    for (int d = 0; d < kD; ++d) col[d] = sh[d * kD];
+    const uint32_t kh = h % key_heads;
+    const uint32_t key_width = key_heads * kD;
+    const uint32_t channels = 2 * key_width + value_heads * kD;
+    const uint32_t K = conv_kernel;
+    const uint32_t slot = *pos & 1u;
+    const float* hin = hist + static_cast<uint64_t>(slot) * channels * K;
+    float* hout = hist + static_cast<uint64_t>(slot ^ 1u) * channels * K;
+    auto conv = [&](uint32_t c, bool write) -> float {
+        const float* hc = hin + static_cast<uint64_t>(c) * K;
+        const float* wc = conv_w + static_cast<uint64_t>(c) * K;
+        float* oc = hout + static_cast<uint64_t>(c) * K;
+        double sum = 0.0;
+        for (uint32_t i = 0; i < K; ++i) {
+            const float v = i + 1 < K ? hc[i + 1] : qkv[c];
+            if (write) oc[i] = v;
+            sum = __dadd_rn(sum, __dmul_rn(static_cast<double>(v), static_cast<double>(wc[i])));
+        }
+        return ref_silu(__double2float_rn(sum));
+    };
+    const bool owner = h < key_heads;
+    const float q = conv(kh * kD + t, owner);
+    const float k = conv(key_width + kh * kD + t, owner);
+    const float v = conv(2 * key_width + h * kD + t, true);
+    // gated_delta_step: l2-normalised q (scaled by 1/sqrt(key_dim)) and k
+    const double q_norm = block_sum_f64(__dmul_rn(static_cast<double>(q), static_cast<double>(q)), scratch);
+    const double k_norm = block_sum_f64(__dmul_rn(static_cast<double>(k), static_cast<double>(k)), scratch);
+    const double e = static_cast<double>(eps);
+    const float inv_q = __double2float_rn(__ddiv_rn(1.0, fmax(__dsqrt_rn(q_norm), e)));
+    const float inv_k = __double2float_rn(__ddiv_rn(1.0, fmax(__dsqrt_rn(k_norm), e)));
+    const float q_scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(kD)));
+    nq[t] = __fmul_rn(__fmul_rn(q, inv_q), q_scale);
+    nk[t] = __fmul_rn(k, inv_k);
+    __syncthreads();
+    const float b = ref_sigmoid(beta_in[h]);
+    const float log_decay = __fmul_rn(ref_softplus(__fadd_rn(alpha[h], dt_bias[h])), decay_a[h]);
+    const float decay = expf(log_decay);
+    float mem = 0.0f;
+#pragma unroll
+    for (int d = 0; d < kD; ++d) {
+        col[d] = __fmul_rn(col[d], decay);
+        mem = __fadd_rn(mem, __fmul_rn(col[d], nk[d]));
+    }
+    const float delta = __fmul_rn(__fsub_rn(v, mem), b);
+    double o = 0.0;
+#pragma unroll
+    for (int d = 0; d < kD; ++d) {
+        col[d] = __fadd_rn(col[d], __fmul_rn(nk[d], delta));
+        o = __dadd_rn(o, __dmul_rn(static_cast<double>(col[d]), static_cast<double>(nq[d])));
+    }
+#pragma unroll
+    for (int d = 0; d < kD; ++d) sh[d * kD] = col[d];
+    const float of = __double2float_rn(o);
+    // rms_norm_rows over the head's row, then gated *= silu(z)
+    const float inv = rms_inverse(block_sum_f64(__dmul_rn(static_cast<double>(of), static_cast<double>(of)), scratch),
+                                  kD, eps);
+    const float g = __fmul_rn(__fmul_rn(of, inv), norm_w[t]);
+    out[static_cast<uint64_t>(h) * kD + t] = __fmul_rn(g, ref_silu(z[static_cast<uint64_t>(h) * kD + t]));
+}
+
+// The gated attention block up to its softmax, as one kernel per query head
+// (thread t = dimension, blockDim.x = head_dim): the query half of the joint
+// query/gate projection (qwen35_block.cpp:676-688), its per-head RMSNorm
+// (:693-700) and RoPE at *pos; the CTA h = group * kv_head also normalises
+// and rotates that KV head's key and appends key and value to the cache at
+// *pos (KvCache::append).  Position-table overflow: kDevKvOverflow.
+__global__ void attention_prep_kernel(const float* __restrict__ q_full, const float* __restrict__ k_proj,
+                                      const float* __restrict__ v_proj, const float* __restrict__ q_norm,
+                                      const float* __restrict__ k_norm, float eps, const float* __restrict__ table,
+                                      uint32_t half, uint32_t q_heads, uint32_t kv_heads, float* keys, float* values,
+                                      uint32_t capacity, const uint32_t* __restrict__ pos, float* __restrict__ q_out,
+                                      DeviceStatus* st) {
+    __shared__ double scratch[32];
+    __shared__ float row[1024];
+    const uint32_t D = blockDim.x, h = blockIdx.x, t = threadIdx.x;
+    const uint32_t p = *pos;
+    if (p >= capacity) {
+        if (h == 0 && t == 0) report_overflow(st, p);
+        return;
+    }
+    const float* rope = table + static_cast<uint64_t>(p) * half * 2;
+    auto norm_rope = [&](float x, const float* w) -> float {
+        const float inv = rms_inverse(block_sum_f64(__dmul_rn(static_cast<double>(x), static_cast<double>(x)), scratch),
+                                      D, eps);
+        row[t] = __fmul_rn(__fmul_rn(x, inv), w[t]);
+        __syncthreads();
+        float r = row[t];
+        if (t < half) {
+            const float a = row[t], b = row[t + half], c = rope[2 * t], s = rope[2 * t + 1];
+            r = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        } else if (t < 2 * half) {
+            const uint32_t f = t - half;
+            const float a = row[f], b = row[t], c = rope[2 * f], s = rope[2 * f + 1];
+            r = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+        }
+        __syncthreads();
+        return r;
+    };
+    q_out[static_cast<uint64_t>(h) * D + t] = norm_rope(q_full[static_cast<uint64_t>(h) * 2 * D + t], q_norm);
+    const uint32_t group = q_heads / kv_heads;
+    if (h % group == 0) {
+        const uint32_t kvh = h / group;
+        const float kr = norm_rope(k_proj[static_cast<uint64_t>(kvh) * D + t], k_norm);
+        const uint64_t at = (static_cast<uint64_t>(p) * kv_heads + kvh) * D + t;
+        keys[at] = kr;
+        values[at] = v_proj[static_cast<uint64_t>(kvh) * D + t];
+    }
 }
 
 }  // namespace oracle_cuda

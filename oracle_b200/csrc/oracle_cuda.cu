@@ -55,6 +55,8 @@ struct oracle_cuda_context {
     unsigned int* program_counters = nullptr;  // kProgramMaxOps + 1, zero between launches
     uint8_t* image_scratch = nullptr;          // prebuilt activation images of programs
     uint64_t image_scratch_bytes = 0;
+    uint8_t* act_scratch = nullptr;            // SwiGLU activations formed in program epilogues
+    uint64_t act_scratch_bytes = 0;
     std::string last_error;
     std::set<const void*> smem_configured;
     // resident copies for the host-pointer drop-ins
@@ -531,6 +533,7 @@ oracle_cuda_status oracle_cuda_destroy(oracle_cuda_context* ctx) {
     if (ctx->status) cudaFree(ctx->status);
     if (ctx->program_counters) cudaFree(ctx->program_counters);
     if (ctx->image_scratch) cudaFree(ctx->image_scratch);
+    if (ctx->act_scratch) cudaFree(ctx->act_scratch);
     if (ctx->gemm_x) cudaFree(ctx->gemm_x);
     if (ctx->argmax_key) cudaFree(ctx->argmax_key);
     delete ctx;
@@ -686,19 +689,42 @@ namespace {
 
 constexpr uint64_t kGatherHeader = 256;
 
-oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops, uint32_t n_ops,
+oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matvec_op_ex* ops, uint32_t n_ops,
                                void* stream, const oracle_cuda_peer_group* group);
+
+oracle_cuda_status program_run_base(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops, uint32_t n_ops,
+                                    void* stream, const oracle_cuda_peer_group* group) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (!ops || n_ops == 0 || n_ops > kProgramMaxOps)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                    "a matvec program holds 1 to " + std::to_string(kProgramMaxOps) + " ops");
+    oracle_cuda_matvec_op_ex ex[kProgramMaxOps] = {};
+    for (uint32_t k = 0; k < n_ops; ++k) ex[k].base = ops[k];
+    return program_run(ctx, ex, n_ops, stream, group);
+}
 
 }  // namespace
 
 oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops,
                                               uint32_t n_ops, void* stream) {
+    return program_run_base(ctx, ops, n_ops, stream, nullptr);
+}
+
+oracle_cuda_status oracle_cuda_matvec_program_ex(oracle_cuda_context* ctx, const oracle_cuda_matvec_op_ex* ops,
+                                                 uint32_t n_ops, void* stream) {
     return program_run(ctx, ops, n_ops, stream, nullptr);
 }
 
 namespace {
 
-oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops, uint32_t n_ops,
+// Two ops read the same activation image when their sources are identical.
+bool same_source(const oracle_cuda_matvec_op_ex& a, const oracle_cuda_matvec_op_ex& b) {
+    return a.base.x_dev == b.base.x_dev && a.base.cols == b.base.cols && a.xform == b.xform &&
+           (a.xform != ORACLE_CUDA_XFORM_SWIGLU || a.x2_dev == b.x2_dev) &&
+           (a.xform != ORACLE_CUDA_XFORM_RMS || (a.norm_dev == b.norm_dev && a.eps == b.eps));
+}
+
+oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matvec_op_ex* ops, uint32_t n_ops,
                                void* stream, const oracle_cuda_peer_group* group) {
     if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
     if (!ops || n_ops == 0 || n_ops > kProgramMaxOps)
@@ -707,9 +733,16 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
     ProgramParams pp{};
     pp.n_ops = n_ops;
     uint64_t max_rows = 0, stage = 0;
-    uint32_t act_total = 0;
     for (uint32_t k = 0; k < n_ops; ++k) {
-        const oracle_cuda_matvec_op& o = ops[k];
+        const oracle_cuda_matvec_op_ex& e = ops[k];
+        if (e.xform > ORACLE_CUDA_XFORM_SWIGLU)
+            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "op " + std::to_string(k) + ": unknown activation transform");
+        if (e.xform == ORACLE_CUDA_XFORM_RMS && (!e.norm_dev || !(e.eps > 0.0f) || !std::isfinite(e.eps)))
+            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                        "op " + std::to_string(k) + ": RMS transform needs weights and a positive finite epsilon");
+        if (e.xform == ORACLE_CUDA_XFORM_SWIGLU && !e.x2_dev)
+            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "op " + std::to_string(k) + ": SwiGLU transform needs up");
+        const oracle_cuda_matvec_op& o = e.base;
         uint64_t rb = 0, batch = 0;
         oracle_cuda_status st = validate_matvec(ctx, ORACLE_CUDA_CONTRACT_Q8K, o.type, o.rows, o.cols, o.w_nbytes,
                                                 o.cols, o.rows, &rb, &batch);
@@ -729,9 +762,11 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         p.type = o.type;
         p.nb = static_cast<uint32_t>(o.cols / 256);
         p.after_previous = (o.after_previous && k > 0) ? 1u : 0u;
-        if (p.after_previous) pp.ops[k - 1].publish = 1u;
-        p.act_offset = act_total;
-        act_total += q8k_image_bytes(p.nb);
+        pp.ext[k].xform = e.xform;
+        pp.ext[k].eps = e.eps;
+        pp.ext[k].x2 = e.x2_dev;
+        pp.ext[k].norm = e.norm_dev;
+        p.residual = e.residual_dev;
         uint64_t R = ctx->stage_target / rb;
         if (R > uint64_t(kProgramWarps)) R = kProgramWarps;
         if (R < 1) R = 1;
@@ -740,22 +775,70 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         if (sb > stage) stage = sb;
         if (o.rows > max_rows) max_rows = o.rows;
     }
-    pp.act_bytes = act_total;
+    // A SwiGLU op whose gate and up are outputs of two earlier ops of this
+    // launch over the same rows: the later of the two forms silu(gate) * up
+    // row by row in its epilogue (once per element, by the CTA that owns the
+    // row in both ops), and the SwiGLU op reads that vector plainly.
+    {
+        uint64_t need = 0;
+        for (uint32_t j = 0; j < n_ops; ++j)
+            if (ops[j].xform == ORACLE_CUDA_XFORM_SWIGLU) need += ops[j].base.cols * sizeof(float);
+        if (need > 0 && !group) {
+            oracle_cuda_status gs = grow_device(ctx, ctx->act_scratch, ctx->act_scratch_bytes, need);
+            if (gs != ORACLE_CUDA_OK) return gs;
+        }
+        uint64_t used = 0;
+        for (uint32_t j = 0; j < n_ops && !group; ++j) {
+            if (ops[j].xform != ORACLE_CUDA_XFORM_SWIGLU) continue;
+            int a = -1, b = -1;
+            for (uint32_t i = 0; i < j; ++i) {
+                if (ops[i].base.y_dev == ops[j].base.x_dev) a = static_cast<int>(i);
+                if (ops[i].base.y_dev == ops[j].x2_dev) b = static_cast<int>(i);
+            }
+            if (a < 0 || b < 0 || a == b || ops[a].base.rows != ops[j].base.cols ||
+                ops[b].base.rows != ops[j].base.cols || pp.ext[a].act || pp.ext[b].act)
+                continue;
+            const int later = a > b ? a : b;
+            float* act = reinterpret_cast<float*>(ctx->act_scratch + used);
+            used += ops[j].base.cols * sizeof(float);
+            pp.ext[later].act = act;
+            // later == b: this op computes up, `other` is the gate output; else the reverse
+            pp.ext[later].other = later == b ? ops[a].base.y_dev : ops[b].base.y_dev;
+            pp.ext[later].other_is_gate = later == b ? 1u : 0u;
+            pp.ops[j].x = act;
+            pp.ext[j].xform = kXformNone;
+            pp.ext[j].x2 = nullptr;
+        }
+    }
     // Images of ops whose activation comes from outside the launch are built
     // once by quantize_images_kernel into the scratch region, laid out with
-    // the dependent ops' images last, so one contiguous copy serves them.
+    // the dependent ops' images last, so one contiguous copy serves them.  An
+    // op whose source equals an earlier op's shares that op's image: it needs
+    // neither a build nor a wait of its own.
     ImageJobs jobs{};
-    uint32_t prebuilt = 0, blocks = 0;
+    uint32_t prebuilt = 0, blocks = 0, act_total = 0;
     {
+        int owner[kProgramMaxOps];
+        for (uint32_t k = 0; k < n_ops; ++k) {
+            owner[k] = -1;
+            for (uint32_t j = 0; j < k && owner[k] < 0; ++j)
+                if (owner[j] < 0 && same_source(ops[j], ops[k])) owner[k] = static_cast<int>(j);
+            if (owner[k] >= 0) pp.ops[k].after_previous = 0u;
+        }
         uint32_t off = 0;
         for (uint32_t k = 0; k < n_ops; ++k)
-            if (!pp.ops[k].after_previous) {
+            if (owner[k] < 0 && !pp.ops[k].after_previous) {
                 pp.ops[k].act_offset = off;
                 pp.ops[k].prebuilt = 1u;
-                jobs.x[jobs.n_jobs] = pp.ops[k].x;
-                jobs.nb[jobs.n_jobs] = pp.ops[k].nb;
-                jobs.offset[jobs.n_jobs] = off;
-                jobs.first_block[jobs.n_jobs] = blocks;
+                const uint32_t jn = jobs.n_jobs;
+                jobs.x[jn] = pp.ops[k].x;
+                jobs.x2[jn] = pp.ext[k].x2;
+                jobs.norm[jn] = pp.ext[k].norm;
+                jobs.eps[jn] = pp.ext[k].eps;
+                jobs.xform[jn] = pp.ext[k].xform;
+                jobs.nb[jn] = pp.ops[k].nb;
+                jobs.offset[jn] = off;
+                jobs.first_block[jn] = blocks;
                 blocks += pp.ops[k].nb;
                 jobs.n_jobs++;
                 off += q8k_image_bytes(pp.ops[k].nb);
@@ -763,11 +846,18 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         prebuilt = off;
         jobs.first_block[jobs.n_jobs] = blocks;
         for (uint32_t k = 0; k < n_ops; ++k)
-            if (pp.ops[k].after_previous) {
+            if (owner[k] < 0 && pp.ops[k].after_previous) {
                 pp.ops[k].act_offset = off;
+                pp.ext[k].build = 1u;
                 off += q8k_image_bytes(pp.ops[k].nb);
             }
+        for (uint32_t k = 0; k < n_ops; ++k)
+            if (owner[k] >= 0) pp.ops[k].act_offset = pp.ops[owner[k]].act_offset;
+        for (uint32_t k = 1; k < n_ops; ++k)
+            if (pp.ops[k].after_previous) pp.ops[k - 1].publish = 1u;
+        act_total = off + 256;  // + reduction scratch
     }
+    pp.act_bytes = act_total;
     const uint64_t budget = ctx->smem_budget - stream_barrier_bytes(16) - pp.act_bytes;
     if (pp.act_bytes > 96 * 1024 || stage * 2 > budget)
         return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "matvec program rows too long for the shared-memory stage ring");
@@ -776,7 +866,7 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
     pp.stages = static_cast<uint32_t>(S);
     pp.stage_bytes = static_cast<uint32_t>(stage);
     pp.copy_chunk = ctx->copy_chunk;
-    pp.max_inflight = ctx->max_inflight;
+    pp.max_inflight = ctx->max_inflight < pp.stages ? ctx->max_inflight : pp.stages;
     pp.prebuilt_bytes = prebuilt;
     pp.counters = ctx->program_counters;
     pp.status = ctx->status;
@@ -787,8 +877,8 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         const float* lo = reinterpret_cast<const float*>(group->local + kGatherHeader);
         const float* hi = lo + group->data_bytes / sizeof(float);
         for (uint32_t k = 0; k < n_ops; ++k) {
-            const float* y0 = ops[k].y_dev;
-            if (y0 < lo || y0 + ops[k].rows > hi)
+            const float* y0 = ops[k].base.y_dev;
+            if (y0 < lo || y0 + ops[k].base.rows > hi)
                 return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
                             "op " + std::to_string(k) + ": output must lie inside the peer group's gather buffer");
         }
@@ -818,8 +908,8 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
     int types = 0;
     bool short_rows = true;
     for (uint32_t k = 0; k < n_ops; ++k) {
-        types |= ops[k].type == kTypeQ4_K ? 1 : 2;
-        short_rows = short_rows && ops[k].cols <= 16 * 256;
+        types |= ops[k].base.type == kTypeQ4_K ? 1 : 2;
+        short_rows = short_rows && ops[k].base.cols <= 16 * 256;
     }
     if (types == 2 && short_rows) types = 4;
     auto kernel = types == 1 ? matvec_program_kernel<kProgramWarps, 1>
@@ -915,7 +1005,7 @@ extern "C" oracle_cuda_status oracle_cuda_matvec_program_allgather(oracle_cuda_c
                                                                    const oracle_cuda_matvec_op* ops, uint32_t n_ops,
                                                                    void* stream) {
     if (!group) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "peer group is null");
-    return program_run(ctx, ops, n_ops, stream, group);
+    return program_run_base(ctx, ops, n_ops, stream, group);
 }
 
 oracle_cuda_status oracle_cuda_weight_upload(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
@@ -1207,9 +1297,10 @@ extern "C" oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cu
     for (uint32_t k = 0; k < n_ops; ++k)
         if (pp.ops[k].after_previous) {
             pp.ops[k].act_offset = off;
+            pp.ext[k].build = 1u;
             off += q8k_image_bytes(pp.ops[k].nb);
         }
-    pp.act_bytes = off;
+    pp.act_bytes = off + 256;  // + reduction scratch
     const uint64_t budget = uint64_t(dev->smem_optin) - stream_barrier_bytes(16) - pp.act_bytes;
     if (pp.act_bytes > 96 * 1024 || stage * 2 > budget)
         return fail(nullptr, ORACLE_CUDA_UNSUPPORTED, "matvec program rows too long for the shared-memory stage ring");
@@ -1218,7 +1309,7 @@ extern "C" oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cu
     pp.stages = static_cast<uint32_t>(S);
     pp.stage_bytes = static_cast<uint32_t>(stage);
     pp.copy_chunk = 32768;
-    pp.max_inflight = 16;
+    pp.max_inflight = pp.stages;
     pp.images = dev->scratch;
     pp.prebuilt_bytes = prebuilt_bytes;
     pp.counters = reinterpret_cast<unsigned int*>(dev->scratch + kNoAllocCountersOffset);
@@ -1730,8 +1821,8 @@ extern "C" oracle_cuda_status oracle_cuda_attention_step_at(oracle_cuda_context*
                static_cast<const float*>(keys_dev), pos_dev, cap, q_heads, kv_heads, key_dim, scale, scores_dev);
     if (s != ORACLE_CUDA_OK) return s;
     s = launch(ctx, attention_output_pos_kernel, dim3(q_heads), dim3(256), 0, st, false, scores_dev,
-               static_cast<const float*>(values_dev), pos_dev, cap, q_heads, kv_heads, value_dim, out_dev,
-               ctx->status);
+               static_cast<const float*>(values_dev), pos_dev, cap, q_heads, kv_heads, value_dim,
+               static_cast<const float*>(nullptr), 0u, out_dev, ctx->status);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
 
@@ -1808,5 +1899,86 @@ extern "C" oracle_cuda_status oracle_cuda_token_commit(oracle_cuda_context* ctx,
     const oracle_cuda_status s =
         launch(ctx, token_commit_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), false, key_dev,
                prompt_dev, n_prompt, pos_dev, next_id_dev, tokens_dev, tokens_capacity, ctx->status);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+// ---------------------------------------------------------------- fused block cores
+
+extern "C" oracle_cuda_status oracle_cuda_gdn_core(oracle_cuda_context* ctx, const float* qkv_dev, const float* z_dev,
+                                                   const float* beta_dev, const float* alpha_dev,
+                                                   const float* time_step_bias_dev, const float* decay_dev,
+                                                   const float* conv_weights_dev, float* history_dev,
+                                                   float* state_dev, const float* norm_dev, uint32_t key_heads,
+                                                   uint32_t value_heads, uint32_t head_dim, uint32_t conv_kernel,
+                                                   float eps, const uint32_t* pos_dev, float* out_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (key_heads == 0 || value_heads == 0 || value_heads % key_heads != 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Qwen3.5 repeated-head dimensions are incompatible");
+    if (conv_kernel == 0 || head_dim == 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Qwen3.5 recurrent state dimensions do not match the manifest");
+    if (head_dim != 64 && head_dim != 128)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "fused recurrent block supports head widths 64 and 128");
+    if (!(eps > 0.0f) || !std::isfinite(eps))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Qwen3.5 RMSNorm epsilon must be positive and finite");
+    if (!pos_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "position pointer is null");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s =
+        launch(ctx, head_dim == 128 ? gdn_core_kernel<128> : gdn_core_kernel<64>, dim3(value_heads), dim3(head_dim), 0,
+               static_cast<cudaStream_t>(stream), false, qkv_dev, z_dev, beta_dev, alpha_dev, time_step_bias_dev,
+               decay_dev, conv_weights_dev, history_dev, state_dev, norm_dev, key_heads, value_heads, conv_kernel,
+               eps, pos_dev, out_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_attention_prep_at(oracle_cuda_context* ctx, const float* q_full_dev,
+                                                            const float* k_dev, const float* v_dev,
+                                                            const float* q_norm_dev, const float* k_norm_dev,
+                                                            float eps, const float* table_dev, uint64_t rotary_dim,
+                                                            uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                                                            float* keys_dev, float* values_dev, uint64_t capacity,
+                                                            const uint32_t* pos_dev, float* q_out_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (kv_heads == 0 || q_heads % kv_heads != 0 || head_dim == 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "causal_attention_step dimensions are incompatible");
+    if (rotary_dim == 0 || rotary_dim % 2 != 0 || rotary_dim > head_dim)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "RoPE dimension must be non-zero, even, and within head width");
+    if (head_dim % 32 != 0 || head_dim > 1024)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "fused attention needs a head width that is a multiple of 32 up to 1024");
+    if (!(eps > 0.0f) || !std::isfinite(eps))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Qwen3.5 RMSNorm epsilon must be positive and finite");
+    if (capacity == 0 || capacity > 0xFFFFFFFFull || !pos_dev || !table_dev)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "KV cache capacity must be in [1, 2^32) with a position and table");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s =
+        launch(ctx, attention_prep_kernel, dim3(q_heads), dim3(head_dim), 0, static_cast<cudaStream_t>(stream), false,
+               q_full_dev, k_dev, v_dev, q_norm_dev, k_norm_dev, eps, table_dev,
+               static_cast<uint32_t>(rotary_dim / 2), q_heads, kv_heads, keys_dev, values_dev,
+               static_cast<uint32_t>(capacity), pos_dev, q_out_dev, ctx->status);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_attention_core_at(oracle_cuda_context* ctx, const float* q_dev,
+                                                            const float* keys_dev, const float* values_dev,
+                                                            uint64_t capacity, const uint32_t* pos_dev,
+                                                            uint32_t q_heads, uint32_t kv_heads, uint32_t key_dim,
+                                                            uint32_t value_dim, const float* gate_dev,
+                                                            uint32_t gate_stride, float* scores_dev, float* out_dev,
+                                                            void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (kv_heads == 0 || q_heads % kv_heads != 0 || key_dim == 0 || value_dim == 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "causal_attention_step dimensions are incompatible");
+    if (capacity == 0 || capacity > 0xFFFFFFFFull || !pos_dev)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "KV cache capacity must be in [1, 2^32) with a position");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const uint32_t cap = static_cast<uint32_t>(capacity);
+    const float scale = 1.0f / std::sqrt(static_cast<float>(key_dim));
+    uint32_t chunks = static_cast<uint32_t>((capacity + 255) / 256);
+    if (chunks > 64) chunks = 64;
+    oracle_cuda_status s = launch(ctx, attention_scores_pos_kernel, dim3(q_heads, chunks), dim3(256), 0, st, false,
+                                  q_dev, keys_dev, pos_dev, cap, q_heads, kv_heads, key_dim, scale, scores_dev);
+    if (s != ORACLE_CUDA_OK) return s;
+    s = launch(ctx, attention_output_pos_kernel, dim3(q_heads), dim3(256), 0, st, false, scores_dev, values_dev,
+               pos_dev, cap, q_heads, kv_heads, value_dim, gate_dev, gate_stride, out_dev, ctx->status);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }

@@ -38,6 +38,22 @@ struct ProgramOp {
     uint32_t publish;         // 1: a later op depends on this one; count completions
     uint32_t act_offset;      // byte offset of this op's activation image
     uint32_t prebuilt;        // 1: the image was built by quantize_images_kernel
+    const float* residual;    // optional: y = residual + W.x (Oracle's add_vectors, qwen35_block.cpp:190-200)
+};
+
+// Per-op data read only at op boundaries (kept out of ProgramOp, whose copy
+// stays live through the row loop).
+struct ProgramOpExtra {
+    uint32_t build;           // 1: consumers build the image here (after the wait, if any)
+    uint32_t xform;           // activation transform (q8k.cuh kXform*)
+    float eps;                // kXformRms
+    uint32_t other_is_gate;
+    const float* x2;          // kXformSwiglu: up
+    const float* norm;        // kXformRms: weights
+    // optional SwiGLU pass after the op: act[r] = other_is_gate ? silu(other[r]) * y[r]
+    // : silu(y[r]) * other[r], `other` an earlier op's output over the same rows
+    const float* other;
+    float* act;
 };
 
 constexpr uint32_t kMaxPeers = 8;
@@ -63,12 +79,13 @@ struct PeerExchange {
 
 struct ProgramParams {
     ProgramOp ops[kProgramMaxOps];
+    ProgramOpExtra ext[kProgramMaxOps];
     uint32_t n_ops;
     uint32_t stages;
     uint32_t stage_bytes;
-    uint32_t act_bytes;
+    uint32_t act_bytes;      // images, then 256 bytes of reduction scratch
     uint32_t copy_chunk;
-    uint32_t max_inflight;   // at most this many issued stages not yet landed (>= 1)
+    uint32_t max_inflight;   // at most this many issued stages not yet landed (1 .. stages)
     const uint8_t* images;   // prebuilt images (global, same layout as shared memory)
     uint32_t prebuilt_bytes; // bytes of the prebuilt region (multiple of 16)
     unsigned int* counters;  // kProgramMaxOps completion counters + 1 exit counter, zero at launch
@@ -148,8 +165,9 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
             const uint8_t* slot = stage0 + s * stage_bytes + head;
             uint32_t j = warp >= static_cast<int>(owner_base) ? warp - owner_base : warp + NCW - owner_base;
             for (; j < n_here; j += NCW) {
-                const float v = q8k_row_dot<kType, kXReg>(op.nb, img, slot + j * rb, xw, xbs, xd, lane);
+                float v = q8k_row_dot<kType, kXReg>(op.nb, img, slot + j * rb, xw, xbs, xd, lane);
                 if (lane == 0) {
+                    if (op.residual) v = __fadd_rn(__ldcg(op.residual + r0 + q_lo + j), v);
                     y[q_lo + j] = v;
                     if (px.world > 1) {
                         // the same row into every peer's gather buffer (NVLink store)
@@ -213,7 +231,10 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                 bool w_ok = true;
                 // Keep at most max_inflight stages in the memory system: deeper
                 // queues add latency to the activation loads that share them.
-                if (lane == 0 && g >= pp.max_inflight) {
+                // The window must not exceed the ring: stage h's slot is then
+                // reused by no stage issued after h, so the parity wait below
+                // refers to stage h itself and never to a later, unissued use.
+                if (lane == 0 && pp.max_inflight <= S && g >= pp.max_inflight) {
                     const uint32_t h = g - pp.max_inflight;
                     w_ok = mbar_wait(&full[h % S], (h / S) & 1, pp.status, 15);
                 }
@@ -273,16 +294,32 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
     }
     named_barrier_sync(1, NCW * 32);
     uint32_t s = 0, phase = 0;  // slot and parity of the global stage counter
+    double* scratch = reinterpret_cast<double*>(act + pp.act_bytes - 256);
     for (uint32_t k = 0; k < pp.n_ops; ++k) {
         const ProgramOp op = pp.ops[k];
         if (op.after_previous && k > 0) {
-            if (!failed) {
-                bool ok = true;
-                if (lane == 0) ok = wait_counter(pp.counters + (k - 1), gridDim.x, pp.status, 13);
-                failed = !__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0);
+            // One poller per CTA: with every warp of every CTA polling, the
+            // completion counts they wait for reached L2 microseconds late.
+            // Its acquire, then the CTA barrier, order every warp's loads.
+            uint32_t* wait_ok = reinterpret_cast<uint32_t*>(scratch + 24);
+            if (threadIdx.x == 0)
+                *wait_ok = (!failed && wait_counter(pp.counters + (k - 1), gridDim.x, pp.status, 13)) ? 1u : 0u;
+            named_barrier_sync(1, NCW * 32);
+            failed = failed || *wait_ok == 0u;
+        }
+        if (pp.ext[k].build) {
+            const ProgramOpExtra& e = pp.ext[k];
+            const ActSource a{op.x, e.x2, e.norm, e.eps, e.xform};
+            float inv = 0.0f;
+            if (e.xform == kXformRms) {
+                // the whole vector's sum of squares, reduced over the consumer warps
+                const uint32_t n = op.nb * 256u;
+                const double part = warp_sum_f64(failed ? 0.0 : sum_squares_f64(op.x, warp * 32 + lane, n, NCW * 32));
+                if (lane == 0) scratch[warp] = part;
+                named_barrier_sync(1, NCW * 32);
+                inv = rms_inverse(warp_sum_f64(lane < NCW ? scratch[lane] : 0.0), n, e.eps);
             }
-            named_barrier_sync(1, NCW * 32);  // (orders the acquire above before every warp's loads)
-            if (!failed) quantize_to_image(op.x, op.nb, q8k_image(act + op.act_offset, op.nb), warp, NCW, lane);
+            if (!failed) quantize_xform_to_image(a, op.nb, inv, q8k_image(act + op.act_offset, op.nb), warp, NCW, lane);
             named_barrier_sync(1, NCW * 32);
         }
         const bool q4 = kTypes == 1 || (kTypes == 3 && op.type == 12);
@@ -302,6 +339,18 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             // register-resident variant does not fit beside the Q4_K code in 128 registers
             program_walk_op<NCW, 14, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                             pp.status, pp.px, warp, lane);
+        }
+        if (pp.ext[k].act && !failed) {
+            // the SwiGLU activation of this CTA's rows, once its warps have
+            // written them (and, earlier, the same rows of `other`)
+            const ProgramOpExtra& e = pp.ext[k];
+            named_barrier_sync(1, NCW * 32);
+            const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
+            const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
+            for (uint64_t r = r0 + threadIdx.x; r < r1; r += NCW * 32) {
+                const float v = __ldcg(op.y + r), o = __ldcg(e.other + r);
+                e.act[r] = e.other_is_gate ? __fmul_rn(ref_silu(o), v) : __fmul_rn(ref_silu(v), o);
+            }
         }
         if (op.publish) {
             // publish this CTA's completion of op k (its y rows are written)

@@ -193,6 +193,105 @@ __device__ __forceinline__ void quantize_to_image(const float* __restrict__ x, u
     }
 }
 
+// Activation transforms applied while quantizing, so that the f32 vector a
+// matvec reads never has to be written out (decode programs):
+//   kXformNone    v = x
+//   kXformRms     v = (x * inv) * w, inv = rms_inverse(sum of x^2 over the
+//                 whole vector): Oracle's rms_norm_rows for one row
+//                 (qwen35_block.cpp:161-188)
+//   kXformSwiglu  v = silu(x) * x2: the MLP activation (qwen35_block.cpp:315-318)
+enum : uint32_t { kXformNone = 0, kXformRms = 1, kXformSwiglu = 2 };
+
+struct ActSource {
+    const float* x;
+    const float* x2;    // swiglu: up
+    const float* norm;  // rms: weights
+    float eps;
+    uint32_t xform;
+};
+
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The lane's 8 transformed values of block i (inv: the rms inverse, else unused).
+__device__ __forceinline__ void load_lane8_xform(const ActSource& a, uint32_t i, int lane, float inv, float (&v)[8]) {
+    const float* xb = a.x + 256ull * i;
+    load_lane8(xb, lane, aligned16(xb), v);
+    if (a.xform == kXformRms) {
+        float w[8];
+        const float* wb = a.norm + 256ull * i;
+        load_lane8(wb, lane, aligned16(wb), w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], inv), w[j]);
+    } else if (a.xform == kXformSwiglu) {
+        float u[8];
+        const float* ub = a.x2 + 256ull * i;
+        load_lane8(ub, lane, aligned16(ub), u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(ref_silu(v[j]), u[j]);
+    }
+}
+
+// A warp's partial double sum of squares over elements [first, n) with stride
+// `stride` (each product exact in double, sums rounded).
+__device__ __forceinline__ double sum_squares_f64(const float* __restrict__ x, uint32_t first, uint32_t n,
+                                                  uint32_t stride) {
+    double s = 0.0;
+    uint32_t c = first;
+    // four loads in flight per round; the additions keep the element order
+    for (; c + 3 * stride < n; c += 4 * stride) {
+        const double a = __ldcg(x + c), b = __ldcg(x + c + stride);
+        const double e = __ldcg(x + c + 2 * stride), f = __ldcg(x + c + 3 * stride);
+        s = __dadd_rn(s, __dmul_rn(a, a));
+        s = __dadd_rn(s, __dmul_rn(b, b));
+        s = __dadd_rn(s, __dmul_rn(e, e));
+        s = __dadd_rn(s, __dmul_rn(f, f));
+    }
+    for (; c < n; c += stride) {
+        const double v = static_cast<double>(__ldcg(x + c));
+        s = __dadd_rn(s, __dmul_rn(v, v));
+    }
+    return s;
+}
+
+// Quantize `nb` transformed blocks into the image, warps [0, nwarps) of the
+// calling group cooperating (inv as for load_lane8_xform).
+__device__ __forceinline__ void quantize_xform_to_image(const ActSource& a, uint32_t nb, float inv, ActImage img,
+                                                        int warp, int nwarps, int lane) {
+    if (a.xform == kXformNone) {
+        // kPlainBatch blocks per round: their loads are in flight together
+        constexpr int kPlainBatch = 2;
+        for (uint32_t i = warp; i < nb; i += kPlainBatch * nwarps) {
+            float v[kPlainBatch][8];
+#pragma unroll
+            for (int m = 0; m < kPlainBatch; ++m) {
+                const uint32_t im = i + m * nwarps;
+                if (im < nb) load_lane8(a.x + 256ull * im, lane, aligned16(a.x + 256ull * im), v[m]);
+            }
+#pragma unroll
+            for (int m = 0; m < kPlainBatch; ++m) {
+                const uint32_t im = i + m * nwarps;
+                if (im >= nb) break;
+                const Q8KLane r = quantize_q8k_lane_values(v[m], lane);
+                store_block_to_image(img, im, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
+            }
+        }
+        return;
+    }
+    // two blocks per round: both blocks' loads are in flight together
+    for (uint32_t i = warp; i < nb; i += 2 * nwarps) {
+        const uint32_t i2 = i + nwarps;
+        float v[8], v2[8];
+        load_lane8_xform(a, i, lane, inv, v);
+        if (i2 < nb) load_lane8_xform(a, i2, lane, inv, v2);
+        const Q8KLane r = quantize_q8k_lane_values(v, lane);
+        store_block_to_image(img, i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
+        if (i2 < nb) {
+            const Q8KLane r2 = quantize_q8k_lane_values(v2, lane);
+            store_block_to_image(img, i2, lane, r2.q_lo, r2.q_hi, r2.bsum16, r2.d);
+        }
+    }
+}
+
 // Quantize up to kMaxImageJobs activations, each into its own image inside
 // one global buffer laid out exactly like the shared-memory images, so a
 // consumer can copy the whole region into shared memory unchanged.  One warp
@@ -200,6 +299,10 @@ __device__ __forceinline__ void quantize_to_image(const float* __restrict__ x, u
 constexpr int kMaxImageJobs = 16;
 struct ImageJobs {
     const float* x[kMaxImageJobs];
+    const float* x2[kMaxImageJobs];
+    const float* norm[kMaxImageJobs];
+    float eps[kMaxImageJobs];
+    uint32_t xform[kMaxImageJobs];
     uint32_t nb[kMaxImageJobs];
     uint32_t offset[kMaxImageJobs];  // byte offset of the job's image
     uint32_t first_block[kMaxImageJobs + 1];
@@ -211,8 +314,15 @@ __device__ __forceinline__ void quantize_image_block(const ImageJobs& jobs, uint
     uint32_t j = 0;
     while (gw >= jobs.first_block[j + 1]) ++j;
     const uint32_t i = gw - jobs.first_block[j];
-    const float* xb = jobs.x[j] + 256ull * i;
-    const Q8KLane r = quantize_q8k_block_warp(xb, lane, (reinterpret_cast<uintptr_t>(xb) & 15u) == 0);
+    const ActSource a{jobs.x[j], jobs.x2[j], jobs.norm[j], jobs.eps[j], jobs.xform[j]};
+    float inv = 0.0f;
+    if (a.xform == kXformRms) {
+        const uint32_t n = jobs.nb[j] * 256u;
+        inv = rms_inverse(warp_sum_f64(sum_squares_f64(a.x, lane, n, 32u)), n, a.eps);
+    }
+    float v[8];
+    load_lane8_xform(a, i, lane, inv, v);
+    const Q8KLane r = quantize_q8k_lane_values(v, lane);
     store_block_to_image(q8k_image(images + jobs.offset[j], jobs.nb[j]), i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
 }
 

@@ -24,7 +24,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import CONTRACT_F32, CONTRACT_Q8K, Context, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K
+from . import CONTRACT_F32, XFORM_RMS, XFORM_SWIGLU, Context, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K
 from .qwen35 import Qwen35Config
 
 
@@ -66,13 +66,17 @@ class Qwen35Decoder:
     f32 contract; any storage type the reference admits)."""
 
     def __init__(self, ctx: Context, cfg: Qwen35Config, tensors, contract: str = "q8k",
-                 capacity: int | None = None, max_new: int = 4096, device: int = 0):
+                 capacity: int | None = None, max_new: int = 4096, device: int = 0, fused: bool = True):
         import torch
 
         if contract not in ("q8k", "f32"):
             raise ValueError("contract must be 'q8k' or 'f32'")
         self.torch = torch
         self.ctx, self.cfg, self.contract = ctx, cfg, contract
+        # fused (Q8_K contract only): one matvec program per block boundary
+        # (output projection + MLP + the next block's input projections, norms,
+        # SwiGLU and residual adds applied inside) and one kernel per block core
+        self.fused = fused and contract == "q8k"
         self.dev = torch.device("cuda", device)
         self.cap = int(capacity or cfg.context)
         self.max_new = int(max_new)
@@ -105,7 +109,8 @@ class Qwen35Decoder:
                 self.keys[i] = f32(self.cap * cfg.kv_width)
                 self.values[i] = f32(self.cap * cfg.kv_width)
             else:
-                self.hist[i] = f32(cfg.conv_channels * cfg.conv_kernel)
+                # the fused core double-buffers the history by position parity
+                self.hist[i] = f32((2 if self.fused else 1) * cfg.conv_channels * cfg.conv_kernel)
                 self.state[i] = f32(cfg.value_heads * cfg.state_size * cfg.state_size)
         self.rope_table = f32(self.cap * cfg.rope_dim)
         ctx.rope_table(cfg.rope_dim, cfg.rope_sections, cfg.rope_base, self.cap, self.rope_table)
@@ -176,7 +181,86 @@ class Qwen35Decoder:
         ctx.gate_sigmoid_mul(self.attn, self.gate, cfg.q_width, s)
         self._project([(p + "attn_output.weight", self.attn, self.branch)], s)
 
+    # ---------------------------------------------------------------- fused step
+    def _mv(self, name, x, y, after=False, xform=0, x2=None, norm=None, residual=None) -> dict:
+        qtype, dims, w = self.w[name]
+        return dict(qtype=qtype, rows=dims[1], cols=dims[0], w=w, x=x, y=y, after=after, xform=xform,
+                    eps=self.cfg.eps, x2=x2, norm=norm, residual=residual)
+
+    def _input_projections(self, i: int, after: bool) -> list:
+        """Block i's projections of rms_norm(hidden) (qwen35_block.cpp:441-463, 643-657)."""
+        p = f"blk.{i}."
+        kw = dict(after=after, xform=XFORM_RMS, norm=self._vec(p + "attn_norm.weight"))
+        if self.cfg.is_attention(i):
+            return [self._mv(p + "attn_q.weight", self.hidden, self.q_full, **kw),
+                    self._mv(p + "attn_k.weight", self.hidden, self.k, **kw),
+                    self._mv(p + "attn_v.weight", self.hidden, self.v, **kw)]
+        return [self._mv(p + "attn_qkv.weight", self.hidden, self.qkv, **kw),
+                self._mv(p + "attn_gate.weight", self.hidden, self.z, **kw),
+                self._mv(p + "ssm_beta.weight", self.hidden, self.beta, **kw),
+                self._mv(p + "ssm_alpha.weight", self.hidden, self.alpha, **kw)]
+
+    def _block_tail(self, i: int) -> list:
+        """Block i's output projection and MLP with finish_block's adds and norm
+        (qwen35_block.cpp:298-352): resid = hidden + out(x); hidden = resid +
+        down(silu(gate(rms(resid))) * up(rms(resid)))."""
+        p = f"blk.{i}."
+        attn = self.cfg.is_attention(i)
+        out, x = (p + "attn_output.weight", self.attn) if attn else (p + "ssm_out.weight", self.gated)
+        post = dict(after=True, xform=XFORM_RMS, norm=self._vec(p + "post_attention_norm.weight"))
+        return [self._mv(out, x, self.resid, residual=self.hidden),
+                self._mv(p + "ffn_gate.weight", self.resid, self.ffn_gate, **post),
+                self._mv(p + "ffn_up.weight", self.resid, self.ffn_up, **post),
+                self._mv(p + "ffn_down.weight", self.ffn_gate, self.hidden, after=True, xform=XFORM_SWIGLU,
+                         x2=self.ffn_up, residual=self.resid)]
+
+    def _core(self, i: int, s) -> None:
+        cfg, ctx, p = self.cfg, self.ctx, f"blk.{i}."
+        D = cfg.head_dim
+        if cfg.is_attention(i):
+            ctx.attention_prep_at(self.q_full, self.k, self.v, self._vec(p + "attn_q_norm.weight"),
+                                  self._vec(p + "attn_k_norm.weight"), cfg.eps, self.rope_table, cfg.rope_dim,
+                                  cfg.heads, cfg.kv_heads, D, self.keys[i], self.values[i], self.cap, self.pos,
+                                  self.qn, s)
+            ctx.attention_core_at(self.qn, self.keys[i], self.values[i], self.cap, self.pos, cfg.heads, cfg.kv_heads,
+                                  D, D, self.q_full[D:], 2 * D, self.scores, self.attn, s)
+        else:
+            ctx.gdn_core(self.qkv, self.z, self.beta, self.alpha, self._vec(p + "ssm_dt.bias"),
+                         self._vec(p + "ssm_a"), self._vec(p + "ssm_conv1d.weight"), self.hist[i], self.state[i],
+                         self._vec(p + "ssm_norm.weight"), cfg.key_heads, cfg.value_heads, cfg.state_size,
+                         cfg.conv_kernel, cfg.eps, self.pos, self.gated, s)
+
+    def _program(self, ops, s) -> None:
+        if self.timer is not None:
+            ev = (self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
+            ev[0].record(self.stream)
+        self.ctx.matvec_program_ex(ops, s)
+        if self.timer is not None:
+            ev[1].record(self.stream)
+            self.timer.append((ev, sum(o["w"].numel() for o in ops)))
+
+    def _enqueue_fused_step(self, n_prompt: int, s) -> None:
+        cfg, ctx = self.cfg, self.ctx
+        et, edims, emb = self.w["token_embd.weight"]
+        ctx.gather_rows(et, edims[1], edims[0], emb, self.next_id, self.hidden, s)
+        self._program(self._input_projections(0, after=False), s)
+        out = "output.weight" if "output.weight" in self.w else "token_embd.weight"
+        for i in range(cfg.layers):
+            self._core(i, s)
+            ops = self._block_tail(i)
+            if i + 1 < cfg.layers:
+                ops += self._input_projections(i + 1, after=True)
+            else:  # the final norm and the LM head (qwen35_forward.cpp:446-466)
+                ops.append(self._mv(out, self.hidden, self.logits, after=True, xform=XFORM_RMS,
+                                    norm=self._vec("output_norm.weight")))
+            self._program(ops, s)
+        ctx.argmax(self.logits, self.key, 0, s)
+        ctx.token_commit(self.key, self.prompt, n_prompt, self.pos, self.next_id, self.tokens, self.max_new, s)
+
     def _enqueue_step(self, n_prompt: int, s) -> None:
+        if self.fused:
+            self._enqueue_fused_step(n_prompt, s)
+            return
         cfg, ctx = self.cfg, self.ctx
         H = cfg.hidden
         et, edims, emb = self.w["token_embd.weight"]

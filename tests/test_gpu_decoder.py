@@ -85,3 +85,20 @@ def test_kv_capacity_overflow_reported(ctx, gguf_models):
         dec.generate(PROMPT[:6], 4)
     ctx.device_status()  # cleared: the context stays usable
     assert len(dec.generate(PROMPT[:4], 4)) == 4
+
+
+def test_fused_step_matches_unfused(ctx, gguf_models):
+    """The fused step (one matvec program per block boundary with norms, SwiGLU
+    and residual adds inside; one kernel per block core) against the step of
+    separate kernels: same tokens, logits equal up to the order of the double
+    sums inside RMSNorm (float results differ in rare last-bit cases)."""
+    path = gguf_models["q4_k_m"]
+    fused = _decoder(ctx, path, "q8k", capacity=512, max_new=64, fused=True)
+    plain = _decoder(ctx, path, "q8k", capacity=512, max_new=64, fused=False)
+    assert np.array_equal(fused.generate(PROMPT, 32), plain.generate(PROMPT, 32))
+    fused.start(PROMPT)
+    plain.start(PROMPT)
+    for t in PROMPT[:4]:
+        a, b = fused.forward(int(t)), plain.forward(int(t))
+        assert np.abs(a - b).max() <= 1e-4 * b.std()
+    assert fused.launches_per_step() < plain.launches_per_step() // 4
