@@ -882,6 +882,10 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
                 return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
                             "op " + std::to_string(k) + ": output must lie inside the peer group's gather buffer");
         }
+        for (uint32_t k = 0; k < n_ops; ++k)
+            if (ops[k].residual_dev || ops[k].xform != ORACLE_CUDA_XFORM_NONE)
+                return fail(ctx, ORACLE_CUDA_UNSUPPORTED,
+                            "op " + std::to_string(k) + ": transforms and residual outputs are single-GPU only");
         pp.px.world = group->world;
         pp.px.rank = group->rank;
         pp.px.local_base = lo;

@@ -165,9 +165,8 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
             const uint8_t* slot = stage0 + s * stage_bytes + head;
             uint32_t j = warp >= static_cast<int>(owner_base) ? warp - owner_base : warp + NCW - owner_base;
             for (; j < n_here; j += NCW) {
-                float v = q8k_row_dot<kType, kXReg>(op.nb, img, slot + j * rb, xw, xbs, xd, lane);
+                const float v = q8k_row_dot<kType, kXReg>(op.nb, img, slot + j * rb, xw, xbs, xd, lane);
                 if (lane == 0) {
-                    if (op.residual) v = __fadd_rn(__ldcg(op.residual + r0 + q_lo + j), v);
                     y[q_lo + j] = v;
                     if (px.world > 1) {
                         // the same row into every peer's gather buffer (NVLink store)
@@ -340,6 +339,14 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             program_walk_op<NCW, 14, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                             pp.status, pp.px, warp, lane);
         }
+        if (op.residual && !failed) {
+            // y = residual + W.x for this CTA's rows, once its warps wrote them
+            named_barrier_sync(1, NCW * 32);
+            const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
+            const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
+            for (uint64_t r = r0 + threadIdx.x; r < r1; r += NCW * 32)
+                op.y[r] = __fadd_rn(__ldcg(op.residual + r), __ldcg(op.y + r));
+        }
         if (pp.ext[k].act && !failed) {
             // the SwiGLU activation of this CTA's rows, once its warps have
             // written them (and, earlier, the same rows of `other`)
@@ -356,7 +363,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             // publish this CTA's completion of op k (its y rows are written)
             named_barrier_sync(1, NCW * 32);
             if (threadIdx.x == 0) {
-                __threadfence();
+                // the release (after the CTA barrier) covers every warp's rows;
+                // an extra full fence here cost ~1 us per dependency
                 red_release_gpu_add(pp.counters + k, 1u);
             }
         }
