@@ -352,6 +352,7 @@ class Context:
         _raise(_lib.oracle_cuda_create(device, C.byref(h)), None)
         self._h = h.value
         self.device = device
+        self.flags = 0
         if flags:
             self.set_flags(flags)
 
@@ -372,6 +373,7 @@ class Context:
 
     def set_flags(self, flags: int) -> None:
         self._check(_lib.oracle_cuda_set_flags(self._h, flags))
+        self.flags = flags
 
     def device_status(self) -> None:
         """Raise DeviceTimeout if any kernel's bounded wait expired."""

@@ -193,4 +193,19 @@ __device__ __forceinline__ float rms_inverse(double sum_squares, uint32_t width,
     return __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(mean, static_cast<double>(eps)))));
 }
 
+// Programmatic dependent launch: wait for the preceding grid's results (no-op
+// when the launch did not opt in), and let the next grid begin launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Kernels of the decode step open with this: the next kernel on the stream
+// may start launching (its own wait keeps it ordered), and nothing here reads
+// or writes memory before the preceding kernel has completed.
+__device__ __forceinline__ void pdl_enter() {
+    pdl_launch_dependents();
+    pdl_wait();
+}
+
 }  // namespace oracle_cuda

@@ -82,6 +82,7 @@ __global__ void __launch_bounds__(256) attention_scores_pos_kernel(const float* 
                                                                    uint32_t q_heads, uint32_t kv_heads,
                                                                    uint32_t key_dim, float scale,
                                                                    float* __restrict__ scores) {
+    pdl_enter();
     if (*pos >= capacity) return;
     const uint32_t tokens = *pos + 1;
     const uint32_t h = blockIdx.x, lane = threadIdx.x & 31;
@@ -106,6 +107,7 @@ __global__ void __launch_bounds__(256) attention_output_pos_kernel(float* __rest
                                                                    uint32_t value_dim, const float* __restrict__ gate,
                                                                    uint32_t gate_stride, float* __restrict__ out,
                                                                    DeviceStatus* st) {
+    pdl_enter();
     __shared__ double scratch[32];
     __shared__ float fmax_s[32];
     if (*pos >= capacity) return;
@@ -212,15 +214,19 @@ __global__ void __launch_bounds__(kD) gdn_core_kernel(const float* __restrict__ 
                                                       const float* __restrict__ norm_w, uint32_t key_heads,
                                                       uint32_t value_heads, uint32_t conv_kernel, float eps,
                                                       const uint32_t* __restrict__ pos, float* __restrict__ out) {
+    pdl_launch_dependents();
     __shared__ float nq[kD], nk[kD];
     __shared__ double scratch[32];
     const uint32_t h = blockIdx.x, t = threadIdx.x;
     // the head's state column t, [key d][value t], held in registers: loads
-    // issued up front, independent of everything computed before the update
+    // issued up front, independent of everything computed before the update.
+    // Only this block's own earlier steps write the state, so the loads may
+    // overlap the tail of the preceding kernel (programmatic launch).
     float* sh = state + static_cast<uint64_t>(h) * kD * kD + t;
     float col[kD];
 #pragma unroll
     for (int d = 0; d < kD; ++d) col[d] = sh[d * kD];
+    pdl_wait();
     const uint32_t kh = h % key_heads;
     const uint32_t key_width = key_heads * kD;
     const uint32_t channels = 2 * key_width + value_heads * kD;
@@ -292,6 +298,7 @@ __global__ void attention_prep_kernel(const float* __restrict__ q_full, const fl
                                       uint32_t half, uint32_t q_heads, uint32_t kv_heads, float* keys, float* values,
                                       uint32_t capacity, const uint32_t* __restrict__ pos, float* __restrict__ q_out,
                                       DeviceStatus* st) {
+    pdl_enter();
     __shared__ double scratch[32];
     __shared__ float row[1024];
     const uint32_t D = blockDim.x, h = blockIdx.x, t = threadIdx.x;

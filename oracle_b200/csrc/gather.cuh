@@ -29,6 +29,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint8_t* __restr
                                                           uint64_t row_bytes, const uint32_t* __restrict__ ids,
                                                           uint64_t n_ids, float* __restrict__ out,
                                                           DeviceStatus* st) {
+    pdl_enter();
     const uint32_t chunks = (k + 3) / 4;
     const uint64_t total = n_ids * chunks;
     for (uint64_t c = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; c < total;
@@ -61,6 +62,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index
 
 __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ x, uint64_t n, uint32_t index_base,
                                                      unsigned long long* __restrict__ key_out) {
+    pdl_enter();
     __shared__ unsigned long long warp_best[8];
     unsigned long long best = 0;
     for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x) {
@@ -125,6 +127,7 @@ enum : unsigned int { kDevLogitsNaN = 5, kDevLogitsNonFinite = 6 };
 __global__ void token_commit_kernel(const unsigned long long* __restrict__ key, const uint32_t* __restrict__ prompt,
                                     uint32_t n_prompt, uint32_t* pos, uint32_t* next_id, uint32_t* tokens_out,
                                     uint32_t out_capacity, DeviceStatus* st) {
+    pdl_enter();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     const ArgmaxResult r = decode_argmax_key(*key);
     const uint32_t p = *pos;

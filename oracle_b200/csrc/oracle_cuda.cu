@@ -1491,7 +1491,8 @@ oracle_cuda_status launch_gather_typed(oracle_cuda_context* ctx, const uint8_t* 
     const uint64_t cap = uint64_t(ctx->sm_count) * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    return launch(ctx, gather_rows_kernel<kType>, dim3(static_cast<uint32_t>(blocks)), dim3(256), 0, stream, false, w,
+    return launch(ctx, gather_rows_kernel<kType>, dim3(static_cast<uint32_t>(blocks)), dim3(256), 0, stream,
+                  (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, w,
                   rows, static_cast<uint32_t>(cols), row_bytes, ids, n_ids, out, ctx->status);
 }
 
@@ -1545,7 +1546,8 @@ extern "C" oracle_cuda_status oracle_cuda_argmax(oracle_cuda_context* ctx, const
     uint64_t blocks = (n + 255) / 256;
     if (blocks > uint64_t(ctx->sm_count) * 4) blocks = uint64_t(ctx->sm_count) * 4;
     const oracle_cuda_status s =
-        launch(ctx, argmax_kernel, dim3(static_cast<uint32_t>(blocks)), dim3(256), 0, st, false, x_dev, n, index_base,
+        launch(ctx, argmax_kernel, dim3(static_cast<uint32_t>(blocks)), dim3(256), 0, st,
+               (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, x_dev, n, index_base,
                key_dev);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
@@ -1901,7 +1903,8 @@ extern "C" oracle_cuda_status oracle_cuda_token_commit(oracle_cuda_context* ctx,
         return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "token commit pointer is null");
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
     const oracle_cuda_status s =
-        launch(ctx, token_commit_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), false, key_dev,
+        launch(ctx, token_commit_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
+               (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, key_dev,
                prompt_dev, n_prompt, pos_dev, next_id_dev, tokens_dev, tokens_capacity, ctx->status);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
@@ -1928,7 +1931,7 @@ extern "C" oracle_cuda_status oracle_cuda_gdn_core(oracle_cuda_context* ctx, con
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
     const oracle_cuda_status s =
         launch(ctx, head_dim == 128 ? gdn_core_kernel<128> : gdn_core_kernel<64>, dim3(value_heads), dim3(head_dim), 0,
-               static_cast<cudaStream_t>(stream), false, qkv_dev, z_dev, beta_dev, alpha_dev, time_step_bias_dev,
+               static_cast<cudaStream_t>(stream), (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, qkv_dev, z_dev, beta_dev, alpha_dev, time_step_bias_dev,
                decay_dev, conv_weights_dev, history_dev, state_dev, norm_dev, key_heads, value_heads, conv_kernel,
                eps, pos_dev, out_dev);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
@@ -1954,7 +1957,8 @@ extern "C" oracle_cuda_status oracle_cuda_attention_prep_at(oracle_cuda_context*
         return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "KV cache capacity must be in [1, 2^32) with a position and table");
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
     const oracle_cuda_status s =
-        launch(ctx, attention_prep_kernel, dim3(q_heads), dim3(head_dim), 0, static_cast<cudaStream_t>(stream), false,
+        launch(ctx, attention_prep_kernel, dim3(q_heads), dim3(head_dim), 0, static_cast<cudaStream_t>(stream),
+               (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0,
                q_full_dev, k_dev, v_dev, q_norm_dev, k_norm_dev, eps, table_dev,
                static_cast<uint32_t>(rotary_dim / 2), q_heads, kv_heads, keys_dev, values_dev,
                static_cast<uint32_t>(capacity), pos_dev, q_out_dev, ctx->status);
@@ -1979,10 +1983,11 @@ extern "C" oracle_cuda_status oracle_cuda_attention_core_at(oracle_cuda_context*
     const float scale = 1.0f / std::sqrt(static_cast<float>(key_dim));
     uint32_t chunks = static_cast<uint32_t>((capacity + 255) / 256);
     if (chunks > 64) chunks = 64;
-    oracle_cuda_status s = launch(ctx, attention_scores_pos_kernel, dim3(q_heads, chunks), dim3(256), 0, st, false,
+    const bool pdl = (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0;
+    oracle_cuda_status s = launch(ctx, attention_scores_pos_kernel, dim3(q_heads, chunks), dim3(256), 0, st, pdl,
                                   q_dev, keys_dev, pos_dev, cap, q_heads, kv_heads, key_dim, scale, scores_dev);
     if (s != ORACLE_CUDA_OK) return s;
-    s = launch(ctx, attention_output_pos_kernel, dim3(q_heads), dim3(256), 0, st, false, scores_dev, values_dev,
+    s = launch(ctx, attention_output_pos_kernel, dim3(q_heads), dim3(256), 0, st, pdl, scores_dev, values_dev,
                pos_dev, cap, q_heads, kv_heads, value_dim, gate_dev, gate_stride, out_dev, ctx->status);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }

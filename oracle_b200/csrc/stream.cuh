@@ -48,12 +48,6 @@ __host__ inline uint64_t stream_smem_bytes(const StreamParams& p) {
     return stream_barrier_bytes(p.stages) + uint64_t(p.act_bytes) + uint64_t(p.stages) * p.stage_bytes;
 }
 
-// Programmatic dependent launch: wait for the preceding grid's results (no-op
-// when the launch did not opt in), and let the next grid begin launching.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
 
 template <class Consumer>
 __global__ void __launch_bounds__((Consumer::kWarps + 1) * 32, 1)

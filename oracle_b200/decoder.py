@@ -24,7 +24,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import CONTRACT_F32, XFORM_RMS, XFORM_SWIGLU, Context, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K
+from . import CONTRACT_F32, FLAG_PDL, XFORM_RMS, XFORM_SWIGLU, Context, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K
 from .qwen35 import Qwen35Config
 
 
@@ -120,6 +120,10 @@ class Qwen35Decoder:
         self.key = torch.zeros(1, dtype=torch.int64, device=dev)
         self.stream = torch.cuda.Stream(device=dev)
         self.graph, self.graph_prompt = None, None
+        # programmatic dependent launch: each kernel of the step launches while
+        # its predecessor drains (programs start streaming weights early)
+        if self.fused:
+            ctx.set_flags(ctx.flags | FLAG_PDL)
         self.timer = None  # list of (start, end) CUDA events around projections, when set
 
     # ---------------------------------------------------------------- pieces
