@@ -202,8 +202,11 @@ oracle_cuda_status oracle_cuda_matvec_program(oracle_cuda_context* ctx, const or
  * each then quantized to Q8_K exactly as oracle_cuda_quantize_q8_k would
  * quantize the transformed vector.  Ops whose sources (x, xform, x2 / norm,
  * eps) are identical share one image: an op repeating an earlier op's source
- * needs no wait (after_previous is then ignored).  No Oracle counterpart:
- * Oracle runs each projection, norm and add as its own call. */
+ * needs no wait (after_previous is then ignored).  A SWIGLU op whose gate and
+ * up are outputs of two earlier ops of the call over the same rows gets the
+ * SwiGLU vector formed once, in the epilogue of the later of the two, at
+ * act_dev (or in context scratch when act_dev is NULL).  No Oracle
+ * counterpart: Oracle runs each projection, norm and add as its own call. */
 #define ORACLE_CUDA_XFORM_NONE 0u
 #define ORACLE_CUDA_XFORM_RMS 1u
 #define ORACLE_CUDA_XFORM_SWIGLU 2u
@@ -214,6 +217,7 @@ typedef struct oracle_cuda_matvec_op_ex {
     const float* x2_dev;
     const float* norm_dev;
     const float* residual_dev;
+    float* act_dev;      /* optional (SWIGLU ops): where the SwiGLU vector (cols floats) is formed */
 } oracle_cuda_matvec_op_ex;
 
 oracle_cuda_status oracle_cuda_matvec_program_ex(oracle_cuda_context* ctx, const oracle_cuda_matvec_op_ex* ops,
@@ -428,6 +432,15 @@ oracle_cuda_status oracle_cuda_peer_group_create(oracle_cuda_context* ctx, uint3
 oracle_cuda_status oracle_cuda_peer_group_connect(oracle_cuda_peer_group* group, const void* handles);
 oracle_cuda_status oracle_cuda_peer_group_data(oracle_cuda_peer_group* group, float** data_dev);
 oracle_cuda_status oracle_cuda_peer_group_destroy(oracle_cuda_peer_group* group);
+/* The extended program over a peer group: every op's rows are this rank's
+ * shard, outputs (y, residual outputs, SwiGLU vectors at act_dev) lie in the
+ * gather buffer and reach every rank; an op with after_previous (or a
+ * transform of an earlier op's output) waits until EVERY rank has finished the
+ * op before it, so transforms see whole vectors.  Results on every rank equal
+ * the single-GPU program's bit for bit. */
+oracle_cuda_status oracle_cuda_matvec_program_ex_allgather(oracle_cuda_context* ctx, oracle_cuda_peer_group* group,
+                                                           const oracle_cuda_matvec_op_ex* ops, uint32_t n_ops,
+                                                           void* stream);
 oracle_cuda_status oracle_cuda_matvec_program_allgather(oracle_cuda_context* ctx, oracle_cuda_peer_group* group,
                                                         const oracle_cuda_matvec_op* ops, uint32_t n_ops,
                                                         void* stream);

@@ -87,13 +87,14 @@ class MatvecOp(C.Structure):
 class MatvecOpEx(C.Structure):
     """oracle_cuda_matvec_op_ex of include/oracle_cuda.h."""
     _fields_ = [("base", MatvecOp), ("xform", C.c_uint32), ("eps", C.c_float), ("x2_dev", C.c_void_p),
-                ("norm_dev", C.c_void_p), ("residual_dev", C.c_void_p)]
+                ("norm_dev", C.c_void_p), ("residual_dev", C.c_void_p), ("act_dev", C.c_void_p)]
 
 
 XFORM_NONE, XFORM_RMS, XFORM_SWIGLU = 0, 1, 2
 PROGRAM_MAX_OPS = 16
 _proto("oracle_cuda_matvec_program", [_vp, C.POINTER(MatvecOp), _u32, _vp])
 _proto("oracle_cuda_matvec_program_ex", [_vp, C.POINTER(MatvecOpEx), _u32, _vp])
+_proto("oracle_cuda_matvec_program_ex_allgather", [_vp, _vp, C.POINTER(MatvecOpEx), _u32, _vp])
 _proto("oracle_cuda_matvec_program_noalloc", [C.POINTER(MatvecOp), _u32, _vp])
 NOALLOC_IMAGE_BYTES = 65536
 
@@ -412,9 +413,8 @@ class Context:
             arr[i] = MatvecOp(qtype, 1 if after else 0, rows, cols, _addr(w), _nbytes(w), _addr(x), _addr(y))
         self._check(_lib.oracle_cuda_matvec_program(self._h, arr, len(ops), _stream(stream)))
 
-    def matvec_program_ex(self, ops, stream=None) -> None:
-        """ops: sequence of dicts with keys qtype, rows, cols, w, x, y and
-        optional after (bool), xform (XFORM_*), eps, x2, norm, residual."""
+    @staticmethod
+    def _ops_ex(ops):
         arr = (MatvecOpEx * len(ops))()
         for i, o in enumerate(ops):
             arr[i].base = MatvecOp(o["qtype"], 1 if o.get("after") else 0, o["rows"], o["cols"], _addr(o["w"]),
@@ -424,7 +424,19 @@ class Context:
             arr[i].x2_dev = _addr(o.get("x2"))
             arr[i].norm_dev = _addr(o.get("norm"))
             arr[i].residual_dev = _addr(o.get("residual"))
-        self._check(_lib.oracle_cuda_matvec_program_ex(self._h, arr, len(ops), _stream(stream)))
+            arr[i].act_dev = _addr(o.get("act"))
+        return arr
+
+    def matvec_program_ex_allgather(self, group: "PeerGroup", ops, stream=None) -> None:
+        """oracle_cuda_matvec_program_ex_allgather: ops as for matvec_program_ex,
+        rows this rank's shard, outputs inside the group's gather buffer."""
+        self._check(_lib.oracle_cuda_matvec_program_ex_allgather(self._h, group._h, self._ops_ex(ops), len(ops),
+                                                                 _stream(stream)))
+
+    def matvec_program_ex(self, ops, stream=None) -> None:
+        """ops: sequence of dicts with keys qtype, rows, cols, w, x, y and
+        optional after (bool), xform (XFORM_*), eps, x2, norm, residual, act."""
+        self._check(_lib.oracle_cuda_matvec_program_ex(self._h, self._ops_ex(ops), len(ops), _stream(stream)))
 
     def gather_rows(self, qtype, rows, cols, w, ids, out, stream=None, w_nbytes=None) -> None:
         """oracle_cuda_gather_rows: out[t] = decode(row ids[t]) (device uint32 ids, f32 out)."""

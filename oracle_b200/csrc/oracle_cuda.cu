@@ -687,7 +687,8 @@ struct oracle_cuda_peer_group {
 
 namespace {
 
-constexpr uint64_t kGatherHeader = 256;
+constexpr uint64_t kGatherHeader = 256;  // arrival counter, epoch, ..., op counters
+constexpr uint32_t kGatherOpCounters = 16;  // uint index of the [2][kProgramMaxOps] op counters
 
 oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matvec_op_ex* ops, uint32_t n_ops,
                                void* stream, const oracle_cuda_peer_group* group);
@@ -782,26 +783,40 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
     {
         uint64_t need = 0;
         for (uint32_t j = 0; j < n_ops; ++j)
-            if (ops[j].xform == ORACLE_CUDA_XFORM_SWIGLU) need += ops[j].base.cols * sizeof(float);
+            if (ops[j].xform == ORACLE_CUDA_XFORM_SWIGLU && !ops[j].act_dev) need += ops[j].base.cols * sizeof(float);
         if (need > 0 && !group) {
             oracle_cuda_status gs = grow_device(ctx, ctx->act_scratch, ctx->act_scratch_bytes, need);
             if (gs != ORACLE_CUDA_OK) return gs;
         }
         uint64_t used = 0;
-        for (uint32_t j = 0; j < n_ops && !group; ++j) {
+        for (uint32_t j = 0; j < n_ops; ++j) {
             if (ops[j].xform != ORACLE_CUDA_XFORM_SWIGLU) continue;
+            if (group && !ops[j].act_dev) continue;  // peers need the vector in the gather buffer
+            // gate = the earlier op whose rows lie in x, up = the one whose rows lie
+            // in x2, over the same rows at the same offsets (a row shard of the
+            // vector when the ranks of a peer group split it)
+            auto inside = [&](const oracle_cuda_matvec_op_ex& o, const float* v) {
+                return o.base.y_dev >= v && o.base.y_dev + o.base.rows <= v + ops[j].base.cols;
+            };
             int a = -1, b = -1;
             for (uint32_t i = 0; i < j; ++i) {
-                if (ops[i].base.y_dev == ops[j].base.x_dev) a = static_cast<int>(i);
-                if (ops[i].base.y_dev == ops[j].x2_dev) b = static_cast<int>(i);
+                if (inside(ops[i], ops[j].base.x_dev)) a = static_cast<int>(i);
+                if (inside(ops[i], ops[j].x2_dev)) b = static_cast<int>(i);
             }
-            if (a < 0 || b < 0 || a == b || ops[a].base.rows != ops[j].base.cols ||
-                ops[b].base.rows != ops[j].base.cols || pp.ext[a].act || pp.ext[b].act)
+            if (a < 0 || b < 0 || a == b || ops[a].base.rows != ops[b].base.rows ||
+                ops[a].base.y_dev - ops[j].base.x_dev != ops[b].base.y_dev - ops[j].x2_dev || pp.ext[a].act ||
+                pp.ext[b].act)
                 continue;
+            // single GPU: the two producers must cover the whole vector
+            if (!group && ops[a].base.rows != ops[j].base.cols) continue;
             const int later = a > b ? a : b;
-            float* act = reinterpret_cast<float*>(ctx->act_scratch + used);
-            used += ops[j].base.cols * sizeof(float);
-            pp.ext[later].act = act;
+            float* act = ops[j].act_dev;
+            if (!act) {
+                act = reinterpret_cast<float*>(ctx->act_scratch + used);
+                used += ops[j].base.cols * sizeof(float);
+            }
+            // the later op writes its rows at the same offsets as in its own output
+            pp.ext[later].act = act + (ops[later].base.y_dev - (later == b ? ops[j].x2_dev : ops[j].base.x_dev));
             // later == b: this op computes up, `other` is the gate output; else the reverse
             pp.ext[later].other = later == b ? ops[a].base.y_dev : ops[b].base.y_dev;
             pp.ext[later].other_is_gate = later == b ? 1u : 0u;
@@ -882,10 +897,6 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
                 return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
                             "op " + std::to_string(k) + ": output must lie inside the peer group's gather buffer");
         }
-        for (uint32_t k = 0; k < n_ops; ++k)
-            if (ops[k].residual_dev || ops[k].xform != ORACLE_CUDA_XFORM_NONE)
-                return fail(ctx, ORACLE_CUDA_UNSUPPORTED,
-                            "op " + std::to_string(k) + ": transforms and residual outputs are single-GPU only");
         pp.px.world = group->world;
         pp.px.rank = group->rank;
         pp.px.local_base = lo;
@@ -895,6 +906,15 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         }
         pp.px.my_counter = reinterpret_cast<unsigned int*>(group->local);
         pp.px.my_epoch = reinterpret_cast<unsigned int*>(group->local) + 1;
+        pp.px.my_op = reinterpret_cast<unsigned int*>(group->local) + kGatherOpCounters;
+        for (uint32_t r = 0; r < group->world; ++r)
+            pp.px.peer_op[r] = reinterpret_cast<unsigned int*>(group->mapped[r]) + kGatherOpCounters;
+        // SwiGLU vectors and residual outputs reach the peers from the end-of-op
+        // passes: they must sit in the gather buffer too
+        for (uint32_t k = 0; k < n_ops; ++k)
+            if (pp.ext[k].act && (pp.ext[k].act < lo || pp.ext[k].act + pp.ops[k].rows > hi))
+                return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                            "op " + std::to_string(k) + ": the SwiGLU vector must lie inside the peer group's gather buffer");
     }
     const uint32_t grid = static_cast<uint32_t>(max_rows < uint64_t(ctx->sm_count) ? max_rows : ctx->sm_count);
     const size_t smem = stream_barrier_bytes(pp.stages) + pp.act_bytes + size_t(pp.stages) * pp.stage_bytes;
@@ -1990,4 +2010,12 @@ extern "C" oracle_cuda_status oracle_cuda_attention_core_at(oracle_cuda_context*
     s = launch(ctx, attention_output_pos_kernel, dim3(q_heads), dim3(256), 0, st, pdl, scores_dev, values_dev,
                pos_dev, cap, q_heads, kv_heads, value_dim, gate_dev, gate_stride, out_dev, ctx->status);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_matvec_program_ex_allgather(oracle_cuda_context* ctx,
+                                                                      oracle_cuda_peer_group* group,
+                                                                      const oracle_cuda_matvec_op_ex* ops,
+                                                                      uint32_t n_ops, void* stream) {
+    if (!group) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "peer group is null");
+    return program_run(ctx, ops, n_ops, stream, group);
 }

@@ -75,6 +75,14 @@ struct PeerExchange {
     unsigned int* peer_counter[kMaxPeers];   // each rank's arrival counter, mapped here
     unsigned int* my_counter;
     unsigned int* my_epoch;                  // launches completed (local only)
+    // Dependencies between ops of one launch across ranks: the last CTA of a
+    // rank to finish op k adds 1 to counter [bank][k] of every peer; an op
+    // after it waits until its own counter holds world - 1.  bank = epoch & 1:
+    // a rank resets its bank once every peer has ended the launch, and peers
+    // reach the next launch that uses the same bank only after this rank's
+    // next exchange.
+    unsigned int* my_op;                     // [2][kProgramMaxOps], this rank's
+    unsigned int* peer_op[kMaxPeers];        // each rank's, mapped here
 };
 
 struct ProgramParams {
@@ -127,6 +135,31 @@ __device__ __forceinline__ bool wait_counter(const unsigned int* counter, unsign
         __nanosleep(64);
     }
     return true;
+}
+
+// wait_counter at system scope (arrivals from other GPUs).
+__device__ __forceinline__ bool wait_counter_sys(const unsigned int* counter, unsigned int target, DeviceStatus* st,
+                                                 unsigned int where) {
+    if (ld_acquire_sys(counter) >= target) return true;
+    const unsigned long long t0 = global_timer_ns();
+    while (ld_acquire_sys(counter) < target) {
+        if (global_timer_ns() - t0 > kWaitNs) {
+            report_timeout(st, where);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
+// The same value into every peer's gather buffer at the offset of `at` in this
+// rank's (NVLink stores to IPC-mapped memory).
+__device__ __forceinline__ void push_to_peers(const PeerExchange& px, const float* at, float v) {
+    if (px.world <= 1) return;
+    const size_t off = static_cast<size_t>(at - px.local_base);
+#pragma unroll
+    for (uint32_t p = 0; p < kMaxPeers; ++p)
+        if (p < px.world && p != px.rank) px.peer_base[p][off] = v;
 }
 
 // Consumer walk over one op's stages with the row code specialised at compile
@@ -282,6 +315,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
     // be left waiting at a barrier without a deadline.
     pdl_wait();
     bool failed = false;
+    const PeerExchange& px = pp.px;
+    const uint32_t bank = px.world > 1 ? (*px.my_epoch & 1u) * kProgramMaxOps : 0u;
     // Every op that reads an activation from outside this launch had its image
     // built once, before this kernel, by quantize_images_kernel (the preceding
     // launch on the stream); copy those images into shared memory, so
@@ -301,8 +336,11 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             // completion counts they wait for reached L2 microseconds late.
             // Its acquire, then the CTA barrier, order every warp's loads.
             uint32_t* wait_ok = reinterpret_cast<uint32_t*>(scratch + 24);
-            if (threadIdx.x == 0)
-                *wait_ok = (!failed && wait_counter(pp.counters + (k - 1), gridDim.x, pp.status, 13)) ? 1u : 0u;
+            if (threadIdx.x == 0) {
+                bool ok = !failed && wait_counter(pp.counters + (k - 1), gridDim.x, pp.status, 13);
+                if (ok && px.world > 1) ok = wait_counter_sys(px.my_op + bank + (k - 1), px.world - 1, pp.status, 17);
+                *wait_ok = ok ? 1u : 0u;
+            }
             named_barrier_sync(1, NCW * 32);
             failed = failed || *wait_ok == 0u;
         }
@@ -344,8 +382,11 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             named_barrier_sync(1, NCW * 32);
             const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
             const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
-            for (uint64_t r = r0 + threadIdx.x; r < r1; r += NCW * 32)
-                op.y[r] = __fadd_rn(__ldcg(op.residual + r), __ldcg(op.y + r));
+            for (uint64_t r = r0 + threadIdx.x; r < r1; r += NCW * 32) {
+                const float v = __fadd_rn(__ldcg(op.residual + r), __ldcg(op.y + r));
+                op.y[r] = v;
+                push_to_peers(px, op.y + r, v);
+            }
         }
         if (pp.ext[k].act && !failed) {
             // the SwiGLU activation of this CTA's rows, once its warps have
@@ -356,16 +397,30 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
             for (uint64_t r = r0 + threadIdx.x; r < r1; r += NCW * 32) {
                 const float v = __ldcg(op.y + r), o = __ldcg(e.other + r);
-                e.act[r] = e.other_is_gate ? __fmul_rn(ref_silu(o), v) : __fmul_rn(ref_silu(v), o);
+                const float a = e.other_is_gate ? __fmul_rn(ref_silu(o), v) : __fmul_rn(ref_silu(v), o);
+                e.act[r] = a;
+                push_to_peers(px, e.act + r, a);
             }
         }
         if (op.publish) {
             // publish this CTA's completion of op k (its y rows are written)
             named_barrier_sync(1, NCW * 32);
             if (threadIdx.x == 0) {
-                // the release (after the CTA barrier) covers every warp's rows;
-                // an extra full fence here cost ~1 us per dependency
-                red_release_gpu_add(pp.counters + k, 1u);
+                if (px.world == 1) {
+                    // the release (after the CTA barrier) covers every warp's rows;
+                    // an extra full fence here cost ~1 us per dependency
+                    red_release_gpu_add(pp.counters + k, 1u);
+                } else {
+                    // every warp's rows and peer stores precede the count; the
+                    // rank's last CTA announces the op to every peer
+                    __threadfence();
+                    if (atomicAdd(pp.counters + k, 1u) == gridDim.x - 1) {
+                        __threadfence_system();
+#pragma unroll
+                        for (uint32_t p = 0; p < kMaxPeers; ++p)
+                            if (p < px.world && p != px.rank) red_release_sys_add(px.peer_op[p] + bank + k, 1u);
+                    }
+                }
             }
         }
     }
@@ -401,6 +456,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                     }
                     __nanosleep(128);
                 }
+                // every peer has ended this launch, so all its op arrivals for
+                // this launch are in: clear this bank for the launch after next
+                for (uint32_t k = 0; k < kProgramMaxOps; ++k) pp.px.my_op[(epoch & 1u) * kProgramMaxOps + k] = 0u;
                 // a timed-out exchange still advances the epoch: the next launch
                 // then waits for its own arrivals, not for this one's stragglers
                 *pp.px.my_epoch = epoch + 1u;

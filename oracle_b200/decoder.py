@@ -66,13 +66,17 @@ class Qwen35Decoder:
     f32 contract; any storage type the reference admits)."""
 
     def __init__(self, ctx: Context, cfg: Qwen35Config, tensors, contract: str = "q8k",
-                 capacity: int | None = None, max_new: int = 4096, device: int = 0, fused: bool = True):
+                 capacity: int | None = None, max_new: int = 4096, device: int = 0, fused: bool = True,
+                 rank: int = 0, world: int = 1, exchange=None):
         import torch
 
         if contract not in ("q8k", "f32"):
             raise ValueError("contract must be 'q8k' or 'f32'")
+        if world > 1 and (contract != "q8k" or not fused or exchange is None):
+            raise ValueError("several GPUs need the fused Q8_K step and an `exchange` of peer handles")
         self.torch = torch
         self.ctx, self.cfg, self.contract = ctx, cfg, contract
+        self.rank, self.world = rank, world
         # fused (Q8_K contract only): one matvec program per block boundary
         # (output projection + MLP + the next block's input projections, norms,
         # SwiGLU and residual adds applied inside) and one kernel per block core
@@ -81,9 +85,21 @@ class Qwen35Decoder:
         self.cap = int(capacity or cfg.context)
         self.max_new = int(max_new)
         dev = self.dev
-        self.w = {}
+        # Several GPUs: every projection's rows are split evenly over the ranks
+        # (each rank uploads only its rows); the outputs of every projection
+        # live in a peer group's gather buffer, which the programs fill on every
+        # rank over NVLink; the block cores, the embedding and the sampling run
+        # on every rank on the whole vectors (they are small), so every rank
+        # holds the same state and produces the same tokens as one GPU.
+        self.w, self.shard = {}, {}
         for name, qtype, dims, data in tensors:
             arr = np.ascontiguousarray(data).view(np.uint8)
+            if world > 1 and len(dims) == 2 and name not in ("token_embd.weight",) and qtype != TYPE_F32:
+                rows = dims[1]
+                rb = arr.size // rows
+                lo, hi = rank * rows // world, (rank + 1) * rows // world
+                arr = arr[lo * rb:hi * rb]
+                self.shard[name] = (lo, hi - lo)
             host = torch.from_numpy(arr if arr.flags.writeable else arr.copy())
             self.w[name] = (int(qtype), tuple(dims), host.to(dev))
             if contract == "q8k" and len(dims) == 2 and qtype not in (TYPE_F32, TYPE_Q4_K, TYPE_Q6_K) \
@@ -91,18 +107,31 @@ class Qwen35Decoder:
                 raise ValueError(f"{name}: the Q8_K contract runs Q4_K / Q6_K matrices only")
         H, F = cfg.hidden, cfg.ffn
         f32 = lambda n: torch.zeros(n, dtype=torch.float32, device=dev)  # noqa: E731
-        self.hidden, self.normed, self.resid, self.branch = f32(H), f32(H), f32(H), f32(H)
-        self.ffn_gate, self.ffn_up, self.ffn_act, self.ffn_out = f32(F), f32(F), f32(F), f32(H)
+        gathered = dict(hidden=H, resid=H, ffn_gate=F, ffn_up=F, ffn_act=F, qkv=cfg.conv_channels,
+                        z=cfg.value_width, beta=cfg.value_heads, alpha=cfg.value_heads, q_full=2 * cfg.q_width,
+                        k=cfg.kv_width, v=cfg.kv_width, logits=cfg.vocab)
+        self.group = None
+        if world > 1:
+            from . import PeerGroup
+            sizes = {k: (n + 3) // 4 * 4 for k, n in gathered.items()}  # 16-byte aligned vectors
+            self.group = PeerGroup(ctx, rank, world, sum(sizes.values()) * 4)
+            self.group.connect(exchange(self.group.handle))
+            data, off = self.group.tensor(), 0
+            for k, n in gathered.items():
+                setattr(self, k, data[off:off + n])
+                off += sizes[k]
+        else:
+            for k, n in gathered.items():
+                setattr(self, k, f32(n))
+        self.normed, self.branch, self.ffn_out = f32(H), f32(H), f32(H)
         # recurrent blocks
-        self.qkv, self.conv_out, self.z = f32(cfg.conv_channels), f32(cfg.conv_channels), f32(cfg.value_width)
-        self.beta, self.alpha = f32(cfg.value_heads), f32(cfg.value_heads)
+        self.conv_out = f32(cfg.conv_channels)
         self.beta_s, self.log_decay = f32(cfg.value_heads), f32(cfg.value_heads)
         self.rec_out, self.gated = f32(cfg.value_width), f32(cfg.value_width)
         # attention blocks
-        self.q_full, self.q, self.gate = f32(2 * cfg.q_width), f32(cfg.q_width), f32(cfg.q_width)
-        self.qn, self.k, self.kn, self.v = f32(cfg.q_width), f32(cfg.kv_width), f32(cfg.kv_width), f32(cfg.kv_width)
+        self.q, self.gate = f32(cfg.q_width), f32(cfg.q_width)
+        self.qn, self.kn = f32(cfg.q_width), f32(cfg.kv_width)
         self.attn, self.scores = f32(cfg.q_width), f32(cfg.heads * self.cap)
-        self.logits = f32(cfg.vocab)
         self.keys, self.values, self.hist, self.state = {}, {}, {}, {}
         for i in range(cfg.layers):
             if cfg.is_attention(i):
@@ -186,10 +215,13 @@ class Qwen35Decoder:
         self._project([(p + "attn_output.weight", self.attn, self.branch)], s)
 
     # ---------------------------------------------------------------- fused step
-    def _mv(self, name, x, y, after=False, xform=0, x2=None, norm=None, residual=None) -> dict:
+    def _mv(self, name, x, y, after=False, xform=0, x2=None, norm=None, residual=None, act=None) -> dict:
+        """One program op; on several GPUs, this rank's rows of it."""
         qtype, dims, w = self.w[name]
-        return dict(qtype=qtype, rows=dims[1], cols=dims[0], w=w, x=x, y=y, after=after, xform=xform,
-                    eps=self.cfg.eps, x2=x2, norm=norm, residual=residual)
+        lo, n = self.shard.get(name, (0, dims[1]))
+        return dict(qtype=qtype, rows=n, cols=dims[0], w=w, x=x, y=y[lo:lo + n], after=after, xform=xform,
+                    eps=self.cfg.eps, x2=x2, norm=norm, residual=None if residual is None else residual[lo:lo + n],
+                    act=act)
 
     def _input_projections(self, i: int, after: bool) -> list:
         """Block i's projections of rms_norm(hidden) (qwen35_block.cpp:441-463, 643-657)."""
@@ -216,7 +248,7 @@ class Qwen35Decoder:
                 self._mv(p + "ffn_gate.weight", self.resid, self.ffn_gate, **post),
                 self._mv(p + "ffn_up.weight", self.resid, self.ffn_up, **post),
                 self._mv(p + "ffn_down.weight", self.ffn_gate, self.hidden, after=True, xform=XFORM_SWIGLU,
-                         x2=self.ffn_up, residual=self.resid)]
+                         x2=self.ffn_up, residual=self.resid, act=self.ffn_act)]
 
     def _core(self, i: int, s) -> None:
         cfg, ctx, p = self.cfg, self.ctx, f"blk.{i}."
@@ -238,7 +270,10 @@ class Qwen35Decoder:
         if self.timer is not None:
             ev = (self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
             ev[0].record(self.stream)
-        self.ctx.matvec_program_ex(ops, s)
+        if self.group is not None:
+            self.ctx.matvec_program_ex_allgather(self.group, ops, s)
+        else:
+            self.ctx.matvec_program_ex(ops, s)
         if self.timer is not None:
             ev[1].record(self.stream)
             self.timer.append((ev, sum(o["w"].numel() for o in ops)))
@@ -372,6 +407,14 @@ class Qwen35Decoder:
         timer, self.timer = self.timer, None
         self.reset()
         return (sum(n for _, n in timer), sum(e[0].elapsed_time(e[1]) for e, _ in timer), a.elapsed_time(b))
+
+    def close(self) -> None:
+        """Release the graph and the peer group (before the process group goes)."""
+        self.graph = None
+        if self.group is not None:
+            self.stream.synchronize()
+            self.group.close()
+            self.group = None
 
     def launches_per_step(self) -> int:
         """Kernels one step launches (counted by the context on an uncaptured step)."""
