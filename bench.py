@@ -65,7 +65,9 @@ def algorithmic_bytes(qtype: int, k: int, n: int) -> int:
 class Workload:
     """One step of a benchmark configuration: a list of matvecs (qtype, K, N)."""
 
-    def __init__(self, name, metric, description, ops, contract, pool_sets, program, cpu_kind, dtype):
+    def __init__(self, name, metric, description, ops, contract, pool_sets, program, cpu_kind, dtype,
+                 steps_per_launch=1):
+        self.steps_per_launch = steps_per_launch
         self.name, self.metric, self.description = name, metric, description
         self.ops, self.contract, self.pool_sets, self.program = ops, contract, pool_sets, program
         self.cpu_kind, self.dtype = cpu_kind, dtype
@@ -87,9 +89,10 @@ WORKLOADS = {
     "config2": Workload(
         "config2", "Q4_K x Q8_K decode matvec GB/s",
         "config2: Q4_K x Q8_K decode matvec, batch 1, shapes 4096->12288, 12288->4096, 4096->4096 "
-        "(activations quantized to Q8_K in the call), one matvec-program launch per step",
-        [(TYPE_Q4_K, 4096, 12288), (TYPE_Q4_K, 12288, 4096), (TYPE_Q4_K, 4096, 4096)], CONTRACT_Q8K, 6, True,
-        "port", "int8 x u4 -> int32, f32 combine"),
+        "(each step's own activations quantized to Q8_K in the launch); one matvec-program launch runs 5 "
+        "consecutive steps (15 matvecs, each with its own activation, weights and output)",
+        [(TYPE_Q4_K, 4096, 12288), (TYPE_Q4_K, 12288, 4096), (TYPE_Q4_K, 4096, 4096)], CONTRACT_Q8K, 10, True,
+        "port", "int8 x u4 -> int32, f32 combine", steps_per_launch=5),
     "config3": Workload(
         "config3", "Q6_K x Q8_K LM-head matvec GB/s",
         "config3: Q6_K x Q8_K LM-head matvec 4096->151936, batch 1", [(TYPE_Q6_K, 4096, 151936)], CONTRACT_Q8K, 2,
@@ -267,6 +270,12 @@ def max_over_ranks(value: float, world: int) -> float:
 
 # ---------------------------------------------------------------- CPU legs
 
+def synth_activation(wl: Workload, k: int, slot: int) -> np.ndarray:
+    """Activation of width k for step slot `slot` > 0 of a launch (seeded, N(0,1))."""
+    from oracle_b200 import synth
+    return synth.activations(k, 1, wl.name, f"x_{k}_slot{slot}")[0]
+
+
 def host_weights(wl: Workload):
     from oracle_b200 import synth
     ws = [synth.weight(t, n, k, wl.name, f"W_{k}_{n}") for t, k, n in wl.ops]
@@ -386,7 +395,12 @@ def gpu_arm(args, wl: Workload) -> None:
     for s in range(wl.pool_sets):
         pool.append([torch.from_numpy(np.roll(w.reshape(-1), s * BLOCK[t][1])).to(dev)
                      for w, (t, _, _) in zip(ws_local, wl.ops)])
-    x_dev = [torch.from_numpy(x).to(dev) for x in xs]
+    # P steps per launch: step slot p of a launch has its own activations
+    # (slot 0: the seeded ones) and its own outputs
+    P = wl.steps_per_launch
+    xs_sets = [xs] + [[synth_activation(wl, k, p) for _, k, _ in wl.ops] for p in range(1, P)]
+    x_sets = [[torch.from_numpy(x).to(dev) for x in xset] for xset in xs_sets]
+    x_dev = x_sets[0]
     # N > 1, Q8_K contract: the all-gather is fused into the matvec program
     # (rows stored into every peer's gather buffer over NVLink, CUDA IPC);
     # --exchange nccl (or the f32 contract) uses one NCCL all-gather instead
@@ -394,16 +408,20 @@ def gpu_arm(args, wl: Workload) -> None:
     group = None
     if fused:
         import torch.distributed as dist
-        group = ob.PeerGroup(ctx, rank, world, (world * plan.pack_len * 4 + 15) // 16 * 16)
+        group = ob.PeerGroup(ctx, rank, world, (P * world * plan.pack_len * 4 + 15) // 16 * 16)
         handles = [None] * world
         dist.all_gather_object(handles, group.handle)
         group.connect(handles)
-        gathered = group.tensor()[:world * plan.pack_len]
-        y_pack = gathered[rank * plan.pack_len:(rank + 1) * plan.pack_len]
+        region = group.tensor()
+        gathered_sets = [region[p * world * plan.pack_len:(p + 1) * world * plan.pack_len] for p in range(P)]
+        y_packs = [g[rank * plan.pack_len:(rank + 1) * plan.pack_len] for g in gathered_sets]
     else:
-        y_pack = torch.empty(plan.pack_len, dtype=torch.float32, device=dev)
-        gathered = torch.empty(world * plan.pack_len, dtype=torch.float32, device=dev) if world > 1 else None
-    y_dev = [y_pack[o:o + sh.local_rows] for o, sh in zip(plan.offsets, plan.shards)]
+        y_packs = [torch.empty(plan.pack_len, dtype=torch.float32, device=dev) for _ in range(P)]
+        gathered_sets = [torch.empty(world * plan.pack_len, dtype=torch.float32, device=dev) if world > 1 else None
+                         for _ in range(P)]
+    gathered, y_pack = gathered_sets[0], y_packs[0]
+    y_sets = [[yp[o:o + sh.local_rows] for o, sh in zip(plan.offsets, plan.shards)] for yp in y_packs]
+    y_dev = y_sets[0]
     stream = torch.cuda.Stream(dev)
 
     def exchange():
@@ -411,17 +429,29 @@ def gpu_arm(args, wl: Workload) -> None:
             import torch.distributed as dist
             dist.all_gather_into_tensor(gathered, y_pack)
 
-    def step(s: int):
-        ws_ = pool[s % wl.pool_sets]
-        ops_ = [(t, n, k, ws_[i], x_dev[i], y_dev[i], 0) for i, (t, k, n) in enumerate(local_ops)]
+    def launch(s0: int, count: int):
+        """Steps s0 .. s0+count-1 (count <= P): with a program, ONE persistent
+        launch runs all their (independent) matvecs back to back."""
+        if not (fused or wl.program):
+            for s in range(s0, s0 + count):
+                step_separate(s)
+            return
+        ops_ = []
+        for s in range(s0, s0 + count):
+            ws_, p = pool[s % wl.pool_sets], s % P
+            ops_ += [(t, n, k, ws_[i], x_sets[p][i], y_sets[p][i], 0) for i, (t, k, n) in enumerate(local_ops)]
         if fused:
             ctx.matvec_program_allgather(group, ops_, stream=stream)
-        elif wl.program:
-            # one persistent launch runs all the (independent) matvecs of the step
-            ctx.matvec_program(ops_, stream=stream)
-            exchange()
         else:
-            step_separate(s)
+            ctx.matvec_program(ops_, stream=stream)
+            if world > 1:
+                import torch.distributed as dist
+                for p in sorted({s % P for s in range(s0, s0 + count)}):
+                    dist.all_gather_into_tensor(gathered_sets[p], y_packs[p])
+
+    def steps(s0: int, count: int):
+        for a in range(s0, s0 + count, P):
+            launch(a, min(P, s0 + count - a))
 
     def step_separate(s: int):
         ws_ = pool[s % wl.pool_sets]
@@ -429,53 +459,56 @@ def gpu_arm(args, wl: Workload) -> None:
             ctx.storage_matvec(wl.contract, t, n, k, ws_[i], x_dev[i], y_dev[i], stream=stream)
         exchange()
 
-    def outputs() -> list:
+    def outputs(p: int = 0) -> list:
         if world > 1:
-            return plan.unpack(gathered.cpu().numpy())
-        return [y.cpu().numpy() for y in y_dev]
+            return plan.unpack(gathered_sets[p].cpu().numpy())
+        return [y.cpu().numpy() for y in y_sets[p]]
 
-    # correctness gate on this box: set 0 of every op against the CPU checker
+    # correctness gate on this box: the first launch (steps 0 .. P-1, weight
+    # sets 0 .. P-1, activation slots 0 .. P-1), every op against the CPU checker
     with torch.cuda.stream(stream):
-        step(0)
+        steps(0, P)
     stream.synchronize()
     ctx.device_status()
     import oracle
     port = oracle.port()
     wants = []
-    got = outputs()
-    for i, (t, k, n) in enumerate(wl.ops):
-        if wl.contract == CONTRACT_Q8K:
-            wants.append(port.matvec_q8_k(t, n, k, ws[i], port.quantize_q8_k(xs[i]))[0])
-        else:
-            wants.append(port.storage_matvec_f32(t, n, k, ws[i], xs[i])[0])
-        if not np.array_equal(got[i].view(np.uint32), wants[i].view(np.uint32)):
-            raise SystemExit("GPU result differs from the CPU checker; refusing to report a number")
+    for p in range(P):
+        got = outputs(p)
+        for i, (t, k, n) in enumerate(wl.ops):
+            w_host = np.roll(ws[i].reshape(-1), p * BLOCK[t][1]).reshape(ws[i].shape) if p % wl.pool_sets else ws[i]
+            x_host = xs_sets[p][i]
+            if wl.contract == CONTRACT_Q8K:
+                want = port.matvec_q8_k(t, n, k, w_host, port.quantize_q8_k(x_host))[0]
+            else:
+                want = port.storage_matvec_f32(t, n, k, w_host, x_host)[0]
+            if p == 0:
+                wants.append(want)
+            if not np.array_equal(got[i].view(np.uint32), want.view(np.uint32)):
+                raise SystemExit("GPU result differs from the CPU checker; refusing to report a number")
 
     # graph of one pass over the pool (pool_sets steps); K mod pool_sets more from a tail graph
     launches0 = ctx.launch_count()
     with torch.cuda.stream(stream):
-        for s in range(wl.pool_sets):
-            step(s)
+        steps(0, wl.pool_sets)
     stream.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        for s in range(wl.pool_sets):
-            step(s)
-    launches_per_step = (ctx.launch_count() - launches0) // (2 * wl.pool_sets)
+        steps(0, wl.pool_sets)
+    launches_per_pass = (ctx.launch_count() - launches0) / 2
+    launches_per_step = launches_per_pass / wl.pool_sets
     rem = args.steps % wl.pool_sets
     tail = None
     if rem:
         tail = torch.cuda.CUDAGraph()
         with torch.cuda.graph(tail, stream=stream):
-            for s in range(rem):
-                step(s)
+            steps(0, rem)
     # graph replays go to the current stream: make that the capture stream, so
     # the events below bracket exactly the replayed kernels
     with torch.cuda.stream(stream):
         for _ in range(args.warmup // wl.pool_sets):
             graph.replay()
-        for s in range(args.warmup % wl.pool_sets):
-            step(s)
+        steps(0, args.warmup % wl.pool_sets)
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
@@ -518,6 +551,24 @@ def gpu_arm(args, wl: Workload) -> None:
         sep_us = a.elapsed_time(b) * 1e3 / (20 * wl.pool_sets)
         extra["separate_launches"] = {"us_per_step": sep_us, "gbs": wl.step_bytes / (sep_us * 1e-6) / 1e9}
         del gsep
+        if P > 1:
+            # the same steps, one program launch each
+            g1 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g1, stream=stream):
+                for s in range(wl.pool_sets):
+                    launch(s, 1)
+            with torch.cuda.stream(stream):
+                g1.replay()
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(20):
+                    g1.replay()
+                b.record(stream)
+                torch.cuda.synchronize()
+            one_us = a.elapsed_time(b) * 1e3 / (20 * wl.pool_sets)
+            extra["one_step_per_launch"] = {"us_per_step": one_us, "gbs": wl.step_bytes / (one_us * 1e-6) / 1e9}
+            del g1
         per_op = []
         reps = 60
         for i, (t, k, n) in enumerate(wl.ops):
@@ -562,7 +613,7 @@ def gpu_arm(args, wl: Workload) -> None:
             with torch.cuda.stream(stream):
                 for i in range(len(wl.ops)):
                     x_dev[i].copy_(x_pin[i], non_blocking=True)
-                step(0)
+                launch(0, 1)
                 g_pin.copy_(gathered, non_blocking=True)
             stream.synchronize()
 
@@ -595,7 +646,7 @@ def gpu_arm(args, wl: Workload) -> None:
                 "warmup": args.warmup, "ms_per_step": ms / steps_timed, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype,
                 "data": f"synthetic (seeded; BASELINE {wl.name} distributions)", "config": wl.config(world),
-                "gpu_launches": launches_per_step * steps_timed,
+                "gpu_launches": int(round(launches_per_step * steps_timed)),
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": e2e_d2h,
                         "how": e2e_how},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

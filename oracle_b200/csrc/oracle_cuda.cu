@@ -49,6 +49,7 @@ struct oracle_cuda_context {
     uint64_t stage_target = 36864;  // bytes per stage the stage plan aims for
     uint32_t copy_chunk = 32768;    // largest single bulk copy
     uint32_t max_inflight = 16;     // stages a program producer keeps in flight
+    uint32_t jit_image_threshold = 48 * 1024;  // prebuilt image bytes above which programs copy per op
     uint32_t flags = 0;
     uint64_t launches = 0;
     DeviceStatus* status = nullptr;
@@ -871,6 +872,29 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         for (uint32_t k = 1; k < n_ops; ++k)
             if (pp.ops[k].after_previous) pp.ops[k - 1].publish = 1u;
         act_total = off + 256;  // + reduction scratch
+        // Images that would crowd the stage ring out of shared memory stay in
+        // global memory; each op copies its own into one of two slots.
+        if (prebuilt > ctx->jit_image_threshold) {
+            uint32_t slot = 0, old_offset[kProgramMaxOps];
+            bool pre[kProgramMaxOps];
+            for (uint32_t k = 0; k < n_ops; ++k) {
+                old_offset[k] = pp.ops[k].act_offset;
+                pre[k] = pp.ops[k].prebuilt || (owner[k] >= 0 && pp.ops[owner[k]].prebuilt);
+                if (pre[k] && q8k_image_bytes(pp.ops[k].nb) > slot) slot = q8k_image_bytes(pp.ops[k].nb);
+            }
+            uint32_t jit_index = 0;
+            for (uint32_t k = 0; k < n_ops; ++k) {
+                if (pre[k]) {  // a fed-in image (its own or one it shares): copied into a slot
+                    pp.ext[k].jit_src = old_offset[k];
+                    pp.ops[k].prebuilt = 1u;
+                    pp.ops[k].act_offset = (jit_index++ & 1u) * slot;
+                } else {       // built in the kernel: after the two slots
+                    pp.ops[k].act_offset = old_offset[k] - prebuilt + 2 * slot;
+                }
+            }
+            pp.jit_slot_bytes = slot;
+            act_total = act_total - prebuilt + 2 * slot;
+        }
     }
     pp.act_bytes = act_total;
     const uint64_t budget = ctx->smem_budget - stream_barrier_bytes(16) - pp.act_bytes;

@@ -48,6 +48,7 @@ struct ProgramOpExtra {
     uint32_t xform;           // activation transform (q8k.cuh kXform*)
     float eps;                // kXformRms
     uint32_t other_is_gate;
+    uint32_t jit_src;         // jit_slot_bytes > 0: the op's image offset in the global images
     const float* x2;          // kXformSwiglu: up
     const float* norm;        // kXformRms: weights
     // optional SwiGLU pass after the op: act[r] = other_is_gate ? silu(other[r]) * y[r]
@@ -96,6 +97,10 @@ struct ProgramParams {
     uint32_t max_inflight;   // at most this many issued stages not yet landed (1 .. stages)
     const uint8_t* images;   // prebuilt images (global, same layout as shared memory)
     uint32_t prebuilt_bytes; // bytes of the prebuilt region (multiple of 16)
+    // > 0: the prebuilt images stay in global memory and each op's image is
+    // copied into one of two shared-memory slots of this size when the op
+    // starts (programs whose images would not fit in shared memory at once)
+    uint32_t jit_slot_bytes;
     unsigned int* counters;  // kProgramMaxOps completion counters + 1 exit counter, zero at launch
     DeviceStatus* status;
     PeerExchange px;
@@ -236,10 +241,22 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
     const int lane = threadIdx.x & 31;
     const uint32_t S = pp.stages;
 
+    // image slots (jit_slot_bytes > 0): img_full[slot] completes when the
+    // producer's copy of an op's image lands, img_empty[slot] when every
+    // consumer warp has left the op that read the slot (in the reduction
+    // scratch's last 32 bytes)
+    uint64_t* img_full = reinterpret_cast<uint64_t*>(act + pp.act_bytes - 32);
+    uint64_t* img_empty = img_full + 2;
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NCW);
+        }
+        if (pp.jit_slot_bytes) {
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(&img_full[i], 1);
+                mbar_init(&img_empty[i], NCW);
+            }
         }
         fence_mbar_init();
         pdl_launch_dependents();
@@ -250,9 +267,32 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
         // ---------------- producer: every op's stages, back to back
         const uint64_t policy = l2_policy_evict_first();
         uint32_t g = 0;  // global stage counter across ops
+        uint32_t j = 0;  // image copies issued
         bool ok = true;
         for (uint32_t k = 0; k < pp.n_ops && ok; ++k) {
             const ProgramOp op = pp.ops[k];
+            if (pp.jit_slot_bytes != 0 && op.prebuilt) {
+                // the op's image into its slot, once the op two images back has left it
+                bool i_ok = true;
+                if (lane == 0) {
+                    const uint32_t slot = j & 1u;
+                    if (j >= 2) i_ok = mbar_wait(&img_empty[slot], ((j >> 1) - 1) & 1u, pp.status, 18);
+                    if (i_ok) {
+                        const uint32_t bytes = q8k_image_bytes(op.nb);
+                        mbar_arrive_expect_tx(&img_full[slot], bytes);
+                        const uint8_t* src = pp.images + pp.ext[k].jit_src;
+                        for (uint32_t off = 0; off < bytes; off += pp.copy_chunk) {
+                            const uint32_t n = bytes - off < pp.copy_chunk ? bytes - off : pp.copy_chunk;
+                            bulk_copy_g2s(act + op.act_offset + off, src + off, n, &img_full[slot], policy);
+                        }
+                    }
+                }
+                ++j;
+                if (!__shfl_sync(0xFFFFFFFFu, i_ok ? 1 : 0, 0)) {
+                    ok = false;
+                    break;
+                }
+            }
             const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
             const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
             const uint32_t R = op.rows_per_stage;
@@ -305,6 +345,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
         if (lane == 0) {
             const uint32_t first = g > S ? g - S : 0;
             for (uint32_t t = first; t < g; ++t) mbar_wait(&full[t % S], (t / S) & 1, pp.status, 12);
+            // no image copy may still be in flight when the CTA exits
+            for (uint32_t i = j > 2 ? j - 2 : 0; i < j; ++i) mbar_wait(&img_full[i & 1u], (i >> 1) & 1u, pp.status, 19);
         }
         return;
     }
@@ -321,7 +363,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
     // built once, before this kernel, by quantize_images_kernel (the preceding
     // launch on the stream); copy those images into shared memory, so
     // consumers flow from one op's rows into the next without stopping.
-    {
+    if (pp.jit_slot_bytes == 0) {
         const uint4* src = reinterpret_cast<const uint4*>(pp.images);
         uint4* dst = reinterpret_cast<uint4*>(act);
         for (uint32_t i = threadIdx.x; i < pp.prebuilt_bytes / 16; i += NCW * 32) dst[i] = __ldcg(src + i);
@@ -329,8 +371,14 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
     named_barrier_sync(1, NCW * 32);
     uint32_t s = 0, phase = 0;  // slot and parity of the global stage counter
     double* scratch = reinterpret_cast<double*>(act + pp.act_bytes - 256);
+    uint32_t jc = 0;  // image slots consumed
     for (uint32_t k = 0; k < pp.n_ops; ++k) {
         const ProgramOp op = pp.ops[k];
+        if (pp.jit_slot_bytes != 0 && op.prebuilt && !failed) {
+            // the producer copies this op's image into its slot ahead of time
+            const bool ok = mbar_wait(&img_full[jc & 1u], (jc >> 1) & 1u, pp.status, 20);
+            failed = !__all_sync(0xFFFFFFFFu, ok);
+        }
         if (op.after_previous && k > 0) {
             // One poller per CTA: with every warp of every CTA polling, the
             // completion counts they wait for reached L2 microseconds late.
@@ -376,6 +424,12 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             // register-resident variant does not fit beside the Q4_K code in 128 registers
             program_walk_op<NCW, 14, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                             pp.status, pp.px, warp, lane);
+        }
+        if (pp.jit_slot_bytes != 0 && op.prebuilt) {
+            // this warp has left the slot
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&img_empty[jc & 1u]);
+            ++jc;
         }
         if (op.residual && !failed) {
             // y = residual + W.x for this CTA's rows, once its warps wrote them

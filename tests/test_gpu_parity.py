@@ -319,6 +319,23 @@ def test_program_dependent_chain_and_repeat(ctx, port):
             assert bits_equal(y.cpu().numpy(), w)
 
 
+def test_program_many_images_slots(ctx, port):
+    """Programs whose fed-in activation images exceed shared memory's share
+    (15 distinct activations, ~150 KB of images) copy each op's image into one
+    of two slots when the op starts; a dependent op's in-kernel image follows
+    the slots; repeated launches reuse everything."""
+    specs = [(ob.TYPE_Q4_K, 333 + 7 * i, 4096 if i % 3 else 12288, 0) for i in range(15)]
+    specs.append((ob.TYPE_Q4_K, 500, 333 + 7 * 14 - (333 + 7 * 14) % 256, 1))
+    ops, want = _program_case(port, specs, "prog_slots")
+    for _ in range(2):
+        for op in ops:
+            op[5].fill_(float("nan"))
+        ctx.matvec_program(ops)
+        ctx.device_status()
+        for (_, _, _, _, _, y, _), w in zip(ops, want):
+            assert bits_equal(y.cpu().numpy(), w)
+
+
 def test_program_mixed_types(ctx, port):
     specs = [(ob.TYPE_Q6_K, 1000, 4096, 0), (ob.TYPE_Q4_K, 300, 768, 0), (ob.TYPE_Q6_K, 513, 768, 0)]
     ops, want = _program_case(port, specs, "prog_mixed")
