@@ -387,14 +387,16 @@ def gpu_arm(args, wl: Workload) -> None:
     from oracle_b200.shard import PackPlan
     plan = PackPlan([n for _, _, n in wl.ops], world, rank)
     local_ops = [(t, k, sh.local_rows) for (t, k, _), sh in zip(wl.ops, plan.shards)]
-    ws_local = [np.ascontiguousarray(sh.weight_slice(w)) for w, sh in zip(ws, plan.shards)]
     # weight pool: set 0 is the seeded host weights; the others are rotations
     # by whole blocks (same distribution, distinct addresses), so no step finds
     # its weights in L2
+    # (set s = this rank's rows of the full matrix rolled by s blocks, so every
+    # set is a whole matrix the CPU checker can reproduce at any rank count)
     pool = []
     for s in range(wl.pool_sets):
-        pool.append([torch.from_numpy(np.roll(w.reshape(-1), s * BLOCK[t][1])).to(dev)
-                     for w, (t, _, _) in zip(ws_local, wl.ops)])
+        pool.append([torch.from_numpy(np.ascontiguousarray(
+            sh.weight_slice(np.roll(w.reshape(-1), s * BLOCK[t][1]).reshape(w.shape)))).to(dev)
+            for w, sh, (t, _, _) in zip(ws, plan.shards, wl.ops)])
     # P steps per launch: step slot p of a launch has its own activations
     # (slot 0: the seeded ones) and its own outputs
     P = wl.steps_per_launch
