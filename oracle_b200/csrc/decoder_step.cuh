@@ -190,42 +190,48 @@ __global__ void __launch_bounds__(256) mul_silu_kernel(float* __restrict__ x, co
 // A Gated DeltaNet block between its input projections and its output
 // projection, as ONE kernel: Oracle's recurrent block (qwen35_block.cpp:
 // 472-592) from the projected qkv / z / beta / alpha to the gated vector the
-// output projection reads.  One CTA per value head, thread t = value (and key)
-// index, key_dim == value_dim == kD; thread t keeps state column t in
-// registers for the whole update (one read and one write of the state):
-//   gates      beta = sigmoid(beta), log_decay = softplus(alpha + dt_bias) * a
+// output projection reads.  One CTA per value head, key_dim == value_dim ==
+// kD, 4 * kD threads:
 //   conv       the depthwise causal conv + SiLU of the head's q, k (key head
-//              h % key_heads, repeat_heads_tiled) and v channels; the
-//              convolution history is double-buffered by position parity
+//              h % key_heads, repeat_heads_tiled) and v channels, one channel
+//              per thread; the history is double-buffered by position parity
 //              (read slot pos & 1, write the other), so the CTAs that share a
-//              key head read a history nobody writes during the step; the
-//              CTA h < key_heads writes the shared q / k channels
+//              key head read a history nobody writes during the step; the CTA
+//              h < key_heads writes the shared q / k channels
+//   gates      beta = sigmoid(beta), log_decay = softplus(alpha + dt_bias) * a
 //   delta      gated_delta_step (reference_kernels.cpp:221-335) on the head's
-//              [key][value] state
+//              [key][value] state: thread (t, part) keeps rows part * kD/4 ..
+//              of state column t in registers; the two sums over the key
+//              index (the f32 memory read-out and the f64 output) run as four
+//              sequential partial sums combined pairwise, ((p0 + p1) + (p2 +
+//              p3)), instead of one chain of kD terms: the same terms, a
+//              different rounding order (within the decoder's tolerance; the
+//              unfused gated_delta_kernel keeps the reference's order)
 //   out        rms_norm_rows over the head's row, then * silu(z)
-// Each stage keeps the operations and order of the corresponding separate
-// kernel (decoder_ops.cuh), so results are those of the unfused sequence.
 template <int kD>
-__global__ void __launch_bounds__(kD) gdn_core_kernel(const float* __restrict__ qkv, const float* __restrict__ z,
-                                                      const float* __restrict__ beta_in, const float* __restrict__ alpha,
-                                                      const float* __restrict__ dt_bias,
-                                                      const float* __restrict__ decay_a,
-                                                      const float* __restrict__ conv_w, float* hist, float* state,
-                                                      const float* __restrict__ norm_w, uint32_t key_heads,
-                                                      uint32_t value_heads, uint32_t conv_kernel, float eps,
-                                                      const uint32_t* __restrict__ pos, float* __restrict__ out) {
+__global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restrict__ qkv, const float* __restrict__ z,
+                                                          const float* __restrict__ beta_in,
+                                                          const float* __restrict__ alpha,
+                                                          const float* __restrict__ dt_bias,
+                                                          const float* __restrict__ decay_a,
+                                                          const float* __restrict__ conv_w, float* hist, float* state,
+                                                          const float* __restrict__ norm_w, uint32_t key_heads,
+                                                          uint32_t value_heads, uint32_t conv_kernel, float eps,
+                                                          const uint32_t* __restrict__ pos, float* __restrict__ out) {
+    constexpr int kQ = kD / 4;  // key rows per thread
     pdl_launch_dependents();
-    __shared__ float nq[kD], nk[kD];
+    __shared__ float q_s[kD], k_s[kD], v_s[kD], nq[kD], nk[kD], o_s[kD];
     __shared__ double scratch[32];
-    const uint32_t h = blockIdx.x, t = threadIdx.x;
-    // the head's state column t, [key d][value t], held in registers: loads
-    // issued up front, independent of everything computed before the update.
-    // Only this block's own earlier steps write the state, so the loads may
-    // overlap the tail of the preceding kernel (programmatic launch).
-    float* sh = state + static_cast<uint64_t>(h) * kD * kD + t;
-    float col[kD];
+    __shared__ float gate_s[2];
+    const uint32_t h = blockIdx.x, tid = threadIdx.x;
+    const uint32_t t = tid >> 2, part = tid & 3u;  // state column, quarter of the key rows
+    // the state rows of this thread, loaded up front: only this block's own
+    // earlier steps write the state, so the loads may overlap the tail of the
+    // preceding kernel (programmatic launch)
+    float* sh = state + static_cast<uint64_t>(h) * kD * kD + static_cast<uint64_t>(part) * kQ * kD + t;
+    float col[kQ];
 #pragma unroll
-    for (int d = 0; d < kD; ++d) col[d] = sh[d * kD];
+    for (int j = 0; j < kQ; ++j) col[j] = sh[j * kD];
     pdl_wait();
     const uint32_t kh = h % key_heads;
     const uint32_t key_width = key_heads * kD;
@@ -234,56 +240,72 @@ __global__ void __launch_bounds__(kD) gdn_core_kernel(const float* __restrict__ 
     const uint32_t slot = *pos & 1u;
     const float* hin = hist + static_cast<uint64_t>(slot) * channels * K;
     float* hout = hist + static_cast<uint64_t>(slot ^ 1u) * channels * K;
-    auto conv = [&](uint32_t c, bool write) -> float {
+    if (tid < 3 * kD) {
+        const uint32_t which = tid / kD, i = tid % kD;  // 0: q, 1: k, 2: v
+        const uint32_t c = which == 0 ? kh * kD + i : which == 1 ? key_width + kh * kD + i : 2 * key_width + h * kD + i;
+        const bool write = which == 2 || h < key_heads;
         const float* hc = hin + static_cast<uint64_t>(c) * K;
         const float* wc = conv_w + static_cast<uint64_t>(c) * K;
         float* oc = hout + static_cast<uint64_t>(c) * K;
         double sum = 0.0;
-        for (uint32_t i = 0; i < K; ++i) {
-            const float v = i + 1 < K ? hc[i + 1] : qkv[c];
-            if (write) oc[i] = v;
-            sum = __dadd_rn(sum, __dmul_rn(static_cast<double>(v), static_cast<double>(wc[i])));
+        for (uint32_t j = 0; j < K; ++j) {
+            const float v = j + 1 < K ? hc[j + 1] : qkv[c];
+            if (write) oc[j] = v;
+            sum = __dadd_rn(sum, __dmul_rn(static_cast<double>(v), static_cast<double>(wc[j])));
         }
-        return ref_silu(__double2float_rn(sum));
-    };
-    const bool owner = h < key_heads;
-    const float q = conv(kh * kD + t, owner);
-    const float k = conv(key_width + kh * kD + t, owner);
-    const float v = conv(2 * key_width + h * kD + t, true);
-    // gated_delta_step: l2-normalised q (scaled by 1/sqrt(key_dim)) and k
-    const double q_norm = block_sum_f64(__dmul_rn(static_cast<double>(q), static_cast<double>(q)), scratch);
-    const double k_norm = block_sum_f64(__dmul_rn(static_cast<double>(k), static_cast<double>(k)), scratch);
-    const double e = static_cast<double>(eps);
-    const float inv_q = __double2float_rn(__ddiv_rn(1.0, fmax(__dsqrt_rn(q_norm), e)));
-    const float inv_k = __double2float_rn(__ddiv_rn(1.0, fmax(__dsqrt_rn(k_norm), e)));
-    const float q_scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(kD)));
-    nq[t] = __fmul_rn(__fmul_rn(q, inv_q), q_scale);
-    nk[t] = __fmul_rn(k, inv_k);
+        const float r = ref_silu(__double2float_rn(sum));
+        (which == 0 ? q_s : which == 1 ? k_s : v_s)[i] = r;
+    } else if (tid == 3 * kD) {
+        gate_s[0] = ref_sigmoid(beta_in[h]);
+        gate_s[1] = expf(__fmul_rn(ref_softplus(__fadd_rn(alpha[h], dt_bias[h])), decay_a[h]));
+    }
     __syncthreads();
-    const float b = ref_sigmoid(beta_in[h]);
-    const float log_decay = __fmul_rn(ref_softplus(__fadd_rn(alpha[h], dt_bias[h])), decay_a[h]);
-    const float decay = expf(log_decay);
+    // gated_delta_step: l2-normalised q (scaled by 1/sqrt(key_dim)) and k
+    const double qv = tid < kD ? static_cast<double>(q_s[tid]) : 0.0;
+    const double kv = tid < kD ? static_cast<double>(k_s[tid]) : 0.0;
+    const double q_norm = block_sum_f64(__dmul_rn(qv, qv), scratch);
+    const double k_norm = block_sum_f64(__dmul_rn(kv, kv), scratch);
+    if (tid < kD) {
+        const double e = static_cast<double>(eps);
+        const float inv_q = __double2float_rn(__ddiv_rn(1.0, fmax(__dsqrt_rn(q_norm), e)));
+        const float inv_k = __double2float_rn(__ddiv_rn(1.0, fmax(__dsqrt_rn(k_norm), e)));
+        const float q_scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(kD)));
+        nq[tid] = __fmul_rn(__fmul_rn(q_s[tid], inv_q), q_scale);
+        nk[tid] = __fmul_rn(k_s[tid], inv_k);
+    }
+    __syncthreads();
+    const float b = gate_s[0], decay = gate_s[1];
+    const float* nkp = nk + part * kQ;
+    const float* nqp = nq + part * kQ;
     float mem = 0.0f;
 #pragma unroll
-    for (int d = 0; d < kD; ++d) {
-        col[d] = __fmul_rn(col[d], decay);
-        mem = __fadd_rn(mem, __fmul_rn(col[d], nk[d]));
+    for (int j = 0; j < kQ; ++j) {
+        col[j] = __fmul_rn(col[j], decay);
+        mem = __fadd_rn(mem, __fmul_rn(col[j], nkp[j]));
     }
-    const float delta = __fmul_rn(__fsub_rn(v, mem), b);
+    mem = __fadd_rn(mem, __shfl_xor_sync(0xFFFFFFFFu, mem, 1));
+    mem = __fadd_rn(mem, __shfl_xor_sync(0xFFFFFFFFu, mem, 2));
+    const float delta = __fmul_rn(__fsub_rn(v_s[t], mem), b);
     double o = 0.0;
 #pragma unroll
-    for (int d = 0; d < kD; ++d) {
-        col[d] = __fadd_rn(col[d], __fmul_rn(nk[d], delta));
-        o = __dadd_rn(o, __dmul_rn(static_cast<double>(col[d]), static_cast<double>(nq[d])));
+    for (int j = 0; j < kQ; ++j) {
+        col[j] = __fadd_rn(col[j], __fmul_rn(nkp[j], delta));
+        o = __dadd_rn(o, __dmul_rn(static_cast<double>(col[j]), static_cast<double>(nqp[j])));
     }
+    o = __dadd_rn(o, __shfl_xor_sync(0xFFFFFFFFu, o, 1));
+    o = __dadd_rn(o, __shfl_xor_sync(0xFFFFFFFFu, o, 2));
 #pragma unroll
-    for (int d = 0; d < kD; ++d) sh[d * kD] = col[d];
-    const float of = __double2float_rn(o);
+    for (int j = 0; j < kQ; ++j) sh[j * kD] = col[j];
+    if (part == 0) o_s[t] = __double2float_rn(o);
+    __syncthreads();
     // rms_norm_rows over the head's row, then gated *= silu(z)
+    const float of = tid < kD ? o_s[tid] : 0.0f;
     const float inv = rms_inverse(block_sum_f64(__dmul_rn(static_cast<double>(of), static_cast<double>(of)), scratch),
                                   kD, eps);
-    const float g = __fmul_rn(__fmul_rn(of, inv), norm_w[t]);
-    out[static_cast<uint64_t>(h) * kD + t] = __fmul_rn(g, ref_silu(z[static_cast<uint64_t>(h) * kD + t]));
+    if (tid < kD) {
+        const float g = __fmul_rn(__fmul_rn(of, inv), norm_w[tid]);
+        out[static_cast<uint64_t>(h) * kD + tid] = __fmul_rn(g, ref_silu(z[static_cast<uint64_t>(h) * kD + tid]));
+    }
 }
 
 // The gated attention block up to its softmax, as one kernel per query head

@@ -1974,7 +1974,7 @@ extern "C" oracle_cuda_status oracle_cuda_gdn_core(oracle_cuda_context* ctx, con
     if (!pos_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "position pointer is null");
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
     const oracle_cuda_status s =
-        launch(ctx, head_dim == 128 ? gdn_core_kernel<128> : gdn_core_kernel<64>, dim3(value_heads), dim3(head_dim), 0,
+        launch(ctx, head_dim == 128 ? gdn_core_kernel<128> : gdn_core_kernel<64>, dim3(value_heads), dim3(4 * head_dim), 0,
                static_cast<cudaStream_t>(stream), (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, qkv_dev, z_dev, beta_dev, alpha_dev, time_step_bias_dev,
                decay_dev, conv_weights_dev, history_dev, state_dev, norm_dev, key_heads, value_heads, conv_kernel,
                eps, pos_dev, out_dev);

@@ -7,7 +7,9 @@
   integer dots / add, each as Oracle's or GGML's code does it).
 * The fused Gated DeltaNet core and the fused attention kernels against the
   separate kernels they replace (themselves checked against Oracle's compiled
-  functions): bit-identical outputs, states and caches over several steps.
+  functions) over several steps: attention bit-identical; the recurrent core
+  within 1e-5 relative / 1e-6 absolute (its key-index sums are split four
+  ways), conv histories bit-identical.
 """
 from __future__ import annotations
 
@@ -25,6 +27,12 @@ EPS = float(np.float32(1e-6))
 
 def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def close(got, want, rel=1e-5, ab=1e-6):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    bad = np.abs(got - want) > ab + rel * np.abs(want)
+    assert not bad.any(), (int(bad.sum()), float(np.abs(got - want).max()))
 
 
 def same(a, b):
@@ -127,8 +135,10 @@ def test_gdn_core_matches_separate_kernels(ctx):
         ctx.gdn_core(qkv, z, beta, alpha, dt, a, conv_w, hist2, state2, norm, kh, vh, D, K, EPS, pos, fused)
         ctx.position_advance(pos)
         ctx.device_status()
-        assert same(fused.cpu().numpy(), gated.cpu().numpy()), step
-        assert same(state2.cpu().numpy(), state1.cpu().numpy()), step
+        # the fused core sums the key index as four partial sums: same terms,
+        # another rounding order (the decoder's 1e-5 / 1e-6 tolerance)
+        close(fused.cpu().numpy(), gated.cpu().numpy())
+        close(state2.cpu().numpy(), state1.cpu().numpy())
         slot = (step + 1) & 1
         assert same(hist2[slot * C * K:(slot + 1) * C * K].cpu().numpy(), hist1.cpu().numpy()), step
 
