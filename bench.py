@@ -992,7 +992,7 @@ def decoder_reference_arm(args, wl: DecoderWorkload) -> None:
                    "(single-threaded); Q4_K/Q6_K projections through the C restatement of GGML's Q8_K dot, "
                    "since Oracle's own decoder rejects Q4_K"}
     line = {"impl": "reference", "metric": wl.metric, "value": tps, "unit": wl.unit, "n_gpus": args.gpus,
-            "steps": n, "warmup": 0, "ms_per_step": s * 1e3 / n, "higher_is_better": True, "scaling": "weak",
+            "steps": n, "warmup": 0, "ms_per_step": s * 1e3 / n, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded Q4_K_M weights)",
             "config": wl.config(1), "cpu_baseline": cpu,
             "e2e": {"value": tps, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
