@@ -80,6 +80,10 @@ struct GemmParams {
     uint32_t k_per_split;    // columns per blockIdx.z (multiple of 256)
     uint32_t accumulate;     // 1: add into y (split K), 0: store
     DeviceStatus* status;
+    // tiles_m > 0: blockIdx.x numbers tiles from tile_base in m-fastest order
+    // (tile t = n_tile * tiles_m + m_tile), so a launch may cover any run of
+    // tiles; 0: blockIdx.x / blockIdx.y are the n / m tile
+    uint32_t tile_base, tiles_m;
 };
 
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms of
@@ -278,7 +282,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = kPair ? cluster_rank() : 0u;
-    const uint32_t n0 = blockIdx.x * kGemmTileN, m0 = blockIdx.y * kGemmTileM;
+    const uint32_t tile = p.tile_base + blockIdx.x;
+    const uint32_t n0 = (p.tiles_m ? tile / p.tiles_m : blockIdx.x) * kGemmTileN;
+    const uint32_t m0 = (p.tiles_m ? tile % p.tiles_m : blockIdx.y) * kGemmTileM;
     const uint32_t b_row0 = m0 + rank * Plan::kBRows;  // this CTA's B rows (tokens)
     const uint32_t k_begin = blockIdx.z * p.k_per_split;
     const uint32_t k_end = p.k - k_begin < p.k_per_split ? p.k : k_begin + p.k_per_split;

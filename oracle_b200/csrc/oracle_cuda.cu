@@ -1487,9 +1487,51 @@ extern "C" oracle_cuda_status oracle_cuda_prefill_gemm(oracle_cuda_context* ctx,
     gp.n = static_cast<uint32_t>(rows);
     gp.m = static_cast<uint32_t>(m);
     gp.k = static_cast<uint32_t>(cols);
-    gp.k_per_split = gemm_k_per_split(tiles_m * grid_n, cols, ctx->sm_count);
-    gp.accumulate = gp.k_per_split < cols ? 1u : 0u;
     gp.status = ctx->status;
+    const uint64_t tiles = tiles_m * grid_n;
+    const uint64_t sms = static_cast<uint64_t>(ctx->sm_count);
+    // Whole waves of whole tiles, then the remaining tiles (rounded up to
+    // whole weight-row tiles, so their outputs are whole column ranges of y)
+    // split along K so that they fill the last wave: one launch each, when
+    // splitting the remainder shortens it (else one launch of every tile).
+    uint64_t tail = tiles % sms, best_splits = 1;
+    tail = (tail + tiles_m - 1) / tiles_m * tiles_m;
+    if (!pair && tiles > sms && tail < tiles) {
+        double best_cost = static_cast<double>((tail + sms - 1) / sms);
+        for (uint64_t sp = 2; sp <= 8; sp *= 2) {
+            if ((cols / 256) % sp != 0 || cols / sp < 1024) break;
+            const double cost = static_cast<double>((tail * sp + sms - 1) / sms) / static_cast<double>(sp);
+            if (cost < best_cost - 1e-9) {
+                best_cost = cost;
+                best_splits = sp;
+            }
+        }
+    }
+    if (best_splits > 1) {
+        const uint64_t head = tiles - tail;
+        gp.tiles_m = static_cast<uint32_t>(tiles_m);
+        if (head > 0) {
+            gp.tile_base = 0;
+            gp.k_per_split = static_cast<uint32_t>(cols);
+            gp.accumulate = 0;
+            oracle_cuda_status ls = launch(ctx, gemm_q4k_bf16_kernel<false>, dim3(static_cast<uint32_t>(head), 1, 1),
+                                           dim3(kGemmThreads), GemmPlan<false>::kSmemBytes, stream, false, tx, tw, gp);
+            if (ls != ORACLE_CUDA_OK) return ls;
+        }
+        gp.tile_base = static_cast<uint32_t>(head);
+        gp.k_per_split = static_cast<uint32_t>(cols / best_splits);
+        gp.accumulate = 1u;
+        const uint64_t n_first = head / tiles_m * kGemmTileN;  // first weight row of the tail tiles
+        ORACLE_CUDA_TRY(ctx,
+                        cudaMemset2DAsync(y_dev + n_first, rows * sizeof(float), 0, (rows - n_first) * sizeof(float),
+                                          m, stream),
+                        "cudaMemset2DAsync");
+        return launch(ctx, gemm_q4k_bf16_kernel<false>,
+                      dim3(static_cast<uint32_t>(tail), 1, static_cast<uint32_t>(best_splits)), dim3(kGemmThreads),
+                      GemmPlan<false>::kSmemBytes, stream, false, tx, tw, gp);
+    }
+    gp.k_per_split = gemm_k_per_split(tiles, cols, ctx->sm_count);
+    gp.accumulate = gp.k_per_split < cols ? 1u : 0u;
     if (gp.accumulate) ORACLE_CUDA_TRY(ctx, cudaMemsetAsync(y_dev, 0, m * rows * sizeof(float), stream), "cudaMemsetAsync");
     const dim3 grid(static_cast<uint32_t>(grid_n), static_cast<uint32_t>(tiles_m),
                     static_cast<uint32_t>(cols / gp.k_per_split));

@@ -69,6 +69,22 @@ def test_gemm_config4(ctx, port, n, k, m):
     check(port, w, x, n, k, m, got, mi, ni)
 
 
+def test_gemm_wave_tail_split(ctx, port):
+    """More tiles than SMs: whole waves of whole tiles, then the leftover weight-row
+    tiles split along K (zeroed output columns, accumulation) in a second launch.
+    150 tiles of 128 rows x 256 tokens: 148 whole, the last weight-row tile split in two."""
+    import torch
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    n, k, m = 128 * ((sms + 2) // 2), 2048, 512
+    w = synth.weight(ob.TYPE_Q4_K, n, k, "gemm", f"tail_w_{n}")
+    x = synth.activations(k, m, "gemm", "tail_x")
+    got = run_gemm(ctx, w, x, n, k, m)
+    rng = np.random.default_rng(5)
+    mi, ni = sample(rng, m, n, 1500)
+    tail_rows = rng.integers(n - 256, n, 1500)  # the K-split tiles
+    check(port, w, x, n, k, m, got, np.concatenate([mi, rng.integers(0, m, 1500)]), np.concatenate([ni, tail_rows]))
+
+
 def test_gemm_repeatable(ctx):
     """Without a K split the result does not depend on timing: two calls agree bit for bit."""
     n, k, m = 12288, 1024, 512  # 192 tiles: no K split
