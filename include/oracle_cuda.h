@@ -110,6 +110,12 @@ oracle_cuda_status oracle_cuda_destroy(oracle_cuda_context* ctx);
  * only before reading activations.  Only safe when the preceding kernel does
  * not write the weight bytes. */
 #define ORACLE_CUDA_FLAG_PDL 1u
+/* ORACLE_CUDA_FLAG_BUILD_IN_KERNEL: matvec programs quantize the activations
+ * of their first ops inside the program kernel (every CTA its own copy)
+ * instead of a separate quantizer launch before it: one launch fewer per
+ * program, for chains of short programs (a decode step).  Programs whose
+ * fed-in images would not fit in shared memory keep the quantizer launch. */
+#define ORACLE_CUDA_FLAG_BUILD_IN_KERNEL 2u
 oracle_cuda_status oracle_cuda_set_flags(oracle_cuda_context* ctx, uint32_t flags);
 
 /* Device status word written by kernels whose bounded waits expired.  Reads it

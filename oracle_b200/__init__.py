@@ -40,6 +40,7 @@ TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K, TYPE_Q8_K, TYPE_
     0, 1, 8, 12, 13, 14, 15, 30)
 CONTRACT_F32, CONTRACT_Q8K = 0, 1
 FLAG_PDL = 1
+FLAG_BUILD_IN_KERNEL = 2
 Q8K_BLOCK_BYTES = 292
 
 if not os.path.exists(LIB_PATH):

@@ -841,9 +841,15 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
                 if (owner[j] < 0 && same_source(ops[j], ops[k])) owner[k] = static_cast<int>(j);
             if (owner[k] >= 0) pp.ops[k].after_previous = 0u;
         }
+        // in-kernel builds of fed-in images only while they all fit in shared
+        // memory beside the ring; otherwise prebuilt images (slots when large)
+        uint64_t fed = 0;
+        for (uint32_t k = 0; k < n_ops; ++k)
+            if (owner[k] < 0 && !pp.ops[k].after_previous) fed += q8k_image_bytes(pp.ops[k].nb);
+        const bool in_kernel = (ctx->flags & ORACLE_CUDA_FLAG_BUILD_IN_KERNEL) != 0 && fed <= ctx->jit_image_threshold;
         uint32_t off = 0;
         for (uint32_t k = 0; k < n_ops; ++k)
-            if (owner[k] < 0 && !pp.ops[k].after_previous) {
+            if (owner[k] < 0 && !pp.ops[k].after_previous && !in_kernel) {
                 pp.ops[k].act_offset = off;
                 pp.ops[k].prebuilt = 1u;
                 const uint32_t jn = jobs.n_jobs;
@@ -862,7 +868,7 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         prebuilt = off;
         jobs.first_block[jobs.n_jobs] = blocks;
         for (uint32_t k = 0; k < n_ops; ++k)
-            if (owner[k] < 0 && pp.ops[k].after_previous) {
+            if (owner[k] < 0 && (pp.ops[k].after_previous || in_kernel)) {
                 pp.ops[k].act_offset = off;
                 pp.ext[k].build = 1u;
                 off += q8k_image_bytes(pp.ops[k].nb);

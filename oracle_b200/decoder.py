@@ -24,7 +24,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import CONTRACT_F32, FLAG_PDL, XFORM_RMS, XFORM_SWIGLU, Context, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K
+from . import CONTRACT_F32, FLAG_BUILD_IN_KERNEL, FLAG_PDL, XFORM_RMS, XFORM_SWIGLU, Context, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K
 from .qwen35 import Qwen35Config
 
 
@@ -67,7 +67,7 @@ class Qwen35Decoder:
 
     def __init__(self, ctx: Context, cfg: Qwen35Config, tensors, contract: str = "q8k",
                  capacity: int | None = None, max_new: int = 4096, device: int = 0, fused: bool = True,
-                 rank: int = 0, world: int = 1, exchange=None):
+                 rank: int = 0, world: int = 1, exchange=None, build_in_kernel: bool = False):
         import torch
 
         if contract not in ("q8k", "f32"):
@@ -152,7 +152,7 @@ class Qwen35Decoder:
         # programmatic dependent launch: each kernel of the step launches while
         # its predecessor drains (programs start streaming weights early)
         if self.fused:
-            ctx.set_flags(ctx.flags | FLAG_PDL)
+            ctx.set_flags(ctx.flags | FLAG_PDL | (FLAG_BUILD_IN_KERNEL if build_in_kernel else 0))
         self.timer = None  # list of (start, end) CUDA events around projections, when set
 
     # ---------------------------------------------------------------- pieces

@@ -357,6 +357,29 @@ def test_program_q6k_only(ctx, port, specs):
         assert bits_equal(y.cpu().numpy(), w)
 
 
+@pytest.mark.parametrize("specs", [
+    # Q4_K rows of 17..136 super-blocks (ragged last passes, row counts not
+    # multiples of the warps), beside short rows, and long-row ops fed by the
+    # previous op
+    [(ob.TYPE_Q4_K, 149, 17 * 256, 0), (ob.TYPE_Q4_K, 301, 33 * 256, 0), (ob.TYPE_Q4_K, 5, 40 * 256, 0),
+     (ob.TYPE_Q4_K, 777, 48 * 256, 0), (ob.TYPE_Q4_K, 333, 4096, 0), (ob.TYPE_Q4_K, 1000, 21 * 256, 0)],
+    [(ob.TYPE_Q4_K, 160, 136 * 256, 0)],
+    [(ob.TYPE_Q4_K, 211, 112 * 256, 0), (ob.TYPE_Q4_K, 90, 40 * 256, 0)],
+    [(ob.TYPE_Q4_K, 5000, 4096, 0), (ob.TYPE_Q4_K, 700, 19 * 256, 1), (ob.TYPE_Q4_K, 4864, 700 - 700 % 256, 1)],
+    [(ob.TYPE_Q6_K, 400, 4096, 0), (ob.TYPE_Q4_K, 611, 12288, 0), (ob.TYPE_Q6_K, 99, 12288, 0)]])   # mixed
+def test_program_long_rows(ctx, port, specs):
+    """Rows longer than 16 super-blocks (several passes over the activation
+    image per row), bit-identical to the restatement."""
+    ops, want = _program_case(port, specs, f"prog_long_{len(specs)}")
+    for _ in range(2):
+        for op in ops:
+            op[5].fill_(float("nan"))
+        ctx.matvec_program(ops)
+        ctx.device_status()
+        for (_, _, _, _, _, y, _), w in zip(ops, want):
+            assert bits_equal(y.cpu().numpy(), w)
+
+
 def test_program_validation(ctx):
     w = to_dev(synth.weight(ob.TYPE_Q4_K, 4, 256, "gpu", "progval"))
     x = torch.zeros(256, dtype=torch.float32, device=DEV)

@@ -61,9 +61,21 @@ def test_rms_transform_prebuilt(ctx, port):
     assert same(y.cpu().numpy(), want)
 
 
-def test_decode_chain_in_one_launch(ctx, port):
+@pytest.mark.parametrize("in_kernel", [False, True])
+def test_decode_chain_in_one_launch(ctx, port, in_kernel):
     """out-projection (+residual) -> gate/up of rms(resid) (shared image) ->
-    down of swiglu(gate, up) (+residual) -> next projections of rms(hidden)."""
+    down of swiglu(gate, up) (+residual) -> next projections of rms(hidden).
+    The first op's image comes from the quantizer launch, or (in_kernel) is
+    built by every CTA of the program itself."""
+    saved = ctx.flags
+    ctx.set_flags((saved & ~ob.FLAG_BUILD_IN_KERNEL) | (ob.FLAG_BUILD_IN_KERNEL if in_kernel else 0))
+    try:
+        _decode_chain(ctx, port)
+    finally:
+        ctx.set_flags(saved)
+
+
+def _decode_chain(ctx, port):
     H, F = 1024, 3072
     hidden = RNG.standard_normal(H).astype(np.float32)
     xin = RNG.standard_normal(H).astype(np.float32)
