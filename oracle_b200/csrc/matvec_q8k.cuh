@@ -167,14 +167,16 @@ __device__ __forceinline__ void fetch_lane_x(const ActImage& img, uint32_t i, in
 // kXReg: rows of at most 16 super-blocks (one pass) with the lane's activation
 // slice (xw, xbs, xd) already in registers; otherwise every pass re-reads it
 // from the shared-memory image (conflict-free).
-template <uint32_t kType, bool kXReg>
+// kUnroll: passes unrolled by this factor (2 lets a pass's shared loads
+// overlap the previous pass's arithmetic, where registers allow).
+template <uint32_t kType, bool kXReg, int kUnroll = 1>
 __device__ __forceinline__ float q8k_row_dot(uint32_t nb, const ActImage& img, const uint8_t* rowp,
                                              const uint32_t (&xw)[32], const int (&xbs)[8], float xd, int lane) {
     const int j = lane >> 1, part = lane & 1;
     constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
     const uint32_t passes = kXReg ? 1u : (nb + 15u) / 16u;
     float acc0 = 0.0f, acc1 = 0.0f;
-#pragma unroll 1
+#pragma unroll kUnroll
     for (uint32_t k = 0; k < passes; ++k) {
         const uint32_t i = 16u * k + j;
         const bool active = i < nb;
@@ -216,6 +218,81 @@ __device__ __forceinline__ float q8k_row_dot(uint32_t nb, const ActImage& img, c
     float v = __fadd_rn(acc0, acc1);
 #pragma unroll
     for (int off = 16; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+    return v;
+}
+
+// Two rows at once (the same activation slice fetched once per pass for
+// both): each row's terms and its per-lane accumulators exactly as
+// q8k_row_dot computes them; the two butterflies share their first level
+// (lanes 0-15 keep row A's sums of pairs j and j + 8, lanes 16-31 row B's,
+// by one exchange), then fold 8, 4, 2 lanes as one.  The result is row A's
+// dot product on lane 0 and row B's on lane 16, bit-identical to
+// q8k_row_dot (every addition has the same two operands; fadd commutes).
+template <uint32_t kType, bool kXReg>
+__device__ __forceinline__ float q8k_row_dot2(uint32_t nb, const ActImage& img, const uint8_t* rowa,
+                                              const uint8_t* rowb, const uint32_t (&xw)[32], const int (&xbs)[8],
+                                              float xd, int lane) {
+    const int j = lane >> 1, part = lane & 1;
+    constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
+    const uint32_t passes = kXReg ? 1u : (nb + 15u) / 16u;
+    float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+#pragma unroll 1
+    for (uint32_t k = 0; k < passes; ++k) {
+        const uint32_t i = 16u * k + j;
+        const bool active = i < nb;
+        int ia = 0, ma = 0, ib = 0, mb = 0;
+        float dwa = 0.0f, dmwa = 0.0f, dwb = 0.0f, dmwb = 0.0f, dx = 0.0f;
+        if (active) {
+            const size_t off = size_t(i) * kBlockBytes;
+            if constexpr (kXReg) {
+                dx = xd;
+                if (kType == 12) {
+                    q4k_half_sums(rowa + off, part, xw, xbs, ia, ma, dwa, dmwa);
+                    q4k_half_sums(rowb + off, part, xw, xbs, ib, mb, dwb, dmwb);
+                } else {
+                    q6k_half_sums(rowa + off, part, xw, xbs, ia, dwa);
+                    q6k_half_sums(rowb + off, part, xw, xbs, ib, dwb);
+                }
+            } else {
+                uint32_t w[32];
+                int bs[8];
+                fetch_lane_x<kType>(img, i, part, w, bs, dx);
+                if (kType == 12) {
+                    q4k_half_sums(rowa + off, part, w, bs, ia, ma, dwa, dmwa);
+                    q4k_half_sums(rowb + off, part, w, bs, ib, mb, dwb, dmwb);
+                } else {
+                    q6k_half_sums(rowa + off, part, w, bs, ia, dwa);
+                    q6k_half_sums(rowb + off, part, w, bs, ib, dwb);
+                }
+            }
+        }
+        ia += __shfl_xor_sync(0xFFFFFFFFu, ia, 1);
+        ib += __shfl_xor_sync(0xFFFFFFFFu, ib, 1);
+        if (kType == 12) {
+            ma += __shfl_xor_sync(0xFFFFFFFFu, ma, 1);
+            mb += __shfl_xor_sync(0xFFFFFFFFu, mb, 1);
+        }
+        if (active) {
+            float pa = __fmul_rn(__fmul_rn(dwa, dx), __int2float_rn(ia));
+            float pb = __fmul_rn(__fmul_rn(dwb, dx), __int2float_rn(ib));
+            if (kType == 12) {
+                pa = __fsub_rn(pa, __fmul_rn(__fmul_rn(dmwa, dx), __int2float_rn(ma)));
+                pb = __fsub_rn(pb, __fmul_rn(__fmul_rn(dmwb, dx), __int2float_rn(mb)));
+            }
+            if (k & 1) {
+                a1 = __fadd_rn(a1, pa);
+                b1 = __fadd_rn(b1, pb);
+            } else {
+                a0 = __fadd_rn(a0, pa);
+                b0 = __fadd_rn(b0, pb);
+            }
+        }
+    }
+    const float va = __fadd_rn(a0, a1), vb = __fadd_rn(b0, b1);
+    const bool low = lane < 16;
+    float v = __fadd_rn(low ? va : vb, __shfl_xor_sync(0xFFFFFFFFu, low ? vb : va, 16));
+#pragma unroll
+    for (int off = 8; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
     return v;
 }
 

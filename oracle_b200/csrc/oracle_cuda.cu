@@ -47,6 +47,9 @@ struct oracle_cuda_context {
     int max_smem_optin = 0;
     uint64_t smem_budget = 0;  // per-CTA shared memory for stream kernels (0 = all)
     uint64_t stage_target = 36864;  // bytes per stage the stage plan aims for
+    // matvec programs: bytes per stage (two rows per consumer warp, e.g. 28
+    // rows of 16 super-blocks) while at least kProgramMinStages stages fit
+    uint64_t program_stage_target = 65536;
     uint32_t copy_chunk = 32768;    // largest single bulk copy
     uint32_t max_inflight = 16;     // stages a program producer keeps in flight
     uint32_t jit_image_threshold = 48 * 1024;  // prebuilt image bytes above which programs copy per op
@@ -221,6 +224,7 @@ constexpr int kQ8KConsumerWarps = 16;
 // registers, which leaves room for one warp of the next step's quantizer
 // (quantize_images_kernel, one warp per CTA) to run beside a program CTA.
 constexpr int kProgramWarps = 14;
+constexpr uint64_t kProgramMinStages = 3;
 
 template <class Consumer>
 oracle_cuda_status launch_stream(oracle_cuda_context* ctx, const uint8_t* w, uint64_t rows, uint64_t row_bytes,
@@ -489,6 +493,10 @@ oracle_cuda_status oracle_cuda_create(int device, oracle_cuda_context** out) {
     if (const char* env = std::getenv("ORACLE_CUDA_STAGE_BYTES")) {
         const unsigned long long v = std::strtoull(env, nullptr, 10);
         if (v >= 4096 && v <= 200000) ctx->stage_target = v;
+    }
+    if (const char* env = std::getenv("ORACLE_CUDA_PROGRAM_STAGE_BYTES")) {
+        const unsigned long long v = std::strtoull(env, nullptr, 10);
+        if (v >= 4096 && v <= 200000) ctx->program_stage_target = v;
     }
     if (const char* env = std::getenv("ORACLE_CUDA_MAX_INFLIGHT")) {
         const unsigned long long v = std::strtoull(env, nullptr, 10);
@@ -769,12 +777,6 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         pp.ext[k].x2 = e.x2_dev;
         pp.ext[k].norm = e.norm_dev;
         p.residual = e.residual_dev;
-        uint64_t R = ctx->stage_target / rb;
-        if (R > uint64_t(kProgramWarps)) R = kProgramWarps;
-        if (R < 1) R = 1;
-        p.rows_per_stage = static_cast<uint32_t>(R);
-        const uint64_t sb = align_up(static_cast<uint32_t>(R * rb + 32), 128u);
-        if (sb > stage) stage = sb;
         if (o.rows > max_rows) max_rows = o.rows;
     }
     // A SwiGLU op whose gate and up are outputs of two earlier ops of this
@@ -903,8 +905,26 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         }
     }
     pp.act_bytes = act_total;
+    if (pp.act_bytes > 96 * 1024)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "matvec program rows too long for the shared-memory stage ring");
     const uint64_t budget = ctx->smem_budget - stream_barrier_bytes(16) - pp.act_bytes;
-    if (pp.act_bytes > 96 * 1024 || stage * 2 > budget)
+    {
+        // rows per stage: up to two per consumer warp (Q4_K rows of <= 16
+        // super-blocks are computed in pairs), within the stage target, and
+        // small enough that kProgramMinStages stages fit beside the images
+        uint64_t target = budget / kProgramMinStages;
+        if (target > ctx->program_stage_target) target = ctx->program_stage_target;
+        for (uint32_t k = 0; k < n_ops; ++k) {
+            const uint64_t rb = pp.ops[k].row_bytes;
+            uint64_t R = target > 32 ? (target - 32) / rb : 0;
+            if (R > uint64_t(2 * kProgramWarps)) R = 2 * kProgramWarps;
+            if (R < 1) R = 1;
+            pp.ops[k].rows_per_stage = static_cast<uint32_t>(R);
+            const uint64_t sb = align_up(static_cast<uint32_t>(R * rb + 32), 128u);
+            if (sb > stage) stage = sb;
+        }
+    }
+    if (stage * 2 > budget)
         return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "matvec program rows too long for the shared-memory stage ring");
     uint64_t S = budget / stage;
     if (S > 16) S = 16;

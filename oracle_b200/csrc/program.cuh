@@ -171,7 +171,19 @@ __device__ __forceinline__ void push_to_peers(const PeerExchange& px, const floa
 // time (weight type; activation slice in registers or re-read per pass).
 // Every warp walks every stage (also those holding none of its rows) and
 // arrives on its `empty` barrier, so no warp ever waits two phases ahead.
-template <int NCW, uint32_t kType, bool kXReg>
+// One output row: into y here and, in a peer group, into every peer's gather
+// buffer at the same offset (NVLink store).
+__device__ __forceinline__ void program_store_row(const PeerExchange& px, float* yr, float v) {
+    *yr = v;
+    if (px.world > 1) {
+        const size_t off = static_cast<size_t>(yr - px.local_base);
+#pragma unroll
+        for (uint32_t p = 0; p < kMaxPeers; ++p)
+            if (p < px.world && p != px.rank) px.peer_base[p][off] = v;
+    }
+}
+
+template <int NCW, uint32_t kType, bool kXReg, int kUnroll = 1>
 __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* act, uint8_t* stage0,
                                                 uint32_t stage_bytes, uint32_t S, uint64_t* full, uint64_t* empty,
                                                 uint32_t& s, uint32_t& phase, bool& failed, DeviceStatus* status,
@@ -190,7 +202,13 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
     const uint32_t wlo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w));
     const uint32_t row0 = static_cast<uint32_t>(r0);
     float* const y = op.y + r0;
-    uint32_t owner_base = 0;  // (t * R) % NCW
+    // A warp's task: two consecutive rows of a stage computed together by
+    // q8k_row_dot2 (Q4_K rows with the slice in registers; the last task of a
+    // stage may hold one row), else one row.  Tasks rotate over the warps
+    // from stage to stage.
+    constexpr uint32_t kPer = (kType == 12 && kXReg) ? 2u : 1u;
+    const uint32_t step = ((R + kPer - 1) / kPer) % NCW;
+    uint32_t owner_base = 0;  // (t * ceil(R / kPer)) % NCW
     for (uint32_t t = 0; t < T; ++t) {
         if (!failed) {
             const bool ok = mbar_wait(&full[s], phase, status, 14);
@@ -201,18 +219,19 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
             const uint32_t n_here = nrows - q_lo < R ? nrows - q_lo : R;
             const uint32_t head = (wlo + (row0 + q_lo) * rb) & 15u;
             const uint8_t* slot = stage0 + s * stage_bytes + head;
-            uint32_t j = warp >= static_cast<int>(owner_base) ? warp - owner_base : warp + NCW - owner_base;
-            for (; j < n_here; j += NCW) {
-                const float v = q8k_row_dot<kType, kXReg>(op.nb, img, slot + j * rb, xw, xbs, xd, lane);
-                if (lane == 0) {
-                    y[q_lo + j] = v;
-                    if (px.world > 1) {
-                        // the same row into every peer's gather buffer (NVLink store)
-                        const size_t off = static_cast<size_t>(y + q_lo + j - px.local_base);
-#pragma unroll
-                        for (uint32_t p = 0; p < kMaxPeers; ++p)
-                            if (p < px.world && p != px.rank) px.peer_base[p][off] = v;
-                    }
+            const uint32_t n_tasks = (n_here + kPer - 1) / kPer;
+            uint32_t task = warp >= static_cast<int>(owner_base) ? warp - owner_base : warp + NCW - owner_base;
+            for (; task < n_tasks; task += NCW) {
+                const uint32_t ja = kPer * task;
+                const uint8_t* pa = slot + ja * rb;
+                if constexpr (kPer == 2) {
+                    const bool has_b = ja + 1 < n_here;
+                    const float v = q8k_row_dot2<kType, kXReg>(op.nb, img, pa, has_b ? pa + rb : pa, xw, xbs, xd, lane);
+                    if ((lane & 15) == 0 && (lane == 0 || has_b))  // lane 0: first row, lane 16: second
+                        program_store_row(px, y + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), v);
+                } else {
+                    const float v = q8k_row_dot<kType, kXReg, kUnroll>(op.nb, img, pa, xw, xbs, xd, lane);
+                    if (lane == 0) program_store_row(px, y + q_lo + ja, v);
                 }
             }
         }
@@ -222,7 +241,7 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
             s = 0;
             phase ^= 1u;
         }
-        owner_base += R % NCW;
+        owner_base += step;
         if (owner_base >= NCW) owner_base -= NCW;
     }
 }
@@ -373,7 +392,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
     double* scratch = reinterpret_cast<double*>(act + pp.act_bytes - 256);
     uint32_t jc = 0;  // image slots consumed
     for (uint32_t k = 0; k < pp.n_ops; ++k) {
-        const ProgramOp op = pp.ops[k];
+        // a reference into the parameter space: a register copy of the op
+        // would stay live through the row loops
+        const ProgramOp& op = pp.ops[k];
         if (pp.jit_slot_bytes != 0 && op.prebuilt && !failed) {
             // the producer copies this op's image into its slot ahead of time
             const bool ok = mbar_wait(&img_full[jc & 1u], (jc >> 1) & 1u, pp.status, 20);
@@ -413,17 +434,17 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             if (op.nb <= 16)
                 program_walk_op<NCW, 12, true>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                                pp.status, pp.px, warp, lane);
-            else
-                program_walk_op<NCW, 12, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
-                                                pp.status, pp.px, warp, lane);
+            else  // passes unrolled by two where the registers allow (not beside the Q6_K code)
+                program_walk_op<NCW, 12, false, kTypes == 3 ? 1 : 2>(op, act, stage0, pp.stage_bytes, S, full, empty, s,
+                                                                      phase, failed, pp.status, pp.px, warp, lane);
         } else if (kTypes == 4) {
             program_walk_op<NCW, 14, true>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                            pp.status, pp.px, warp, lane);
         } else {
             // in mixed programs Q6_K ops re-read their activation slice per pass: the
             // register-resident variant does not fit beside the Q4_K code in 128 registers
-            program_walk_op<NCW, 14, false>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
-                                            pp.status, pp.px, warp, lane);
+            program_walk_op<NCW, 14, false, kTypes == 2 ? 2 : 1>(op, act, stage0, pp.stage_bytes, S, full, empty, s,
+                                                                  phase, failed, pp.status, pp.px, warp, lane);
         }
         if (pp.jit_slot_bytes != 0 && op.prebuilt) {
             // this warp has left the slot
