@@ -986,10 +986,15 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         short_rows = short_rows && ops[k].base.cols <= 16 * 256;
     }
     if (types == 2 && short_rows) types = 4;
-    auto kernel = types == 1 ? matvec_program_kernel<kProgramWarps, 1>
-                  : types == 2 ? matvec_program_kernel<kProgramWarps, 2>
-                  : types == 4 ? matvec_program_kernel<kProgramWarps, 4>
-                               : matvec_program_kernel<kProgramWarps, 3>;
+    // the peer-group stores are compiled only into the row-sharded kernels
+    auto kernel = group ? (types == 1   ? matvec_program_kernel<kProgramWarps, 1, true>
+                           : types == 2 ? matvec_program_kernel<kProgramWarps, 2, true>
+                           : types == 4 ? matvec_program_kernel<kProgramWarps, 4, true>
+                                        : matvec_program_kernel<kProgramWarps, 3, true>)
+                        : (types == 1   ? matvec_program_kernel<kProgramWarps, 1>
+                           : types == 2 ? matvec_program_kernel<kProgramWarps, 2>
+                           : types == 4 ? matvec_program_kernel<kProgramWarps, 4>
+                                        : matvec_program_kernel<kProgramWarps, 3>);
     oracle_cuda_status st = launch(ctx, kernel, dim3(grid), dim3((kProgramWarps + 1) * 32), smem,
                                    static_cast<cudaStream_t>(stream), (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, pp);
     return st == ORACLE_CUDA_OK ? ok(ctx) : st;

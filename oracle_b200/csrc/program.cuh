@@ -173,9 +173,10 @@ __device__ __forceinline__ void push_to_peers(const PeerExchange& px, const floa
 // arrives on its `empty` barrier, so no warp ever waits two phases ahead.
 // One output row: into y here and, in a peer group, into every peer's gather
 // buffer at the same offset (NVLink store).
+template <bool kPeers>
 __device__ __forceinline__ void program_store_row(const PeerExchange& px, float* yr, float v) {
     *yr = v;
-    if (px.world > 1) {
+    if (kPeers && px.world > 1) {
         const size_t off = static_cast<size_t>(yr - px.local_base);
 #pragma unroll
         for (uint32_t p = 0; p < kMaxPeers; ++p)
@@ -183,7 +184,7 @@ __device__ __forceinline__ void program_store_row(const PeerExchange& px, float*
     }
 }
 
-template <int NCW, uint32_t kType, bool kXReg, int kUnroll = 1>
+template <int NCW, uint32_t kType, bool kXReg, int kUnroll, bool kPeers>
 __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* act, uint8_t* stage0,
                                                 uint32_t stage_bytes, uint32_t S, uint64_t* full, uint64_t* empty,
                                                 uint32_t& s, uint32_t& phase, bool& failed, DeviceStatus* status,
@@ -228,10 +229,10 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
                     const bool has_b = ja + 1 < n_here;
                     const float v = q8k_row_dot2<kType, kXReg>(op.nb, img, pa, has_b ? pa + rb : pa, xw, xbs, xd, lane);
                     if ((lane & 15) == 0 && (lane == 0 || has_b))  // lane 0: first row, lane 16: second
-                        program_store_row(px, y + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), v);
+                        program_store_row<kPeers>(px, y + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), v);
                 } else {
                     const float v = q8k_row_dot<kType, kXReg, kUnroll>(op.nb, img, pa, xw, xbs, xd, lane);
-                    if (lane == 0) program_store_row(px, y + q_lo + ja, v);
+                    if (lane == 0) program_store_row<kPeers>(px, y + q_lo + ja, v);
                 }
             }
         }
@@ -248,7 +249,9 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
 
 // kTypes: 1 = every op is q4_K, 2 = every op is q6_K, 3 = mixed, 4 = every op is
 // q6_K with at most 16 super-blocks per row (activation slice in registers).
-template <int kWarps, int kTypes>
+// kPeers: compiled with the peer-group stores (row-sharded programs); without
+// it every output row is a single predicated store.
+template <int kWarps, int kTypes, bool kPeers = false>
 __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(const __grid_constant__ ProgramParams pp) {
     constexpr int NCW = kWarps;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -432,18 +435,18 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
         static_assert(kTypes >= 1 && kTypes <= 4, "program type set");
         if (q4) {
             if (op.nb <= 16)
-                program_walk_op<NCW, 12, true>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
+                program_walk_op<NCW, 12, true, 1, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                                pp.status, pp.px, warp, lane);
             else  // passes unrolled by two where the registers allow (not beside the Q6_K code)
-                program_walk_op<NCW, 12, false, kTypes == 3 ? 1 : 2>(op, act, stage0, pp.stage_bytes, S, full, empty, s,
+                program_walk_op<NCW, 12, false, kTypes == 3 ? 1 : 2, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s,
                                                                       phase, failed, pp.status, pp.px, warp, lane);
         } else if (kTypes == 4) {
-            program_walk_op<NCW, 14, true>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
+            program_walk_op<NCW, 14, true, 1, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                            pp.status, pp.px, warp, lane);
         } else {
             // in mixed programs Q6_K ops re-read their activation slice per pass: the
             // register-resident variant does not fit beside the Q4_K code in 128 registers
-            program_walk_op<NCW, 14, false, kTypes == 2 ? 2 : 1>(op, act, stage0, pp.stage_bytes, S, full, empty, s,
+            program_walk_op<NCW, 14, false, kTypes == 2 ? 2 : 1, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s,
                                                                   phase, failed, pp.status, pp.px, warp, lane);
         }
         if (pp.jit_slot_bytes != 0 && op.prebuilt) {
