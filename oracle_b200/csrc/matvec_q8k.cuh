@@ -296,6 +296,70 @@ __device__ __forceinline__ float q8k_row_dot2(uint32_t nb, const ActImage& img, 
     return v;
 }
 
+// Pass `seg` of q8k_row_dot2 for two rows whose super-blocks 16 * seg .. are at
+// sega and segb (the segment's start): the activation slice of the segment
+// is fetched once for both rows, and the pass terms are added into the
+// rows' accumulators exactly as q8k_row_dot adds them (acc0 for even
+// passes, acc1 for odd).
+template <uint32_t kType>
+__device__ __forceinline__ void q8k_segment_pass2(uint32_t nb, const ActImage& img, uint32_t seg,
+                                                  const uint8_t* sega, const uint8_t* segb, int lane, float& a0,
+                                                  float& a1, float& b0, float& b1) {
+    constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
+    const int part = lane & 1;
+    const uint32_t j = static_cast<uint32_t>(lane) >> 1;
+    const uint32_t i = 16u * seg + j;
+    const bool active = i < nb;
+    int ia = 0, ma = 0, ib = 0, mb = 0;
+    float dwa = 0.0f, dmwa = 0.0f, dwb = 0.0f, dmwb = 0.0f, dx = 0.0f;
+    if (active) {
+        uint32_t w[32];
+        int bs[8];
+        fetch_lane_x<kType>(img, i, part, w, bs, dx);
+        const uint32_t off = j * kBlockBytes;
+        if (kType == 12) {
+            q4k_half_sums(sega + off, part, w, bs, ia, ma, dwa, dmwa);
+            q4k_half_sums(segb + off, part, w, bs, ib, mb, dwb, dmwb);
+        } else {
+            q6k_half_sums(sega + off, part, w, bs, ia, dwa);
+            q6k_half_sums(segb + off, part, w, bs, ib, dwb);
+        }
+    }
+    ia += __shfl_xor_sync(0xFFFFFFFFu, ia, 1);
+    ib += __shfl_xor_sync(0xFFFFFFFFu, ib, 1);
+    if (kType == 12) {
+        ma += __shfl_xor_sync(0xFFFFFFFFu, ma, 1);
+        mb += __shfl_xor_sync(0xFFFFFFFFu, mb, 1);
+    }
+    if (active) {
+        float pa = __fmul_rn(__fmul_rn(dwa, dx), __int2float_rn(ia));
+        float pb = __fmul_rn(__fmul_rn(dwb, dx), __int2float_rn(ib));
+        if (kType == 12) {
+            pa = __fsub_rn(pa, __fmul_rn(__fmul_rn(dmwa, dx), __int2float_rn(ma)));
+            pb = __fsub_rn(pb, __fmul_rn(__fmul_rn(dmwb, dx), __int2float_rn(mb)));
+        }
+        if (seg & 1u) {
+            a1 = __fadd_rn(a1, pa);
+            b1 = __fadd_rn(b1, pb);
+        } else {
+            a0 = __fadd_rn(a0, pa);
+            b0 = __fadd_rn(b0, pb);
+        }
+    }
+}
+
+// The end of q8k_row_dot2: each row's two accumulators added, the two
+// butterflies with their first level shared; row A's dot product on lane 0,
+// row B's on lane 16.
+__device__ __forceinline__ float q8k_fold2(float a0, float a1, float b0, float b1, int lane) {
+    const float va = __fadd_rn(a0, a1), vb = __fadd_rn(b0, b1);
+    const bool low = lane < 16;
+    float v = __fadd_rn(low ? va : vb, __shfl_xor_sync(0xFFFFFFFFu, low ? vb : va, 16));
+#pragma unroll
+    for (int off = 8; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+    return v;
+}
+
 // The lane's activation slice for register-resident rows (<= 16 super-blocks).
 template <uint32_t kType>
 __device__ __forceinline__ void load_lane_x(const ActImage& img, uint32_t nb, int lane, uint32_t (&xw)[32],

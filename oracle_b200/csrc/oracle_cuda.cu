@@ -914,12 +914,16 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         // small enough that kProgramMinStages stages fit beside the images
         uint64_t target = budget / kProgramMinStages;
         if (target > ctx->program_stage_target) target = ctx->program_stage_target;
+        // Q4_K rows of more than 16 super-blocks stream segment-major: a stage
+        // holds one 16-super-block segment of up to two rows per consumer warp
         for (uint32_t k = 0; k < n_ops; ++k) {
-            const uint64_t rb = pp.ops[k].row_bytes;
+            ProgramOp& p = pp.ops[k];
+            p.segmented = (p.type == kTypeQ4_K && p.nb > kSegmentBlocks) ? 1u : 0u;
+            const uint64_t rb = p.segmented ? uint64_t(kSegmentBlocks) * 144u : p.row_bytes;
             uint64_t R = target > 32 ? (target - 32) / rb : 0;
             if (R > uint64_t(2 * kProgramWarps)) R = 2 * kProgramWarps;
             if (R < 1) R = 1;
-            pp.ops[k].rows_per_stage = static_cast<uint32_t>(R);
+            p.rows_per_stage = static_cast<uint32_t>(R);
             const uint64_t sb = align_up(static_cast<uint32_t>(R * rb + 32), 128u);
             if (sb > stage) stage = sb;
         }

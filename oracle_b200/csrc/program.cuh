@@ -39,7 +39,16 @@ struct ProgramOp {
     uint32_t act_offset;      // byte offset of this op's activation image
     uint32_t prebuilt;        // 1: the image was built by quantize_images_kernel
     const float* residual;    // optional: y = residual + W.x (Oracle's add_vectors, qwen35_block.cpp:190-200)
+    // 1: rows of > 16 super-blocks stream segment-major (program_walk_segmented):
+    // the stages of a group of rows_per_stage rows hold 16-super-block segment
+    // 0 of every row of the group, then segment 1, ...
+    uint32_t segmented;
 };
+
+// Segment-major streaming: segment g of a row is super-blocks 16g .. 16g + 15,
+// kSegmentBytes apart in a stage (the last segment may be shorter).
+constexpr uint32_t kSegmentBlocks = 16;
+__host__ __device__ inline uint32_t program_segment_count(uint32_t nb) { return (nb + kSegmentBlocks - 1) / kSegmentBlocks; }
 
 // Per-op data read only at op boundaries (kept out of ProgramOp, whose copy
 // stays live through the row loop).
@@ -247,6 +256,57 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
     }
 }
 
+// Consumers of a segment-major op (rows of G > 1 segments, at most 2 * NCW rows
+// per group): warp w takes rows 2w, 2w + 1 of every group and walks the group's
+// G stages, adding each segment's pass terms into the rows' accumulators in
+// registers (q8k_segment_pass2: the segment's activation slice fetched once for
+// both rows), then folds them (q8k_fold2).  Bit-identical to q8k_row_dot: the
+// same terms reach the same accumulators in the same order.
+template <int NCW, uint32_t kType, bool kPeers>
+__device__ __forceinline__ void program_walk_segmented(const ProgramOp& op, uint8_t* act, uint8_t* stage0,
+                                                       uint32_t stage_bytes, uint32_t S, uint64_t* full,
+                                                       uint64_t* empty, uint32_t& s, uint32_t& phase, bool& failed,
+                                                       DeviceStatus* status, const PeerExchange& px, int warp,
+                                                       int lane) {
+    const ActImage img = q8k_image(act + op.act_offset, op.nb);
+    const uint32_t G = program_segment_count(op.nb);
+    const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
+    const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
+    const uint32_t nrows = static_cast<uint32_t>(r1 - r0);
+    const uint32_t R = op.rows_per_stage;
+    const uint32_t groups = (nrows + R - 1) / R;
+    const uint32_t ja = 2u * static_cast<uint32_t>(warp);
+    for (uint32_t q = 0; q < groups; ++q) {
+        const uint32_t q_lo = q * R;
+        const uint32_t n_here = nrows - q_lo < R ? nrows - q_lo : R;
+        const bool mine = ja < n_here;
+        const bool has_b = ja + 1 < n_here;
+        float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+        for (uint32_t sg = 0; sg < G; ++sg) {
+            if (!failed) {
+                const bool ok = mbar_wait(&full[s], phase, status, 14);
+                failed = !__all_sync(0xFFFFFFFFu, ok);
+            }
+            if (!failed && mine) {
+                const uint8_t* pa = stage0 + s * stage_bytes + ja * (kSegmentBlocks * 144u);
+                q8k_segment_pass2<kType>(op.nb, img, sg, pa, has_b ? pa + kSegmentBlocks * 144u : pa, lane, a0, a1,
+                                         b0, b1);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == S) {
+                s = 0;
+                phase ^= 1u;
+            }
+        }
+        if (!failed && mine) {
+            const float v = q8k_fold2(a0, a1, b0, b1, lane);
+            if ((lane & 15) == 0 && (lane == 0 || has_b))  // lane 0: first row, lane 16: second
+                program_store_row<kPeers>(px, op.y + r0 + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), v);
+        }
+    }
+}
+
 // kTypes: 1 = every op is q4_K, 2 = every op is q6_K, 3 = mixed, 4 = every op is
 // q6_K with at most 16 super-blocks per row (activation slice in registers).
 // kPeers: compiled with the peer-group stores (row-sharded programs); without
@@ -318,7 +378,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
             const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
             const uint32_t R = op.rows_per_stage;
-            const uint32_t T = static_cast<uint32_t>((r1 - r0 + R - 1) / R);
+            const uint32_t groups = static_cast<uint32_t>((r1 - r0 + R - 1) / R);
+            const uint32_t G = op.segmented ? program_segment_count(op.nb) : 1u;
+            const uint32_t T = groups * G;
             const uintptr_t wbase = reinterpret_cast<uintptr_t>(op.w);
             for (uint32_t t = 0; t < T; ++t, ++g) {
                 const uint32_t s = g % S;
@@ -336,6 +398,26 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                 if (!__shfl_sync(0xFFFFFFFFu, w_ok ? 1 : 0, 0)) {
                     ok = false;
                     break;
+                }
+                if (op.segmented) {
+                    // segment sg of rows lo .. hi - 1, one bulk copy per row
+                    // (Q4_K rows and segments are 16-byte multiples; the weight
+                    // pointer is 16-byte aligned)
+                    const uint32_t sg = t % G;
+                    const uint64_t lo = r0 + uint64_t(t / G) * R;
+                    const uint32_t n = static_cast<uint32_t>((lo + R < r1 ? lo + R : r1) - lo);
+                    const uint32_t nblk = op.nb - kSegmentBlocks * sg < kSegmentBlocks ? op.nb - kSegmentBlocks * sg
+                                                                                       : kSegmentBlocks;
+                    const uint32_t seg_bytes = nblk * 144u;
+                    uint8_t* dst = stage0 + size_t(s) * pp.stage_bytes;
+                    if (lane == 0) mbar_arrive_expect_tx(&full[s], n * seg_bytes);
+                    __syncwarp();
+                    if (static_cast<uint32_t>(lane) < n)
+                        bulk_copy_g2s(dst + lane * (kSegmentBlocks * 144u),
+                                      reinterpret_cast<const void*>(wbase + (lo + lane) * op.row_bytes +
+                                                                    sg * (kSegmentBlocks * 144u)),
+                                      seg_bytes, &full[s], policy);
+                    continue;
                 }
                 const uint64_t lo = r0 + uint64_t(t) * R;
                 const uint64_t hi = lo + R < r1 ? lo + R : r1;
@@ -437,6 +519,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             if (op.nb <= 16)
                 program_walk_op<NCW, 12, true, 1, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                                pp.status, pp.px, warp, lane);
+            else if (op.segmented)
+                program_walk_segmented<NCW, 12, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase,
+                                                        failed, pp.status, pp.px, warp, lane);
             else  // passes unrolled by two where the registers allow (not beside the Q6_K code)
                 program_walk_op<NCW, 12, false, kTypes == 3 ? 1 : 2, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s,
                                                                       phase, failed, pp.status, pp.px, warp, lane);
