@@ -90,13 +90,31 @@ __global__ void __launch_bounds__(256) attention_scores_pos_kernel(const float* 
     const uint32_t nw = gridDim.y * (blockDim.x >> 5);
     const uint32_t kvh = h / (q_heads / kv_heads);
     const float* qh = q + static_cast<uint64_t>(h) * key_dim;
-    for (uint32_t t = w; t < tokens; t += nw) {
-        const float* kt = keys + (static_cast<uint64_t>(t) * kv_heads + kvh) * key_dim;
-        double s = 0.0;
-        for (uint32_t d = lane; d < key_dim; d += 32)
-            s = __dadd_rn(s, __dmul_rn(static_cast<double>(qh[d]), static_cast<double>(kt[d])));
-        s = warp_sum_f64(s);
-        if (lane == 0) scores[static_cast<uint64_t>(h) * capacity + t] = __fmul_rn(__double2float_rn(s), scale);
+    // four of the warp's tokens at a time (their loads in flight together);
+    // each token's sum is the lane sums in dimension order, then warp_sum_f64
+    constexpr uint32_t kU = 4;
+    for (uint32_t t0 = w; t0 < tokens; t0 += kU * nw) {
+        double s[kU];
+#pragma unroll
+        for (uint32_t u = 0; u < kU; ++u) {
+            const uint32_t t = t0 + u * nw;
+            s[u] = 0.0;
+            if (t < tokens) {
+                const float* kt = keys + (static_cast<uint64_t>(t) * kv_heads + kvh) * key_dim;
+                for (uint32_t d = lane; d < key_dim; d += 32)
+                    s[u] = __dadd_rn(s[u], __dmul_rn(static_cast<double>(qh[d]), static_cast<double>(kt[d])));
+            }
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kU; ++u) s[u] = warp_sum_f64(s[u]);
+        if (lane == 0) {
+#pragma unroll
+            for (uint32_t u = 0; u < kU; ++u) {
+                const uint32_t t = t0 + u * nw;
+                if (t < tokens)
+                    scores[static_cast<uint64_t>(h) * capacity + t] = __fmul_rn(__double2float_rn(s[u]), scale);
+            }
+        }
     }
 }
 
@@ -135,6 +153,7 @@ __global__ void __launch_bounds__(256) attention_output_pos_kernel(float* __rest
     }
     for (uint32_t t = threadIdx.x; t < tokens; t += blockDim.x)
         sc[t] = __double2float_rn(__ddiv_rn(static_cast<double>(sc[t]), den));
+    if (!values) return;  // the weighted sum is attention_values_pos_kernel's
     __syncthreads();
     for (uint32_t d = threadIdx.x; d < value_dim; d += blockDim.x) {
         const float* vp = values + static_cast<uint64_t>(kvh) * value_dim + d;
@@ -145,6 +164,87 @@ __global__ void __launch_bounds__(256) attention_output_pos_kernel(float* __rest
         if (gate) acc = __fmul_rn(acc, ref_sigmoid(gate[static_cast<uint64_t>(h) * gate_stride + d]));
         out[static_cast<uint64_t>(h) * value_dim + d] = acc;
     }
+}
+
+// The weighted sum of the values for every query head of one KV head and a
+// kAttnDims-wide slice of the value dimensions: grid (kv_heads, value_dim /
+// kAttnDims), block (q_heads / kv_heads) * kAttnDims threads, thread (head hl,
+// dim dl).  Each thread adds p[t] * v[t] in token order in f32 (the order of
+// attention_output_pos_kernel's loop, bit for bit).  Chunks of kAttnChunk
+// positions of the value slice and of the group's probabilities are staged
+// in shared memory by asynchronous copies, two chunks in flight, so the
+// dependent chain reads shared memory while the next chunk loads.
+constexpr uint32_t kAttnDims = 16;
+constexpr uint32_t kAttnChunk = 256;
+__host__ __device__ constexpr uint32_t attn_values_smem_floats(uint32_t group) {
+    return 2u * kAttnChunk * (kAttnDims + group);
+}
+__global__ void __launch_bounds__(1024) attention_values_pos_kernel(const float* __restrict__ probs,
+                                                                    const float* __restrict__ values,
+                                                                    const uint32_t* __restrict__ pos,
+                                                                    uint32_t capacity, uint32_t q_heads,
+                                                                    uint32_t kv_heads, uint32_t value_dim,
+                                                                    const float* __restrict__ gate,
+                                                                    uint32_t gate_stride, float* __restrict__ out) {
+    pdl_enter();
+    extern __shared__ __align__(16) float attn_smem[];
+    if (*pos >= capacity) return;
+    const uint32_t tokens = *pos + 1;
+    const uint32_t group = q_heads / kv_heads;
+    const uint32_t kvh = blockIdx.x, d0 = blockIdx.y * kAttnDims;
+    const uint32_t hl = threadIdx.x / kAttnDims, dl = threadIdx.x % kAttnDims;
+    const uint32_t h = kvh * group + hl;
+    const uint32_t buf_floats = kAttnChunk * (kAttnDims + group);  // [kAttnChunk][kAttnDims], then [group][kAttnChunk]
+    const uint64_t vstride = static_cast<uint64_t>(kv_heads) * value_dim;
+    // probability rows may be copied 16 bytes at a time when every chunk start is
+    // 16-byte aligned; the rounded-up tail stays inside the row (capacity % 4 == 0)
+    const bool p16 = capacity % 4 == 0 && reinterpret_cast<uintptr_t>(probs) % 16 == 0;
+    auto stage = [&](uint32_t c0, uint32_t b) {
+        float* vs = attn_smem + b * buf_floats;
+        float* ps = vs + kAttnChunk * kAttnDims;
+        const uint32_t n = tokens - c0 < kAttnChunk ? tokens - c0 : kAttnChunk;
+        for (uint32_t i = threadIdx.x; i < n * (kAttnDims / 4); i += blockDim.x) {
+            const uint32_t t = i / (kAttnDims / 4), q4 = i % (kAttnDims / 4);
+            async_copy16(vs + 4 * i, values + (c0 + t) * vstride + static_cast<uint64_t>(kvh) * value_dim + d0 + 4 * q4);
+        }
+        if (p16) {
+            const uint32_t n4 = (n + 3) / 4;
+            for (uint32_t i = threadIdx.x; i < group * n4; i += blockDim.x) {
+                const uint32_t g = i / n4, t4 = i % n4;
+                async_copy16(ps + g * kAttnChunk + 4 * t4,
+                             probs + static_cast<uint64_t>(kvh * group + g) * capacity + c0 + 4 * t4);
+            }
+        } else {
+            for (uint32_t i = threadIdx.x; i < group * n; i += blockDim.x) {
+                const uint32_t g = i / n, t = i % n;
+                async_copy4(ps + g * kAttnChunk + t, probs + static_cast<uint64_t>(kvh * group + g) * capacity + c0 + t);
+            }
+        }
+        async_commit();
+    };
+    const uint32_t chunks = (tokens + kAttnChunk - 1) / kAttnChunk;
+    stage(0, 0);
+    float acc = 0.0f;
+    for (uint32_t c = 0; c < chunks; ++c) {
+        if (c + 1 < chunks) {
+            stage((c + 1) * kAttnChunk, (c + 1) & 1u);
+            async_wait<1>();
+        } else {
+            async_wait<0>();
+        }
+        __syncthreads();
+        const float* vs = attn_smem + (c & 1u) * buf_floats;
+        const float* pr = vs + kAttnChunk * kAttnDims + hl * kAttnChunk;
+        const uint32_t c0 = c * kAttnChunk;
+        const uint32_t n = tokens - c0 < kAttnChunk ? tokens - c0 : kAttnChunk;
+#pragma unroll 8
+        for (uint32_t t = 0; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(pr[t], vs[t * kAttnDims + dl]));
+        __syncthreads();  // the buffer is refilled by the stage after next
+    }
+    const uint32_t d = d0 + dl;
+    // the output gate, attention *= sigmoid(gate) (qwen35_block.cpp:738-742)
+    if (gate) acc = __fmul_rn(acc, ref_sigmoid(gate[static_cast<uint64_t>(h) * gate_stride + d]));
+    out[static_cast<uint64_t>(h) * value_dim + d] = acc;
 }
 
 __global__ void step_advance_kernel(uint32_t* pos) {

@@ -1921,6 +1921,30 @@ extern "C" oracle_cuda_status oracle_cuda_rope_at(oracle_cuda_context* ctx, floa
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
 
+namespace {
+// The probabilities (attention_output_pos_kernel with no values: max, exp,
+// double sum, normalisation, in place) then their weighted sum of the values
+// (attention_values_pos_kernel), or the single output kernel where the
+// shapes do not fit the staged kernel.
+oracle_cuda_status launch_attention_output(oracle_cuda_context* ctx, cudaStream_t st, bool pdl, float* scores,
+                                           const float* values, const uint32_t* pos, uint32_t cap,
+                                           uint32_t q_heads, uint32_t kv_heads, uint32_t value_dim,
+                                           const float* gate, uint32_t gate_stride, float* out) {
+    const uint32_t group = q_heads / kv_heads;
+    const bool staged = value_dim % kAttnDims == 0 && group * kAttnDims <= 1024 &&
+                        reinterpret_cast<uintptr_t>(values) % 16 == 0 &&
+                        attn_values_smem_floats(group) * sizeof(float) <= size_t(ctx->max_smem_optin);
+    oracle_cuda_status s = launch(ctx, attention_output_pos_kernel, dim3(q_heads), dim3(256), 0, st, pdl, scores,
+                                  staged ? static_cast<const float*>(nullptr) : values, pos, cap, q_heads, kv_heads,
+                                  value_dim, gate, gate_stride, out, ctx->status);
+    if (s != ORACLE_CUDA_OK || !staged) return s;
+    const size_t smem = size_t(attn_values_smem_floats(group)) * sizeof(float);
+    return launch(ctx, attention_values_pos_kernel, dim3(kv_heads, value_dim / kAttnDims), dim3(group * kAttnDims),
+                  smem, st, pdl, static_cast<const float*>(scores), values, pos, cap, q_heads, kv_heads, value_dim,
+                  gate, gate_stride, out);
+}
+}  // namespace
+
 extern "C" oracle_cuda_status oracle_cuda_attention_step_at(oracle_cuda_context* ctx, const float* q_dev,
                                                             const float* k_new_dev, const float* v_new_dev,
                                                             float* keys_dev, float* values_dev, uint64_t capacity,
@@ -1947,11 +1971,11 @@ extern "C" oracle_cuda_status oracle_cuda_attention_step_at(oracle_cuda_context*
     s = launch(ctx, attention_scores_pos_kernel, dim3(q_heads, chunks), dim3(256), 0, st, false, q_dev,
                static_cast<const float*>(keys_dev), pos_dev, cap, q_heads, kv_heads, key_dim, scale, scores_dev);
     if (s != ORACLE_CUDA_OK) return s;
-    s = launch(ctx, attention_output_pos_kernel, dim3(q_heads), dim3(256), 0, st, false, scores_dev,
-               static_cast<const float*>(values_dev), pos_dev, cap, q_heads, kv_heads, value_dim,
-               static_cast<const float*>(nullptr), 0u, out_dev, ctx->status);
+    s = launch_attention_output(ctx, st, false, scores_dev, values_dev, pos_dev, cap, q_heads, kv_heads, value_dim,
+                                nullptr, 0u, out_dev);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
+
 
 extern "C" oracle_cuda_status oracle_cuda_position_advance(oracle_cuda_context* ctx, uint32_t* pos_dev,
                                                            void* stream) {
@@ -2108,8 +2132,8 @@ extern "C" oracle_cuda_status oracle_cuda_attention_core_at(oracle_cuda_context*
     oracle_cuda_status s = launch(ctx, attention_scores_pos_kernel, dim3(q_heads, chunks), dim3(256), 0, st, pdl,
                                   q_dev, keys_dev, pos_dev, cap, q_heads, kv_heads, key_dim, scale, scores_dev);
     if (s != ORACLE_CUDA_OK) return s;
-    s = launch(ctx, attention_output_pos_kernel, dim3(q_heads), dim3(256), 0, st, pdl, scores_dev, values_dev,
-               pos_dev, cap, q_heads, kv_heads, value_dim, gate_dev, gate_stride, out_dev, ctx->status);
+    s = launch_attention_output(ctx, st, pdl, scores_dev, values_dev, pos_dev, cap, q_heads, kv_heads, value_dim,
+                                gate_dev, gate_stride, out_dev);
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
 

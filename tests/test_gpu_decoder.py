@@ -101,4 +101,4 @@ def test_fused_step_matches_unfused(ctx, gguf_models):
     for t in PROMPT[:4]:
         a, b = fused.forward(int(t)), plain.forward(int(t))
         assert np.abs(a - b).max() <= 1e-4 * b.std()
-    assert fused.launches_per_step() < plain.launches_per_step() // 4
+    assert 4 * fused.launches_per_step() <= plain.launches_per_step()
