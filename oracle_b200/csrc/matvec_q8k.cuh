@@ -348,6 +348,38 @@ __device__ __forceinline__ void q8k_segment_pass2(uint32_t nb, const ActImage& i
     }
 }
 
+// q8k_segment_pass2 for one row (where two rows' registers would spill).
+template <uint32_t kType>
+__device__ __forceinline__ void q8k_segment_pass1(uint32_t nb, const ActImage& img, uint32_t seg,
+                                                  const uint8_t* sega, int lane, float& a0, float& a1) {
+    constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
+    const int part = lane & 1;
+    const uint32_t j = static_cast<uint32_t>(lane) >> 1;
+    const uint32_t i = 16u * seg + j;
+    const bool active = i < nb;
+    int ia = 0, ma = 0;
+    float dwa = 0.0f, dmwa = 0.0f, dx = 0.0f;
+    if (active) {
+        uint32_t w[32];
+        int bs[8];
+        fetch_lane_x<kType>(img, i, part, w, bs, dx);
+        if (kType == 12)
+            q4k_half_sums(sega + j * kBlockBytes, part, w, bs, ia, ma, dwa, dmwa);
+        else
+            q6k_half_sums(sega + j * kBlockBytes, part, w, bs, ia, dwa);
+    }
+    ia += __shfl_xor_sync(0xFFFFFFFFu, ia, 1);
+    if (kType == 12) ma += __shfl_xor_sync(0xFFFFFFFFu, ma, 1);
+    if (active) {
+        float pa = __fmul_rn(__fmul_rn(dwa, dx), __int2float_rn(ia));
+        if (kType == 12) pa = __fsub_rn(pa, __fmul_rn(__fmul_rn(dmwa, dx), __int2float_rn(ma)));
+        if (seg & 1u)
+            a1 = __fadd_rn(a1, pa);
+        else
+            a0 = __fadd_rn(a0, pa);
+    }
+}
+
 // The end of q8k_row_dot2: each row's two accumulators added, the two
 // butterflies with their first level shared; row A's dot product on lane 0,
 // row B's on lane 16.

@@ -918,10 +918,18 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         // holds one 16-super-block segment of up to two rows per consumer warp
         for (uint32_t k = 0; k < n_ops; ++k) {
             ProgramOp& p = pp.ops[k];
-            p.segmented = (p.type == kTypeQ4_K && p.nb > kSegmentBlocks) ? 1u : 0u;
-            const uint64_t rb = p.segmented ? uint64_t(kSegmentBlocks) * 144u : p.row_bytes;
+            // Q6_K: every segment a 16-byte multiple (nb % 8 == 0) from a
+            // 16-byte aligned weight pointer (bulk copies), one row per warp
+            const bool q6 = p.type == kTypeQ6_K;
+            p.segmented = (p.nb > kSegmentBlocks &&
+                           (p.type == kTypeQ4_K ||
+                            (q6 && p.nb % 8 == 0 && reinterpret_cast<uintptr_t>(p.w) % 16 == 0)))
+                              ? 1u
+                              : 0u;
+            const uint64_t rb = p.segmented ? uint64_t(kSegmentBlocks) * (q6 ? 210u : 144u) : p.row_bytes;
             uint64_t R = target > 32 ? (target - 32) / rb : 0;
-            if (R > uint64_t(2 * kProgramWarps)) R = 2 * kProgramWarps;
+            const uint64_t cap = (p.segmented && q6) ? kProgramWarps : 2 * kProgramWarps;
+            if (R > cap) R = cap;
             if (R < 1) R = 1;
             p.rows_per_stage = static_cast<uint32_t>(R);
             const uint64_t sb = align_up(static_cast<uint32_t>(R * rb + 32), 128u);

@@ -256,12 +256,14 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
     }
 }
 
-// Consumers of a segment-major op (rows of G > 1 segments, at most 2 * NCW rows
-// per group): warp w takes rows 2w, 2w + 1 of every group and walks the group's
-// G stages, adding each segment's pass terms into the rows' accumulators in
-// registers (q8k_segment_pass2: the segment's activation slice fetched once for
-// both rows), then folds them (q8k_fold2).  Bit-identical to q8k_row_dot: the
-// same terms reach the same accumulators in the same order.
+// Consumers of a segment-major op (rows of G > 1 segments): for Q4_K (at most
+// 2 * NCW rows per group) warp w takes rows 2w, 2w + 1 of every group, for
+// Q6_K (at most NCW rows) row w, and walks the group's G stages, adding each
+// segment's pass terms into the rows' accumulators in registers
+// (q8k_segment_pass2: the segment's activation slice fetched once for both
+// rows; q8k_segment_pass1), then folds them (q8k_fold2 / the butterfly of
+// q8k_row_dot).  Bit-identical to q8k_row_dot: the same terms reach the same
+// accumulators in the same order.
 template <int NCW, uint32_t kType, bool kPeers>
 __device__ __forceinline__ void program_walk_segmented(const ProgramOp& op, uint8_t* act, uint8_t* stage0,
                                                        uint32_t stage_bytes, uint32_t S, uint64_t* full,
@@ -275,12 +277,14 @@ __device__ __forceinline__ void program_walk_segmented(const ProgramOp& op, uint
     const uint32_t nrows = static_cast<uint32_t>(r1 - r0);
     const uint32_t R = op.rows_per_stage;
     const uint32_t groups = (nrows + R - 1) / R;
-    const uint32_t ja = 2u * static_cast<uint32_t>(warp);
+    constexpr uint32_t kPer = kType == 12 ? 2u : 1u;  // rows per warp
+    constexpr uint32_t kSeg = kSegmentBlocks * (kType == 12 ? 144u : 210u);
+    const uint32_t ja = kPer * static_cast<uint32_t>(warp);
     for (uint32_t q = 0; q < groups; ++q) {
         const uint32_t q_lo = q * R;
         const uint32_t n_here = nrows - q_lo < R ? nrows - q_lo : R;
         const bool mine = ja < n_here;
-        const bool has_b = ja + 1 < n_here;
+        const bool has_b = kPer == 2 && ja + 1 < n_here;
         float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
         for (uint32_t sg = 0; sg < G; ++sg) {
             if (!failed) {
@@ -288,9 +292,11 @@ __device__ __forceinline__ void program_walk_segmented(const ProgramOp& op, uint
                 failed = !__all_sync(0xFFFFFFFFu, ok);
             }
             if (!failed && mine) {
-                const uint8_t* pa = stage0 + s * stage_bytes + ja * (kSegmentBlocks * 144u);
-                q8k_segment_pass2<kType>(op.nb, img, sg, pa, has_b ? pa + kSegmentBlocks * 144u : pa, lane, a0, a1,
-                                         b0, b1);
+                const uint8_t* pa = stage0 + s * stage_bytes + ja * kSeg;
+                if constexpr (kPer == 2)
+                    q8k_segment_pass2<kType>(op.nb, img, sg, pa, has_b ? pa + kSeg : pa, lane, a0, a1, b0, b1);
+                else
+                    q8k_segment_pass1<kType>(op.nb, img, sg, pa, lane, a0, a1);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -300,9 +306,16 @@ __device__ __forceinline__ void program_walk_segmented(const ProgramOp& op, uint
             }
         }
         if (!failed && mine) {
-            const float v = q8k_fold2(a0, a1, b0, b1, lane);
-            if ((lane & 15) == 0 && (lane == 0 || has_b))  // lane 0: first row, lane 16: second
-                program_store_row<kPeers>(px, op.y + r0 + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), v);
+            if constexpr (kPer == 2) {
+                const float v = q8k_fold2(a0, a1, b0, b1, lane);
+                if ((lane & 15) == 0 && (lane == 0 || has_b))  // lane 0: first row, lane 16: second
+                    program_store_row<kPeers>(px, op.y + r0 + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), v);
+            } else {
+                float v = __fadd_rn(a0, a1);
+#pragma unroll
+                for (int off = 16; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+                if (lane == 0) program_store_row<kPeers>(px, op.y + r0 + q_lo + ja, v);
+            }
         }
     }
 }
@@ -401,21 +414,22 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                 }
                 if (op.segmented) {
                     // segment sg of rows lo .. hi - 1, one bulk copy per row
-                    // (Q4_K rows and segments are 16-byte multiples; the weight
-                    // pointer is 16-byte aligned)
+                    // (rows and segments are 16-byte multiples and the weight
+                    // pointer is 16-byte aligned: checked by the host)
                     const uint32_t sg = t % G;
                     const uint64_t lo = r0 + uint64_t(t / G) * R;
                     const uint32_t n = static_cast<uint32_t>((lo + R < r1 ? lo + R : r1) - lo);
                     const uint32_t nblk = op.nb - kSegmentBlocks * sg < kSegmentBlocks ? op.nb - kSegmentBlocks * sg
                                                                                        : kSegmentBlocks;
-                    const uint32_t seg_bytes = nblk * 144u;
+                    const uint32_t bb = op.type == 12 ? 144u : 210u;
+                    const uint32_t seg_bytes = nblk * bb;
                     uint8_t* dst = stage0 + size_t(s) * pp.stage_bytes;
                     if (lane == 0) mbar_arrive_expect_tx(&full[s], n * seg_bytes);
                     __syncwarp();
                     if (static_cast<uint32_t>(lane) < n)
-                        bulk_copy_g2s(dst + lane * (kSegmentBlocks * 144u),
+                        bulk_copy_g2s(dst + lane * (kSegmentBlocks * bb),
                                       reinterpret_cast<const void*>(wbase + (lo + lane) * op.row_bytes +
-                                                                    sg * (kSegmentBlocks * 144u)),
+                                                                    sg * (kSegmentBlocks * bb)),
                                       seg_bytes, &full[s], policy);
                     continue;
                 }
@@ -525,6 +539,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             else  // passes unrolled by two where the registers allow (not beside the Q6_K code)
                 program_walk_op<NCW, 12, false, kTypes == 3 ? 1 : 2, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s,
                                                                       phase, failed, pp.status, pp.px, warp, lane);
+        } else if (op.segmented) {
+            program_walk_segmented<NCW, 14, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
+                                                    pp.status, pp.px, warp, lane);
         } else if (kTypes == 4) {
             program_walk_op<NCW, 14, true, 1, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                            pp.status, pp.px, warp, lane);

@@ -366,7 +366,11 @@ def test_program_q6k_only(ctx, port, specs):
     [(ob.TYPE_Q4_K, 160, 136 * 256, 0)],
     [(ob.TYPE_Q4_K, 211, 112 * 256, 0), (ob.TYPE_Q4_K, 90, 40 * 256, 0)],
     [(ob.TYPE_Q4_K, 5000, 4096, 0), (ob.TYPE_Q4_K, 700, 19 * 256, 1), (ob.TYPE_Q4_K, 4864, 700 - 700 % 256, 1)],
-    [(ob.TYPE_Q6_K, 400, 4096, 0), (ob.TYPE_Q4_K, 611, 12288, 0), (ob.TYPE_Q6_K, 99, 12288, 0)]])   # mixed
+    [(ob.TYPE_Q6_K, 400, 4096, 0), (ob.TYPE_Q4_K, 611, 12288, 0), (ob.TYPE_Q6_K, 99, 12288, 0)],   # mixed
+    # Q6_K long rows: segment-major when every segment is a 16-byte multiple
+    # (48 and 40 super-blocks), row by row otherwise (20)
+    [(ob.TYPE_Q6_K, 333, 48 * 256, 0), (ob.TYPE_Q6_K, 57, 40 * 256, 0), (ob.TYPE_Q6_K, 50, 20 * 256, 0),
+     (ob.TYPE_Q6_K, 29, 4096, 0)]])
 def test_program_long_rows(ctx, port, specs):
     """Rows longer than 16 super-blocks (several passes over the activation
     image per row), bit-identical to the restatement."""
