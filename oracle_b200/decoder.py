@@ -67,7 +67,7 @@ class Qwen35Decoder:
 
     def __init__(self, ctx: Context, cfg: Qwen35Config, tensors, contract: str = "q8k",
                  capacity: int | None = None, max_new: int = 4096, device: int = 0, fused: bool = True,
-                 rank: int = 0, world: int = 1, exchange=None, build_in_kernel: bool = False):
+                 rank: int = 0, world: int = 1, exchange=None, build_in_kernel: bool = True):
         import torch
 
         if contract not in ("q8k", "f32"):
