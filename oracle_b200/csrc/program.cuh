@@ -517,14 +517,47 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             const ActSource a{op.x, e.x2, e.norm, e.eps, e.xform};
             float inv = 0.0f;
             if (e.xform == kXformRms) {
-                // the whole vector's sum of squares, reduced over the consumer warps
+                // The warp's first block of x and of the norm weights is loaded
+                // first, in flight with the sum of squares' loads; every block is
+                // scaled, quantized and stored exactly as quantize_xform_to_image
+                // does (the later blocks after the sum).
                 const uint32_t n = op.nb * 256u;
+                const uint32_t i0 = warp;
+                float v0[8], w0[8];
+                if (!failed && i0 < op.nb) {
+                    load_lane8(op.x + 256ull * i0, lane, aligned16(op.x + 256ull * i0), v0);
+                    load_lane8(e.norm + 256ull * i0, lane, aligned16(e.norm + 256ull * i0), w0);
+                }
                 const double part = warp_sum_f64(failed ? 0.0 : sum_squares_f64(op.x, warp * 32 + lane, n, NCW * 32));
                 if (lane == 0) scratch[warp] = part;
                 named_barrier_sync(1, NCW * 32);
                 inv = rms_inverse(warp_sum_f64(lane < NCW ? scratch[lane] : 0.0), n, e.eps);
+                const ActImage img = q8k_image(act + op.act_offset, op.nb);
+                if (!failed && i0 < op.nb) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v0[j] = __fmul_rn(__fmul_rn(v0[j], inv), w0[j]);
+                    const Q8KLane r = quantize_q8k_lane_values(v0, lane);
+                    store_block_to_image(img, i0, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
+                }
+                for (uint32_t i = i0 + NCW; !failed && i < op.nb; i += NCW) {
+                    float v[8];
+                    load_lane8_xform(a, i, lane, inv, v);
+                    const Q8KLane r = quantize_q8k_lane_values(v, lane);
+                    store_block_to_image(img, i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
+                }
+            } else {
+                if (e.xform == kXformRms) {
+                    // the whole vector's sum of squares, reduced over the consumer warps
+                    const uint32_t n = op.nb * 256u;
+                    const double part =
+                        warp_sum_f64(failed ? 0.0 : sum_squares_f64(op.x, warp * 32 + lane, n, NCW * 32));
+                    if (lane == 0) scratch[warp] = part;
+                    named_barrier_sync(1, NCW * 32);
+                    inv = rms_inverse(warp_sum_f64(lane < NCW ? scratch[lane] : 0.0), n, e.eps);
+                }
+                if (!failed)
+                    quantize_xform_to_image(a, op.nb, inv, q8k_image(act + op.act_offset, op.nb), warp, NCW, lane);
             }
-            if (!failed) quantize_xform_to_image(a, op.nb, inv, q8k_image(act + op.act_offset, op.nb), warp, NCW, lane);
             named_barrier_sync(1, NCW * 32);
         }
         const bool q4 = kTypes == 1 || (kTypes == 3 && op.type == 12);

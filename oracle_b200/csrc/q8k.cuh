@@ -237,14 +237,14 @@ __device__ __forceinline__ double sum_squares_f64(const float* __restrict__ x, u
                                                   uint32_t stride) {
     double s = 0.0;
     uint32_t c = first;
-    // four loads in flight per round; the additions keep the element order
-    for (; c + 3 * stride < n; c += 4 * stride) {
-        const double a = __ldcg(x + c), b = __ldcg(x + c + stride);
-        const double e = __ldcg(x + c + 2 * stride), f = __ldcg(x + c + 3 * stride);
-        s = __dadd_rn(s, __dmul_rn(a, a));
-        s = __dadd_rn(s, __dmul_rn(b, b));
-        s = __dadd_rn(s, __dmul_rn(e, e));
-        s = __dadd_rn(s, __dmul_rn(f, f));
+    // eight loads in flight per round; the additions keep the element order
+    constexpr uint32_t kB = 8;
+    for (; c + (kB - 1) * stride < n; c += kB * stride) {
+        float v[kB];
+#pragma unroll
+        for (uint32_t u = 0; u < kB; ++u) v[u] = __ldcg(x + c + u * stride);
+#pragma unroll
+        for (uint32_t u = 0; u < kB; ++u) s = __dadd_rn(s, __dmul_rn(static_cast<double>(v[u]), static_cast<double>(v[u])));
     }
     for (; c < n; c += stride) {
         const double v = static_cast<double>(__ldcg(x + c));
