@@ -23,6 +23,7 @@
 #include "gather.cuh"
 #include "gemm_q4k.cuh"
 #include "layout.hpp"
+#include "matvec_q80_lane.cuh"
 #include "matvec_seq.cuh"
 #include "matvec_q8k.cuh"
 #include "program.cuh"
@@ -264,8 +265,14 @@ oracle_cuda_status launch_q8k(oracle_cuda_context* ctx, uint32_t type, const voi
     return launch_q8k_typed<14>(ctx, wb, rows, row_bytes, cp, stream);
 }
 
+oracle_cuda_status launch_q80_lane(oracle_cuda_context* ctx, const MatvecSeqParams& sp, cudaStream_t stream);
+bool q80_lane_fits(const MatvecSeqParams& sp);
+
 template <uint32_t kType, uint32_t kBatch>
 oracle_cuda_status launch_seq_batch(oracle_cuda_context* ctx, MatvecSeqParams sp, cudaStream_t stream) {
+    // Q8_0 vectors one at a time: lane-per-row kernel (same operations, same order)
+    if constexpr (kType == 8 && kBatch == 1)
+        if (q80_lane_fits(sp)) return launch_q80_lane(ctx, sp, stream);
     const uint64_t grid = (sp.rows + kSeqRows - 1) / kSeqRows;
     if (grid > 0x7FFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "too many rows for one launch");
     const uint64_t budget = ctx->smem_budget ? ctx->smem_budget : uint64_t(ctx->max_smem_optin);
@@ -1450,6 +1457,31 @@ EncodeTiledFn encode_tiled() {
             fn = reinterpret_cast<EncodeTiledFn>(p);
     });
     return fn;
+}
+
+bool q80_lane_fits(const MatvecSeqParams& sp) {
+    return sp.k % kQ80ChunkElems == 0 && sp.rows > 0 && sp.rows <= 0x7FFFFFFFull &&
+           reinterpret_cast<uintptr_t>(sp.w) % 16 == 0 && reinterpret_cast<uintptr_t>(sp.x) % 16 == 0 &&
+           sp.row_bytes == uint64_t(sp.k) / 32u * 34u;
+}
+
+oracle_cuda_status launch_q80_lane(oracle_cuda_context* ctx, const MatvecSeqParams& sp, cudaStream_t stream) {
+    const EncodeTiledFn encode = encode_tiled();
+    if (!encode) return fail(ctx, ORACLE_CUDA_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
+    CUtensorMap tw{};
+    // the rows as 2-byte elements (Q8_0 blocks are 34 bytes): a box of 136 x 32
+    // is 8 blocks of 32 rows, 272 bytes per row (a multiple of 16)
+    const cuuint64_t dims[2] = {sp.row_bytes / 2, sp.rows};
+    const cuuint64_t strides[1] = {sp.row_bytes};
+    const cuuint32_t box[2] = {kQ80ChunkBytes / 2, kQ80LaneRows};
+    const cuuint32_t estr[2] = {1, 1};
+    if (encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(sp.w), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return fail(ctx, ORACLE_CUDA_CUDA_ERROR, "tensor map for the Q8_0 rows rejected");
+    const uint32_t grid = static_cast<uint32_t>((sp.rows + kQ80LaneRows - 1) / kQ80LaneRows);
+    return launch(ctx, matvec_q80_lane_kernel, dim3(grid), dim3(32), q80_lane_smem_bytes(), stream, false, tw, sp.x,
+                  sp.y, static_cast<uint32_t>(sp.rows), sp.k, ctx->status);
 }
 
 // Columns per split of K: halve while the grid is at most half the SMs and

@@ -146,7 +146,10 @@ def test_config3_lm_head_q6k(ctx, port):
 # ---------------------------------------------------------------- Oracle's f32 contract
 
 @pytest.mark.parametrize("qtype,rows,k", [
-    (ob.TYPE_Q8_0, 4096, 4096), (ob.TYPE_Q8_0, 5, 32), (ob.TYPE_Q8_0, 19, 160),
+    # Q8_0 with K % 256 == 0: the lane-per-row kernel (one chunk, ragged row
+    # counts, several passes over the stage ring); other K: the producer kernel
+    (ob.TYPE_Q8_0, 4096, 4096), (ob.TYPE_Q8_0, 33, 256), (ob.TYPE_Q8_0, 100, 2304),
+    (ob.TYPE_Q8_0, 5, 32), (ob.TYPE_Q8_0, 19, 160),
     (ob.TYPE_Q4_K, 33, 4096), (ob.TYPE_Q5_K, 21, 1024), (ob.TYPE_Q6_K, 45, 4096),
     (ob.TYPE_F16, 6, 37), (ob.TYPE_BF16, 6, 300), (ob.TYPE_F32, 7, 129)])
 def test_f32_contract(ctx, port, qtype, rows, k):
