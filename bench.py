@@ -642,7 +642,7 @@ def gpu_arm(args, wl: Workload) -> None:
     cpu = cpu_baseline_leg(wl) if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         kernel = ("matvec_program_kernel" if wl.program else
-                  "matvec_q80_lane_kernel (lane per row, sequential f32)" if wl.contract == CONTRACT_F32 else
+                  "matvec_q80_split_kernel (lane per row, sequential f32)" if wl.contract == CONTRACT_F32 else
                   "stream_rows_kernel<MatvecQ8KConsumer>")
         line = {"metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps_timed,
                 "warmup": args.warmup, "ms_per_step": ms / steps_timed, "higher_is_better": True,

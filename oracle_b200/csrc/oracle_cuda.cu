@@ -1480,7 +1480,8 @@ oracle_cuda_status launch_q80_lane(oracle_cuda_context* ctx, const MatvecSeqPara
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return fail(ctx, ORACLE_CUDA_CUDA_ERROR, "tensor map for the Q8_0 rows rejected");
     const uint32_t grid = static_cast<uint32_t>((sp.rows + kQ80LaneRows - 1) / kQ80LaneRows);
-    return launch(ctx, matvec_q80_lane_kernel, dim3(grid), dim3(32), q80_lane_smem_bytes(), stream, false, tw, sp.x,
+    return launch(ctx, matvec_q80_split_kernel, dim3(grid), dim3(32 * (1 + kQ80ProdWarps)), q80_split_smem_bytes(),
+                  stream, false, tw, sp.x,
                   sp.y, static_cast<uint32_t>(sp.rows), sp.k, ctx->status);
 }
 
