@@ -42,6 +42,68 @@ __host__ __device__ constexpr uint32_t q80_split_smem_bytes() {
     return kQ80Stages * kQ80StageBytes + kQ80ProdStages * kQ80ProdBytes + (2 * kQ80Stages + 2 * kQ80ProdStages) * 8u;
 }
 
+// The 9 words of block b of a lane's 272-byte chunk row, (34 b) / 4 .. + 8, from
+// three aligned 16-byte loads (rows 272 bytes apart put 4-byte loads of lanes
+// l, l + 8, l + 16, l + 24 on one bank; 16-byte loads take the minimum 4
+// wavefronts anyway).
+template <uint32_t kB>
+__device__ __forceinline__ void q80_block_words(const uint4* row4, uint32_t (&w)[9]) {
+    constexpr uint32_t w0 = (34u * kB) / 4u, q0 = w0 / 4u, o = w0 % 4u;
+    uint32_t u[12];
+#pragma unroll
+    for (uint32_t v = 0; v < 3; ++v) {
+        const uint4 t = row4[q0 + v];
+        u[4 * v + 0] = t.x;
+        u[4 * v + 1] = t.y;
+        u[4 * v + 2] = t.z;
+        u[4 * v + 3] = t.w;
+    }
+#pragma unroll
+    for (uint32_t i = 0; i < 9; ++i) w[i] = u[o + i];
+}
+
+// Product warp kP's blocks b = kP, kP + 2, ... of one chunk: d in the low (b
+// even) or high (b odd) half of word 0, quant word t the funnel of words t,
+// t + 1 (b even) or word t + 1 (b odd) -- the words ld_u32_even<true> reads;
+// each product d * q * x rounded as decode4<8> and matvec_seq do; the next
+// block's words and x loaded while this one computes.
+template <uint32_t kP, uint32_t kJ = 0>
+__device__ __forceinline__ void q80_products_from(const uint4* row4, const float4* x4, float4* po,
+                                                  const uint32_t (&wa)[9], const float4 (&xa)[8]) {
+    constexpr uint32_t b = kP + kQ80ProdWarps * kJ;
+    constexpr bool kLast = kJ + 1 == kQ80ChunkBlocks / kQ80ProdWarps;
+    uint32_t wn[9];
+    float4 xn[8];
+    if constexpr (!kLast) {
+        q80_block_words<b + kQ80ProdWarps>(row4, wn);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xn[i] = x4[8 * (b + kQ80ProdWarps) + i];
+    }
+    constexpr bool odd = (b & 1u) != 0;
+    const float d = f16_bits_to_f32(static_cast<uint16_t>(odd ? (wa[0] >> 16) : (wa[0] & 0xFFFFu)));
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        const uint32_t qw = (odd ? wa[t + 1] : __funnelshift_r(wa[t], wa[t + 1], 16)) ^ 0x80808080u;
+        float4 o;
+        o.x = __fmul_rn(__fmul_rn(d, __fsub_rn(small_uint_to_f32(qw, 0), 8388736.0f)), xa[t].x);
+        o.y = __fmul_rn(__fmul_rn(d, __fsub_rn(small_uint_to_f32(qw, 1), 8388736.0f)), xa[t].y);
+        o.z = __fmul_rn(__fmul_rn(d, __fsub_rn(small_uint_to_f32(qw, 2), 8388736.0f)), xa[t].z);
+        o.w = __fmul_rn(__fmul_rn(d, __fsub_rn(small_uint_to_f32(qw, 3), 8388736.0f)), xa[t].w);
+        po[8 * b + t] = o;
+    }
+    if constexpr (!kLast) q80_products_from<kP, kJ + 1>(row4, x4, po, wn, xn);
+}
+
+template <uint32_t kP>
+__device__ __forceinline__ void q80_products(const uint4* row4, const float4* x4, float4* po) {
+    uint32_t wa[9];
+    float4 xa[8];
+    q80_block_words<kP>(row4, wa);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xa[i] = x4[8 * kP + i];
+    q80_products_from<kP>(row4, x4, po, wa, xa);
+}
+
 __global__ void __launch_bounds__(32 * (1 + kQ80ProdWarps)) matvec_q80_split_kernel(const __grid_constant__ CUtensorMap wmap,
                                                               const float* __restrict__ x, float* __restrict__ y,
                                                               uint32_t rows, uint32_t k, DeviceStatus* st) {
@@ -121,49 +183,10 @@ __global__ void __launch_bounds__(32 * (1 + kQ80ProdWarps)) matvec_q80_split_ker
         const uint32_t* rw = reinterpret_cast<const uint32_t*>(q80_smem + s * kQ80StageBytes + lane * kQ80ChunkBytes);
         const float4* x4 = reinterpret_cast<const float4*>(q80_smem + s * kQ80StageBytes + kQ80LaneRows * kQ80ChunkBytes);
         float4* po = reinterpret_cast<float4*>(prod + ps * (kQ80LaneRows * kQ80ProdStride) + lane * kQ80ProdStride);
-        // this warp's blocks b = p + kQ80ProdWarps j: words (34 b) / 4 .. + 8 and x, one block ahead
-        uint32_t wa[9];
-        float4 xa[8];
-        {
-            const uint32_t w0 = (34u * p) / 4u;
-#pragma unroll
-            for (int i = 0; i < 9; ++i) wa[i] = rw[w0 + i];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) xa[i] = x4[8 * p + i];
-        }
-#pragma unroll
-        for (uint32_t j = 0; j < kQ80ChunkBlocks / kQ80ProdWarps; ++j) {
-            const uint32_t b = p + kQ80ProdWarps * j;
-            uint32_t wn[9];
-            float4 xn[8];
-            if (j + 1 < kQ80ChunkBlocks / kQ80ProdWarps) {
-                const uint32_t w1 = (34u * (b + kQ80ProdWarps)) / 4u;
-#pragma unroll
-                for (int i = 0; i < 9; ++i) wn[i] = rw[w1 + i];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) xn[i] = x4[8 * (b + kQ80ProdWarps) + i];
-            }
-            // b's parity is p's (kQ80ProdWarps is even): d in the low (even) or
-            // high (odd) half of word 0
-            const bool odd = (p & 1u) != 0;
-            const float d = f16_bits_to_f32(static_cast<uint16_t>(odd ? (wa[0] >> 16) : (wa[0] & 0xFFFFu)));
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const uint32_t qw = (odd ? wa[t + 1] : __funnelshift_r(wa[t], wa[t + 1], 16)) ^ 0x80808080u;
-                float4 o;
-                o.x = __fmul_rn(__fmul_rn(d, __fsub_rn(small_uint_to_f32(qw, 0), 8388736.0f)), xa[t].x);
-                o.y = __fmul_rn(__fmul_rn(d, __fsub_rn(small_uint_to_f32(qw, 1), 8388736.0f)), xa[t].y);
-                o.z = __fmul_rn(__fmul_rn(d, __fsub_rn(small_uint_to_f32(qw, 2), 8388736.0f)), xa[t].z);
-                o.w = __fmul_rn(__fmul_rn(d, __fsub_rn(small_uint_to_f32(qw, 3), 8388736.0f)), xa[t].w);
-                po[8 * b + t] = o;
-            }
-            if (j + 1 < kQ80ChunkBlocks / kQ80ProdWarps) {
-#pragma unroll
-                for (int i = 0; i < 9; ++i) wa[i] = wn[i];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) xa[i] = xn[i];
-            }
-        }
+        if (p == 0)
+            q80_products<0>(reinterpret_cast<const uint4*>(rw), x4, po);
+        else
+            q80_products<1>(reinterpret_cast<const uint4*>(rw), x4, po);
         mbar_arrive(&prod_full[ps]);  // this lane's products of chunk c are written
         mbar_arrive(&raw_empty[s]);   // ... and it has left weight stage s
         if (issuer && issued < chunks) {
