@@ -265,14 +265,14 @@ oracle_cuda_status launch_q8k(oracle_cuda_context* ctx, uint32_t type, const voi
     return launch_q8k_typed<14>(ctx, wb, rows, row_bytes, cp, stream);
 }
 
-oracle_cuda_status launch_q80_lane(oracle_cuda_context* ctx, const MatvecSeqParams& sp, cudaStream_t stream);
-bool q80_lane_fits(const MatvecSeqParams& sp);
+oracle_cuda_status launch_q80_split(oracle_cuda_context* ctx, const MatvecSeqParams& sp, cudaStream_t stream);
+bool q80_split_fits(const MatvecSeqParams& sp);
 
 template <uint32_t kType, uint32_t kBatch>
 oracle_cuda_status launch_seq_batch(oracle_cuda_context* ctx, MatvecSeqParams sp, cudaStream_t stream) {
     // Q8_0 vectors one at a time: lane-per-row kernel (same operations, same order)
     if constexpr (kType == 8 && kBatch == 1)
-        if (q80_lane_fits(sp)) return launch_q80_lane(ctx, sp, stream);
+        if (q80_split_fits(sp)) return launch_q80_split(ctx, sp, stream);
     const uint64_t grid = (sp.rows + kSeqRows - 1) / kSeqRows;
     if (grid > 0x7FFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "too many rows for one launch");
     const uint64_t budget = ctx->smem_budget ? ctx->smem_budget : uint64_t(ctx->max_smem_optin);
@@ -1459,13 +1459,13 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-bool q80_lane_fits(const MatvecSeqParams& sp) {
+bool q80_split_fits(const MatvecSeqParams& sp) {
     return sp.k % kQ80ChunkElems == 0 && sp.rows > 0 && sp.rows <= 0x7FFFFFFFull &&
            reinterpret_cast<uintptr_t>(sp.w) % 16 == 0 && reinterpret_cast<uintptr_t>(sp.x) % 16 == 0 &&
            sp.row_bytes == uint64_t(sp.k) / 32u * 34u;
 }
 
-oracle_cuda_status launch_q80_lane(oracle_cuda_context* ctx, const MatvecSeqParams& sp, cudaStream_t stream) {
+oracle_cuda_status launch_q80_split(oracle_cuda_context* ctx, const MatvecSeqParams& sp, cudaStream_t stream) {
     const EncodeTiledFn encode = encode_tiled();
     if (!encode) return fail(ctx, ORACLE_CUDA_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
     CUtensorMap tw{};
