@@ -34,6 +34,22 @@ __device__ __forceinline__ double block_sum_f64(double v, double* scratch) {
     return warp_sum_f64(t);
 }
 
+// Two block_sum_f64 reductions at once (scratch of 64 doubles), each with
+// the same additions in the same order as a block_sum_f64 of its own.
+__device__ __forceinline__ void block_sum2_f64(double a, double b, double* scratch, double& sa, double& sb) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    a = warp_sum_f64(a);
+    b = warp_sum_f64(b);
+    __syncthreads();
+    if (lane == 0) {
+        scratch[warp] = a;
+        scratch[32 + warp] = b;
+    }
+    __syncthreads();
+    sa = warp_sum_f64(lane < nw ? scratch[lane] : 0.0);
+    sb = warp_sum_f64(lane < nw ? scratch[32 + lane] : 0.0);
+}
+
 // One CTA per row.
 __global__ void __launch_bounds__(256) rms_norm_rows_kernel(const float* __restrict__ in, const float* __restrict__ w,
                                                             uint32_t width, float eps, float* __restrict__ out) {

@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restric
     constexpr int kQ = kD / 4;  // key rows per thread
     pdl_launch_dependents();
     __shared__ float q_s[kD], k_s[kD], v_s[kD], nq[kD], nk[kD], o_s[kD];
-    __shared__ double scratch[32];
+    __shared__ double scratch[64];
     __shared__ float gate_s[2];
     const uint32_t h = blockIdx.x, tid = threadIdx.x;
     const uint32_t t = tid >> 2, part = tid & 3u;  // state column, quarter of the key rows
@@ -332,29 +332,55 @@ __global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restric
     float col[kQ];
 #pragma unroll
     for (int j = 0; j < kQ; ++j) col[j] = sh[j * kD];
-    pdl_wait();
     const uint32_t kh = h % key_heads;
     const uint32_t key_width = key_heads * kD;
     const uint32_t channels = 2 * key_width + value_heads * kD;
     const uint32_t K = conv_kernel;
+    // the position, the conv weights and the history this step reads are
+    // written by no kernel of this step (the history slot by this layer's core
+    // one step earlier), so they load with the state, before the wait
     const uint32_t slot = *pos & 1u;
     const float* hin = hist + static_cast<uint64_t>(slot) * channels * K;
     float* hout = hist + static_cast<uint64_t>(slot ^ 1u) * channels * K;
+    const uint32_t which = tid / kD, ci = tid % kD;  // 0: q, 1: k, 2: v
+    const uint32_t c = which == 0 ? kh * kD + ci : which == 1 ? key_width + kh * kD + ci : 2 * key_width + h * kD + ci;
+    constexpr uint32_t kMaxK = 8;
+    float hv[kMaxK], wv[kMaxK];
+    const bool conv = tid < 3 * kD && K <= kMaxK;
+    if (conv) {
+#pragma unroll
+        for (uint32_t j = 0; j < kMaxK; ++j) {
+            if (j < K) {
+                hv[j] = j + 1 < K ? hin[static_cast<uint64_t>(c) * K + j + 1] : 0.0f;
+                wv[j] = conv_w[static_cast<uint64_t>(c) * K + j];
+            }
+        }
+    }
+    pdl_wait();
     if (tid < 3 * kD) {
-        const uint32_t which = tid / kD, i = tid % kD;  // 0: q, 1: k, 2: v
-        const uint32_t c = which == 0 ? kh * kD + i : which == 1 ? key_width + kh * kD + i : 2 * key_width + h * kD + i;
         const bool write = which == 2 || h < key_heads;
         const float* hc = hin + static_cast<uint64_t>(c) * K;
         const float* wc = conv_w + static_cast<uint64_t>(c) * K;
         float* oc = hout + static_cast<uint64_t>(c) * K;
         double sum = 0.0;
-        for (uint32_t j = 0; j < K; ++j) {
-            const float v = j + 1 < K ? hc[j + 1] : qkv[c];
-            if (write) oc[j] = v;
-            sum = __dadd_rn(sum, __dmul_rn(static_cast<double>(v), static_cast<double>(wc[j])));
+        if (conv) {
+#pragma unroll
+            for (uint32_t j = 0; j < kMaxK; ++j) {
+                if (j < K) {
+                    const float v = j + 1 < K ? hv[j] : qkv[c];
+                    if (write) oc[j] = v;
+                    sum = __dadd_rn(sum, __dmul_rn(static_cast<double>(v), static_cast<double>(wv[j])));
+                }
+            }
+        } else {
+            for (uint32_t j = 0; j < K; ++j) {
+                const float v = j + 1 < K ? hc[j + 1] : qkv[c];
+                if (write) oc[j] = v;
+                sum = __dadd_rn(sum, __dmul_rn(static_cast<double>(v), static_cast<double>(wc[j])));
+            }
         }
         const float r = ref_silu(__double2float_rn(sum));
-        (which == 0 ? q_s : which == 1 ? k_s : v_s)[i] = r;
+        (which == 0 ? q_s : which == 1 ? k_s : v_s)[ci] = r;
     } else if (tid == 3 * kD) {
         gate_s[0] = ref_sigmoid(beta_in[h]);
         gate_s[1] = expf(__fmul_rn(ref_softplus(__fadd_rn(alpha[h], dt_bias[h])), decay_a[h]));
@@ -363,8 +389,9 @@ __global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restric
     // gated_delta_step: l2-normalised q (scaled by 1/sqrt(key_dim)) and k
     const double qv = tid < kD ? static_cast<double>(q_s[tid]) : 0.0;
     const double kv = tid < kD ? static_cast<double>(k_s[tid]) : 0.0;
-    const double q_norm = block_sum_f64(__dmul_rn(qv, qv), scratch);
-    const double k_norm = block_sum_f64(__dmul_rn(kv, kv), scratch);
+    // both sums in one block reduction (each in block_sum_f64's order)
+    double q_norm, k_norm;
+    block_sum2_f64(__dmul_rn(qv, qv), __dmul_rn(kv, kv), scratch, q_norm, k_norm);
     if (tid < kD) {
         const double e = static_cast<double>(eps);
         const float inv_q = __double2float_rn(__ddiv_rn(1.0, fmax(__dsqrt_rn(q_norm), e)));
