@@ -1525,8 +1525,8 @@ extern "C" oracle_cuda_status oracle_cuda_prefill_gemm(oracle_cuda_context* ctx,
 
     // activations to bf16
     const uint64_t n4 = m * cols / 4;
-    uint64_t blocks = (n4 + 255) / 256;
-    if (blocks > uint64_t(ctx->sm_count) * 16) blocks = uint64_t(ctx->sm_count) * 16;
+    uint64_t blocks = (n4 + 256 * kConvertUnroll - 1) / (256 * kConvertUnroll);
+    if (blocks > uint64_t(ctx->sm_count) * 8) blocks = uint64_t(ctx->sm_count) * 8;
     s = launch(ctx, convert_bf16_kernel, dim3(static_cast<uint32_t>(blocks)), dim3(256), 0, stream, false, x_dev,
                reinterpret_cast<uint32_t*>(ctx->gemm_x), n4);
     if (s != ORACLE_CUDA_OK) return s;
