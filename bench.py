@@ -52,6 +52,26 @@ UNIT = "GB/s"
 BLOCK = {TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144), TYPE_Q6_K: (256, 210)}
 
 
+def product_library_mapped() -> bool:
+    """Whether this process has mapped the product library (liboracle_cuda.so).
+    The reference arm must not: it times only the CPU implementation."""
+    try:
+        with open("/proc/self/maps") as f:
+            return "liboracle_cuda.so" in f.read()
+    except OSError:
+        return False
+
+
+def print_reference_line(line: dict) -> None:
+    """The reference arm's JSON line, after checking that nothing of the
+    product was loaded into this process."""
+    mapped = product_library_mapped()
+    if mapped:
+        raise SystemExit("reference arm: liboracle_cuda.so is mapped into the reference process")
+    line["product_library_mapped"] = mapped
+    print(json.dumps(line), flush=True)
+
+
 def weight_bytes(qtype: int, k: int, n: int) -> int:
     be, bb = BLOCK[qtype]
     return n * (k // be) * bb
@@ -366,7 +386,7 @@ def reference_arm(args, wl: Workload) -> None:
             "data": "synthetic", "config": wl.config(args.gpus),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": wl.cpu_kind, "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    print_reference_line(line)
 
 
 # ---------------------------------------------------------------- GPU arm
@@ -741,7 +761,7 @@ def gemm_reference_arm(args, wl: GemmWorkload) -> None:
             "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
                              "sample": f"{samples} sampled output elements per shape per step on {threads} threads"},
             "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    print_reference_line(line)
 
 
 def gemm_arm(args, wl: GemmWorkload) -> None:
@@ -996,7 +1016,7 @@ def decoder_reference_arm(args, wl: DecoderWorkload) -> None:
             "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded Q4_K_M weights)",
             "config": wl.config(1), "cpu_baseline": cpu,
             "e2e": {"value": tps, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    print_reference_line(line)
 
 
 def decoder_arm(args, wl: DecoderWorkload) -> None:

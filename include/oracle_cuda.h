@@ -243,12 +243,28 @@ oracle_cuda_status oracle_cuda_matvec_program_ex(oracle_cuda_context* ctx, const
  * other threads) race with each other.  Programs whose activation images need
  * more than ORACLE_CUDA_NOALLOC_IMAGE_BYTES are rejected with
  * INVALID_ARGUMENT.  Errors are reported through oracle_cuda_last_error(NULL);
- * device-side wait timeouts are not reported.  Results equal those of
- * oracle_cuda_matvec_program.  No counterpart in the reference (Oracle's path
- * never touches device memory). */
+ * a device-side wait that expired is reported by oracle_cuda_noalloc_status
+ * (below), which reads the status word of the last call.  Results equal those
+ * of oracle_cuda_matvec_program.  No counterpart in the reference (Oracle's
+ * path never touches device memory). */
 #define ORACLE_CUDA_NOALLOC_IMAGE_BYTES 65536
 oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cuda_matvec_op* ops, uint32_t n_ops,
                                                       void* stream);
+
+/* The status of the last oracle_cuda_matvec_program_noalloc (or no-allocation
+ * self-test) call on `device`: waits for that device's work to finish, then
+ * returns ORACLE_CUDA_DEVICE_TIMEOUT (with the site in
+ * oracle_cuda_last_error(NULL)) if one of the call's bounded device-side waits
+ * expired -- its outputs are then incomplete -- else OK.  Reads the static
+ * array's status word with a device-to-host copy; allocates nothing.  No
+ * counterpart in the reference. */
+oracle_cuda_status oracle_cuda_noalloc_status(int device);
+
+/* A test of that status path: one kernel waits, on the no-allocation status
+ * word of the current device, for a barrier nothing completes, and gives up
+ * after limit_ns (0 < limit_ns <= 2 s); oracle_cuda_noalloc_status then reports
+ * the timeout.  No counterpart in the reference. */
+oracle_cuda_status oracle_cuda_noalloc_selftest_bounded_wait(uint64_t limit_ns, void* stream);
 
 /* ------------------------------------------------------------------ either side of the matvecs
  * Embedding gather: out[t][0..cols) = the exact f32 decode of row ids[t] of a

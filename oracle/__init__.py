@@ -27,7 +27,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_PATH = os.path.join(HERE, "liboracle_port.so")
 REF_PATH = os.path.join(HERE, "_ref", "liboracle_ref.so")
 REF_Q8K_PATH = os.path.join(HERE, "_ref", "liboracle_ref_q8k.so")
-REFERENCE_TREE = "/root/reference"
+REF_GATE_PATH = os.path.join(HERE, "_ref", "liboracle_ref_gate.so")
+# Oracle's source tree, for (re)building the reference checker; no default.
+REFERENCE_TREE = os.environ.get("ORACLE_REFERENCE_TREE", "")
 
 TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K, TYPE_Q8_K, TYPE_BF16 = (
     0, 1, 8, 12, 13, 14, 15, 30)
@@ -43,8 +45,8 @@ def build(reference_tree: str | None = REFERENCE_TREE) -> None:
     """Compile the restatement, and the reference checker when its tree exists."""
     targets = ["port"]
     if reference_tree and os.path.isdir(reference_tree):
-        targets += ["ref", "ref_q8k"]
-    subprocess.run(["make", "-s", "-C", HERE, f"REF={reference_tree}", *targets], check=True)
+        targets += ["ref", "ref_q8k", "ref_gate"]
+    subprocess.run(["make", "-s", "-C", HERE, f"REF={reference_tree or ''}", *targets], check=True)
 
 
 def _ptr(a: np.ndarray, t):
@@ -390,7 +392,7 @@ _qwen35_libs = {}
 
 
 def _qwen35_lib(contract: str):
-    path = {"f32": REF_PATH, "q8k": REF_Q8K_PATH}[contract]
+    path = {"f32": REF_PATH, "q8k": REF_Q8K_PATH, "gate": REF_GATE_PATH}[contract]
     if contract not in _qwen35_libs:
         if not os.path.exists(path):
             build()
@@ -419,7 +421,11 @@ class Qwen35Reference:
     contract "f32": the reference compiled unmodified (its f32 contract; its
     binder admits Q5_K/Q6_K/Q8_0/float matrices).  contract "q8k": the same
     sources with Q4_K/Q6_K projections on GGML's Q8_K contract and Q4_K
-    admitted (``admit_q4k``).  The model is a GGUF file (``gguf_path``) or
+    admitted (``admit_q4k``) by this checker's own binding.  contract
+    "gate": the "q8k" build whose binder is the reference's own
+    ``bind_qwen35_weights`` compiled with the one-line type-gate change
+    (Q4_K admitted in ``allowed_storage_type``'s matrix branch,
+    qwen35_weights.cpp:49-59; ``oracle/Makefile`` target ``ref_gate``).  The model is a GGUF file (``gguf_path``) or
     host buffers: ``tensors`` = [(name, ggml_type, dims, uint8 array)], dims
     GGUF-ordered (dims[0] = columns), with ``manifest`` a dict of
     ``_Qwen35Manifest`` fields."""
@@ -510,4 +516,4 @@ def ref() -> _Ref:
 
 
 def ref_available() -> bool:
-    return os.path.exists(REF_PATH) or os.path.isdir(REFERENCE_TREE)
+    return os.path.exists(REF_PATH) or bool(REFERENCE_TREE and os.path.isdir(REFERENCE_TREE))

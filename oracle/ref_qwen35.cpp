@@ -20,6 +20,13 @@
 // decoder still rejects Q4_K, so that mode is only useful in
 // liboracle_ref_q8k.so, where the projections run GGML's Q8_K contract
 // (ref_q8k_projection.cpp).
+//
+// liboracle_ref_gate.so (OREF_GATE_PATCHED) is the same Q8_K build whose
+// qwen35_weights.cpp is a build-directory copy of the reference's with that
+// one-line change applied (Q4_K admitted in allowed_storage_type's matrix
+// branch, oracle/Makefile); there admit_q4k = 1 binds with the reference's
+// own bind_qwen35_weights, so the binder's names, shapes, byte sizes and
+// roles are checked by the reference itself.
 #include "oracle/model/mapped_gguf.hpp"
 #include "oracle/model/qwen35_manifest.hpp"
 #include "oracle/model/qwen35_weights.hpp"
@@ -156,8 +163,13 @@ int oref_qwen35_open_gguf(const char* path, int admit_q4k, uint64_t max_tokens, 
         auto m = std::make_unique<oref_qwen35>();
         m->mapped = std::make_unique<model::MappedGgufModel>(path);
         m->manifest = model::load_qwen35_manifest(m->mapped->file());
+#ifdef OREF_GATE_PATCHED
+        (void)admit_q4k;
+        m->weights = model::bind_qwen35_weights(*m->mapped, m->manifest);
+#else
         m->weights = admit_q4k ? bind_admitting_q4k(m->mapped->tensors(), m->manifest)
                                : model::bind_qwen35_weights(*m->mapped, m->manifest);
+#endif
         m->cache = std::make_unique<runtime::HybridCache>(m->manifest, max_tokens);
         *out = m.release();
     });
@@ -204,7 +216,12 @@ int oref_qwen35_open_buffers(const oref_qwen35_manifest* mf, uint32_t n, const c
             m->views.emplace_back(&m->infos[i], layout, static_cast<const std::byte*>(data[i]),
                                   static_cast<std::size_t>(sizes[i]), 0);
         }
+#ifdef OREF_GATE_PATCHED
+        (void)admit_q4k;
+        m->weights = model::bind_qwen35_weights(m->views, g);
+#else
         m->weights = admit_q4k ? bind_admitting_q4k(m->views, g) : model::bind_qwen35_weights(m->views, g);
+#endif
         m->cache = std::make_unique<runtime::HybridCache>(g, max_tokens);
         *out = m.release();
     });

@@ -48,17 +48,51 @@ if not os.path.exists(LIB_PATH):
         f"{LIB_PATH} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'` "
         "(there is no CPU fallback for this path)")
 
-_lib = C.CDLL(LIB_PATH)
+
+class _Library:
+    """liboracle_cuda.so, mapped on the first call through it.
+
+    Importing the package (its seeded generators, the model description)
+    maps nothing, so a process that only uses those -- the CPU checkers and
+    ``bench.py --impl reference`` -- never loads the CUDA library.  The first
+    attribute access loads it and applies every prototype declared with
+    :func:`_proto`."""
+
+    def __init__(self, path: str):
+        self._path = path
+        self._cdll = None
+        self._protos = {}
+
+    def _load(self):
+        if self._cdll is None:
+            lib = C.CDLL(self._path)
+            for name, (args, res) in self._protos.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = res
+            self._cdll = lib
+        return self._cdll
+
+    def __getattr__(self, name):
+        if name.startswith("_"):
+            raise AttributeError(name)
+        return getattr(self._load(), name)
+
+
+_lib = _Library(LIB_PATH)
 
 _vp, _u32, _u64, _i32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int
 _u64p = C.POINTER(C.c_uint64)
 
 
 def _proto(name, args, res=C.c_int):
-    fn = getattr(_lib, name)
-    fn.argtypes = args
-    fn.restype = res
-    return fn
+    """Declare an entry point's argument and result types (applied on load)."""
+    _lib._protos[name] = (args, res)
+
+
+def loaded() -> bool:
+    """Whether this process has mapped liboracle_cuda.so yet."""
+    return _lib._cdll is not None
 
 
 _proto("oracle_cuda_abi_version", [])
@@ -97,6 +131,8 @@ _proto("oracle_cuda_matvec_program", [_vp, C.POINTER(MatvecOp), _u32, _vp])
 _proto("oracle_cuda_matvec_program_ex", [_vp, C.POINTER(MatvecOpEx), _u32, _vp])
 _proto("oracle_cuda_matvec_program_ex_allgather", [_vp, _vp, C.POINTER(MatvecOpEx), _u32, _vp])
 _proto("oracle_cuda_matvec_program_noalloc", [C.POINTER(MatvecOp), _u32, _vp])
+_proto("oracle_cuda_noalloc_status", [_i32])
+_proto("oracle_cuda_noalloc_selftest_bounded_wait", [_u64, _vp])
 NOALLOC_IMAGE_BYTES = 65536
 
 
@@ -114,6 +150,19 @@ def matvec_program_noalloc(ops, stream=None) -> None:
     ops as for :meth:`Context.matvec_program`."""
     arr = _matvec_ops(ops)
     _raise(_lib.oracle_cuda_matvec_program_noalloc(arr, len(ops), _stream(stream)), None)
+
+
+def noalloc_status(device: int = 0) -> None:
+    """oracle_cuda_noalloc_status: raise DeviceTimeout if a bounded device-side
+    wait of the last no-allocation call on ``device`` expired (waits for the
+    device's work; allocates nothing)."""
+    _raise(_lib.oracle_cuda_noalloc_status(device), None)
+
+
+def noalloc_selftest_bounded_wait(limit_ns: int, stream=None) -> None:
+    """oracle_cuda_noalloc_selftest_bounded_wait: a wait nothing completes,
+    given up after limit_ns, recorded in the no-allocation status word."""
+    _raise(_lib.oracle_cuda_noalloc_selftest_bounded_wait(limit_ns, _stream(stream)), None)
 _proto("oracle_cuda_weight_upload", [_vp, _u32, _u64, _u64, _vp, _u64, _u64, _u64, C.POINTER(_vp)])
 _proto("oracle_cuda_weight_free", [_vp])
 _proto("oracle_cuda_weight_info", [_vp, C.POINTER(_u32), _u64p, _u64p, _u64p, C.POINTER(_vp), _u64p])

@@ -4,8 +4,10 @@
   plus the C ABI of ``include/oracle_cuda.h``, built by nvcc with
   ``-gencode arch=compute_100a,code=sm_100a`` (cudart linked statically).
 * ``oracle/liboracle_port.so`` and ``oracle/_ref/liboracle_ref.so`` -- the CPU
-  checkers used by the tests (``oracle/Makefile``); the second one only where
-  the reference tree exists.
+  checkers used by the tests (``oracle/Makefile``); the second one only when
+  the environment variable ``ORACLE_REFERENCE_TREE`` names Oracle's source
+  tree (there is no default).  Without it the build says so and keeps the
+  checker libraries already built, if any.
 
 This file is loaded by path (``__graft_entry__.build``, ``tests/conftest.py``)
 so that it runs before the package's library exists.
@@ -23,7 +25,19 @@ LIB = os.path.join(HERE, "liboracle_cuda.so")
 CSRC = os.path.join(HERE, "csrc")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-REFERENCE_TREE = "/root/reference"
+# Oracle's source tree (the checker and the C++ tests compile its files);
+# no default: a machine without it uses the checker libraries built elsewhere.
+REFERENCE_TREE = os.environ.get("ORACLE_REFERENCE_TREE", "")
+
+
+def _reference_tree() -> str | None:
+    if REFERENCE_TREE and os.path.isdir(os.path.join(REFERENCE_TREE, "src")):
+        return REFERENCE_TREE
+    return None
+
+
+def _say(msg: str) -> None:
+    print(f"[oracle_b200.build] {msg}", file=sys.stderr, flush=True)
 
 
 def _sources():
@@ -50,9 +64,15 @@ def build_cuda(force: bool = False, verbose: bool = False) -> str:
 
 def build_oracle() -> None:
     targets = ["port"]
-    if os.path.isdir(REFERENCE_TREE):
-        targets += ["ref", "ref_q8k"]
-    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={REFERENCE_TREE}", *targets],
+    tree = _reference_tree()
+    if tree:
+        targets += ["ref", "ref_q8k", "ref_gate"]
+    else:
+        have = [p for p in ("liboracle_ref.so", "liboracle_ref_q8k.so", "liboracle_ref_gate.so")
+                if os.path.exists(os.path.join(ROOT, "oracle", "_ref", p))]
+        _say("ORACLE_REFERENCE_TREE is not set to Oracle's source tree: the reference checker "
+             f"(oracle/_ref) is NOT rebuilt; prebuilt libraries present: {have or 'none'}")
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={tree or ''}", *targets],
                    check=True)
 
 
@@ -64,9 +84,11 @@ def build_cpp_tests() -> None:
     """The C++ tests (tests/cpp/adapter_test.cpp, gguf_test.cpp): compiled
     against Oracle's headers, so only where the reference tree exists; the
     binaries travel with the repository snapshot."""
-    inc = os.path.join(REFERENCE_TREE, "include")
-    if not os.path.isdir(inc):
+    tree = _reference_tree()
+    if not tree:
+        _say("ORACLE_REFERENCE_TREE is not set: the C++ adapter tests (tests/cpp) are NOT rebuilt")
         return
+    inc = os.path.join(tree, "include")
     ref_dir = os.path.join(ROOT, "oracle", "_ref")
     port_dir = os.path.join(ROOT, "oracle")
     for binary, name in ((CPP_TEST, "adapter_test.cpp"), (CPP_GGUF_TEST, "gguf_test.cpp")):

@@ -734,6 +734,72 @@ oracle_cuda_status oracle_cuda_matvec_program_ex(oracle_cuda_context* ctx, const
 
 namespace {
 
+// Rows per stage, segment-major streaming and the shared-memory stage ring of
+// a program whose ops and activation image bytes (pp.act_bytes) are set.  One
+// planner for every entry point that launches matvec_program_kernel, so they
+// all stream the same stages for the same ops.
+oracle_cuda_status plan_program_ring(ProgramParams& pp, uint64_t smem_budget, uint64_t stage_target,
+                                     std::string& why) {
+    why = "matvec program rows too long for the shared-memory stage ring";
+    if (pp.act_bytes > 96 * 1024) return ORACLE_CUDA_UNSUPPORTED;
+    const uint64_t budget = smem_budget - stream_barrier_bytes(16) - pp.act_bytes;
+    uint64_t stage = 0;
+    // rows per stage: up to two per consumer warp (Q4_K rows of <= 16
+    // super-blocks are computed in pairs), within the stage target, and
+    // small enough that kProgramMinStages stages fit beside the images
+    uint64_t target = budget / kProgramMinStages;
+    if (target > stage_target) target = stage_target;
+    // Q4_K rows of more than 16 super-blocks stream segment-major: a stage
+    // holds one 16-super-block segment of up to two rows per consumer warp
+    for (uint32_t k = 0; k < pp.n_ops; ++k) {
+        ProgramOp& p = pp.ops[k];
+        // Q6_K: every segment a 16-byte multiple (nb % 8 == 0) from a
+        // 16-byte aligned weight pointer (bulk copies), one row per warp
+        const bool q6 = p.type == kTypeQ6_K;
+        p.segmented = (p.nb > kSegmentBlocks &&
+                       (p.type == kTypeQ4_K || (q6 && p.nb % 8 == 0 && reinterpret_cast<uintptr_t>(p.w) % 16 == 0)))
+                          ? 1u
+                          : 0u;
+        const uint64_t rb = p.segmented ? uint64_t(kSegmentBlocks) * (q6 ? 210u : 144u) : p.row_bytes;
+        uint64_t R = target > 32 ? (target - 32) / rb : 0;
+        const uint64_t cap = (p.segmented && q6) ? kProgramWarps : 2 * kProgramWarps;
+        if (R > cap) R = cap;
+        if (R < 1) R = 1;
+        p.rows_per_stage = static_cast<uint32_t>(R);
+        const uint64_t sb = align_up(static_cast<uint32_t>(R * rb + 32), 128u);
+        if (sb > stage) stage = sb;
+    }
+    if (stage * 2 > budget) return ORACLE_CUDA_UNSUPPORTED;
+    uint64_t S = budget / stage;
+    if (S > 16) S = 16;
+    pp.stages = static_cast<uint32_t>(S);
+    pp.stage_bytes = static_cast<uint32_t>(stage);
+    return ORACLE_CUDA_OK;
+}
+
+using ProgramKernel = void (*)(const ProgramParams);
+
+// The program kernel specialised for the ops' weight types (and, in a peer
+// group, with the peer stores compiled in).
+ProgramKernel select_program_kernel(const ProgramParams& pp, bool peers) {
+    int types = 0;
+    bool short_rows = true;
+    for (uint32_t k = 0; k < pp.n_ops; ++k) {
+        types |= pp.ops[k].type == kTypeQ4_K ? 1 : 2;
+        short_rows = short_rows && pp.ops[k].nb <= 16;
+    }
+    if (types == 2 && short_rows) types = 4;
+    if (peers)
+        return types == 1   ? matvec_program_kernel<kProgramWarps, 1, true>
+               : types == 2 ? matvec_program_kernel<kProgramWarps, 2, true>
+               : types == 4 ? matvec_program_kernel<kProgramWarps, 4, true>
+                            : matvec_program_kernel<kProgramWarps, 3, true>;
+    return types == 1   ? matvec_program_kernel<kProgramWarps, 1>
+           : types == 2 ? matvec_program_kernel<kProgramWarps, 2>
+           : types == 4 ? matvec_program_kernel<kProgramWarps, 4>
+                        : matvec_program_kernel<kProgramWarps, 3>;
+}
+
 // Two ops read the same activation image when their sources are identical.
 bool same_source(const oracle_cuda_matvec_op_ex& a, const oracle_cuda_matvec_op_ex& b) {
     return a.base.x_dev == b.base.x_dev && a.base.cols == b.base.cols && a.xform == b.xform &&
@@ -749,7 +815,7 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
                     "a matvec program holds 1 to " + std::to_string(kProgramMaxOps) + " ops");
     ProgramParams pp{};
     pp.n_ops = n_ops;
-    uint64_t max_rows = 0, stage = 0;
+    uint64_t max_rows = 0;
     for (uint32_t k = 0; k < n_ops; ++k) {
         const oracle_cuda_matvec_op_ex& e = ops[k];
         if (e.xform > ORACLE_CUDA_XFORM_SWIGLU)
@@ -912,43 +978,11 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         }
     }
     pp.act_bytes = act_total;
-    if (pp.act_bytes > 96 * 1024)
-        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "matvec program rows too long for the shared-memory stage ring");
-    const uint64_t budget = ctx->smem_budget - stream_barrier_bytes(16) - pp.act_bytes;
     {
-        // rows per stage: up to two per consumer warp (Q4_K rows of <= 16
-        // super-blocks are computed in pairs), within the stage target, and
-        // small enough that kProgramMinStages stages fit beside the images
-        uint64_t target = budget / kProgramMinStages;
-        if (target > ctx->program_stage_target) target = ctx->program_stage_target;
-        // Q4_K rows of more than 16 super-blocks stream segment-major: a stage
-        // holds one 16-super-block segment of up to two rows per consumer warp
-        for (uint32_t k = 0; k < n_ops; ++k) {
-            ProgramOp& p = pp.ops[k];
-            // Q6_K: every segment a 16-byte multiple (nb % 8 == 0) from a
-            // 16-byte aligned weight pointer (bulk copies), one row per warp
-            const bool q6 = p.type == kTypeQ6_K;
-            p.segmented = (p.nb > kSegmentBlocks &&
-                           (p.type == kTypeQ4_K ||
-                            (q6 && p.nb % 8 == 0 && reinterpret_cast<uintptr_t>(p.w) % 16 == 0)))
-                              ? 1u
-                              : 0u;
-            const uint64_t rb = p.segmented ? uint64_t(kSegmentBlocks) * (q6 ? 210u : 144u) : p.row_bytes;
-            uint64_t R = target > 32 ? (target - 32) / rb : 0;
-            const uint64_t cap = (p.segmented && q6) ? kProgramWarps : 2 * kProgramWarps;
-            if (R > cap) R = cap;
-            if (R < 1) R = 1;
-            p.rows_per_stage = static_cast<uint32_t>(R);
-            const uint64_t sb = align_up(static_cast<uint32_t>(R * rb + 32), 128u);
-            if (sb > stage) stage = sb;
-        }
+        std::string why;
+        const oracle_cuda_status rs = plan_program_ring(pp, ctx->smem_budget, ctx->program_stage_target, why);
+        if (rs != ORACLE_CUDA_OK) return fail(ctx, rs, why);
     }
-    if (stage * 2 > budget)
-        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "matvec program rows too long for the shared-memory stage ring");
-    uint64_t S = budget / stage;
-    if (S > 16) S = 16;
-    pp.stages = static_cast<uint32_t>(S);
-    pp.stage_bytes = static_cast<uint32_t>(stage);
     pp.copy_chunk = ctx->copy_chunk;
     pp.max_inflight = ctx->max_inflight < pp.stages ? ctx->max_inflight : pp.stages;
     pp.prebuilt_bytes = prebuilt;
@@ -998,22 +1032,7 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
                     (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, jobs, ctx->image_scratch);
         if (gs != ORACLE_CUDA_OK) return gs;
     }
-    int types = 0;
-    bool short_rows = true;
-    for (uint32_t k = 0; k < n_ops; ++k) {
-        types |= ops[k].base.type == kTypeQ4_K ? 1 : 2;
-        short_rows = short_rows && ops[k].base.cols <= 16 * 256;
-    }
-    if (types == 2 && short_rows) types = 4;
-    // the peer-group stores are compiled only into the row-sharded kernels
-    auto kernel = group ? (types == 1   ? matvec_program_kernel<kProgramWarps, 1, true>
-                           : types == 2 ? matvec_program_kernel<kProgramWarps, 2, true>
-                           : types == 4 ? matvec_program_kernel<kProgramWarps, 4, true>
-                                        : matvec_program_kernel<kProgramWarps, 3, true>)
-                        : (types == 1   ? matvec_program_kernel<kProgramWarps, 1>
-                           : types == 2 ? matvec_program_kernel<kProgramWarps, 2>
-                           : types == 4 ? matvec_program_kernel<kProgramWarps, 4>
-                                        : matvec_program_kernel<kProgramWarps, 3>);
+    const auto kernel = select_program_kernel(pp, group != nullptr);
     oracle_cuda_status st = launch(ctx, kernel, dim3(grid), dim3((kProgramWarps + 1) * 32), smem,
                                    static_cast<cudaStream_t>(stream), (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, pp);
     return st == ORACLE_CUDA_OK ? ok(ctx) : st;
@@ -1340,7 +1359,7 @@ extern "C" oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cu
 
     ProgramParams pp{};
     pp.n_ops = n_ops;
-    uint64_t max_rows = 0, stage = 0, prebuilt = 0, dependent = 0;
+    uint64_t max_rows = 0, prebuilt = 0;
     for (uint32_t k = 0; k < n_ops; ++k) {
         const oracle_cuda_matvec_op& o = ops[k];
         uint64_t rb = 0, batch = 0;
@@ -1361,14 +1380,8 @@ extern "C" oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cu
         p.nb = static_cast<uint32_t>(o.cols / 256);
         p.after_previous = (o.after_previous && k > 0) ? 1u : 0u;
         if (p.after_previous) pp.ops[k - 1].publish = 1u;
-        uint64_t R = 36864 / rb;
-        if (R > uint64_t(kProgramWarps)) R = kProgramWarps;
-        if (R < 1) R = 1;
-        p.rows_per_stage = static_cast<uint32_t>(R);
-        const uint64_t sb = align_up(static_cast<uint32_t>(R * rb + 32), 128u);
-        if (sb > stage) stage = sb;
         if (o.rows > max_rows) max_rows = o.rows;
-        (p.after_previous ? dependent : prebuilt) += q8k_image_bytes(p.nb);
+        if (!p.after_previous) prebuilt += q8k_image_bytes(p.nb);
     }
     // The activation images of ops fed from outside the call live in the
     // static array; they must fit its stated size.
@@ -1399,19 +1412,20 @@ extern "C" oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cu
             off += q8k_image_bytes(pp.ops[k].nb);
         }
     pp.act_bytes = off + 256;  // + reduction scratch
-    const uint64_t budget = uint64_t(dev->smem_optin) - stream_barrier_bytes(16) - pp.act_bytes;
-    if (pp.act_bytes > 96 * 1024 || stage * 2 > budget)
-        return fail(nullptr, ORACLE_CUDA_UNSUPPORTED, "matvec program rows too long for the shared-memory stage ring");
-    uint64_t S = budget / stage;
-    if (S > 16) S = 16;
-    pp.stages = static_cast<uint32_t>(S);
-    pp.stage_bytes = static_cast<uint32_t>(stage);
-    pp.copy_chunk = 32768;
-    pp.max_inflight = pp.stages;
+    {
+        // the same stage planning as the context entry points, with their defaults
+        const oracle_cuda_context defaults{};
+        std::string why;
+        st = plan_program_ring(pp, uint64_t(dev->smem_optin), defaults.program_stage_target, why);
+        if (st != ORACLE_CUDA_OK) return fail(nullptr, st, why);
+        pp.copy_chunk = defaults.copy_chunk;
+        pp.max_inflight = defaults.max_inflight < pp.stages ? defaults.max_inflight : pp.stages;
+    }
     pp.images = dev->scratch;
     pp.prebuilt_bytes = prebuilt_bytes;
     pp.counters = reinterpret_cast<unsigned int*>(dev->scratch + kNoAllocCountersOffset);
     pp.status = reinterpret_cast<DeviceStatus*>(dev->scratch + kNoAllocStatusOffset);
+    pp.px.world = 1;  // one GPU: the single-GPU release path for dependent ops
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // Counters and status must start at zero; the array keeps whatever the
@@ -1419,22 +1433,56 @@ extern "C" oracle_cuda_status oracle_cuda_matvec_program_noalloc(const oracle_cu
     if ((e = cudaMemsetAsync(dev->scratch + kNoAllocCountersOffset, 0, 512, s)) != cudaSuccess)
         return cuda_fail(nullptr, e, "cudaMemsetAsync(no-allocation counters)");
     if (prebuilt_bytes > 0) {
-        const uint32_t qgrid = (blocks * 32 + 255) / 256;
-        quantize_images_kernel<<<qgrid, 256, 0, s>>>(jobs, dev->scratch);
+        // one warp per 256-block, as the context entry points launch it
+        quantize_images_kernel<<<blocks, 32, 0, s>>>(jobs, dev->scratch);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(nullptr, e, "quantize_images_kernel launch");
     }
-    int types = 0;
-    for (uint32_t k = 0; k < n_ops; ++k) types |= ops[k].type == kTypeQ4_K ? 1 : 2;
     const uint32_t grid = static_cast<uint32_t>(max_rows < uint64_t(dev->sm_count) ? max_rows : dev->sm_count);
     const size_t smem = stream_barrier_bytes(pp.stages) + pp.act_bytes + size_t(pp.stages) * pp.stage_bytes;
-    const dim3 block((kProgramWarps + 1) * 32);
-    if (types == 1)
-        matvec_program_kernel<kProgramWarps, 1><<<grid, block, smem, s>>>(pp);
-    else if (types == 2)
-        matvec_program_kernel<kProgramWarps, 2><<<grid, block, smem, s>>>(pp);
-    else
-        matvec_program_kernel<kProgramWarps, 3><<<grid, block, smem, s>>>(pp);
+    select_program_kernel(pp, false)<<<grid, dim3((kProgramWarps + 1) * 32), smem, s>>>(pp);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(nullptr, e, "matvec_program_kernel launch");
+    return ORACLE_CUDA_OK;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_noalloc_status(int device) {
+    int current = 0;
+    cudaError_t e = cudaGetDevice(&current);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDevice");
+    if (current != device && (e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(nullptr, e, "cudaSetDevice");
+    NoAllocDevice* dev = nullptr;
+    oracle_cuda_status st = noalloc_setup(device, &dev);  // with `device` current
+    if (st != ORACLE_CUDA_OK) {
+        if (current != device) cudaSetDevice(current);
+        return st;
+    }
+    // a plain device-to-host copy of the status word (it waits for the device's
+    // work to finish and allocates nothing); the next call clears the word
+    DeviceStatus h{};
+    e = cudaMemcpy(&h, dev->scratch + kNoAllocStatusOffset, sizeof(h), cudaMemcpyDeviceToHost);
+    if (current != device) cudaSetDevice(current);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaMemcpy(no-allocation status)");
+    if (h.code != kDevOk)
+        return fail(nullptr, ORACLE_CUDA_DEVICE_TIMEOUT,
+                    "kernel wait timed out at site " + std::to_string(h.where) + " in block " +
+                        std::to_string(h.block) + " (last no-allocation call)");
+    return ORACLE_CUDA_OK;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_noalloc_selftest_bounded_wait(uint64_t limit_ns, void* stream) {
+    if (limit_ns == 0 || limit_ns > 2000000000ull)
+        return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "self-test deadline must be in (0, 2 s]");
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDevice");
+    NoAllocDevice* dev = nullptr;
+    oracle_cuda_status st = noalloc_setup(device, &dev);
+    if (st != ORACLE_CUDA_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if ((e = cudaMemsetAsync(dev->scratch + kNoAllocCountersOffset, 0, 512, s)) != cudaSuccess)
+        return cuda_fail(nullptr, e, "cudaMemsetAsync(no-allocation counters)");
+    bounded_wait_selftest_kernel<<<1, 32, 0, s>>>(reinterpret_cast<DeviceStatus*>(dev->scratch + kNoAllocStatusOffset),
+                                                 limit_ns);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(nullptr, e, "bounded_wait_selftest_kernel launch");
     return ORACLE_CUDA_OK;
 }
 

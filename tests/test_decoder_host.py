@@ -9,8 +9,12 @@
   and from host buffers, for both checker builds.
 * The Q8_K checker build routes Q4_K / Q6_K projections to GGML's contract
   and leaves the others to the reference.
+* With the one-line type-gate change compiled in, the reference's own binder
+  binds the Q4_K_M model.
 """
 from __future__ import annotations
+
+import os
 
 import numpy as np
 import pytest
@@ -91,3 +95,48 @@ def test_q8k_checker_routes_q6k_projections(models):
     assert np.abs(a - f32).max() < 0.25 * f32.std()  # 8-bit activations: ~1% per projection
     rb = oracle.Qwen35Reference("q8k", tensors=tensors, manifest=qwen35.SMALL.manifest(), max_tokens=64)
     assert np.array_equal(rb.forward(7), a)
+
+
+def _gate_checker_or_skip():
+    import oracle
+    if not os.path.exists(oracle.REF_GATE_PATH):
+        pytest.skip("gate-patched reference checker (oracle/_ref/liboracle_ref_gate.so) not built")
+    return oracle
+
+
+def test_patched_type_gate_binds_q4k_m_through_reference_binder(models):
+    """The type gate with the one-line change of the integration notes
+    (Q4_K admitted in allowed_storage_type's matrix branch,
+    src/model/qwen35_weights.cpp:49-59), compiled into the reference's own
+    bind_qwen35_weights (oracle/Makefile, target ref_gate): the Q4_K_M model
+    binds through the reference's binder -- names, shapes, byte sizes and
+    roles checked by the reference itself -- from a mapped GGUF file and from
+    host buffers, and decodes to the same greedy tokens as the checker build
+    that binds with its own gate-free binding.  The unmodified binder still
+    rejects the same file (test_reference_binder_rejects_q4k)."""
+    oracle = _gate_checker_or_skip()
+    path, tensors = models["q4_k_m"]
+    prompt = np.arange(3, 15, dtype=np.uint32) * 53 % qwen35.SMALL.vocab
+    gated = oracle.Qwen35Reference("gate", gguf_path=path, max_tokens=64).greedy(prompt, 10)
+    gated_buffers = oracle.Qwen35Reference("gate", tensors=tensors, manifest=qwen35.SMALL.manifest(),
+                                           max_tokens=64).greedy(prompt, 10)
+    own = oracle.Qwen35Reference("q8k", gguf_path=path, admit_q4k=True, max_tokens=64).greedy(prompt, 10)
+    assert np.array_equal(gated, own)
+    assert np.array_equal(gated_buffers, own)
+    assert len(set(gated.tolist())) > 1
+
+
+def test_patched_type_gate_still_checks_geometry(models):
+    """The patched gate admits Q4_K but the reference binder's other checks
+    stay: a Q4_K matrix with the wrong shape is still rejected with the
+    reference's message."""
+    oracle = _gate_checker_or_skip()
+    _, tensors = models["q4_k_m"]
+    bad = []
+    for name, qtype, dims, data in tensors:
+        if name == "blk.0.ffn_gate.weight":
+            dims = (dims[0], dims[1] - 1)
+            data = data[: len(data) - dims[0] // 256 * 144]
+        bad.append((name, qtype, dims, data))
+    with pytest.raises(oracle.ReferenceError_, match="blk.0.ffn_gate.weight: expected dimensions"):
+        oracle.Qwen35Reference("gate", tensors=bad, manifest=qwen35.SMALL.manifest(), max_tokens=64)

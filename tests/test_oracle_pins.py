@@ -9,6 +9,9 @@
    (tests/golden/decode_ggufpy.npz), the outside pin for Q4_K.
 4. Q8_K quantizer properties and integer dots re-derived with numpy integer
    arithmetic, plus the committed regression fixture tests/golden/q8k.npz.
+5. The integer dot's semantics (nibbles, scales, mins, the Q6_K offset) tied
+   to gguf-py's dequantization in f64, and the quantizer's defining
+   properties (scale from the signed largest element, nearest quants).
 """
 from __future__ import annotations
 
@@ -297,3 +300,80 @@ def test_matvec_q8k_fixture(port):
                           g["y4"].view(np.uint32))
     assert np.array_equal(port.matvec_q8_k(T.TYPE_Q6_K, 3, k, g["w6"], g["q8k"])[0].view(np.uint32),
                           g["y6"].view(np.uint32))
+
+
+# ---------------------------------------------------------------- the integer dot against a third party
+
+@pytest.mark.parametrize("qtype,k", [(T.TYPE_Q4_K, 4096), (T.TYPE_Q4_K, 12288), (T.TYPE_Q6_K, 4096)])
+def test_integer_dot_pinned_to_ggufpy_decode(port, qtype, k):
+    """The Q4_K/Q6_K x Q8_K integer dot tied to gguf-py 0.19.0 (a third
+    party): for seeded rows of the config-2/3 shapes, every super-block term
+    the restatement forms from its exact integer sums, d_w*d_x*isum -
+    dmin_w*d_x*msum (Q4_K) or d_w*d_x*isum (Q6_K, the -32 folded through the
+    bsums), equals sum_e w_e * (d_x * q8_e) computed in f64 from gguf-py's own
+    dequantization of the weights and the Q8_K block's quants.  The only
+    difference allowed is gguf-py's f32 rounding of each w_e (at most four
+    roundings of 2^-24 each), so a wrong nibble order, scale or min index, or
+    offset would miss by the size of the term itself.  The row results of the
+    canonical f32 combine then sit within the north star's 1e-6 absolute +
+    1e-5 relative (to the summed term magnitudes) of the f64 row sums."""
+    gq = pytest.importorskip("gguf.quants")
+    import gguf
+    rows = 24
+    w = synth.weight(qtype, rows, k, "pins", f"ggufpy_dot_{qtype}_{k}")
+    x = synth.activations(k, 1, "pins", f"ggufpy_dot_x_{k}")[0]
+    raw = port.quantize_q8_k(x)[0]
+    d8, q8, _ = split_q8k(raw)
+    xq = (q8.astype(np.float64) * d8.astype(np.float64)[:, None]).reshape(-1)
+    gtype = gguf.GGMLQuantizationType(qtype)
+    wf = gq.dequantize(w.reshape(rows, -1), gtype).astype(np.float64).reshape(rows, k)
+    nb = k // 256
+    prod = (wf * xq).reshape(rows, nb, 256)
+    ref_terms = prod.sum(axis=2)
+    ref_mag = np.abs(prod).sum(axis=2)
+    bb = 144 if qtype == T.TYPE_Q4_K else 210
+    q8b = raw.reshape(-1, 292)
+    dx = d8.astype(np.float64)
+    terms = np.zeros((rows, nb))
+    mags = np.zeros(rows)
+    for r in range(rows):
+        for i in range(nb):
+            blk = w[r, bb * i:bb * (i + 1)]
+            isum, msum = port.block_sums(qtype, blk, q8b[i])
+            if qtype == T.TYPE_Q4_K:
+                d, dmin = blk[0:4].copy().view(np.float16).astype(np.float64)
+            else:
+                d, dmin = blk[208:210].copy().view(np.float16).astype(np.float64)[0], 0.0
+            terms[r, i] = d * dx[i] * isum - dmin * dx[i] * msum
+            mags[r] += abs(d * dx[i] * isum) + abs(dmin * dx[i] * msum)
+    assert np.all(np.abs(terms - ref_terms) <= 4 * 2.0 ** -24 * ref_mag + 1e-30), \
+        (np.abs(terms - ref_terms) / ref_mag).max()
+    y = port.matvec_q8_k(qtype, rows, k, w, raw)[0].astype(np.float64)
+    assert np.all(np.abs(y - ref_terms.sum(axis=1)) <= 1e-6 + 1e-5 * mags)
+    # the pin has teeth: the same check against a decode with one sub-block's
+    # scale index swapped fails by far more than the bound
+    if qtype == T.TYPE_Q4_K:
+        bad = wf.reshape(rows, nb, 8, 32).copy()
+        bad[:, :, [0, 1]] = bad[:, :, [1, 0]]
+        bad_terms = (bad.reshape(rows, k) * xq).reshape(rows, nb, 256).sum(axis=2)
+        assert np.abs(terms - bad_terms).max() > 1e3 * (4 * 2.0 ** -24 * ref_mag).max()
+
+
+def test_q8k_quantizer_rounding_properties(port):
+    """What the Q8_K quantizer's definition fixes, checked on seeded config-2
+    activations without a GGML vector (none exists in the reference or this
+    image): d is the signed largest-magnitude element over -127 (its quant
+    is -127 exactly), every quant is the nearest integer to x/d within half a
+    step (clamped to [-127, 127]), and every bsum is the sum of its 16
+    quants.  Bit-level choices (IEEE division for the scale, ties to even)
+    stay pinned only to the restatement."""
+    x = synth.activations(12288, 1, "pins", "q8k_rounding")[0]
+    d, q, bs = split_q8k(port.quantize_q8_k(x)[0])
+    xb = x.reshape(-1, 256).astype(np.float64)
+    i = np.abs(xb).argmax(axis=1)
+    assert np.all(q[np.arange(len(xb)), i] == -127)
+    assert np.allclose(d.astype(np.float64), -xb[np.arange(len(xb)), i] / 127.0, rtol=2e-7)
+    err = np.abs(xb - q.astype(np.float64) * d.astype(np.float64)[:, None])
+    assert np.all(err <= 0.5 * np.abs(d.astype(np.float64))[:, None] * (1 + 1e-6))
+    assert np.all(np.abs(q.astype(np.int32)) <= 127)
+    assert np.array_equal(bs.astype(np.int32), q.astype(np.int32).reshape(-1, 16, 16).sum(axis=2))

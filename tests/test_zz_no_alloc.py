@@ -7,9 +7,10 @@ device) is not allowed.  Its scratch is one static device array instead of a
 context's buffers.  These tests call it through the C ABI and check that two
 calls in a row give exactly what the context-based oracle_cuda_matvec_program
 gives (the bar for this path is bit equality), including a dependent chain
-whose completion counters live in that array, and that a program too large for
-the array is refused.  The file is collected last and also passes when run
-alone in a fresh process.
+whose completion counters live in that array, that a program too large for
+the array is refused, and that a device-side wait that expired is reported by
+oracle_cuda_noalloc_status.  The file is collected last and also passes when
+run alone in a fresh process.
 """
 from __future__ import annotations
 
@@ -74,3 +75,23 @@ def test_noalloc_program_rejects_oversize_images():
     y = torch.empty(2, dtype=torch.float32, device=DEV)
     with pytest.raises(ob.InvalidArgument, match="no-allocation entry point holds at most 65536"):
         ob.matvec_program_noalloc([(ob.TYPE_Q4_K, 2, 8192, w, x, y, 0)] * 12)
+
+
+def test_noalloc_status_reports_an_expired_wait():
+    """A call's outputs are only complete when none of its bounded waits
+    expired; oracle_cuda_noalloc_status says which.  A wait that nothing
+    completes (the self-test kernel, on the array's status word) gives up
+    after 2 ms and is reported; the next call clears the word."""
+    torch.cuda.set_device(0)
+    ob.noalloc_status(0)  # the previous calls' waits all completed
+    ob.noalloc_selftest_bounded_wait(2_000_000)
+    with pytest.raises(ob.DeviceTimeout, match="site 99"):
+        ob.noalloc_status(0)
+    ops_ref, ops_na = _program(SPECS[:2], "noalloc_status")
+    with ob.Context(0) as ctx:
+        ctx.matvec_program(ops_ref)
+        ctx.device_status()
+    ob.matvec_program_noalloc(ops_na)
+    ob.noalloc_status(0)
+    for a, b in zip(ops_ref, ops_na):
+        assert np.array_equal(a[5].cpu().numpy().view(np.uint32), b[5].cpu().numpy().view(np.uint32))
