@@ -498,10 +498,24 @@ oracle_cuda_status oracle_cuda_weight_info(const oracle_cuda_weight* weight, uin
                                            const void** dev, uint64_t* nbytes);
 
 /* ------------------------------------------------------------------ host-pointer drop-ins
- * Synchronous, host spans in and out, exactly the reference's signatures.  The
- * weight bytes are made resident in HBM on first use, keyed by (host address,
- * byte size, type, rows, cols), and reused afterwards, since Oracle's weights
- * never change under a live mapping. */
+ * Synchronous, host spans in and out, exactly the reference's signatures (the
+ * reference's functions are pure: they read the caller's bytes on every call).
+ * A weight span the caller has REGISTERED (below) is read from its resident
+ * copy in HBM; any other span is copied to the device on every call, so a
+ * buffer whose bytes change between calls always gives the new result. */
+
+/* Register host weight bytes (rows x cols of `type`, exactly `nbytes`): they
+ * are copied to HBM now and the host-pointer calls given the same (address,
+ * nbytes, type, rows, cols) read that copy from then on.  The caller promises
+ * the bytes do not change while registered -- true of Oracle's GGUF tensors,
+ * read-only MAP_PRIVATE pages owned by MappedGgufModel
+ * (include/oracle/model/mapped_gguf.hpp:56-59).  Registering the same span
+ * again is a no-op.  No counterpart in the reference (it has no device). */
+oracle_cuda_status oracle_cuda_register_host_weight(oracle_cuda_context* ctx, uint32_t type, uint64_t rows,
+                                                    uint64_t cols, const void* host, uint64_t nbytes);
+/* Drop the resident copy of a registered span (OUT_OF_RANGE if it is not
+ * registered).  No counterpart in the reference. */
+oracle_cuda_status oracle_cuda_unregister_host_weight(oracle_cuda_context* ctx, const void* host, uint64_t nbytes);
 
 /* reference_storage_matvec (quantized_reference.cpp:128-162). */
 oracle_cuda_status oracle_cuda_host_storage_matvec(oracle_cuda_context* ctx, int contract,
@@ -523,8 +537,29 @@ oracle_cuda_status oracle_cuda_host_decode_rows(oracle_cuda_context* ctx, uint32
                                                 uint64_t w_nbytes, float* out_host,
                                                 uint64_t out_len);
 
-/* Drop every resident copy made by the host-pointer calls. */
+/* Unregister every registered weight span (drops their resident copies). */
 oracle_cuda_status oracle_cuda_evict_resident(oracle_cuda_context* ctx);
+
+/* A matvec program over host spans: several Q8_K-contract matvecs (q4_K /
+ * q6_K weights) in ONE device launch with one synchronize, e.g. a layer's
+ * projections.  Every x is copied in and every y out in one transfer each.
+ * An op whose x_host is the y_host of an earlier op of the same call reads
+ * that op's result on the device (cols must equal that op's rows): a
+ * dependent op, as in oracle_cuda_matvec_program.  Weights as for the
+ * host-pointer calls above (registered: resident; otherwise copied per call).
+ * Results equal oracle_cuda_matvec_program's.  No counterpart in the
+ * reference (its products run one at a time, qwen35_block.cpp:108-119). */
+typedef struct oracle_cuda_host_matvec_op {
+    uint32_t type;
+    uint64_t rows;
+    uint64_t cols;
+    const void* w_host;
+    uint64_t w_nbytes;
+    const float* x_host;  /* cols floats, or an earlier op's y_host */
+    float* y_host;        /* rows floats */
+} oracle_cuda_host_matvec_op;
+oracle_cuda_status oracle_cuda_host_matvec_program(oracle_cuda_context* ctx, const oracle_cuda_host_matvec_op* ops,
+                                                   uint32_t n_ops);
 
 #ifdef __cplusplus
 }

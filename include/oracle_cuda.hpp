@@ -16,8 +16,10 @@
 // (std::invalid_argument, std::out_of_range, std::overflow_error,
 // std::runtime_error, std::logic_error) with the reference's message; CUDA
 // failures throw std::runtime_error.  Calls are synchronous, like the
-// reference.  Weight bytes become resident in HBM on first use and stay there
-// (Oracle's weights are immutable mmap pages).
+// reference.  The GGUF-tensor forms register the tensor's bytes on first use
+// (Oracle's weights are immutable mmap pages, so they stay resident in HBM);
+// the span forms copy their bytes on every call, as the reference reads them
+// on every call, unless the caller registered the span (register_span).
 #pragma once
 
 #include "oracle_cuda.h"
@@ -76,6 +78,12 @@ public:
                                               output.size()));
     }
 
+    // Make a span's bytes resident (the caller promises they never change
+    // while registered); the calls above then read the resident copy.
+    void register_span(std::uint32_t type, std::size_t rows, std::size_t cols, std::span<const std::byte> bytes) {
+        check(oracle_cuda_register_host_weight(ctx_, type, rows, cols, bytes.data(), bytes.size()));
+    }
+
     // decode_storage_row's row form and the GGUF-tensor form (rows x dims[0])
     void decode_rows(std::uint32_t type, std::size_t rows, std::size_t cols, std::span<const std::byte> bytes,
                      std::span<float> output) {
@@ -106,8 +114,9 @@ public:
                               std::span<float> output) {
         const auto dims = tensor.dimensions();
         if (dims.size() != 2) throw std::invalid_argument("mapped tensor matvec requires a rank-2 tensor");
-        storage_matvec(tensor.layout().type, static_cast<std::size_t>(dims[1]), static_cast<std::size_t>(dims[0]),
-                       tensor.bytes(), vector, output);
+        const auto rows = static_cast<std::size_t>(dims[1]), cols = static_cast<std::size_t>(dims[0]);
+        register_mapped(tensor.layout().type, rows, cols, tensor.bytes());
+        storage_matvec(tensor.layout().type, rows, cols, tensor.bytes(), vector, output);
     }
 
     // reference_decode_mapped_tensor (quantized_reference.cpp:85-105)
@@ -116,11 +125,18 @@ public:
         const auto dims = tensor.dimensions();
         if (output.size() != rows * static_cast<std::size_t>(dims.front()))
             throw std::invalid_argument("mapped tensor decode output length mismatch");
+        register_mapped(tensor.layout().type, rows, static_cast<std::size_t>(dims.front()), tensor.bytes());
         decode_rows(tensor.layout().type, rows, static_cast<std::size_t>(dims.front()), tensor.bytes(), output);
     }
 #endif
 
 private:
+    // A mapped tensor's bytes are registered when its geometry is valid; an
+    // invalid one is left to the call, which reports the reference's error.
+    void register_mapped(std::uint32_t type, std::size_t rows, std::size_t cols, std::span<const std::byte> bytes) {
+        (void)oracle_cuda_register_host_weight(ctx_, type, rows, cols, bytes.data(), bytes.size());
+    }
+
     void check(oracle_cuda_status s) const {
         if (s != ORACLE_CUDA_OK) throw_status(s, oracle_cuda_last_error(ctx_));
     }

@@ -170,6 +170,17 @@ _proto("oracle_cuda_host_storage_matvec", [_vp, _i32, _u32, _u64, _u64, _vp, _u6
 _proto("oracle_cuda_host_storage_dot", [_vp, _i32, _u32, _u64, _vp, _u64, _vp, _u64, _vp])
 _proto("oracle_cuda_host_decode_rows", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64])
 _proto("oracle_cuda_evict_resident", [_vp])
+_proto("oracle_cuda_register_host_weight", [_vp, _u32, _u64, _u64, _vp, _u64])
+_proto("oracle_cuda_unregister_host_weight", [_vp, _vp, _u64])
+
+
+class HostMatvecOp(C.Structure):
+    """oracle_cuda_host_matvec_op of include/oracle_cuda.h."""
+    _fields_ = [("type", C.c_uint32), ("rows", C.c_uint64), ("cols", C.c_uint64), ("w_host", C.c_void_p),
+                ("w_nbytes", C.c_uint64), ("x_host", C.c_void_p), ("y_host", C.c_void_p)]
+
+
+_proto("oracle_cuda_host_matvec_program", [_vp, C.POINTER(HostMatvecOp), _u32])
 _proto("oracle_cuda_prefill_gemm", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _vp])
 _proto("oracle_cuda_peer_group_create", [_vp, _u32, _u32, _u64, C.POINTER(_vp), _vp])
 _proto("oracle_cuda_peer_group_connect", [_vp, _vp])
@@ -653,4 +664,29 @@ class Context:
         return out
 
     def evict_resident(self) -> None:
+        """oracle_cuda_evict_resident: unregister every registered weight span."""
         self._check(_lib.oracle_cuda_evict_resident(self._h))
+
+    def register_host_weight(self, qtype, rows, cols, w: np.ndarray) -> None:
+        """oracle_cuda_register_host_weight: the bytes of ``w`` (which must not
+        change while registered) become resident; host calls given the same
+        array then read the resident copy."""
+        if not (w.flags.c_contiguous and w.dtype == np.uint8):
+            raise InvalidArgument("register a C-contiguous uint8 array (the host calls must see the same address)")
+        self._check(_lib.oracle_cuda_register_host_weight(self._h, qtype, rows, cols, w.ctypes.data, w.nbytes))
+
+    def unregister_host_weight(self, w: np.ndarray) -> None:
+        self._check(_lib.oracle_cuda_unregister_host_weight(self._h, w.ctypes.data, w.nbytes))
+
+    def host_matvec_program(self, ops) -> None:
+        """oracle_cuda_host_matvec_program: ops = [(qtype, rows, cols, w, x, y)]
+        with host numpy arrays (uint8 weights, f32 x and y); an op whose x is
+        an earlier op's y (the same array) reads that result on the device.
+        One launch, one synchronize; y arrays are filled in place."""
+        arr = (HostMatvecOp * len(ops))()
+        for i, (qtype, rows, cols, w, x, y) in enumerate(ops):
+            for a, dt in ((w, np.uint8), (x, np.float32), (y, np.float32)):
+                if not (a.flags.c_contiguous and a.dtype == dt):
+                    raise InvalidArgument(f"op {i}: host arrays must be C-contiguous {np.dtype(dt).name}")
+            arr[i] = HostMatvecOp(qtype, rows, cols, w.ctypes.data, w.nbytes, x.ctypes.data, y.ctypes.data)
+        self._check(_lib.oracle_cuda_host_matvec_program(self._h, arr, len(ops)))

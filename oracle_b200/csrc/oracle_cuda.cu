@@ -64,8 +64,11 @@ struct oracle_cuda_context {
     uint64_t act_scratch_bytes = 0;
     std::string last_error;
     std::set<const void*> smem_configured;
-    // resident copies for the host-pointer drop-ins
+    // registered host weight spans and their resident copies (host-pointer calls)
     std::map<std::tuple<const void*, uint64_t, uint32_t, uint64_t, uint64_t>, oracle_cuda_weight*> resident;
+    // device copies of unregistered weight spans, made on every host-pointer call
+    uint8_t* stage_w = nullptr;
+    uint64_t stage_w_len = 0;
     // staging for the host-pointer drop-ins (grown on demand)
     float* pin_x = nullptr;
     float* pin_y = nullptr;
@@ -402,21 +405,30 @@ oracle_cuda_status grow_device(oracle_cuda_context* ctx, T*& p, uint64_t& have, 
     return ORACLE_CUDA_OK;
 }
 
-oracle_cuda_status resident_weight(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
-                                   const void* host, uint64_t nbytes, oracle_cuda_weight** out) {
-    auto key = std::make_tuple(host, nbytes, type, rows, cols);
-    auto it = ctx->resident.find(key);
+// The device bytes a host-pointer call reads for a weight span: the resident
+// copy of a registered span, else a fresh copy into the staging buffer at
+// byte `stage_off` (16-byte aligned; the caller advances it by the span).
+// The reference reads the caller's bytes on every call; so does this, unless
+// the caller has promised (by registering) that they never change.
+oracle_cuda_status weight_bytes_for_call(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
+                                         const void* host, uint64_t nbytes, uint64_t stage_off, cudaStream_t stream,
+                                         const void** dev) {
+    auto it = ctx->resident.find(std::make_tuple(host, nbytes, type, rows, cols));
     if (it != ctx->resident.end()) {
-        *out = it->second;
+        *dev = it->second->dev;
         return ORACLE_CUDA_OK;
     }
-    oracle_cuda_weight* w = nullptr;
-    oracle_cuda_status s = oracle_cuda_weight_upload(ctx, type, rows, cols, host, nbytes, 0, rows, &w);
-    if (s != ORACLE_CUDA_OK) return s;
-    w->owned_by_cache = true;
-    ctx->resident[key] = w;
-    *out = w;
+    ORACLE_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->stage_w + stage_off, host, nbytes, cudaMemcpyHostToDevice, stream),
+                    "cudaMemcpyAsync(weight)");
+    *dev = ctx->stage_w + stage_off;
     return ORACLE_CUDA_OK;
+}
+
+// Bytes of staging needed for an unregistered span (0 for a registered one).
+uint64_t weight_stage_need(const oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
+                           const void* host, uint64_t nbytes) {
+    if (ctx->resident.count(std::make_tuple(host, nbytes, type, rows, cols))) return 0;
+    return (nbytes + 16 + 15) / 16 * 16;  // +16: aligned word reads stay inside
 }
 
 bool is_pinned(const void* p) {
@@ -542,6 +554,7 @@ oracle_cuda_status oracle_cuda_destroy(oracle_cuda_context* ctx) {
         cudaFree(kv.second->dev);
         delete kv.second;
     }
+    if (ctx->stage_w) cudaFree(ctx->stage_w);
     if (ctx->pin_x) cudaFreeHost(ctx->pin_x);
     if (ctx->pin_y) cudaFreeHost(ctx->pin_y);
     if (ctx->dev_x) cudaFree(ctx->dev_x);
@@ -1162,7 +1175,7 @@ oracle_cuda_status oracle_cuda_weight_upload(oracle_cuda_context* ctx, uint32_t 
 
 oracle_cuda_status oracle_cuda_weight_free(oracle_cuda_weight* w) {
     if (!w) return ORACLE_CUDA_OK;
-    if (w->owned_by_cache) return fail(w->ctx, ORACLE_CUDA_INVALID_ARGUMENT, "resident cache entries are freed by oracle_cuda_evict_resident");
+    if (w->owned_by_cache) return fail(w->ctx, ORACLE_CUDA_INVALID_ARGUMENT, "registered host weights are freed by oracle_cuda_unregister_host_weight or oracle_cuda_evict_resident");
     cudaSetDevice(w->ctx->device);
     cudaFree(w->dev);
     delete w;
@@ -1179,6 +1192,107 @@ oracle_cuda_status oracle_cuda_weight_info(const oracle_cuda_weight* w, uint32_t
     if (dev) *dev = w->dev;
     if (nbytes) *nbytes = w->nbytes;
     return ORACLE_CUDA_OK;
+}
+
+oracle_cuda_status oracle_cuda_register_host_weight(oracle_cuda_context* ctx, uint32_t type, uint64_t rows,
+                                                    uint64_t cols, const void* host, uint64_t nbytes) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    const auto key = std::make_tuple(host, nbytes, type, rows, cols);
+    if (ctx->resident.count(key)) return ok(ctx);
+    oracle_cuda_weight* w = nullptr;
+    oracle_cuda_status s = oracle_cuda_weight_upload(ctx, type, rows, cols, host, nbytes, 0, rows, &w);
+    if (s != ORACLE_CUDA_OK) return s;
+    w->owned_by_cache = true;
+    ctx->resident[key] = w;
+    return ok(ctx);
+}
+
+oracle_cuda_status oracle_cuda_unregister_host_weight(oracle_cuda_context* ctx, const void* host, uint64_t nbytes) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    bool found = false;
+    for (auto it = ctx->resident.begin(); it != ctx->resident.end();) {
+        if (std::get<0>(it->first) == host && std::get<1>(it->first) == nbytes) {
+            if (!found) {
+                cudaSetDevice(ctx->device);
+                cudaDeviceSynchronize();  // no launch may still read the copy
+            }
+            found = true;
+            cudaFree(it->second->dev);
+            delete it->second;
+            it = ctx->resident.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    if (!found) return fail(ctx, ORACLE_CUDA_OUT_OF_RANGE, "host weight span is not registered");
+    return ok(ctx);
+}
+
+oracle_cuda_status oracle_cuda_host_matvec_program(oracle_cuda_context* ctx, const oracle_cuda_host_matvec_op* ops,
+                                                   uint32_t n_ops) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (!ops || n_ops == 0 || n_ops > kProgramMaxOps)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                    "a matvec program holds 1 to " + std::to_string(kProgramMaxOps) + " ops");
+    // layout of the call's device buffers: fed-in x vectors, every y, staged weights
+    int src[kProgramMaxOps];
+    uint64_t x_off[kProgramMaxOps], y_off[kProgramMaxOps], w_off[kProgramMaxOps];
+    uint64_t x_total = 0, y_total = 0, w_total = 0;
+    for (uint32_t k = 0; k < n_ops; ++k) {
+        const oracle_cuda_host_matvec_op& o = ops[k];
+        uint64_t rb = 0, batch = 0;
+        oracle_cuda_status s = validate_matvec(ctx, ORACLE_CUDA_CONTRACT_Q8K, o.type, o.rows, o.cols, o.w_nbytes,
+                                               o.cols, o.rows, &rb, &batch);
+        if (s != ORACLE_CUDA_OK) {
+            ctx->last_error = "op " + std::to_string(k) + ": " + ctx->last_error;
+            return s;
+        }
+        if (!o.w_host || !o.x_host || !o.y_host)
+            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "op " + std::to_string(k) + ": null pointer");
+        src[k] = -1;
+        for (uint32_t j = 0; j < k; ++j)
+            if (ops[j].y_host == o.x_host) src[k] = static_cast<int>(j);
+        if (src[k] >= 0 && ops[src[k]].rows != o.cols)
+            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                        "op " + std::to_string(k) + ": reads op " + std::to_string(src[k]) +
+                            "'s output, whose length is not its column count");
+        x_off[k] = x_total;
+        if (src[k] < 0) x_total += o.cols;
+        y_off[k] = y_total;
+        y_total += o.rows;
+        w_off[k] = w_total;
+        w_total += weight_stage_need(ctx, o.type, o.rows, o.cols, o.w_host, o.w_nbytes);
+    }
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    oracle_cuda_status s = ORACLE_CUDA_OK;
+    if ((x_total && (s = grow_device(ctx, ctx->dev_x, ctx->dev_x_len, x_total)) != ORACLE_CUDA_OK) ||
+        (s = grow_device(ctx, ctx->dev_y, ctx->dev_y_len, y_total)) != ORACLE_CUDA_OK ||
+        (x_total && (s = grow_pinned(ctx, ctx->pin_x, ctx->pin_x_len, x_total)) != ORACLE_CUDA_OK) ||
+        (s = grow_pinned(ctx, ctx->pin_y, ctx->pin_y_len, y_total)) != ORACLE_CUDA_OK ||
+        (w_total && (s = grow_device(ctx, ctx->stage_w, ctx->stage_w_len, w_total)) != ORACLE_CUDA_OK))
+        return s;
+    cudaStream_t st = nullptr;
+    oracle_cuda_matvec_op dops[kProgramMaxOps] = {};
+    for (uint32_t k = 0; k < n_ops; ++k) {
+        const oracle_cuda_host_matvec_op& o = ops[k];
+        const void* wdev = nullptr;
+        if ((s = weight_bytes_for_call(ctx, o.type, o.rows, o.cols, o.w_host, o.w_nbytes, w_off[k], st, &wdev)) !=
+            ORACLE_CUDA_OK)
+            return s;
+        if (src[k] < 0) std::memcpy(ctx->pin_x + x_off[k], o.x_host, o.cols * sizeof(float));
+        dops[k] = oracle_cuda_matvec_op{o.type, src[k] >= 0 ? 1u : 0u, o.rows, o.cols, wdev, o.w_nbytes,
+                                        src[k] >= 0 ? ctx->dev_y + y_off[src[k]] : ctx->dev_x + x_off[k],
+                                        ctx->dev_y + y_off[k]};
+    }
+    if (x_total)
+        ORACLE_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->dev_x, ctx->pin_x, x_total * sizeof(float), cudaMemcpyHostToDevice, st),
+                        "cudaMemcpyAsync(x)");
+    if ((s = program_run_base(ctx, dops, n_ops, st, nullptr)) != ORACLE_CUDA_OK) return s;
+    ORACLE_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->pin_y, ctx->dev_y, y_total * sizeof(float), cudaMemcpyDeviceToHost, st),
+                    "cudaMemcpyAsync(y)");
+    ORACLE_CUDA_TRY(ctx, cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    for (uint32_t k = 0; k < n_ops; ++k) std::memcpy(ops[k].y_host, ctx->pin_y + y_off[k], ops[k].rows * sizeof(float));
+    return ok(ctx);
 }
 
 oracle_cuda_status oracle_cuda_evict_resident(oracle_cuda_context* ctx) {
@@ -1203,8 +1317,11 @@ oracle_cuda_status oracle_cuda_host_storage_matvec(oracle_cuda_context* ctx, int
     if (s != ORACLE_CUDA_OK) return s;
     if (!w_host || !x_host || !y_host) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "null pointer");
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
-    oracle_cuda_weight* w = nullptr;
-    if ((s = resident_weight(ctx, type, rows, cols, w_host, w_nbytes, &w)) != ORACLE_CUDA_OK) return s;
+    cudaStream_t st = nullptr;
+    const uint64_t need = weight_stage_need(ctx, type, rows, cols, w_host, w_nbytes);
+    if (need && (s = grow_device(ctx, ctx->stage_w, ctx->stage_w_len, need)) != ORACLE_CUDA_OK) return s;
+    const void* wdev = nullptr;
+    if ((s = weight_bytes_for_call(ctx, type, rows, cols, w_host, w_nbytes, 0, st, &wdev)) != ORACLE_CUDA_OK) return s;
     if ((s = grow_device(ctx, ctx->dev_x, ctx->dev_x_len, x_len)) != ORACLE_CUDA_OK) return s;
     if ((s = grow_device(ctx, ctx->dev_y, ctx->dev_y_len, y_len)) != ORACLE_CUDA_OK) return s;
     const bool x_pinned = is_pinned(x_host), y_pinned = is_pinned(y_host);
@@ -1219,10 +1336,9 @@ oracle_cuda_status oracle_cuda_host_storage_matvec(oracle_cuda_context* ctx, int
         if ((s = grow_pinned(ctx, ctx->pin_y, ctx->pin_y_len, y_len)) != ORACLE_CUDA_OK) return s;
         ydst = ctx->pin_y;
     }
-    cudaStream_t st = nullptr;
     ORACLE_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->dev_x, xsrc, x_len * sizeof(float), cudaMemcpyHostToDevice, st),
                     "cudaMemcpyAsync(x)");
-    s = run_matvec(ctx, contract, type, rows, cols, rb, w->dev, ctx->dev_x, batch, ctx->dev_y, st);
+    s = run_matvec(ctx, contract, type, rows, cols, rb, wdev, ctx->dev_x, batch, ctx->dev_y, st);
     if (s != ORACLE_CUDA_OK) return s;
     ORACLE_CUDA_TRY(ctx, cudaMemcpyAsync(ydst, ctx->dev_y, y_len * sizeof(float), cudaMemcpyDeviceToHost, st),
                     "cudaMemcpyAsync(y)");
@@ -1262,11 +1378,14 @@ oracle_cuda_status oracle_cuda_host_decode_rows(oracle_cuda_context* ctx, uint32
         return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "mapped tensor decode output length mismatch");
     if (!w_host || !out_host) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "null pointer");
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
-    oracle_cuda_weight* w = nullptr;
-    oracle_cuda_status s = resident_weight(ctx, type, rows, cols, w_host, w_nbytes, &w);
-    if (s != ORACLE_CUDA_OK) return s;
+    oracle_cuda_status s = ORACLE_CUDA_OK;
+    const uint64_t need = weight_stage_need(ctx, type, rows, cols, w_host, w_nbytes);
+    if (need && (s = grow_device(ctx, ctx->stage_w, ctx->stage_w_len, need)) != ORACLE_CUDA_OK) return s;
+    const void* wdev = nullptr;
+    if ((s = weight_bytes_for_call(ctx, type, rows, cols, w_host, w_nbytes, 0, nullptr, &wdev)) != ORACLE_CUDA_OK)
+        return s;
     if ((s = grow_device(ctx, ctx->dev_y, ctx->dev_y_len, out_len)) != ORACLE_CUDA_OK) return s;
-    s = launch_decode(ctx, type, w->dev, rows, cols, rb, ctx->dev_y, nullptr);
+    s = launch_decode(ctx, type, wdev, rows, cols, rb, ctx->dev_y, nullptr);
     if (s != ORACLE_CUDA_OK) return s;
     ORACLE_CUDA_TRY(ctx, cudaMemcpy(out_host, ctx->dev_y, out_len * sizeof(float), cudaMemcpyDeviceToHost),
                     "cudaMemcpy(out)");

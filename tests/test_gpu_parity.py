@@ -222,8 +222,81 @@ def test_host_q8k_matches_device(ctx, port):
     x = synth.activations(k, 1, "gpu", "host_q8k_x")
     got = ctx.host_storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, rows, k, w, x)
     assert bits_equal(got, port.matvec_q8_k(ob.TYPE_Q4_K, rows, k, w, port.quantize_q8_k(x))[0])
-    got2 = ctx.host_storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, rows, k, w, x)  # resident copy reused
+    ctx.register_host_weight(ob.TYPE_Q4_K, rows, k, w)
+    try:
+        got2 = ctx.host_storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, rows, k, w, x)  # the resident copy
+    finally:
+        ctx.unregister_host_weight(w)
     assert bits_equal(got, got2)
+
+
+def test_host_buffer_reused_with_new_bytes(ctx, port):
+    """The host-pointer calls read the caller's bytes on every call, as the
+    reference does: a buffer refilled with other weights at the same address
+    gives the new result.  A registered span is read from its resident copy
+    (the caller promised it would not change) until it is unregistered."""
+    rows, k = 96, 4096
+    a = synth.weight(ob.TYPE_Q4_K, rows, k, "gpu", "reuse_a")
+    b = synth.weight(ob.TYPE_Q4_K, rows, k, "gpu", "reuse_b")
+    x = synth.activations(k, 1, "gpu", "reuse_x")
+    q = port.quantize_q8_k(x)
+    want_a = port.matvec_q8_k(ob.TYPE_Q4_K, rows, k, a, q)[0]
+    want_b = port.matvec_q8_k(ob.TYPE_Q4_K, rows, k, b, q)[0]
+    buf = a.copy()
+    assert bits_equal(ctx.host_storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, rows, k, buf, x), want_a)
+    buf[...] = b
+    assert bits_equal(ctx.host_storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, rows, k, buf, x), want_b)
+    # storage_dot on a row rebuilt at the same address (the reference's tests
+    # build rows on the stack) sees the new row too
+    row = a[0].copy()
+    d0 = ctx.host_storage_dot(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, k, row, x)
+    row[...] = b[0]
+    assert ctx.host_storage_dot(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, k, row, x) == want_b[0] and d0 == want_a[0]
+    # registered: the resident copy, until unregistered
+    ctx.register_host_weight(ob.TYPE_Q4_K, rows, k, buf)
+    buf[...] = a
+    assert bits_equal(ctx.host_storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, rows, k, buf, x), want_b)
+    ctx.unregister_host_weight(buf)
+    assert bits_equal(ctx.host_storage_matvec(ob.CONTRACT_Q8K, ob.TYPE_Q4_K, rows, k, buf, x), want_a)
+    with pytest.raises(ob.OutOfRange, match="not registered"):
+        ctx.unregister_host_weight(buf)
+
+
+def test_host_matvec_program(ctx, port):
+    """oracle_cuda_host_matvec_program: host spans in and out, one launch and
+    one synchronize; an op fed by an earlier op's output (the same host array)
+    reads it on the device.  Bit-identical to the restatement, registered or
+    not."""
+    specs = [(ob.TYPE_Q4_K, 700, 4096), (ob.TYPE_Q6_K, 300, 4096)]
+    ws = [synth.weight(t, n, k, "gpu", f"hostprog{i}") for i, (t, n, k) in enumerate(specs)]
+    x0 = synth.activations(4096, 1, "gpu", "hostprog_x")[0]
+    ys = [np.full(n, np.nan, np.float32) for _, n, _ in specs]
+    # two independent ops on x0, then a 512-row op whose whole output feeds a
+    # dependent op (a dependent op reads an earlier op's whole output)
+    ops = [(specs[0][0], 700, 4096, ws[0], x0, ys[0]), (specs[1][0], 300, 4096, ws[1], x0, ys[1])]
+    wdep = synth.weight(ob.TYPE_Q4_K, 128, 512, "gpu", "hostprog_dep")
+    wsrc = synth.weight(ob.TYPE_Q4_K, 512, 4096, "gpu", "hostprog_src")
+    ysrc = np.full(512, np.nan, np.float32)
+    ydep = np.full(128, np.nan, np.float32)
+    ops += [(ob.TYPE_Q4_K, 512, 4096, wsrc, x0, ysrc), (ob.TYPE_Q4_K, 128, 512, wdep, ysrc, ydep)]
+    q0 = port.quantize_q8_k(x0)
+    want0 = port.matvec_q8_k(ob.TYPE_Q4_K, 700, 4096, ws[0], q0)[0]
+    want1 = port.matvec_q8_k(ob.TYPE_Q6_K, 300, 4096, ws[1], q0)[0]
+    wantsrc = port.matvec_q8_k(ob.TYPE_Q4_K, 512, 4096, wsrc, q0)[0]
+    wantdep = port.matvec_q8_k(ob.TYPE_Q4_K, 128, 512, wdep, port.quantize_q8_k(wantsrc))[0]
+    for registered in (False, True):
+        if registered:
+            for t, n, k, w, _, _ in ops:
+                ctx.register_host_weight(t, n, k, w)
+        for y in (ys[0], ys[1], ysrc, ydep):
+            y.fill(np.nan)
+        ctx.host_matvec_program(ops)
+        assert bits_equal(ys[0], want0) and bits_equal(ys[1], want1)
+        assert bits_equal(ysrc, wantsrc) and bits_equal(ydep, wantdep)
+    ctx.evict_resident()
+    with pytest.raises(ob.InvalidArgument, match="op 1: reads op 0's output"):
+        ctx.host_matvec_program([(ob.TYPE_Q4_K, 700, 4096, ws[0], x0, ys[0]),
+                                 (ob.TYPE_Q4_K, 128, 512, wdep, ys[0], ydep)])
 
 
 # ---------------------------------------------------------------- errors: same class and message as the reference
