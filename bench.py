@@ -633,12 +633,16 @@ def gpu_arm(args, wl: Workload) -> None:
             for (t, k, n), w in zip(wl.ops, wset):
                 ctx.register_host_weight(t, n, k, w)
         if wl.contract == CONTRACT_Q8K:
-            def e2e_step(s=0):
-                wset = ws_host[s % wl.pool_sets]
-                ctx.host_matvec_program([(t, n, k, wset[i], x_np[i], y_np[i]) for i, (t, k, n) in enumerate(wl.ops)])
+            host_steps = [ctx.prepare_host_program([(t, n, k, wset[i], x_np[i], y_np[i])
+                                                    for i, (t, k, n) in enumerate(wl.ops)])
+                          for wset in ws_host]
 
-            e2e_how = ("oracle_cuda_host_matvec_program: the step's matvecs in one call (pinned host x in, y out, "
-                       "one launch, one synchronize), registered weights rotating over the pool's sets; wall clock "
+            def e2e_step(s=0):
+                host_steps[s % wl.pool_sets]()
+
+            e2e_how = ("oracle_cuda_host_program_run: the step's matvecs prepared once per weight set "
+                       "(oracle_cuda_host_program_create, registered weights rotating over the pool's sets), each "
+                       "call copying pinned host x in and y out around one launch and one synchronize; wall clock "
                        "over synchronous calls")
         else:
             def e2e_step(s=0):

@@ -561,6 +561,25 @@ typedef struct oracle_cuda_host_matvec_op {
 oracle_cuda_status oracle_cuda_host_matvec_program(oracle_cuda_context* ctx, const oracle_cuda_host_matvec_op* ops,
                                                    uint32_t n_ops);
 
+/* The same call prepared once for a caller that repeats it (a decode step
+ * over the same buffers): the op list is validated and planned, and the
+ * copy-in, the program launch and the copy-out are captured into one CUDA
+ * graph on a stream of the prepared call's own.  Every weight must be
+ * registered (INVALID_ARGUMENT otherwise); x and y stay the caller's arrays,
+ * read and written at each run.  When every x and y is page-locked host
+ * memory mapped for the device (cudaHostAlloc, cudaHostRegister) two small
+ * kernels of the graph read x and write y there in place; otherwise the run
+ * copies them through page-locked buffers the prepared call owns.  run() is
+ * synchronous and gives exactly what
+ * oracle_cuda_host_matvec_program gives for the arrays' current contents.
+ * The context must outlive the prepared call.  No counterpart in the
+ * reference. */
+typedef struct oracle_cuda_host_program oracle_cuda_host_program;
+oracle_cuda_status oracle_cuda_host_program_create(oracle_cuda_context* ctx, const oracle_cuda_host_matvec_op* ops,
+                                                   uint32_t n_ops, oracle_cuda_host_program** out);
+oracle_cuda_status oracle_cuda_host_program_run(oracle_cuda_host_program* program);
+oracle_cuda_status oracle_cuda_host_program_destroy(oracle_cuda_host_program* program);
+
 #ifdef __cplusplus
 }
 #endif

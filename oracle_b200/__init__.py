@@ -181,6 +181,9 @@ class HostMatvecOp(C.Structure):
 
 
 _proto("oracle_cuda_host_matvec_program", [_vp, C.POINTER(HostMatvecOp), _u32])
+_proto("oracle_cuda_host_program_create", [_vp, C.POINTER(HostMatvecOp), _u32, C.POINTER(_vp)])
+_proto("oracle_cuda_host_program_run", [_vp])
+_proto("oracle_cuda_host_program_destroy", [_vp])
 _proto("oracle_cuda_prefill_gemm", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _vp])
 _proto("oracle_cuda_peer_group_create", [_vp, _u32, _u32, _u64, C.POINTER(_vp), _vp])
 _proto("oracle_cuda_peer_group_connect", [_vp, _vp])
@@ -683,10 +686,70 @@ class Context:
         with host numpy arrays (uint8 weights, f32 x and y); an op whose x is
         an earlier op's y (the same array) reads that result on the device.
         One launch, one synchronize; y arrays are filled in place."""
-        arr = (HostMatvecOp * len(ops))()
-        for i, (qtype, rows, cols, w, x, y) in enumerate(ops):
-            for a, dt in ((w, np.uint8), (x, np.float32), (y, np.float32)):
-                if not (a.flags.c_contiguous and a.dtype == dt):
-                    raise InvalidArgument(f"op {i}: host arrays must be C-contiguous {np.dtype(dt).name}")
-            arr[i] = HostMatvecOp(qtype, rows, cols, w.ctypes.data, w.nbytes, x.ctypes.data, y.ctypes.data)
-        self._check(_lib.oracle_cuda_host_matvec_program(self._h, arr, len(ops)))
+        self.host_program(ops)()
+
+    def prepare_host_program(self, ops) -> "PreparedHostProgram":
+        """oracle_cuda_host_program_create: the op list of
+        :meth:`host_matvec_program` planned and captured once (every weight
+        registered); call the result to run it on the arrays' contents."""
+        return PreparedHostProgram(self, ops)
+
+    def host_program(self, ops) -> "HostProgram":
+        """The op list of :meth:`host_matvec_program` marshalled once; calling
+        the result runs oracle_cuda_host_matvec_program on the arrays' current
+        contents (a caller that repeats a step pays only the C call)."""
+        return HostProgram(self, ops)
+
+
+def _host_ops(ops):
+    arr = (HostMatvecOp * len(ops))()
+    for i, (qtype, rows, cols, w, x, y) in enumerate(ops):
+        for a, dt in ((w, np.uint8), (x, np.float32), (y, np.float32)):
+            if not (a.flags.c_contiguous and a.dtype == dt):
+                raise InvalidArgument(f"op {i}: host arrays must be C-contiguous {np.dtype(dt).name}")
+        arr[i] = HostMatvecOp(qtype, rows, cols, w.ctypes.data, w.nbytes, x.ctypes.data, y.ctypes.data)
+    return arr
+
+
+class HostProgram:
+    """An oracle_cuda_host_matvec_program op list marshalled once (see
+    :meth:`Context.host_program`).  Keeps the arrays alive."""
+
+    def __init__(self, ctx: "Context", ops):
+        self._ctx = ctx
+        self._keep = list(ops)
+        self._arr = _host_ops(ops)
+        self._n = len(ops)
+        self._fn = _lib.oracle_cuda_host_matvec_program
+
+    def __call__(self) -> None:
+        self._ctx._check(self._fn(self._ctx._h, self._arr, self._n))
+
+
+class PreparedHostProgram:
+    """oracle_cuda_host_program_create / _run / _destroy: the host program
+    planned and captured once (every weight registered); each call copies
+    the arrays' current x in and y out around one graph replay."""
+
+    def __init__(self, ctx: "Context", ops):
+        self._ctx = ctx
+        self._keep = list(ops)
+        arr = _host_ops(ops)
+        h = C.c_void_p()
+        ctx._check(_lib.oracle_cuda_host_program_create(ctx._h, arr, len(ops), C.byref(h)))
+        self._h = h.value
+        self._run = _lib.oracle_cuda_host_program_run
+
+    def __call__(self) -> None:
+        self._ctx._check(self._run(self._h))
+
+    def close(self) -> None:
+        if self._h:
+            _lib.oracle_cuda_host_program_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -431,6 +431,17 @@ uint64_t weight_stage_need(const oracle_cuda_context* ctx, uint32_t type, uint64
     return (nbytes + 16 + 15) / 16 * 16;  // +16: aligned word reads stay inside
 }
 
+// Page-locked host memory the device reaches at the same address (unified
+// addressing maps cudaHostAlloc'd and registered memory so).
+bool is_device_mapped_host(const void* p) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return attr.type == cudaMemoryTypeHost && attr.devicePointer == p;
+}
+
 bool is_pinned(const void* p) {
     cudaPointerAttributes attr{};
     if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
@@ -1287,12 +1298,216 @@ oracle_cuda_status oracle_cuda_host_matvec_program(oracle_cuda_context* ctx, con
     if (x_total)
         ORACLE_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->dev_x, ctx->pin_x, x_total * sizeof(float), cudaMemcpyHostToDevice, st),
                         "cudaMemcpyAsync(x)");
-    if ((s = program_run_base(ctx, dops, n_ops, st, nullptr)) != ORACLE_CUDA_OK) return s;
+    // a synchronous call pays every launch's latency: the program quantizes
+    // its activations itself (no quantizer launch before it)
+    const uint32_t saved_flags = ctx->flags;
+    ctx->flags |= ORACLE_CUDA_FLAG_BUILD_IN_KERNEL;
+    s = program_run_base(ctx, dops, n_ops, st, nullptr);
+    ctx->flags = saved_flags;
+    if (s != ORACLE_CUDA_OK) return s;
     ORACLE_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->pin_y, ctx->dev_y, y_total * sizeof(float), cudaMemcpyDeviceToHost, st),
                     "cudaMemcpyAsync(y)");
     ORACLE_CUDA_TRY(ctx, cudaStreamSynchronize(st), "cudaStreamSynchronize");
     for (uint32_t k = 0; k < n_ops; ++k) std::memcpy(ops[k].y_host, ctx->pin_y + y_off[k], ops[k].rows * sizeof(float));
     return ok(ctx);
+}
+
+}  // extern "C"
+
+// Copies between page-locked host arrays (device-mapped) and device buffers
+// for prepared host programs: one launch moves every op's vector, so the
+// captured graph holds no copy-engine transfers (each costs microseconds of
+// latency for a few kilobytes).
+struct HostCopies {
+    const float* src[kProgramMaxOps];
+    float* dst[kProgramMaxOps];
+    uint32_t n[kProgramMaxOps];
+    uint32_t count;
+    uint32_t wait_previous;  // 1: griddepcontrol.wait first (y after the program)
+};
+
+__global__ void __launch_bounds__(256) host_copies_kernel(const __grid_constant__ HostCopies c) {
+    pdl_launch_dependents();
+    if (c.wait_previous) pdl_wait();
+    for (uint32_t k = 0; k < c.count; ++k) {
+        const float* src = c.src[k];
+        float* dst = c.dst[k];
+        for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < c.n[k]; i += gridDim.x * blockDim.x)
+            dst[i] = src[i];
+    }
+}
+
+struct oracle_cuda_host_program {
+    oracle_cuda_context* ctx = nullptr;
+    uint32_t n_ops = 0;
+    oracle_cuda_host_matvec_op ops[kProgramMaxOps] = {};
+    int src[kProgramMaxOps] = {};
+    uint64_t x_off[kProgramMaxOps] = {}, y_off[kProgramMaxOps] = {};
+    uint64_t x_total = 0, y_total = 0;
+    bool direct = false;  // every x and y is device-mapped page-locked memory: read and written in place
+    float* pin_x = nullptr;
+    float* pin_y = nullptr;
+    float* dev_x = nullptr;
+    float* dev_y = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
+namespace {
+
+void host_program_free(oracle_cuda_host_program* p) {
+    if (!p) return;
+    if (p->ctx) cudaSetDevice(p->ctx->device);
+    if (p->stream) cudaStreamSynchronize(p->stream);
+    if (p->exec) cudaGraphExecDestroy(p->exec);
+    if (p->graph) cudaGraphDestroy(p->graph);
+    if (p->stream) cudaStreamDestroy(p->stream);
+    if (p->pin_x) cudaFreeHost(p->pin_x);
+    if (p->pin_y) cudaFreeHost(p->pin_y);
+    if (p->dev_x) cudaFree(p->dev_x);
+    if (p->dev_y) cudaFree(p->dev_y);
+    delete p;
+}
+
+}  // namespace
+
+extern "C" {
+
+oracle_cuda_status oracle_cuda_host_program_create(oracle_cuda_context* ctx, const oracle_cuda_host_matvec_op* ops,
+                                                   uint32_t n_ops, oracle_cuda_host_program** out) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (!out) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "output pointer is null");
+    *out = nullptr;
+    if (!ops || n_ops == 0 || n_ops > kProgramMaxOps)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                    "a matvec program holds 1 to " + std::to_string(kProgramMaxOps) + " ops");
+    auto* p = new oracle_cuda_host_program();
+    p->ctx = ctx;
+    p->n_ops = n_ops;
+    const void* wdev[kProgramMaxOps];
+    bool pinned = true;
+    for (uint32_t k = 0; k < n_ops; ++k) {
+        const oracle_cuda_host_matvec_op& o = ops[k];
+        p->ops[k] = o;
+        uint64_t rb = 0, batch = 0;
+        oracle_cuda_status s = validate_matvec(ctx, ORACLE_CUDA_CONTRACT_Q8K, o.type, o.rows, o.cols, o.w_nbytes,
+                                               o.cols, o.rows, &rb, &batch);
+        if (s != ORACLE_CUDA_OK) {
+            ctx->last_error = "op " + std::to_string(k) + ": " + ctx->last_error;
+            host_program_free(p);
+            return s;
+        }
+        if (!o.w_host || !o.x_host || !o.y_host) {
+            host_program_free(p);
+            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "op " + std::to_string(k) + ": null pointer");
+        }
+        auto it = ctx->resident.find(std::make_tuple(o.w_host, o.w_nbytes, o.type, o.rows, o.cols));
+        if (it == ctx->resident.end()) {
+            host_program_free(p);
+            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                        "op " + std::to_string(k) + ": a prepared host program needs registered weights");
+        }
+        wdev[k] = it->second->dev;
+        p->src[k] = -1;
+        for (uint32_t j = 0; j < k; ++j)
+            if (ops[j].y_host == o.x_host) p->src[k] = static_cast<int>(j);
+        if (p->src[k] >= 0 && ops[p->src[k]].rows != o.cols) {
+            host_program_free(p);
+            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                        "op " + std::to_string(k) + ": reads op " + std::to_string(p->src[k]) +
+                            "'s output, whose length is not its column count");
+        }
+        p->x_off[k] = p->x_total;
+        if (p->src[k] < 0) {
+            p->x_total += o.cols;
+            pinned = pinned && is_device_mapped_host(o.x_host);
+        }
+        p->y_off[k] = p->y_total;
+        p->y_total += o.rows;
+        pinned = pinned && is_device_mapped_host(o.y_host);
+    }
+    p->direct = pinned;
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e == cudaSuccess && p->x_total) e = cudaMalloc(reinterpret_cast<void**>(&p->dev_x), p->x_total * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&p->dev_y), p->y_total * sizeof(float));
+    if (e == cudaSuccess && !p->direct && p->x_total)
+        e = cudaHostAlloc(reinterpret_cast<void**>(&p->pin_x), p->x_total * sizeof(float), cudaHostAllocDefault);
+    if (e == cudaSuccess && !p->direct)
+        e = cudaHostAlloc(reinterpret_cast<void**>(&p->pin_y), p->y_total * sizeof(float), cudaHostAllocDefault);
+    if (e == cudaSuccess) e = cudaStreamCreate(&p->stream);
+    if (e != cudaSuccess) {
+        host_program_free(p);
+        return cuda_fail(ctx, e, "prepared host program buffers");
+    }
+    oracle_cuda_matvec_op dops[kProgramMaxOps] = {};
+    for (uint32_t k = 0; k < n_ops; ++k) {
+        const oracle_cuda_host_matvec_op& o = ops[k];
+        dops[k] = oracle_cuda_matvec_op{o.type, p->src[k] >= 0 ? 1u : 0u, o.rows, o.cols, wdev[k], o.w_nbytes,
+                                        p->src[k] >= 0 ? p->dev_y + p->y_off[p->src[k]] : p->dev_x + p->x_off[k],
+                                        p->dev_y + p->y_off[k]};
+    }
+    // capture: x in, the program (quantizing its activations in the kernel), y out
+    oracle_cuda_status s = ORACLE_CUDA_OK;
+    HostCopies xin{}, yout{};
+    for (uint32_t k = 0; k < n_ops; ++k) {
+        if (p->src[k] < 0) {
+            xin.src[xin.count] = p->direct ? ops[k].x_host : p->pin_x + p->x_off[k];
+            xin.dst[xin.count] = p->dev_x + p->x_off[k];
+            xin.n[xin.count++] = static_cast<uint32_t>(ops[k].cols);
+        }
+        yout.src[yout.count] = p->dev_y + p->y_off[k];
+        yout.dst[yout.count] = p->direct ? ops[k].y_host : p->pin_y + p->y_off[k];
+        yout.n[yout.count++] = static_cast<uint32_t>(ops[k].rows);
+    }
+    yout.wait_previous = 1;
+    e = cudaStreamBeginCapture(p->stream, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+        // x in, the program (quantizing its activations in the kernel; its
+        // weight stream starts beside the copy), y out after it
+        if (xin.count) s = launch(ctx, host_copies_kernel, dim3(16), dim3(256), 0, p->stream, false, xin);
+        if (s == ORACLE_CUDA_OK) {
+            const uint32_t saved_flags = ctx->flags;
+            ctx->flags |= ORACLE_CUDA_FLAG_BUILD_IN_KERNEL | ORACLE_CUDA_FLAG_PDL;
+            s = program_run_base(ctx, dops, n_ops, p->stream, nullptr);
+            ctx->flags = saved_flags;
+        }
+        if (s == ORACLE_CUDA_OK) s = launch(ctx, host_copies_kernel, dim3(16), dim3(256), 0, p->stream, true, yout);
+        const cudaError_t e2 = cudaStreamEndCapture(p->stream, &p->graph);
+        if (e == cudaSuccess) e = e2;
+    }
+    if (e == cudaSuccess && s == ORACLE_CUDA_OK) e = cudaGraphInstantiate(&p->exec, p->graph, 0);
+    if (s != ORACLE_CUDA_OK || e != cudaSuccess) {
+        const std::string msg = ctx->last_error;
+        host_program_free(p);
+        cudaGetLastError();
+        if (s != ORACLE_CUDA_OK) return fail(ctx, s, msg);
+        return cuda_fail(ctx, e, "prepared host program capture");
+    }
+    *out = p;
+    return ok(ctx);
+}
+
+oracle_cuda_status oracle_cuda_host_program_run(oracle_cuda_host_program* p) {
+    if (!p) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "prepared host program is null");
+    oracle_cuda_context* ctx = p->ctx;
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (!p->direct)
+        for (uint32_t k = 0; k < p->n_ops; ++k)
+            if (p->src[k] < 0)
+                std::memcpy(p->pin_x + p->x_off[k], p->ops[k].x_host, p->ops[k].cols * sizeof(float));
+    ORACLE_CUDA_TRY(ctx, cudaGraphLaunch(p->exec, p->stream), "cudaGraphLaunch");
+    ORACLE_CUDA_TRY(ctx, cudaStreamSynchronize(p->stream), "cudaStreamSynchronize");
+    ctx->launches += 1;
+    if (!p->direct)
+        for (uint32_t k = 0; k < p->n_ops; ++k)
+            std::memcpy(p->ops[k].y_host, p->pin_y + p->y_off[k], p->ops[k].rows * sizeof(float));
+    return ok(ctx);
+}
+
+oracle_cuda_status oracle_cuda_host_program_destroy(oracle_cuda_host_program* p) {
+    host_program_free(p);
+    return ORACLE_CUDA_OK;
 }
 
 oracle_cuda_status oracle_cuda_evict_resident(oracle_cuda_context* ctx) {

@@ -293,7 +293,29 @@ def test_host_matvec_program(ctx, port):
         ctx.host_matvec_program(ops)
         assert bits_equal(ys[0], want0) and bits_equal(ys[1], want1)
         assert bits_equal(ysrc, wantsrc) and bits_equal(ydep, wantdep)
+        # prepared once (registered weights only), run twice on changing x
+        if registered:
+            import torch
+            for pinned in (False, True):
+                xin = torch.from_numpy(x0.copy()).pin_memory().numpy() if pinned else x0.copy()
+                outs = [torch.empty(n, dtype=torch.float32).pin_memory().numpy() if pinned else
+                        np.empty(n, np.float32) for n in (700, 300, 512, 128)]
+                prep = ctx.prepare_host_program([(t, n, k, w, xin if i < 3 else outs[2], outs[i])
+                                                 for i, (t, n, k, w, _, _) in enumerate(ops)])
+                for rep in range(2):
+                    for o in outs:
+                        o.fill(np.nan)
+                    prep()
+                    assert bits_equal(outs[0], want0) and bits_equal(outs[1], want1)
+                    assert bits_equal(outs[2], wantsrc) and bits_equal(outs[3], wantdep)
+                xin[:] = x0[::-1]
+                prep()
+                q1 = port.quantize_q8_k(x0[::-1].copy())
+                assert bits_equal(outs[0], port.matvec_q8_k(ob.TYPE_Q4_K, 700, 4096, ws[0], q1)[0])
+                prep.close()
     ctx.evict_resident()
+    with pytest.raises(ob.InvalidArgument, match="needs registered weights"):
+        ctx.prepare_host_program(ops)
     with pytest.raises(ob.InvalidArgument, match="op 1: reads op 0's output"):
         ctx.host_matvec_program([(ob.TYPE_Q4_K, 700, 4096, ws[0], x0, ys[0]),
                                  (ob.TYPE_Q4_K, 128, 512, wdep, ys[0], ydep)])
