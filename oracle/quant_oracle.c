@@ -325,13 +325,20 @@ static float kq_block_partial(uint32_t type, const uint8_t* w, const uint8_t* q8
 float oq_vec_dot_q8_k(uint32_t type, uint64_t k, const uint8_t* wrow, const uint8_t* q8row) {
     int bb = kq_block_bytes(type);
     if (!bb || k == 0 || k % 256) return NAN;
-    float slot[32];
-    for (int s = 0; s < 32; ++s) slot[s] = 0.0f;
-    for (uint64_t i = 0; i < k / 256; ++i)
-        slot[i % 32] += kq_block_partial(type, wrow + (uint64_t)bb * i, q8row + 292 * i);
-    for (int stride = 16; stride >= 1; stride /= 2)
-        for (int s = 0; s < stride; ++s) slot[s] += slot[s + stride];
-    return slot[0];
+    const uint64_t nb = k / 256;
+    float total = 0.0f;
+    for (uint64_t g = 0; g * 16 < nb; ++g) {
+        float leaf[16];
+        for (int j = 0; j < 16; ++j) {
+            const uint64_t i = 16 * g + (uint64_t)j;
+            leaf[j] = 0.0f;
+            if (i < nb) leaf[j] += kq_block_partial(type, wrow + (uint64_t)bb * i, q8row + 292 * i);
+        }
+        for (int stride = 8; stride >= 1; stride /= 2)
+            for (int s = 0; s < stride; ++s) leaf[s] += leaf[s + stride];
+        total += leaf[0];
+    }
+    return total;
 }
 
 /* GGML generic order: per super-block, 8 interleaved int32 partial sums of

@@ -80,8 +80,12 @@ void oq_block_sums_q6_k(const uint8_t* wblock, const uint8_t* q8block, int32_t* 
 
 /* Row dot against Q8_K activations in this build's canonical f32 order:
  *   p_i   = (d_w * d_x) * (float)isum_i - (dmin_w * d_x) * (float)msum_i
- *   slot[i % 32] += p_i   (increasing i, slots start at +0.0f)
- *   for stride in 16, 8, 4, 2, 1: slot[s] += slot[s + stride] for s < stride
+ *   per 16-super-block segment g: leaf[j] = 0.0f + p_{16g+j} (+0.0f past the
+ *   row's end); for stride in 8, 4, 2, 1: leaf[s] += leaf[s + stride] for
+ *   s < stride; seg_g = leaf[0]
+ *   total = ((0.0f + seg_0) + seg_1) + ...   (increasing g)
+ * A fixed tree inside a segment (lanes of a warp, or the super-blocks of a
+ * stage), a running sum across segments (stages streamed in order).
  * Types: q4_K, q6_K. */
 float oq_vec_dot_q8_k(uint32_t type, uint64_t k, const uint8_t* wrow, const uint8_t* q8row);
 

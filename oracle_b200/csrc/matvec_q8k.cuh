@@ -7,16 +7,17 @@
 //         p_i  = (d_w * d_x) * isum - (dmin_w * d_x) * msum
 //   Q6_K: isum = sum_s sc_s * (sum_16(q6 * q8) - 32 * bsum_s),  p_i = (d_w * d_x) * isum
 // The integer sums are exact (dp4a).  The f32 sum over i is this build's
-// canonical order: slot[i % 32] accumulates p_i in increasing i, then slots
-// fold by strides 16, 8, 4, 2, 1.  The CPU restatement (oq_vec_dot_q8_k)
+// canonical order: per 16-super-block segment, leaves 0 + p_i folded by a
+// fixed tree (strides 8, 4, 2, 1), then a running sum of the segments in
+// increasing order, starting from +0.  The CPU restatement (oq_vec_dot_q8_k)
 // performs the same f32 operations, so results match bit for bit.
 //
 // Work mapping (one warp per row): lane = 2*j + part.  Pass k covers
-// super-blocks 16k..16k+15; lane (j, part) takes super-block 16k + j and the
-// half `part` of its 256 elements (Q4_K: 64-element groups 2*part, 2*part+1;
-// Q6_K: half part).  The two lanes of a pair add their integer sums with one
-// shuffle; slot[j] and slot[j + 16] live in the pair's two accumulators, and
-// the stride-8..1 folds are xor-16..2 lane shuffles.
+// super-blocks 16k..16k+15 (segment k); lane (j, part) takes super-block
+// 16k + j and the half `part` of its 256 elements (Q4_K: 64-element groups
+// 2*part, 2*part+1; Q6_K: half part).  The two lanes of a pair add their
+// integer sums with one shuffle; the segment's tree is the xor-16..2 lane
+// butterfly, and each lane keeps the running sum of the segments.
 //
 // The activation is quantized once per CTA into a shared-memory image
 // (q8k.cuh).  For rows of at most 16 super-blocks the lane's slice of it (32
@@ -175,7 +176,7 @@ __device__ __forceinline__ float q8k_row_dot(uint32_t nb, const ActImage& img, c
     const int j = lane >> 1, part = lane & 1;
     constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
     const uint32_t passes = kXReg ? 1u : (nb + 15u) / 16u;
-    float acc0 = 0.0f, acc1 = 0.0f;
+    float total = 0.0f;
 #pragma unroll kUnroll
     for (uint32_t k = 0; k < passes; ++k) {
         const uint32_t i = 16u * k + j;
@@ -202,6 +203,7 @@ __device__ __forceinline__ float q8k_row_dot(uint32_t nb, const ActImage& img, c
         }
         isum += __shfl_xor_sync(0xFFFFFFFFu, isum, 1);
         if (kType == 12) msum += __shfl_xor_sync(0xFFFFFFFFu, msum, 1);
+        float leaf = 0.0f;
         if (active) {
             const float dd = __fmul_rn(dw, dx);
             float pi = __fmul_rn(dd, __int2float_rn(isum));
@@ -209,15 +211,25 @@ __device__ __forceinline__ float q8k_row_dot(uint32_t nb, const ActImage& img, c
                 const float dm = __fmul_rn(dmw, dx);
                 pi = __fsub_rn(pi, __fmul_rn(dm, __int2float_rn(msum)));
             }
-            if (k & 1)
-                acc1 = __fadd_rn(acc1, pi);
-            else
-                acc0 = __fadd_rn(acc0, pi);
+            leaf = __fadd_rn(leaf, pi);
         }
-    }
-    float v = __fadd_rn(acc0, acc1);
 #pragma unroll
-    for (int off = 16; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+        for (int off = 16; off >= 2; off >>= 1) leaf = __fadd_rn(leaf, __shfl_xor_sync(0xFFFFFFFFu, leaf, off));
+        total = __fadd_rn(total, leaf);
+    }
+    return total;
+}
+
+// One segment's tree for two rows at once: leaves la (row A) and lb (row B)
+// on lanes 2j + part (both lanes of a pair hold the same leaf), the two
+// trees sharing their first level (lanes 0-15 keep row A's sums of leaves j
+// and j + 8, lanes 16-31 row B's, by one exchange), then folding 4, 2, 1 as
+// one.  Row A's segment sum on lanes 0-15, row B's on lanes 16-31.
+__device__ __forceinline__ float q8k_segment_tree2(float la, float lb, int lane) {
+    const bool low = lane < 16;
+    float v = __fadd_rn(low ? la : lb, __shfl_xor_sync(0xFFFFFFFFu, low ? lb : la, 16));
+#pragma unroll
+    for (int off = 8; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
     return v;
 }
 
@@ -235,7 +247,7 @@ __device__ __forceinline__ float q8k_row_dot2(uint32_t nb, const ActImage& img, 
     const int j = lane >> 1, part = lane & 1;
     constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
     const uint32_t passes = kXReg ? 1u : (nb + 15u) / 16u;
-    float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+    float total = 0.0f;  // lanes 0-15: row A's running sum, lanes 16-31: row B's
 #pragma unroll 1
     for (uint32_t k = 0; k < passes; ++k) {
         const uint32_t i = 16u * k + j;
@@ -272,6 +284,7 @@ __device__ __forceinline__ float q8k_row_dot2(uint32_t nb, const ActImage& img, 
             ma += __shfl_xor_sync(0xFFFFFFFFu, ma, 1);
             mb += __shfl_xor_sync(0xFFFFFFFFu, mb, 1);
         }
+        float la = 0.0f, lb = 0.0f;
         if (active) {
             float pa = __fmul_rn(__fmul_rn(dwa, dx), __int2float_rn(ia));
             float pb = __fmul_rn(__fmul_rn(dwb, dx), __int2float_rn(ib));
@@ -279,32 +292,22 @@ __device__ __forceinline__ float q8k_row_dot2(uint32_t nb, const ActImage& img, 
                 pa = __fsub_rn(pa, __fmul_rn(__fmul_rn(dmwa, dx), __int2float_rn(ma)));
                 pb = __fsub_rn(pb, __fmul_rn(__fmul_rn(dmwb, dx), __int2float_rn(mb)));
             }
-            if (k & 1) {
-                a1 = __fadd_rn(a1, pa);
-                b1 = __fadd_rn(b1, pb);
-            } else {
-                a0 = __fadd_rn(a0, pa);
-                b0 = __fadd_rn(b0, pb);
-            }
+            la = __fadd_rn(la, pa);
+            lb = __fadd_rn(lb, pb);
         }
+        total = __fadd_rn(total, q8k_segment_tree2(la, lb, lane));
     }
-    const float va = __fadd_rn(a0, a1), vb = __fadd_rn(b0, b1);
-    const bool low = lane < 16;
-    float v = __fadd_rn(low ? va : vb, __shfl_xor_sync(0xFFFFFFFFu, low ? vb : va, 16));
-#pragma unroll
-    for (int off = 8; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-    return v;
+    return total;
 }
 
 // Pass `seg` of q8k_row_dot2 for two rows whose super-blocks 16 * seg .. are at
 // sega and segb (the segment's start): the activation slice of the segment
-// is fetched once for both rows, and the pass terms are added into the
-// rows' accumulators exactly as q8k_row_dot adds them (acc0 for even
-// passes, acc1 for odd).
+// is fetched once for both rows; la and lb are the rows' leaves (0 + p_i, or
+// +0 past the row's end) exactly as q8k_row_dot2 forms them.
 template <uint32_t kType>
 __device__ __forceinline__ void q8k_segment_pass2(uint32_t nb, const ActImage& img, uint32_t seg,
-                                                  const uint8_t* sega, const uint8_t* segb, int lane, float& a0,
-                                                  float& a1, float& b0, float& b1) {
+                                                  const uint8_t* sega, const uint8_t* segb, int lane, float& la,
+                                                  float& lb) {
     constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
     const int part = lane & 1;
     const uint32_t j = static_cast<uint32_t>(lane) >> 1;
@@ -338,20 +341,17 @@ __device__ __forceinline__ void q8k_segment_pass2(uint32_t nb, const ActImage& i
             pa = __fsub_rn(pa, __fmul_rn(__fmul_rn(dmwa, dx), __int2float_rn(ma)));
             pb = __fsub_rn(pb, __fmul_rn(__fmul_rn(dmwb, dx), __int2float_rn(mb)));
         }
-        if (seg & 1u) {
-            a1 = __fadd_rn(a1, pa);
-            b1 = __fadd_rn(b1, pb);
-        } else {
-            a0 = __fadd_rn(a0, pa);
-            b0 = __fadd_rn(b0, pb);
-        }
+        la = __fadd_rn(0.0f, pa);
+        lb = __fadd_rn(0.0f, pb);
+    } else {
+        la = lb = 0.0f;
     }
 }
 
 // q8k_segment_pass2 for one row (where two rows' registers would spill).
 template <uint32_t kType>
 __device__ __forceinline__ void q8k_segment_pass1(uint32_t nb, const ActImage& img, uint32_t seg,
-                                                  const uint8_t* sega, int lane, float& a0, float& a1) {
+                                                  const uint8_t* sega, int lane, float& la) {
     constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
     const int part = lane & 1;
     const uint32_t j = static_cast<uint32_t>(lane) >> 1;
@@ -373,23 +373,10 @@ __device__ __forceinline__ void q8k_segment_pass1(uint32_t nb, const ActImage& i
     if (active) {
         float pa = __fmul_rn(__fmul_rn(dwa, dx), __int2float_rn(ia));
         if (kType == 12) pa = __fsub_rn(pa, __fmul_rn(__fmul_rn(dmwa, dx), __int2float_rn(ma)));
-        if (seg & 1u)
-            a1 = __fadd_rn(a1, pa);
-        else
-            a0 = __fadd_rn(a0, pa);
+        la = __fadd_rn(0.0f, pa);
+    } else {
+        la = 0.0f;
     }
-}
-
-// The end of q8k_row_dot2: each row's two accumulators added, the two
-// butterflies with their first level shared; row A's dot product on lane 0,
-// row B's on lane 16.
-__device__ __forceinline__ float q8k_fold2(float a0, float a1, float b0, float b1, int lane) {
-    const float va = __fadd_rn(a0, a1), vb = __fadd_rn(b0, b1);
-    const bool low = lane < 16;
-    float v = __fadd_rn(low ? va : vb, __shfl_xor_sync(0xFFFFFFFFu, low ? vb : va, 16));
-#pragma unroll
-    for (int off = 8; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-    return v;
 }
 
 // The lane's activation slice for register-resident rows (<= 16 super-blocks).

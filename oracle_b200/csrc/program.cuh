@@ -261,9 +261,9 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
 // Q6_K (at most NCW rows) row w, and walks the group's G stages, adding each
 // segment's pass terms into the rows' accumulators in registers
 // (q8k_segment_pass2: the segment's activation slice fetched once for both
-// rows; q8k_segment_pass1), then folds them (q8k_fold2 / the butterfly of
-// q8k_row_dot).  Bit-identical to q8k_row_dot: the same terms reach the same
-// accumulators in the same order.
+// rows; q8k_segment_pass1), folds each segment's leaves by its tree and adds
+// the segment sums in order.  Bit-identical to q8k_row_dot: the same terms
+// take the same additions in the same order.
 template <int NCW, uint32_t kType, bool kPeers>
 __device__ __forceinline__ void program_walk_segmented(const ProgramOp& op, uint8_t* act, uint8_t* stage0,
                                                        uint32_t stage_bytes, uint32_t S, uint64_t* full,
@@ -285,7 +285,9 @@ __device__ __forceinline__ void program_walk_segmented(const ProgramOp& op, uint
         const uint32_t n_here = nrows - q_lo < R ? nrows - q_lo : R;
         const bool mine = ja < n_here;
         const bool has_b = kPer == 2 && ja + 1 < n_here;
-        float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+        // running sum of the segments' trees: for Q4_K pairs, lanes 0-15
+        // row ja's and lanes 16-31 row ja + 1's
+        float total = 0.0f;
         for (uint32_t sg = 0; sg < G; ++sg) {
             if (!failed) {
                 const bool ok = mbar_wait(&full[s], phase, status, 14);
@@ -293,10 +295,18 @@ __device__ __forceinline__ void program_walk_segmented(const ProgramOp& op, uint
             }
             if (!failed && mine) {
                 const uint8_t* pa = stage0 + s * stage_bytes + ja * kSeg;
-                if constexpr (kPer == 2)
-                    q8k_segment_pass2<kType>(op.nb, img, sg, pa, has_b ? pa + kSeg : pa, lane, a0, a1, b0, b1);
-                else
-                    q8k_segment_pass1<kType>(op.nb, img, sg, pa, lane, a0, a1);
+                if constexpr (kPer == 2) {
+                    float la, lb;
+                    q8k_segment_pass2<kType>(op.nb, img, sg, pa, has_b ? pa + kSeg : pa, lane, la, lb);
+                    total = __fadd_rn(total, q8k_segment_tree2(la, lb, lane));
+                } else {
+                    float leaf;
+                    q8k_segment_pass1<kType>(op.nb, img, sg, pa, lane, leaf);
+#pragma unroll
+                    for (int off = 16; off >= 2; off >>= 1)
+                        leaf = __fadd_rn(leaf, __shfl_xor_sync(0xFFFFFFFFu, leaf, off));
+                    total = __fadd_rn(total, leaf);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -307,14 +317,10 @@ __device__ __forceinline__ void program_walk_segmented(const ProgramOp& op, uint
         }
         if (!failed && mine) {
             if constexpr (kPer == 2) {
-                const float v = q8k_fold2(a0, a1, b0, b1, lane);
                 if ((lane & 15) == 0 && (lane == 0 || has_b))  // lane 0: first row, lane 16: second
-                    program_store_row<kPeers>(px, op.y + r0 + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), v);
+                    program_store_row<kPeers>(px, op.y + r0 + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), total);
             } else {
-                float v = __fadd_rn(a0, a1);
-#pragma unroll
-                for (int off = 16; off >= 2; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-                if (lane == 0) program_store_row<kPeers>(px, op.y + r0 + q_lo + ja, v);
+                if (lane == 0) program_store_row<kPeers>(px, op.y + r0 + q_lo + ja, total);
             }
         }
     }

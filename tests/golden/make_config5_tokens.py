@@ -61,7 +61,9 @@ def _worker(mode: str, q) -> None:
                                  max_tokens=PROMPT_LEN + N_NEW + 1)
     t0 = time.perf_counter()
     if mode == "greedy":
-        q.put((mode, ref.greedy(p, N_NEW), None, None, time.perf_counter() - t0))
+        toks = ref.greedy(p, N_NEW)
+        np.save(OUT + ".greedy.npy", toks)  # kept until the fixture is written
+        q.put((mode, toks, None, None, time.perf_counter() - t0))
         return
     tokens = np.zeros(N_NEW, np.uint32)
     margins = np.zeros(N_NEW, np.float32)
@@ -76,10 +78,12 @@ def _worker(mode: str, q) -> None:
         top[g], margins[g] = logits[tok], float(two[1]) - float(two[0])
         if g + 1 < N_NEW:
             logits = ref.forward(tok)
+    np.savez(OUT + ".margins.npz", tokens=tokens, margins=margins, top_logit=top)
     q.put((mode, tokens, margins, top, time.perf_counter() - t0))
 
 
 def main() -> None:
+    sys.path.insert(0, ROOT)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_worker, args=(m, q)) for m in ("greedy", "margins")]
@@ -97,6 +101,8 @@ def main() -> None:
         raise SystemExit(f"greedy and token-by-token decodes disagree: {greedy.tolist()} vs {tokens.tolist()}")
     from oracle_b200 import qwen35
     np.savez_compressed(OUT, prompt=prompt(qwen35.CONFIG5.vocab), tokens=greedy, margins=margins, top_logit=top)
+    for part in (OUT + ".greedy.npy", OUT + ".margins.npz"):
+        os.remove(part)
     print(f"wrote {OUT}: min top-2 margin {margins.min():.3g} at step {int(margins.argmin())}")
 
 
