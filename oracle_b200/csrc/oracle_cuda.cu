@@ -23,6 +23,7 @@
 #include "gather.cuh"
 #include "gemm_q4k.cuh"
 #include "layout.hpp"
+#include "matvec_batch.cuh"
 #include "matvec_q80_lane.cuh"
 #include "matvec_seq.cuh"
 #include "matvec_q8k.cuh"
@@ -81,6 +82,11 @@ struct oracle_cuda_context {
     uint64_t gemm_x_len = 0;
     bool gemm_pair = false;
     unsigned long long* argmax_key = nullptr;  // one key for oracle_cuda_greedy_token  // prefill GEMM on CTA pairs (cta_group::2); ORACLE_CUDA_GEMM_PAIR=1
+    // batched Q8_K matvec: activation images and per-segment partial sums
+    uint8_t* batch_image = nullptr;
+    uint64_t batch_image_len = 0;
+    float* batch_partial = nullptr;
+    uint64_t batch_partial_len = 0;
 };
 
 namespace {
@@ -358,6 +364,11 @@ oracle_cuda_status launch_decode(oracle_cuda_context* ctx, uint32_t type, const 
     }
 }
 
+bool batch_q8k_fits(oracle_cuda_context* ctx, const void* w, uint64_t rows, uint64_t cols);
+oracle_cuda_status launch_q8k_batch(oracle_cuda_context* ctx, uint32_t type, const void* w, uint64_t rows,
+                                    uint64_t cols, uint64_t row_bytes, const float* x, uint32_t batch, float* y,
+                                    cudaStream_t stream);
+
 // Validation shared by the device and host matvec entry points.
 oracle_cuda_status validate_matvec(oracle_cuda_context* ctx, int contract, uint32_t type, uint64_t rows, uint64_t cols,
                                    uint64_t w_nbytes, uint64_t x_len, uint64_t y_len, uint64_t* row_bytes,
@@ -375,6 +386,18 @@ oracle_cuda_status run_matvec(oracle_cuda_context* ctx, int contract, uint32_t t
                               uint64_t row_bytes, const void* w, const float* x, uint64_t batch, float* y,
                               cudaStream_t stream) {
     if (contract == ORACLE_CUDA_CONTRACT_F32) return launch_f32(ctx, type, w, rows, cols, row_bytes, x, batch, y, stream);
+    if (batch > 1 && batch_q8k_fits(ctx, w, rows, cols)) {
+        // up to 16 vectors per launch, each weight byte read once per launch
+        for (uint64_t b0 = 0; b0 < batch; b0 += kBatchMax) {
+            const uint64_t nbv = batch - b0 < uint64_t(kBatchMax) ? batch - b0 : uint64_t(kBatchMax);
+            oracle_cuda_status s = nbv == 1 ? launch_q8k(ctx, type, w, rows, cols, row_bytes, x + b0 * cols, nullptr,
+                                                         y + b0 * rows, stream)
+                                            : launch_q8k_batch(ctx, type, w, rows, cols, row_bytes, x + b0 * cols,
+                                                               static_cast<uint32_t>(nbv), y + b0 * rows, stream);
+            if (s != ORACLE_CUDA_OK) return s;
+        }
+        return ORACLE_CUDA_OK;
+    }
     for (uint64_t b = 0; b < batch; ++b) {
         oracle_cuda_status s = launch_q8k(ctx, type, w, rows, cols, row_bytes, x + b * cols, nullptr, y + b * rows, stream);
         if (s != ORACLE_CUDA_OK) return s;
@@ -403,6 +426,63 @@ oracle_cuda_status grow_device(oracle_cuda_context* ctx, T*& p, uint64_t& have, 
     ORACLE_CUDA_TRY(ctx, cudaMalloc(reinterpret_cast<void**>(&p), need * sizeof(T)), "cudaMalloc");
     have = need;
     return ORACLE_CUDA_OK;
+}
+
+// The batched Q8_K kernel's limits: 16-byte aligned weights, at least one CTA
+// per segment, and tile counts in 32 bits.
+bool batch_q8k_fits(oracle_cuda_context* ctx, const void* w, uint64_t rows, uint64_t cols) {
+    if (reinterpret_cast<uintptr_t>(w) & 15u) return false;
+    const uint64_t nb = cols / 256, G = (nb + 15) / 16, T = (rows + kBatchTileRows - 1) / kBatchTileRows;
+    return nb > 0 && G <= uint64_t(ctx->sm_count) && T < 0x7FFFFFFFull &&
+           batch_stage_offset(static_cast<uint32_t>(nb < 16 ? nb : 16)) + 2 * batch_stage_bytes(kTypeQ6_K) <=
+               uint64_t(ctx->max_smem_optin);
+}
+
+// Batched Q8_K matvec (matvec_batch.cuh): 2..16 vectors x[b][cols] -> y[b][rows].
+oracle_cuda_status launch_q8k_batch(oracle_cuda_context* ctx, uint32_t type, const void* w, uint64_t rows,
+                                    uint64_t cols, uint64_t row_bytes, const float* x, uint32_t batch, float* y,
+                                    cudaStream_t stream) {
+    const uint32_t nb = static_cast<uint32_t>(cols / 256), G = (nb + 15) / 16;
+    const uint64_t T = (rows + kBatchTileRows - 1) / kBatchTileRows;
+    if (oracle_cuda_status s = grow_device(ctx, ctx->batch_image, ctx->batch_image_len,
+                                           uint64_t(nb) * kBatchImageBlockBytes))
+        return s;
+    if (G > 1)
+        if (oracle_cuda_status s =
+                grow_device(ctx, ctx->batch_partial, ctx->batch_partial_len, G * uint64_t(batch) * rows))
+            return s;
+    const bool pdl = (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0;
+    if (oracle_cuda_status s = launch(ctx, quantize_batch_image_kernel, dim3(2 * nb), dim3(256), 0, stream, pdl, x,
+                                      batch, nb, type, ctx->batch_image))
+        return s;
+    BatchParams bp{};
+    bp.w = static_cast<const uint8_t*>(w);
+    bp.image = ctx->batch_image;
+    bp.out = G > 1 ? ctx->batch_partial : y;
+    bp.rows = rows;
+    bp.row_bytes = row_bytes;
+    bp.nb = nb;
+    bp.batch = batch;
+    bp.status = ctx->status;
+    const uint64_t items = T * G;
+    const uint32_t grid = static_cast<uint32_t>(items < uint64_t(ctx->sm_count) ? items : ctx->sm_count);
+    const uint64_t budget = ctx->smem_budget ? ctx->smem_budget : uint64_t(ctx->max_smem_optin);
+    const uint32_t off = batch_stage_offset(nb);
+    const uint32_t stage = type == kTypeQ4_K ? batch_stage_bytes(12) : batch_stage_bytes(14);
+    uint64_t stages = budget > off ? (budget - off) / stage : 0;
+    if (stages > uint64_t(kBatchMaxStages)) stages = kBatchMaxStages;
+    if (stages < 2) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "shared-memory budget too small for the batched matvec");
+    bp.stages = static_cast<uint32_t>(stages);
+    const size_t smem = off + stages * stage;
+    oracle_cuda_status s =
+        type == kTypeQ4_K
+            ? launch(ctx, matvec_batch_kernel<12>, dim3(grid), dim3(kBatchThreads), smem, stream, pdl, bp)
+            : launch(ctx, matvec_batch_kernel<14>, dim3(grid), dim3(kBatchThreads), smem, stream, pdl, bp);
+    if (s != ORACLE_CUDA_OK || G == 1) return s;
+    const uint64_t n = uint64_t(batch) * rows;
+    const uint64_t blocks = (n + 255) / 256;
+    return launch(ctx, batch_combine_kernel, dim3(static_cast<uint32_t>(blocks < 4096 ? blocks : 4096)), dim3(256), 0,
+                  stream, pdl, static_cast<const float*>(ctx->batch_partial), y, n, G);
 }
 
 // The device bytes a host-pointer call reads for a weight span: the resident
@@ -576,6 +656,8 @@ oracle_cuda_status oracle_cuda_destroy(oracle_cuda_context* ctx) {
     if (ctx->act_scratch) cudaFree(ctx->act_scratch);
     if (ctx->gemm_x) cudaFree(ctx->gemm_x);
     if (ctx->argmax_key) cudaFree(ctx->argmax_key);
+    if (ctx->batch_image) cudaFree(ctx->batch_image);
+    if (ctx->batch_partial) cudaFree(ctx->batch_partial);
     delete ctx;
     return ORACLE_CUDA_OK;
 }
