@@ -165,6 +165,30 @@ oracle_cuda_status oracle_cuda_matvec_q8k_prequantized(oracle_cuda_context* ctx,
                                                        const void* q8k_dev, uint64_t q8k_nbytes,
                                                        float* y_dev, uint64_t y_len, void* stream);
 
+/* Batched decode: the Q8_K matvec of up to 16 activation vectors in one pass
+ * over the weights (each weight byte read once, not once per vector).  Two
+ * steps, so that one quantization serves every matrix that reads the same
+ * activations (a block's q / k / v, gate / up):
+ *   oracle_cuda_batch_quantize  x[batch][cols] (batch 1..16, cols a multiple
+ *       of 256) -> a batch image of oracle_cuda_batch_image_bytes(cols) bytes
+ *       (16-byte aligned device buffer): GGML's quantize_row_q8_K per vector,
+ *       laid out for the tensor-core kernel;
+ *   oracle_cuda_batch_matvec    y[b][r] = the Q8_K-contract dot of weight row r
+ *       (q4_K / q6_K, 16-byte aligned) with vector b of the image, for
+ *       b < batch; y_len == batch * rows.  Bit-identical, vector by vector, to
+ *       oracle_cuda_storage_matvec with CONTRACT_Q8K.
+ * These replace a loop of reference_storage_matvec calls over the batch
+ * (quantized_reference.cpp:128-162), which reads the weights once per vector.
+ * oracle_cuda_storage_matvec with CONTRACT_Q8K and 2..16 vectors takes the
+ * same path internally. */
+uint64_t oracle_cuda_batch_image_bytes(uint64_t cols);
+oracle_cuda_status oracle_cuda_batch_quantize(oracle_cuda_context* ctx, const float* x_dev, uint64_t cols,
+                                              uint32_t batch, void* image_dev, uint64_t image_nbytes, void* stream);
+oracle_cuda_status oracle_cuda_batch_matvec(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
+                                            const void* w_dev, uint64_t w_nbytes, const void* image_dev,
+                                            uint64_t image_nbytes, uint32_t batch, float* y_dev, uint64_t y_len,
+                                            void* stream);
+
 /* Matvec program: up to ORACLE_CUDA_PROGRAM_MAX_OPS Q8_K-contract matvecs
  * (q4_K / q6_K weights) in ONE persistent launch.  The weights of all ops
  * stream through one shared-memory ring without pausing at op boundaries;
@@ -387,6 +411,19 @@ oracle_cuda_status oracle_cuda_token_commit(oracle_cuda_context* ctx, const unsi
                                             const uint32_t* prompt_dev, uint32_t n_prompt, uint32_t* pos_dev,
                                             uint32_t* next_id_dev, uint32_t* tokens_dev, uint32_t tokens_capacity,
                                             void* stream);
+/* Batched greedy sampling for sequences decoded in lockstep (one shared
+ * position): oracle_cuda_argmax_rows writes the argmax key of each logits row
+ * x[b][n] (b < rows) to keys_dev[b]; oracle_cuda_token_commit_rows applies
+ * token_commit to each sequence b (prompt_dev[b * n_prompt ..], next_id_dev[b],
+ * tokens_dev[b * tokens_capacity ..]), clears the keys and advances *pos_dev
+ * once.  A NaN / non-finite maximum in any row is reported like
+ * oracle_cuda_token_commit and stops the batch (no advance). */
+oracle_cuda_status oracle_cuda_argmax_rows(oracle_cuda_context* ctx, const float* x_dev, uint32_t rows, uint64_t n,
+                                           unsigned long long* keys_dev, void* stream);
+oracle_cuda_status oracle_cuda_token_commit_rows(oracle_cuda_context* ctx, unsigned long long* keys_dev,
+                                                 uint32_t rows, const uint32_t* prompt_dev, uint32_t n_prompt,
+                                                 uint32_t* pos_dev, uint32_t* next_id_dev, uint32_t* tokens_dev,
+                                                 uint32_t tokens_capacity, void* stream);
 /* Fused block cores (graph-replayable, position in device memory):
  *   gdn_core        a Gated DeltaNet block from its projections to the vector
  *                   its output projection reads (qwen35_block.cpp:472-592):
@@ -409,6 +446,18 @@ oracle_cuda_status oracle_cuda_gdn_core(oracle_cuda_context* ctx, const float* q
                                         const float* norm_dev, uint32_t key_heads, uint32_t value_heads,
                                         uint32_t head_dim, uint32_t conv_kernel, float eps, const uint32_t* pos_dev,
                                         float* out_dev, void* stream);
+/* gdn_core for `seqs` sequences decoded in lockstep: sequence s reads and
+ * writes its own stacked buffers (qkv_dev + s * channels, z / out + s *
+ * value_heads * head_dim, beta / alpha + s * value_heads, history + s * 2 *
+ * channels * conv_kernel, state + s * value_heads * head_dim^2); the weights
+ * and the position are shared.  seqs == 1 is oracle_cuda_gdn_core. */
+oracle_cuda_status oracle_cuda_gdn_core_seqs(oracle_cuda_context* ctx, const float* qkv_dev, const float* z_dev,
+                                             const float* beta_dev, const float* alpha_dev,
+                                             const float* time_step_bias_dev, const float* decay_dev,
+                                             const float* conv_weights_dev, float* history_dev, float* state_dev,
+                                             const float* norm_dev, uint32_t key_heads, uint32_t value_heads,
+                                             uint32_t head_dim, uint32_t conv_kernel, float eps,
+                                             const uint32_t* pos_dev, uint32_t seqs, float* out_dev, void* stream);
 oracle_cuda_status oracle_cuda_attention_prep_at(oracle_cuda_context* ctx, const float* q_full_dev, const float* k_dev,
                                                  const float* v_dev, const float* q_norm_dev, const float* k_norm_dev,
                                                  float eps, const float* table_dev, uint64_t rotary_dim,

@@ -110,6 +110,9 @@ _proto("oracle_cuda_decode_rows", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, 
 _proto("oracle_cuda_quantize_q8_k", [_vp, _vp, _u64, _u64, _vp, _u64, _vp])
 _proto("oracle_cuda_storage_matvec", [_vp, _i32, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _u64, _vp])
 _proto("oracle_cuda_matvec_q8k_prequantized", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _u64, _vp])
+_proto("oracle_cuda_batch_image_bytes", [_u64], C.c_uint64)
+_proto("oracle_cuda_batch_quantize", [_vp, _vp, _u64, _u32, _vp, _u64, _vp])
+_proto("oracle_cuda_batch_matvec", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _u32, _vp, _u64, _vp])
 
 
 class MatvecOp(C.Structure):
@@ -211,6 +214,10 @@ _proto("oracle_cuda_gate_sigmoid_mul", [_vp, _vp, _vp, _u64, _vp])
 _proto("oracle_cuda_mul_silu", [_vp, _vp, _vp, _u64, _vp])
 _proto("oracle_cuda_gdn_gates", [_vp, _vp, _vp, _vp, _vp, _u32, _vp, _vp, _vp])
 _proto("oracle_cuda_token_commit", [_vp, _vp, _vp, _u32, _vp, _vp, _vp, _u32, _vp])
+_proto("oracle_cuda_argmax_rows", [_vp, _vp, _u32, _u64, _vp, _vp])
+_proto("oracle_cuda_token_commit_rows", [_vp, _vp, _u32, _vp, _u32, _vp, _vp, _vp, _u32, _vp])
+_proto("oracle_cuda_gdn_core_seqs", [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32,
+                                     C.c_float, _vp, _u32, _vp, _vp])
 _proto("oracle_cuda_gdn_core", [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32,
                                 C.c_float, _vp, _vp, _vp])
 _proto("oracle_cuda_attention_prep_at", [_vp, _vp, _vp, _vp, _vp, _vp, C.c_float, _vp, _u64, _u32, _u32, _u32, _vp,
@@ -464,6 +471,22 @@ class Context:
             self._h, contract, qtype, rows, cols, _addr(w), _nbytes(w) if w_nbytes is None else w_nbytes,
             _addr(x), _numel(x), _addr(y), _numel(y), _stream(stream)))
 
+    @staticmethod
+    def batch_image_bytes(cols: int) -> int:
+        """oracle_cuda_batch_image_bytes: size of the batch image of cols-wide vectors."""
+        return int(_lib.oracle_cuda_batch_image_bytes(cols))
+
+    def batch_quantize(self, x, cols, batch, image, stream=None) -> None:
+        """oracle_cuda_batch_quantize: x[batch][cols] (device f32) -> batch image (device uint8)."""
+        self._check(_lib.oracle_cuda_batch_quantize(self._h, _addr(x), cols, batch, _addr(image), _nbytes(image),
+                                                    _stream(stream)))
+
+    def batch_matvec(self, qtype, rows, cols, w, image, batch, y, stream=None, w_nbytes=None) -> None:
+        """oracle_cuda_batch_matvec: y[b][rows] = W (q4_K / q6_K) x vector b of a batch image."""
+        self._check(_lib.oracle_cuda_batch_matvec(self._h, qtype, rows, cols, _addr(w),
+                                                  _nbytes(w) if w_nbytes is None else w_nbytes, _addr(image),
+                                                  _nbytes(image), batch, _addr(y), _numel(y), _stream(stream)))
+
     def matvec_q8k_prequantized(self, qtype, rows, cols, w, q8k, y, stream=None) -> None:
         self._check(_lib.oracle_cuda_matvec_q8k_prequantized(
             self._h, qtype, rows, cols, _addr(w), _nbytes(w), _addr(q8k), _nbytes(q8k), _addr(y), _numel(y),
@@ -579,6 +602,24 @@ class Context:
     def token_commit(self, key, prompt, n_prompt, pos, next_id, tokens, tokens_capacity, stream=None) -> None:
         self._check(_lib.oracle_cuda_token_commit(self._h, _addr(key), _addr(prompt), n_prompt, _addr(pos),
                                                   _addr(next_id), _addr(tokens), tokens_capacity, _stream(stream)))
+
+    def argmax_rows(self, x, rows, n, keys, stream=None) -> None:
+        """oracle_cuda_argmax_rows: keys[b] = argmax key of logits row x[b][n]."""
+        self._check(_lib.oracle_cuda_argmax_rows(self._h, _addr(x), rows, n, _addr(keys), _stream(stream)))
+
+    def token_commit_rows(self, keys, rows, prompt, n_prompt, pos, next_id, tokens, tokens_capacity,
+                          stream=None) -> None:
+        self._check(_lib.oracle_cuda_token_commit_rows(self._h, _addr(keys), rows, _addr(prompt), n_prompt,
+                                                       _addr(pos), _addr(next_id), _addr(tokens), tokens_capacity,
+                                                       _stream(stream)))
+
+    def gdn_core_seqs(self, qkv, z, beta, alpha, time_step_bias, decay, conv_weights, history, state, norm,
+                      key_heads, value_heads, head_dim, conv_kernel, eps, pos, seqs, out, stream=None) -> None:
+        self._check(_lib.oracle_cuda_gdn_core_seqs(self._h, _addr(qkv), _addr(z), _addr(beta), _addr(alpha),
+                                                   _addr(time_step_bias), _addr(decay), _addr(conv_weights),
+                                                   _addr(history), _addr(state), _addr(norm), key_heads,
+                                                   value_heads, head_dim, conv_kernel, eps, _addr(pos), seqs,
+                                                   _addr(out), _stream(stream)))
 
     def gdn_core(self, qkv, z, beta, alpha, time_step_bias, decay, conv_weights, history, state, norm, key_heads,
                  value_heads, head_dim, conv_kernel, eps, pos, out, stream=None) -> None:

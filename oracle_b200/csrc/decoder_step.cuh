@@ -302,12 +302,13 @@ __global__ void __launch_bounds__(256) mul_silu_kernel(float* __restrict__ x, co
 //   delta      gated_delta_step (reference_kernels.cpp:221-335) on the head's
 //              [key][value] state: thread (t, part) keeps rows part * kD/4 ..
 //              of state column t in registers; the two sums over the key
-//              index (the f32 memory read-out and the f64 output) run as four
-//              sequential partial sums combined pairwise, ((p0 + p1) + (p2 +
-//              p3)), instead of one chain of kD terms: the same terms, a
-//              different rounding order (within the decoder's tolerance; the
-//              unfused gated_delta_kernel keeps the reference's order)
+//              index (the f32 memory read-out and the f64 output) are one
+//              chain from key row 0 to kD - 1 each, the reference's order
+//              (the column's four threads add their quarters in turn), so the
+//              block matches gated_delta_kernel bit for bit
 //   out        rms_norm_rows over the head's row, then * silu(z)
+// A batched decode runs its sequences as grid rows (blockIdx.y), each on its
+// own stacked buffers (the history [2][channels][conv_kernel] per sequence).
 template <int kD>
 __global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restrict__ qkv, const float* __restrict__ z,
                                                           const float* __restrict__ beta_in,
@@ -320,6 +321,19 @@ __global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restric
                                                           const uint32_t* __restrict__ pos, float* __restrict__ out) {
     constexpr int kQ = kD / 4;  // key rows per thread
     pdl_launch_dependents();
+    {
+        // blockIdx.y: the sequence of a batched decode, with its own inputs,
+        // history, state and output stacked after the previous sequence's
+        const uint64_t seq = blockIdx.y;
+        const uint64_t ch = 2ull * key_heads * kD + uint64_t(value_heads) * kD;
+        qkv += seq * ch;
+        z += seq * value_heads * kD;
+        beta_in += seq * value_heads;
+        alpha += seq * value_heads;
+        hist += seq * 2 * ch * conv_kernel;
+        state += seq * value_heads * kD * kD;
+        out += seq * value_heads * kD;
+    }
     __shared__ float q_s[kD], k_s[kD], v_s[kD], nq[kD], nk[kD], o_s[kD];
     __shared__ double scratch[64];
     __shared__ float gate_s[2];
@@ -404,23 +418,34 @@ __global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restric
     const float b = gate_s[0], decay = gate_s[1];
     const float* nkp = nk + part * kQ;
     const float* nqp = nq + part * kQ;
+    // Both sums over the key rows run in gated_delta_step's order, one chain
+    // from row 0 to row kD - 1: the four threads of column t (adjacent lanes)
+    // add their quarters in turn, handing the running sum on by shuffle.
+    const uint32_t lane = tid & 31u, group = lane & ~3u;
+#pragma unroll
+    for (int j = 0; j < kQ; ++j) col[j] = __fmul_rn(col[j], decay);
     float mem = 0.0f;
 #pragma unroll
-    for (int j = 0; j < kQ; ++j) {
-        col[j] = __fmul_rn(col[j], decay);
-        mem = __fadd_rn(mem, __fmul_rn(col[j], nkp[j]));
+    for (uint32_t p = 0; p < 4; ++p) {
+        if (part == p) {
+#pragma unroll
+            for (int j = 0; j < kQ; ++j) mem = __fadd_rn(mem, __fmul_rn(col[j], nkp[j]));
+        }
+        mem = __shfl_sync(0xFFFFFFFFu, mem, group | p);
     }
-    mem = __fadd_rn(mem, __shfl_xor_sync(0xFFFFFFFFu, mem, 1));
-    mem = __fadd_rn(mem, __shfl_xor_sync(0xFFFFFFFFu, mem, 2));
     const float delta = __fmul_rn(__fsub_rn(v_s[t], mem), b);
+#pragma unroll
+    for (int j = 0; j < kQ; ++j) col[j] = __fadd_rn(col[j], __fmul_rn(nkp[j], delta));
     double o = 0.0;
 #pragma unroll
-    for (int j = 0; j < kQ; ++j) {
-        col[j] = __fadd_rn(col[j], __fmul_rn(nkp[j], delta));
-        o = __dadd_rn(o, __dmul_rn(static_cast<double>(col[j]), static_cast<double>(nqp[j])));
+    for (uint32_t p = 0; p < 4; ++p) {
+        if (part == p) {
+#pragma unroll
+            for (int j = 0; j < kQ; ++j)
+                o = __dadd_rn(o, __dmul_rn(static_cast<double>(col[j]), static_cast<double>(nqp[j])));
+        }
+        o = __shfl_sync(0xFFFFFFFFu, o, group | p);
     }
-    o = __dadd_rn(o, __shfl_xor_sync(0xFFFFFFFFu, o, 1));
-    o = __dadd_rn(o, __shfl_xor_sync(0xFFFFFFFFu, o, 2));
 #pragma unroll
     for (int j = 0; j < kQ; ++j) sh[j * kD] = col[j];
     if (part == 0) o_s[t] = __double2float_rn(o);

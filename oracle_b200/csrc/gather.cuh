@@ -63,6 +63,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index
 __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ x, uint64_t n, uint32_t index_base,
                                                      unsigned long long* __restrict__ key_out) {
     pdl_enter();
+    x += blockIdx.y * n;  // row blockIdx.y of a batch of logits vectors, one key each
+    key_out += blockIdx.y;
     __shared__ unsigned long long warp_best[8];
     unsigned long long best = 0;
     for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x) {
@@ -146,6 +148,50 @@ __global__ void token_commit_kernel(const unsigned long long* __restrict__ key, 
         if (i < out_capacity) tokens_out[i] = r.index;
     }
     *pos = p + 1;
+}
+
+// token_commit_kernel for a batch of sequences decoded in lockstep (one
+// position): sequence b's key is keys[b], its prompt prompt[b * n_prompt ..],
+// its next input next_id[b] and its tokens tokens_out[b * out_capacity ..].
+// Each key is cleared after it is read (the next step's argmax accumulates
+// into it).  A NaN or non-finite maximum in any sequence is reported and
+// stops the batch: the position does not advance.
+__global__ void __launch_bounds__(256) token_commit_rows_kernel(unsigned long long* __restrict__ keys, uint32_t rows,
+                                                                const uint32_t* __restrict__ prompt,
+                                                                uint32_t n_prompt, uint32_t* pos,
+                                                                uint32_t* __restrict__ next_id,
+                                                                uint32_t* __restrict__ tokens_out,
+                                                                uint32_t out_capacity, DeviceStatus* st) {
+    pdl_enter();
+    __shared__ int bad;
+    if (threadIdx.x == 0) bad = 0;
+    __syncthreads();
+    const uint32_t p = *pos;
+    for (uint32_t b = threadIdx.x; b < rows; b += blockDim.x) {
+        const ArgmaxResult r = decode_argmax_key(keys[b]);
+        if (r.nan || !r.finite) {
+            bad = 1;
+            if (st && atomicCAS(&st->code, kDevOk, r.nan ? kDevLogitsNaN : kDevLogitsNonFinite) == kDevOk) {
+                st->where = p;
+                st->block = b;
+            }
+        }
+    }
+    __syncthreads();
+    if (bad) return;
+    for (uint32_t b = threadIdx.x; b < rows; b += blockDim.x) {
+        const ArgmaxResult r = decode_argmax_key(keys[b]);
+        keys[b] = 0ull;
+        if (p + 1 < n_prompt) {
+            next_id[b] = prompt[uint64_t(b) * n_prompt + p + 1];
+        } else {
+            next_id[b] = r.index;
+            const uint32_t i = p + 1 - n_prompt;
+            if (i < out_capacity) tokens_out[uint64_t(b) * out_capacity + i] = r.index;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *pos = p + 1;
 }
 
 }  // namespace oracle_cuda

@@ -25,10 +25,10 @@
 //
 // Work items are (tile of 8 rows, segment).  The CTAs are shared out among the
 // segments (CTA c works on segment c * G / grid) and each splits its
-// segment's tiles evenly, so a CTA copies one activation image (16 vectors x
-// up to 16 super-blocks) into shared memory once.  Per item, 16 consumer warps
-// share a stage of 8 rows x the segment's super-blocks: warp r computes leaf r
-// (0 + p_r, or 0 past the row's end).  The leaves meet in shared memory and
+// segment's tiles evenly.  Per item, 16 consumer warps share a stage of
+// 8 rows x the segment's super-blocks: warp r computes leaf r (0 + p_r, or 0
+// past the row's end) and, working on super-block r for every tile, holds that
+// block's activation operands in registers for the whole launch.  The leaves meet in shared memory and
 // the tree runs across lanes in its own order --
 // ((L0 + L8) + (L4 + L12)) + ((L2 + L10) + (L6 + L14)) for N3(0) and the odd
 // leaves for N3(1), root = N3(0) + N3(1).  With one segment per row
@@ -54,32 +54,28 @@ constexpr int kBatchMaxStages = 12;
 //                lane 4g + t holds words 4k + 2h + u = elements
 //                32k + 16h + 4t .. +3 of vector g + 8u, stored [k][lane][4]
 //                so that a warp's 16-byte reads are contiguous;
-//   [4096, 4608) the split sub-block sums in the m16n8k16 A-fragment order,
-//                uint4 of lane 4g + t = {lo(g), lo(g + 8), hi(g), hi(g + 8)},
-//                each word the bytes for sub-blocks 4t .. 4t + 3 (Q6_K:
-//                16-element sums, Q4_K: 32-element sums, sub-blocks 8..15
-//                zero), sum = 64 * hi + lo with lo in 0..63;
-//   [4608, 4672) d_x of the 16 vectors.
-// Vectors past the batch are zero.
-constexpr uint32_t kBatchImageBlockBytes = 4096 + 512 + kBatchMax * 4;  // 4672
-constexpr uint32_t kBatchImageBsumOffset = 4096;
-constexpr uint32_t kBatchImageDOffset = 4608;
+//   [4096, 4608) the 16-element sub-block sums (the Q6_K offset term), split
+//                as sum = 64 * hi + lo with lo in 0..63, in the m16n8k16
+//                A-fragment order: uint4 of lane 4g + t =
+//                {lo(g), lo(g + 8), hi(g), hi(g + 8)}, each word the bytes for
+//                sub-blocks 4t .. 4t + 3;
+//   [4608, 5120) the 32-element sub-block sums (the Q4_K min term), the same
+//                way (sub-blocks 8..15 zero);
+//   [5120, 5184) d_x of the 16 vectors.
+// Vectors past the batch are zero.  The image depends on the activations
+// only, so one image serves every matrix that reads them.
+constexpr uint32_t kBatchImageBlockBytes = 4096 + 512 + 512 + kBatchMax * 4;  // 5184
+constexpr uint32_t kBatchImageBsum16Offset = 4096;
+constexpr uint32_t kBatchImageBsum32Offset = 4608;
+constexpr uint32_t kBatchImageDOffset = 5120;
 
 // Shared-memory layout of matvec_batch_kernel: barriers, two items of leaves
 // (16 warps x 4 outputs x 32 lanes, each warp's block padded by 8 floats so
-// that the tree's reads hit distinct banks), the segment's activation image,
-// then the stage ring.
+// that the tree's reads hit distinct banks), then the stage ring.
 constexpr uint32_t kBatchBarrierBytes = 256;
 constexpr uint32_t kBatchLeafPitch = 4 * 32 + 8;
 constexpr uint32_t kBatchScratchBytes = 2 * kBatchConsumerWarps * kBatchLeafPitch * 4;
-constexpr uint32_t kBatchAOffset = kBatchBarrierBytes + kBatchScratchBytes;
-
-__host__ __device__ inline uint32_t batch_a_bytes(uint32_t nb) {
-    return (nb < 16u ? nb : 16u) * kBatchImageBlockBytes;
-}
-__host__ __device__ inline uint32_t batch_stage_offset(uint32_t nb) {
-    return align_up(kBatchAOffset + batch_a_bytes(nb), 128u);
-}
+constexpr uint32_t kBatchStageOffset = align_up(kBatchBarrierBytes + kBatchScratchBytes, 128u);
 // A stage row holds a segment of 16 super-blocks plus the 16-byte alignment
 // window of a Q6_K row; a stride of 16 mod 128 bytes puts the 8 rows of a
 // stage in different shared-memory banks.
@@ -90,10 +86,9 @@ __host__ __device__ constexpr uint32_t batch_stage_bytes(uint32_t type) {
 
 // One warp per (vector, block): the batch-1 quantizer's arithmetic (GGML's
 // quantize_row_q8_K), scattered into the fragment order, plus the split
-// sub-block sums for weight type `type` (12 = Q4_K, 14 = Q6_K).
+// sub-block sums of both widths.
 __global__ void __launch_bounds__(256) quantize_batch_image_kernel(const float* __restrict__ x, uint32_t batch,
-                                                                   uint32_t nb, uint32_t type,
-                                                                   uint8_t* __restrict__ image) {
+                                                                   uint32_t nb, uint8_t* __restrict__ image) {
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
@@ -102,7 +97,6 @@ __global__ void __launch_bounds__(256) quantize_batch_image_kernel(const float* 
     const uint32_t v = gw % kBatchMax, i = gw / kBatchMax;
     uint8_t* blk = image + uint64_t(i) * kBatchImageBlockBytes;
     uint32_t* q = reinterpret_cast<uint32_t*>(blk);
-    uint32_t* bs = reinterpret_cast<uint32_t*>(blk + kBatchImageBsumOffset);
     float* d = reinterpret_cast<float*>(blk + kBatchImageDOffset);
     Q8KLane r{0u, 0u, 0, 0.0f};
     if (v < batch) {  // warp-uniform
@@ -119,22 +113,28 @@ __global__ void __launch_bounds__(256) quantize_batch_image_kernel(const float* 
         const uint32_t dst_lane = 4u * (v & 7u) + t;
         q[(k * 32u + dst_lane) * 4u + 2u * h + (v >> 3)] = w[h2];
     }
-    // lane s (< 16) takes the sum of 16-element sub-block s (lanes 2s, 2s + 1)
+    // lane s (< 16) takes the sum of 16-element sub-block s (lanes 2s, 2s + 1);
+    // lane j (< 8) the sum of 32-element sub-block j
     const int b16 = __shfl_sync(0xFFFFFFFFu, r.bsum16, (2 * lane) & 31);
     const int pa = __shfl_sync(0xFFFFFFFFu, b16, (2 * lane) & 31);
     const int pb = __shfl_sync(0xFFFFFFFFu, b16, (2 * lane + 1) & 31);
-    const int val = type == 12 ? (lane < 8 ? pa + pb : 0) : (lane < 16 ? b16 : 0);
-    const uint32_t lo = static_cast<uint32_t>(val & 63), hi = static_cast<uint32_t>((val >> 6) & 0xFF);
-    uint32_t lo_w = 0, hi_w = 0;
 #pragma unroll
-    for (int qq = 0; qq < 4; ++qq) {
-        lo_w |= __shfl_sync(0xFFFFFFFFu, lo, (4 * (lane & 3) + qq) & 31) << (8 * qq);
-        hi_w |= __shfl_sync(0xFFFFFFFFu, hi, (4 * (lane & 3) + qq) & 31) << (8 * qq);
-    }
-    if (lane < 4) {
-        const uint32_t dst_lane = 4u * (v & 7u) + lane;
-        bs[dst_lane * 4u + (v >> 3)] = lo_w;
-        bs[dst_lane * 4u + 2u + (v >> 3)] = hi_w;
+    for (int width = 0; width < 2; ++width) {
+        const int val = width == 0 ? (lane < 16 ? b16 : 0) : (lane < 8 ? pa + pb : 0);
+        const uint32_t lo = static_cast<uint32_t>(val & 63), hi = static_cast<uint32_t>((val >> 6) & 0xFF);
+        uint32_t lo_w = 0, hi_w = 0;
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+            lo_w |= __shfl_sync(0xFFFFFFFFu, lo, (4 * (lane & 3) + qq) & 31) << (8 * qq);
+            hi_w |= __shfl_sync(0xFFFFFFFFu, hi, (4 * (lane & 3) + qq) & 31) << (8 * qq);
+        }
+        uint32_t* bs = reinterpret_cast<uint32_t*>(blk + (width == 0 ? kBatchImageBsum16Offset
+                                                                      : kBatchImageBsum32Offset));
+        if (lane < 4) {
+            const uint32_t dst_lane = 4u * (v & 7u) + lane;
+            bs[dst_lane * 4u + (v >> 3)] = lo_w;
+            bs[dst_lane * 4u + 2u + (v >> 3)] = hi_w;
+        }
     }
     if (lane == 0) d[v] = r.d;
 }
@@ -182,19 +182,38 @@ struct EvenRow {
     }
 };
 
+// A warp's activation operands for one super-block, held in registers for
+// every tile of the launch: the lane's quant fragments, the split sums the
+// weight type needs, and d_x of vectors g and g + 8.
+struct BatchA {
+    uint4 q[8];
+    uint4 bs;
+    float dxl, dxh;
+};
+
+// From the image in global memory (written by the preceding kernel: L2 reads).
+__device__ __forceinline__ void batch_load_a(const uint8_t* blk, int lane, uint32_t bsum_offset, BatchA& A) {
+    const uint4* src = reinterpret_cast<const uint4*>(blk) + lane;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) A.q[k] = __ldcg(src + 32 * k);
+    A.bs = __ldcg(reinterpret_cast<const uint4*>(blk + bsum_offset) + lane);
+    const float* d = reinterpret_cast<const float*>(blk + kBatchImageDOffset);
+    A.dxl = __ldcg(d + (lane >> 2));
+    A.dxh = __ldcg(d + (lane >> 2) + 8);
+}
+
 // The term p for the thread's four (vector, row) outputs of one Q4_K
 // super-block.  rg: the block in row g (the B operand); ra / rb: rows 2t and
-// 2t + 1 (the outputs' scales and d); a: the activation image block.
+// 2t + 1 (the outputs' scales and d); A: the activation operands.
 __device__ __forceinline__ void batch_q4k_terms(const uint8_t* rg, const uint8_t* ra, const uint8_t* rb,
-                                                const uint8_t* a, int lane, float (&p)[4]) {
-    const int g = lane >> 2, t = lane & 3;
+                                                const BatchA& A, int lane, float (&p)[4]) {
+    const int t = lane & 3;
     const uint4 hg = *reinterpret_cast<const uint4*>(rg);
     const uint4 ha = *reinterpret_cast<const uint4*>(ra);
     const uint4 hb = *reinterpret_cast<const uint4*>(rb);
     // 6-bit scales of rows 2t, 2t + 1 for sub-blocks 0..3 / 4..7
     const uint32_t sa_lo = ha.y & 0x3F3F3F3Fu, sa_hi = (ha.w & 0x0F0F0F0Fu) | ((ha.y >> 2) & 0x30303030u);
     const uint32_t sb_lo = hb.y & 0x3F3F3F3Fu, sb_hi = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
-    const uint4* av = reinterpret_cast<const uint4*>(a) + lane;
     int isum[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int g64 = 0; g64 < 4; ++g64) {
@@ -206,7 +225,7 @@ __device__ __forceinline__ void batch_q4k_terms(const uint8_t* rg, const uint8_t
             const uint32_t b0 = hi ? ((w0 >> 4) & 0x0F0F0F0Fu) : (w0 & 0x0F0F0F0Fu);
             const uint32_t b1 = hi ? ((w1 >> 4) & 0x0F0F0F0Fu) : (w1 & 0x0F0F0F0Fu);
             int c[4] = {0, 0, 0, 0};
-            mma_k32_s8u8(c, av[32 * j], b0, b1);
+            mma_k32_s8u8(c, A.q[j], b0, b1);
             const int sca = byte_u(j < 4 ? sa_lo : sa_hi, j & 3);
             const int scb = byte_u(j < 4 ? sb_lo : sb_hi, j & 3);
             isum[0] += sca * c[0];
@@ -218,12 +237,10 @@ __device__ __forceinline__ void batch_q4k_terms(const uint8_t* rg, const uint8_t
     // min term: the mins of row g for sub-blocks 4t .. 4t + 3 against the split sums
     const uint32_t mn = t == 0 ? (hg.z & 0x3F3F3F3Fu)
                                : t == 1 ? (((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u)) : 0u;
-    const uint4 bs = reinterpret_cast<const uint4*>(a + kBatchImageBsumOffset)[lane];
     int mlo[4] = {0, 0, 0, 0}, mhi[4] = {0, 0, 0, 0};
-    mma_k16_s8u8(mlo, bs.x, bs.y, mn);
-    mma_k16_s8u8(mhi, bs.z, bs.w, mn);
-    const float* dxp = reinterpret_cast<const float*>(a + kBatchImageDOffset);
-    const float dxl = dxp[g], dxh = dxp[g + 8];
+    mma_k16_s8u8(mlo, A.bs.x, A.bs.y, mn);
+    mma_k16_s8u8(mhi, A.bs.z, A.bs.w, mn);
+    const float dxl = A.dxl, dxh = A.dxh;
     const float dwa = f16_bits_to_f32(static_cast<uint16_t>(ha.x & 0xFFFFu));
     const float dma = f16_bits_to_f32(static_cast<uint16_t>(ha.x >> 16));
     const float dwb = f16_bits_to_f32(static_cast<uint16_t>(hb.x & 0xFFFFu));
@@ -239,10 +256,9 @@ __device__ __forceinline__ void batch_q4k_terms(const uint8_t* rg, const uint8_t
 
 // The same for one Q6_K super-block (blocks at even shared addresses).
 __device__ __forceinline__ void batch_q6k_terms(const uint8_t* rg, const uint8_t* ra, const uint8_t* rb,
-                                                const uint8_t* a, int lane, float (&p)[4]) {
-    const int g = lane >> 2, t = lane & 3;
+                                                const BatchA& A, int lane, float (&p)[4]) {
+    const int t = lane & 3;
     const EvenRow RG(rg), RA(ra), RB(rb);
-    const uint4* av = reinterpret_cast<const uint4*>(a) + lane;
     int isum[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -268,7 +284,7 @@ __device__ __forceinline__ void batch_q6k_terms(const uint8_t* rg, const uint8_t
                 const int si = 2 * seg + sub;  // sub-block within the half
                 const int s = 8 * h + si;
                 const int j = s >> 1, hh = s & 1;
-                const uint4 aj = av[32 * j];
+                const uint4 aj = A.q[j];
                 int c[4] = {0, 0, 0, 0};
                 mma_k16_s8u8(c, hh ? aj.z : aj.x, hh ? aj.w : aj.y, nib | top);
                 const int sca = byte_s(si < 4 ? sa0 : sa1, si & 3);
@@ -282,12 +298,10 @@ __device__ __forceinline__ void batch_q6k_terms(const uint8_t* rg, const uint8_t
     }
     // offset term: row g's scales for sub-blocks 4t .. 4t + 3 against the split sums
     const uint32_t scg = RG.at(192 + 4 * t);
-    const uint4 bs = reinterpret_cast<const uint4*>(a + kBatchImageBsumOffset)[lane];
     int olo[4] = {0, 0, 0, 0}, ohi[4] = {0, 0, 0, 0};
-    mma_k16_s8s8(olo, bs.x, bs.y, scg);
-    mma_k16_s8s8(ohi, bs.z, bs.w, scg);
-    const float* dxp = reinterpret_cast<const float*>(a + kBatchImageDOffset);
-    const float dxl = dxp[g], dxh = dxp[g + 8];
+    mma_k16_s8s8(olo, A.bs.x, A.bs.y, scg);
+    mma_k16_s8s8(ohi, A.bs.z, A.bs.w, scg);
+    const float dxl = A.dxl, dxh = A.dxh;
     const float dwa = f16_bits_to_f32(static_cast<uint16_t>(RA.at(208) & 0xFFFFu));
     const float dwb = f16_bits_to_f32(static_cast<uint16_t>(RB.at(208) & 0xFFFFu));
     const float dw[4] = {dwa, dwb, dwa, dwb}, dx[4] = {dxl, dxl, dxh, dxh};
@@ -319,10 +333,8 @@ __global__ void __launch_bounds__(kBatchThreads, 1) matvec_batch_kernel(const __
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kBatchMaxStages;
-    uint64_t* afull = empty + kBatchMaxStages;
     float* scratch = reinterpret_cast<float*>(smem + kBatchBarrierBytes);
-    uint8_t* abuf = smem + kBatchAOffset;
-    uint8_t* stage0 = smem + batch_stage_offset(bp.nb);
+    uint8_t* stage0 = smem + kBatchStageOffset;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t nb = bp.nb, S = bp.stages;
     const uint32_t G = (nb + 15u) / 16u;
@@ -341,7 +353,6 @@ __global__ void __launch_bounds__(kBatchThreads, 1) matvec_batch_kernel(const __
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NCW);
         }
-        mbar_init(afull, 1);
         fence_mbar_init();
         pdl_launch_dependents();
     }
@@ -351,18 +362,6 @@ __global__ void __launch_bounds__(kBatchThreads, 1) matvec_batch_kernel(const __
         // ---------------- producer
         const uint64_t policy = l2_policy_evict_first();
         const uintptr_t wbase = reinterpret_cast<uintptr_t>(bp.w);
-        if (lane == 0 && t0 < t1) {
-            // the segment's activation image (written by the preceding kernel)
-            pdl_wait();
-            const uint32_t bytes = nblk * kBatchImageBlockBytes;
-            mbar_arrive_expect_tx(afull, bytes);
-            for (uint32_t off = 0; off < bytes; off += 32768u) {
-                const uint32_t n = bytes - off < 32768u ? bytes - off : 32768u;
-                bulk_copy_g2s(abuf + off, bp.image + uint64_t(sg) * 16u * kBatchImageBlockBytes + off, n, afull,
-                              policy);
-            }
-        }
-        __syncwarp();
         uint32_t q = 0;  // stages issued
         for (uint32_t tile = t0; tile < t1; ++tile, ++q) {
             const uint32_t s = q % S;
@@ -391,7 +390,6 @@ __global__ void __launch_bounds__(kBatchThreads, 1) matvec_batch_kernel(const __
         // every copy this CTA issued lands before the CTA exits
         if (lane == 0) {
             for (uint32_t k = q > S ? q - S : 0; k < q; ++k) mbar_wait(&full[k % S], (k / S) & 1u, bp.status, 42);
-            if (t0 < t1) mbar_wait(afull, 0, bp.status, 43);
         }
         return;
     }
@@ -399,17 +397,17 @@ __global__ void __launch_bounds__(kBatchThreads, 1) matvec_batch_kernel(const __
     // ---------------- consumers.  A warp whose wait timed out skips the work
     // but takes every barrier and stage arrival, so no other warp waits on it.
     const uintptr_t wbase = reinterpret_cast<uintptr_t>(bp.w);
-    pdl_wait();  // the outputs may still be read by the preceding kernels
+    pdl_wait();  // the image comes from the preceding kernel; the outputs may still be read by it
     bool failed = false;
-    if (t0 < t1) {
-        const bool ok = mbar_wait(afull, 0, bp.status, 40);
-        failed = !__all_sync(0xFFFFFFFFu, ok);
-    }
     const int g = lane >> 2, t = lane & 3;
     // the tree's reader: output o = 8 warp + lane / 4 (e = o / 32, fragment lane o % 32), quarter s = lane % 4
     const uint32_t ro = 8u * warp + (lane >> 2), re = ro >> 5, rl = ro & 31u, rs = lane & 3;
     const uint32_t rvec = ((rl >> 2) + 8u * (re >> 1)), rrow = 2u * (rl & 3u) + (re & 1u);
-    const uint8_t* a = abuf + warp * kBatchImageBlockBytes;  // this warp's super-block of the image
+    // this warp's super-block of the segment: its activation operands, once
+    BatchA A;
+    if (t0 < t1 && static_cast<uint32_t>(warp) < nblk)
+        batch_load_a(bp.image + (uint64_t(sg) * 16u + warp) * kBatchImageBlockBytes, lane,
+                     kType == 12 ? kBatchImageBsum32Offset : kBatchImageBsum16Offset, A);
     uint32_t q = 0;
     for (uint32_t tile = t0; tile < t1; ++tile, ++q) {
         const uint32_t s = q % S;
@@ -429,9 +427,9 @@ __global__ void __launch_bounds__(kBatchThreads, 1) matvec_batch_kernel(const __
                 return st + r * kStride + (o & 15u);
             };
             if (kType == 12)
-                batch_q4k_terms(at(g), at(2 * t), at(2 * t + 1), a, lane, p);
+                batch_q4k_terms(at(g), at(2 * t), at(2 * t + 1), A, lane, p);
             else
-                batch_q6k_terms(at(g), at(2 * t), at(2 * t + 1), a, lane, p);
+                batch_q6k_terms(at(g), at(2 * t), at(2 * t + 1), A, lane, p);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);

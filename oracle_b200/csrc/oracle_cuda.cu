@@ -434,30 +434,31 @@ bool batch_q8k_fits(oracle_cuda_context* ctx, const void* w, uint64_t rows, uint
     if (reinterpret_cast<uintptr_t>(w) & 15u) return false;
     const uint64_t nb = cols / 256, G = (nb + 15) / 16, T = (rows + kBatchTileRows - 1) / kBatchTileRows;
     return nb > 0 && G <= uint64_t(ctx->sm_count) && T < 0x7FFFFFFFull &&
-           batch_stage_offset(static_cast<uint32_t>(nb < 16 ? nb : 16)) + 2 * batch_stage_bytes(kTypeQ6_K) <=
+           kBatchStageOffset + 2 * batch_stage_bytes(kTypeQ6_K) <=
                uint64_t(ctx->max_smem_optin);
 }
 
-// Batched Q8_K matvec (matvec_batch.cuh): 2..16 vectors x[b][cols] -> y[b][rows].
-oracle_cuda_status launch_q8k_batch(oracle_cuda_context* ctx, uint32_t type, const void* w, uint64_t rows,
-                                    uint64_t cols, uint64_t row_bytes, const float* x, uint32_t batch, float* y,
-                                    cudaStream_t stream) {
+// Batch image of x[batch][cols] (batch <= 16) into `image` (nb blocks).
+oracle_cuda_status launch_batch_quantize(oracle_cuda_context* ctx, const float* x, uint32_t batch, uint32_t nb,
+                                         uint8_t* image, cudaStream_t stream) {
+    return launch(ctx, quantize_batch_image_kernel, dim3(2 * nb), dim3(256), 0, stream,
+                  (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, x, batch, nb, image);
+}
+
+// Batched Q8_K matvec (matvec_batch.cuh) of a batch image -> y[b][rows].
+oracle_cuda_status launch_batch_matvec(oracle_cuda_context* ctx, uint32_t type, const void* w, uint64_t rows,
+                                       uint64_t cols, uint64_t row_bytes, const uint8_t* image, uint32_t batch,
+                                       float* y, cudaStream_t stream) {
     const uint32_t nb = static_cast<uint32_t>(cols / 256), G = (nb + 15) / 16;
     const uint64_t T = (rows + kBatchTileRows - 1) / kBatchTileRows;
-    if (oracle_cuda_status s = grow_device(ctx, ctx->batch_image, ctx->batch_image_len,
-                                           uint64_t(nb) * kBatchImageBlockBytes))
-        return s;
     if (G > 1)
         if (oracle_cuda_status s =
                 grow_device(ctx, ctx->batch_partial, ctx->batch_partial_len, G * uint64_t(batch) * rows))
             return s;
     const bool pdl = (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0;
-    if (oracle_cuda_status s = launch(ctx, quantize_batch_image_kernel, dim3(2 * nb), dim3(256), 0, stream, pdl, x,
-                                      batch, nb, type, ctx->batch_image))
-        return s;
     BatchParams bp{};
     bp.w = static_cast<const uint8_t*>(w);
-    bp.image = ctx->batch_image;
+    bp.image = image;
     bp.out = G > 1 ? ctx->batch_partial : y;
     bp.rows = rows;
     bp.row_bytes = row_bytes;
@@ -467,7 +468,7 @@ oracle_cuda_status launch_q8k_batch(oracle_cuda_context* ctx, uint32_t type, con
     const uint64_t items = T * G;
     const uint32_t grid = static_cast<uint32_t>(items < uint64_t(ctx->sm_count) ? items : ctx->sm_count);
     const uint64_t budget = ctx->smem_budget ? ctx->smem_budget : uint64_t(ctx->max_smem_optin);
-    const uint32_t off = batch_stage_offset(nb);
+    const uint32_t off = kBatchStageOffset;
     const uint32_t stage = type == kTypeQ4_K ? batch_stage_bytes(12) : batch_stage_bytes(14);
     uint64_t stages = budget > off ? (budget - off) / stage : 0;
     if (stages > uint64_t(kBatchMaxStages)) stages = kBatchMaxStages;
@@ -483,6 +484,18 @@ oracle_cuda_status launch_q8k_batch(oracle_cuda_context* ctx, uint32_t type, con
     const uint64_t blocks = (n + 255) / 256;
     return launch(ctx, batch_combine_kernel, dim3(static_cast<uint32_t>(blocks < 4096 ? blocks : 4096)), dim3(256), 0,
                   stream, pdl, static_cast<const float*>(ctx->batch_partial), y, n, G);
+}
+
+// 2..16 vectors x[b][cols] -> y[b][rows] through the context's image buffer.
+oracle_cuda_status launch_q8k_batch(oracle_cuda_context* ctx, uint32_t type, const void* w, uint64_t rows,
+                                    uint64_t cols, uint64_t row_bytes, const float* x, uint32_t batch, float* y,
+                                    cudaStream_t stream) {
+    const uint32_t nb = static_cast<uint32_t>(cols / 256);
+    if (oracle_cuda_status s = grow_device(ctx, ctx->batch_image, ctx->batch_image_len,
+                                           uint64_t(nb) * kBatchImageBlockBytes))
+        return s;
+    if (oracle_cuda_status s = launch_batch_quantize(ctx, x, batch, nb, ctx->batch_image, stream)) return s;
+    return launch_batch_matvec(ctx, type, w, rows, cols, row_bytes, ctx->batch_image, batch, y, stream);
 }
 
 // The device bytes a host-pointer call reads for a weight span: the resident
@@ -766,6 +779,53 @@ oracle_cuda_status oracle_cuda_storage_matvec(oracle_cuda_context* ctx, int cont
     if (!x_dev || !y_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "activation or output pointer is null");
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
     s = run_matvec(ctx, contract, type, rows, cols, rb, w_dev, x_dev, batch, y_dev, static_cast<cudaStream_t>(stream));
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+uint64_t oracle_cuda_batch_image_bytes(uint64_t cols) {
+    return cols == 0 || cols % 256 != 0 ? 0 : cols / 256 * kBatchImageBlockBytes;
+}
+
+oracle_cuda_status oracle_cuda_batch_quantize(oracle_cuda_context* ctx, const float* x_dev, uint64_t cols,
+                                              uint32_t batch, void* image_dev, uint64_t image_nbytes, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (cols == 0 || cols % 256 != 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Q8_K activations need a multiple of 256 columns");
+    if (batch == 0 || batch > uint32_t(kBatchMax))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "a batch image holds 1 to 16 vectors");
+    if (cols / 256 > 0xFFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "rows longer than 2^36 elements");
+    if (image_nbytes < oracle_cuda_batch_image_bytes(cols))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "batch image buffer too small");
+    if (!x_dev || !image_dev || (reinterpret_cast<uintptr_t>(image_dev) & 15u))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "activation pointer null or image pointer not 16-byte aligned");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s = launch_batch_quantize(ctx, x_dev, batch, static_cast<uint32_t>(cols / 256),
+                                                       static_cast<uint8_t*>(image_dev),
+                                                       static_cast<cudaStream_t>(stream));
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+oracle_cuda_status oracle_cuda_batch_matvec(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
+                                            const void* w_dev, uint64_t w_nbytes, const void* image_dev,
+                                            uint64_t image_nbytes, uint32_t batch, float* y_dev, uint64_t y_len,
+                                            void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (batch == 0 || batch > uint32_t(kBatchMax))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "a batch image holds 1 to 16 vectors");
+    uint64_t rb = 0, nvec = 0;
+    oracle_cuda_status s = validate_matvec(ctx, ORACLE_CUDA_CONTRACT_Q8K, type, rows, cols, w_nbytes,
+                                           uint64_t(batch) * cols, y_len, &rb, &nvec);
+    if (s != ORACLE_CUDA_OK) return s;
+    if (image_nbytes < oracle_cuda_batch_image_bytes(cols))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "batch image buffer too small");
+    if (!image_dev || !y_dev || (reinterpret_cast<uintptr_t>(image_dev) & 15u))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "output pointer null or image pointer not 16-byte aligned");
+    if (!batch_q8k_fits(ctx, w_dev, rows, cols))
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED,
+                    "batched matvec needs 16-byte aligned weights and at most one 4096-column segment per SM");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    s = launch_batch_matvec(ctx, type, w_dev, rows, cols, rb, static_cast<const uint8_t*>(image_dev), batch, y_dev,
+                            static_cast<cudaStream_t>(stream));
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
 
@@ -2543,6 +2603,43 @@ extern "C" oracle_cuda_status oracle_cuda_gdn_gates(oracle_cuda_context* ctx, co
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
 
+extern "C" oracle_cuda_status oracle_cuda_argmax_rows(oracle_cuda_context* ctx, const float* x_dev, uint32_t rows,
+                                                      uint64_t n, unsigned long long* keys_dev, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (n == 0 || rows == 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "cannot sample an empty logits vector");
+    if (n > 0xFFFFFFFFull) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "logits vector exceeds token-id range");
+    if (rows > 65535) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "at most 65535 logits rows per call");
+    if (!x_dev || !keys_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "null logits or key");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    ORACLE_CUDA_TRY(ctx, cudaMemsetAsync(keys_dev, 0, rows * sizeof(unsigned long long), st), "cudaMemsetAsync");
+    uint64_t blocks = (n + 255) / 256;
+    const uint64_t cap = (uint64_t(ctx->sm_count) * 4 + rows - 1) / rows;
+    if (blocks > cap) blocks = cap;
+    const oracle_cuda_status s =
+        launch(ctx, argmax_kernel, dim3(static_cast<uint32_t>(blocks), rows), dim3(256), 0, st,
+               (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, x_dev, n, 0u, keys_dev);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
+extern "C" oracle_cuda_status oracle_cuda_token_commit_rows(oracle_cuda_context* ctx, unsigned long long* keys_dev,
+                                                            uint32_t rows, const uint32_t* prompt_dev,
+                                                            uint32_t n_prompt, uint32_t* pos_dev,
+                                                            uint32_t* next_id_dev, uint32_t* tokens_dev,
+                                                            uint32_t tokens_capacity, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (rows == 0) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "no sequences to commit");
+    if (!keys_dev || !pos_dev || !next_id_dev || (n_prompt > 0 && !prompt_dev) ||
+        (tokens_capacity > 0 && !tokens_dev))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "token commit pointer is null");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s =
+        launch(ctx, token_commit_rows_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream),
+               (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, keys_dev, rows, prompt_dev, n_prompt, pos_dev, next_id_dev,
+               tokens_dev, tokens_capacity, ctx->status);
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
 extern "C" oracle_cuda_status oracle_cuda_token_commit(oracle_cuda_context* ctx, const unsigned long long* key_dev,
                                                        const uint32_t* prompt_dev, uint32_t n_prompt,
                                                        uint32_t* pos_dev, uint32_t* next_id_dev,
@@ -2568,7 +2665,21 @@ extern "C" oracle_cuda_status oracle_cuda_gdn_core(oracle_cuda_context* ctx, con
                                                    float* state_dev, const float* norm_dev, uint32_t key_heads,
                                                    uint32_t value_heads, uint32_t head_dim, uint32_t conv_kernel,
                                                    float eps, const uint32_t* pos_dev, float* out_dev, void* stream) {
+    return oracle_cuda_gdn_core_seqs(ctx, qkv_dev, z_dev, beta_dev, alpha_dev, time_step_bias_dev, decay_dev,
+                                     conv_weights_dev, history_dev, state_dev, norm_dev, key_heads, value_heads,
+                                     head_dim, conv_kernel, eps, pos_dev, 1, out_dev, stream);
+}
+
+extern "C" oracle_cuda_status oracle_cuda_gdn_core_seqs(oracle_cuda_context* ctx, const float* qkv_dev,
+                                                        const float* z_dev, const float* beta_dev,
+                                                        const float* alpha_dev, const float* time_step_bias_dev,
+                                                        const float* decay_dev, const float* conv_weights_dev,
+                                                        float* history_dev, float* state_dev, const float* norm_dev,
+                                                        uint32_t key_heads, uint32_t value_heads, uint32_t head_dim,
+                                                        uint32_t conv_kernel, float eps, const uint32_t* pos_dev,
+                                                        uint32_t seqs, float* out_dev, void* stream) {
     if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (seqs == 0 || seqs > 65535) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "sequence count must be in [1, 65535]");
     if (key_heads == 0 || value_heads == 0 || value_heads % key_heads != 0)
         return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Qwen3.5 repeated-head dimensions are incompatible");
     if (conv_kernel == 0 || head_dim == 0)
@@ -2580,7 +2691,8 @@ extern "C" oracle_cuda_status oracle_cuda_gdn_core(oracle_cuda_context* ctx, con
     if (!pos_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "position pointer is null");
     ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
     const oracle_cuda_status s =
-        launch(ctx, head_dim == 128 ? gdn_core_kernel<128> : gdn_core_kernel<64>, dim3(value_heads), dim3(4 * head_dim), 0,
+        launch(ctx, head_dim == 128 ? gdn_core_kernel<128> : gdn_core_kernel<64>, dim3(value_heads, seqs),
+               dim3(4 * head_dim), 0,
                static_cast<cudaStream_t>(stream), (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, qkv_dev, z_dev, beta_dev, alpha_dev, time_step_bias_dev,
                decay_dev, conv_weights_dev, history_dev, state_dev, norm_dev, key_heads, value_heads, conv_kernel,
                eps, pos_dev, out_dev);
