@@ -52,10 +52,38 @@ def _stale(target: str, deps) -> bool:
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 
+BUILD_DIR = os.path.join(HERE, "_build")
+LIBM_GEN_SRC = os.path.join(CSRC, "libm_tables.c")
+LIBM_TABLES = os.path.join(BUILD_DIR, "libm_tables.bin")
+LIBM_OBJ = os.path.join(BUILD_DIR, "libm_blob.o")
+
+
+def build_libm_tables() -> str:
+    """The host C library's expf / log1pf correction tables (csrc/libm_tables.c:
+    runs the library on every float input of the decoder's domains, ~1 min on 8
+    cores), assembled into an object that is linked into liboracle_cuda.so."""
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    gen = os.path.join(BUILD_DIR, "libm_tables")
+    if _stale(gen, [LIBM_GEN_SRC]):
+        subprocess.run(["gcc", "-O2", "-pthread", "-o", gen, LIBM_GEN_SRC, "-lm"], check=True)
+    if _stale(LIBM_TABLES, [gen]):
+        _say("generating the expf/log1pf tables from the host C library (about a minute)")
+        subprocess.run([gen, LIBM_TABLES], check=True)
+    if _stale(LIBM_OBJ, [LIBM_TABLES]):
+        asm = os.path.join(BUILD_DIR, "libm_blob.S")
+        with open(asm, "w") as f:
+            f.write("\t.section .rodata\n\t.balign 16\n\t.globl oracle_libm_blob\noracle_libm_blob:\n"
+                    f"\t.incbin \"{LIBM_TABLES}\"\n\t.globl oracle_libm_blob_end\noracle_libm_blob_end:\n"
+                    "\t.section .note.GNU-stack,\"\",@progbits\n")
+        subprocess.run(["gcc", "-c", "-fPIC", "-o", LIBM_OBJ, asm], check=True)
+    return LIBM_OBJ
+
+
 def build_cuda(force: bool = False, verbose: bool = False) -> str:
-    if force or _stale(LIB, _sources()):
+    obj = build_libm_tables()
+    if force or _stale(LIB, _sources() + [obj]):
         cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-               "-o", LIB, os.path.join(CSRC, "oracle_cuda.cu")]
+               "-o", LIB, os.path.join(CSRC, "oracle_cuda.cu"), obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         subprocess.run(cmd, check=True)

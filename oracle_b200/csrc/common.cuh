@@ -178,14 +178,63 @@ __device__ __forceinline__ int sbyte(uint32_t w, int i) {
     return static_cast<int>(static_cast<int8_t>((w >> (8 * i)) & 0xFFu));
 }
 
+// ---------------------------------------------------------------- the host library's expf / log1pf
+//
+// Oracle evaluates exp and log1p on floats with the host C library (expf,
+// log1pf), which is not correctly rounded everywhere; under the Q8_K contract
+// a last-bit difference of an activation can change a quantized value, so
+// the decoder reproduces the library's results bit for bit: the value in
+// double precision rounded once to float (correctly rounded unless the exact
+// value is within 2^-48 of a float midpoint), corrected from tables that the
+// build generates by running the library (csrc/libm_tables.c) on every float
+// input of the domain: expf on [-104, 89], log1pf on expf([-20, 20]).
+// Layout of g_libm (uint32 words): magic, expf entries, log1pf entries, 0,
+// expf bucket offsets [2^20 + 1], log1pf bucket offsets [2^20 + 1], then
+// (key bits, value bits) pairs sorted by key, expf's then log1pf's; bucket =
+// key >> 12.  Zeroed (no corrections) until the host loads the tables.
+constexpr uint32_t kLibmBuckets = 1u << 20;
+constexpr uint64_t kLibmHeaderWords = 4;
+constexpr uint64_t kLibmMaxWords = 12'000'000;  // 48 MB: ~11 M words used
+__device__ uint32_t g_libm[kLibmMaxWords];
+
+__device__ __forceinline__ bool libm_correction(uint32_t table, uint32_t key, uint32_t& value) {
+    const uint32_t* off = g_libm + kLibmHeaderWords + uint64_t(table) * (kLibmBuckets + 1);
+    const uint32_t first = __ldg(off + (key >> 12)), last = __ldg(off + (key >> 12) + 1);
+    if (first == last) return false;
+    const uint64_t base = kLibmHeaderWords + 2ull * (kLibmBuckets + 1) + (table ? 2ull * __ldg(g_libm + 1) : 0ull);
+    const uint2* e = reinterpret_cast<const uint2*>(g_libm + base);
+    for (uint32_t i = first; i < last; ++i) {
+        const uint2 kv = __ldg(e + i);
+        if (kv.x == key) {
+            value = kv.y;
+            return true;
+        }
+    }
+    return false;
+}
+
+// expf as the host library computes it.
+__device__ __forceinline__ float ref_expf(float x) {
+    uint32_t v;
+    if (libm_correction(0, __float_as_uint(x), v)) return __uint_as_float(v);
+    return __double2float_rn(exp(static_cast<double>(x)));
+}
+
+// log1pf as the host library computes it, for arguments expf(v), v in [-20, 20].
+__device__ __forceinline__ float ref_log1pf(float y) {
+    uint32_t v;
+    if (libm_correction(1, __float_as_uint(y), v)) return __uint_as_float(v);
+    return __double2float_rn(log1p(static_cast<double>(y)));
+}
+
 // sigmoid and silu of Oracle's block code (qwen35_block.cpp:138-159): float
 // arithmetic around the float exponential.
 __device__ __forceinline__ float ref_sigmoid(float v) {
     if (v >= 0.0f) {
-        const float e = expf(-v);
+        const float e = ref_expf(-v);
         return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
     }
-    const float e = expf(v);
+    const float e = ref_expf(v);
     return __fdiv_rn(e, __fadd_rn(1.0f, e));
 }
 

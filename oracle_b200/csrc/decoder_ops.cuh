@@ -6,8 +6,9 @@
 // wherever the order is a sequential sum.  Where the reference sums
 // sequentially in double, these kernels sum in double in a tree; the double
 // result is then rounded to float, so the float outputs agree except when the
-// double sums straddle a float rounding boundary.  exp() is CUDA's expf,
-// within 2 ulp of glibc's.
+// double sums straddle a float rounding boundary.  exp() and log1p() are the
+// host C library's float functions bit for bit (ref_expf / ref_log1pf,
+// common.cuh).
 //   rms_norm_rows_kernel   <- rms_norm_rows           (qwen35_block.cpp:161-188)
 //   rope_kernel            <- apply_qwen35_rope       (reference_kernels.cpp:74-123),
 //                             cos/sin from a table the host computes with the
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(256) attention_output_kernel(float* __restrict
     for (uint32_t w = 0; w < (blockDim.x >> 5); ++w) m = fmaxf(m, fmax_s[w]);
     double den = 0.0;
     for (uint32_t t = threadIdx.x; t < tokens; t += blockDim.x) {
-        const float e = expf(__fsub_rn(sc[t], m));
+        const float e = ref_expf(__fsub_rn(sc[t], m));
         sc[t] = e;
         den = __dadd_rn(den, static_cast<double>(e));
     }
@@ -208,7 +209,7 @@ __global__ void gated_delta_kernel(const float* __restrict__ q, const float* __r
     }
     __syncthreads();
     if (vi >= value_dim) return;
-    const float decay = expf(log_decay[h]);
+    const float decay = ref_expf(log_decay[h]);
     const float b = beta[h];
     float* sh = state + static_cast<uint64_t>(h) * key_dim * value_dim + vi;
     float mem = 0.0f;

@@ -35,8 +35,8 @@ __device__ __forceinline__ void report_overflow(DeviceStatus* st, uint32_t pos) 
 __device__ __forceinline__ float ref_softplus(float v) {
     // qwen35_block.cpp:147-155
     if (v > 20.0f) return v;
-    if (v < -20.0f) return expf(v);
-    return log1pf(expf(v));
+    if (v < -20.0f) return ref_expf(v);
+    return ref_log1pf(ref_expf(v));
 }
 
 __global__ void __launch_bounds__(256) rope_pos_kernel(float* __restrict__ heads, uint32_t n_heads, uint32_t head_dim,
@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(256) attention_output_pos_kernel(float* __rest
     for (uint32_t w = 0; w < (blockDim.x >> 5); ++w) m = fmaxf(m, fmax_s[w]);
     double den = 0.0;
     for (uint32_t t = threadIdx.x; t < tokens; t += blockDim.x) {
-        const float e = expf(__fsub_rn(sc[t], m));
+        const float e = ref_expf(__fsub_rn(sc[t], m));
         sc[t] = e;
         den = __dadd_rn(den, static_cast<double>(e));
     }
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restric
         (which == 0 ? q_s : which == 1 ? k_s : v_s)[ci] = r;
     } else if (tid == 3 * kD) {
         gate_s[0] = ref_sigmoid(beta_in[h]);
-        gate_s[1] = expf(__fmul_rn(ref_softplus(__fadd_rn(alpha[h], dt_bias[h])), decay_a[h]));
+        gate_s[1] = ref_expf(__fmul_rn(ref_softplus(__fadd_rn(alpha[h], dt_bias[h])), decay_a[h]));
     }
     __syncthreads();
     // gated_delta_step: l2-normalised q (scaled by 1/sqrt(key_dim)) and k

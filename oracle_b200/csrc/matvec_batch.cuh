@@ -25,13 +25,15 @@
 //
 // Work items are (tile of 8 rows, segment).  The CTAs are shared out among the
 // segments (CTA c works on segment c * G / grid) and each splits its
-// segment's tiles evenly.  Per item, 16 consumer warps share a stage of
-// 8 rows x the segment's super-blocks: warp r computes leaf r (0 + p_r, or 0
-// past the row's end) and, working on super-block r for every tile, holds that
-// block's activation operands in registers for the whole launch.  The leaves meet in shared memory and
-// the tree runs across lanes in its own order --
-// ((L0 + L8) + (L4 + L12)) + ((L2 + L10) + (L6 + L14)) for N3(0) and the odd
-// leaves for N3(1), root = N3(0) + N3(1).  With one segment per row
+// segment's tiles evenly.  Per item, 8 consumer warps share a stage of
+// 8 rows x the segment's super-blocks: warp r computes leaves r and r + 8
+// (0 + p, or 0 past the row's end) side by side and adds them -- the tree's
+// first level, N1(r) = L_r + L_{r+8} -- and, working on the same two
+// super-blocks for every tile, holds their activation operands in registers
+// for the whole launch.  The N1 values meet in shared memory and the rest of
+// the tree runs across lanes in its own order:
+// N3(0) = (N1(0) + N1(4)) + (N1(2) + N1(6)), N3(1) the same over the odd
+// ones, root = N3(0) + N3(1).  With one segment per row
 // y = 0 + root; with several, each root goes to a partial-sum buffer and a
 // second kernel adds a row's segments in order (batch_combine_kernel).
 //
@@ -44,7 +46,7 @@
 namespace oracle_cuda {
 
 constexpr int kBatchMax = 16;             // vectors per launch (the MMA's M)
-constexpr int kBatchConsumerWarps = 16;   // warp r: super-block r of a segment
+constexpr int kBatchConsumerWarps = 8;    // warp r: super-blocks r and r + 8 of a segment
 constexpr int kBatchThreads = (kBatchConsumerWarps + 1) * 32;
 constexpr int kBatchTileRows = 8;         // weight rows per item (the MMA's N)
 constexpr int kBatchMaxStages = 12;
@@ -69,11 +71,12 @@ constexpr uint32_t kBatchImageBsum16Offset = 4096;
 constexpr uint32_t kBatchImageBsum32Offset = 4608;
 constexpr uint32_t kBatchImageDOffset = 5120;
 
-// Shared-memory layout of matvec_batch_kernel: barriers, two items of leaves
-// (16 warps x 4 outputs x 32 lanes, each warp's block padded by 8 floats so
-// that the tree's reads hit distinct banks), then the stage ring.
+// Shared-memory layout of matvec_batch_kernel: barriers, two items of the
+// tree's first level (8 warps x 4 outputs x 32 lanes, each warp's block padded
+// by 16 floats so that the tree's reads hit distinct banks), then the stage
+// ring.
 constexpr uint32_t kBatchBarrierBytes = 256;
-constexpr uint32_t kBatchLeafPitch = 4 * 32 + 8;
+constexpr uint32_t kBatchLeafPitch = 4 * 32 + 16;
 constexpr uint32_t kBatchScratchBytes = 2 * kBatchConsumerWarps * kBatchLeafPitch * 4;
 constexpr uint32_t kBatchStageOffset = align_up(kBatchBarrierBytes + kBatchScratchBytes, 128u);
 // A stage row holds a segment of 16 super-blocks plus the 16-byte alignment
@@ -214,7 +217,10 @@ __device__ __forceinline__ void batch_q4k_terms(const uint8_t* rg, const uint8_t
     // 6-bit scales of rows 2t, 2t + 1 for sub-blocks 0..3 / 4..7
     const uint32_t sa_lo = ha.y & 0x3F3F3F3Fu, sa_hi = (ha.w & 0x0F0F0F0Fu) | ((ha.y >> 2) & 0x30303030u);
     const uint32_t sb_lo = hb.y & 0x3F3F3F3Fu, sb_hi = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
-    int isum[4] = {0, 0, 0, 0};
+    // The high-nibble sub-blocks multiply the bytes as stored (16 x nibble,
+    // still u8): their scaled sums are exactly 16 x the true ones (|sum| <
+    // 2^28) and are divided back once at the end, saving a shift per word.
+    int isum[4] = {0, 0, 0, 0}, isum16[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int g64 = 0; g64 < 4; ++g64) {
         const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rg + 16 + 32 * g64 + 4 * t);
@@ -222,18 +228,20 @@ __device__ __forceinline__ void batch_q4k_terms(const uint8_t* rg, const uint8_t
 #pragma unroll
         for (int hi = 0; hi < 2; ++hi) {
             const int j = 2 * g64 + hi;
-            const uint32_t b0 = hi ? ((w0 >> 4) & 0x0F0F0F0Fu) : (w0 & 0x0F0F0F0Fu);
-            const uint32_t b1 = hi ? ((w1 >> 4) & 0x0F0F0F0Fu) : (w1 & 0x0F0F0F0Fu);
+            const uint32_t mask = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
             int c[4] = {0, 0, 0, 0};
-            mma_k32_s8u8(c, A.q[j], b0, b1);
+            mma_k32_s8u8(c, A.q[j], w0 & mask, w1 & mask);
             const int sca = byte_u(j < 4 ? sa_lo : sa_hi, j & 3);
             const int scb = byte_u(j < 4 ? sb_lo : sb_hi, j & 3);
-            isum[0] += sca * c[0];
-            isum[1] += scb * c[1];
-            isum[2] += sca * c[2];
-            isum[3] += scb * c[3];
+            int (&acc)[4] = hi ? isum16 : isum;
+            acc[0] += sca * c[0];
+            acc[1] += scb * c[1];
+            acc[2] += sca * c[2];
+            acc[3] += scb * c[3];
         }
     }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) isum[e] += isum16[e] >> 4;
     // min term: the mins of row g for sub-blocks 4t .. 4t + 3 against the split sums
     const uint32_t mn = t == 0 ? (hg.z & 0x3F3F3F3Fu)
                                : t == 1 ? (((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u)) : 0u;
@@ -400,14 +408,15 @@ __global__ void __launch_bounds__(kBatchThreads, 1) matvec_batch_kernel(const __
     pdl_wait();  // the image comes from the preceding kernel; the outputs may still be read by it
     bool failed = false;
     const int g = lane >> 2, t = lane & 3;
-    // the tree's reader: output o = 8 warp + lane / 4 (e = o / 32, fragment lane o % 32), quarter s = lane % 4
-    const uint32_t ro = 8u * warp + (lane >> 2), re = ro >> 5, rl = ro & 31u, rs = lane & 3;
+    // the tree's reader: output o = 16 warp + lane / 2 (e = o / 32, fragment lane o % 32), half s = lane % 2
+    const uint32_t ro = 16u * warp + (lane >> 1), re = ro >> 5, rl = ro & 31u, rs = lane & 1;
     const uint32_t rvec = ((rl >> 2) + 8u * (re >> 1)), rrow = 2u * (rl & 3u) + (re & 1u);
-    // this warp's super-block of the segment: its activation operands, once
-    BatchA A;
-    if (t0 < t1 && static_cast<uint32_t>(warp) < nblk)
-        batch_load_a(bp.image + (uint64_t(sg) * 16u + warp) * kBatchImageBlockBytes, lane,
-                     kType == 12 ? kBatchImageBsum32Offset : kBatchImageBsum16Offset, A);
+    // this warp's two super-blocks of the segment: their activation operands, once
+    const uint32_t sb0 = warp, sb1 = warp + 8;
+    const uint32_t bsum = kType == 12 ? kBatchImageBsum32Offset : kBatchImageBsum16Offset;
+    BatchA A0{}, A1{};
+    if (t0 < t1 && sb0 < nblk) batch_load_a(bp.image + (uint64_t(sg) * 16u + sb0) * kBatchImageBlockBytes, lane, bsum, A0);
+    if (t0 < t1 && sb1 < nblk) batch_load_a(bp.image + (uint64_t(sg) * 16u + sb1) * kBatchImageBlockBytes, lane, bsum, A1);
     uint32_t q = 0;
     for (uint32_t tile = t0; tile < t1; ++tile, ++q) {
         const uint32_t s = q % S;
@@ -416,33 +425,46 @@ __global__ void __launch_bounds__(kBatchThreads, 1) matvec_batch_kernel(const __
             const bool ok = mbar_wait(&full[s], (q / S) & 1u, bp.status, 44);
             failed = !__all_sync(0xFFFFFFFFu, ok);
         }
-        float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (!failed && static_cast<uint32_t>(warp) < nblk) {
+        float p0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, p1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (!failed) {
             // a stage row starts at the segment's first byte rounded down to 16;
-            // super-block `warp` sits at that remainder + warp * kBB
-            const uint8_t* st = stage0 + size_t(s) * kStage + warp * kBB;
-            auto at = [&](uint32_t r) {
-                if (kType == 12) return st + r * kStride;  // rows are 16-byte multiples
+            // super-block sb sits at that remainder + sb * kBB.  Both blocks are
+            // computed unconditionally (one basic block, so their instructions
+            // interleave); a block past the row's end reads stale bytes inside
+            // the stage row and its term is replaced by 0 below.
+            const uint8_t* st = stage0 + size_t(s) * kStage;
+            auto head = [&](uint32_t r) -> uint32_t {
+                if (kType == 12) return r * kStride;  // rows are 16-byte multiples
                 const uintptr_t o = wbase + (row0 + r) * bp.row_bytes + seg_off;
-                return st + r * kStride + (o & 15u);
+                return r * kStride + static_cast<uint32_t>(o & 15u);
             };
-            if (kType == 12)
-                batch_q4k_terms(at(g), at(2 * t), at(2 * t + 1), A, lane, p);
-            else
-                batch_q6k_terms(at(g), at(2 * t), at(2 * t + 1), A, lane, p);
+            const uint32_t hg = head(g), ha = head(2 * t), hb = head(2 * t + 1);
+            const uint8_t* s0 = st + sb0 * kBB;
+            const uint8_t* s1 = st + sb1 * kBB;
+            if (kType == 12) {
+                batch_q4k_terms(s0 + hg, s0 + ha, s0 + hb, A0, lane, p0);
+                batch_q4k_terms(s1 + hg, s1 + ha, s1 + hb, A1, lane, p1);
+            } else {
+                batch_q6k_terms(s0 + hg, s0 + ha, s0 + hb, A0, lane, p0);
+                batch_q6k_terms(s1 + hg, s1 + ha, s1 + hb, A1, lane, p1);
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        // leaf r = 0 + p_r (0 past the row's end) into shared memory
+        // the tree's first level in registers: N1(r) = L_r + L_{r+8}, leaves
+        // 0 + p (0 past the row's end)
         float* sc = scratch + (q & 1u) * (NCW * kBatchLeafPitch);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sc[warp * kBatchLeafPitch + e * 32 + lane] = __fadd_rn(0.0f, p[e]);
+        for (int e = 0; e < 4; ++e) {
+            const float l0 = sb0 < nblk ? __fadd_rn(0.0f, p0[e]) : 0.0f;
+            const float l1 = sb1 < nblk ? __fadd_rn(0.0f, p1[e]) : 0.0f;
+            sc[warp * kBatchLeafPitch + e * 32 + lane] = __fadd_rn(l0, l1);
+        }
         named_barrier_sync(1, NCW * 32);
-        // N2(s) = (L_s + L_{s+8}) + (L_{s+4} + L_{s+12}); N3 = N2(s) + N2(s ^ 2); root = N3(0) + N3(1)
+        // N3(s) = (N1(s) + N1(s+4)) + (N1(s+2) + N1(s+6)); root = N3(0) + N3(1)
         const float* lf = sc + re * 32 + rl;
-        const float n2 = __fadd_rn(__fadd_rn(lf[rs * kBatchLeafPitch], lf[(rs + 8) * kBatchLeafPitch]),
-                                   __fadd_rn(lf[(rs + 4) * kBatchLeafPitch], lf[(rs + 12) * kBatchLeafPitch]));
-        const float n3 = __fadd_rn(n2, __shfl_xor_sync(0xFFFFFFFFu, n2, 2));
+        const float n3 = __fadd_rn(__fadd_rn(lf[rs * kBatchLeafPitch], lf[(rs + 4) * kBatchLeafPitch]),
+                                   __fadd_rn(lf[(rs + 2) * kBatchLeafPitch], lf[(rs + 6) * kBatchLeafPitch]));
         const float root = __fadd_rn(n3, __shfl_xor_sync(0xFFFFFFFFu, n3, 1));
         if (rs == 0 && !failed && rvec < bp.batch && row0 + rrow < bp.rows) {
             const uint64_t yi = uint64_t(rvec) * bp.rows + row0 + rrow;

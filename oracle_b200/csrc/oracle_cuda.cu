@@ -589,6 +589,35 @@ oracle_cuda_status oracle_ggml_row_byte_size(uint64_t row_elements, uint32_t typ
     return ORACLE_CUDA_OK;
 }
 
+// The host C library's expf / log1pf corrections (common.cuh, g_libm), generated
+// at build time by csrc/libm_tables.c and linked into this library as a blob.
+extern "C" const unsigned char oracle_libm_blob[];
+extern "C" const unsigned char oracle_libm_blob_end[];
+
+namespace {
+
+std::mutex g_libm_mutex;
+bool g_libm_loaded[64] = {};
+
+// Once per device, with that device current: copy the tables into g_libm.
+oracle_cuda_status libm_tables_load(int device) {
+    if (device < 0 || device >= 64) return fail(nullptr, ORACLE_CUDA_UNSUPPORTED, "device index too large");
+    std::lock_guard<std::mutex> lock(g_libm_mutex);
+    if (g_libm_loaded[device]) return ORACLE_CUDA_OK;
+    const uint64_t bytes = static_cast<uint64_t>(oracle_libm_blob_end - oracle_libm_blob);
+    uint32_t hdr[4] = {};
+    if (bytes >= sizeof hdr) std::memcpy(hdr, oracle_libm_blob, sizeof hdr);
+    const uint64_t words = kLibmHeaderWords + 2ull * (kLibmBuckets + 1) + 2ull * (uint64_t(hdr[1]) + hdr[2]);
+    if (bytes < sizeof hdr || hdr[0] != 0x314D424Cu || bytes != words * 4 || words > kLibmMaxWords)
+        return fail(nullptr, ORACLE_CUDA_CUDA_ERROR, "the library's expf/log1pf tables are missing or malformed");
+    const cudaError_t e = cudaMemcpyToSymbol(g_libm, oracle_libm_blob, bytes);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaMemcpyToSymbol(expf/log1pf tables)");
+    g_libm_loaded[device] = true;
+    return ORACLE_CUDA_OK;
+}
+
+}  // namespace
+
 oracle_cuda_status oracle_cuda_create(int device, oracle_cuda_context** out) {
     if (!out) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "output pointer is null");
     *out = nullptr;
@@ -604,6 +633,7 @@ oracle_cuda_status oracle_cuda_create(int device, oracle_cuda_context** out) {
     if (prop.major != 10)
         return fail(nullptr, ORACLE_CUDA_UNSUPPORTED,
                     std::string("this library is built for sm_100a (B200); device is ") + prop.name);
+    if (oracle_cuda_status ls = libm_tables_load(device)) return ls;
     auto* ctx = new oracle_cuda_context();
     ctx->device = device;
     ctx->sm_count = prop.multiProcessorCount;

@@ -11,10 +11,12 @@ Sampler compiled from its sources (oracle/ref_qwen35.cpp):
   contract from the same file.
 
 Criterion: identical greedy tokens (the north star's decoder bar).  Logits of
-the first steps are also compared: bit-identical matvecs, so the differences
-come from CUDA's expf/log1pf (within 2 ulp of glibc's) and the order of
-double sums inside RMSNorm / attention / gated delta; after 4 blocks they stay
-below 1e-3 of the logits' standard deviation (measured 1e-6 .. 1e-5).
+the first steps are also compared: the matvecs are bit-identical and exp /
+log1p reproduce the host C library's results bit for bit (the decoder's
+correction tables), so the only remaining freedom is the order of double sums
+inside RMSNorm / attention / gated delta, which changes a float result only
+when a double sum straddles a float rounding boundary; the bound kept here is
+1e-3 of the logits' standard deviation (measured: 0 on the q8k model).
 """
 from __future__ import annotations
 
