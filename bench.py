@@ -966,27 +966,31 @@ class DecoderWorkload:
     n_new = 256
     dtype = "f32 activations, Q8_K x Q4_K/Q6_K integer dots"
 
-    def __init__(self):
+    def __init__(self, batch: int = 1):
         from oracle_b200 import qwen35
         self.cfg = qwen35.CONFIG5
         self.specs = qwen35.tensor_specs(self.cfg)
+        self.batch = batch
+        if batch > 1:
+            self.metric = f"batch-{batch} decode tokens/s (Qwen3.5-style hybrid, Q4_K_M)"
 
     def config(self, n_gpus: int) -> dict:
         c = self.cfg
         return {"workload": "config5: synthetic Qwen3.5-style hybrid decoder, 32 blocks (24 Gated DeltaNet + 8 "
                             "gated GQA attention), hidden 4096, FFN 12288, vocab 151936, Q4_K_M, greedy",
-                "batch": 1, "prompt_tokens": self.prompt_len, "new_tokens": self.n_new, "kv_capacity": c.context,
+                "batch": self.batch, "prompt_tokens": self.prompt_len, "new_tokens": self.n_new,
+                "kv_capacity": c.context,
                 "contract": "q8k",
                 "parallelism": "single GPU" if n_gpus == 1 else
                 f"tp{n_gpus}: projection rows split over the GPUs, all-gather inside the matvec programs, "
                 f"block cores on every GPU",
                 "l2": "no flush needed: each step streams 4.7 GB of weights (> 37x the 126 MB L2)"}
 
-    def step_bytes(self, position: int) -> int:
+    def step_bytes(self, position: int, batch: int = 1) -> int:
         """Algorithmic HBM bytes of one decode step at a cache length: every
-        projection's packed weights, one embedding row, each recurrent
-        state read and written once, the conv histories, and the KV rows
-        read by attention."""
+        projection's packed weights (once, whatever the batch), one embedding
+        row per sequence, and per sequence each recurrent state read and
+        written once, the conv histories, and the KV rows read by attention."""
         from oracle_b200 import qwen35
         c = self.cfg
         total = 0
@@ -994,13 +998,13 @@ class DecoderWorkload:
             be, bb = qwen35.BLOCK[qtype]
             n = int(np.prod(dims)) // be * bb
             if name == "token_embd.weight":
-                n //= dims[1]
+                n = n // dims[1] * batch
             total += n
         recurrent = sum(not c.is_attention(i) for i in range(c.layers))
         attention = c.layers - recurrent
-        total += recurrent * (2 * c.value_heads * c.state_size * c.state_size * 4 + 2 * c.conv_channels * 4 * 4)
-        total += attention * (position + 1) * 2 * c.kv_width * 4
-        return total
+        per_seq = recurrent * (2 * c.value_heads * c.state_size * c.state_size * 4 + 2 * c.conv_channels * 4 * 4)
+        per_seq += attention * (position + 1) * 2 * c.kv_width * 4
+        return total + batch * per_seq
 
 
 def decoder_host_model(wl: DecoderWorkload):
@@ -1043,6 +1047,106 @@ def decoder_reference_arm(args, wl: DecoderWorkload) -> None:
             "config": wl.config(1), "cpu_baseline": cpu,
             "e2e": {"value": tps, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print_reference_line(line)
+
+
+def batch_prompts(wl: DecoderWorkload, prompt: np.ndarray) -> np.ndarray:
+    """Sequence 0 gets the batch-1 prompt; sequence b > 0 a prompt seeded 5150 + b."""
+    rows = [prompt] + [np.random.default_rng(5150 + b).integers(0, wl.cfg.vocab, wl.prompt_len).astype(np.uint32)
+                       for b in range(1, wl.batch)]
+    return np.stack(rows)
+
+
+def decoder_batch_arm(args, wl: DecoderWorkload) -> None:
+    """Batched decoding (oracle_b200/batch_decoder.py): B sequences in lockstep,
+    every projection's weights streamed once per step for all of them."""
+    import torch
+
+    import oracle_b200 as ob
+    from oracle_b200.batch_decoder import BatchDecoder
+
+    if args.gpus != 1:
+        raise SystemExit("batched decoding runs on one GPU (replicas for more)")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ctx = ob.Context(0)
+    tensors, prompt = decoder_host_model(wl)
+    prompts = batch_prompts(wl, prompt)
+    B = wl.batch
+    max_new = max(wl.n_new, args.warmup + args.steps + 1)
+    if wl.prompt_len + max_new > wl.cfg.context:
+        raise SystemExit("warm-up + timed steps exceed the KV cache capacity")
+    dec = BatchDecoder(ctx, wl.cfg, tensors, B, capacity=wl.cfg.context, max_new=max_new)
+
+    # gate: sequence 0's greedy tokens on a short prompt equal Oracle's decode loop's
+    cpu = None
+    if not args.no_cpu:
+        want, tps, n, s = decoder_cpu_leg(wl, tensors, prompt)
+        got = dec.generate(prompts[:, :2], 2)
+        if not np.array_equal(got[0], want):
+            raise SystemExit(f"GPU tokens {got[0].tolist()} differ from the CPU reference {want.tolist()}")
+        cpu = {"value": tps, "unit": "tokens/s", "cores": 1, "kind": "reference",
+               "sample": f"{n} decode steps (2-token prompt, 2 new tokens) of the full config-5 model, one sequence",
+               "note": "Oracle's execute_qwen35_reference_token + greedy Sampler compiled from its sources "
+                       "(single-threaded, one sequence per call: a batch costs B times this); tokens identical "
+                       "to the GPU's sequence 0"}
+
+    dec.start(prompts)
+    launches = dec.launches_per_step()
+    dec.start(prompts)
+    with torch.cuda.stream(dec.stream):
+        for _ in range(wl.prompt_len + args.warmup):
+            dec.graph.replay()
+    dec.stream.synchronize()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(0)
+    with sampler, torch.cuda.stream(dec.stream):
+        start.record(dec.stream)
+        for _ in range(args.steps):
+            dec.graph.replay()
+        end.record(dec.stream)
+        dec.stream.synchronize()
+    ms = start.elapsed_time(end)
+    ctx.device_status()
+    value = B * args.steps / (ms / 1e3)
+    ms_step = ms / args.steps
+    mid = wl.prompt_len + args.warmup + args.steps // 2
+    step_bytes = wl.step_bytes(mid, B)
+    peak, peak_kind = load_peaks()
+    dec.start(prompts)
+    with torch.cuda.stream(dec.stream):
+        for _ in range(wl.prompt_len):
+            dec.graph.replay()
+    proj_bytes, proj_ms, _ = dec.profile_projections()
+    proj_gbs = proj_bytes / (proj_ms * 1e-3) / 1e9
+
+    # e2e: B host prompts in, BatchDecoder.generate, B x n_new host tokens out
+    dec.generate(prompts, 8)
+    t0 = time.perf_counter()
+    toks = dec.generate(prompts, wl.n_new)
+    e2e_s = time.perf_counter() - t0
+    forwards = wl.prompt_len + wl.n_new - 1
+    line = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded Q4_K_M weights and prompts)",
+            "config": wl.config(1), "gpu_launches": launches * args.steps,
+            "e2e": {"value": B * wl.n_new / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 4 * B,
+                    "d2h_bytes_per_step": 4 * B,
+                    "how": f"BatchDecoder.generate: {B} host prompts of {wl.prompt_len} tokens in, {B} x {wl.n_new} "
+                           f"greedy tokens out ({forwards} graph replays); value = generated tokens / wall time",
+                    "first_tokens_seq0": toks[0, :8].tolist()},
+            "roofline": {"bound": "hbm", "achieved": proj_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": proj_gbs / peak, "peak_source": peak_kind, "traffic": None,
+                         "kernel": "matvec_batch_kernel (the step's batched projections, one uncaptured step timed "
+                                   "with CUDA events around each call)",
+                         "projection_ms_per_step": proj_ms, "projection_bytes_per_step": proj_bytes,
+                         "step_bytes": step_bytes, "step_achieved": step_bytes / (ms_step * 1e-3) / 1e9,
+                         "step_frac": step_bytes / (ms_step * 1e-3) / 1e9 / peak, "launches_per_step": launches},
+            "cpu_baseline": cpu, "clocks": sampler.summary()}
+    print(json.dumps(line), flush=True)
+    dec.close()
+    del dec
+    ctx.close()
 
 
 def decoder_arm(args, wl: DecoderWorkload) -> None:
@@ -1167,14 +1271,18 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["config4", "config5"], default="config2")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--batch", type=int, default=1, help="config5: sequences decoded together (1..16)")
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
                     help="N > 1: all-gather inside the matvec kernel (fused) or one NCCL all-gather per step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.workload == "config5":
-        wl5 = DecoderWorkload()
-        (decoder_reference_arm if args.impl == "reference" else decoder_arm)(args, wl5)
+        wl5 = DecoderWorkload(args.batch)
+        if args.impl == "reference":
+            decoder_reference_arm(args, wl5)
+        else:
+            (decoder_batch_arm if args.batch > 1 else decoder_arm)(args, wl5)
         return
     if args.workload == "config4":
         wl = GemmWorkload()

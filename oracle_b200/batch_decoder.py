@@ -90,6 +90,7 @@ class BatchDecoder:
         self.am_keys = torch.zeros(B, dtype=torch.int64, device=dev)
         self.stream = torch.cuda.Stream(device=dev)
         self.graph, self.graph_prompt = None, None
+        self.timer = None  # list of (start, end) CUDA events around the matvecs, when set
         ctx.set_flags(ctx.flags | FLAG_PDL)
 
     # ---------------------------------------------------------------- pieces
@@ -102,7 +103,13 @@ class BatchDecoder:
     def _mv(self, name, y, s) -> None:
         """y[b] = W x_b for every sequence, x the last quantized input."""
         qtype, dims, w = self.w[name]
+        if self.timer is not None:
+            ev = (self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
+            ev[0].record(self.stream)
         self.ctx.batch_matvec(qtype, dims[1], dims[0], w, self.image, self.B, y[:self.B * dims[1]], s)
+        if self.timer is not None:
+            ev[1].record(self.stream)
+            self.timer.append((ev, w.numel()))
 
     def _recurrent(self, i: int, s) -> None:
         cfg, p = self.cfg, f"blk.{i}."
@@ -235,6 +242,21 @@ class BatchDecoder:
         self.stream.synchronize()
         self.ctx.device_status()
         return self.logits.view(self.B, self.cfg.vocab).cpu().numpy().copy()
+
+    def profile_projections(self) -> tuple:
+        """One uncaptured step with CUDA events around every batched matvec:
+        (weight bytes they stream, their summed milliseconds, the step's
+        milliseconds).  The state is reset afterwards."""
+        torch = self.torch
+        self.timer = []
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(self.stream)
+        self._enqueue_step(self.graph_prompt or 1, self.stream.cuda_stream)
+        b.record(self.stream)
+        self.stream.synchronize()
+        timer, self.timer = self.timer, None
+        self.reset()
+        return (sum(n for _, n in timer), sum(e[0].elapsed_time(e[1]) for e, _ in timer), a.elapsed_time(b))
 
     def launches_per_step(self) -> int:
         """Kernels one step launches (counted by the context on an uncaptured step)."""

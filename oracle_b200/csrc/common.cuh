@@ -183,48 +183,185 @@ __device__ __forceinline__ int sbyte(uint32_t w, int i) {
 // Oracle evaluates exp and log1p on floats with the host C library (expf,
 // log1pf), which is not correctly rounded everywhere; under the Q8_K contract
 // a last-bit difference of an activation can change a quantized value, so
-// the decoder reproduces the library's results bit for bit: the value in
-// double precision rounded once to float (correctly rounded unless the exact
-// value is within 2^-48 of a float midpoint), corrected from tables that the
-// build generates by running the library (csrc/libm_tables.c) on every float
-// input of the domain: expf on [-104, 89], log1pf on expf([-20, 20]).
-// Layout of g_libm (uint32 words): magic, expf entries, log1pf entries, 0,
-// expf bucket offsets [2^20 + 1], log1pf bucket offsets [2^20 + 1], then
-// (key bits, value bits) pairs sorted by key, expf's then log1pf's; bucket =
-// key >> 12.  Zeroed (no corrections) until the host loads the tables.
-constexpr uint32_t kLibmBuckets = 1u << 20;
-constexpr uint64_t kLibmHeaderWords = 4;
-constexpr uint64_t kLibmMaxWords = 12'000'000;  // 48 MB: ~11 M words used
-__device__ uint32_t g_libm[kLibmMaxWords];
+// the decoder reproduces the library's results bit for bit.  The value is
+// computed in double precision and rounded once to float: correctly rounded
+// unless the double lies within 2^-49 (relative) of a float rounding midpoint
+// (CUDA's double exp / log1p are within 2^-52).  Then it is corrected from
+// tables the build generates by running the library on every float input of
+// the domain (csrc/libm_tables.c; expf on [-104, 89], log1pf on
+// expf([-20, 20])): the inputs where the library is the other float neighbour
+// (a hash table of 128-byte lines: one line read per call), and the few inputs
+// within 2^-48 of a midpoint with the library's value (searched only when the
+// double is that close).  Layout of g_libm (uint32 words): header [8]
+// (magic, expf lines, log1pf lines, expf hard, log1pf hard), expf key lines
+// [lines x 32], expf direction bits [lines], log1pf key lines [lines x 32]
+// (direction in bit 31), expf hard pairs, log1pf hard pairs.  All zero (no
+// corrections) until the host loads the tables.
+constexpr uint64_t kLibmHeaderWords = 8;
+constexpr uint64_t kLibmMaxWords = 10'000'000;  // 40 MB: ~8.9 M words used
+constexpr uint32_t kLibmEmpty = 0xFFFFFFFFu;
+__device__ __align__(16) uint32_t g_libm[kLibmMaxWords];
 
-__device__ __forceinline__ bool libm_correction(uint32_t table, uint32_t key, uint32_t& value) {
-    const uint32_t* off = g_libm + kLibmHeaderWords + uint64_t(table) * (kLibmBuckets + 1);
-    const uint32_t first = __ldg(off + (key >> 12)), last = __ldg(off + (key >> 12) + 1);
-    if (first == last) return false;
-    const uint64_t base = kLibmHeaderWords + 2ull * (kLibmBuckets + 1) + (table ? 2ull * __ldg(g_libm + 1) : 0ull);
-    const uint2* e = reinterpret_cast<const uint2*>(g_libm + base);
-    for (uint32_t i = first; i < last; ++i) {
-        const uint2 kv = __ldg(e + i);
-        if (kv.x == key) {
-            value = kv.y;
+// Is d within 2^-49 |d| of the midpoint between r (= d rounded) and a float
+// neighbour of r?  r >= 0.
+__device__ __forceinline__ bool libm_near_midpoint(double d, float r) {
+    const uint32_t b = __float_as_uint(r);
+    const double rd = r == INFINITY ? 3.4028234663852886e38 : static_cast<double>(r);
+    const uint32_t bl = r == INFINITY ? 0x7F7FFFFEu : (b > 0 ? b - 1 : 0u);
+    const uint32_t bh = r == INFINITY ? 0x7F800000u : b + 1;
+    const double lo = static_cast<double>(__uint_as_float(bl));
+    const double hi = bh >= 0x7F800000u ? 0x1p128 : static_cast<double>(__uint_as_float(bh));
+    const double dist = fmin(fabs(d - 0.5 * (rd + lo)), fabs(d - 0.5 * (rd + hi)));
+    return dist < fabs(d) * 0x1p-49;
+}
+
+// Table reads keep their lines in L2 (evict-last): the weight streams that
+// run beside them are marked evict-first, so the lines a decode step uses stay
+// resident from token to token.
+__device__ __forceinline__ uint4 libm_ld4(const uint4* p, uint64_t policy) {
+    uint4 v;
+    asm("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p), "l"(policy));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t libm_ld(const uint32_t* p, uint64_t policy) {
+    uint32_t v;
+    asm("ld.global.nc.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(policy));
+    return v;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Slot of `key` in a line hash table (lines a power of two), or -1.  With
+// dir_in_key the table's words carry a direction bit in bit 31.
+__device__ __forceinline__ int64_t libm_slot_any(const uint32_t* keys, uint32_t lines, uint32_t key, bool dir_in_key,
+                                                 uint32_t& word);
+template <bool kDirInKey>
+__device__ __forceinline__ int64_t libm_slot(const uint32_t* keys, uint32_t lines, uint32_t key, uint32_t& word) {
+    return libm_slot_any(keys, lines, key, kDirInKey, word);
+}
+__device__ __forceinline__ int64_t libm_slot_any(const uint32_t* keys, uint32_t lines, uint32_t key, bool dir_in_key,
+                                                 uint32_t& word) {
+    const uint32_t shift = 32u - (31u - __clz(lines));
+    const uint64_t policy = l2_policy_evict_last();
+    uint32_t l = shift >= 32u ? 0u : (key * 0x9E3779B1u) >> shift;
+    for (uint32_t probe = 0; probe < lines; ++probe) {
+        const uint4* p = reinterpret_cast<const uint4*>(keys + uint64_t(l) * 32u);
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = libm_ld4(p + k, policy);
+        bool empty = false;
+        int64_t found = -1;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t w4[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t w = w4[c];
+                if (w == kLibmEmpty) empty = true;
+                else if ((dir_in_key ? (w & 0x7FFFFFFFu) : w) == key) {
+                    found = int64_t(l) * 32 + 4 * k + c;
+                    word = w;
+                }
+            }
+        }
+        if (found >= 0 || empty) return found;
+        l = (l + 1) & (lines - 1);
+    }
+    return -1;
+}
+
+// The library's value among a sorted (key, value) list, if listed.
+__device__ __forceinline__ bool libm_hard(const uint32_t* pairs, uint32_t n, uint32_t key, uint32_t& value) {
+    uint32_t lo = 0, hi = n;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) / 2, k = __ldg(pairs + 2 * mid);
+        if (k == key) {
+            value = __ldg(pairs + 2 * mid + 1);
             return true;
         }
+        if (k < key) lo = mid + 1;
+        else hi = mid;
     }
     return false;
 }
 
 // expf as the host library computes it.
 __device__ __forceinline__ float ref_expf(float x) {
-    uint32_t v;
-    if (libm_correction(0, __float_as_uint(x), v)) return __uint_as_float(v);
-    return __double2float_rn(exp(static_cast<double>(x)));
+    const double d = exp(static_cast<double>(x));
+    const float r = __double2float_rn(d);
+    const uint32_t lines_e = g_libm[1];
+    if (lines_e == 0 || !(x >= -104.0f && x <= 89.0f)) return r;
+    const uint32_t key = __float_as_uint(x);
+    const uint32_t lines_l = g_libm[2], hard_e = g_libm[3];
+    const uint32_t* keys_e = g_libm + kLibmHeaderWords;
+    const uint32_t* dir_e = keys_e + uint64_t(lines_e) * 32u;
+    if (libm_near_midpoint(d, r)) {
+        const uint32_t* pairs = dir_e + lines_e + uint64_t(lines_l) * 32u;
+        uint32_t v;
+        if (libm_hard(pairs, hard_e, key, v)) return __uint_as_float(v);
+        return r;
+    }
+    uint32_t w;
+    const int64_t slot = libm_slot<false>(keys_e, lines_e, key, w);
+    if (slot < 0) return r;
+    const bool up = (libm_ld(dir_e + slot / 32, l2_policy_evict_last()) >> (slot % 32)) & 1u;
+    return __uint_as_float(__float_as_uint(r) + (up ? 1u : 0xFFFFFFFFu));
 }
 
 // log1pf as the host library computes it, for arguments expf(v), v in [-20, 20].
 __device__ __forceinline__ float ref_log1pf(float y) {
-    uint32_t v;
-    if (libm_correction(1, __float_as_uint(y), v)) return __uint_as_float(v);
-    return __double2float_rn(log1p(static_cast<double>(y)));
+    const double d = log1p(static_cast<double>(y));
+    const float r = __double2float_rn(d);
+    const uint32_t lines_e = g_libm[1], lines_l = g_libm[2];
+    if (lines_l == 0 || !(y > 0.0f)) return r;
+    const uint32_t key = __float_as_uint(y);
+    const uint32_t* keys_l = g_libm + kLibmHeaderWords + uint64_t(lines_e) * 33u;
+    if (libm_near_midpoint(d, r)) {
+        const uint32_t* pairs = keys_l + uint64_t(lines_l) * 32u + 2ull * g_libm[3];
+        uint32_t v;
+        if (libm_hard(pairs, g_libm[4], key, v)) return __uint_as_float(v);
+        return r;
+    }
+    uint32_t w;
+    if (libm_slot<true>(keys_l, lines_l, key, w) < 0) return r;
+    return __uint_as_float(__float_as_uint(r) + ((w >> 31) ? 1u : 0xFFFFFFFFu));
+}
+
+// expf(x) (log = false) or log1pf(x) (log = true), the function chosen per
+// lane through one instruction stream: lanes of a warp that need different
+// functions make their table reads together instead of one after the other.
+__device__ __forceinline__ float libm_eval(bool log, float x) {
+    const double dx = static_cast<double>(x);
+    const double de = exp(dx), dl = log1p(dx);
+    const double d = log ? dl : de;
+    const float r = __double2float_rn(d);
+    const uint32_t lines_e = g_libm[1], lines_l = g_libm[2];
+    const uint32_t lines = log ? lines_l : lines_e;
+    const bool in_domain = log ? x > 0.0f : (x >= -104.0f && x <= 89.0f);
+    if (lines == 0 || !in_domain) return r;
+    const uint32_t key = __float_as_uint(x);
+    const uint32_t* keys_e = g_libm + kLibmHeaderWords;
+    const uint32_t* dir_e = keys_e + uint64_t(lines_e) * 32u;
+    const uint32_t* keys_l = dir_e + lines_e;
+    if (libm_near_midpoint(d, r)) {
+        const uint32_t* hard_e = keys_l + uint64_t(lines_l) * 32u;
+        const uint32_t* pairs = log ? hard_e + 2ull * g_libm[3] : hard_e;
+        uint32_t v;
+        if (libm_hard(pairs, log ? g_libm[4] : g_libm[3], key, v)) return __uint_as_float(v);
+        return r;
+    }
+    uint32_t w = 0;
+    const int64_t slot = libm_slot_any(log ? keys_l : keys_e, lines, key, log, w);
+    if (slot < 0) return r;
+    const bool up = log ? (w >> 31) != 0 : ((libm_ld(dir_e + slot / 32, l2_policy_evict_last()) >> (slot % 32)) & 1u);
+    return __uint_as_float(__float_as_uint(r) + (up ? 1u : 0xFFFFFFFFu));
 }
 
 // sigmoid and silu of Oracle's block code (qwen35_block.cpp:138-159): float

@@ -39,6 +39,34 @@ __device__ __forceinline__ float ref_softplus(float v) {
     return ref_log1pf(ref_expf(v));
 }
 
+// One recurrent head's gates (qwen35_block.cpp:472-489), computed by a whole
+// warp so that the library functions' table reads overlap: beta =
+// sigmoid(beta_in), decay = exp(softplus(alpha + dt_bias) * a).  The first
+// round evaluates, side by side, expf(-|beta_in|) (lane 0), expf(v) (lane 1)
+// and log1pf at the three floats expf(v) can be -- its correctly rounded
+// value and the two neighbours, since the library is within one float of it
+// (lanes 2-4); the lane that guessed expf(v) supplies softplus.  The second
+// round is the decay's expf.  Same values as ref_sigmoid / ref_softplus.
+__device__ __forceinline__ void gdn_gates_warp(float beta_in, float alpha, float dt_bias, float a, uint32_t lane,
+                                               float* gate_s) {
+    const float v = __fadd_rn(alpha, dt_bias);
+    const float ycr = __double2float_rn(exp(static_cast<double>(v)));
+    const uint32_t nb = lane == 2 ? 0u : lane == 3 ? 1u : 0xFFFFFFFFu;
+    const bool log = lane >= 2 && lane <= 4;
+    const float arg = lane == 0 ? -fabsf(beta_in) : lane == 1 ? v : log ? __uint_as_float(__float_as_uint(ycr) + nb) : 0.0f;
+    const float r = libm_eval(log, arg);
+    const float e_beta = __shfl_sync(0xFFFFFFFFu, r, 0);
+    const float y = __shfl_sync(0xFFFFFFFFu, r, 1);
+    const uint32_t dy = __float_as_uint(y) - __float_as_uint(ycr);
+    const float l1p = __shfl_sync(0xFFFFFFFFu, r, dy == 0u ? 2 : dy == 1u ? 3 : 4);
+    const float s = v > 20.0f ? v : v < -20.0f ? y : l1p;
+    const float decay = ref_expf(__fmul_rn(s, a));
+    if (lane == 0) {
+        gate_s[0] = beta_in >= 0.0f ? __fdiv_rn(1.0f, __fadd_rn(1.0f, e_beta)) : __fdiv_rn(e_beta, __fadd_rn(1.0f, e_beta));
+        gate_s[1] = decay;
+    }
+}
+
 __global__ void __launch_bounds__(256) rope_pos_kernel(float* __restrict__ heads, uint32_t n_heads, uint32_t head_dim,
                                                        uint32_t half, const float* __restrict__ table,
                                                        const uint32_t* __restrict__ pos, uint32_t positions,
@@ -224,6 +252,10 @@ __global__ void __launch_bounds__(1024) attention_values_pos_kernel(const float*
     };
     const uint32_t chunks = (tokens + kAttnChunk - 1) / kAttnChunk;
     stage(0, 0);
+    // the output gate's sigmoid (qwen35_block.cpp:738-742) needs only the
+    // projection: evaluated while the first chunk loads
+    const uint32_t d = d0 + dl;
+    const float sg = gate ? ref_sigmoid(gate[static_cast<uint64_t>(h) * gate_stride + d]) : 1.0f;
     float acc = 0.0f;
     for (uint32_t c = 0; c < chunks; ++c) {
         if (c + 1 < chunks) {
@@ -241,9 +273,8 @@ __global__ void __launch_bounds__(1024) attention_values_pos_kernel(const float*
         for (uint32_t t = 0; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(pr[t], vs[t * kAttnDims + dl]));
         __syncthreads();  // the buffer is refilled by the stage after next
     }
-    const uint32_t d = d0 + dl;
-    // the output gate, attention *= sigmoid(gate) (qwen35_block.cpp:738-742)
-    if (gate) acc = __fmul_rn(acc, ref_sigmoid(gate[static_cast<uint64_t>(h) * gate_stride + d]));
+    // the output gate, attention *= sigmoid(gate)
+    if (gate) acc = __fmul_rn(acc, sg);
     out[static_cast<uint64_t>(h) * value_dim + d] = acc;
 }
 
@@ -337,6 +368,7 @@ __global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restric
     __shared__ float q_s[kD], k_s[kD], v_s[kD], nq[kD], nk[kD], o_s[kD];
     __shared__ double scratch[64];
     __shared__ float gate_s[2];
+    __shared__ float zs_s[kD];  // silu(z) of the head
     const uint32_t h = blockIdx.x, tid = threadIdx.x;
     const uint32_t t = tid >> 2, part = tid & 3u;  // state column, quarter of the key rows
     // the state rows of this thread, loaded up front: only this block's own
@@ -395,9 +427,15 @@ __global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restric
         }
         const float r = ref_silu(__double2float_rn(sum));
         (which == 0 ? q_s : which == 1 ? k_s : v_s)[ci] = r;
-    } else if (tid == 3 * kD) {
-        gate_s[0] = ref_sigmoid(beta_in[h]);
-        gate_s[1] = ref_expf(__fmul_rn(ref_softplus(__fadd_rn(alpha[h], dt_bias[h])), decay_a[h]));
+    } else {
+        // the threads the conv leaves idle: one warp computes the gates, the
+        // others silu(z) of the head, which only the last phase needs
+        const uint32_t u = tid - 3 * kD;
+        if (u < 32) {
+            gdn_gates_warp(beta_in[h], alpha[h], dt_bias[h], decay_a[h], u, gate_s);
+        } else {
+            for (uint32_t i = u - 32; i < kD; i += kD - 32) zs_s[i] = ref_silu(z[static_cast<uint64_t>(h) * kD + i]);
+        }
     }
     __syncthreads();
     // gated_delta_step: l2-normalised q (scaled by 1/sqrt(key_dim)) and k
@@ -456,7 +494,7 @@ __global__ void __launch_bounds__(4 * kD) gdn_core_kernel(const float* __restric
                                   kD, eps);
     if (tid < kD) {
         const float g = __fmul_rn(__fmul_rn(of, inv), norm_w[tid]);
-        out[static_cast<uint64_t>(h) * kD + tid] = __fmul_rn(g, ref_silu(z[static_cast<uint64_t>(h) * kD + tid]));
+        out[static_cast<uint64_t>(h) * kD + tid] = __fmul_rn(g, zs_s[tid]);
     }
 }
 

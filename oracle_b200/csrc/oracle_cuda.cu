@@ -605,10 +605,12 @@ oracle_cuda_status libm_tables_load(int device) {
     std::lock_guard<std::mutex> lock(g_libm_mutex);
     if (g_libm_loaded[device]) return ORACLE_CUDA_OK;
     const uint64_t bytes = static_cast<uint64_t>(oracle_libm_blob_end - oracle_libm_blob);
-    uint32_t hdr[4] = {};
+    uint32_t hdr[kLibmHeaderWords] = {};
     if (bytes >= sizeof hdr) std::memcpy(hdr, oracle_libm_blob, sizeof hdr);
-    const uint64_t words = kLibmHeaderWords + 2ull * (kLibmBuckets + 1) + 2ull * (uint64_t(hdr[1]) + hdr[2]);
-    if (bytes < sizeof hdr || hdr[0] != 0x314D424Cu || bytes != words * 4 || words > kLibmMaxWords)
+    const auto pow2 = [](uint32_t v) { return v != 0 && (v & (v - 1)) == 0; };
+    const uint64_t words = kLibmHeaderWords + 33ull * hdr[1] + 32ull * hdr[2] + 2ull * (uint64_t(hdr[3]) + hdr[4]);
+    if (bytes < sizeof hdr || hdr[0] != 0x324D424Cu || !pow2(hdr[1]) || !pow2(hdr[2]) || bytes != words * 4 ||
+        words > kLibmMaxWords)
         return fail(nullptr, ORACLE_CUDA_CUDA_ERROR, "the library's expf/log1pf tables are missing or malformed");
     const cudaError_t e = cudaMemcpyToSymbol(g_libm, oracle_libm_blob, bytes);
     if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaMemcpyToSymbol(expf/log1pf tables)");
