@@ -516,6 +516,69 @@ oracle_cuda_status oracle_cuda_matvec_program_allgather(oracle_cuda_context* ctx
                                                         const oracle_cuda_matvec_op* ops, uint32_t n_ops,
                                                         void* stream);
 
+/* ------------------------------------------------------------------ head-sharded programs
+ * The decode step with heads sharded over the ranks (one process per GPU): a
+ * rank computes its own heads' input projections (rows of its heads only)
+ * and, for a projection whose input is sharded (the block output projection
+ * over the rank's heads, the MLP down projection over the rank's FFN
+ * columns), PARTIAL sums of every row over its own super-blocks.  Rank q of
+ * `world` (1, 2, 4 or 8) owns super-blocks j with j % world == q of every
+ * 16-super-block segment; its partial of a row is the canonical fold of
+ * those leaves (a row of that rank's columns only, one matvec per segment),
+ * and the next op's transform ORACLE_CUDA_XFORM_COMBINE_RMS folds every
+ * rank's partials by the remaining strides, adds the segments in order and
+ * the residual, so every rank obtains the unsharded program's vector bit for
+ * bit.  Per op, on top of oracle_cuda_matvec_op_ex:
+ *   push      1: y_dev lies in the gather buffer and every row is also stored
+ *             into every peer's buffer at the same offset (NVLink stores);
+ *   wait      0: x is produced before the call; 1: x is produced by the op
+ *             before (this rank's CTAs are waited for); 2: as 1, and the op
+ *             before must `announce`: its outputs from EVERY rank are waited
+ *             for; 3: x is produced by an earlier op that a previous op of
+ *             this call already waited for (no wait; the image is built when
+ *             the op starts);
+ *   announce  1: once this rank finished the op (and all before it), every
+ *             peer is told (one cross-rank dependency; numbered within the
+ *             step from `first_dep`);
+ *   segments  XFORM_COMBINE_RMS: x_dev = the residual vector (cols floats),
+ *             x2_dev = the partial sums [world][segments][cols] inside the
+ *             gather buffer, norm_dev / eps as for XFORM_RMS; with wait 2, or
+ *             wait 3 when an earlier op of the call has the same source;
+ *   swiglu_gate  optional: after the op, act_dev[r] = silu(swiglu_gate[r]) *
+ *             y[r] for the op's rows (the MLP activation from the gate
+ *             rows of an earlier op and this op's up rows);
+ *   combined_dev  XFORM_COMBINE_RMS, optional: receives the combined vector
+ *             (cols floats, before the norm).
+ * `step`: first_dep = the index within the decode step of this call's first
+ * announcement, deps_per_step = announcements per step (the same on every
+ * rank), end_of_step = 1 on the step's last call, tail_wait = 1: the call's
+ * grid ends only once every peer announced this call's last announcement
+ * (outputs the next kernel reads from every rank).  Every rank issues the
+ * same calls in the same order; peers waited for longer than one second make
+ * the kernel record a device timeout (oracle_cuda_device_status).  No
+ * counterpart in the reference (Oracle runs on one CPU thread); the north
+ * star's head-sharded decoder with per-layer collectives is what this
+ * replaces, with two cross-rank dependencies per block. */
+#define ORACLE_CUDA_XFORM_COMBINE_RMS 3u
+typedef struct oracle_cuda_sharded_op {
+    oracle_cuda_matvec_op_ex ex;
+    uint32_t push;
+    uint32_t wait;
+    uint32_t announce;
+    uint32_t segments;
+    const float* swiglu_gate;
+    float* combined_dev;
+} oracle_cuda_sharded_op;
+typedef struct oracle_cuda_sharded_step {
+    uint32_t first_dep;
+    uint32_t deps_per_step;
+    uint32_t end_of_step;
+    uint32_t tail_wait;
+} oracle_cuda_sharded_step;
+oracle_cuda_status oracle_cuda_matvec_program_sharded(oracle_cuda_context* ctx, oracle_cuda_peer_group* group,
+                                                      const oracle_cuda_sharded_op* ops, uint32_t n_ops,
+                                                      const oracle_cuda_sharded_step* step, void* stream);
+
 /* ------------------------------------------------------------------ prefill dequant-GEMM
  * Y[m][n] = sum_k X[m][k] * W[n][k] for m < m_tokens: the batched form of the
  * matvec for prompt ingestion (M >= 64 tokens).  W: `rows` GGML rows of `cols`

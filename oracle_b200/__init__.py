@@ -128,11 +128,24 @@ class MatvecOpEx(C.Structure):
                 ("norm_dev", C.c_void_p), ("residual_dev", C.c_void_p), ("act_dev", C.c_void_p)]
 
 
-XFORM_NONE, XFORM_RMS, XFORM_SWIGLU = 0, 1, 2
+XFORM_NONE, XFORM_RMS, XFORM_SWIGLU, XFORM_COMBINE_RMS = 0, 1, 2, 3
 PROGRAM_MAX_OPS = 16
+
+
+class ShardedOp(C.Structure):
+    """oracle_cuda_sharded_op of include/oracle_cuda.h."""
+    _fields_ = [("ex", MatvecOpEx), ("push", C.c_uint32), ("wait", C.c_uint32), ("announce", C.c_uint32),
+                ("segments", C.c_uint32), ("swiglu_gate", C.c_void_p), ("combined_dev", C.c_void_p)]
+
+
+class ShardedStep(C.Structure):
+    """oracle_cuda_sharded_step of include/oracle_cuda.h."""
+    _fields_ = [("first_dep", C.c_uint32), ("deps_per_step", C.c_uint32), ("end_of_step", C.c_uint32),
+                ("tail_wait", C.c_uint32)]
 _proto("oracle_cuda_matvec_program", [_vp, C.POINTER(MatvecOp), _u32, _vp])
 _proto("oracle_cuda_matvec_program_ex", [_vp, C.POINTER(MatvecOpEx), _u32, _vp])
 _proto("oracle_cuda_matvec_program_ex_allgather", [_vp, _vp, C.POINTER(MatvecOpEx), _u32, _vp])
+_proto("oracle_cuda_matvec_program_sharded", [_vp, _vp, C.POINTER(ShardedOp), _u32, C.POINTER(ShardedStep), _vp])
 _proto("oracle_cuda_matvec_program_noalloc", [C.POINTER(MatvecOp), _u32, _vp])
 _proto("oracle_cuda_noalloc_status", [_i32])
 _proto("oracle_cuda_noalloc_selftest_bounded_wait", [_u64, _vp])
@@ -519,6 +532,26 @@ class Context:
         rows this rank's shard, outputs inside the group's gather buffer."""
         self._check(_lib.oracle_cuda_matvec_program_ex_allgather(self._h, group._h, self._ops_ex(ops), len(ops),
                                                                  _stream(stream)))
+
+    def matvec_program_sharded(self, group: "PeerGroup", ops, first_dep: int, deps_per_step: int,
+                               end_of_step: bool = False, tail_wait: bool = False, stream=None) -> None:
+        """oracle_cuda_matvec_program_sharded: ops as for matvec_program_ex plus
+        push (bool), wait (0-3), announce (bool), segments and combined
+        (combine ops) and swiglu_gate (epilogue, into act); xform
+        XFORM_COMBINE_RMS takes the residual as x and the partial sums as x2."""
+        ex = self._ops_ex(ops)
+        arr = (ShardedOp * len(ops))()
+        for i, o in enumerate(ops):
+            arr[i].ex = ex[i]
+            arr[i].push = 1 if o.get("push") else 0
+            arr[i].wait = int(o.get("wait", 0))
+            arr[i].announce = 1 if o.get("announce") else 0
+            arr[i].segments = int(o.get("segments", 0))
+            arr[i].swiglu_gate = _addr(o.get("swiglu_gate"))
+            arr[i].combined_dev = _addr(o.get("combined"))
+        st = ShardedStep(first_dep, deps_per_step, 1 if end_of_step else 0, 1 if tail_wait else 0)
+        self._check(_lib.oracle_cuda_matvec_program_sharded(self._h, group._h, arr, len(ops), C.byref(st),
+                                                            _stream(stream)))
 
     def matvec_program_ex(self, ops, stream=None) -> None:
         """ops: sequence of dicts with keys qtype, rows, cols, w, x, y and

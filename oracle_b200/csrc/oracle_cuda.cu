@@ -903,9 +903,14 @@ namespace {
 
 constexpr uint64_t kGatherHeader = 256;  // arrival counter, epoch, ..., op counters
 constexpr uint32_t kGatherOpCounters = 16;  // uint index of the [2][kProgramMaxOps] op counters
+constexpr uint32_t kGatherXdep = 2;         // uint index of the sharded programs' announcement counter
+constexpr uint32_t kGatherStep = 3;         // uint index of the sharded programs' step counter
 
+// sh / step: head-sharded programs (oracle_cuda_matvec_program_sharded), else null.
 oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matvec_op_ex* ops, uint32_t n_ops,
-                               void* stream, const oracle_cuda_peer_group* group);
+                               void* stream, const oracle_cuda_peer_group* group,
+                               const oracle_cuda_sharded_op* sh = nullptr,
+                               const oracle_cuda_sharded_step* step = nullptr);
 
 oracle_cuda_status program_run_base(oracle_cuda_context* ctx, const oracle_cuda_matvec_op* ops, uint32_t n_ops,
                                     void* stream, const oracle_cuda_peer_group* group) {
@@ -1006,7 +1011,8 @@ bool same_source(const oracle_cuda_matvec_op_ex& a, const oracle_cuda_matvec_op_
 }
 
 oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matvec_op_ex* ops, uint32_t n_ops,
-                               void* stream, const oracle_cuda_peer_group* group) {
+                               void* stream, const oracle_cuda_peer_group* group, const oracle_cuda_sharded_op* sh,
+                               const oracle_cuda_sharded_step* step) {
     if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
     if (!ops || n_ops == 0 || n_ops > kProgramMaxOps)
         return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
@@ -1016,8 +1022,27 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
     uint64_t max_rows = 0;
     for (uint32_t k = 0; k < n_ops; ++k) {
         const oracle_cuda_matvec_op_ex& e = ops[k];
-        if (e.xform > ORACLE_CUDA_XFORM_SWIGLU)
-            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "op " + std::to_string(k) + ": unknown activation transform");
+        const std::string at = "op " + std::to_string(k) + ": ";
+        if (e.xform > ORACLE_CUDA_XFORM_SWIGLU && !(sh && e.xform == ORACLE_CUDA_XFORM_COMBINE_RMS))
+            return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, at + "unknown activation transform");
+        if (sh) {
+            if (sh[k].wait > 3) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, at + "wait must be 0, 1, 2 or 3");
+            if (sh[k].wait != 0 && k == 0)
+                return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, at + "the first op cannot wait for an earlier op");
+            if (sh[k].wait == 2 && !sh[k - 1].announce)
+                return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, at + "waiting for every rank needs the op before to announce");
+            if (e.xform == ORACLE_CUDA_XFORM_COMBINE_RMS) {
+                if (sh[k].wait < 2 || !e.x2_dev || sh[k].segments == 0 || !e.norm_dev || !(e.eps > 0.0f) ||
+                    !std::isfinite(e.eps))
+                    return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                                at + "the combine transform needs wait 2 or 3, partial sums, segments, norm weights "
+                                     "and a positive finite epsilon");
+                if (reinterpret_cast<uintptr_t>(e.x2_dev) % 4 || reinterpret_cast<uintptr_t>(e.base.x_dev) % 4)
+                    return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, at + "combine vectors must be 4-byte aligned");
+            }
+            if (sh[k].swiglu_gate && !e.act_dev)
+                return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, at + "a SwiGLU epilogue needs act_dev");
+        }
         if (e.xform == ORACLE_CUDA_XFORM_RMS && (!e.norm_dev || !(e.eps > 0.0f) || !std::isfinite(e.eps)))
             return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
                         "op " + std::to_string(k) + ": RMS transform needs weights and a positive finite epsilon");
@@ -1042,19 +1067,33 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         p.row_bytes = rb;
         p.type = o.type;
         p.nb = static_cast<uint32_t>(o.cols / 256);
-        p.after_previous = (o.after_previous && k > 0) ? 1u : 0u;
+        p.after_previous = sh ? ((sh[k].wait == 1 || sh[k].wait == 2) ? 1u : 0u)
+                              : ((o.after_previous && k > 0) ? 1u : 0u);
+        p.push = sh ? (sh[k].push ? 1u : 0u) : (group ? 1u : 0u);
         pp.ext[k].xform = e.xform;
         pp.ext[k].eps = e.eps;
         pp.ext[k].x2 = e.x2_dev;
         pp.ext[k].norm = e.norm_dev;
         p.residual = e.residual_dev;
+        if (sh && e.xform == ORACLE_CUDA_XFORM_COMBINE_RMS) {
+            pp.ext[k].partials = e.x2_dev;
+            pp.ext[k].x2 = nullptr;
+            pp.ext[k].segments = sh[k].segments;
+            pp.ext[k].combined = sh[k].combined_dev;
+        }
+        if (sh && sh[k].swiglu_gate) {
+            pp.ext[k].act = e.act_dev;
+            pp.ext[k].other = sh[k].swiglu_gate;
+            pp.ext[k].other_is_gate = 1u;
+        }
         if (o.rows > max_rows) max_rows = o.rows;
     }
     // A SwiGLU op whose gate and up are outputs of two earlier ops of this
     // launch over the same rows: the later of the two forms silu(gate) * up
     // row by row in its epilogue (once per element, by the CTA that owns the
     // row in both ops), and the SwiGLU op reads that vector plainly.
-    {
+    // (Sharded programs name their SwiGLU epilogues explicitly: swiglu_gate.)
+    if (!sh) {
         uint64_t need = 0;
         for (uint32_t j = 0; j < n_ops; ++j)
             if (ops[j].xform == ORACLE_CUDA_XFORM_SWIGLU && !ops[j].act_dev) need += ops[j].base.cols * sizeof(float);
@@ -1105,24 +1144,42 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
     // op whose source equals an earlier op's shares that op's image: it needs
     // neither a build nor a wait of its own.
     ImageJobs jobs{};
-    uint32_t prebuilt = 0, blocks = 0, act_total = 0;
+    uint32_t prebuilt = 0, blocks = 0, act_total = 0, combine_off = 0;
     {
+        // produced[k]: x comes from earlier ops of this launch (waited for by
+        // this op, or, sharded wait 3, by an earlier one): built in the kernel
+        bool produced[kProgramMaxOps];
+        for (uint32_t k = 0; k < n_ops; ++k)
+            produced[k] = pp.ops[k].after_previous != 0 || (sh && sh[k].wait == 3);
+        auto same = [&](uint32_t j, uint32_t k) {
+            if (!same_source(ops[j], ops[k])) return false;
+            if (!sh) return true;
+            if (produced[j] != produced[k]) return false;
+            return ops[j].xform != ORACLE_CUDA_XFORM_COMBINE_RMS ||
+                   (ops[j].x2_dev == ops[k].x2_dev && sh[j].segments == sh[k].segments &&
+                    sh[j].combined_dev == sh[k].combined_dev && ops[j].norm_dev == ops[k].norm_dev &&
+                    ops[j].eps == ops[k].eps);
+        };
         int owner[kProgramMaxOps];
         for (uint32_t k = 0; k < n_ops; ++k) {
             owner[k] = -1;
             for (uint32_t j = 0; j < k && owner[k] < 0; ++j)
-                if (owner[j] < 0 && same_source(ops[j], ops[k])) owner[k] = static_cast<int>(j);
+                if (owner[j] < 0 && same(j, k)) owner[k] = static_cast<int>(j);
             if (owner[k] >= 0) pp.ops[k].after_previous = 0u;
+            // a combine reads every rank's partials: the op that builds it waits for them
+            if (sh && owner[k] < 0 && ops[k].xform == ORACLE_CUDA_XFORM_COMBINE_RMS && sh[k].wait != 2)
+                return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                            "op " + std::to_string(k) + ": a combine transform not shared with an earlier op needs wait 2");
         }
         // in-kernel builds of fed-in images only while they all fit in shared
         // memory beside the ring; otherwise prebuilt images (slots when large)
         uint64_t fed = 0;
         for (uint32_t k = 0; k < n_ops; ++k)
-            if (owner[k] < 0 && !pp.ops[k].after_previous) fed += q8k_image_bytes(pp.ops[k].nb);
+            if (owner[k] < 0 && !produced[k]) fed += q8k_image_bytes(pp.ops[k].nb);
         const bool in_kernel = (ctx->flags & ORACLE_CUDA_FLAG_BUILD_IN_KERNEL) != 0 && fed <= ctx->jit_image_threshold;
         uint32_t off = 0;
         for (uint32_t k = 0; k < n_ops; ++k)
-            if (owner[k] < 0 && !pp.ops[k].after_previous && !in_kernel) {
+            if (owner[k] < 0 && !produced[k] && !in_kernel) {
                 pp.ops[k].act_offset = off;
                 pp.ops[k].prebuilt = 1u;
                 const uint32_t jn = jobs.n_jobs;
@@ -1141,7 +1198,7 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         prebuilt = off;
         jobs.first_block[jobs.n_jobs] = blocks;
         for (uint32_t k = 0; k < n_ops; ++k)
-            if (owner[k] < 0 && (pp.ops[k].after_previous || in_kernel)) {
+            if (owner[k] < 0 && (produced[k] || in_kernel)) {
                 pp.ops[k].act_offset = off;
                 pp.ext[k].build = 1u;
                 off += q8k_image_bytes(pp.ops[k].nb);
@@ -1150,7 +1207,14 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
             if (owner[k] >= 0) pp.ops[k].act_offset = pp.ops[owner[k]].act_offset;
         for (uint32_t k = 1; k < n_ops; ++k)
             if (pp.ops[k].after_previous) pp.ops[k - 1].publish = 1u;
-        act_total = off + 256;  // + reduction scratch
+        // the combined vectors of combine transforms (one at a time) after the images
+        uint32_t combine_bytes = 0;
+        for (uint32_t k = 0; k < n_ops; ++k)
+            if (pp.ext[k].xform == kXformCombineRms && pp.ext[k].build)
+                combine_bytes = std::max(combine_bytes, pp.ops[k].nb * 256u * 4u);
+        combine_off = off;
+        for (uint32_t k = 0; k < n_ops; ++k) pp.ext[k].combine_offset = combine_off;
+        act_total = off + combine_bytes + 256;  // + reduction scratch
         // Images that would crowd the stage ring out of shared memory stay in
         // global memory; each op copies its own into one of two slots.
         if (prebuilt > ctx->jit_image_threshold) {
@@ -1173,6 +1237,7 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
             }
             pp.jit_slot_bytes = slot;
             act_total = act_total - prebuilt + 2 * slot;
+            for (uint32_t k = 0; k < n_ops; ++k) pp.ext[k].combine_offset = combine_off - prebuilt + 2 * slot;
         }
     }
     pp.act_bytes = act_total;
@@ -1194,9 +1259,41 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         const float* hi = lo + group->data_bytes / sizeof(float);
         for (uint32_t k = 0; k < n_ops; ++k) {
             const float* y0 = ops[k].base.y_dev;
-            if (y0 < lo || y0 + ops[k].base.rows > hi)
+            if (pp.ops[k].push && (y0 < lo || y0 + ops[k].base.rows > hi))
                 return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
                             "op " + std::to_string(k) + ": output must lie inside the peer group's gather buffer");
+        }
+        if (sh) {
+            const uint32_t w = group->world;
+            if (w & (w - 1)) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "sharded programs need 1, 2, 4 or 8 ranks");
+            if (!step) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "sharded program without step information");
+            uint32_t j = step->first_dep, last = 0;
+            for (uint32_t k = 0; k < n_ops; ++k) {
+                if (pp.ext[k].partials) {
+                    const float* p0 = pp.ext[k].partials;
+                    if (p0 < lo || p0 + uint64_t(w) * pp.ext[k].segments * ops[k].base.cols > hi)
+                        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                                    "op " + std::to_string(k) + ": partial sums must lie inside the gather buffer");
+                }
+                if (sh[k].announce) {
+                    pp.ext[k].announce = 1u + j++;
+                    pp.ops[k].publish = 1u;
+                    last = pp.ext[k].announce;
+                }
+                if (sh[k].wait == 2) pp.ext[k].xwait = pp.ext[k - 1].announce;
+            }
+            if (j > step->deps_per_step)
+                return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "more announcements than deps_per_step");
+            if (step->tail_wait && last == 0)
+                return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "tail_wait needs an announcing op");
+            pp.px.sharded = 1u;
+            pp.px.deps_per_step = step->deps_per_step;
+            pp.px.end_of_step = step->end_of_step ? 1u : 0u;
+            pp.px.tail_wait = step->tail_wait ? last : 0u;
+            pp.px.my_xdep = reinterpret_cast<unsigned int*>(group->local) + kGatherXdep;
+            pp.px.my_step = reinterpret_cast<unsigned int*>(group->local) + kGatherStep;
+            for (uint32_t r = 0; r < w; ++r)
+                pp.px.peer_xdep[r] = reinterpret_cast<unsigned int*>(group->mapped[r]) + kGatherXdep;
         }
         pp.px.world = group->world;
         pp.px.rank = group->rank;
@@ -1213,7 +1310,7 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
         // SwiGLU vectors and residual outputs reach the peers from the end-of-op
         // passes: they must sit in the gather buffer too
         for (uint32_t k = 0; k < n_ops; ++k)
-            if (pp.ext[k].act && (pp.ext[k].act < lo || pp.ext[k].act + pp.ops[k].rows > hi))
+            if (pp.ext[k].act && pp.ops[k].push && (pp.ext[k].act < lo || pp.ext[k].act + pp.ops[k].rows > hi))
                 return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
                             "op " + std::to_string(k) + ": the SwiGLU vector must lie inside the peer group's gather buffer");
     }
@@ -2792,4 +2889,19 @@ extern "C" oracle_cuda_status oracle_cuda_matvec_program_ex_allgather(oracle_cud
                                                                       uint32_t n_ops, void* stream) {
     if (!group) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "peer group is null");
     return program_run(ctx, ops, n_ops, stream, group);
+}
+
+extern "C" oracle_cuda_status oracle_cuda_matvec_program_sharded(oracle_cuda_context* ctx,
+                                                                 oracle_cuda_peer_group* group,
+                                                                 const oracle_cuda_sharded_op* ops, uint32_t n_ops,
+                                                                 const oracle_cuda_sharded_step* step, void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (!group) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "peer group is null");
+    if (!ops || n_ops == 0 || n_ops > kProgramMaxOps)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                    "a matvec program holds 1 to " + std::to_string(kProgramMaxOps) + " ops");
+    if (!step) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "step information is null");
+    oracle_cuda_matvec_op_ex ex[kProgramMaxOps] = {};
+    for (uint32_t k = 0; k < n_ops; ++k) ex[k] = ops[k].ex;
+    return program_run(ctx, ex, n_ops, stream, group, ops, step);
 }

@@ -43,6 +43,9 @@ struct ProgramOp {
     // the stages of a group of rows_per_stage rows hold 16-super-block segment
     // 0 of every row of the group, then segment 1, ...
     uint32_t segmented;
+    // peer groups: 1 = every output row (and the residual / SwiGLU epilogue
+    // values) is also stored into every peer's gather buffer
+    uint32_t push;
 };
 
 // Segment-major streaming: segment g of a row is super-blocks 16g .. 16g + 15,
@@ -64,6 +67,20 @@ struct ProgramOpExtra {
     // : silu(y[r]) * other[r], `other` an earlier op's output over the same rows
     const float* other;
     float* act;
+    // kXformCombineRms: the activation is rms(x + fold(partials)), partials
+    // [world][segments][cols] in the gather buffer (every rank's partial sums
+    // of the same rows); the folded vector is staged in shared memory at
+    // combine_offset of the activation region and, by CTA 0, written to
+    // `combined` (optional)
+    const float* partials;
+    float* combined;
+    uint32_t segments;
+    uint32_t combine_offset;
+    // sharded peer groups: 1 + the step-wide index of the announcement made
+    // once this rank finished this op (0: none), and 1 + the index of the
+    // announcement an after_previous op waits for besides its own CTAs (0: none)
+    uint32_t announce;
+    uint32_t xwait;
 };
 
 constexpr uint32_t kMaxPeers = 8;
@@ -93,6 +110,24 @@ struct PeerExchange {
     // next exchange.
     unsigned int* my_op;                     // [2][kProgramMaxOps], this rank's
     unsigned int* peer_op[kMaxPeers];        // each rank's, mapped here
+    // Sharded programs (sharded = 1: each rank computes its own heads and its
+    // partial sums; see program_fold_partials).  Only the ops flagged
+    // `announce` are seen by the peers: the last CTA of the rank to finish one
+    // adds 1 to every peer's xdep counter, which only grows.  Announcement j
+    // of step s has arrived from every peer once the own counter reaches
+    // (s * deps_per_step + j + 1) * (world - 1): a peer cannot announce j + 1
+    // before every rank announced j, so no later announcement is counted
+    // early.  No end-of-launch exchange; the step's last launch (end_of_step)
+    // advances the step counter as its grid exits.  tail_wait: 1 + the index
+    // of an announcement every CTA waits for before it exits (outputs the next
+    // kernel reads from every rank).
+    uint32_t sharded;
+    uint32_t deps_per_step;
+    uint32_t end_of_step;
+    uint32_t tail_wait;
+    unsigned int* my_xdep;
+    unsigned int* peer_xdep[kMaxPeers];
+    unsigned int* my_step;
 };
 
 struct ProgramParams {
@@ -166,6 +201,51 @@ __device__ __forceinline__ bool wait_counter_sys(const unsigned int* counter, un
     return true;
 }
 
+// Sharded programs: wait (bounded) until announcement j of the current step
+// has arrived from every peer (wrap-safe compare).
+__device__ __forceinline__ bool wait_announcement(const PeerExchange& px, uint32_t j, DeviceStatus* st,
+                                                  unsigned int where) {
+    const unsigned int step = __ldcg(px.my_step);
+    const unsigned int target = (step * px.deps_per_step + j + 1u) * (px.world - 1u);
+    if (static_cast<int>(ld_acquire_sys(px.my_xdep) - target) >= 0) return true;
+    const unsigned long long t0 = global_timer_ns();
+    while (static_cast<int>(ld_acquire_sys(px.my_xdep) - target) < 0) {
+        if (global_timer_ns() - t0 > kWaitNs) {
+            report_timeout(st, where);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
+// Element c of base + fold(partials): the canonical Q8_K combine order
+// (per 16-super-block segment, leaves folded by strides 8, 4, 2, 1; the
+// segments added in order into 0) when rank q of `world` (a power of two)
+// computed, per row and segment, the fold of the leaves j with j % world == q
+// (strides 8 .. world): the strides world / 2 .. 1 remain, then the running
+// sum over the segments, then the residual add of the unsharded op
+// (residual + W.x).
+__device__ __forceinline__ float program_fold_partials(const float* base, const float* partials, uint32_t segments,
+                                                       uint32_t world, uint32_t n, uint32_t c) {
+    float total = 0.0f;
+    for (uint32_t g = 0; g < segments; ++g) {
+        float s[kMaxPeers];
+#pragma unroll
+        for (uint32_t q = 0; q < kMaxPeers; ++q)
+            s[q] = q < world ? __ldcg(partials + (static_cast<uint64_t>(q) * segments + g) * n + c) : 0.0f;
+#pragma unroll
+        for (uint32_t h = kMaxPeers / 2; h >= 1; h >>= 1) {
+            if (h < world) {
+#pragma unroll
+                for (uint32_t q = 0; q < h; ++q) s[q] = __fadd_rn(s[q], s[q + h]);
+            }
+        }
+        total = __fadd_rn(total, s[0]);
+    }
+    return __fadd_rn(__ldcg(base + c), total);
+}
+
 // The same value into every peer's gather buffer at the offset of `at` in this
 // rank's (NVLink stores to IPC-mapped memory).
 __device__ __forceinline__ void push_to_peers(const PeerExchange& px, const float* at, float v) {
@@ -183,9 +263,9 @@ __device__ __forceinline__ void push_to_peers(const PeerExchange& px, const floa
 // One output row: into y here and, in a peer group, into every peer's gather
 // buffer at the same offset (NVLink store).
 template <bool kPeers>
-__device__ __forceinline__ void program_store_row(const PeerExchange& px, float* yr, float v) {
+__device__ __forceinline__ void program_store_row(const PeerExchange& px, bool push, float* yr, float v) {
     *yr = v;
-    if (kPeers && px.world > 1) {
+    if (kPeers && push && px.world > 1) {
         const size_t off = static_cast<size_t>(yr - px.local_base);
 #pragma unroll
         for (uint32_t p = 0; p < kMaxPeers; ++p)
@@ -238,10 +318,10 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
                     const bool has_b = ja + 1 < n_here;
                     const float v = q8k_row_dot2<kType, kXReg>(op.nb, img, pa, has_b ? pa + rb : pa, xw, xbs, xd, lane);
                     if ((lane & 15) == 0 && (lane == 0 || has_b))  // lane 0: first row, lane 16: second
-                        program_store_row<kPeers>(px, y + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), v);
+                        program_store_row<kPeers>(px, op.push != 0, y + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), v);
                 } else {
                     const float v = q8k_row_dot<kType, kXReg, kUnroll>(op.nb, img, pa, xw, xbs, xd, lane);
-                    if (lane == 0) program_store_row<kPeers>(px, y + q_lo + ja, v);
+                    if (lane == 0) program_store_row<kPeers>(px, op.push != 0, y + q_lo + ja, v);
                 }
             }
         }
@@ -318,9 +398,9 @@ __device__ __forceinline__ void program_walk_segmented(const ProgramOp& op, uint
         if (!failed && mine) {
             if constexpr (kPer == 2) {
                 if ((lane & 15) == 0 && (lane == 0 || has_b))  // lane 0: first row, lane 16: second
-                    program_store_row<kPeers>(px, op.y + r0 + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), total);
+                    program_store_row<kPeers>(px, op.push != 0, op.y + r0 + q_lo + ja + (static_cast<uint32_t>(lane) >> 4), total);
             } else {
-                if (lane == 0) program_store_row<kPeers>(px, op.y + r0 + q_lo + ja, total);
+                if (lane == 0) program_store_row<kPeers>(px, op.push != 0, op.y + r0 + q_lo + ja, total);
             }
         }
     }
@@ -512,7 +592,12 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             uint32_t* wait_ok = reinterpret_cast<uint32_t*>(scratch + 24);
             if (threadIdx.x == 0) {
                 bool ok = !failed && wait_counter(pp.counters + (k - 1), gridDim.x, pp.status, 13);
-                if (ok && px.world > 1) ok = wait_counter_sys(px.my_op + bank + (k - 1), px.world - 1, pp.status, 17);
+                if (ok && px.world > 1) {
+                    if (!px.sharded)
+                        ok = wait_counter_sys(px.my_op + bank + (k - 1), px.world - 1, pp.status, 17);
+                    else if (pp.ext[k].xwait)
+                        ok = wait_announcement(px, pp.ext[k].xwait - 1u, pp.status, 21);
+                }
                 *wait_ok = ok ? 1u : 0u;
             }
             named_barrier_sync(1, NCW * 32);
@@ -551,6 +636,38 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                     const Q8KLane r = quantize_q8k_lane_values(v, lane);
                     store_block_to_image(img, i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
                 }
+            } else if (e.xform == kXformCombineRms) {
+                // x + the fold of every rank's partial sums, element by element
+                // in sum_squares_f64's order (so the RMS inverse equals the
+                // kXformRms one of the unsharded vector), staged in shared
+                // memory; then scaled, quantized and stored as kXformRms does
+                const uint32_t n = op.nb * 256u;
+                float* vec = reinterpret_cast<float*>(act + e.combine_offset);
+                double part = 0.0;
+                if (!failed) {
+                    for (uint32_t c = warp * 32 + lane; c < n; c += NCW * 32) {
+                        const float v = program_fold_partials(op.x, e.partials, e.segments, px.world, n, c);
+                        vec[c] = v;
+                        part = __dadd_rn(part, __dmul_rn(static_cast<double>(v), static_cast<double>(v)));
+                    }
+                }
+                part = warp_sum_f64(part);
+                if (lane == 0) scratch[warp] = part;
+                named_barrier_sync(1, NCW * 32);
+                inv = rms_inverse(warp_sum_f64(lane < NCW ? scratch[lane] : 0.0), n, e.eps);
+                const ActImage img = q8k_image(act + op.act_offset, op.nb);
+                for (uint32_t i = warp; !failed && i < op.nb; i += NCW) {
+                    const float4* vb = reinterpret_cast<const float4*>(vec + 256u * i) + 2 * lane;
+                    const float4 lo = vb[0], hi = vb[1];
+                    float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w}, w[8];
+                    load_lane8(e.norm + 256ull * i, lane, aligned16(e.norm + 256ull * i), w);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], inv), w[j]);
+                    const Q8KLane r = quantize_q8k_lane_values(v, lane);
+                    store_block_to_image(img, i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
+                }
+                if (blockIdx.x == 0 && e.combined && !failed)
+                    for (uint32_t c = threadIdx.x; c < n; c += NCW * 32) e.combined[c] = vec[c];
             } else {
                 if (e.xform == kXformRms) {
                     // the whole vector's sum of squares, reduced over the consumer warps
@@ -604,7 +721,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             for (uint64_t r = r0 + threadIdx.x; r < r1; r += NCW * 32) {
                 const float v = __fadd_rn(__ldcg(op.residual + r), __ldcg(op.y + r));
                 op.y[r] = v;
-                push_to_peers(px, op.y + r, v);
+                if (op.push) push_to_peers(px, op.y + r, v);
             }
         }
         if (pp.ext[k].act && !failed) {
@@ -618,14 +735,14 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                 const float v = __ldcg(op.y + r), o = __ldcg(e.other + r);
                 const float a = e.other_is_gate ? __fmul_rn(ref_silu(o), v) : __fmul_rn(ref_silu(v), o);
                 e.act[r] = a;
-                push_to_peers(px, e.act + r, a);
+                if (op.push) push_to_peers(px, e.act + r, a);
             }
         }
         if (op.publish) {
             // publish this CTA's completion of op k (its y rows are written)
             named_barrier_sync(1, NCW * 32);
             if (threadIdx.x == 0) {
-                if (px.world == 1) {
+                if (px.world == 1 || (px.sharded && !pp.ext[k].announce)) {
                     // the release (after the CTA barrier) covers every warp's rows;
                     // an extra full fence here cost ~1 us per dependency
                     red_release_gpu_add(pp.counters + k, 1u);
@@ -637,7 +754,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                         __threadfence_system();
 #pragma unroll
                         for (uint32_t p = 0; p < kMaxPeers; ++p)
-                            if (p < px.world && p != px.rank) red_release_sys_add(px.peer_op[p] + bank + k, 1u);
+                            if (p < px.world && p != px.rank)
+                                red_release_sys_add(px.sharded ? px.peer_xdep[p] : px.peer_op[p] + bank + k, 1u);
                     }
                 }
             }
@@ -645,6 +763,10 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
     }
     // every consumer warp's rows (and peer stores) precede this CTA's exit count
     if (pp.px.world > 1) named_barrier_sync(1, NCW * 32);
+    // Sharded programs whose last outputs the next kernel reads from every
+    // rank: each CTA leaves only once that announcement arrived from every peer.
+    if (pp.px.sharded && pp.px.tail_wait && pp.px.world > 1 && threadIdx.x == 0 && !failed)
+        wait_announcement(pp.px, pp.px.tail_wait - 1u, pp.status, 22);
     // The last CTA to finish zeroes the counters for the next launch.  A later
     // launch reads them only after its griddepcontrol.wait, i.e. after this
     // grid has completed.
@@ -652,7 +774,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
         __threadfence();
         const unsigned int done = atomicAdd(pp.counters + kProgramMaxOps, 1u);
         if (done == gridDim.x - 1) {
-            if (pp.px.world > 1) {
+            // every CTA has passed its waits of this step: the next step's targets
+            if (pp.px.sharded && pp.px.end_of_step) *pp.px.my_step = *pp.px.my_step + 1u;
+            if (pp.px.world > 1 && !pp.px.sharded) {
                 // Every CTA's rows (and their peer stores) happen before its
                 // exit-counter increment, which this thread acquired: after a
                 // system-scope fence, one release arrival per peer announces

@@ -200,7 +200,10 @@ __device__ __forceinline__ void quantize_to_image(const float* __restrict__ x, u
 //                 whole vector): Oracle's rms_norm_rows for one row
 //                 (qwen35_block.cpp:161-188)
 //   kXformSwiglu  v = silu(x) * x2: the MLP activation (qwen35_block.cpp:315-318)
-enum : uint32_t { kXformNone = 0, kXformRms = 1, kXformSwiglu = 2 };
+//   kXformCombineRms  (matvec programs of a sharded peer group only) v =
+//                 kXformRms of x + the fold of every rank's partial sums
+//                 (program.cuh, program_fold_partials)
+enum : uint32_t { kXformNone = 0, kXformRms = 1, kXformSwiglu = 2, kXformCombineRms = 3 };
 
 struct ActSource {
     const float* x;
