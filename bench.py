@@ -982,8 +982,9 @@ class DecoderWorkload:
                 "kv_capacity": c.context,
                 "contract": "q8k",
                 "parallelism": "single GPU" if n_gpus == 1 else
-                f"tp{n_gpus}: projection rows split over the GPUs, all-gather inside the matvec programs, "
-                f"block cores on every GPU",
+                f"tp{n_gpus}: heads sharded (Gated DeltaNet value heads, attention query heads, FFN columns, "
+                f"vocabulary rows per GPU); output projection and ffn_down as canonical-order partial sums "
+                f"exchanged over NVLink inside the matvec programs, 2 cross-GPU dependencies per block",
                 "l2": "no flush needed: each step streams 4.7 GB of weights (> 37x the 126 MB L2)"}
 
     def step_bytes(self, position: int, batch: int = 1) -> int:
@@ -1168,10 +1169,16 @@ def decoder_arm(args, wl: DecoderWorkload) -> None:
         dist.all_gather_object(hs, handle)
         return hs
 
-    # several GPUs: tensor parallel (every projection's rows split over the
-    # ranks, exchange inside the matvec programs); the job decodes ONE sequence
-    dec = Qwen35Decoder(ctx, wl.cfg, tensors, contract="q8k", capacity=wl.cfg.context, max_new=max_new,
-                        device=local, rank=rank, world=world, exchange=exchange if world > 1 else None)
+    # several GPUs: heads sharded (each rank its own heads, FFN columns and
+    # vocabulary rows; partial sums exchanged inside the matvec programs); the
+    # job decodes ONE sequence
+    if world > 1:
+        from oracle_b200.tp_decoder import HeadShardedDecoder
+        dec = HeadShardedDecoder(ctx, wl.cfg, tensors, rank, world, exchange, capacity=wl.cfg.context,
+                                 max_new=max_new, device=local)
+    else:
+        dec = Qwen35Decoder(ctx, wl.cfg, tensors, contract="q8k", capacity=wl.cfg.context, max_new=max_new,
+                            device=local)
     if wl.prompt_len + max_new > wl.cfg.context:
         raise SystemExit("warm-up + timed steps exceed the KV cache capacity")
 
@@ -1185,6 +1192,7 @@ def decoder_arm(args, wl: DecoderWorkload) -> None:
                        "(single-threaded); Q4_K/Q6_K projections through the C restatement of GGML's Q8_K "
                        "dot, since Oracle's own decoder rejects Q4_K; tokens identical to the GPU's"}
     if not args.no_cpu:
+        barrier(world)  # rank 0 ran the CPU leg: every rank's first step starts together
         got = dec.generate(prompt[:2], 2)
         if rank == 0 and not np.array_equal(got, want):
             raise SystemExit(f"GPU tokens {got.tolist()} differ from the CPU reference {want.tolist()}")
@@ -1239,7 +1247,7 @@ def decoder_arm(args, wl: DecoderWorkload) -> None:
                 "config": wl.config(world), "gpu_launches": launches * args.steps,
                 "e2e": {"value": wl.n_new / e2e_s, "unit": wl.unit, "h2d_bytes_per_step": 4,
                         "d2h_bytes_per_step": 4,
-                        "how": f"Qwen35Decoder.generate: 128-token host prompt in, {wl.n_new} greedy tokens out "
+                        "how": f"{type(dec).__name__}.generate: 128-token host prompt in, {wl.n_new} greedy tokens out "
                                f"({forwards} graph replays, prompt ingested token by token as Oracle does); "
                                f"value = generated tokens / wall time",
                         "forward_steps_per_s": forwards / e2e_s, "first_tokens": toks[:8].tolist()},

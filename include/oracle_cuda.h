@@ -547,8 +547,8 @@ oracle_cuda_status oracle_cuda_matvec_program_allgather(oracle_cuda_context* ctx
  *   swiglu_gate  optional: after the op, act_dev[r] = silu(swiglu_gate[r]) *
  *             y[r] for the op's rows (the MLP activation from the gate
  *             rows of an earlier op and this op's up rows);
- *   combined_dev  XFORM_COMBINE_RMS, optional: receives the combined vector
- *             (cols floats, before the norm).
+ *   combined_dev  XFORM_COMBINE_RMS: receives the combined vector (cols
+ *             floats, before the norm; device memory other than x_dev).
  * `step`: first_dep = the index within the decode step of this call's first
  * announcement, deps_per_step = announcements per step (the same on every
  * rank), end_of_step = 1 on the step's last call, tail_wait = 1: the call's
@@ -578,6 +578,20 @@ typedef struct oracle_cuda_sharded_step {
 oracle_cuda_status oracle_cuda_matvec_program_sharded(oracle_cuda_context* ctx, oracle_cuda_peer_group* group,
                                                       const oracle_cuda_sharded_op* ops, uint32_t n_ops,
                                                       const oracle_cuda_sharded_step* step, void* stream);
+
+/* Launch trace of the matvec programs (all entry points that launch one):
+ * with `records` > 0, the programs launched from now on write global-timer
+ * stamps (ns) into trace_dev (device memory, 8-byte aligned, 1 + records *
+ * ORACLE_CUDA_TRACE_WORDS words, word 0 zero to start): word 0 counts
+ * launches; launch r (while r < records) fills words 1 + r * TRACE_WORDS
+ * onward, as seen by CTA 0: [0] consumers start (after the wait for the
+ * preceding kernel), per op k [1 + 3k] its wait for earlier ops done,
+ * [2 + 3k] its activation image built, [3 + 3k] its rows written and
+ * published, [TRACE_WORDS - 1] CTA 0 done.  records = 0 switches it off.
+ * Launches captured in a CUDA graph keep the setting of their capture. */
+#define ORACLE_CUDA_TRACE_WORDS 50
+oracle_cuda_status oracle_cuda_set_program_trace(oracle_cuda_context* ctx, unsigned long long* trace_dev,
+                                                 uint32_t records);
 
 /* ------------------------------------------------------------------ prefill dequant-GEMM
  * Y[m][n] = sum_k X[m][k] * W[n][k] for m < m_tokens: the batched form of the

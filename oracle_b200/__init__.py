@@ -146,6 +146,8 @@ _proto("oracle_cuda_matvec_program", [_vp, C.POINTER(MatvecOp), _u32, _vp])
 _proto("oracle_cuda_matvec_program_ex", [_vp, C.POINTER(MatvecOpEx), _u32, _vp])
 _proto("oracle_cuda_matvec_program_ex_allgather", [_vp, _vp, C.POINTER(MatvecOpEx), _u32, _vp])
 _proto("oracle_cuda_matvec_program_sharded", [_vp, _vp, C.POINTER(ShardedOp), _u32, C.POINTER(ShardedStep), _vp])
+_proto("oracle_cuda_set_program_trace", [_vp, _vp, _u32])
+TRACE_WORDS = 50
 _proto("oracle_cuda_matvec_program_noalloc", [C.POINTER(MatvecOp), _u32, _vp])
 _proto("oracle_cuda_noalloc_status", [_i32])
 _proto("oracle_cuda_noalloc_selftest_bounded_wait", [_u64, _vp])
@@ -552,6 +554,13 @@ class Context:
         st = ShardedStep(first_dep, deps_per_step, 1 if end_of_step else 0, 1 if tail_wait else 0)
         self._check(_lib.oracle_cuda_matvec_program_sharded(self._h, group._h, arr, len(ops), C.byref(st),
                                                             _stream(stream)))
+
+    def set_program_trace(self, trace, records: int) -> None:
+        """oracle_cuda_set_program_trace: trace = int64 CUDA tensor of at least
+        1 + records * TRACE_WORDS words (word 0 zero), or None / records 0 to stop."""
+        if records and (trace is None or trace.numel() < 1 + records * TRACE_WORDS):
+            raise InvalidArgument("trace buffer too small")
+        self._check(_lib.oracle_cuda_set_program_trace(self._h, _addr(trace), records))
 
     def matvec_program_ex(self, ops, stream=None) -> None:
         """ops: sequence of dicts with keys qtype, rows, cols, w, x, y and

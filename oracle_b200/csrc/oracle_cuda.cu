@@ -58,7 +58,9 @@ struct oracle_cuda_context {
     uint32_t flags = 0;
     uint64_t launches = 0;
     DeviceStatus* status = nullptr;
-    unsigned int* program_counters = nullptr;  // kProgramMaxOps + 1, zero between launches
+    unsigned int* program_counters = nullptr;  // kProgramCounters, zero between launches
+    unsigned long long* trace = nullptr;       // matvec program launch trace (caller's memory), or null
+    uint32_t trace_records = 0;
     uint8_t* image_scratch = nullptr;          // prebuilt activation images of programs
     uint64_t image_scratch_bytes = 0;
     uint8_t* act_scratch = nullptr;            // SwiGLU activations formed in program epilogues
@@ -672,12 +674,12 @@ oracle_cuda_status oracle_cuda_create(int device, oracle_cuda_context** out) {
     }
     cudaMemset(ctx->status, 0, sizeof(DeviceStatus));
     if ((e = cudaMalloc(reinterpret_cast<void**>(&ctx->program_counters),
-                        (kProgramMaxOps + 1) * sizeof(unsigned int))) != cudaSuccess) {
+                        kProgramCounters * sizeof(unsigned int))) != cudaSuccess) {
         cudaFree(ctx->status);
         delete ctx;
         return cuda_fail(nullptr, e, "cudaMalloc(program counters)");
     }
-    cudaMemset(ctx->program_counters, 0, (kProgramMaxOps + 1) * sizeof(unsigned int));
+    cudaMemset(ctx->program_counters, 0, kProgramCounters * sizeof(unsigned int));
     *out = ctx;
     return ORACLE_CUDA_OK;
 }
@@ -723,7 +725,7 @@ oracle_cuda_status oracle_cuda_device_status(oracle_cuda_context* ctx) {
     ORACLE_CUDA_TRY(ctx, cudaMemcpy(&st, ctx->status, sizeof st, cudaMemcpyDeviceToHost), "cudaMemcpy(status)");
     ORACLE_CUDA_TRY(ctx, cudaMemset(ctx->status, 0, sizeof st), "cudaMemset(status)");
     if (st.code != kDevOk)  // an aborted program may have left its counters set
-        ORACLE_CUDA_TRY(ctx, cudaMemset(ctx->program_counters, 0, (kProgramMaxOps + 1) * sizeof(unsigned int)),
+        ORACLE_CUDA_TRY(ctx, cudaMemset(ctx->program_counters, 0, kProgramCounters * sizeof(unsigned int)),
                         "cudaMemset(program counters)");
     if (st.code == 3u)  // causal_attention_step (reference_kernels.cpp:170-172)
         return fail(ctx, ORACLE_CUDA_RUNTIME_ERROR, "causal attention softmax normalization failed");
@@ -942,7 +944,7 @@ namespace {
 // planner for every entry point that launches matvec_program_kernel, so they
 // all stream the same stages for the same ops.
 oracle_cuda_status plan_program_ring(ProgramParams& pp, uint64_t smem_budget, uint64_t stage_target,
-                                     std::string& why) {
+                                     std::string& why, bool narrow_walk = false) {
     why = "matvec program rows too long for the shared-memory stage ring";
     if (pp.act_bytes > 96 * 1024) return ORACLE_CUDA_UNSUPPORTED;
     const uint64_t budget = smem_budget - stream_barrier_bytes(16) - pp.act_bytes;
@@ -965,7 +967,9 @@ oracle_cuda_status plan_program_ring(ProgramParams& pp, uint64_t smem_budget, ui
                           : 0u;
         const uint64_t rb = p.segmented ? uint64_t(kSegmentBlocks) * (q6 ? 210u : 144u) : p.row_bytes;
         uint64_t R = target > 32 ? (target - 32) / rb : 0;
-        const uint64_t cap = (p.segmented && q6) ? kProgramWarps : 2 * kProgramWarps;
+        // narrow rows (<= 8 super-blocks): 32 / L rows per warp task (L = 2, 4, 8)
+        const uint64_t narrow = !narrow_walk ? 0 : p.nb <= 2 ? 16 : p.nb <= 4 ? 8 : p.nb <= 8 ? 4 : 0;
+        const uint64_t cap = (p.segmented && q6) ? kProgramWarps : narrow ? narrow * kProgramWarps : 2 * kProgramWarps;
         if (R > cap) R = cap;
         if (R < 1) R = 1;
         p.rows_per_stage = static_cast<uint32_t>(R);
@@ -1037,7 +1041,11 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
                     return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
                                 at + "the combine transform needs wait 2 or 3, partial sums, segments, norm weights "
                                      "and a positive finite epsilon");
-                if (reinterpret_cast<uintptr_t>(e.x2_dev) % 4 || reinterpret_cast<uintptr_t>(e.base.x_dev) % 4)
+                if (!sh[k].combined_dev || sh[k].combined_dev == e.base.x_dev)
+                    return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT,
+                                at + "the combine transform needs combined_dev, distinct from x_dev");
+                if (reinterpret_cast<uintptr_t>(e.x2_dev) % 4 || reinterpret_cast<uintptr_t>(e.base.x_dev) % 4 ||
+                    reinterpret_cast<uintptr_t>(sh[k].combined_dev) % 4)
                     return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, at + "combine vectors must be 4-byte aligned");
             }
             if (sh[k].swiglu_gate && !e.act_dev)
@@ -1144,7 +1152,7 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
     // op whose source equals an earlier op's shares that op's image: it needs
     // neither a build nor a wait of its own.
     ImageJobs jobs{};
-    uint32_t prebuilt = 0, blocks = 0, act_total = 0, combine_off = 0;
+    uint32_t prebuilt = 0, blocks = 0, act_total = 0;
     {
         // produced[k]: x comes from earlier ops of this launch (waited for by
         // this op, or, sharded wait 3, by an earlier one): built in the kernel
@@ -1207,14 +1215,7 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
             if (owner[k] >= 0) pp.ops[k].act_offset = pp.ops[owner[k]].act_offset;
         for (uint32_t k = 1; k < n_ops; ++k)
             if (pp.ops[k].after_previous) pp.ops[k - 1].publish = 1u;
-        // the combined vectors of combine transforms (one at a time) after the images
-        uint32_t combine_bytes = 0;
-        for (uint32_t k = 0; k < n_ops; ++k)
-            if (pp.ext[k].xform == kXformCombineRms && pp.ext[k].build)
-                combine_bytes = std::max(combine_bytes, pp.ops[k].nb * 256u * 4u);
-        combine_off = off;
-        for (uint32_t k = 0; k < n_ops; ++k) pp.ext[k].combine_offset = combine_off;
-        act_total = off + combine_bytes + 256;  // + reduction scratch
+        act_total = off + 256;  // + reduction scratch
         // Images that would crowd the stage ring out of shared memory stay in
         // global memory; each op copies its own into one of two slots.
         if (prebuilt > ctx->jit_image_threshold) {
@@ -1237,13 +1238,14 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
             }
             pp.jit_slot_bytes = slot;
             act_total = act_total - prebuilt + 2 * slot;
-            for (uint32_t k = 0; k < n_ops; ++k) pp.ext[k].combine_offset = combine_off - prebuilt + 2 * slot;
         }
     }
     pp.act_bytes = act_total;
     {
         std::string why;
-        const oracle_cuda_status rs = plan_program_ring(pp, ctx->smem_budget, ctx->program_stage_target, why);
+        // peer-group programs walk rows of <= 8 super-blocks narrow (more rows per stage)
+        const oracle_cuda_status rs =
+            plan_program_ring(pp, ctx->smem_budget, ctx->program_stage_target, why, group != nullptr);
         if (rs != ORACLE_CUDA_OK) return fail(ctx, rs, why);
     }
     pp.copy_chunk = ctx->copy_chunk;
@@ -1251,6 +1253,8 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
     pp.prebuilt_bytes = prebuilt;
     pp.counters = ctx->program_counters;
     pp.status = ctx->status;
+    pp.trace = ctx->trace;
+    pp.trace_records = ctx->trace_records;
     pp.px.world = 1;
     if (group) {
         if (!group->connected) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "peer group is not connected");
@@ -1894,6 +1898,7 @@ namespace {
 
 constexpr uint64_t kNoAllocImageBytes = ORACLE_CUDA_NOALLOC_IMAGE_BYTES;
 constexpr uint64_t kNoAllocCountersOffset = kNoAllocImageBytes;
+static_assert(kProgramCounters * sizeof(unsigned int) <= 256, "no-allocation counters fit before the status word");
 constexpr uint64_t kNoAllocStatusOffset = kNoAllocImageBytes + 256;
 constexpr uint64_t kNoAllocScratchBytes = kNoAllocImageBytes + 512;
 constexpr int kNoAllocMaxDevices = 64;
@@ -2889,6 +2894,19 @@ extern "C" oracle_cuda_status oracle_cuda_matvec_program_ex_allgather(oracle_cud
                                                                       uint32_t n_ops, void* stream) {
     if (!group) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "peer group is null");
     return program_run(ctx, ops, n_ops, stream, group);
+}
+
+static_assert(kTraceWords == ORACLE_CUDA_TRACE_WORDS, "trace record size");
+
+extern "C" oracle_cuda_status oracle_cuda_set_program_trace(oracle_cuda_context* ctx, unsigned long long* trace_dev,
+                                                            uint32_t records) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (records > 0 && !trace_dev) return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "trace buffer is null");
+    if (trace_dev && reinterpret_cast<uintptr_t>(trace_dev) % 8)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "trace buffer must be 8-byte aligned");
+    ctx->trace = records > 0 ? trace_dev : nullptr;
+    ctx->trace_records = records;
+    return ok(ctx);
 }
 
 extern "C" oracle_cuda_status oracle_cuda_matvec_program_sharded(oracle_cuda_context* ctx,

@@ -24,6 +24,10 @@
 namespace oracle_cuda {
 
 constexpr int kProgramMaxOps = 16;
+// Completion counters of a launch: [k] op k's CTAs done, [kProgramMaxOps] CTAs
+// exited, [kProgramMaxOps + 1 + k] op k's combine slices written; zero between
+// launches (the last CTA to exit clears them).
+constexpr uint32_t kProgramCounters = 2 * kProgramMaxOps + 1;
 
 struct ProgramOp {
     const uint8_t* w;
@@ -69,13 +73,11 @@ struct ProgramOpExtra {
     float* act;
     // kXformCombineRms: the activation is rms(x + fold(partials)), partials
     // [world][segments][cols] in the gather buffer (every rank's partial sums
-    // of the same rows); the folded vector is staged in shared memory at
-    // combine_offset of the activation region and, by CTA 0, written to
-    // `combined` (optional)
+    // of the same rows); the folded vector is formed in `combined` (global,
+    // each CTA its slice)
     const float* partials;
     float* combined;
     uint32_t segments;
-    uint32_t combine_offset;
     // sharded peer groups: 1 + the step-wide index of the announcement made
     // once this rank finished this op (0: none), and 1 + the index of the
     // announcement an after_previous op waits for besides its own CTAs (0: none)
@@ -111,16 +113,17 @@ struct PeerExchange {
     unsigned int* my_op;                     // [2][kProgramMaxOps], this rank's
     unsigned int* peer_op[kMaxPeers];        // each rank's, mapped here
     // Sharded programs (sharded = 1: each rank computes its own heads and its
-    // partial sums; see program_fold_partials).  Only the ops flagged
-    // `announce` are seen by the peers: the last CTA of the rank to finish one
-    // adds 1 to every peer's xdep counter, which only grows.  Announcement j
-    // of step s has arrived from every peer once the own counter reaches
-    // (s * deps_per_step + j + 1) * (world - 1): a peer cannot announce j + 1
-    // before every rank announced j, so no later announcement is counted
-    // early.  No end-of-launch exchange; the step's last launch (end_of_step)
-    // advances the step counter as its grid exits.  tail_wait: 1 + the index
-    // of an announcement every CTA waits for before it exits (outputs the next
-    // kernel reads from every rank).
+    // partial sums, which it stores into every rank's gather buffer; see
+    // program_fold_partials).  Only the ops flagged `announce` are seen
+    // across ranks: the last CTA of a rank to finish one adds 1 (system-scope
+    // fence, then release) to every peer's xdep counter, which only grows.
+    // Announcement j of step s has arrived from every peer once the own
+    // counter reaches (s * deps_per_step + j + 1) * (world - 1): no rank
+    // announces j + 1 before every rank announced j, so no later announcement
+    // is counted early.  No end-of-launch exchange; the step's
+    // last launch (end_of_step) advances the step counter as its grid exits.
+    // tail_wait: 1 + the index of an announcement every CTA waits for before
+    // it exits (outputs the next kernel reads from every rank).
     uint32_t sharded;
     uint32_t deps_per_step;
     uint32_t end_of_step;
@@ -148,7 +151,16 @@ struct ProgramParams {
     unsigned int* counters;  // kProgramMaxOps completion counters + 1 exit counter, zero at launch
     DeviceStatus* status;
     PeerExchange px;
+    // Optional launch trace (null: off): the first consumer thread of CTA 0
+    // takes record r = trace[0]++ and, while r < trace_records, writes global
+    // timer stamps into trace[1 + r * kTraceWords ...]: [0] consumers start
+    // (after the programmatic-launch wait), per op k [1 + 3k] its wait done,
+    // [2 + 3k] its image built, [3 + 3k] its rows written and published,
+    // [kTraceWords - 1] CTA 0 done.
+    unsigned long long* trace;
+    uint32_t trace_records;
 };
+constexpr uint32_t kTraceWords = 2 + 3 * kProgramMaxOps;
 
 __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
     unsigned int v;
@@ -226,11 +238,14 @@ __device__ __forceinline__ bool wait_announcement(const PeerExchange& px, uint32
 // (strides 8 .. world): the strides world / 2 .. 1 remain, then the running
 // sum over the segments, then the residual add of the unsharded op
 // (residual + W.x).
-__device__ __forceinline__ float program_fold_partials(const float* base, const float* partials, uint32_t segments,
-                                                       uint32_t world, uint32_t n, uint32_t c) {
+__device__ __forceinline__ float program_fold_partials(const PeerExchange& px, const float* base,
+                                                       const float* partials, uint32_t segments, uint32_t n,
+                                                       uint32_t c) {
+    const uint32_t world = px.world;
     float total = 0.0f;
     for (uint32_t g = 0; g < segments; ++g) {
         float s[kMaxPeers];
+        // every rank's partials were stored into this rank's gather buffer
 #pragma unroll
         for (uint32_t q = 0; q < kMaxPeers; ++q)
             s[q] = q < world ? __ldcg(partials + (static_cast<uint64_t>(q) * segments + g) * n + c) : 0.0f;
@@ -323,6 +338,69 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
                     const float v = q8k_row_dot<kType, kXReg, kUnroll>(op.nb, img, pa, xw, xbs, xd, lane);
                     if (lane == 0) program_store_row<kPeers>(px, op.push != 0, y + q_lo + ja, v);
                 }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == S) {
+            s = 0;
+            phase ^= 1u;
+        }
+        owner_base += step;
+        if (owner_base >= NCW) owner_base -= NCW;
+    }
+}
+
+// Consumer walk over an op of narrow rows (at most 8 super-blocks): a warp's
+// task is 32 / L consecutive rows of a stage (L = 2, 4 or 8 >= nb; two rows per
+// group of 2L lanes, q8k_rows_narrow), tasks rotating over the warps from stage
+// to stage as in program_walk_op.  Rows past the stage's end read a row of the
+// task (in bounds) and are not stored.
+template <int NCW, uint32_t kType, bool kXReg, bool kPeers>
+__device__ __forceinline__ void program_walk_narrow(const ProgramOp& op, uint32_t L, uint8_t* act, uint8_t* stage0,
+                                                    uint32_t stage_bytes, uint32_t S, uint64_t* full, uint64_t* empty,
+                                                    uint32_t& s, uint32_t& phase, bool& failed, DeviceStatus* status,
+                                                    const PeerExchange& px, int warp, int lane) {
+    const ActImage img = q8k_image(act + op.act_offset, op.nb);
+    const uint32_t W = 2u * L;
+    const uint32_t li = static_cast<uint32_t>(lane) & (W - 1u);
+    const uint32_t group = static_cast<uint32_t>(lane) >> (L == 2u ? 2u : L == 4u ? 3u : 4u);
+    const uint32_t per = 32u / L;  // rows per task
+    uint32_t xw[32];
+    int xbs[8];
+    float xd = 0.0f;
+    if (kXReg && !failed) load_lane_x<kType>(img, op.nb, static_cast<int>(li), xw, xbs, xd);
+    const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
+    const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
+    const uint32_t nrows = static_cast<uint32_t>(r1 - r0);
+    const uint32_t R = op.rows_per_stage;
+    const uint32_t T = (nrows + R - 1) / R;
+    const uint32_t rb = static_cast<uint32_t>(op.row_bytes);
+    const uint32_t wlo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w));
+    const uint32_t row0 = static_cast<uint32_t>(r0);
+    float* const y = op.y + r0;
+    const uint32_t step = ((R + per - 1) / per) % NCW;
+    uint32_t owner_base = 0;
+    for (uint32_t t = 0; t < T; ++t) {
+        if (!failed) {
+            const bool ok = mbar_wait(&full[s], phase, status, 14);
+            failed = !__all_sync(0xFFFFFFFFu, ok);
+        }
+        if (!failed) {
+            const uint32_t q_lo = t * R;
+            const uint32_t n_here = nrows - q_lo < R ? nrows - q_lo : R;
+            const uint32_t head = (wlo + (row0 + q_lo) * rb) & 15u;
+            const uint8_t* slot = stage0 + s * stage_bytes + head;
+            const uint32_t n_tasks = (n_here + per - 1) / per;
+            uint32_t task = warp >= static_cast<int>(owner_base) ? warp - owner_base : warp + NCW - owner_base;
+            for (; task < n_tasks; task += NCW) {
+                const uint32_t ja = per * task + 2u * group;
+                const bool has_a = ja < n_here, has_b = ja + 1u < n_here;
+                const uint8_t* pa = slot + (has_a ? ja : per * task) * rb;
+                const uint8_t* pb = has_b ? pa + rb : pa;
+                const float v = q8k_rows_narrow<kType, kXReg>(op.nb, L, img, pa, pb, xw, xbs, xd, lane);
+                if ((li == 0u && has_a) || (li == L && has_b))
+                    program_store_row<kPeers>(px, op.push != 0, y + q_lo + ja + (li == L ? 1u : 0u), v);
             }
         }
         __syncwarp();
@@ -562,6 +640,12 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
     pdl_wait();
     bool failed = false;
     const PeerExchange& px = pp.px;
+    unsigned long long* trace = nullptr;
+    if (pp.trace && blockIdx.x == 0 && threadIdx.x == 0) {
+        const unsigned long long r = atomicAdd(pp.trace, 1ull);
+        if (r < pp.trace_records) trace = pp.trace + 1 + r * kTraceWords;
+        if (trace) trace[0] = global_timer_ns();
+    }
     const uint32_t bank = px.world > 1 ? (*px.my_epoch & 1u) * kProgramMaxOps : 0u;
     // Every op that reads an activation from outside this launch had its image
     // built once, before this kernel, by quantize_images_kernel (the preceding
@@ -603,23 +687,49 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             named_barrier_sync(1, NCW * 32);
             failed = failed || *wait_ok == 0u;
         }
+        if (trace) trace[1 + 3 * k] = global_timer_ns();
         if (pp.ext[k].build) {
             const ProgramOpExtra& e = pp.ext[k];
-            const ActSource a{op.x, e.x2, e.norm, e.eps, e.xform};
+            const float* src = op.x;
+            if (kPeers && e.xform == kXformCombineRms) {
+                // x + the fold of every rank's partial sums: each CTA folds its
+                // slice of the vector into `combined`, every CTA waits for all
+                // slices (this op's combine counter), and the image is built
+                // from `combined` by the kXformRms code below (the unsharded
+                // program's sum order, so the same RMS inverse)
+                const uint32_t n = op.nb * 256u;
+                const uint32_t lo = blockIdx.x * n / gridDim.x, hi = (blockIdx.x + 1u) * n / gridDim.x;
+                if (!failed)
+                    for (uint32_t c = lo + threadIdx.x; c < hi; c += NCW * 32)
+                        e.combined[c] = program_fold_partials(px, op.x, e.partials, e.segments, n, c);
+                named_barrier_sync(1, NCW * 32);
+                uint32_t* wait_ok = reinterpret_cast<uint32_t*>(scratch + 24);
+                if (threadIdx.x == 0) {
+                    unsigned int* slices = pp.counters + kProgramMaxOps + 1 + k;
+                    red_release_gpu_add(slices, 1u);  // after the CTA barrier: covers every warp's slice
+                    *wait_ok = (!failed && wait_counter(slices, gridDim.x, pp.status, 23)) ? 1u : 0u;
+                }
+                named_barrier_sync(1, NCW * 32);
+                failed = failed || *wait_ok == 0u;
+                src = e.combined;
+            }
+            const uint32_t xf = e.xform == kXformCombineRms ? kXformRms : e.xform;
+            const ActSource a{src, e.x2, e.norm, e.eps, xf};
             float inv = 0.0f;
-            if (e.xform == kXformRms) {
+            if (xf == kXformRms) {
                 // The warp's first block of x and of the norm weights is loaded
                 // first, in flight with the sum of squares' loads; every block is
                 // scaled, quantized and stored exactly as quantize_xform_to_image
                 // does (the later blocks after the sum).
                 const uint32_t n = op.nb * 256u;
-                const uint32_t i0 = warp;
+                const uint32_t i0 = warp, i1 = warp + NCW;
                 float v0[8], w0[8];
                 if (!failed && i0 < op.nb) {
-                    load_lane8(op.x + 256ull * i0, lane, aligned16(op.x + 256ull * i0), v0);
+                    load_lane8(src + 256ull * i0, lane, aligned16(src + 256ull * i0), v0);
                     load_lane8(e.norm + 256ull * i0, lane, aligned16(e.norm + 256ull * i0), w0);
                 }
-                const double part = warp_sum_f64(failed ? 0.0 : sum_squares_f64(op.x, warp * 32 + lane, n, NCW * 32));
+
+                const double part = warp_sum_f64(failed ? 0.0 : sum_squares_f64(src, warp * 32 + lane, n, NCW * 32));
                 if (lane == 0) scratch[warp] = part;
                 named_barrier_sync(1, NCW * 32);
                 inv = rms_inverse(warp_sum_f64(lane < NCW ? scratch[lane] : 0.0), n, e.eps);
@@ -630,44 +740,12 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                     const Q8KLane r = quantize_q8k_lane_values(v0, lane);
                     store_block_to_image(img, i0, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
                 }
-                for (uint32_t i = i0 + NCW; !failed && i < op.nb; i += NCW) {
+                for (uint32_t i = i1; !failed && i < op.nb; i += NCW) {
                     float v[8];
                     load_lane8_xform(a, i, lane, inv, v);
                     const Q8KLane r = quantize_q8k_lane_values(v, lane);
                     store_block_to_image(img, i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
                 }
-            } else if (e.xform == kXformCombineRms) {
-                // x + the fold of every rank's partial sums, element by element
-                // in sum_squares_f64's order (so the RMS inverse equals the
-                // kXformRms one of the unsharded vector), staged in shared
-                // memory; then scaled, quantized and stored as kXformRms does
-                const uint32_t n = op.nb * 256u;
-                float* vec = reinterpret_cast<float*>(act + e.combine_offset);
-                double part = 0.0;
-                if (!failed) {
-                    for (uint32_t c = warp * 32 + lane; c < n; c += NCW * 32) {
-                        const float v = program_fold_partials(op.x, e.partials, e.segments, px.world, n, c);
-                        vec[c] = v;
-                        part = __dadd_rn(part, __dmul_rn(static_cast<double>(v), static_cast<double>(v)));
-                    }
-                }
-                part = warp_sum_f64(part);
-                if (lane == 0) scratch[warp] = part;
-                named_barrier_sync(1, NCW * 32);
-                inv = rms_inverse(warp_sum_f64(lane < NCW ? scratch[lane] : 0.0), n, e.eps);
-                const ActImage img = q8k_image(act + op.act_offset, op.nb);
-                for (uint32_t i = warp; !failed && i < op.nb; i += NCW) {
-                    const float4* vb = reinterpret_cast<const float4*>(vec + 256u * i) + 2 * lane;
-                    const float4 lo = vb[0], hi = vb[1];
-                    float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w}, w[8];
-                    load_lane8(e.norm + 256ull * i, lane, aligned16(e.norm + 256ull * i), w);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], inv), w[j]);
-                    const Q8KLane r = quantize_q8k_lane_values(v, lane);
-                    store_block_to_image(img, i, lane, r.q_lo, r.q_hi, r.bsum16, r.d);
-                }
-                if (blockIdx.x == 0 && e.combined && !failed)
-                    for (uint32_t c = threadIdx.x; c < n; c += NCW * 32) e.combined[c] = vec[c];
             } else {
                 if (e.xform == kXformRms) {
                     // the whole vector's sum of squares, reduced over the consumer warps
@@ -683,13 +761,25 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
             }
             named_barrier_sync(1, NCW * 32);
         }
+        if (trace) trace[2 + 3 * k] = global_timer_ns();
         const bool q4 = kTypes == 1 || (kTypes == 3 && op.type == 12);
         static_assert(kTypes >= 1 && kTypes <= 4, "program type set");
-        if (q4) {
-            if (op.nb <= 16)
-                program_walk_op<NCW, 12, true, 1, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
-                                               pp.status, pp.px, warp, lane);
-            else if (op.segmented)
+        // rows of at most 8 super-blocks: the narrow walk, compiled only into
+        // the peer-group programs (whose column shards have such rows), so the
+        // single-GPU programs keep their register allocation
+        if (kPeers && q4 && op.nb <= 8) {
+            const uint32_t L = op.nb <= 2 ? 2u : op.nb <= 4 ? 4u : 8u;
+            program_walk_narrow<NCW, 12, true, kPeers>(op, L, act, stage0, pp.stage_bytes, S, full, empty, s, phase,
+                                                      failed, pp.status, pp.px, warp, lane);
+        } else if (q4 && op.nb <= 16) {
+            program_walk_op<NCW, 12, true, 1, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
+                                                      pp.status, pp.px, warp, lane);
+        } else if (kPeers && !q4 && op.nb <= 8) {
+            const uint32_t L = op.nb <= 2 ? 2u : op.nb <= 4 ? 4u : 8u;
+            program_walk_narrow<NCW, 14, false, kPeers>(op, L, act, stage0, pp.stage_bytes, S, full, empty, s, phase,
+                                                       failed, pp.status, pp.px, warp, lane);
+        } else if (q4) {
+            if (op.segmented)
                 program_walk_segmented<NCW, 12, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase,
                                                         failed, pp.status, pp.px, warp, lane);
             else  // passes unrolled by two where the registers allow (not beside the Q6_K code)
@@ -760,6 +850,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                 }
             }
         }
+        if (trace) trace[3 + 3 * k] = global_timer_ns();
     }
     // every consumer warp's rows (and peer stores) precede this CTA's exit count
     if (pp.px.world > 1) named_barrier_sync(1, NCW * 32);
@@ -767,6 +858,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
     // rank: each CTA leaves only once that announcement arrived from every peer.
     if (pp.px.sharded && pp.px.tail_wait && pp.px.world > 1 && threadIdx.x == 0 && !failed)
         wait_announcement(pp.px, pp.px.tail_wait - 1u, pp.status, 22);
+    if (trace) trace[kTraceWords - 1] = global_timer_ns();
     // The last CTA to finish zeroes the counters for the next launch.  A later
     // launch reads them only after its griddepcontrol.wait, i.e. after this
     // grid has completed.
@@ -807,7 +899,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
                 *pp.px.my_epoch = epoch + 1u;
                 (void)ok;
             }
-            for (uint32_t k = 0; k <= kProgramMaxOps; ++k) pp.counters[k] = 0u;
+            for (uint32_t k = 0; k < kProgramCounters; ++k) pp.counters[k] = 0u;
             __threadfence();
         }
     }

@@ -239,19 +239,17 @@ __device__ __forceinline__ void load_lane8_xform(const ActSource& a, uint32_t i,
 __device__ __forceinline__ double sum_squares_f64(const float* __restrict__ x, uint32_t first, uint32_t n,
                                                   uint32_t stride) {
     double s = 0.0;
-    uint32_t c = first;
-    // eight loads in flight per round; the additions keep the element order
-    constexpr uint32_t kB = 8;
-    for (; c + (kB - 1) * stride < n; c += kB * stride) {
+    // sixteen (predicated) loads in flight per round, so a thread's share of a
+    // decode-sized vector is one round; the additions keep the element order
+    constexpr uint32_t kB = 16;
+    for (uint32_t c = first; c < n; c += kB * stride) {
         float v[kB];
 #pragma unroll
-        for (uint32_t u = 0; u < kB; ++u) v[u] = __ldcg(x + c + u * stride);
+        for (uint32_t u = 0; u < kB; ++u) v[u] = c + u * stride < n ? __ldcg(x + c + u * stride) : 0.0f;
 #pragma unroll
-        for (uint32_t u = 0; u < kB; ++u) s = __dadd_rn(s, __dmul_rn(static_cast<double>(v[u]), static_cast<double>(v[u])));
-    }
-    for (; c < n; c += stride) {
-        const double v = static_cast<double>(__ldcg(x + c));
-        s = __dadd_rn(s, __dmul_rn(v, v));
+        for (uint32_t u = 0; u < kB; ++u)
+            if (c + u * stride < n)
+                s = __dadd_rn(s, __dmul_rn(static_cast<double>(v[u]), static_cast<double>(v[u])));
     }
     return s;
 }

@@ -155,3 +155,24 @@ def test_partial_fold_two_gloo_ranks():
         p.join(timeout=60)
     for rank, ok, err in results:
         assert ok, f"rank {rank}: {err}"
+
+
+def test_trace_step_breakdown():
+    """oracle_b200.trace.step_breakdown on a hand-made trace of two steps of
+    two programs (one op, then two ops)."""
+    from oracle_b200 import TRACE_WORDS
+    from oracle_b200.trace import step_breakdown
+    recs = np.zeros((5, TRACE_WORDS), np.int64)
+    t = 0
+    for i in range(5):
+        recs[i, 0] = t                                # consumers start
+        ops = 1 if i % 2 == 0 else 2
+        for k in range(ops):
+            recs[i, 1 + 3 * k:4 + 3 * k] = (t + 1000, t + 3000, t + 7000)  # wait 1, build 2, rows 4 us
+            t += 7000
+        recs[i, -1] = t + 500                         # CTA 0 done
+        t += 500 + 2000                               # 2 us to the next program
+    words = np.concatenate([[5], recs.reshape(-1)])
+    got = step_breakdown(words, 2, [0, 1], lambda p: f"p{p}")
+    assert got["p0"] == {"total": 7.5, "gap_to_next": 2.0, "op0_wait": 1.0, "op0_build": 2.0, "op0_rows": 4.0}
+    assert got["p1"]["op1_wait"] == 1.0 and got["p1"]["total"] == 14.5
