@@ -379,78 +379,6 @@ __device__ __forceinline__ void q8k_segment_pass1(uint32_t nb, const ActImage& i
     }
 }
 
-// Narrow rows (at most L <= 8 super-blocks, L = 2, 4 or 8): the warp splits
-// into 32 / (2L) groups of 2L lanes, lane = 2L * group + 2j + part, and each
-// group computes two rows (A, B) at once, so a warp takes 32 / L rows where a
-// full-width walk takes two.  Per row, the canonical order of a row of at most
-// L super-blocks: leaves j >= nb and the folds of strides 8 .. L add +0 (the
-// leaves are never -0), which changes no bit, so the fold of strides L / 2 ..
-// 1 over the L leaves gives the same sum; the segment is the row's only one,
-// so its running sum is that fold (0 + s).  The two rows share their first
-// level as in q8k_segment_tree2: lanes with j < L / 2 keep row A's sums of
-// leaves j and j + L / 2, the others row B's.  Result: row A's sum on lane
-// 2L * group, row B's on lane 2L * group + L.  kXReg: the lane's activation
-// slice (super-block j of the row) is already in registers.
-template <uint32_t kType, bool kXReg>
-__device__ __forceinline__ float q8k_rows_narrow(uint32_t nb, uint32_t L, const ActImage& img, const uint8_t* rowa,
-                                                 const uint8_t* rowb, const uint32_t (&xw)[32], const int (&xbs)[8],
-                                                 float xd, int lane) {
-    const uint32_t li = static_cast<uint32_t>(lane) & (2u * L - 1u);
-    const uint32_t j = li >> 1;
-    const int part = lane & 1;
-    constexpr uint32_t kBlockBytes = kType == 12 ? 144u : 210u;
-    const bool active = j < nb;
-    int ia = 0, ma = 0, ib = 0, mb = 0;
-    float dwa = 0.0f, dmwa = 0.0f, dwb = 0.0f, dmwb = 0.0f, dx = 0.0f;
-    if (active) {
-        const size_t off = size_t(j) * kBlockBytes;
-        if constexpr (kXReg) {
-            dx = xd;
-            if (kType == 12) {
-                q4k_half_sums(rowa + off, part, xw, xbs, ia, ma, dwa, dmwa);
-                q4k_half_sums(rowb + off, part, xw, xbs, ib, mb, dwb, dmwb);
-            } else {
-                q6k_half_sums(rowa + off, part, xw, xbs, ia, dwa);
-                q6k_half_sums(rowb + off, part, xw, xbs, ib, dwb);
-            }
-        } else {
-            uint32_t w[32];
-            int bs[8];
-            fetch_lane_x<kType>(img, j, part, w, bs, dx);
-            if (kType == 12) {
-                q4k_half_sums(rowa + off, part, w, bs, ia, ma, dwa, dmwa);
-                q4k_half_sums(rowb + off, part, w, bs, ib, mb, dwb, dmwb);
-            } else {
-                q6k_half_sums(rowa + off, part, w, bs, ia, dwa);
-                q6k_half_sums(rowb + off, part, w, bs, ib, dwb);
-            }
-        }
-    }
-    ia += __shfl_xor_sync(0xFFFFFFFFu, ia, 1);
-    ib += __shfl_xor_sync(0xFFFFFFFFu, ib, 1);
-    if (kType == 12) {
-        ma += __shfl_xor_sync(0xFFFFFFFFu, ma, 1);
-        mb += __shfl_xor_sync(0xFFFFFFFFu, mb, 1);
-    }
-    float la = 0.0f, lb = 0.0f;
-    if (active) {
-        float pa = __fmul_rn(__fmul_rn(dwa, dx), __int2float_rn(ia));
-        float pb = __fmul_rn(__fmul_rn(dwb, dx), __int2float_rn(ib));
-        if (kType == 12) {
-            pa = __fsub_rn(pa, __fmul_rn(__fmul_rn(dmwa, dx), __int2float_rn(ma)));
-            pb = __fsub_rn(pb, __fmul_rn(__fmul_rn(dmwb, dx), __int2float_rn(mb)));
-        }
-        la = __fadd_rn(la, pa);
-        lb = __fadd_rn(lb, pb);
-    }
-    // first level (stride L / 2 in j, lane distance L): A on the low half, B on the high
-    const bool low = (li & L) == 0;
-    float v = __fadd_rn(low ? la : lb, __shfl_xor_sync(0xFFFFFFFFu, low ? lb : la, static_cast<int>(L)));
-    for (uint32_t off = L >> 1; off >= 2; off >>= 1)
-        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, static_cast<int>(off)));
-    return __fadd_rn(0.0f, v);
-}
-
 // The lane's activation slice for register-resident rows (<= 16 super-blocks).
 template <uint32_t kType>
 __device__ __forceinline__ void load_lane_x(const ActImage& img, uint32_t nb, int lane, uint32_t (&xw)[32],

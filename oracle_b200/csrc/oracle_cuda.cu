@@ -944,7 +944,7 @@ namespace {
 // planner for every entry point that launches matvec_program_kernel, so they
 // all stream the same stages for the same ops.
 oracle_cuda_status plan_program_ring(ProgramParams& pp, uint64_t smem_budget, uint64_t stage_target,
-                                     std::string& why, bool narrow_walk = false) {
+                                     std::string& why) {
     why = "matvec program rows too long for the shared-memory stage ring";
     if (pp.act_bytes > 96 * 1024) return ORACLE_CUDA_UNSUPPORTED;
     const uint64_t budget = smem_budget - stream_barrier_bytes(16) - pp.act_bytes;
@@ -967,9 +967,7 @@ oracle_cuda_status plan_program_ring(ProgramParams& pp, uint64_t smem_budget, ui
                           : 0u;
         const uint64_t rb = p.segmented ? uint64_t(kSegmentBlocks) * (q6 ? 210u : 144u) : p.row_bytes;
         uint64_t R = target > 32 ? (target - 32) / rb : 0;
-        // narrow rows (<= 8 super-blocks): 32 / L rows per warp task (L = 2, 4, 8)
-        const uint64_t narrow = !narrow_walk ? 0 : p.nb <= 2 ? 16 : p.nb <= 4 ? 8 : p.nb <= 8 ? 4 : 0;
-        const uint64_t cap = (p.segmented && q6) ? kProgramWarps : narrow ? narrow * kProgramWarps : 2 * kProgramWarps;
+        const uint64_t cap = (p.segmented && q6) ? kProgramWarps : 2 * kProgramWarps;
         if (R > cap) R = cap;
         if (R < 1) R = 1;
         p.rows_per_stage = static_cast<uint32_t>(R);
@@ -1243,9 +1241,7 @@ oracle_cuda_status program_run(oracle_cuda_context* ctx, const oracle_cuda_matve
     pp.act_bytes = act_total;
     {
         std::string why;
-        // peer-group programs walk rows of <= 8 super-blocks narrow (more rows per stage)
-        const oracle_cuda_status rs =
-            plan_program_ring(pp, ctx->smem_budget, ctx->program_stage_target, why, group != nullptr);
+        const oracle_cuda_status rs = plan_program_ring(pp, ctx->smem_budget, ctx->program_stage_target, why);
         if (rs != ORACLE_CUDA_OK) return fail(ctx, rs, why);
     }
     pp.copy_chunk = ctx->copy_chunk;

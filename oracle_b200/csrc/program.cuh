@@ -351,69 +351,6 @@ __device__ __forceinline__ void program_walk_op(const ProgramOp& op, uint8_t* ac
     }
 }
 
-// Consumer walk over an op of narrow rows (at most 8 super-blocks): a warp's
-// task is 32 / L consecutive rows of a stage (L = 2, 4 or 8 >= nb; two rows per
-// group of 2L lanes, q8k_rows_narrow), tasks rotating over the warps from stage
-// to stage as in program_walk_op.  Rows past the stage's end read a row of the
-// task (in bounds) and are not stored.
-template <int NCW, uint32_t kType, bool kXReg, bool kPeers>
-__device__ __forceinline__ void program_walk_narrow(const ProgramOp& op, uint32_t L, uint8_t* act, uint8_t* stage0,
-                                                    uint32_t stage_bytes, uint32_t S, uint64_t* full, uint64_t* empty,
-                                                    uint32_t& s, uint32_t& phase, bool& failed, DeviceStatus* status,
-                                                    const PeerExchange& px, int warp, int lane) {
-    const ActImage img = q8k_image(act + op.act_offset, op.nb);
-    const uint32_t W = 2u * L;
-    const uint32_t li = static_cast<uint32_t>(lane) & (W - 1u);
-    const uint32_t group = static_cast<uint32_t>(lane) >> (L == 2u ? 2u : L == 4u ? 3u : 4u);
-    const uint32_t per = 32u / L;  // rows per task
-    uint32_t xw[32];
-    int xbs[8];
-    float xd = 0.0f;
-    if (kXReg && !failed) load_lane_x<kType>(img, op.nb, static_cast<int>(li), xw, xbs, xd);
-    const uint64_t r0 = blockIdx.x * op.rows / gridDim.x;
-    const uint64_t r1 = (blockIdx.x + 1ull) * op.rows / gridDim.x;
-    const uint32_t nrows = static_cast<uint32_t>(r1 - r0);
-    const uint32_t R = op.rows_per_stage;
-    const uint32_t T = (nrows + R - 1) / R;
-    const uint32_t rb = static_cast<uint32_t>(op.row_bytes);
-    const uint32_t wlo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(op.w));
-    const uint32_t row0 = static_cast<uint32_t>(r0);
-    float* const y = op.y + r0;
-    const uint32_t step = ((R + per - 1) / per) % NCW;
-    uint32_t owner_base = 0;
-    for (uint32_t t = 0; t < T; ++t) {
-        if (!failed) {
-            const bool ok = mbar_wait(&full[s], phase, status, 14);
-            failed = !__all_sync(0xFFFFFFFFu, ok);
-        }
-        if (!failed) {
-            const uint32_t q_lo = t * R;
-            const uint32_t n_here = nrows - q_lo < R ? nrows - q_lo : R;
-            const uint32_t head = (wlo + (row0 + q_lo) * rb) & 15u;
-            const uint8_t* slot = stage0 + s * stage_bytes + head;
-            const uint32_t n_tasks = (n_here + per - 1) / per;
-            uint32_t task = warp >= static_cast<int>(owner_base) ? warp - owner_base : warp + NCW - owner_base;
-            for (; task < n_tasks; task += NCW) {
-                const uint32_t ja = per * task + 2u * group;
-                const bool has_a = ja < n_here, has_b = ja + 1u < n_here;
-                const uint8_t* pa = slot + (has_a ? ja : per * task) * rb;
-                const uint8_t* pb = has_b ? pa + rb : pa;
-                const float v = q8k_rows_narrow<kType, kXReg>(op.nb, L, img, pa, pb, xw, xbs, xd, lane);
-                if ((li == 0u && has_a) || (li == L && has_b))
-                    program_store_row<kPeers>(px, op.push != 0, y + q_lo + ja + (li == L ? 1u : 0u), v);
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == S) {
-            s = 0;
-            phase ^= 1u;
-        }
-        owner_base += step;
-        if (owner_base >= NCW) owner_base -= NCW;
-    }
-}
-
 // Consumers of a segment-major op (rows of G > 1 segments): for Q4_K (at most
 // 2 * NCW rows per group) warp w takes rows 2w, 2w + 1 of every group, for
 // Q6_K (at most NCW rows) row w, and walks the group's G stages, adding each
@@ -764,20 +701,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1) matvec_program_kernel(co
         if (trace) trace[2 + 3 * k] = global_timer_ns();
         const bool q4 = kTypes == 1 || (kTypes == 3 && op.type == 12);
         static_assert(kTypes >= 1 && kTypes <= 4, "program type set");
-        // rows of at most 8 super-blocks: the narrow walk, compiled only into
-        // the peer-group programs (whose column shards have such rows), so the
-        // single-GPU programs keep their register allocation
-        if (kPeers && q4 && op.nb <= 8) {
-            const uint32_t L = op.nb <= 2 ? 2u : op.nb <= 4 ? 4u : 8u;
-            program_walk_narrow<NCW, 12, true, kPeers>(op, L, act, stage0, pp.stage_bytes, S, full, empty, s, phase,
-                                                      failed, pp.status, pp.px, warp, lane);
-        } else if (q4 && op.nb <= 16) {
+        if (q4 && op.nb <= 16) {
             program_walk_op<NCW, 12, true, 1, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase, failed,
                                                       pp.status, pp.px, warp, lane);
-        } else if (kPeers && !q4 && op.nb <= 8) {
-            const uint32_t L = op.nb <= 2 ? 2u : op.nb <= 4 ? 4u : 8u;
-            program_walk_narrow<NCW, 14, false, kPeers>(op, L, act, stage0, pp.stage_bytes, S, full, empty, s, phase,
-                                                       failed, pp.status, pp.px, warp, lane);
         } else if (q4) {
             if (op.segmented)
                 program_walk_segmented<NCW, 12, kPeers>(op, act, stage0, pp.stage_bytes, S, full, empty, s, phase,
