@@ -110,8 +110,9 @@ WORKLOADS = {
     "config2": Workload(
         "config2", "Q4_K x Q8_K decode matvec GB/s",
         "config2: Q4_K x Q8_K decode matvec, batch 1, shapes 4096->12288, 12288->4096, 4096->4096 "
-        "(each step's activations quantized to Q8_K in the launch); one matvec-program launch per step "
-        "(the three matvecs), as a decode step runs them",
+        "(each step's activations quantized to Q8_K in the launch); one GPU: one launch per matvec, "
+        "chained by programmatic dependent launch (the one-launch matvec program is timed beside it); "
+        "several GPUs: one matvec-program launch per step with the all-gather inside the kernel",
         [(TYPE_Q4_K, 4096, 12288), (TYPE_Q4_K, 12288, 4096), (TYPE_Q4_K, 4096, 4096)], CONTRACT_Q8K, 10, True,
         "port", "int8 x u4 -> int32, f32 combine", steps_per_launch=1),
     "config3": Workload(
@@ -455,7 +456,11 @@ def gpu_arm(args, wl: Workload) -> None:
     def launch(s0: int, count: int):
         """Steps s0 .. s0+count-1 (count <= P): with a program, ONE persistent
         launch runs all their (independent) matvecs back to back."""
-        if not (fused or wl.program):
+        # one GPU: one single-matvec launch per op (programmatic dependent launch
+        # chains them); the matvec program, which runs them in one persistent
+        # launch, is timed beside it.  Several GPUs: the program (its all-gather
+        # runs inside the kernel) or, with --exchange nccl, the program + NCCL
+        if not (fused or (wl.program and world > 1)):
             for s in range(s0, s0 + count):
                 step_separate(s)
             return
@@ -557,11 +562,19 @@ def gpu_arm(args, wl: Workload) -> None:
 
     extra = {}
     if wl.program and world == 1:
-        # the same step as separate single-matvec launches
+        # the same step as ONE matvec-program launch (the three matvecs in one persistent kernel)
+        def step_program(s: int):
+            ws_, p = pool[s % wl.pool_sets], s % P
+            ctx.matvec_program([(t, n, k, ws_[i], x_sets[p][i], y_sets[p][i], 0) for i, (t, k, n) in
+                                enumerate(local_ops)], stream=stream)
+
+        with torch.cuda.stream(stream):
+            step_program(0)  # sizes the context's scratch outside the capture
+        stream.synchronize()
         gsep = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gsep, stream=stream):
             for s in range(wl.pool_sets):
-                step_separate(s)
+                step_program(s)
         with torch.cuda.stream(stream):
             gsep.replay()
             torch.cuda.synchronize()
@@ -572,7 +585,7 @@ def gpu_arm(args, wl: Workload) -> None:
             b.record(stream)
             torch.cuda.synchronize()
         sep_us = a.elapsed_time(b) * 1e3 / (20 * wl.pool_sets)
-        extra["separate_launches"] = {"us_per_step": sep_us, "gbs": wl.step_bytes / (sep_us * 1e-6) / 1e9}
+        extra["program_launch"] = {"us_per_step": sep_us, "gbs": wl.step_bytes / (sep_us * 1e-6) / 1e9}
         del gsep
         if P > 1:
             # the same steps, one program launch each
@@ -687,7 +700,7 @@ def gpu_arm(args, wl: Workload) -> None:
 
     cpu = cpu_baseline_leg(wl) if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
-        kernel = ("matvec_program_kernel" if wl.program else
+        kernel = ("matvec_program_kernel" if wl.program and world > 1 else
                   "matvec_q80_split_kernel (lane per row, sequential f32)" if wl.contract == CONTRACT_F32 else
                   "stream_rows_kernel<MatvecQ8KConsumer>")
         line = {"metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps_timed,
