@@ -188,6 +188,19 @@ oracle_cuda_status oracle_cuda_batch_matvec(oracle_cuda_context* ctx, uint32_t t
                                             const void* w_dev, uint64_t w_nbytes, const void* image_dev,
                                             uint64_t image_nbytes, uint32_t batch, float* y_dev, uint64_t y_len,
                                             void* stream);
+/* The residual add and RMSNorm before a projection, fused into its
+ * quantization (arguments and checks as oracle_cuda_batch_quantize): s = a + b
+ * (b may be NULL: s = a), written to sum_dev when it is not NULL (the
+ * residual stream; not one of the inputs), then rms_norm_rows of s with
+ * weight_dev / eps (src/runtime/qwen35_block.cpp:161-188, 190-200; the same
+ * double sum as oracle_cuda_rms_norm_rows) quantized into the batch image;
+ * cols at most 8192.  The same image as oracle_cuda_add,
+ * oracle_cuda_rms_norm_rows and oracle_cuda_batch_quantize in one launch
+ * instead of three. */
+oracle_cuda_status oracle_cuda_batch_norm_quantize(oracle_cuda_context* ctx, const float* a_dev, const float* b_dev,
+                                                   float* sum_dev, const float* weight_dev, float eps, uint64_t cols,
+                                                   uint32_t batch, void* image_dev, uint64_t image_nbytes,
+                                                   void* stream);
 
 /* Matvec program: up to ORACLE_CUDA_PROGRAM_MAX_OPS Q8_K-contract matvecs
  * (q4_K / q6_K weights) in ONE persistent launch.  The weights of all ops

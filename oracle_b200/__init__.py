@@ -112,6 +112,7 @@ _proto("oracle_cuda_storage_matvec", [_vp, _i32, _u32, _u64, _u64, _vp, _u64, _v
 _proto("oracle_cuda_matvec_q8k_prequantized", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _vp, _u64, _vp])
 _proto("oracle_cuda_batch_image_bytes", [_u64], C.c_uint64)
 _proto("oracle_cuda_batch_quantize", [_vp, _vp, _u64, _u32, _vp, _u64, _vp])
+_proto("oracle_cuda_batch_norm_quantize", [_vp, _vp, _vp, _vp, _vp, C.c_float, _u64, _u32, _vp, _u64, _vp])
 _proto("oracle_cuda_batch_matvec", [_vp, _u32, _u64, _u64, _vp, _u64, _vp, _u64, _u32, _vp, _u64, _vp])
 
 
@@ -495,6 +496,13 @@ class Context:
         """oracle_cuda_batch_quantize: x[batch][cols] (device f32) -> batch image (device uint8)."""
         self._check(_lib.oracle_cuda_batch_quantize(self._h, _addr(x), cols, batch, _addr(image), _nbytes(image),
                                                     _stream(stream)))
+
+    def batch_norm_quantize(self, a, b, sum_out, weight, eps, cols, batch, image, stream=None) -> None:
+        """oracle_cuda_batch_norm_quantize: rms_norm(a (+ b)) into a batch image; the
+        sum a + b is also written to sum_out when given."""
+        self._check(_lib.oracle_cuda_batch_norm_quantize(self._h, _addr(a), _addr(b), _addr(sum_out), _addr(weight),
+                                                         eps, cols, batch, _addr(image), _nbytes(image),
+                                                         _stream(stream)))
 
     def batch_matvec(self, qtype, rows, cols, w, image, batch, y, stream=None, w_nbytes=None) -> None:
         """oracle_cuda_batch_matvec: y[b][rows] = W (q4_K / q6_K) x vector b of a batch image."""

@@ -11,7 +11,8 @@ step together, and every projection reads its weights ONCE for all of them:
   into a batch image (``Context.batch_quantize``) that every matrix reading it
   shares, and each matrix is one ``Context.batch_matvec`` (int8 tensor-core
   MMAs, bit-identical per sequence to the single-vector Q8_K kernels);
-* RMSNorm, residual adds and SwiGLU are row-wise kernels over B rows;
+* RMSNorm, with the residual add before it, is fused into the quantization
+  of the projection input it feeds (one launch); SwiGLU is a row-wise kernel;
 * attention runs the sequences as B x heads query heads over a KV cache laid
   out [token][sequence][kv_head][dim] (a GQA group never crosses a sequence),
   with the batch-1 decoder's fused prep / core kernels unchanged;
@@ -61,7 +62,7 @@ class BatchDecoder:
                 raise ValueError(f"{name}: batched decoding runs Q4_K / Q6_K matrices only")
         B, H, F = self.B, cfg.hidden, cfg.ffn
         f32 = lambda n: torch.zeros(n, dtype=torch.float32, device=dev)  # noqa: E731
-        self.hidden, self.resid, self.normed, self.branch, self.ffn_out = (f32(B * H) for _ in range(5))
+        self.hidden, self.resid, self.branch, self.ffn_out = (f32(B * H) for _ in range(4))
         self.ffn_gate, self.ffn_up, self.ffn_act = f32(B * F), f32(B * F), f32(B * F)
         widest = max(H, F, cfg.q_width, cfg.value_width)
         self.image = torch.zeros(Context.batch_image_bytes(widest), dtype=torch.uint8, device=dev)
@@ -144,26 +145,27 @@ class BatchDecoder:
         H, F = cfg.hidden, cfg.ffn
         et, edims, emb = self.w["token_embd.weight"]
         ctx.gather_rows(et, edims[1], edims[0], emb, self.next_id, self.hidden, s)
+        # the residual adds and norms are fused into the quantization of the
+        # projection input they feed: hidden = resid + ffn_out (the previous
+        # block's end) with this block's input norm, resid = hidden + branch
+        # with the post-attention norm (finish_block, qwen35_block.cpp:326-352)
+        ctx.batch_norm_quantize(self.hidden, None, None, self._vec("blk.0.attn_norm.weight"), cfg.eps, H, B,
+                                self.image, s)
         for i in range(cfg.layers):
             p = f"blk.{i}."
-            ctx.rms_norm_rows(self.hidden, self._vec(p + "attn_norm.weight"), B, H, cfg.eps, self.normed, s)
-            self._quantize(self.normed, H, s)
             if cfg.is_attention(i):
                 self._attention(i, s)
             else:
                 self._recurrent(i, s)
-            # finish_block (qwen35_block.cpp:326-352)
-            ctx.add(self.hidden, self.branch, B * H, self.resid, s)
-            ctx.rms_norm_rows(self.resid, self._vec(p + "post_attention_norm.weight"), B, H, cfg.eps, self.normed, s)
-            self._quantize(self.normed, H, s)
+            ctx.batch_norm_quantize(self.hidden, self.branch, self.resid, self._vec(p + "post_attention_norm.weight"),
+                                    cfg.eps, H, B, self.image, s)
             self._mv(p + "ffn_gate.weight", self.ffn_gate, s)
             self._mv(p + "ffn_up.weight", self.ffn_up, s)
             ctx.swiglu(self.ffn_gate, self.ffn_up, B * F, self.ffn_act, s)
             self._quantize(self.ffn_act, F, s)
             self._mv(p + "ffn_down.weight", self.ffn_out, s)
-            ctx.add(self.resid, self.ffn_out, B * H, self.hidden, s)
-        ctx.rms_norm_rows(self.hidden, self._vec("output_norm.weight"), B, H, cfg.eps, self.normed, s)
-        self._quantize(self.normed, H, s)
+            nxt = f"blk.{i + 1}.attn_norm.weight" if i + 1 < cfg.layers else "output_norm.weight"
+            ctx.batch_norm_quantize(self.resid, self.ffn_out, self.hidden, self._vec(nxt), cfg.eps, H, B, self.image, s)
         self._mv("output.weight" if "output.weight" in self.w else "token_embd.weight", self.logits, s)
         ctx.argmax_rows(self.logits, B, cfg.vocab, self.am_keys, s)
         ctx.token_commit_rows(self.am_keys, B, self.prompt, n_prompt, self.pos, self.next_id, self.tokens,

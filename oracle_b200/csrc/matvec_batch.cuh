@@ -41,6 +41,7 @@
 // e = 0: (vector g, row 2t), 1: (g, 2t + 1), 2: (g + 8, 2t), 3: (g + 8, 2t + 1).
 #pragma once
 
+#include "decoder_ops.cuh"
 #include "q8k.cuh"
 
 namespace oracle_cuda {
@@ -90,24 +91,12 @@ __host__ __device__ constexpr uint32_t batch_stage_bytes(uint32_t type) {
 // One warp per (vector, block): the batch-1 quantizer's arithmetic (GGML's
 // quantize_row_q8_K), scattered into the fragment order, plus the split
 // sub-block sums of both widths.
-__global__ void __launch_bounds__(256) quantize_batch_image_kernel(const float* __restrict__ x, uint32_t batch,
-                                                                   uint32_t nb, uint8_t* __restrict__ image) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
-    const int lane = threadIdx.x & 31;
-    if (gw >= uint32_t(kBatchMax) * nb) return;
-    const uint32_t v = gw % kBatchMax, i = gw / kBatchMax;
+// Vector v's Q8_K block i (the lane's quantized values r) into the batch image.
+__device__ __forceinline__ void batch_image_store_block(uint8_t* __restrict__ image, uint32_t v, uint32_t i,
+                                                        const Q8KLane& r, int lane) {
     uint8_t* blk = image + uint64_t(i) * kBatchImageBlockBytes;
     uint32_t* q = reinterpret_cast<uint32_t*>(blk);
     float* d = reinterpret_cast<float*>(blk + kBatchImageDOffset);
-    Q8KLane r{0u, 0u, 0, 0.0f};
-    if (v < batch) {  // warp-uniform
-        const float* xb = x + (uint64_t(v) * nb + i) * 256;
-        float vals[8];
-        load_lane8(xb, lane, (reinterpret_cast<uintptr_t>(xb) & 15u) == 0, vals);
-        r = quantize_q8k_lane_values(vals, lane);
-    }
     const uint32_t w[2] = {r.q_lo, r.q_hi};
 #pragma unroll
     for (int h2 = 0; h2 < 2; ++h2) {
@@ -140,6 +129,86 @@ __global__ void __launch_bounds__(256) quantize_batch_image_kernel(const float* 
         }
     }
     if (lane == 0) d[v] = r.d;
+}
+
+// One warp per (vector, block): x [batch][nb * 256] quantized into the batch image.
+__global__ void __launch_bounds__(256) quantize_batch_image_kernel(const float* __restrict__ x, uint32_t batch,
+                                                                   uint32_t nb, uint8_t* __restrict__ image) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    const int lane = threadIdx.x & 31;
+    if (gw >= uint32_t(kBatchMax) * nb) return;
+    const uint32_t v = gw % kBatchMax, i = gw / kBatchMax;
+    Q8KLane r{0u, 0u, 0, 0.0f};
+    if (v < batch) {  // warp-uniform
+        const uint64_t at = (uint64_t(v) * nb + i) * 256;
+        float vals[8];
+        load_lane8(x + at, lane, (reinterpret_cast<uintptr_t>(x + at) & 15u) == 0, vals);
+        r = quantize_q8k_lane_values(vals, lane);
+    }
+    batch_image_store_block(image, v, i, r, lane);
+}
+
+// One CTA (kBatchNormThreads threads) per vector: s = a (+ b), written to
+// s_out when given (the residual stream), then rms_norm_rows over the row
+// with weights w -- the same double sum as rms_norm_rows_kernel (thread t adds
+// elements t, t + 256, ... in order, then block_sum_f64), so the same values
+// -- quantized into the batch image.  The normalised row is staged in shared
+// memory (width <= kBatchNormMaxWidth).  Vectors past the batch are zero.
+constexpr uint32_t kBatchNormThreads = 256;
+constexpr uint32_t kBatchNormMaxWidth = 8192;
+__global__ void __launch_bounds__(kBatchNormThreads) batch_norm_quantize_kernel(
+    const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ s_out,
+    const float* __restrict__ w, float eps, uint32_t batch, uint32_t width, uint8_t* __restrict__ image) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ double scratch[32];
+    __shared__ __align__(16) float row[kBatchNormMaxWidth];
+    const uint32_t v = blockIdx.x, nb = width / 256u;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (v >= batch) {  // CTA-uniform: zero blocks for the vectors past the batch
+        for (uint32_t i = warp; i < nb; i += kBatchNormThreads / 32)
+            batch_image_store_block(image, v, i, Q8KLane{0u, 0u, 0, 0.0f}, lane);
+        return;
+    }
+    const float* av = a + uint64_t(v) * width;
+    const float* bv = b ? b + uint64_t(v) * width : nullptr;
+    double sum = 0.0;
+    // eight elements' loads in flight per round; the squares are added in
+    // element order
+    constexpr uint32_t kRound = 8;
+    for (uint32_t c0 = threadIdx.x; c0 < width; c0 += kRound * kBatchNormThreads) {
+        float x[kRound];
+#pragma unroll
+        for (uint32_t u = 0; u < kRound; ++u) {
+            const uint32_t c = c0 + u * kBatchNormThreads;
+            x[u] = c < width ? (bv ? __fadd_rn(__ldg(av + c), __ldg(bv + c)) : __ldg(av + c)) : 0.0f;
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kRound; ++u) {
+            const uint32_t c = c0 + u * kBatchNormThreads;
+            if (c < width) {
+                row[c] = x[u];
+                const double d = static_cast<double>(x[u]);
+                sum = __dadd_rn(sum, __dmul_rn(d, d));
+            }
+        }
+    }
+    if (s_out)
+        for (uint32_t c = threadIdx.x; c < width; c += kBatchNormThreads) s_out[uint64_t(v) * width + c] = row[c];
+    const float inv = rms_inverse(block_sum_f64(sum, scratch), width, eps);
+    for (uint32_t i = warp; i < nb; i += kBatchNormThreads / 32) {
+        float vals[8], wv[8];
+        const float4* rp = reinterpret_cast<const float4*>(row + 256u * i) + 2 * lane;
+        const float4 lo = rp[0], hi = rp[1];
+        vals[0] = lo.x; vals[1] = lo.y; vals[2] = lo.z; vals[3] = lo.w;
+        vals[4] = hi.x; vals[5] = hi.y; vals[6] = hi.z; vals[7] = hi.w;
+        load_lane8(w + 256ull * i, lane, (reinterpret_cast<uintptr_t>(w + 256ull * i) & 15u) == 0, wv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) vals[j] = __fmul_rn(__fmul_rn(vals[j], inv), wv[j]);
+        batch_image_store_block(image, v, i, quantize_q8k_lane_values(vals, lane), lane);
+    }
 }
 
 __device__ __forceinline__ void mma_k32_s8u8(int (&c)[4], const uint4& a, uint32_t b0, uint32_t b1) {

@@ -839,6 +839,43 @@ oracle_cuda_status oracle_cuda_batch_quantize(oracle_cuda_context* ctx, const fl
     return s == ORACLE_CUDA_OK ? ok(ctx) : s;
 }
 
+namespace {
+// The checks of oracle_cuda_batch_quantize, shared by the fused form.
+oracle_cuda_status check_batch_image_args(oracle_cuda_context* ctx, const float* x_dev, uint64_t cols, uint32_t batch,
+                                          const void* image_dev, uint64_t image_nbytes) {
+    if (cols == 0 || cols % 256 != 0)
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "Q8_K activations need a multiple of 256 columns");
+    if (batch == 0 || batch > uint32_t(kBatchMax))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "a batch image holds 1 to 16 vectors");
+    if (cols / 256 > 0xFFFFFFFull) return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "rows longer than 2^36 elements");
+    if (image_nbytes < oracle_cuda_batch_image_bytes(cols))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "batch image buffer too small");
+    if (!x_dev || !image_dev || (reinterpret_cast<uintptr_t>(image_dev) & 15u))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "activation pointer null or image pointer not 16-byte aligned");
+    return ORACLE_CUDA_OK;
+}
+}  // namespace
+
+oracle_cuda_status oracle_cuda_batch_norm_quantize(oracle_cuda_context* ctx, const float* a_dev, const float* b_dev,
+                                                   float* sum_dev, const float* weight_dev, float eps, uint64_t cols,
+                                                   uint32_t batch, void* image_dev, uint64_t image_nbytes,
+                                                   void* stream) {
+    if (!ctx) return fail(nullptr, ORACLE_CUDA_INVALID_ARGUMENT, "context is null");
+    if (oracle_cuda_status s = check_batch_image_args(ctx, a_dev, cols, batch, image_dev, image_nbytes)) return s;
+    if (cols > kBatchNormMaxWidth)
+        return fail(ctx, ORACLE_CUDA_UNSUPPORTED, "batched norm rows of more than 8192 columns");
+    if (!weight_dev || !(eps > 0.0f) || !std::isfinite(eps))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "norm weights null or epsilon not positive and finite");
+    if (sum_dev && (sum_dev == a_dev || sum_dev == b_dev))
+        return fail(ctx, ORACLE_CUDA_INVALID_ARGUMENT, "the sum must not overwrite an input");
+    ORACLE_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    const oracle_cuda_status s =
+        launch(ctx, batch_norm_quantize_kernel, dim3(kBatchMax), dim3(kBatchNormThreads), 0,
+               static_cast<cudaStream_t>(stream), (ctx->flags & ORACLE_CUDA_FLAG_PDL) != 0, a_dev, b_dev, sum_dev,
+               weight_dev, eps, batch, static_cast<uint32_t>(cols), static_cast<uint8_t*>(image_dev));
+    return s == ORACLE_CUDA_OK ? ok(ctx) : s;
+}
+
 oracle_cuda_status oracle_cuda_batch_matvec(oracle_cuda_context* ctx, uint32_t type, uint64_t rows, uint64_t cols,
                                             const void* w_dev, uint64_t w_nbytes, const void* image_dev,
                                             uint64_t image_nbytes, uint32_t batch, float* y_dev, uint64_t y_len,

@@ -100,3 +100,32 @@ def test_batch_special_values(ctx, port):
         ctx.storage_matvec(ob.CONTRACT_Q8K, qtype, rows, k, to_dev(w), to_dev(x), y)
         ctx.device_status()
         assert bits_equal(y.cpu().numpy(), want), qtype
+
+
+@pytest.mark.parametrize("batch,cols", [(16, 4096), (5, 512), (1, 8192)])
+def test_fused_norm_quantize_equals_separate_kernels(ctx, batch, cols):
+    """oracle_cuda_batch_norm_quantize gives the image (and the residual sum)
+    of the separate add, rms_norm_rows and batch_quantize launches, byte for
+    byte."""
+    a = to_dev(synth.activations(cols, batch, "glue", "a"))
+    b = to_dev(synth.activations(cols, batch, "glue", "b"))
+    w = to_dev(synth.activations(cols, 1, "glue", "w"))
+    eps = float(np.float32(1e-6))
+    nbytes = ob.Context.batch_image_bytes(cols)
+    want, got = (torch.zeros(nbytes, dtype=torch.uint8, device=DEV) for _ in range(2))
+    s_want, normed = (torch.zeros(batch * cols, device=DEV) for _ in range(2))
+    s_got = torch.full((batch * cols,), 7.0, device=DEV)
+    ctx.add(a, b, batch * cols, s_want)
+    ctx.rms_norm_rows(s_want, w, batch, cols, eps, normed)
+    ctx.batch_quantize(normed, cols, batch, want)
+    ctx.batch_norm_quantize(a, b, s_got, w, eps, cols, batch, got)
+    torch.cuda.synchronize()
+    assert torch.equal(want, got) and bits_equal(s_want.cpu(), s_got.cpu())
+    ctx.rms_norm_rows(a, w, batch, cols, eps, normed)            # no residual add, no sum written
+    ctx.batch_quantize(normed, cols, batch, want)
+    ctx.batch_norm_quantize(a, None, None, w, eps, cols, batch, got)
+    torch.cuda.synchronize()
+    ctx.device_status()
+    assert torch.equal(want, got)
+    with pytest.raises(ob.InvalidArgument):
+        ctx.batch_norm_quantize(a, b, a, w, eps, cols, batch, got)   # the sum would overwrite an input
