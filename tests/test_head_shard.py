@@ -176,3 +176,39 @@ def test_trace_step_breakdown():
     got = step_breakdown(words, 2, [0, 1], lambda p: f"p{p}")
     assert got["p0"] == {"total": 7.5, "gap_to_next": 2.0, "op0_wait": 1.0, "op0_build": 2.0, "op0_rows": 4.0}
     assert got["p1"]["op1_wait"] == 1.0 and got["p1"]["total"] == 14.5
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_announcement_counter_protocol(world):
+    """The sharded programs' cross-rank protocol, modelled on the host with
+    random interleavings: each rank announces dependency j of step s (adds 1
+    to every peer's counter) and then waits until its own counter reaches
+    (s * D + j + 1) * (world - 1) before going on (to announce j + 1, or the
+    next step's first).  Whenever a wait passes, every peer has announced
+    (s, j) -- the counter never fills early with later announcements -- and
+    no rank deadlocks."""
+    rng = np.random.default_rng(world)
+    D, steps = 5, 6
+    total = D * steps
+    counter = [0] * world
+    announced = [0] * world          # dependencies announced so far, per rank
+    state = ["announce"] * world     # next action
+    for _ in range(200_000):  # a deadlock runs out of moves and fails below
+        if all(st == "done" for st in state):
+            break
+        runnable = [r for r in range(world) if state[r] != "done"]
+        r = int(rng.choice(runnable))
+        g = announced[r]             # the rank's current dependency (s * D + j)
+        if state[r] == "announce":
+            for p in range(world):
+                if p != r:
+                    counter[p] += 1
+            announced[r] += 1
+            state[r] = "wait"
+        elif state[r] == "wait":
+            target = g * (world - 1)  # (s * D + j + 1) * (world - 1) for the dependency just announced
+            if counter[r] >= target:
+                assert all(a >= g for a in announced), (r, g, announced)
+                state[r] = "announce" if g < total else "done"
+    assert all(st == "done" for st in state)
+    assert counter == [total * (world - 1)] * world
